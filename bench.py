@@ -1,0 +1,378 @@
+"""Benchmark: flow-LM decode frames/s (config 5 shard) with decode-attention GB/s vs HBM peak.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload (the largest single-GPU configuration): the 40m flow LM shape
+(9 layers, d_model 512, 8 heads of 64, ff 2048), random-init int8 per-output-channel weights
+(scales U(0.005, 0.02), seed 4), 512 independent streams per GPU (GPU g holds streams
+512g..512g+511 of 4096), prefixes U{32..512} prefilled before timing, then decode frames: one
+row per stream per frame through all layers (QKV + RoPE + KV append + split-KV attention +
+out_proj + FFN) replayed as one CUDA graph. Config 5 runs 250 frames; steps beyond that cycle
+the 250-frame window (lengths return to the prefixes), so every timed step is a frame of the
+same length distribution. A step = one frame for all streams of a GPU.
+
+value  = stream-frames per second over all GPUs, inputs resident in HBM.
+e2e    = the same through ptts_b200_step with pinned HOST input/output (H2D + D2H per step).
+roofline = the decode-attention kernel: algorithmic bytes (K and V rows read for every
+           attended position, q read, output written) / its CUDA-event duration in a traced
+           pass over the same frames, against MEASURED_PEAKS.json's HBM copy bandwidth.
+cpu_baseline = the C oracle (a port of the reference's CPU path) on the host cores, on a
+           sample of 16 streams of the same workload.
+Multi-GPU: one process per GPU (torchrun), independent shards, no data-path collective; NCCL
+only for the start barrier and the max over ranks of the timed duration.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+STREAMS_PER_GPU = 512
+TOTAL_STREAMS = 4096
+FRAMES = 250
+SEED = 4
+PREFIX_LO, PREFIX_HI = 32, 512
+METRIC = "decode attn GB/s (% HBM peak) & flow-LM frames/sec at 1/2/4/8 B200"
+CPU_SAMPLE_STREAMS = 16
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def traffic_per_launch():
+    """Per-launch DRAM bytes of the decode-attention kernel from a committed ncu summary."""
+    path = os.path.join(ROOT, "profiles", "decode_attn_traffic.json")
+    try:
+        with open(path) as f:
+            return json.load(f)
+    except Exception:
+        return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        if self.thread:
+            self.thread.join(timeout=2)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def load():
+    import __graft_entry__ as ge
+    return ge.load_package(), ge.load_workloads()
+
+
+def shard_prefixes(wl, rank: int):
+    allp = wl.prefix_lengths(TOTAL_STREAMS, PREFIX_LO, PREFIX_HI, SEED)
+    return allp[rank * STREAMS_PER_GPU:(rank + 1) * STREAMS_PER_GPU]
+
+
+def cpu_baseline(ptts, wl, cfg, weights, steps: int | None = None, budget_s: float = 12.0):
+    """The oracle on the host cores: a sample of CPU_SAMPLE_STREAMS streams of rank 0's shard,
+    prefilled (untimed), then decode frames timed until `steps` frames or `budget_s` seconds."""
+    import numpy as np
+    import torch
+    import oracle
+
+    n = CPU_SAMPLE_STREAMS
+    prefixes = shard_prefixes(wl, 0)[:n].astype(np.int32)
+    cap = int(prefixes.max()) + FRAMES
+    om = oracle.Model(cfg, weights)
+    shape = (cfg.num_layers, n, cap, cfg.num_heads, cfg.head_dim)
+    kc = np.zeros(shape, np.float32)
+    vc = np.zeros(shape, np.float32)
+    g = torch.Generator().manual_seed(SEED * 7919)
+    offs = np.concatenate([[0], np.cumsum(prefixes)]).astype(np.int32)
+    x = torch.randn(int(offs[-1]), cfg.d_model, generator=g).bfloat16().float().numpy()
+    lengths = np.zeros(n, np.int32)
+    streams = np.arange(n, dtype=np.int32)
+    threads = oracle.threads()
+    om.forward(x, kc, vc, lengths, streams, offs, store_bf16=True, n_threads=threads)
+    lengths = prefixes.copy()
+    one = np.arange(n + 1, dtype=np.int32)
+    frames = [torch.randn(n, cfg.d_model, generator=g).bfloat16().float().numpy() for _ in range(8)]
+    done, t0 = 0, time.perf_counter()
+    while True:
+        if done and done % FRAMES == 0:
+            lengths = prefixes.copy()
+        om.forward(frames[done % len(frames)], kc, vc, lengths, streams, one, store_bf16=True,
+                   n_threads=threads)
+        lengths += 1
+        done += 1
+        el = time.perf_counter() - t0
+        if (steps is not None and done >= steps) or (steps is None and el >= budget_s) or done >= 4 * FRAMES:
+            break
+    el = time.perf_counter() - t0
+    return {"value": n * done / el, "unit": "frames/s", "cores": threads, "kind": "port",
+            "sample": f"{n} streams of the config-5 shard (prefixes U{{32..512}}), {done} decode frames "
+                      f"of the 40m stack after an untimed prefill, C oracle with OpenMP",
+            "seconds": el, "frames": done}
+
+
+def run_reference(args):
+    """--impl reference: the reference's CPU path (the C oracle port) on the host cores."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    ptts, wl = load()
+    cfg = ptts.PHONON_40M
+    weights = ptts.random_weights(cfg, SEED)
+    import oracle
+    oracle.lib()
+    # Warm-up frames are part of the same sampled run; time exactly `steps` frames after them.
+    cb = cpu_baseline(ptts, wl, cfg, weights, steps=args.warmup + args.steps)
+    per_frame = cb["seconds"] / cb["frames"]
+    value = CPU_SAMPLE_STREAMS / per_frame
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "frames/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": per_frame * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32 (bf16-rounded storage)", "data": "synthetic",
+        "config": {"workload": "config5 shard: 40m flow LM, prefixes U{32..512}, decode frames",
+                   "streams_sampled": CPU_SAMPLE_STREAMS},
+        "cpu_baseline": {"value": value, "unit": "frames/s", "cores": cb["cores"], "kind": "port",
+                         "sample": cb["sample"]},
+        "e2e": {"value": value, "unit": "frames/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args):
+    import numpy as np
+    import torch
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device(f"cuda:{local}")
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+
+    ptts, wl = load()
+    cfg = ptts.PHONON_40M
+    L = cfg.num_layers
+    weights = ptts.random_weights(cfg, SEED)
+    model = ptts.Transformer(cfg, local)
+    model.load(weights)
+    prefixes = shard_prefixes(wl, rank)
+    B = STREAMS_PER_GPU
+    window = max(1, min(FRAMES, args.steps + args.warmup))
+    cap = int(prefixes.max()) + FRAMES
+    streams = np.arange(B, dtype=np.int32)
+    stream = torch.cuda.current_stream()
+
+    def fresh_state():
+        kv = ptts.KvState(L, B, cap, dtype="bf16", device=local)
+        g = torch.Generator(device=dev).manual_seed(SEED * 1000 + rank)
+        x = torch.randn(int(prefixes.sum()), cfg.d_model, generator=g, device=dev).bfloat16()
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record()
+        model.forward(kv, x, streams, prefixes)
+        t1.record()
+        torch.cuda.synchronize()
+        del x
+        return kv, t0.elapsed_time(t1)
+
+    kv, prefill_ms = fresh_state()
+    g = torch.Generator(device=dev).manual_seed(SEED * 2000 + rank)
+    x_frames = torch.randn(FRAMES, B, cfg.d_model, generator=g, device=dev).bfloat16()
+    y = torch.empty(B, cfg.d_model, dtype=torch.float32, device=dev)
+
+    state = {"f": 0}
+
+    def step(x_src, out):
+        f = state["f"]
+        if f and f % FRAMES == 0:
+            kv.set_lengths(streams, prefixes)
+        model.step(kv, streams, x_src(f % FRAMES), out=out)
+        state["f"] = f + 1
+
+    def barrier():
+        if dist is not None:
+            dist.barrier(device_ids=[local])
+        torch.cuda.synchronize()
+
+    def max_over_ranks(ms: float) -> float:
+        if dist is None:
+            return ms
+        t = torch.tensor([ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def timed(x_src, out, k: int):
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(k):
+            step(x_src, out)
+        e1.record(stream)
+        e1.synchronize()
+        return max_over_ranks(e0.elapsed_time(e1))
+
+    # ---- device-resident inputs --------------------------------------------------------------
+    dev_src = lambda f: x_frames[f]
+    for _ in range(args.warmup):
+        step(dev_src, y)
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local)
+    sampler.start()
+    ms = timed(dev_src, y, args.steps)
+    clocks = sampler.stop()
+    value = world * B * args.steps / (ms / 1e3)
+    launches_per_step = 3 + 6 * L
+    gpu_launches = args.steps * launches_per_step + (args.warmup + args.steps) // FRAMES
+
+    # ---- end to end through pinned host buffers ------------------------------------------------
+    x_host = x_frames.cpu().pin_memory()
+    y_host = torch.empty(B, cfg.d_model, dtype=torch.float32).pin_memory()
+    kv.set_lengths(streams, prefixes)
+    state["f"] = 0
+    host_src = lambda f: x_host[f]
+    for _ in range(args.warmup):
+        step(host_src, y_host)
+    torch.cuda.synchronize()
+    ms_e2e = timed(host_src, y_host, args.steps)
+    e2e = {"value": world * B * args.steps / (ms_e2e / 1e3), "unit": "frames/s",
+           "h2d_bytes_per_step": B * cfg.d_model * 2, "d2h_bytes_per_step": B * cfg.d_model * 4,
+           "ms_per_step": ms_e2e / args.steps}
+
+    # ---- traced pass: decode-attention launch durations with CUDA events ------------------------
+    kv.set_lengths(streams, prefixes)
+    state["f"] = 0
+    model.set_tracing(True)
+    model.trace(reset=True)
+    traced = min(args.steps + args.warmup, FRAMES)
+    for _ in range(traced):
+        step(dev_src, y)
+    torch.cuda.synchronize()
+    tr = model.trace(reset=True)
+    model.set_tracing(False)
+    peak, peak_kind = peaks()
+    per_launch_bytes = tr["attn_bytes"] / max(tr["attn_launches"], 1)
+    per_launch_ms = tr["attn_ms"] / max(tr["attn_launches"], 1)
+    achieved = per_launch_bytes / (per_launch_ms / 1e3) / 1e9
+    traffic = traffic_per_launch()
+    roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                "frac": achieved / peak, "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"
+                if peak_kind == "measured" else "fallback 6.65 TB/s",
+                "traffic": traffic.get("bytes_per_launch") if traffic else None,
+                "kernel": "decode_attn_kernel<bf16> (split-KV)",
+                "algorithmic_bytes_per_launch": per_launch_bytes,
+                "launch_ms": per_launch_ms, "launches_timed": tr["attn_launches"],
+                "attn_share_of_traced_step": tr["attn_ms"] / max(tr["step_ms"], 1e-9)}
+    if traffic:
+        roofline["traffic_source"] = traffic.get("source")
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cb = cpu_baseline(ptts, wl, cfg, weights)
+        cpu = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "frames/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded random-init int8 weights and N(0,1) hidden rows)",
+            "config": {"workload": "config5 shard: 40m flow LM (9 layers, d 512, 8x64 heads, ff 2048), "
+                                   "512 streams/GPU, prefixes U{32..512}, 250-frame decode window",
+                       "streams_per_gpu": B, "total_streams": world * B, "layers": L,
+                       "kv_capacity": cap, "parallelism": f"stream-sharded x{world}, no collectives",
+                       "l2": "inputs larger than L2: ~3.8 GB of KV read per step per GPU"},
+            "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": gpu_launches,
+            "clocks": clocks, "prefill_ms": prefill_ms,
+            "prefill_rows_per_s": world * float(prefixes.sum()) / (prefill_ms / 1e3),
+        }
+        print(json.dumps(line), flush=True)
+    kv.check()
+    del kv
+    if dist is not None:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=1000)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be at least 3")
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

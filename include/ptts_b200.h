@@ -1,0 +1,222 @@
+/*
+ * ptts_b200 — B200 (sm_100a) kernels for the flow-LM attention path of Phonon TTS
+ * (gradium-ai/xn-ptts), behind a plain C ABI.
+ *
+ * The reference composes this path from `xn` tensor ops inside
+ *   ptts/src/transformer.rs:183-251  StreamingMultiheadAttention::forward
+ *   ptts/src/transformer.rs:591-634  StreamingTransformerLayer::forward
+ *   ptts/src/transformer.rs:742-838  StreamingTransformer::{forward, forward_step}
+ * and keeps its KV cache in StreamingTransformerState (transformer.rs:12-25, 328-393).
+ * This header replaces those with two objects and a handful of calls:
+ *
+ *   ptts_b200_kv     the per-layer K/V caches of many independent streams plus one
+ *                    length per stream (StreamingMHAState::current_end), resident in HBM;
+ *   ptts_b200_model  the flow-LM transformer's weights (int8, one f32 scale per output row).
+ *
+ * Conventions (mirroring ptts-ffi/include/ptts.h:28-52 and ptts-ffi/src/lib.rs:57-71):
+ *   - every call returns an int status: PTTS_B200_OK (0) or a negative PTTS_B200_ERR_*;
+ *   - on failure ptts_b200_last_error() returns a message for the calling thread;
+ *   - no C++ exception crosses this boundary;
+ *   - tensors passed as `const void*` / `void*` are DEVICE pointers unless the parameter name
+ *     ends in `_host`; `cuda_stream` is a cudaStream_t (NULL = the legacy default stream);
+ *   - calls on one object are serialised by the caller (one generation per session, as the
+ *     reference's in-flight guard enforces at ptts/src/synth.rs:958-975).
+ *
+ * Layouts. K/V caches: [num_layers][num_streams][capacity][num_heads][head_dim], the layout of
+ * StreamingMHAState::k_cache per layer (transformer.rs:15-18). Rows of q/k/v or hidden states are
+ * row-major with heads-major, then head_dim, within a row (transformer.rs:197-211).
+ *
+ * Supported shapes: head_dim 64 and num_heads * head_dim = 512 (the 31m/40m flow LMs);
+ * d_model and dim_feedforward multiples of 64; num_kv_heads dividing num_heads.
+ * Others are refused with PTTS_B200_ERR_UNSUPPORTED.
+ */
+#ifndef PTTS_B200_H
+#define PTTS_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define PTTS_B200_OK 0
+#define PTTS_B200_ERR_ARG (-1)         /* a bad argument: NULL, negative, out of range */
+#define PTTS_B200_ERR_CAPACITY (-2)    /* rows do not fit a stream's capacity */
+#define PTTS_B200_ERR_CUDA (-3)        /* a CUDA runtime call failed */
+#define PTTS_B200_ERR_STATE (-4)       /* missing weights, mismatched objects, wrong order */
+#define PTTS_B200_ERR_UNSUPPORTED (-5) /* a shape or type these kernels do not implement */
+#define PTTS_B200_ERR_DEVICE (-6)      /* a kernel's own bounds check or bounded wait tripped */
+
+/* Element types of caches, inputs and outputs. */
+#define PTTS_B200_F32 0
+#define PTTS_B200_BF16 1
+
+typedef struct ptts_b200_kv ptts_b200_kv;
+typedef struct ptts_b200_model ptts_b200_model;
+
+/* Shape of a flow-LM transformer: FlowLMConfig (ptts/src/flow_lm.rs:114-146) and the
+ * transformer arguments of StreamingTransformer::load (transformer.rs:680-717). */
+typedef struct {
+    int32_t d_model;          /* 512 */
+    int32_t num_heads;        /* 8 */
+    int32_t num_kv_heads;     /* 8 (grouped-query attention when smaller) */
+    int32_t head_dim;         /* 64 */
+    int32_t num_layers;       /* 6 (31m) or 9 (40m) */
+    int32_t dim_feedforward;  /* 2048 */
+    float max_period;         /* RoPE theta, 10000 */
+    int32_t gelu;             /* 0: erf (transformer.rs:624), 1: tanh (transformer.rs:500) */
+} ptts_b200_config;
+
+/* One layer's weights, HOST pointers, copied to the device by ptts_b200_model_load_layer.
+ * Linear weights are int8 [out_features][in_features] with one f32 scale per output row:
+ * W = q * scale[row]. Names follow the checkpoint keys (transformer.rs:529-545). */
+typedef struct {
+    const int8_t* in_proj_host;    /* [(H + 2*KVH)*D][d_model], rows [q | k | v] */
+    const float* in_proj_scale_host;
+    const int8_t* out_proj_host;   /* [d_model][H*D] */
+    const float* out_proj_scale_host;
+    const int8_t* linear1_host;    /* [dim_feedforward][d_model] */
+    const float* linear1_scale_host;
+    const int8_t* linear2_host;    /* [d_model][dim_feedforward] */
+    const float* linear2_scale_host;
+    const float* norm1_weight_host; /* [d_model] */
+    const float* norm1_bias_host;
+    const float* norm2_weight_host;
+    const float* norm2_bias_host;
+} ptts_b200_layer_weights;
+
+/* The message of the last failed call on this thread ("" if none). Borrowed until the next
+ * call on this thread. Replaces ptts_last_error (ptts-ffi/include/ptts.h:50). */
+const char* ptts_b200_last_error(void);
+
+/* Library version string, e.g. "ptts_b200 0.1 sm_100a". */
+const char* ptts_b200_version(void);
+
+/* ---------------------------------------------------------------------------------------
+ * KV state: StreamingTransformerState (transformer.rs:328-393) for many streams at once.
+ * ------------------------------------------------------------------------------------- */
+
+/* A zero-filled cache of num_layers x num_streams x capacity slots, every length 0.
+ * Replaces StreamingMultiheadAttention::init_state (transformer.rs:168-179) and
+ * StreamingTransformer::init_state (transformer.rs:731-740). dtype: PTTS_B200_F32 or _BF16. */
+int ptts_b200_kv_create(int device, int num_layers, int num_streams, int capacity, int num_heads,
+                        int head_dim, int dtype, ptts_b200_kv** out);
+void ptts_b200_kv_destroy(ptts_b200_kv* kv);
+
+/* The filled length (current_end) of every stream, from the host-side mirror, no sync. */
+int ptts_b200_kv_lengths(const ptts_b200_kv* kv, int32_t* lengths_host);
+
+/* Device pointers of one layer's K and V caches ([num_streams][capacity][H][D]) and of the
+ * device lengths ([num_streams] int32). Borrowed; valid until ptts_b200_kv_destroy. */
+int ptts_b200_kv_pointers(const ptts_b200_kv* kv, int layer, void** k, void** v,
+                          int32_t** lengths);
+
+/* Count rows[i] more filled positions for stream streams_host[i], on the host mirror and on
+ * the device (stream-ordered). StreamingTransformerState::advance (transformer.rs:334-343). */
+int ptts_b200_kv_advance(ptts_b200_kv* kv, const int32_t* streams_host, const int32_t* rows_host,
+                         int n, void* cuda_stream);
+
+/* Set the lengths of the listed streams (host mirror and device), keeping their slots: rows
+ * past the new length are no longer attended and are overwritten by the next appends. The
+ * reference lowers current_end the same way when it drops rows (transformer.rs:925). */
+int ptts_b200_kv_set_lengths(ptts_b200_kv* kv, const int32_t* streams_host,
+                             const int32_t* lengths_host, int n, void* cuda_stream);
+
+/* Set stream lengths to 0 and zero their slots (a fresh session for those streams). */
+int ptts_b200_kv_reset(ptts_b200_kv* kv, const int32_t* streams_host, int n, void* cuda_stream);
+
+/* Write `len` rows of K and V (device, [len][H][D], the cache dtype) into slots 0..len of one
+ * layer of one stream; with set_length != 0, also set that stream's length to len. The primed
+ * voice prefix, as StepGraph loads it (ptts/src/step_graph.rs:291-307). */
+int ptts_b200_kv_load_prefix(ptts_b200_kv* kv, int layer, int stream, const void* k,
+                             const void* v, int len, int set_length, void* cuda_stream);
+
+/* Copy stream src_stream of `src` into stream dst_stream of `dst` (same layers, heads and
+ * dtype, any capacities): the filled prefix is copied, the rest of dst's slots zeroed, dst's
+ * length set to src's. Refused with PTTS_B200_ERR_CAPACITY, naming both numbers, when the
+ * prefix does not fit. StreamingTransformerState::with_seq_budget (transformer.rs:350-392). */
+int ptts_b200_kv_copy_stream(ptts_b200_kv* dst, int dst_stream, const ptts_b200_kv* src,
+                             int src_stream, void* cuda_stream);
+
+/* Check the device-side error word that kernels set instead of trapping (bounds, capacity,
+ * timeouts of bounded waits). Synchronises the device. Clears the word. */
+int ptts_b200_kv_check(ptts_b200_kv* kv);
+
+/* ---------------------------------------------------------------------------------------
+ * Attention op: the body of StreamingMultiheadAttention::forward after in_proj
+ * (transformer.rs:197-248): GQA repeat, RoPE, append, then causal attention.
+ * ------------------------------------------------------------------------------------- */
+
+/* For n_seq sequences, sequence i on stream streams_host[i] with rows_host[i] rows:
+ * q [n_rows][H][D], k and v [n_rows][KVH][D] (device, in_dtype), rows grouped by sequence in
+ * order. Row j of sequence i sits at position p = length[stream] + j: q and k are rotated at p
+ * (RotaryEmbedding::forward, rope.rs:81-95, interleaved pairs), k and v are written to slot p
+ * of `layer` (complete_kv, transformer.rs:84-91; repeated over the heads sharing a KV head),
+ * and the row attends to keys 0..=p (materialize_causal_mask, transformer.rs:94-108; the
+ * one-row case is sdpa_decode, transformer.rs:229-230). out [n_rows][H*D] in out_dtype.
+ * Lengths are NOT advanced (call ptts_b200_kv_advance after the last layer), as with the
+ * device-position step (transformer.rs:822-838). Capacity is checked on the host first. */
+int ptts_b200_attend(ptts_b200_kv* kv, int layer, const void* q, const void* k, const void* v,
+                     int in_dtype, int num_kv_heads, const int32_t* streams_host,
+                     const int32_t* rows_host, int n_seq, float max_period, void* out,
+                     int out_dtype, void* cuda_stream);
+
+/* ---------------------------------------------------------------------------------------
+ * Quantised linear: Q::LinearQ::forward (transformer.rs:195, :224, :627) for int8 weights with
+ * one f32 scale per output row. y[m][n] = scale[n] * sum_k x[m][k] * w[n][k].
+ * x [m][k] bf16, w [n][k] int8, scale [n] f32, y [m][n] f32; all device pointers.
+ * k and n must be multiples of 64.
+ * ------------------------------------------------------------------------------------- */
+int ptts_b200_linear_i8(int device, const void* x, const int8_t* w, const float* scale, int m,
+                        int n, int k, float* y, void* cuda_stream);
+
+/* ---------------------------------------------------------------------------------------
+ * Model: StreamingTransformer with int8 per-output-channel linears.
+ * ------------------------------------------------------------------------------------- */
+
+/* StreamingTransformer::load (transformer.rs:680-723) minus the file I/O: shapes only, then
+ * ptts_b200_model_load_layer for each layer. Refuses head counts that do not divide
+ * (transformer.rs:699-707). */
+int ptts_b200_model_create(int device, const ptts_b200_config* config, ptts_b200_model** out);
+void ptts_b200_model_destroy(ptts_b200_model* model);
+int ptts_b200_model_load_layer(ptts_b200_model* model, int layer,
+                               const ptts_b200_layer_weights* weights);
+
+/* StreamingTransformer::forward (transformer.rs:742-808) for a ragged batch of independent
+ * streams: x [n_rows][d_model] bf16 (device) -> y [n_rows][d_model] f32 (device); per layer
+ * x += attn(LN1 x); x += W2 GELU(W1 LN2 x). Sequence i is stream streams_host[i] with
+ * rows_host[i] rows (a prompt when > 1, a host-position decode step when 1). Lengths advance
+ * by rows_host[i] at the end. */
+int ptts_b200_forward(ptts_b200_model* model, ptts_b200_kv* kv, const void* x,
+                      const int32_t* streams_host, const int32_t* rows_host, int n_seq, float* y,
+                      void* cuda_stream);
+
+/* StreamingTransformer::forward_step (transformer.rs:822-838) with DeviceStep
+ * (transformer.rs:111-140): one row per stream for a fixed set of streams whose positions
+ * live on the device, replayed as one CUDA graph per stream set. x [n][d_model] bf16 and
+ * y [n][d_model] f32 may be device or pinned-host pointers. Lengths advance by one on the
+ * device and on the host mirror. The first call for a new stream set records the graph. */
+int ptts_b200_step(ptts_b200_model* model, ptts_b200_kv* kv, const int32_t* streams_host, int n,
+                   const void* x, float* y, void* cuda_stream);
+
+/* Tracing, the counterpart of the reference's `attn` / `transformer-layer` spans
+ * (transformer.rs:182, :590): while on, ptts_b200_step runs its kernels outside the CUDA graph
+ * with CUDA events around every decode-attention launch, and synchronises once per step. */
+typedef struct {
+    int64_t steps;            /* traced steps */
+    int64_t attn_launches;    /* decode-attention launches timed */
+    double attn_ms;           /* their summed device time */
+    double attn_bytes;        /* their summed algorithmic bytes: K and V rows read, q read,
+                                 output written */
+    double step_ms;           /* summed device time of the traced steps */
+} ptts_b200_trace;
+
+int ptts_b200_model_set_tracing(ptts_b200_model* model, int on);
+/* Read (and with reset != 0, clear) the counters. */
+int ptts_b200_model_trace(ptts_b200_model* model, ptts_b200_trace* out, int reset);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,268 @@
+"""GPU parity of the attention op (ptts_b200_attend) against the CPU oracle.
+
+Metric: normwise = ||gpu - oracle||_inf / ||oracle||_inf; the bar is 2e-3 (bf16 storage, f32
+accumulation). `mirror` is the oracle rounding to bf16 where the library stores bf16 (the rotated
+q/k/v rows); `f32` is the reference's CPU semantics (no rounding anywhere). Attention outputs are
+compared in f32 (out_dtype f32) so the check sees the kernels, not the output's own rounding.
+Cache indexing and append positions are checked bit-exactly (which slots change).
+"""
+from __future__ import annotations
+
+import json
+import os
+
+import numpy as np
+import pytest
+
+from conftest import GOLDEN, normwise
+
+pytestmark = pytest.mark.gpu
+TOL = 2e-3
+
+
+def _wl(ptts):
+    import importlib.util, sys
+    if "xn_ptts_b200.workloads" in sys.modules:
+        return sys.modules["xn_ptts_b200.workloads"]
+    path = os.path.join(os.path.dirname(ptts.__file__), "workloads.py")
+    spec = importlib.util.spec_from_file_location("xn_ptts_b200.workloads", path)
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules["xn_ptts_b200.workloads"] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def _f32(t):
+    return t.float().cpu().numpy()
+
+
+def test_config1_single_stream_f32_decode_512_steps(ptts, oracle, cuda):
+    """Config 1: f32 cache, batch 1, 512 sequential decode steps (seed 0); every step's output
+    within 1e-5 normwise of the f32 oracle, cache rows within 1e-5 and at the right slots."""
+    import torch
+    steps = _wl(ptts).config1_steps(512, seed=0)
+    kv = ptts.KvState(1, 1, 512, dtype="f32")
+    kc = np.zeros((1, 512, 8, 64), np.float32)
+    vc = np.zeros_like(kc)
+    worst = 0.0
+    outs = []
+    for s, (q, k, v) in enumerate(steps):
+        out = ptts.attend(kv, 0, q.to(cuda), k.to(cuda), v.to(cuda), [0], [1], out_dtype="f32")
+        kv.advance([0], [1])
+        outs.append(out)
+    kv.check()
+    for s, (q, k, v) in enumerate(steps):
+        want = oracle.attend(q.numpy(), k.numpy(), v.numpy(), kc, vc, [s], [0], [0, 1])
+        worst = max(worst, normwise(_f32(outs[s]), want))
+    assert worst < 1e-5, worst
+    kt, vt, lt = kv.tensors(0)
+    assert int(lt[0]) == 512 and kv.lengths()[0] == 512
+    assert normwise(_f32(kt[0]), kc[0]) < 1e-5
+    np.testing.assert_array_equal(_f32(vt[0]), vc[0])
+
+
+def test_config2_prefill_256(ptts, oracle, cuda):
+    """Config 2: one bf16 prompt of 256 rows (seed 1), causal over itself."""
+    q, k, v = _wl(ptts).config2(seed=1)
+    kv = ptts.KvState(1, 1, 256, dtype="bf16")
+    out = ptts.attend(kv, 0, q.to(cuda), k.to(cuda), v.to(cuda), [0], [256], out_dtype="f32")
+    kv.check()
+    got = _f32(out)
+    offs = [0, 256]
+    for store, tol in ((True, TOL), (False, TOL)):
+        kc = np.zeros((1, 256, 8, 64), np.float32)
+        vc = np.zeros_like(kc)
+        want = oracle.attend(_f32(q), _f32(k), _f32(v), kc, vc, [0], [0], offs, store_bf16=store)
+        err = normwise(got, want)
+        assert err < tol, (store, err)
+        if store:
+            kt, vt, _ = kv.tensors(0)
+            assert np.abs(_f32(kt[0]) - kc[0]).max() <= np.abs(kc[0]).max() * 2 ** -7
+            np.testing.assert_array_equal(_f32(vt[0]), vc[0])
+
+
+@pytest.mark.parametrize("steps,B", [(4, 256)])
+def test_config3_ragged_decode(ptts, oracle, cuda, steps, B):
+    """Config 3 (seed 2): 256 streams with prefilled lengths U{64..2048}, bf16 cache, one
+    query per stream per step through the split-KV kernel."""
+    import torch
+    wl = _wl(ptts).config3(B=B, seed=2)
+    cap = int(wl.lengths.max()) + steps
+    kv = ptts.KvState(1, B, cap, dtype="bf16")
+    kc = np.zeros((B, cap, 8, 64), np.float32)
+    vc = np.zeros_like(kc)
+    for s in range(B):
+        L = int(wl.lengths[s])
+        kv.load_prefix(0, s, wl.prefix_k[s].to(cuda), wl.prefix_v[s].to(cuda))
+        kc[s, :L] = _f32(wl.prefix_k[s])
+        vc[s, :L] = _f32(wl.prefix_v[s])
+    np.testing.assert_array_equal(kv.lengths(), wl.lengths)
+    streams = np.arange(B, dtype=np.int32)
+    lengths = wl.lengths.copy()
+    worst = {True: 0.0, False: 0.0}
+    kc32, vc32 = kc.copy(), vc.copy()
+    for q, k, v in wl.steps(steps):
+        out = ptts.attend(kv, 0, q.to(cuda), k.to(cuda), v.to(cuda), streams, np.ones(B, np.int32))
+        kv.advance(streams, np.ones(B, np.int32))
+        got = _f32(out)
+        offs = np.arange(B + 1, dtype=np.int32)
+        want = oracle.attend(_f32(q), _f32(k), _f32(v), kc, vc, lengths, streams, offs, store_bf16=True)
+        want32 = oracle.attend(_f32(q), _f32(k), _f32(v), kc32, vc32, lengths, streams, offs)
+        worst[True] = max(worst[True], normwise(got, want))
+        worst[False] = max(worst[False], normwise(got, want32))
+        lengths += 1
+    kv.check()
+    print("config3 normwise mirror/f32:", worst)
+    assert worst[True] < TOL and worst[False] < TOL, worst
+    np.testing.assert_array_equal(kv.lengths(), lengths)
+
+
+def test_split_kv_partition_edges(ptts, oracle, cuda):
+    """Streams that are cut by CTA ranges, tiny streams (length 0 before the append), one long
+    stream among short ones, and a subset of the arena's streams in shuffled order."""
+    import torch
+    rng = np.random.default_rng(11)
+    S, cap = 40, 3000
+    lengths = np.array([0, 1, 2, 31, 32, 33, 2999, 7] + list(rng.integers(0, 200, S - 8)), np.int32)
+    kv = ptts.KvState(1, S, cap, dtype="bf16")
+    kc = np.zeros((S, cap, 8, 64), np.float32)
+    vc = np.zeros_like(kc)
+    for s in range(S):
+        L = int(lengths[s])
+        if L:
+            k = torch.randn(L, 8, 64).bfloat16()
+            v = torch.randn(L, 8, 64).bfloat16()
+            kv.load_prefix(0, s, k.to(cuda), v.to(cuda))
+            kc[s, :L], vc[s, :L] = _f32(k), _f32(v)
+        else:
+            kv.load_prefix(0, s, None, None)
+    streams = rng.permutation(S)[:29].astype(np.int32)
+    B = len(streams)
+    q, k, v = (torch.randn(B, 8, 64).bfloat16() for _ in range(3))
+    for out_dtype in ("f32", "bf16"):
+        kv2_k, kv2_v = kc.copy(), vc.copy()
+        out = ptts.attend(kv, 0, q.to(cuda), k.to(cuda), v.to(cuda), streams, np.ones(B, np.int32),
+                          out_dtype=out_dtype)
+        want = oracle.attend(_f32(q), _f32(k), _f32(v), kv2_k, kv2_v, lengths, streams,
+                             np.arange(B + 1, dtype=np.int32), store_bf16=True)
+        tol = TOL if out_dtype == "f32" else TOL + 2 ** -8
+        assert normwise(_f32(out), want) < tol, out_dtype
+    kv.check()
+
+
+def test_gqa_is_attention_with_repeated_kv_heads(ptts, cuda):
+    """transformer.rs:1112-1164 on the device: 2 KV heads shared by 8 query heads give the
+    same outputs and cache as the 8 heads repeated, over a prompt and two single steps."""
+    import torch
+    torch.manual_seed(5)
+    x = [(torch.randn(t, 8, 64), torch.randn(t, 2, 64), torch.randn(t, 2, 64)) for t in (3, 1, 1)]
+    outs = {}
+    for mode in ("grouped", "repeated"):
+        kv = ptts.KvState(1, 1, 8, dtype="f32")
+        res = []
+        for q, k, v in x:
+            if mode == "repeated":
+                k, v = k.repeat_interleave(4, dim=1), v.repeat_interleave(4, dim=1)
+            res.append(_f32(ptts.attend(kv, 0, q.to(cuda), k.contiguous().to(cuda), v.contiguous().to(cuda),
+                                        [0], [q.shape[0]])))
+            kv.advance([0], [q.shape[0]])
+        outs[mode] = (np.concatenate(res), _f32(kv.tensors(0)[0]))
+    np.testing.assert_array_equal(outs["grouped"][0], outs["repeated"][0])
+    np.testing.assert_array_equal(outs["grouped"][1], outs["repeated"][1])
+
+
+def test_append_positions_are_exact_and_nothing_else_is_read(ptts, oracle, cuda):
+    """complete_kv (transformer.rs:84-91): rows land at slots len..len+t of their stream only;
+    slots past the new length hold NaN poison that attention must never read."""
+    import torch
+    S, cap = 3, 64
+    kv = ptts.KvState(1, S, cap, dtype="bf16")
+    poison_k = torch.full((cap, 8, 64), float("nan")).bfloat16().to(cuda)
+    base = torch.randn(cap, 8, 64).bfloat16()
+    lens = [5, 0, 20]
+    for s in range(S):
+        kv.load_prefix(0, s, poison_k, poison_k, set_length=False)
+        if lens[s]:
+            kv.load_prefix(0, s, base[: lens[s]].to(cuda), base[: lens[s]].to(cuda))
+        else:
+            kv.load_prefix(0, s, None, None)
+    streams, rows = [2, 0, 1], [1, 6, 3]
+    n = sum(rows)
+    q, k, v = (torch.randn(n, 8, 64).bfloat16() for _ in range(3))
+    out = ptts.attend(kv, 0, q.to(cuda), k.to(cuda), v.to(cuda), streams, rows)
+    kv.check()
+    assert np.isfinite(_f32(out)).all()
+    kt = _f32(kv.tensors(0)[0])
+    filled = {0: 5 + 6, 1: 0 + 3, 2: 20 + 1}
+    for s in range(S):
+        assert np.isfinite(kt[s, : filled[s]]).all(), s
+        assert np.isnan(kt[s, filled[s]:]).all(), s
+    # Positions: stream 0's six rows are slots 5..10 and carry the rows 1..6 of the batch.
+    kc = np.zeros((S, cap, 8, 64), np.float32)
+    vc = np.zeros_like(kc)
+    for s in range(S):
+        kc[s, : lens[s]] = _f32(base[: lens[s]])
+        vc[s, : lens[s]] = _f32(base[: lens[s]])
+    want = oracle.attend(_f32(q), _f32(k), _f32(v), kc, vc, lens, streams, [0, 1, 7, 10], store_bf16=True)
+    assert normwise(_f32(out), want) < TOL
+    vt = _f32(kv.tensors(0)[1])
+    for s in range(S):
+        np.testing.assert_array_equal(vt[s, : filled[s]], vc[s, : filled[s]])
+
+
+def test_capacity_overflow_is_refused_and_changes_nothing(ptts, cuda):
+    import torch
+    kv = ptts.KvState(1, 2, 4, dtype="bf16")
+    q = torch.randn(5, 8, 64).bfloat16().to(cuda)
+    with pytest.raises(ptts.CapacityError) as e:
+        ptts.attend(kv, 0, q, q, q, [1], [5])
+    assert "5" in e.value.msg and "4" in e.value.msg
+    np.testing.assert_array_equal(kv.lengths(), [0, 0])
+    with pytest.raises(ptts.PttsError):
+        ptts.attend(kv, 0, q[:2], q[:2], q[:2], [0, 0], [1, 1])  # a stream twice
+    with pytest.raises(ptts.PttsError):
+        ptts.attend(kv, 0, q[:1], q[:1], q[:1], [2], [1])  # no such stream
+
+
+def test_with_seq_budget_known_answers(ptts, cuda):
+    """transformer.rs:1022-1100 with the test's pattern k[s, h, d] = s + 100 h (v = -k) on the
+    library's cache shape: prefix copied, tail zeroed, no shared storage, refusal naming both
+    numbers, an equal budget accepted."""
+    import torch
+    g = json.load(open(os.path.join(GOLDEN, "with_seq_budget.json")))
+    for c in g["cases"]:
+        seq, used, budget = c["seq"], c["used"], c["budget"]
+        pat = torch.zeros(seq, 8, 64)
+        for s in range(seq):
+            for h in range(8):
+                pat[s, h] = s + 100 * h
+        src = ptts.KvState(1, 1, seq, dtype="f32")
+        src.load_prefix(0, 0, pat.to(cuda), (-pat).to(cuda), set_length=False)
+        src.load_prefix(0, 0, pat[:used].contiguous().to(cuda), (-pat[:used]).contiguous().to(cuda))
+        if c["refused"]:
+            with pytest.raises(ptts.CapacityError) as e:
+                src.with_seq_budget(budget)
+            assert str(used) in e.value.msg and str(budget) in e.value.msg
+            continue
+        dst = src.with_seq_budget(budget)
+        assert dst.lengths()[0] == used
+        k = _f32(dst.tensors(0)[0])[0]
+        want = np.zeros((budget, 8, 64), np.float32)
+        want[:used] = pat[:used].numpy()
+        np.testing.assert_array_equal(k, want)
+        np.testing.assert_array_equal(_f32(dst.tensors(0)[1])[0], -want)
+        # No shared storage: poisoning the copy leaves the source alone.
+        dst.load_prefix(0, 0, torch.full((1, 8, 64), 9e9).to(cuda), torch.zeros(1, 8, 64).to(cuda), set_length=False)
+        assert _f32(src.tensors(0)[0])[0, 0, 1, 0] == 100.0
+
+
+def test_linear_i8_matches_the_oracle(ptts, oracle, cuda):
+    import torch
+    rng = np.random.default_rng(7)
+    for m, n, k in ((1, 64, 64), (100, 1536, 512), (64, 512, 2048), (129, 2048, 512)):
+        x = torch.from_numpy(rng.normal(size=(m, k)).astype(np.float32)).bfloat16()
+        w = rng.integers(-127, 128, size=(n, k), dtype=np.int8)
+        s = rng.uniform(0.005, 0.02, n).astype(np.float32)
+        y = ptts.linear_i8(x.to(cuda), torch.from_numpy(w).to(cuda), torch.from_numpy(s).to(cuda))
+        want = oracle.linear_i8(_f32(x), w, s)
+        assert normwise(_f32(y), want) < 1e-5, (m, n, k)

@@ -1,0 +1,129 @@
+"""GPU parity of the whole flow-LM stack (ptts_b200_forward / ptts_b200_step) against the
+oracle's StreamingTransformer::forward restatement.
+
+Hidden states are the f32 residual stream after the last layer (per frame). The oracle runs in
+`mirror` mode (bf16 at the library's storage points: rotated q/k/v, normalised GEMM inputs, the
+attention output and the GELU output). Metric: ||gpu - oracle||_inf / ||oracle||_inf <= 2e-3.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from conftest import normwise
+
+pytestmark = pytest.mark.gpu
+TOL = 2e-3
+
+
+def _f32(t):
+    return t.float().cpu().numpy()
+
+
+def _setup(ptts, oracle, cfg, seed, S, cap, cuda):
+    w = ptts.random_weights(cfg, seed)
+    model = ptts.Transformer(cfg)
+    model.load(w)
+    om = oracle.Model(cfg, w)
+    kv = ptts.KvState(cfg.num_layers, S, cap, dtype="bf16")
+    shape = (cfg.num_layers, S, cap, cfg.num_heads, cfg.head_dim)
+    return model, om, kv, np.zeros(shape, np.float32), np.zeros(shape, np.float32)
+
+
+def test_prefill_then_decode_matches_the_oracle(ptts, oracle, cuda):
+    """Ragged prompts (host path, t > 1) then host-position decode steps (t = 1), 31m shape."""
+    import torch
+    cfg = ptts.PHONON_31M
+    S, cap = 6, 96
+    model, om, kv, kc, vc = _setup(ptts, oracle, cfg, 3, S, cap, cuda)
+    rows = [17, 40, 1, 33, 8, 25]
+    streams = [4, 0, 5, 2, 1, 3]
+    offs = np.concatenate([[0], np.cumsum(rows)]).astype(np.int32)
+    x = torch.randn(int(offs[-1]), 512).bfloat16()
+    y = model.forward(kv, x.to(cuda), streams, rows)
+    kv.check()
+    lengths = np.zeros(S, np.int32)
+    want = om.forward(_f32(x), kc, vc, lengths, streams, offs, store_bf16=True)
+    err = normwise(_f32(y), want)
+    print("prefill normwise:", err)
+    assert err < TOL
+    for i, s in enumerate(streams):
+        lengths[s] += rows[i]
+    np.testing.assert_array_equal(kv.lengths(), lengths)
+    worst = 0.0
+    for frame in range(4):
+        xs = torch.randn(S, 512).bfloat16()
+        order = list(range(S))
+        y = model.forward(kv, xs.to(cuda), order, [1] * S)
+        want = om.forward(_f32(xs), kc, vc, lengths, order, np.arange(S + 1, dtype=np.int32), store_bf16=True)
+        lengths += 1
+        worst = max(worst, normwise(_f32(y), want))
+    kv.check()
+    print("decode normwise:", worst)
+    assert worst < TOL
+    for l in range(cfg.num_layers):
+        kt, vt, _ = kv.tensors(l)
+        for s in range(S):
+            n = lengths[s]
+            assert (_f32(kt[s, n:]) == 0).all() and (_f32(vt[s, n:]) == 0).all()
+            d = np.abs(_f32(kt[s, :n]) - kc[l, s, :n]).max() / max(np.abs(kc[l, s, :n]).max(), 1e-30)
+            assert d < 0.05, (l, s, d)
+
+
+def test_a_device_step_is_the_host_step(ptts, cuda):
+    """transformer.rs:1169-1225: the graph-replayed step (positions on the device) gives the
+    host step's output and cache, frame after frame."""
+    import torch
+    cfg = ptts.FlowLMConfig(num_layers=3)
+    w = ptts.random_weights(cfg, 9)
+    model = ptts.Transformer(cfg)
+    model.load(w)
+    S, cap = 5, 40
+    kvs = [ptts.KvState(cfg.num_layers, S, cap, dtype="bf16") for _ in range(2)]
+    prompt = torch.randn(3 * S, 512).bfloat16().to(cuda)
+    for kv in kvs:
+        model.forward(kv, prompt, list(range(S)), [3] * S)
+    streams = [3, 1, 4]
+    for frame in range(5):
+        x = torch.randn(len(streams), 512).bfloat16().to(cuda)
+        host = model.forward(kvs[0], x, streams, [1] * len(streams))
+        dev = model.step(kvs[1], streams, x)
+        torch.cuda.synchronize()
+        np.testing.assert_array_equal(_f32(dev), _f32(host))
+    np.testing.assert_array_equal(kvs[0].lengths(), kvs[1].lengths())
+    for l in range(cfg.num_layers):
+        np.testing.assert_array_equal(_f32(kvs[0].tensors(l)[0]), _f32(kvs[1].tensors(l)[0]))
+    # The device lengths match the host mirror.
+    np.testing.assert_array_equal(_f32(kvs[1].tensors(0)[2]).astype(np.int32), kvs[1].lengths())
+    # A step past the capacity is refused on the host.
+    full = ptts.KvState(cfg.num_layers, 1, 1, dtype="bf16")
+    model.step(full, [0], torch.randn(1, 512).bfloat16().to(cuda))
+    with pytest.raises(ptts.CapacityError):
+        model.step(full, [0], torch.randn(1, 512).bfloat16().to(cuda))
+
+
+def test_config4_decode_frames(ptts, oracle, cuda):
+    """Config 4 (seed 3) shortened to 12 frames: 31m shape, 64 streams, prefix 128, per-frame
+    hidden states of the device step against the oracle."""
+    import torch
+    cfg = ptts.PHONON_31M
+    B, prefix, frames = 64, 128, 12
+    model, om, kv, kc, vc = _setup(ptts, oracle, cfg, 3, B, prefix + frames, cuda)
+    g = torch.Generator().manual_seed(3)
+    x = torch.randn(B * prefix, 512, generator=g).bfloat16()
+    streams = list(range(B))
+    offs = np.arange(0, B * prefix + 1, prefix, dtype=np.int32)
+    model.forward(kv, x.to(cuda), streams, [prefix] * B)
+    lengths = np.zeros(B, np.int32)
+    om.forward(_f32(x), kc, vc, lengths, streams, offs, store_bf16=True)
+    lengths += prefix
+    errs = []
+    for f in range(frames):
+        xs = torch.randn(B, 512, generator=g).bfloat16()
+        y = model.step(kv, streams, xs.to(cuda))
+        want = om.forward(_f32(xs), kc, vc, lengths, streams, np.arange(B + 1, dtype=np.int32), store_bf16=True)
+        lengths += 1
+        errs.append(normwise(_f32(y), want))
+    kv.check()
+    print("config4 per-frame normwise:", ["%.2e" % e for e in errs])
+    assert max(errs) < TOL

@@ -1,0 +1,470 @@
+"""ptts_b200: the flow-LM attention path of Phonon TTS on B200, driven from Python.
+
+A thin mirror, over the C ABI of ``include/ptts_b200.h`` (ctypes), of the reference's operator
+surface for this path:
+
+    KvState       StreamingTransformerState (ptts/src/transformer.rs:328-393)
+    attend        StreamingMultiheadAttention::forward after in_proj (transformer.rs:197-248)
+    linear_i8     Q::LinearQ::forward with int8 per-output-channel weights
+    Transformer   StreamingTransformer::{forward, forward_step} (transformer.rs:742-838)
+
+Device tensors are torch tensors (torch supplies memory, streams and torch.distributed; the
+arithmetic runs in libptts_b200.so). There is no CPU fallback: without the built library or
+without a CUDA device every call raises.
+
+The package directory is ``xn-ptts_b200``; the hyphen keeps it out of ``import``, so load it by
+path (``__graft_entry__.load_package()`` registers it as ``xn_ptts_b200``).
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from dataclasses import dataclass, field
+from typing import Optional, Sequence
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libptts_b200.so")
+
+OK = 0
+ERR_ARG, ERR_CAPACITY, ERR_CUDA, ERR_STATE, ERR_UNSUPPORTED, ERR_DEVICE = -1, -2, -3, -4, -5, -6
+F32, BF16 = 0, 1
+_DTYPES = {"f32": F32, "float32": F32, "bf16": BF16, "bfloat16": BF16}
+
+# Every symbol include/ptts_b200.h declares.
+EXPORTS = (
+    "ptts_b200_last_error", "ptts_b200_version",
+    "ptts_b200_kv_create", "ptts_b200_kv_destroy", "ptts_b200_kv_lengths",
+    "ptts_b200_kv_pointers", "ptts_b200_kv_advance", "ptts_b200_kv_reset",
+    "ptts_b200_kv_set_lengths", "ptts_b200_model_set_tracing", "ptts_b200_model_trace",
+    "ptts_b200_kv_load_prefix", "ptts_b200_kv_copy_stream", "ptts_b200_kv_check",
+    "ptts_b200_attend", "ptts_b200_linear_i8",
+    "ptts_b200_model_create", "ptts_b200_model_destroy", "ptts_b200_model_load_layer",
+    "ptts_b200_forward", "ptts_b200_step",
+)
+
+
+class PttsError(RuntimeError):
+    """A failed ptts_b200 call: `code` is the PTTS_B200_ERR_* status."""
+
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"[{code}] {msg}")
+        self.code = code
+        self.msg = msg
+
+
+class CapacityError(PttsError):
+    pass
+
+
+P, I, F = ctypes.c_void_p, ctypes.c_int, ctypes.c_float
+IP = ctypes.POINTER(ctypes.c_int32)
+
+
+class Config(ctypes.Structure):
+    """ptts_b200_config: FlowLMConfig's transformer shape (ptts/src/flow_lm.rs:114-146)."""
+    _fields_ = [("d_model", ctypes.c_int32), ("num_heads", ctypes.c_int32),
+                ("num_kv_heads", ctypes.c_int32), ("head_dim", ctypes.c_int32),
+                ("num_layers", ctypes.c_int32), ("dim_feedforward", ctypes.c_int32),
+                ("max_period", ctypes.c_float), ("gelu", ctypes.c_int32)]
+
+
+class Trace(ctypes.Structure):
+    """ptts_b200_trace: counters of traced steps (see Transformer.set_tracing)."""
+    _fields_ = [("steps", ctypes.c_int64), ("attn_launches", ctypes.c_int64),
+                ("attn_ms", ctypes.c_double), ("attn_bytes", ctypes.c_double),
+                ("step_ms", ctypes.c_double)]
+
+
+class LayerWeights(ctypes.Structure):
+    _fields_ = [(n, P) for n in (
+        "in_proj_host", "in_proj_scale_host", "out_proj_host", "out_proj_scale_host",
+        "linear1_host", "linear1_scale_host", "linear2_host", "linear2_scale_host",
+        "norm1_weight_host", "norm1_bias_host", "norm2_weight_host", "norm2_bias_host")]
+
+
+_lib = None
+
+
+def build(verbose: bool = False) -> str:
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("_ptts_b200_build", os.path.join(HERE, "build.py"))
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod.build(verbose=verbose)
+
+
+def lib() -> ctypes.CDLL:
+    """The loaded C library. Raises when it has not been built: there is no fallback."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise PttsError(ERR_STATE, f"{LIB_PATH} is missing: build it (python xn-ptts_b200/build.py)")
+        L = ctypes.CDLL(LIB_PATH)
+        L.ptts_b200_last_error.restype = ctypes.c_char_p
+        L.ptts_b200_version.restype = ctypes.c_char_p
+        L.ptts_b200_kv_create.argtypes = [I, I, I, I, I, I, I, ctypes.POINTER(P)]
+        L.ptts_b200_kv_destroy.argtypes = [P]
+        L.ptts_b200_kv_destroy.restype = None
+        L.ptts_b200_kv_lengths.argtypes = [P, IP]
+        L.ptts_b200_kv_pointers.argtypes = [P, I, ctypes.POINTER(P), ctypes.POINTER(P), ctypes.POINTER(P)]
+        L.ptts_b200_kv_advance.argtypes = [P, IP, IP, I, P]
+        L.ptts_b200_kv_reset.argtypes = [P, IP, I, P]
+        L.ptts_b200_kv_set_lengths.argtypes = [P, IP, IP, I, P]
+        L.ptts_b200_model_set_tracing.argtypes = [P, I]
+        L.ptts_b200_model_trace.argtypes = [P, ctypes.POINTER(Trace), I]
+        L.ptts_b200_kv_load_prefix.argtypes = [P, I, I, P, P, I, I, P]
+        L.ptts_b200_kv_copy_stream.argtypes = [P, I, P, I, P]
+        L.ptts_b200_kv_check.argtypes = [P]
+        L.ptts_b200_attend.argtypes = [P, I, P, P, P, I, I, IP, IP, I, F, P, I, P]
+        L.ptts_b200_linear_i8.argtypes = [I, P, P, P, I, I, I, P, P]
+        L.ptts_b200_model_create.argtypes = [I, ctypes.POINTER(Config), ctypes.POINTER(P)]
+        L.ptts_b200_model_destroy.argtypes = [P]
+        L.ptts_b200_model_destroy.restype = None
+        L.ptts_b200_model_load_layer.argtypes = [P, I, ctypes.POINTER(LayerWeights)]
+        L.ptts_b200_forward.argtypes = [P, P, P, IP, IP, I, P, P]
+        L.ptts_b200_step.argtypes = [P, P, IP, I, P, P, P]
+        _lib = L
+    return _lib
+
+
+def version() -> str:
+    return lib().ptts_b200_version().decode()
+
+
+def _check(rc: int):
+    if rc != OK:
+        msg = lib().ptts_b200_last_error().decode(errors="replace")
+        if rc == ERR_CAPACITY:
+            raise CapacityError(rc, msg)
+        raise PttsError(rc, msg)
+
+
+def _i32(a) -> np.ndarray:
+    return np.ascontiguousarray(np.asarray(a, dtype=np.int32))
+
+
+def _ip(a: np.ndarray):
+    return a.ctypes.data_as(IP)
+
+
+def _stream(stream=None) -> ctypes.c_void_p:
+    import torch
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return ctypes.c_void_p(s.cuda_stream)
+
+
+def _dptr(t) -> ctypes.c_void_p:
+    if not t.is_cuda:
+        raise PttsError(ERR_ARG, "expected a CUDA tensor")
+    if not t.is_contiguous():
+        raise PttsError(ERR_ARG, "expected a contiguous tensor")
+    return ctypes.c_void_p(t.data_ptr())
+
+
+def _dtype_code(t) -> int:
+    import torch
+    if t.dtype == torch.bfloat16:
+        return BF16
+    if t.dtype == torch.float32:
+        return F32
+    raise PttsError(ERR_ARG, f"unsupported dtype {t.dtype}")
+
+
+class _Cai:
+    """A raw device buffer exposed through __cuda_array_interface__ (for torch.as_tensor)."""
+
+    def __init__(self, ptr: int, shape, typestr: str):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr,
+                                         "data": (ptr, False), "version": 3, "strides": None}
+
+
+# --------------------------------------------------------------------------------------------
+# KV state
+# --------------------------------------------------------------------------------------------
+
+class KvState:
+    """Per-layer K/V caches of `num_streams` independent streams, `capacity` slots each, plus
+    one filled length per stream: StreamingTransformerState (transformer.rs:328-393) for a
+    whole batch. ``init_state`` there is this constructor (zero caches, lengths 0)."""
+
+    def __init__(self, num_layers: int, num_streams: int, capacity: int, *, num_heads: int = 8,
+                 head_dim: int = 64, dtype: str = "bf16", device: int = 0):
+        self.num_layers, self.num_streams, self.capacity = num_layers, num_streams, capacity
+        self.num_heads, self.head_dim, self.device = num_heads, head_dim, device
+        self.dtype = dtype
+        h = P()
+        _check(lib().ptts_b200_kv_create(device, num_layers, num_streams, capacity, num_heads,
+                                          head_dim, _DTYPES[dtype], ctypes.byref(h)))
+        self._h = h
+
+    def close(self):
+        if getattr(self, "_h", None):
+            lib().ptts_b200_kv_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    @property
+    def handle(self):
+        return self._h
+
+    def lengths(self) -> np.ndarray:
+        out = np.zeros(self.num_streams, np.int32)
+        _check(lib().ptts_b200_kv_lengths(self._h, _ip(out)))
+        return out
+
+    def advance(self, streams: Sequence[int], rows: Sequence[int], stream=None):
+        s, r = _i32(streams), _i32(rows)
+        _check(lib().ptts_b200_kv_advance(self._h, _ip(s), _ip(r), len(s), _stream(stream)))
+
+    def reset(self, streams: Sequence[int], stream=None):
+        s = _i32(streams)
+        _check(lib().ptts_b200_kv_reset(self._h, _ip(s), len(s), _stream(stream)))
+
+    def set_lengths(self, streams: Sequence[int], lengths: Sequence[int], stream=None):
+        """Lower (or raise, up to capacity) stream lengths, keeping the slots."""
+        s, n = _i32(streams), _i32(lengths)
+        _check(lib().ptts_b200_kv_set_lengths(self._h, _ip(s), _ip(n), len(s), _stream(stream)))
+
+    def pointers(self, layer: int):
+        k, v, ln = P(), P(), P()
+        _check(lib().ptts_b200_kv_pointers(self._h, layer, ctypes.byref(k), ctypes.byref(v),
+                                            ctypes.byref(ln)))
+        return k.value, v.value, ln.value
+
+    def tensors(self, layer: int):
+        """Views (torch, no copy) of one layer's K and V caches [S, cap, H, D] and the device
+        lengths [S]."""
+        import torch
+        k, v, ln = self.pointers(layer)
+        shape = (self.num_streams, self.capacity, self.num_heads, self.head_dim)
+        if self.dtype == "bf16":
+            kt = torch.as_tensor(_Cai(k, shape, "<i2"), device=f"cuda:{self.device}").view(torch.bfloat16)
+            vt = torch.as_tensor(_Cai(v, shape, "<i2"), device=f"cuda:{self.device}").view(torch.bfloat16)
+        else:
+            kt = torch.as_tensor(_Cai(k, shape, "<f4"), device=f"cuda:{self.device}")
+            vt = torch.as_tensor(_Cai(v, shape, "<f4"), device=f"cuda:{self.device}")
+        lt = torch.as_tensor(_Cai(ln, (self.num_streams,), "<i4"), device=f"cuda:{self.device}")
+        return kt, vt, lt
+
+    def load_prefix(self, layer: int, stream: int, k, v, set_length: bool = True, cuda_stream=None):
+        """Rows [len, H, D] (device tensors of the cache dtype) into slots 0..len."""
+        n = 0 if k is None else int(k.shape[0])
+        kp = _dptr(k) if n else None
+        vp = _dptr(v) if n else None
+        _check(lib().ptts_b200_kv_load_prefix(self._h, layer, stream, kp, vp, n, int(set_length),
+                                               _stream(cuda_stream)))
+
+    def copy_stream(self, dst_stream: int, src: "KvState", src_stream: int, cuda_stream=None):
+        _check(lib().ptts_b200_kv_copy_stream(self._h, dst_stream, src._h, src_stream,
+                                               _stream(cuda_stream)))
+
+    def with_seq_budget(self, seq_budget: int, streams: Optional[Sequence[int]] = None) -> "KvState":
+        """A fresh state with room for `seq_budget` positions per stream, holding a copy of each
+        stream's filled prefix (transformer.rs:350-392). Refused (CapacityError naming both
+        numbers) when a prefix does not fit."""
+        streams = range(self.num_streams) if streams is None else streams
+        lens = self.lengths()
+        for s in streams:
+            if lens[s] > seq_budget:
+                raise CapacityError(ERR_CAPACITY, f"cannot fit {lens[s]} filled KV positions into a budget of {seq_budget}")
+        out = KvState(self.num_layers, self.num_streams, seq_budget, num_heads=self.num_heads,
+                      head_dim=self.head_dim, dtype=self.dtype, device=self.device)
+        for s in streams:
+            out.copy_stream(s, self, s)
+        return out
+
+    def check(self):
+        """Raise if a kernel's own bounds check or bounded wait tripped (synchronises)."""
+        _check(lib().ptts_b200_kv_check(self._h))
+
+
+# --------------------------------------------------------------------------------------------
+# ops
+# --------------------------------------------------------------------------------------------
+
+def attend(kv: KvState, layer: int, q, k, v, streams: Sequence[int], rows: Sequence[int], *,
+           max_period: float = 10000.0, out_dtype: str = "f32", out=None, stream=None):
+    """RoPE + KV append + causal attention for a ragged batch of streams (see ptts_b200_attend).
+
+    q [n_rows, H, D], k/v [n_rows, KVH, D] (CUDA, bf16 or f32, same dtype), rows grouped by
+    sequence. Returns out [n_rows, H*D]. Lengths are not advanced (KvState.advance)."""
+    import torch
+    if q.dtype != k.dtype or q.dtype != v.dtype:
+        raise PttsError(ERR_ARG, "q, k and v must share a dtype")
+    s, r = _i32(streams), _i32(rows)
+    n_rows = int(q.shape[0])
+    if out is None:
+        out = torch.empty((n_rows, q.shape[1] * q.shape[2]),
+                          dtype=torch.bfloat16 if out_dtype == "bf16" else torch.float32,
+                          device=q.device)
+    _check(lib().ptts_b200_attend(kv.handle, layer, _dptr(q), _dptr(k), _dptr(v), _dtype_code(q),
+                                  int(k.shape[1]), _ip(s), _ip(r), len(s), max_period, _dptr(out),
+                                  _dtype_code(out), _stream(stream)))
+    return out
+
+
+def linear_i8(x, w, scale, stream=None):
+    """y = x W^T with W = w * scale[:, None]: x [m, k] bf16, w [n, k] int8, scale [n] f32."""
+    import torch
+    m, k = x.shape
+    n = w.shape[0]
+    y = torch.empty((m, n), dtype=torch.float32, device=x.device)
+    _check(lib().ptts_b200_linear_i8(x.device.index or 0, _dptr(x), _dptr(w), _dptr(scale), m, n,
+                                     k, _dptr(y), _stream(stream)))
+    return y
+
+
+# --------------------------------------------------------------------------------------------
+# transformer
+# --------------------------------------------------------------------------------------------
+
+@dataclass
+class FlowLMConfig:
+    """The flow LM's transformer shape (FlowLMConfig, ptts/src/flow_lm.rs:114-146)."""
+    d_model: int = 512
+    num_heads: int = 8
+    num_kv_heads: int = 8
+    head_dim: int = 64
+    num_layers: int = 6
+    dim_feedforward: int = 2048
+    max_period: float = 10000.0
+    gelu: str = "erf"
+    scale_group: int = 0  # 0: one scale per output row (the only form the GPU path takes)
+
+    def c_struct(self) -> Config:
+        return Config(self.d_model, self.num_heads, self.num_kv_heads, self.head_dim,
+                      self.num_layers, self.dim_feedforward, self.max_period,
+                      1 if self.gelu == "tanh" else 0)
+
+
+# The 31m and 40m flow LMs: 512 wide, 8 heads, ff 2048, theta 10000; 6 vs 9 layers.
+PHONON_31M = FlowLMConfig(num_layers=6)
+PHONON_40M = FlowLMConfig(num_layers=9)
+
+
+class Transformer:
+    """StreamingTransformer (transformer.rs:674-930) for the flow LM, int8 per-channel."""
+
+    def __init__(self, cfg: FlowLMConfig, device: int = 0):
+        self.cfg, self.device = cfg, device
+        h = P()
+        st = cfg.c_struct()
+        _check(lib().ptts_b200_model_create(device, ctypes.byref(st), ctypes.byref(h)))
+        self._h = h
+
+    def close(self):
+        if getattr(self, "_h", None):
+            lib().ptts_b200_model_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def load_layer(self, layer: int, w: dict):
+        """w: numpy arrays keyed like the checkpoint (in_proj, in_proj_scale, out_proj, ...,
+        norm1_weight, norm1_bias, norm2_weight, norm2_bias)."""
+        keep = {k: np.ascontiguousarray(v) for k, v in w.items()}
+        lw = LayerWeights(*[keep[n].ctypes.data_as(P) for n in (
+            "in_proj", "in_proj_scale", "out_proj", "out_proj_scale", "linear1", "linear1_scale",
+            "linear2", "linear2_scale", "norm1_weight", "norm1_bias", "norm2_weight", "norm2_bias")])
+        _check(lib().ptts_b200_model_load_layer(self._h, layer, ctypes.byref(lw)))
+
+    def load(self, weights: "Weights"):
+        for l in range(self.cfg.num_layers):
+            self.load_layer(l, weights.layer(l))
+
+    def forward(self, kv: KvState, x, streams: Sequence[int], rows: Sequence[int], *, out=None,
+                stream=None):
+        """StreamingTransformer::forward: x [n_rows, d] bf16 -> [n_rows, d] f32; lengths advance."""
+        import torch
+        s, r = _i32(streams), _i32(rows)
+        if out is None:
+            out = torch.empty((x.shape[0], self.cfg.d_model), dtype=torch.float32, device=x.device)
+        _check(lib().ptts_b200_forward(self._h, kv.handle, _dptr(x), _ip(s), _ip(r), len(s),
+                                       _dptr(out), _stream(stream)))
+        return out
+
+    def set_tracing(self, on: bool):
+        """While on, step() times every decode-attention launch with CUDA events (un-graphed,
+        one synchronisation per step); read the counters with trace()."""
+        _check(lib().ptts_b200_model_set_tracing(self._h, int(on)))
+
+    def trace(self, reset: bool = False) -> dict:
+        t = Trace()
+        _check(lib().ptts_b200_model_trace(self._h, ctypes.byref(t), int(reset)))
+        return {n: getattr(t, n) for n, _ in Trace._fields_}
+
+    def step(self, kv: KvState, streams: Sequence[int], x, *, out=None, stream=None):
+        """StreamingTransformer::forward_step: one row per stream, positions on the device, one
+        CUDA graph per stream set. x [n, d] bf16 and out [n, d] f32 may be CUDA or pinned host."""
+        import torch
+        s = _i32(streams)
+        if out is None:
+            out = torch.empty((len(s), self.cfg.d_model), dtype=torch.float32, device=x.device)
+        _check(lib().ptts_b200_step(self._h, kv.handle, _ip(s), len(s), ctypes.c_void_p(x.data_ptr()),
+                                    ctypes.c_void_p(out.data_ptr()), _stream(stream)))
+        return out
+
+
+# --------------------------------------------------------------------------------------------
+# synthetic weights (random init in the checkpoint's layout)
+# --------------------------------------------------------------------------------------------
+
+@dataclass
+class Weights:
+    """All layers' weights, numpy, concatenated over layers (the oracle takes the same)."""
+    w_qkv: np.ndarray
+    s_qkv: np.ndarray
+    w_out: np.ndarray
+    s_out: np.ndarray
+    w_ff1: np.ndarray
+    s_ff1: np.ndarray
+    w_ff2: np.ndarray
+    s_ff2: np.ndarray
+    ln1_g: np.ndarray
+    ln1_b: np.ndarray
+    ln2_g: np.ndarray
+    ln2_b: np.ndarray
+
+    def layer(self, l: int) -> dict:
+        return dict(in_proj=self.w_qkv[l], in_proj_scale=self.s_qkv[l], out_proj=self.w_out[l],
+                    out_proj_scale=self.s_out[l], linear1=self.w_ff1[l], linear1_scale=self.s_ff1[l],
+                    linear2=self.w_ff2[l], linear2_scale=self.s_ff2[l], norm1_weight=self.ln1_g[l],
+                    norm1_bias=self.ln1_b[l], norm2_weight=self.ln2_g[l], norm2_bias=self.ln2_b[l])
+
+
+def random_weights(cfg: FlowLMConfig, seed: int, *, ln_random: bool = False) -> Weights:
+    """int8 ~ U{-127..127}, scales ~ U(0.005, 0.02) per output row, LN gamma 1 / beta 0 (or
+    random when ln_random, for tests)."""
+    rng = np.random.default_rng(seed)
+    L, d, hd = cfg.num_layers, cfg.d_model, cfg.num_heads * cfg.head_dim
+    nqkv = hd + 2 * cfg.num_kv_heads * cfg.head_dim
+    ff = cfg.dim_feedforward
+
+    def q(n, k):
+        return rng.integers(-127, 128, size=(L, n, k), dtype=np.int8)
+
+    def s(n):
+        return rng.uniform(0.005, 0.02, size=(L, n)).astype(np.float32)
+
+    w_qkv, s_qkv = q(nqkv, d), s(nqkv)
+    w_out, s_out = q(d, hd), s(d)
+    w_ff1, s_ff1 = q(ff, d), s(ff)
+    w_ff2, s_ff2 = q(d, ff), s(d)
+    if ln_random:
+        ln = [rng.uniform(0.5, 1.5, (L, d)).astype(np.float32), rng.normal(0, 0.1, (L, d)).astype(np.float32),
+              rng.uniform(0.5, 1.5, (L, d)).astype(np.float32), rng.normal(0, 0.1, (L, d)).astype(np.float32)]
+    else:
+        ln = [np.ones((L, d), np.float32), np.zeros((L, d), np.float32),
+              np.ones((L, d), np.float32), np.zeros((L, d), np.float32)]
+    return Weights(w_qkv, s_qkv, w_out, s_out, w_ff1, s_ff1, w_ff2, s_ff2, *ln)

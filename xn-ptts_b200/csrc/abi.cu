@@ -1,0 +1,905 @@
+// The C ABI of ptts_b200 (include/ptts_b200.h): objects, argument checks, workspaces, launch
+// sequences and the per-stream-set CUDA graph of the device step.
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <exception>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "kernels.h"
+#include "ptts_b200.h"
+
+namespace {
+
+using namespace ptts;
+
+thread_local std::string g_last_error;
+
+struct Error {
+    int code;
+    std::string msg;
+};
+
+[[noreturn]] void fail(int code, const std::string& msg) { throw Error{code, msg}; }
+
+#define CK(call)                                                                             \
+    do {                                                                                     \
+        cudaError_t e_ = (call);                                                             \
+        if (e_ != cudaSuccess) fail(PTTS_B200_ERR_CUDA, std::string(#call) + ": " + cudaGetErrorString(e_)); \
+    } while (0)
+
+template <class F>
+int guarded(F&& f) {
+    try {
+        f();
+        return PTTS_B200_OK;
+    } catch (const Error& e) {
+        g_last_error = e.msg;
+        return e.code;
+    } catch (const std::exception& e) {
+        g_last_error = std::string("internal error: ") + e.what();
+        return PTTS_B200_ERR_STATE;
+    } catch (...) {
+        g_last_error = "internal error: unknown exception";
+        return PTTS_B200_ERR_STATE;
+    }
+}
+
+void require(bool ok, int code, const std::string& msg) {
+    if (!ok) fail(code, msg);
+}
+
+struct DeviceScope {
+    int prev = -1;
+    explicit DeviceScope(int dev) {
+        CK(cudaGetDevice(&prev));
+        if (prev != dev) CK(cudaSetDevice(dev));
+    }
+    ~DeviceScope() {
+        if (prev >= 0) cudaSetDevice(prev);
+    }
+};
+
+// Grow-only device buffer.
+struct DevBuf {
+    void* p = nullptr;
+    size_t bytes = 0;
+    DevBuf() = default;
+    DevBuf(const DevBuf&) = delete;
+    DevBuf& operator=(const DevBuf&) = delete;
+    ~DevBuf() {
+        if (p) cudaFree(p);
+    }
+    void* need(size_t n) {
+        if (n <= bytes) return p;
+        if (p) {
+            CK(cudaDeviceSynchronize());
+            CK(cudaFree(p));
+            p = nullptr;
+            bytes = 0;
+        }
+        CK(cudaMalloc(&p, n));
+        bytes = n;
+        return p;
+    }
+    template <class T>
+    T* as() const {
+        return static_cast<T*>(p);
+    }
+};
+
+// Pinned staging for small host -> device uploads; waits for the previous upload first.
+struct Staging {
+    void* host = nullptr;
+    size_t bytes = 0;
+    cudaEvent_t done = nullptr;
+    ~Staging() {
+        if (host) cudaFreeHost(host);
+        if (done) cudaEventDestroy(done);
+    }
+    void upload(void* dev, const void* src, size_t n, cudaStream_t s) {
+        if (!done) CK(cudaEventCreateWithFlags(&done, cudaEventDisableTiming));
+        CK(cudaEventSynchronize(done));
+        if (n > bytes) {
+            if (host) CK(cudaFreeHost(host));
+            host = nullptr;
+            CK(cudaMallocHost(&host, n));
+            bytes = n;
+        }
+        std::memcpy(host, src, n);
+        CK(cudaMemcpyAsync(dev, host, n, cudaMemcpyHostToDevice, s));
+        CK(cudaEventRecord(done, s));
+    }
+};
+
+int sm_count(int dev) {
+    int n = 0;
+    CK(cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev));
+    return n;
+}
+
+void rope_inv_freq(int head_dim, float max_period, float* out) {
+    // rope.rs:44-48 with the host libm powf, as the reference computes it.
+    const int half = head_dim / 2;
+    for (int i = 0; i < half; ++i) out[i] = 1.0f / powf(max_period, (float)i / (float)half);
+}
+
+constexpr float kLog2e = 1.4426950408889634f;
+
+}  // namespace
+
+struct ptts_b200_kv {
+    uint64_t uid;  // distinguishes a new object at a recycled address
+    int device, layers, streams, capacity, heads, head_dim, dtype;
+    size_t row_bytes;
+    DevBuf k, v, len;
+    DevBuf err;
+    std::vector<int32_t> h_len;
+    // scratch of the attention op
+    DevBuf seq_stream, row_offsets, row_stream, row_pos, prefix, part, q_rot;
+    Staging staging;
+
+    size_t layer_bytes() const { return (size_t)streams * capacity * row_bytes; }
+    size_t stream_bytes() const { return (size_t)capacity * row_bytes; }
+    char* k_layer(int l) const { return k.as<char>() + l * layer_bytes(); }
+    char* v_layer(int l) const { return v.as<char>() + l * layer_bytes(); }
+};
+
+struct StepGraph {
+    std::vector<int32_t> streams;
+    const ptts_b200_kv* kv = nullptr;
+    uint64_t kv_uid = 0;
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t exec = nullptr;
+    DevBuf sid, x, resid, q_rot, attn, ff, row_stream, row_pos, prefix, part;
+    ~StepGraph() {
+        if (exec) cudaGraphExecDestroy(exec);
+        if (graph) cudaGraphDestroy(graph);
+    }
+};
+
+struct ptts_b200_model {
+    int device;
+    ptts_b200_config cfg;
+    float inv_freq[kMaxPairs];
+    struct Layer {
+        DevBuf w_qkv, s_qkv, w_out, s_out, w1, s1, w2, s2, ln1g, ln1b, ln2g, ln2b;
+        bool loaded = false;
+    };
+    std::vector<std::unique_ptr<Layer>> layers;
+    // forward() workspace
+    DevBuf seq_stream, row_offsets, row_stream, row_pos, prefix, part, q_rot, attn, ff;
+    Staging staging;
+    std::unique_ptr<StepGraph> step;
+    cudaStream_t capture_stream = nullptr;
+    // tracing
+    bool tracing = false;
+    std::vector<cudaEvent_t> events;  // [2 * layers] around attention, then step start / end
+    ptts_b200_trace trace{};
+    ~ptts_b200_model() {
+        step.reset();
+        if (capture_stream) cudaStreamDestroy(capture_stream);
+        for (cudaEvent_t e : events) cudaEventDestroy(e);
+    }
+};
+
+namespace {
+
+cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
+
+void check_kv(const ptts_b200_kv* kv) { require(kv != nullptr, PTTS_B200_ERR_ARG, "kv is NULL"); }
+
+void check_launch() {
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) fail(PTTS_B200_ERR_CUDA, std::string("kernel launch: ") + cudaGetErrorString(e));
+}
+
+// Validates sequences against the host mirror; returns total rows, fills offsets.
+int check_sequences(const ptts_b200_kv* kv, const int32_t* streams, const int32_t* rows, int n_seq,
+                    std::vector<int32_t>& offsets) {
+    require(n_seq > 0, PTTS_B200_ERR_ARG, "n_seq must be positive");
+    require(streams != nullptr && rows != nullptr, PTTS_B200_ERR_ARG, "streams/rows are NULL");
+    offsets.assign(n_seq + 1, 0);
+    std::vector<char> seen(kv->streams, 0);
+    long long total = 0;
+    for (int i = 0; i < n_seq; ++i) {
+        const int s = streams[i];
+        require(s >= 0 && s < kv->streams, PTTS_B200_ERR_ARG,
+                "stream " + std::to_string(s) + " is outside 0.." + std::to_string(kv->streams - 1));
+        require(!seen[s], PTTS_B200_ERR_ARG, "stream " + std::to_string(s) + " appears twice");
+        seen[s] = 1;
+        require(rows[i] >= 1, PTTS_B200_ERR_ARG, "every sequence needs at least one row");
+        const long long need = (long long)kv->h_len[s] + rows[i];
+        if (need > kv->capacity)
+            fail(PTTS_B200_ERR_CAPACITY, "cannot fit " + std::to_string(need) +
+                                             " filled KV positions into a budget of " +
+                                             std::to_string(kv->capacity) + " (stream " +
+                                             std::to_string(s) + ")");
+        total += rows[i];
+        require(total < (1LL << 30), PTTS_B200_ERR_ARG, "too many rows");
+        offsets[i + 1] = (int32_t)total;
+    }
+    return (int)total;
+}
+
+// Decode (every sequence one row) or ragged plan into the given buffers.
+RowPlan make_plan(const ptts_b200_kv* kv, bool decode, const int32_t* d_seq_stream,
+                  const int32_t* d_row_offsets, int n_seq, int n_rows, DevBuf& row_stream,
+                  DevBuf& row_pos, DevBuf& prefix, cudaStream_t s) {
+    RowPlan plan;
+    plan.row_stream = static_cast<int32_t*>(row_stream.need(sizeof(int32_t) * n_rows));
+    plan.row_pos = static_cast<int32_t*>(row_pos.need(sizeof(int32_t) * n_rows));
+    plan.prefix = static_cast<int32_t*>(prefix.need(sizeof(int32_t) * (n_rows + 1)));
+    if (decode)
+        launch_plan_decode(kv->len.as<int32_t>(), d_seq_stream, n_seq, kv->streams, kv->capacity,
+                           plan, kv->err.as<uint32_t>(), s);
+    else
+        launch_plan_rows(kv->len.as<int32_t>(), d_seq_stream, d_row_offsets, n_seq, n_rows,
+                         kv->streams, kv->capacity, plan, kv->err.as<uint32_t>(), s);
+    return plan;
+}
+
+void attention(const ptts_b200_kv* kv, int layer, bool decode, const RowPlan& plan, int n_rows,
+               const void* q_rot, void* out, bool out_bf16, DevBuf& part, cudaStream_t s) {
+    const bool bf16 = kv->dtype == PTTS_B200_BF16;
+    const float qscale = (1.0f / sqrtf((float)kv->head_dim)) * kLog2e;  // transformer.rs:215
+    if (decode) {
+        const int grid = sm_count(kv->device);
+        DecodeArgs a{};
+        a.k_cache = kv->k_layer(layer);
+        a.v_cache = kv->v_layer(layer);
+        a.stream_bytes = (long long)kv->stream_bytes();
+        a.row_stream = plan.row_stream;
+        a.prefix = plan.prefix;
+        a.q = q_rot;
+        a.out = out;
+        a.out_bf16 = out_bf16;
+        a.part = static_cast<float*>(part.need(sizeof(float) * decode_part_floats(n_rows, grid)));
+        a.B = n_rows;
+        a.qscale = qscale;
+        a.err = kv->err.as<uint32_t>();
+        launch_decode_attn(a, bf16, grid, s);
+    } else {
+        PrefillArgs a{};
+        a.k_cache = kv->k_layer(layer);
+        a.v_cache = kv->v_layer(layer);
+        a.stream_elems = (long long)kv->capacity * kRowWidth;
+        a.row_stream = plan.row_stream;
+        a.row_pos = plan.row_pos;
+        a.q = q_rot;
+        a.out = out;
+        a.out_bf16 = out_bf16;
+        a.rows = n_rows;
+        a.qscale = qscale;
+        a.err = kv->err.as<uint32_t>();
+        launch_prefill_attn(a, bf16, s);
+    }
+    check_launch();
+}
+
+void check_model_kv(const ptts_b200_model* m, const ptts_b200_kv* kv) {
+    require(m != nullptr, PTTS_B200_ERR_ARG, "model is NULL");
+    check_kv(kv);
+    require(m->device == kv->device, PTTS_B200_ERR_STATE, "model and kv live on different devices");
+    require(kv->layers == m->cfg.num_layers, PTTS_B200_ERR_STATE,
+            "kv has " + std::to_string(kv->layers) + " layers, the model " +
+                std::to_string(m->cfg.num_layers));
+    require(kv->heads == m->cfg.num_heads && kv->head_dim == m->cfg.head_dim, PTTS_B200_ERR_STATE,
+            "kv heads/head_dim differ from the model's");
+    require(kv->dtype == PTTS_B200_BF16, PTTS_B200_ERR_UNSUPPORTED,
+            "the model runs on a bf16 KV cache");
+    for (int l = 0; l < m->cfg.num_layers; ++l)
+        require(m->layers[l]->loaded, PTTS_B200_ERR_STATE,
+                "layer " + std::to_string(l) + " has no weights (ptts_b200_model_load_layer)");
+}
+
+struct LayerBuffers {
+    float* resid;             // [rows][d_model] f32
+    __nv_bfloat16* q_rot;     // [rows][H*D]
+    __nv_bfloat16* attn;      // [rows][H*D]
+    __nv_bfloat16* ff;        // [rows][ff]
+    DevBuf* part;
+};
+
+// StreamingTransformerLayer::forward (transformer.rs:591-634) for every layer.
+void run_layers(const ptts_b200_model* m, const ptts_b200_kv* kv, bool decode, const RowPlan& plan,
+                int rows, const LayerBuffers& b, cudaStream_t s, cudaEvent_t* attn_ev = nullptr) {
+    const ptts_b200_config& c = m->cfg;
+    const int hd = c.num_heads * c.head_dim;
+    const int nqkv = hd + 2 * c.num_kv_heads * c.head_dim;
+    for (int l = 0; l < c.num_layers; ++l) {
+        const auto& L = *m->layers[l];
+        LinearArgs a{};
+        a.M = rows;
+        a.err = kv->err.as<uint32_t>();
+        a.gelu_tanh = c.gelu;
+        // in_proj with LN1 prologue, RoPE + append epilogue
+        a.N = nqkv;
+        a.K = c.d_model;
+        a.x = b.resid;
+        a.ln_g = L.ln1g.as<float>();
+        a.ln_b = L.ln1b.as<float>();
+        a.w = L.w_qkv.as<int8_t>();
+        a.scale = L.s_qkv.as<float>();
+        a.yb = b.q_rot;
+        a.row_stream = plan.row_stream;
+        a.row_pos = plan.row_pos;
+        a.k_cache = reinterpret_cast<__nv_bfloat16*>(kv->k_layer(l));
+        a.v_cache = reinterpret_cast<__nv_bfloat16*>(kv->v_layer(l));
+        a.heads = c.num_heads;
+        a.kv_heads = c.num_kv_heads;
+        a.num_streams = kv->streams;
+        a.capacity = kv->capacity;
+        std::memcpy(a.inv_freq, m->inv_freq, sizeof(a.inv_freq));
+        launch_linear(a, true, EPI_QKV, s);
+        check_launch();
+        // attention over the cache
+        if (attn_ev) CK(cudaEventRecord(attn_ev[2 * l], s));
+        attention(kv, l, decode, plan, rows, b.q_rot, b.attn, true, *b.part, s);
+        if (attn_ev) CK(cudaEventRecord(attn_ev[2 * l + 1], s));
+        // out_proj + residual
+        LinearArgs o{};
+        o.M = rows;
+        o.N = c.d_model;
+        o.K = hd;
+        o.a = b.attn;
+        o.w = L.w_out.as<int8_t>();
+        o.scale = L.s_out.as<float>();
+        o.y = b.resid;
+        o.err = a.err;
+        launch_linear(o, false, EPI_RESID, s);
+        check_launch();
+        // linear1 with LN2 prologue and GELU
+        LinearArgs f1{};
+        f1.M = rows;
+        f1.N = c.dim_feedforward;
+        f1.K = c.d_model;
+        f1.x = b.resid;
+        f1.ln_g = L.ln2g.as<float>();
+        f1.ln_b = L.ln2b.as<float>();
+        f1.w = L.w1.as<int8_t>();
+        f1.scale = L.s1.as<float>();
+        f1.yb = b.ff;
+        f1.gelu_tanh = c.gelu;
+        f1.err = a.err;
+        launch_linear(f1, true, EPI_GELU, s);
+        check_launch();
+        // linear2 + residual
+        LinearArgs f2{};
+        f2.M = rows;
+        f2.N = c.d_model;
+        f2.K = c.dim_feedforward;
+        f2.a = b.ff;
+        f2.w = L.w2.as<int8_t>();
+        f2.scale = L.s2.as<float>();
+        f2.y = b.resid;
+        f2.err = a.err;
+        launch_linear(f2, false, EPI_RESID, s);
+        check_launch();
+    }
+}
+
+bool is_device_pointer(const void* p) {
+    cudaPointerAttributes at{};
+    if (cudaPointerGetAttributes(&at, p) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    return at.type == cudaMemoryTypeDevice || at.type == cudaMemoryTypeManaged;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* ptts_b200_last_error(void) { return g_last_error.c_str(); }
+
+const char* ptts_b200_version(void) { return "ptts_b200 0.1 sm_100a"; }
+
+int ptts_b200_kv_create(int device, int num_layers, int num_streams, int capacity, int num_heads,
+                        int head_dim, int dtype, ptts_b200_kv** out) {
+    return guarded([&] {
+        require(out != nullptr, PTTS_B200_ERR_ARG, "out is NULL");
+        *out = nullptr;
+        require(num_layers > 0 && num_streams > 0 && capacity > 0, PTTS_B200_ERR_ARG,
+                "layers, streams and capacity must be positive");
+        require(head_dim == kHeadDim && num_heads * head_dim == kRowWidth, PTTS_B200_ERR_UNSUPPORTED,
+                "only head_dim 64 with num_heads * head_dim = 512 is implemented");
+        require(dtype == PTTS_B200_F32 || dtype == PTTS_B200_BF16, PTTS_B200_ERR_ARG, "unknown dtype");
+        DeviceScope scope(device);
+        static uint64_t next_uid = 1;
+        auto kv = std::make_unique<ptts_b200_kv>();
+        kv->uid = next_uid++;
+        kv->device = device;
+        kv->layers = num_layers;
+        kv->streams = num_streams;
+        kv->capacity = capacity;
+        kv->heads = num_heads;
+        kv->head_dim = head_dim;
+        kv->dtype = dtype;
+        kv->row_bytes = (size_t)num_heads * head_dim * (dtype == PTTS_B200_BF16 ? 2 : 4);
+        const size_t total = (size_t)num_layers * kv->layer_bytes();
+        CK(cudaMemset(kv->k.need(total), 0, total));
+        CK(cudaMemset(kv->v.need(total), 0, total));
+        CK(cudaMemset(kv->len.need(sizeof(int32_t) * num_streams), 0, sizeof(int32_t) * num_streams));
+        CK(cudaMemset(kv->err.need(sizeof(uint32_t)), 0, sizeof(uint32_t)));
+        kv->h_len.assign(num_streams, 0);
+        CK(cudaDeviceSynchronize());
+        *out = kv.release();
+    });
+}
+
+void ptts_b200_kv_destroy(ptts_b200_kv* kv) {
+    if (!kv) return;
+    int prev = -1;
+    cudaGetDevice(&prev);
+    cudaSetDevice(kv->device);
+    cudaDeviceSynchronize();
+    delete kv;
+    if (prev >= 0) cudaSetDevice(prev);
+}
+
+int ptts_b200_kv_lengths(const ptts_b200_kv* kv, int32_t* lengths_host) {
+    return guarded([&] {
+        check_kv(kv);
+        require(lengths_host != nullptr, PTTS_B200_ERR_ARG, "lengths_host is NULL");
+        std::memcpy(lengths_host, kv->h_len.data(), sizeof(int32_t) * kv->streams);
+    });
+}
+
+int ptts_b200_kv_pointers(const ptts_b200_kv* kv, int layer, void** k, void** v,
+                          int32_t** lengths) {
+    return guarded([&] {
+        check_kv(kv);
+        require(layer >= 0 && layer < kv->layers, PTTS_B200_ERR_ARG, "layer out of range");
+        if (k) *k = kv->k_layer(layer);
+        if (v) *v = kv->v_layer(layer);
+        if (lengths) *lengths = kv->len.as<int32_t>();
+    });
+}
+
+int ptts_b200_kv_advance(ptts_b200_kv* kv, const int32_t* streams_host, const int32_t* rows_host,
+                         int n, void* cuda_stream) {
+    return guarded([&] {
+        check_kv(kv);
+        DeviceScope scope(kv->device);
+        std::vector<int32_t> offsets;
+        check_sequences(kv, streams_host, rows_host, n, offsets);
+        cudaStream_t s = as_stream(cuda_stream);
+        std::vector<int32_t> packed(streams_host, streams_host + n);
+        packed.insert(packed.end(), offsets.begin(), offsets.end());
+        int32_t* d = static_cast<int32_t*>(kv->seq_stream.need(sizeof(int32_t) * packed.size()));
+        kv->staging.upload(d, packed.data(), sizeof(int32_t) * packed.size(), s);
+        launch_advance(kv->len.as<int32_t>(), d, d + n, n, 0, s);
+        check_launch();
+        for (int i = 0; i < n; ++i) kv->h_len[streams_host[i]] += rows_host[i];
+    });
+}
+
+int ptts_b200_kv_reset(ptts_b200_kv* kv, const int32_t* streams_host, int n, void* cuda_stream) {
+    return guarded([&] {
+        check_kv(kv);
+        require(n > 0 && streams_host, PTTS_B200_ERR_ARG, "no streams");
+        for (int i = 0; i < n; ++i)
+            require(streams_host[i] >= 0 && streams_host[i] < kv->streams, PTTS_B200_ERR_ARG,
+                    "stream out of range");
+        DeviceScope scope(kv->device);
+        cudaStream_t s = as_stream(cuda_stream);
+        int32_t* d = static_cast<int32_t*>(kv->seq_stream.need(sizeof(int32_t) * n));
+        kv->staging.upload(d, streams_host, sizeof(int32_t) * n, s);
+        launch_reset_streams(kv->k.p, kv->v.p, kv->len.as<int32_t>(), d, n, kv->layers,
+                             (long long)kv->layer_bytes(), (long long)kv->stream_bytes(), s);
+        check_launch();
+        for (int i = 0; i < n; ++i) kv->h_len[streams_host[i]] = 0;
+    });
+}
+
+int ptts_b200_kv_load_prefix(ptts_b200_kv* kv, int layer, int stream, const void* k,
+                             const void* v, int len, int set_length, void* cuda_stream) {
+    return guarded([&] {
+        check_kv(kv);
+        require(layer >= 0 && layer < kv->layers, PTTS_B200_ERR_ARG, "layer out of range");
+        require(stream >= 0 && stream < kv->streams, PTTS_B200_ERR_ARG, "stream out of range");
+        require(len >= 0, PTTS_B200_ERR_ARG, "negative length");
+        if (len > kv->capacity)
+            fail(PTTS_B200_ERR_CAPACITY, "cannot fit " + std::to_string(len) +
+                                             " filled KV positions into a budget of " +
+                                             std::to_string(kv->capacity));
+        DeviceScope scope(kv->device);
+        cudaStream_t s = as_stream(cuda_stream);
+        const size_t off = (size_t)stream * kv->stream_bytes();
+        if (len > 0) {
+            require(k && v, PTTS_B200_ERR_ARG, "k/v are NULL");
+            CK(cudaMemcpyAsync(kv->k_layer(layer) + off, k, len * kv->row_bytes, cudaMemcpyDefault, s));
+            CK(cudaMemcpyAsync(kv->v_layer(layer) + off, v, len * kv->row_bytes, cudaMemcpyDefault, s));
+        }
+        if (set_length) {
+            kv->h_len[stream] = len;
+            kv->staging.upload(kv->len.as<int32_t>() + stream, &len, sizeof(int32_t), s);
+        }
+    });
+}
+
+int ptts_b200_kv_copy_stream(ptts_b200_kv* dst, int dst_stream, const ptts_b200_kv* src,
+                             int src_stream, void* cuda_stream) {
+    return guarded([&] {
+        check_kv(dst);
+        check_kv(src);
+        require(dst->layers == src->layers && dst->heads == src->heads &&
+                    dst->head_dim == src->head_dim && dst->dtype == src->dtype,
+                PTTS_B200_ERR_STATE, "the two caches differ in layers, heads or dtype");
+        require(dst->device == src->device, PTTS_B200_ERR_STATE, "the two caches are on different devices");
+        require(dst_stream >= 0 && dst_stream < dst->streams && src_stream >= 0 &&
+                    src_stream < src->streams,
+                PTTS_B200_ERR_ARG, "stream out of range");
+        const int used = src->h_len[src_stream];
+        if (used > dst->capacity)
+            fail(PTTS_B200_ERR_CAPACITY, "cannot fit " + std::to_string(used) +
+                                             " filled KV positions into a budget of " +
+                                             std::to_string(dst->capacity));
+        DeviceScope scope(dst->device);
+        cudaStream_t s = as_stream(cuda_stream);
+        for (int l = 0; l < dst->layers; ++l) {
+            char* dk = dst->k_layer(l) + (size_t)dst_stream * dst->stream_bytes();
+            char* dv = dst->v_layer(l) + (size_t)dst_stream * dst->stream_bytes();
+            const char* sk = src->k_layer(l) + (size_t)src_stream * src->stream_bytes();
+            const char* sv = src->v_layer(l) + (size_t)src_stream * src->stream_bytes();
+            const size_t n = (size_t)used * dst->row_bytes;
+            if (n) {
+                CK(cudaMemcpyAsync(dk, sk, n, cudaMemcpyDeviceToDevice, s));
+                CK(cudaMemcpyAsync(dv, sv, n, cudaMemcpyDeviceToDevice, s));
+            }
+            CK(cudaMemsetAsync(dk + n, 0, dst->stream_bytes() - n, s));
+            CK(cudaMemsetAsync(dv + n, 0, dst->stream_bytes() - n, s));
+        }
+        dst->h_len[dst_stream] = used;
+        dst->staging.upload(dst->len.as<int32_t>() + dst_stream, &used, sizeof(int32_t), s);
+    });
+}
+
+int ptts_b200_kv_check(ptts_b200_kv* kv) {
+    return guarded([&] {
+        check_kv(kv);
+        DeviceScope scope(kv->device);
+        CK(cudaDeviceSynchronize());
+        uint32_t e = 0;
+        CK(cudaMemcpy(&e, kv->err.p, sizeof(e), cudaMemcpyDeviceToHost));
+        CK(cudaMemset(kv->err.p, 0, sizeof(e)));
+        if (e) {
+            std::string what;
+            if (e & DEV_ERR_BOUNDS) what += " bounds";
+            if (e & DEV_ERR_CAPACITY) what += " capacity";
+            if (e & DEV_ERR_TIMEOUT) what += " timeout";
+            fail(PTTS_B200_ERR_DEVICE, "device-side check tripped:" + what);
+        }
+    });
+}
+
+int ptts_b200_attend(ptts_b200_kv* kv, int layer, const void* q, const void* k, const void* v,
+                     int in_dtype, int num_kv_heads, const int32_t* streams_host,
+                     const int32_t* rows_host, int n_seq, float max_period, void* out,
+                     int out_dtype, void* cuda_stream) {
+    return guarded([&] {
+        check_kv(kv);
+        require(layer >= 0 && layer < kv->layers, PTTS_B200_ERR_ARG, "layer out of range");
+        require(q && k && v && out, PTTS_B200_ERR_ARG, "q/k/v/out are NULL");
+        require(in_dtype == PTTS_B200_F32 || in_dtype == PTTS_B200_BF16, PTTS_B200_ERR_ARG, "bad in_dtype");
+        require(out_dtype == PTTS_B200_F32 || out_dtype == PTTS_B200_BF16, PTTS_B200_ERR_ARG, "bad out_dtype");
+        require(num_kv_heads > 0 && kv->heads % num_kv_heads == 0, PTTS_B200_ERR_ARG,
+                "the " + std::to_string(num_kv_heads) + " key/value heads do not divide the " +
+                    std::to_string(kv->heads) + " attention heads");
+        require(max_period > 1.0f, PTTS_B200_ERR_ARG, "max_period must be above 1");
+        std::vector<int32_t> offsets;
+        const int n_rows = check_sequences(kv, streams_host, rows_host, n_seq, offsets);
+        bool decode = true;
+        for (int i = 0; i < n_seq; ++i) decode = decode && rows_host[i] == 1;
+        DeviceScope scope(kv->device);
+        cudaStream_t s = as_stream(cuda_stream);
+        std::vector<int32_t> packed(streams_host, streams_host + n_seq);
+        packed.insert(packed.end(), offsets.begin(), offsets.end());
+        int32_t* d = static_cast<int32_t*>(kv->seq_stream.need(sizeof(int32_t) * packed.size()));
+        kv->staging.upload(d, packed.data(), sizeof(int32_t) * packed.size(), s);
+        const RowPlan plan = make_plan(kv, decode, d, d + n_seq, n_seq, n_rows, kv->row_stream,
+                                       kv->row_pos, kv->prefix, s);
+        check_launch();
+        RopeAppendArgs ra{};
+        ra.q = q;
+        ra.k = k;
+        ra.v = v;
+        ra.q_out = kv->q_rot.need((size_t)n_rows * kv->row_bytes);
+        ra.k_cache = kv->k_layer(layer);
+        ra.v_cache = kv->v_layer(layer);
+        ra.row_stream = plan.row_stream;
+        ra.row_pos = plan.row_pos;
+        ra.rows = n_rows;
+        ra.heads = kv->heads;
+        ra.kv_heads = num_kv_heads;
+        ra.num_streams = kv->streams;
+        ra.capacity = kv->capacity;
+        rope_inv_freq(kv->head_dim, max_period, ra.inv_freq);
+        ra.err = kv->err.as<uint32_t>();
+        launch_rope_append(ra, in_dtype == PTTS_B200_BF16, kv->dtype == PTTS_B200_BF16, s);
+        check_launch();
+        attention(kv, layer, decode, plan, n_rows, ra.q_out, out, out_dtype == PTTS_B200_BF16,
+                  kv->part, s);
+    });
+}
+
+int ptts_b200_linear_i8(int device, const void* x, const int8_t* w, const float* scale, int m,
+                        int n, int k, float* y, void* cuda_stream) {
+    return guarded([&] {
+        require(x && w && scale && y, PTTS_B200_ERR_ARG, "NULL argument");
+        require(m > 0 && n > 0 && k > 0, PTTS_B200_ERR_ARG, "sizes must be positive");
+        require(n % 64 == 0 && k % 64 == 0, PTTS_B200_ERR_UNSUPPORTED, "n and k must be multiples of 64");
+        DeviceScope scope(device);
+        LinearArgs a{};
+        a.M = m;
+        a.N = n;
+        a.K = k;
+        a.a = static_cast<const __nv_bfloat16*>(x);
+        a.w = w;
+        a.scale = scale;
+        a.y = y;
+        launch_linear(a, false, EPI_F32, as_stream(cuda_stream));
+        check_launch();
+    });
+}
+
+int ptts_b200_model_create(int device, const ptts_b200_config* config, ptts_b200_model** out) {
+    return guarded([&] {
+        require(out && config, PTTS_B200_ERR_ARG, "NULL argument");
+        *out = nullptr;
+        const ptts_b200_config& c = *config;
+        // transformer.rs:699-707
+        if (c.num_heads <= 0 || c.num_heads * c.head_dim <= 0)
+            fail(PTTS_B200_ERR_ARG, "the config's " + std::to_string(c.num_heads) +
+                                        " attention heads do not divide its width");
+        if (c.num_kv_heads <= 0 || c.num_heads % c.num_kv_heads != 0)
+            fail(PTTS_B200_ERR_ARG, "the config's " + std::to_string(c.num_kv_heads) +
+                                        " key/value heads do not divide its " +
+                                        std::to_string(c.num_heads) + " attention heads");
+        require(c.head_dim == kHeadDim && c.num_heads * c.head_dim == kRowWidth,
+                PTTS_B200_ERR_UNSUPPORTED, "only head_dim 64 with num_heads * head_dim = 512 is implemented");
+        require(c.d_model > 0 && c.d_model % 128 == 0 && c.d_model <= 1024, PTTS_B200_ERR_UNSUPPORTED,
+                "d_model must be a multiple of 128 up to 1024");
+        require(c.dim_feedforward > 0 && c.dim_feedforward % 64 == 0, PTTS_B200_ERR_UNSUPPORTED,
+                "dim_feedforward must be a multiple of 64");
+        require(c.num_layers > 0, PTTS_B200_ERR_ARG, "num_layers must be positive");
+        require(c.max_period > 1.0f, PTTS_B200_ERR_ARG, "max_period must be above 1");
+        require(c.gelu == 0 || c.gelu == 1, PTTS_B200_ERR_ARG, "gelu is 0 (erf) or 1 (tanh)");
+        DeviceScope scope(device);
+        auto m = std::make_unique<ptts_b200_model>();
+        m->device = device;
+        m->cfg = c;
+        rope_inv_freq(c.head_dim, c.max_period, m->inv_freq);
+        for (int l = 0; l < c.num_layers; ++l) m->layers.push_back(std::make_unique<ptts_b200_model::Layer>());
+        CK(cudaStreamCreateWithFlags(&m->capture_stream, cudaStreamNonBlocking));
+        *out = m.release();
+    });
+}
+
+void ptts_b200_model_destroy(ptts_b200_model* model) {
+    if (!model) return;
+    int prev = -1;
+    cudaGetDevice(&prev);
+    cudaSetDevice(model->device);
+    cudaDeviceSynchronize();
+    delete model;
+    if (prev >= 0) cudaSetDevice(prev);
+}
+
+int ptts_b200_model_load_layer(ptts_b200_model* model, int layer,
+                               const ptts_b200_layer_weights* w) {
+    return guarded([&] {
+        require(model && w, PTTS_B200_ERR_ARG, "NULL argument");
+        require(layer >= 0 && layer < model->cfg.num_layers, PTTS_B200_ERR_ARG, "layer out of range");
+        const ptts_b200_config& c = model->cfg;
+        const size_t dm = c.d_model, hd = (size_t)c.num_heads * c.head_dim;
+        const size_t nqkv = hd + 2 * (size_t)c.num_kv_heads * c.head_dim, ff = c.dim_feedforward;
+        require(w->in_proj_host && w->in_proj_scale_host && w->out_proj_host &&
+                    w->out_proj_scale_host && w->linear1_host && w->linear1_scale_host &&
+                    w->linear2_host && w->linear2_scale_host && w->norm1_weight_host &&
+                    w->norm1_bias_host && w->norm2_weight_host && w->norm2_bias_host,
+                PTTS_B200_ERR_ARG, "a weight pointer is NULL");
+        DeviceScope scope(model->device);
+        auto& L = *model->layers[layer];
+        auto put = [](DevBuf& b, const void* src, size_t n) {
+            CK(cudaMemcpy(b.need(n), src, n, cudaMemcpyHostToDevice));
+        };
+        put(L.w_qkv, w->in_proj_host, nqkv * dm);
+        put(L.s_qkv, w->in_proj_scale_host, nqkv * 4);
+        put(L.w_out, w->out_proj_host, dm * hd);
+        put(L.s_out, w->out_proj_scale_host, dm * 4);
+        put(L.w1, w->linear1_host, ff * dm);
+        put(L.s1, w->linear1_scale_host, ff * 4);
+        put(L.w2, w->linear2_host, dm * ff);
+        put(L.s2, w->linear2_scale_host, dm * 4);
+        put(L.ln1g, w->norm1_weight_host, dm * 4);
+        put(L.ln1b, w->norm1_bias_host, dm * 4);
+        put(L.ln2g, w->norm2_weight_host, dm * 4);
+        put(L.ln2b, w->norm2_bias_host, dm * 4);
+        L.loaded = true;
+    });
+}
+
+int ptts_b200_forward(ptts_b200_model* model, ptts_b200_kv* kv, const void* x,
+                      const int32_t* streams_host, const int32_t* rows_host, int n_seq, float* y,
+                      void* cuda_stream) {
+    return guarded([&] {
+        check_model_kv(model, kv);
+        require(x && y, PTTS_B200_ERR_ARG, "x/y are NULL");
+        std::vector<int32_t> offsets;
+        const int rows = check_sequences(kv, streams_host, rows_host, n_seq, offsets);
+        bool decode = true;
+        for (int i = 0; i < n_seq; ++i) decode = decode && rows_host[i] == 1;
+        DeviceScope scope(model->device);
+        cudaStream_t s = as_stream(cuda_stream);
+        const ptts_b200_config& c = model->cfg;
+        std::vector<int32_t> packed(streams_host, streams_host + n_seq);
+        packed.insert(packed.end(), offsets.begin(), offsets.end());
+        int32_t* d = static_cast<int32_t*>(model->seq_stream.need(sizeof(int32_t) * packed.size()));
+        model->staging.upload(d, packed.data(), sizeof(int32_t) * packed.size(), s);
+        const RowPlan plan = make_plan(kv, decode, d, d + n_seq, n_seq, rows, model->row_stream,
+                                       model->row_pos, model->prefix, s);
+        check_launch();
+        const size_t hd = (size_t)c.num_heads * c.head_dim;
+        LayerBuffers b;
+        b.resid = y;  // the residual stream lives in the caller's output
+        b.q_rot = static_cast<__nv_bfloat16*>(model->q_rot.need((size_t)rows * hd * 2));
+        b.attn = static_cast<__nv_bfloat16*>(model->attn.need((size_t)rows * hd * 2));
+        b.ff = static_cast<__nv_bfloat16*>(model->ff.need((size_t)rows * c.dim_feedforward * 2));
+        b.part = &model->part;
+        launch_bf16_to_f32(static_cast<const __nv_bfloat16*>(x), y, (long long)rows * c.d_model, s);
+        check_launch();
+        run_layers(model, kv, decode, plan, rows, b, s);
+        launch_advance(kv->len.as<int32_t>(), d, d + n_seq, n_seq, 0, s);
+        check_launch();
+        for (int i = 0; i < n_seq; ++i) kv->h_len[streams_host[i]] += rows_host[i];
+    });
+}
+
+int ptts_b200_step(ptts_b200_model* model, ptts_b200_kv* kv, const int32_t* streams_host, int n,
+                   const void* x, float* y, void* cuda_stream) {
+    return guarded([&] {
+        check_model_kv(model, kv);
+        require(x && y, PTTS_B200_ERR_ARG, "x/y are NULL");
+        std::vector<int32_t> ones(n > 0 ? n : 0, 1), offsets;
+        check_sequences(kv, streams_host, ones.data(), n, offsets);  // capacity for one more row
+        DeviceScope scope(model->device);
+        cudaStream_t s = as_stream(cuda_stream);
+        const ptts_b200_config& c = model->cfg;
+        const size_t hd = (size_t)c.num_heads * c.head_dim;
+        StepGraph* g = model->step.get();
+        const bool same = g && g->kv == kv && g->kv_uid == kv->uid && g->streams.size() == (size_t)n &&
+                          std::memcmp(g->streams.data(), streams_host, sizeof(int32_t) * n) == 0;
+        if (!same) {
+            // Buffers of this stream set (transformer.rs:822-838 with DeviceStep).
+            CK(cudaStreamSynchronize(s));
+            model->step.reset();
+            auto ng = std::make_unique<StepGraph>();
+            ng->streams.assign(streams_host, streams_host + n);
+            ng->kv = kv;
+            ng->kv_uid = kv->uid;
+            int32_t* sid = static_cast<int32_t*>(ng->sid.need(sizeof(int32_t) * n));
+            CK(cudaMemcpy(sid, streams_host, sizeof(int32_t) * n, cudaMemcpyHostToDevice));
+            ng->x.need((size_t)n * c.d_model * 2);
+            ng->resid.need((size_t)n * c.d_model * 4);
+            ng->q_rot.need((size_t)n * hd * 2);
+            ng->attn.need((size_t)n * hd * 2);
+            ng->ff.need((size_t)n * c.dim_feedforward * 2);
+            ng->part.need(sizeof(float) * decode_part_floats(n, sm_count(kv->device)));
+            ng->row_stream.need(sizeof(int32_t) * n);
+            ng->row_pos.need(sizeof(int32_t) * n);
+            ng->prefix.need(sizeof(int32_t) * (n + 1));
+            model->step = std::move(ng);
+            g = model->step.get();
+        }
+        RowPlan plan;
+        plan.row_stream = g->row_stream.as<int32_t>();
+        plan.row_pos = g->row_pos.as<int32_t>();
+        plan.prefix = g->prefix.as<int32_t>();
+        const int32_t* sid = g->sid.as<int32_t>();
+        LayerBuffers b{g->resid.as<float>(), g->q_rot.as<__nv_bfloat16>(), g->attn.as<__nv_bfloat16>(),
+                       g->ff.as<__nv_bfloat16>(), &g->part};
+        auto body = [&](cudaStream_t cs, cudaEvent_t* ev) {
+            launch_plan_decode(kv->len.as<int32_t>(), sid, n, kv->streams, kv->capacity, plan,
+                               kv->err.as<uint32_t>(), cs);
+            launch_bf16_to_f32(g->x.as<__nv_bfloat16>(), g->resid.as<float>(), (long long)n * c.d_model, cs);
+            run_layers(model, kv, true, plan, n, b, cs, ev);
+            launch_advance(kv->len.as<int32_t>(), sid, nullptr, n, 1, cs);
+            check_launch();
+        };
+        const size_t xb = (size_t)n * c.d_model * 2, yb = (size_t)n * c.d_model * 4;
+        CK(cudaMemcpyAsync(g->x.p, x, xb, is_device_pointer(x) ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, s));
+        if (model->tracing) {
+            const int L = c.num_layers;
+            if (model->events.size() < (size_t)(2 * L + 2)) {
+                for (cudaEvent_t e : model->events) cudaEventDestroy(e);
+                model->events.assign(2 * L + 2, nullptr);
+                for (auto& e : model->events) CK(cudaEventCreate(&e));
+            }
+            cudaEvent_t* ev = model->events.data();
+            CK(cudaEventRecord(ev[2 * L], s));
+            body(s, ev);
+            CK(cudaEventRecord(ev[2 * L + 1], s));
+            CK(cudaEventSynchronize(ev[2 * L + 1]));
+            double bytes = 0.0;
+            for (int i = 0; i < n; ++i) bytes += (double)(kv->h_len[streams_host[i]] + 1) * kv->row_bytes * 2;
+            bytes += (double)n * kv->row_bytes * 2;  // q read, output written
+            for (int l = 0; l < L; ++l) {
+                float ms = 0.f;
+                CK(cudaEventElapsedTime(&ms, ev[2 * l], ev[2 * l + 1]));
+                model->trace.attn_ms += ms;
+                model->trace.attn_launches += 1;
+                model->trace.attn_bytes += bytes;
+            }
+            float ms = 0.f;
+            CK(cudaEventElapsedTime(&ms, ev[2 * L], ev[2 * L + 1]));
+            model->trace.step_ms += ms;
+            model->trace.steps += 1;
+        } else {
+            if (!g->exec) {
+                cudaStream_t cs = model->capture_stream;
+                CK(cudaStreamSynchronize(s));
+                CK(cudaStreamBeginCapture(cs, cudaStreamCaptureModeRelaxed));
+                try {
+                    body(cs, nullptr);
+                } catch (...) {
+                    cudaGraph_t junk = nullptr;
+                    cudaStreamEndCapture(cs, &junk);
+                    if (junk) cudaGraphDestroy(junk);
+                    throw;
+                }
+                CK(cudaStreamEndCapture(cs, &g->graph));
+                CK(cudaGraphInstantiate(&g->exec, g->graph, 0));
+            }
+            CK(cudaGraphLaunch(g->exec, s));
+        }
+        CK(cudaMemcpyAsync(y, g->resid.p, yb, is_device_pointer(y) ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost, s));
+        for (int i = 0; i < n; ++i) kv->h_len[streams_host[i]] += 1;
+    });
+}
+
+int ptts_b200_model_set_tracing(ptts_b200_model* model, int on) {
+    return guarded([&] {
+        require(model != nullptr, PTTS_B200_ERR_ARG, "model is NULL");
+        model->tracing = on != 0;
+    });
+}
+
+int ptts_b200_model_trace(ptts_b200_model* model, ptts_b200_trace* out, int reset) {
+    return guarded([&] {
+        require(model != nullptr && out != nullptr, PTTS_B200_ERR_ARG, "NULL argument");
+        *out = model->trace;
+        if (reset) model->trace = ptts_b200_trace{};
+    });
+}
+
+int ptts_b200_kv_set_lengths(ptts_b200_kv* kv, const int32_t* streams_host,
+                             const int32_t* lengths_host, int n, void* cuda_stream) {
+    return guarded([&] {
+        check_kv(kv);
+        require(n > 0 && streams_host && lengths_host, PTTS_B200_ERR_ARG, "no streams");
+        for (int i = 0; i < n; ++i) {
+            require(streams_host[i] >= 0 && streams_host[i] < kv->streams, PTTS_B200_ERR_ARG,
+                    "stream out of range");
+            if (lengths_host[i] < 0 || lengths_host[i] > kv->capacity)
+                fail(PTTS_B200_ERR_CAPACITY, "cannot fit " + std::to_string(lengths_host[i]) +
+                                                 " filled KV positions into a budget of " +
+                                                 std::to_string(kv->capacity));
+        }
+        DeviceScope scope(kv->device);
+        cudaStream_t s = as_stream(cuda_stream);
+        std::vector<int32_t> packed(streams_host, streams_host + n);
+        packed.insert(packed.end(), lengths_host, lengths_host + n);
+        int32_t* d = static_cast<int32_t*>(kv->seq_stream.need(sizeof(int32_t) * packed.size()));
+        kv->staging.upload(d, packed.data(), sizeof(int32_t) * packed.size(), s);
+        launch_set_lengths(kv->len.as<int32_t>(), d, d + n, n, s);
+        check_launch();
+        for (int i = 0; i < n; ++i) kv->h_len[streams_host[i]] = lengths_host[i];
+    });
+}
+
+}  // extern "C"

@@ -1,0 +1,327 @@
+// Split-KV decode attention: one query row per stream over that stream's cached keys
+// 0..=pos, for a batch of streams with ragged lengths.
+//
+// Reference: the t == 1 branch of StreamingMultiheadAttention::forward, `q.sdpa_decode(k, v,
+// mask, 1/sqrt(d))` (ptts/src/transformer.rs:229-230), and its device-position twin at
+// transformer.rs:216-224, which attends over every slot of the padded cache with a mask. Here
+// only the filled keys are read: key j of a stream is visible iff j <= pos, which is what the
+// mask of DeviceStep (transformer.rs:116-140) selects.
+//
+// Work split. All attended keys of the batch are laid end to end (prefix[b] .. prefix[b+1] for
+// stream b) and cut into `G` equal ranges, one per CTA, so every CTA moves the same number of
+// bytes whatever the length mix. A CTA walks the streams its range touches. A stream that lies
+// wholly inside one range is finished there; the pieces of a stream cut by range ends leave
+// partial (max, sum, acc) records at slot b + c (unique: along the key order each new piece
+// increments b or c or both) and a small second kernel merges them.
+//
+// Data movement. Keys and values of consecutive positions of a stream are contiguous
+// (the cache is [stream][slot][head][dim]), so a chunk of positions is one 1-D bulk copy for K
+// and one for V, issued by a producer warp into a 3-stage shared-memory ring guarded by
+// mbarriers. Eight consumer warps, one per head, read their head's 128-byte slice of every row
+// with 16-byte shared loads (8 lanes per row, 4 rows per warp instruction) and keep an online
+// softmax in the exp2 domain. Every wait is bounded and reports DEV_ERR_TIMEOUT.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace ptts {
+namespace {
+
+constexpr int kHeads = kRowWidth / kHeadDim;  // 8
+constexpr int kConsumerWarps = kHeads;
+constexpr int kThreads = (kConsumerWarps + 1) * 32;
+constexpr int kStages = 3;
+constexpr int kStageBytes = 64 * 1024;  // K half + V half
+constexpr int kMinKeysPerCta = 32;
+constexpr int kSmemBytes = kStages * kStageBytes + 2 * kStages * 8;
+
+template <typename T>
+struct Row;
+template <>
+struct Row<__nv_bfloat16> {
+    static constexpr int kBytes = kRowWidth * 2;  // 1 KB
+};
+template <>
+struct Row<float> {
+    static constexpr int kBytes = kRowWidth * 4;  // 2 KB
+};
+
+__device__ __forceinline__ float fast_exp2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+__device__ __forceinline__ int ctas_in_use(long long total, int grid) {
+    const long long g = (total + kMinKeysPerCta - 1) / kMinKeysPerCta;
+    return (int)(g < 1 ? 1 : (g > grid ? grid : g));
+}
+__device__ __forceinline__ long long cta_start(int c, long long total, int g) {
+    return (long long)c * total / g;
+}
+// The CTA whose range holds key p: the largest c with cta_start(c) <= p.
+__device__ __forceinline__ int cta_of(long long p, long long total, int g) {
+    const long long c = ((p + 1) * g + total - 1) / total - 1;
+    return (int)(c < g - 1 ? c : g - 1);
+}
+
+// Eight elements of a head row for lane slice j: bf16 dims 8j..8j+7; f32 dims 4j..4j+3 and
+// 32+4j..32+4j+3 (two 16-byte loads that stay conflict-free).
+__device__ __forceinline__ void load8(const unsigned char* head_row, int j, float* o,
+                                      __nv_bfloat16*) {
+    const uint4 u = *reinterpret_cast<const uint4*>(head_row + 16 * j);
+    o[0] = bf16lo(u.x); o[1] = bf16hi(u.x); o[2] = bf16lo(u.y); o[3] = bf16hi(u.y);
+    o[4] = bf16lo(u.z); o[5] = bf16hi(u.z); o[6] = bf16lo(u.w); o[7] = bf16hi(u.w);
+}
+__device__ __forceinline__ void load8(const unsigned char* head_row, int j, float* o, float*) {
+    const float4 a = *reinterpret_cast<const float4*>(head_row + 16 * j);
+    const float4 b = *reinterpret_cast<const float4*>(head_row + 128 + 16 * j);
+    o[0] = a.x; o[1] = a.y; o[2] = a.z; o[3] = a.w;
+    o[4] = b.x; o[5] = b.y; o[6] = b.z; o[7] = b.w;
+}
+template <typename T>
+__device__ __forceinline__ int dim_of(int j, int i) {
+    if (sizeof(T) == 2) return 8 * j + i;
+    return i < 4 ? 4 * j + i : 32 + 4 * j + (i - 4);
+}
+
+template <typename T>
+__device__ __forceinline__ void store_out(void* out, int out_bf16, long long at, int j,
+                                          const float* v) {
+    if (out_bf16) {
+        __nv_bfloat16* o = static_cast<__nv_bfloat16*>(out) + at;
+        if (sizeof(T) == 2) {
+            uint4 u;
+            u.x = pack_bf16x2(v[0], v[1]); u.y = pack_bf16x2(v[2], v[3]);
+            u.z = pack_bf16x2(v[4], v[5]); u.w = pack_bf16x2(v[6], v[7]);
+            *reinterpret_cast<uint4*>(o + 8 * j) = u;
+        } else {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) o[dim_of<T>(j, i)] = __float2bfloat16_rn(v[i]);
+        }
+    } else {
+        float* o = static_cast<float*>(out) + at;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) o[dim_of<T>(j, i)] = v[i];
+    }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(DecodeArgs a) {
+    constexpr int RB = Row<T>::kBytes;
+    constexpr int HB = RB / kHeads;              // one head of one row: 128 or 256 bytes
+    constexpr int CH = kStageBytes / 2 / RB;     // rows per chunk: 32 (bf16) or 16 (f32)
+    extern __shared__ __align__(128) unsigned char smem[];
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
+    uint64_t* empty = full + kStages;
+    __shared__ int s_b0;
+
+    const long long total = a.prefix[a.B];
+    const int G = ctas_in_use(total, gridDim.x);
+    const int c = blockIdx.x;
+    if (c >= G) return;
+    const long long start = cta_start(c, total, G), end = cta_start(c + 1, total, G);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        int lo = 0, hi = a.B - 1;  // the last stream whose keys begin at or before `start`
+        while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if (a.prefix[mid] <= start) lo = mid;
+            else hi = mid - 1;
+        }
+        s_b0 = lo;
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kConsumerWarps);
+        }
+        fence_mbar_init();
+    }
+    __syncthreads();
+    const int b0 = s_b0;
+    const unsigned char* kc = static_cast<const unsigned char*>(a.k_cache);
+    const unsigned char* vc = static_cast<const unsigned char*>(a.v_cache);
+
+    if (warp == kConsumerWarps) {
+        // ---- producer: one lane issues the bulk copies -------------------------------
+        if (lane != 0) return;
+        const uint64_t pol = policy_evict_first();
+        int it = 0;
+        bool ok = true;
+        for (int b = b0; b < a.B && ok; ++b) {
+            const long long pb = a.prefix[b], pe = a.prefix[b + 1];
+            if (pb >= end) break;
+            const int s0 = (int)((start > pb ? start : pb) - pb);
+            const int s1 = (int)((end < pe ? end : pe) - pb);
+            const long long base = (long long)a.row_stream[b] * a.stream_bytes;
+            for (int p = s0; p < s1; p += CH, ++it) {
+                const int n = min(CH, s1 - p);
+                const int st = it % kStages;
+                const uint32_t ph = (it / kStages) & 1;
+                if (!mbar_wait(&empty[st], ph ^ 1)) {
+                    set_error(a.err, DEV_ERR_TIMEOUT);
+                    ok = false;
+                    break;
+                }
+                unsigned char* ks = smem + st * kStageBytes;
+                mbar_arrive_expect_tx(&full[st], 2u * n * RB);
+                bulk_g2s(ks, kc + base + (long long)p * RB, n * RB, &full[st], pol);
+                bulk_g2s(ks + kStageBytes / 2, vc + base + (long long)p * RB, n * RB, &full[st], pol);
+            }
+        }
+        // Before leaving, let every copy still in flight land (bounded) so none writes into
+        // shared memory of a CTA that has gone.
+        for (int k = (it > kStages ? it - kStages : 0); k < it; ++k)
+            if (!mbar_wait(&full[k % kStages], (k / kStages) & 1)) set_error(a.err, DEV_ERR_TIMEOUT);
+        return;
+    }
+
+    // ---- consumers: warp h owns head h ---------------------------------------------------
+    const int h = warp;
+    const int g = lane >> 3;  // which of the 4 rows of a warp step
+    const int j = lane & 7;   // which 16-byte slice of the head row
+    int it = 0;
+    for (int b = b0; b < a.B; ++b) {
+        const long long pb = a.prefix[b], pe = a.prefix[b + 1];
+        if (pb >= end) break;
+        const int s0 = (int)((start > pb ? start : pb) - pb);
+        const int s1 = (int)((end < pe ? end : pe) - pb);
+        const bool whole = pb >= start && pe <= end;
+
+        float q[8];
+        load8(static_cast<const unsigned char*>(a.q) + ((long long)b * kHeads + h) * HB, j, q,
+              static_cast<T*>(nullptr));
+#pragma unroll
+        for (int i = 0; i < 8; ++i) q[i] *= a.qscale;
+        float m = -1e30f, l = 0.f, acc[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+
+        for (int p = s0; p < s1; p += CH, ++it) {
+            const int n = min(CH, s1 - p);
+            const int st = it % kStages;
+            const uint32_t ph = (it / kStages) & 1;
+            if (!mbar_wait(&full[st], ph)) {
+                set_error(a.err, DEV_ERR_TIMEOUT);
+                return;
+            }
+            const unsigned char* ks = smem + st * kStageBytes + h * HB;
+            const unsigned char* vs = ks + kStageBytes / 2;
+            for (int r = 0; r < n; r += 8) {
+                const int r0 = r + g, r1 = r + 4 + g;
+                const int rr0 = r0 < n ? r0 : n - 1, rr1 = r1 < n ? r1 : n - 1;
+                float k0[8], k1[8];
+                load8(ks + rr0 * RB, j, k0, static_cast<T*>(nullptr));
+                load8(ks + rr1 * RB, j, k1, static_cast<T*>(nullptr));
+                float d0 = 0.f, d1 = 0.f;
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    d0 = fmaf(q[i], k0[i], d0);
+                    d1 = fmaf(q[i], k1[i], d1);
+                }
+#pragma unroll
+                for (int o = 1; o < 8; o <<= 1) {
+                    d0 += __shfl_xor_sync(0xffffffffu, d0, o);
+                    d1 += __shfl_xor_sync(0xffffffffu, d1, o);
+                }
+                if (r0 >= n) d0 = -INFINITY;
+                if (r1 >= n) d1 = -INFINITY;
+                const float mn = fmaxf(m, fmaxf(d0, d1));
+                const float corr = fast_exp2(m - mn);
+                const float e0 = fast_exp2(d0 - mn), e1 = fast_exp2(d1 - mn);
+                l = fmaf(l, corr, e0 + e1);
+                float v0[8], v1[8];
+                load8(vs + rr0 * RB, j, v0, static_cast<T*>(nullptr));
+                load8(vs + rr1 * RB, j, v1, static_cast<T*>(nullptr));
+#pragma unroll
+                for (int i = 0; i < 8; ++i) acc[i] = fmaf(e1, v1[i], fmaf(e0, v0[i], acc[i] * corr));
+                m = mn;
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[st]);
+        }
+        // Merge the four row groups (lanes j, j+8, j+16, j+24 hold the same dims).
+#pragma unroll
+        for (int o = 8; o <= 16; o <<= 1) {
+            const float mo = __shfl_xor_sync(0xffffffffu, m, o);
+            const float lo = __shfl_xor_sync(0xffffffffu, l, o);
+            const float mn = fmaxf(m, mo);
+            const float fa = fast_exp2(m - mn), fb = fast_exp2(mo - mn);
+            l = l * fa + lo * fb;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) acc[i] = acc[i] * fa + __shfl_xor_sync(0xffffffffu, acc[i], o) * fb;
+            m = mn;
+        }
+        if (g == 0) {
+            if (whole) {
+                const float inv = 1.f / l;
+#pragma unroll
+                for (int i = 0; i < 8; ++i) acc[i] *= inv;
+                store_out<T>(a.out, a.out_bf16, (long long)b * kRowWidth + h * kHeadDim, j, acc);
+            } else {
+                float* rec = a.part + ((long long)(b + c) * kHeads + h) * kPartStride;
+#pragma unroll
+                for (int i = 0; i < 8; ++i) rec[dim_of<T>(j, i)] = acc[i];
+                if (j == 0) {
+                    rec[64] = m;
+                    rec[65] = l;
+                }
+            }
+        }
+    }
+}
+
+// One warp per (stream, head): merge the partial records of streams cut by range ends.
+__global__ void __launch_bounds__(256) decode_combine_kernel(DecodeArgs a, int grid) {
+    const int w = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (w >= a.B * kHeads) return;
+    const int b = w / kHeads, h = w % kHeads;
+    const long long total = a.prefix[a.B];
+    const int G = ctas_in_use(total, grid);
+    const int c0 = cta_of(a.prefix[b], total, G), c1 = cta_of(a.prefix[b + 1] - 1, total, G);
+    if (c0 == c1) return;  // finished by its CTA
+    float mx = -1e30f;
+    for (int c = c0; c <= c1; ++c)
+        mx = fmaxf(mx, a.part[((long long)(b + c) * kHeads + h) * kPartStride + 64]);
+    float n0 = 0.f, n1 = 0.f, den = 0.f;
+    for (int c = c0; c <= c1; ++c) {
+        const float* rec = a.part + ((long long)(b + c) * kHeads + h) * kPartStride;
+        const float f = fast_exp2(rec[64] - mx);
+        den += f * rec[65];
+        n0 += f * rec[2 * lane];
+        n1 += f * rec[2 * lane + 1];
+    }
+    const float inv = 1.f / den;
+    const long long at = (long long)b * kRowWidth + h * kHeadDim + 2 * lane;
+    if (a.out_bf16) {
+        *reinterpret_cast<uint32_t*>(static_cast<__nv_bfloat16*>(a.out) + at) =
+            pack_bf16x2(n0 * inv, n1 * inv);
+    } else {
+        float2 o = make_float2(n0 * inv, n1 * inv);
+        *reinterpret_cast<float2*>(static_cast<float*>(a.out) + at) = o;
+    }
+}
+
+template <typename T>
+void launch_typed(const DecodeArgs& a, int grid, cudaStream_t s) {
+    static bool configured = false;  // per process; the attribute is per function and device
+    if (!configured) {
+        cudaFuncSetAttribute(decode_attn_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             kSmemBytes);
+        configured = true;
+    }
+    decode_attn_kernel<T><<<grid, kThreads, kSmemBytes, s>>>(a);
+    decode_combine_kernel<<<(a.B * kHeads + 7) / 8, 256, 0, s>>>(a, grid);
+}
+
+}  // namespace
+
+size_t decode_part_floats(int B, int grid) {
+    return (size_t)(B + grid) * kHeads * kPartStride;
+}
+
+void launch_decode_attn(const DecodeArgs& a, bool cache_bf16, int grid, cudaStream_t s) {
+    if (cache_bf16) launch_typed<__nv_bfloat16>(a, grid, s);
+    else launch_typed<float>(a, grid, s);
+}
+
+}  // namespace ptts

@@ -1,0 +1,139 @@
+// Internal launchers of the ptts_b200 kernels (not part of the C ABI).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace ptts {
+
+// Bits of the device-side error word. Kernels set these and return instead of trapping.
+enum : uint32_t {
+    DEV_ERR_BOUNDS = 1u,    // an index or position fell outside its buffer
+    DEV_ERR_CAPACITY = 2u,  // a stream's rows did not fit its capacity
+    DEV_ERR_TIMEOUT = 4u,   // a bounded mbarrier wait gave up
+};
+
+
+constexpr int kHeadDim = 64;   // D: the only head size the kernels implement
+constexpr int kRowWidth = 512; // H * D: one cache row of all heads
+constexpr int kMaxPairs = kHeadDim / 2;
+
+// Per-call row plan on the device: which arena stream and position each row has.
+struct RowPlan {
+    int32_t* row_stream = nullptr;  // [rows]
+    int32_t* row_pos = nullptr;     // [rows]
+    int32_t* prefix = nullptr;      // [rows + 1] decode only: prefix sums of attended keys
+};
+
+// ---- plans and bookkeeping (misc.cu) ---------------------------------------------------
+
+// Decode plan: one row per sequence. row_pos[i] = lengths[streams[i]]; prefix[i+1] =
+// sum_{j<=i} min(row_pos[j] + 1, capacity). Sets DEV_ERR_CAPACITY / DEV_ERR_BOUNDS.
+void launch_plan_decode(const int32_t* lengths, const int32_t* streams, int n, int num_streams,
+                        int capacity, RowPlan plan, uint32_t* err, cudaStream_t s);
+
+// Ragged plan: sequence i (stream seq_stream[i]) owns rows row_offsets[i]..row_offsets[i+1];
+// row r of it sits at lengths[stream] + (r - row_offsets[i]).
+void launch_plan_rows(const int32_t* lengths, const int32_t* seq_stream, const int32_t* row_offsets,
+                      int n_seq, int n_rows, int num_streams, int capacity, RowPlan plan,
+                      uint32_t* err, cudaStream_t s);
+
+// lengths[seq_stream[i]] += rows (row_offsets == nullptr) or row_offsets[i+1]-row_offsets[i].
+void launch_advance(int32_t* lengths, const int32_t* seq_stream, const int32_t* row_offsets,
+                    int n_seq, int rows, cudaStream_t s);
+
+// lengths[streams[i]] = values[i].
+void launch_set_lengths(int32_t* lengths, const int32_t* streams, const int32_t* values, int n,
+                        cudaStream_t s);
+
+// Zero `n` bytes of every listed stream's slots in every layer and set their lengths to 0.
+void launch_reset_streams(void* k, void* v, int32_t* lengths, const int32_t* streams, int n,
+                          int layers, long long layer_bytes, long long stream_bytes,
+                          cudaStream_t s);
+
+// bf16 -> f32 copy (the residual stream's start).
+void launch_bf16_to_f32(const __nv_bfloat16* x, float* y, long long n, cudaStream_t s);
+
+// ---- RoPE + append (rope_append.cu) ---------------------------------------------------
+
+struct RopeAppendArgs {
+    const void* q;         // [rows][H][D] in_dtype
+    const void* k;         // [rows][KVH][D]
+    const void* v;
+    void* q_out;           // [rows][H][D] cache dtype, rotated
+    void* k_cache;         // layer base [S][cap][H][D]
+    void* v_cache;
+    const int32_t* row_stream;
+    const int32_t* row_pos;
+    int rows, heads, kv_heads, num_streams, capacity;
+    float inv_freq[kMaxPairs];
+    uint32_t* err;
+};
+void launch_rope_append(const RopeAppendArgs& a, bool in_bf16, bool cache_bf16, cudaStream_t s);
+
+// ---- attention (attn_decode.cu, attn_prefill.cu) -----------------------------------------
+
+struct DecodeArgs {
+    const void* k_cache;      // layer base [S][cap][H][D]
+    const void* v_cache;
+    long long stream_bytes;   // capacity * row bytes
+    const int32_t* row_stream;  // [B] arena stream of each sequence
+    const int32_t* prefix;      // [B + 1] prefix sums of attended keys
+    const void* q;            // [B][H][D] cache dtype, rotated
+    void* out;                // [B][H*D]
+    int out_bf16;
+    float* part;              // [(B + grid) * H * kPartStride]
+    int B;
+    float qscale;             // 1/sqrt(D) * log2(e)
+    uint32_t* err;
+};
+constexpr int kPartStride = 68;  // floats per (slot, head) partial: acc[64], m, l, pad
+// Split-KV decode over the balanced partition of all attended keys, then the merge of the
+// streams that span more than one CTA. `grid` CTAs at most (one per SM).
+void launch_decode_attn(const DecodeArgs& a, bool cache_bf16, int grid, cudaStream_t s);
+size_t decode_part_floats(int B, int grid);
+
+struct PrefillArgs {
+    const void* k_cache;
+    const void* v_cache;
+    long long stream_elems;   // capacity * H * D
+    const int32_t* row_stream;
+    const int32_t* row_pos;
+    const void* q;            // [rows][H][D] cache dtype, rotated
+    void* out;                // [rows][H*D]
+    int out_bf16;
+    int rows;
+    float qscale;
+    uint32_t* err;
+};
+// Causal attention of every row over keys 0..=row_pos (CUDA cores, online softmax).
+void launch_prefill_attn(const PrefillArgs& a, bool cache_bf16, cudaStream_t s);
+
+// ---- int8 linear (linear.cu) ----------------------------------------------------------
+
+enum LinearEpi : int { EPI_F32 = 0, EPI_QKV = 1, EPI_RESID = 2, EPI_GELU = 3 };
+
+struct LinearArgs {
+    int M, N, K;
+    const __nv_bfloat16* a;   // A from global bf16 [M][K] (ln == false)
+    const float* x;           // A = LN(x) [M][K] f32 (ln == true)
+    const float* ln_g;
+    const float* ln_b;
+    const int8_t* w;          // [N][K]
+    const float* scale;       // [N]
+    float* y;                 // EPI_F32: [M][N]; EPI_RESID: [M][N] +=
+    __nv_bfloat16* yb;        // EPI_GELU: [M][N]; EPI_QKV: q_rot [M][H*D]
+    int gelu_tanh;
+    // EPI_QKV
+    const int32_t* row_stream;
+    const int32_t* row_pos;
+    __nv_bfloat16* k_cache;
+    __nv_bfloat16* v_cache;
+    int heads, kv_heads, num_streams, capacity;
+    float inv_freq[kMaxPairs];
+    uint32_t* err;
+};
+void launch_linear(const LinearArgs& a, bool ln, LinearEpi epi, cudaStream_t s);
+
+}  // namespace ptts

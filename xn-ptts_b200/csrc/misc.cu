@@ -1,0 +1,165 @@
+// Row plans, length bookkeeping and small conversions.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace ptts {
+namespace {
+
+constexpr int kPlanThreads = 1024;
+
+// One CTA: a running block scan over the sequences, 1024 at a time.
+__global__ void __launch_bounds__(kPlanThreads) plan_decode_kernel(
+    const int32_t* __restrict__ lengths, const int32_t* __restrict__ streams, int n,
+    int num_streams, int capacity, RowPlan plan, uint32_t* err) {
+    __shared__ int warp_tot[kPlanThreads / 32];
+    __shared__ int carry;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    if (tid == 0) {
+        carry = 0;
+        plan.prefix[0] = 0;
+    }
+    __syncthreads();
+    for (int base = 0; base < n; base += kPlanThreads) {
+        const int i = base + tid;
+        int keys = 0;
+        if (i < n) {
+            int sid = streams[i];
+            if (sid < 0 || sid >= num_streams) {
+                set_error(err, DEV_ERR_BOUNDS);
+                sid = 0;
+            }
+            const int len = lengths[sid];
+            if (len < 0 || len + 1 > capacity) set_error(err, DEV_ERR_CAPACITY);
+            plan.row_stream[i] = sid;
+            plan.row_pos[i] = len;
+            // Clamped so that a refused row never makes a kernel read past the stream's slots.
+            keys = min(max(len, 0) + 1, capacity);
+        }
+        int v = keys;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int t = __shfl_up_sync(0xffffffffu, v, o);
+            if (lane >= o) v += t;
+        }
+        if (lane == 31) warp_tot[warp] = v;
+        __syncthreads();
+        if (warp == 0) {
+            int w = warp_tot[lane];
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int t = __shfl_up_sync(0xffffffffu, w, o);
+                if (lane >= o) w += t;
+            }
+            warp_tot[lane] = w;  // inclusive
+        }
+        __syncthreads();
+        const int before = carry + (warp > 0 ? warp_tot[warp - 1] : 0);
+        if (i < n) plan.prefix[i + 1] = before + v;
+        __syncthreads();
+        if (tid == 0) carry += warp_tot[kPlanThreads / 32 - 1];
+        __syncthreads();
+    }
+}
+
+__global__ void plan_rows_kernel(const int32_t* __restrict__ lengths,
+                                 const int32_t* __restrict__ seq_stream,
+                                 const int32_t* __restrict__ row_offsets, int n_seq, int n_rows,
+                                 int num_streams, int capacity, RowPlan plan, uint32_t* err) {
+    const int r = blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= n_rows) return;
+    int lo = 0, hi = n_seq - 1;
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (row_offsets[mid] <= r) lo = mid;
+        else hi = mid - 1;
+    }
+    int sid = seq_stream[lo];
+    if (sid < 0 || sid >= num_streams) {
+        set_error(err, DEV_ERR_BOUNDS);
+        sid = 0;
+    }
+    const int pos = lengths[sid] + (r - row_offsets[lo]);
+    if (pos < 0 || pos >= capacity) set_error(err, DEV_ERR_CAPACITY);
+    plan.row_stream[r] = sid;
+    plan.row_pos[r] = pos;
+}
+
+__global__ void advance_kernel(int32_t* lengths, const int32_t* __restrict__ seq_stream,
+                               const int32_t* __restrict__ row_offsets, int n_seq, int rows) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n_seq) return;
+    const int add = row_offsets ? row_offsets[i + 1] - row_offsets[i] : rows;
+    lengths[seq_stream[i]] += add;
+}
+
+__global__ void set_lengths_kernel(int32_t* lengths, const int32_t* __restrict__ streams,
+                                   const int32_t* __restrict__ values, int n) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) lengths[streams[i]] = values[i];
+}
+
+__global__ void reset_streams_kernel(uint4* k, uint4* v, int32_t* lengths,
+                                     const int32_t* __restrict__ streams, int n, int layers,
+                                     long long layer_vec, long long stream_vec) {
+    const long long per = stream_vec * layers;
+    const long long total = per * n;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+         i += (long long)gridDim.x * blockDim.x) {
+        const int si = (int)(i / per);
+        const long long rem = i - si * per;
+        const int layer = (int)(rem / stream_vec);
+        const long long off = layer * layer_vec + (long long)streams[si] * stream_vec +
+                              (rem - layer * stream_vec);
+        k[off] = make_uint4(0, 0, 0, 0);
+        v[off] = make_uint4(0, 0, 0, 0);
+        if (rem == 0) lengths[streams[si]] = 0;
+    }
+}
+
+__global__ void bf16_to_f32_kernel(const __nv_bfloat16* __restrict__ x, float* __restrict__ y,
+                                   long long n) {
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+         i += (long long)gridDim.x * blockDim.x)
+        y[i] = __bfloat162float(x[i]);
+}
+
+}  // namespace
+
+void launch_plan_decode(const int32_t* lengths, const int32_t* streams, int n, int num_streams,
+                        int capacity, RowPlan plan, uint32_t* err, cudaStream_t s) {
+    plan_decode_kernel<<<1, kPlanThreads, 0, s>>>(lengths, streams, n, num_streams, capacity,
+                                                   plan, err);
+}
+
+void launch_plan_rows(const int32_t* lengths, const int32_t* seq_stream, const int32_t* row_offsets,
+                      int n_seq, int n_rows, int num_streams, int capacity, RowPlan plan,
+                      uint32_t* err, cudaStream_t s) {
+    plan_rows_kernel<<<(n_rows + 255) / 256, 256, 0, s>>>(lengths, seq_stream, row_offsets, n_seq,
+                                                          n_rows, num_streams, capacity, plan, err);
+}
+
+void launch_advance(int32_t* lengths, const int32_t* seq_stream, const int32_t* row_offsets,
+                    int n_seq, int rows, cudaStream_t s) {
+    advance_kernel<<<(n_seq + 255) / 256, 256, 0, s>>>(lengths, seq_stream, row_offsets, n_seq,
+                                                       rows);
+}
+
+void launch_set_lengths(int32_t* lengths, const int32_t* streams, const int32_t* values, int n,
+                        cudaStream_t s) {
+    set_lengths_kernel<<<(n + 255) / 256, 256, 0, s>>>(lengths, streams, values, n);
+}
+
+void launch_reset_streams(void* k, void* v, int32_t* lengths, const int32_t* streams, int n,
+                          int layers, long long layer_bytes, long long stream_bytes,
+                          cudaStream_t s) {
+    reset_streams_kernel<<<1184, 256, 0, s>>>(static_cast<uint4*>(k), static_cast<uint4*>(v),
+                                              lengths, streams, n, layers, layer_bytes / 16,
+                                              stream_bytes / 16);
+}
+
+void launch_bf16_to_f32(const __nv_bfloat16* x, float* y, long long n, cudaStream_t s) {
+    const long long blocks = (n + 255) / 256;
+    bf16_to_f32_kernel<<<(int)(blocks < 4096 ? blocks : 4096), 256, 0, s>>>(x, y, n);
+}
+
+}  // namespace ptts
