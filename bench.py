@@ -54,7 +54,8 @@ def peaks():
 
 
 def traffic_per_launch():
-    """Per-launch DRAM bytes of the decode-attention kernel from a committed ncu summary."""
+    """DRAM bytes / algorithmic bytes of the decode-attention kernel from a committed ncu
+    summary of a smaller case; traffic grows in proportion to the KV rows read."""
     path = os.path.join(ROOT, "profiles", "decode_attn_traffic.json")
     try:
         with open(path) as f:
@@ -223,7 +224,6 @@ def run_ours(args):
     model.load(weights)
     prefixes = shard_prefixes(wl, rank)
     B = STREAMS_PER_GPU
-    window = max(1, min(FRAMES, args.steps + args.warmup))
     cap = int(prefixes.max()) + FRAMES
     streams = np.arange(B, dtype=np.int32)
     stream = torch.cuda.current_stream()
@@ -306,29 +306,30 @@ def run_ours(args):
     # ---- traced pass: decode-attention launch durations with CUDA events ------------------------
     kv.set_lengths(streams, prefixes)
     state["f"] = 0
-    model.set_tracing(True)
-    model.trace(reset=True)
+    ptts.set_tracing(True)
+    ptts.trace(reset=True)
     traced = min(args.steps + args.warmup, FRAMES)
     for _ in range(traced):
         step(dev_src, y)
     torch.cuda.synchronize()
-    tr = model.trace(reset=True)
-    model.set_tracing(False)
+    tr = ptts.trace(reset=True)
+    ptts.set_tracing(False)
     peak, peak_kind = peaks()
     per_launch_bytes = tr["attn_bytes"] / max(tr["attn_launches"], 1)
     per_launch_ms = tr["attn_ms"] / max(tr["attn_launches"], 1)
     achieved = per_launch_bytes / (per_launch_ms / 1e3) / 1e9
     traffic = traffic_per_launch()
+    ratio = traffic.get("dram_over_algorithmic") if traffic else None
     roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                 "frac": achieved / peak, "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"
                 if peak_kind == "measured" else "fallback 6.65 TB/s",
-                "traffic": traffic.get("bytes_per_launch") if traffic else None,
+                "traffic": ratio * per_launch_bytes if ratio else None,
                 "kernel": "decode_attn_kernel<bf16> (split-KV)",
                 "algorithmic_bytes_per_launch": per_launch_bytes,
                 "launch_ms": per_launch_ms, "launches_timed": tr["attn_launches"],
                 "attn_share_of_traced_step": tr["attn_ms"] / max(tr["step_ms"], 1e-9)}
     if traffic:
-        roofline["traffic_source"] = traffic.get("source")
+        roofline["traffic_source"] = "scaled from profiles/decode_attn_traffic.json: " + traffic.get("source", "")
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -358,6 +359,86 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+def run_config3(args):
+    """Config 3 (seed 2): the attention op alone over 256 ragged streams (prefilled lengths
+    U{64..2048}, bf16 cache), one query per stream per step: RoPE + append + split-KV attention.
+    Steps cycle a 100-step window. value = algorithmic GB/s of the op (bytes per step: K and V
+    rows of every attended position + per stream 1 KB q, 2 KB appended k/v, 1 KB output)."""
+    import numpy as np
+    import torch
+
+    ptts, wl = load()
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda:0")
+    B, window = 256, 100
+    lengths = torch.randint(64, 2049, (B,), generator=torch.Generator().manual_seed(2)).numpy().astype(np.int32)
+    cap = int(lengths.max()) + window
+    kv = ptts.KvState(1, B, cap, dtype="bf16")
+    g = torch.Generator(device=dev).manual_seed(2)
+    kt, vt, _ = kv.tensors(0)
+    kt.normal_(generator=g)
+    vt.normal_(generator=g)
+    streams = np.arange(B, dtype=np.int32)
+    ones = np.ones(B, np.int32)
+    kv.set_lengths(streams, lengths)
+    pool = [torch.randn(window, B, 8, 64, generator=g, device=dev).bfloat16() for _ in range(3)]
+    out = torch.empty(B, 512, dtype=torch.bfloat16, device=dev)
+    state = {"s": 0}
+
+    def bytes_of_step(lens):
+        return float(((lens.astype(np.int64) + 1) * 2048).sum() + B * (1024 + 2048 + 1024))
+
+    def step(acc):
+        s = state["s"]
+        if s and s % window == 0:
+            kv.set_lengths(streams, lengths)
+        i = s % window
+        acc.append(bytes_of_step(lengths + i))
+        ptts.attend(kv, 0, pool[0][i], pool[1][i], pool[2][i], streams, ones, out=out)
+        kv.advance(streams, ones)
+        state["s"] = s + 1
+
+    junk = []
+    for _ in range(args.warmup):
+        step(junk)
+    torch.cuda.synchronize()
+    acc = []
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sampler = ClockSampler(0)
+    sampler.start()
+    e0.record()
+    for _ in range(args.steps):
+        step(acc)
+    e1.record()
+    e1.synchronize()
+    clocks = sampler.stop()
+    ms = e0.elapsed_time(e1)
+    gbs = sum(acc) / (ms / 1e3) / 1e9
+    kv.set_lengths(streams, lengths)
+    state["s"] = 0
+    ptts.set_tracing(True)
+    ptts.trace(reset=True)
+    for _ in range(min(args.steps, window)):
+        step(junk)
+    tr = ptts.trace(reset=True)
+    ptts.set_tracing(False)
+    peak, kind = peaks()
+    per_bytes = tr["attn_bytes"] / max(tr["attn_launches"], 1)
+    per_ms = tr["attn_ms"] / max(tr["attn_launches"], 1)
+    achieved = per_bytes / (per_ms / 1e3) / 1e9
+    print(json.dumps({
+        "metric": "decode attn GB/s (config 3: 256 ragged streams, L0 U{64..2048}, bf16 KV)",
+        "value": gbs, "unit": "GB/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms / args.steps, "higher_is_better": True, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "config3", "streams": B, "window": window},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "peak_kind": kind, "launch_ms": per_ms,
+                     "algorithmic_bytes_per_launch": per_bytes,
+                     "kernel": "decode_attn_kernel<bf16> + combine"},
+        "clocks": clocks}), flush=True)
+    kv.check()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -365,11 +446,15 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", choices=["config5", "config3"], default="config5",
+                    help="config5: the flow-LM frame (default); config3: the attention op alone")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be at least 3")
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload == "config3":
+        run_config3(args)
     else:
         run_ours(args)
 

@@ -201,8 +201,9 @@ int ptts_b200_step(ptts_b200_model* model, ptts_b200_kv* kv, const int32_t* stre
                    const void* x, float* y, void* cuda_stream);
 
 /* Tracing, the counterpart of the reference's `attn` / `transformer-layer` spans
- * (transformer.rs:182, :590): while on, ptts_b200_step runs its kernels outside the CUDA graph
- * with CUDA events around every decode-attention launch, and synchronises once per step. */
+ * (transformer.rs:182, :590), process-wide: while on, ptts_b200_step runs its kernels outside
+ * its CUDA graph and ptts_b200_attend (one row per sequence) runs as usual, both with CUDA events
+ * around every decode-attention launch and one synchronisation per call. */
 typedef struct {
     int64_t steps;            /* traced steps */
     int64_t attn_launches;    /* decode-attention launches timed */
@@ -212,9 +213,9 @@ typedef struct {
     double step_ms;           /* summed device time of the traced steps */
 } ptts_b200_trace;
 
-int ptts_b200_model_set_tracing(ptts_b200_model* model, int on);
+int ptts_b200_set_tracing(int on);
 /* Read (and with reset != 0, clear) the counters. */
-int ptts_b200_model_trace(ptts_b200_model* model, ptts_b200_trace* out, int reset);
+int ptts_b200_trace_read(ptts_b200_trace* out, int reset);
 
 #ifdef __cplusplus
 }

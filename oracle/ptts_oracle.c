@@ -105,15 +105,14 @@ int oracle_attend(const float* q, const float* k, const float* v, int H, int KVH
             for (int h = 0; h < H; h++) {
                 float* qh = qr + (int64_t)r * row + (int64_t)h * D;
                 memcpy(qh, q + (int64_t)r * row + (int64_t)h * D, sizeof(float) * D);
-                rope_at(qh, D, inv_freq, pos);
-                if (store_bf16) oracle_round_bf16(qh, D);
+                rope_at(qh, D, inv_freq, pos); /* q stays f32 in both modes */
             }
             for (int g = 0; g < KVH; g++) {
                 float kr[256], vr[256];
                 memcpy(kr, k + ((int64_t)r * KVH + g) * D, sizeof(float) * D);
                 memcpy(vr, v + ((int64_t)r * KVH + g) * D, sizeof(float) * D);
                 rope_at(kr, D, inv_freq, pos);
-                if (store_bf16) {
+                if (store_bf16 & ORACLE_ROUND_KV) {
                     oracle_round_bf16(kr, D);
                     oracle_round_bf16(vr, D);
                 }
@@ -337,7 +336,7 @@ int oracle_model_forward(const oracle_model* m, float* x, float* k_cache, float*
     for (int l = 0; l < d->num_layers && rc == 0; l++) {
         /* x + attn(norm1(x)) */
         oracle_layer_norm(x, d->ln1_g + (int64_t)l * dm, d->ln1_b + (int64_t)l * dm, rows, dm, 1e-5f, h);
-        if (store_bf16) oracle_round_bf16(h, (int64_t)rows * dm);
+        if (store_bf16 & ORACLE_ROUND_OPERANDS) oracle_round_bf16(h, (int64_t)rows * dm);
         linear_f32w(h, m->wq + (int64_t)l * nqkv * dm, d->s_qkv + l * sq, rows, nqkv, dm, g, qkv,
                     n_threads);
         for (int r = 0; r < rows; r++) { /* [q | k | v] on the last dim, transformer.rs:197-211 */
@@ -348,15 +347,15 @@ int oracle_model_forward(const oracle_model* m, float* x, float* k_cache, float*
         rc = oracle_attend(q, k, v, H, KVH, D, k_cache + l * cache_layer, v_cache + l * cache_layer,
                            num_streams, capacity, lengths, streams, row_offsets, n_seq,
                            d->max_period, store_bf16, a, n_threads);
-        if (store_bf16) oracle_round_bf16(a, (int64_t)rows * hd);
+        if (store_bf16 & ORACLE_ROUND_OPERANDS) oracle_round_bf16(a, (int64_t)rows * hd);
         linear_f32w(a, m->wo + (int64_t)l * dm * hd, d->s_out + l * so, rows, dm, hd, g, y, n_threads);
         for (int64_t i = 0; i < (int64_t)rows * dm; i++) x[i] += y[i];
         /* x + ff(norm2(x)) */
         oracle_layer_norm(x, d->ln2_g + (int64_t)l * dm, d->ln2_b + (int64_t)l * dm, rows, dm, 1e-5f, h);
-        if (store_bf16) oracle_round_bf16(h, (int64_t)rows * dm);
+        if (store_bf16 & ORACLE_ROUND_OPERANDS) oracle_round_bf16(h, (int64_t)rows * dm);
         linear_f32w(h, m->w1 + (int64_t)l * ff * dm, d->s_ff1 + l * s1, rows, ff, dm, g, f, n_threads);
         for (int64_t i = 0; i < (int64_t)rows * ff; i++) f[i] = oracle_gelu(f[i], d->gelu_tanh);
-        if (store_bf16) oracle_round_bf16(f, (int64_t)rows * ff);
+        if (store_bf16 & ORACLE_ROUND_OPERANDS) oracle_round_bf16(f, (int64_t)rows * ff);
         linear_f32w(f, m->w2 + (int64_t)l * dm * ff, d->s_ff2 + l * s2, rows, dm, ff, g, y, n_threads);
         for (int64_t i = 0; i < (int64_t)rows * dm; i++) x[i] += y[i];
     }

@@ -13,10 +13,11 @@
  *   - ptts/src/transformer.rs:1112-1164  (grouped-query == repeated heads, 1e-6)
  *   - ptts/src/transformer.rs:1169-1225  (device-position step == host step, 1e-6)
  *
- * Storage modes. `store_bf16 = 0` is the reference's CPU path (T = f32 everywhere). With
- * `store_bf16 = 1` the oracle rounds to bf16 exactly where the CUDA library stores bf16: the
- * rotated q, k and v rows, the normalised GEMM inputs, the attention output that feeds out_proj
- * and the GELU output; the residual stream stays f32.
+ * Storage modes (`store_bf16`, a bit mask). 0 is the reference's CPU path (T = f32 everywhere).
+ * ORACLE_ROUND_KV rounds the rotated k and the v rows to bf16 as they enter the cache, as the
+ * CUDA library stores them. ORACLE_ROUND_OPERANDS also rounds the GEMM inputs (the normalised
+ * rows, the attention output, the GELU output) to bf16, as a bf16-operand GEMM would. The rotated
+ * q and the residual stream stay f32 in every mode.
  */
 #ifndef PTTS_ORACLE_H
 #define PTTS_ORACLE_H
@@ -26,6 +27,9 @@
 #ifdef __cplusplus
 extern "C" {
 #endif
+
+#define ORACLE_ROUND_KV 1
+#define ORACLE_ROUND_OPERANDS 2
 
 /* bf16 <-> f32, round to nearest even (NaN kept quiet). */
 float oracle_bf16_to_f32(uint16_t h);

@@ -1,10 +1,11 @@
 """GPU parity of the attention op (ptts_b200_attend) against the CPU oracle.
 
 Metric: normwise = ||gpu - oracle||_inf / ||oracle||_inf; the bar is 2e-3 (bf16 storage, f32
-accumulation). `mirror` is the oracle rounding to bf16 where the library stores bf16 (the rotated
-q/k/v rows); `f32` is the reference's CPU semantics (no rounding anywhere). Attention outputs are
-compared in f32 (out_dtype f32) so the check sees the kernels, not the output's own rounding.
-Cache indexing and append positions are checked bit-exactly (which slots change).
+accumulation) against the `mirror` oracle, which rounds to bf16 where the library stores bf16
+(the rotated k and the v rows of the cache). Against `f32`, the reference's CPU semantics with no
+rounding anywhere, the difference is the bf16 cache itself; it is printed and bounded by
+F32_TOL. Attention outputs are compared in f32 (out_dtype f32) so the check sees the kernels,
+not the output's own rounding. Cache indexing and append positions are checked bit-exactly.
 """
 from __future__ import annotations
 
@@ -18,6 +19,7 @@ from conftest import GOLDEN, normwise
 
 pytestmark = pytest.mark.gpu
 TOL = 2e-3
+F32_TOL = 5e-3  # bf16 cache vs an all-f32 computation (storage rounding, not the kernels)
 
 
 def _wl(ptts):
@@ -69,7 +71,7 @@ def test_config2_prefill_256(ptts, oracle, cuda):
     kv.check()
     got = _f32(out)
     offs = [0, 256]
-    for store, tol in ((True, TOL), (False, TOL)):
+    for store, tol in ((True, TOL), (False, F32_TOL)):
         kc = np.zeros((1, 256, 8, 64), np.float32)
         vc = np.zeros_like(kc)
         want = oracle.attend(_f32(q), _f32(k), _f32(v), kc, vc, [0], [0], offs, store_bf16=store)
@@ -113,7 +115,7 @@ def test_config3_ragged_decode(ptts, oracle, cuda, steps, B):
         lengths += 1
     kv.check()
     print("config3 normwise mirror/f32:", worst)
-    assert worst[True] < TOL and worst[False] < TOL, worst
+    assert worst[True] < TOL and worst[False] < F32_TOL, worst
     np.testing.assert_array_equal(kv.lengths(), lengths)
 
 

@@ -2,7 +2,7 @@
 oracle's StreamingTransformer::forward restatement.
 
 Hidden states are the f32 residual stream after the last layer (per frame). The oracle runs in
-`mirror` mode (bf16 at the library's storage points: rotated q/k/v, normalised GEMM inputs, the
+`mirror` mode (bf16 at the library's storage points: rotated k and v in the cache, normalised GEMM inputs, the
 attention output and the GELU output). Metric: ||gpu - oracle||_inf / ||oracle||_inf <= 2e-3.
 """
 from __future__ import annotations
@@ -30,6 +30,13 @@ def _setup(ptts, oracle, cfg, seed, S, cap, cuda):
     return model, om, kv, np.zeros(shape, np.float32), np.zeros(shape, np.float32)
 
 
+def _report(name, got, want):
+    rowerr = np.abs(got - want).max(1) / np.abs(want).max()
+    print(f"{name}: normwise {normwise(got, want):.3e}, median row {np.median(rowerr):.2e}, "
+          f"rows > 1e-3: {(rowerr > 1e-3).sum()}/{len(rowerr)}")
+    return normwise(got, want)
+
+
 def test_prefill_then_decode_matches_the_oracle(ptts, oracle, cuda):
     """Ragged prompts (host path, t > 1) then host-position decode steps (t = 1), 31m shape."""
     import torch
@@ -43,9 +50,10 @@ def test_prefill_then_decode_matches_the_oracle(ptts, oracle, cuda):
     y = model.forward(kv, x.to(cuda), streams, rows)
     kv.check()
     lengths = np.zeros(S, np.int32)
+    kc32, vc32 = kc.copy(), vc.copy()
     want = om.forward(_f32(x), kc, vc, lengths, streams, offs, store_bf16=True)
-    err = normwise(_f32(y), want)
-    print("prefill normwise:", err)
+    err = _report("prefill vs mirror", _f32(y), want)
+    _report("prefill vs f32", _f32(y), om.forward(_f32(x), kc32, vc32, lengths, streams, offs, store_bf16=False))
     assert err < TOL
     for i, s in enumerate(streams):
         lengths[s] += rows[i]

@@ -37,7 +37,7 @@ EXPORTS = (
     "ptts_b200_last_error", "ptts_b200_version",
     "ptts_b200_kv_create", "ptts_b200_kv_destroy", "ptts_b200_kv_lengths",
     "ptts_b200_kv_pointers", "ptts_b200_kv_advance", "ptts_b200_kv_reset",
-    "ptts_b200_kv_set_lengths", "ptts_b200_model_set_tracing", "ptts_b200_model_trace",
+    "ptts_b200_kv_set_lengths", "ptts_b200_set_tracing", "ptts_b200_trace_read",
     "ptts_b200_kv_load_prefix", "ptts_b200_kv_copy_stream", "ptts_b200_kv_check",
     "ptts_b200_attend", "ptts_b200_linear_i8",
     "ptts_b200_model_create", "ptts_b200_model_destroy", "ptts_b200_model_load_layer",
@@ -71,7 +71,7 @@ class Config(ctypes.Structure):
 
 
 class Trace(ctypes.Structure):
-    """ptts_b200_trace: counters of traced steps (see Transformer.set_tracing)."""
+    """ptts_b200_trace: counters of traced decode-attention launches (see set_tracing)."""
     _fields_ = [("steps", ctypes.c_int64), ("attn_launches", ctypes.c_int64),
                 ("attn_ms", ctypes.c_double), ("attn_bytes", ctypes.c_double),
                 ("step_ms", ctypes.c_double)]
@@ -112,8 +112,8 @@ def lib() -> ctypes.CDLL:
         L.ptts_b200_kv_advance.argtypes = [P, IP, IP, I, P]
         L.ptts_b200_kv_reset.argtypes = [P, IP, I, P]
         L.ptts_b200_kv_set_lengths.argtypes = [P, IP, IP, I, P]
-        L.ptts_b200_model_set_tracing.argtypes = [P, I]
-        L.ptts_b200_model_trace.argtypes = [P, ctypes.POINTER(Trace), I]
+        L.ptts_b200_set_tracing.argtypes = [I]
+        L.ptts_b200_trace_read.argtypes = [ctypes.POINTER(Trace), I]
         L.ptts_b200_kv_load_prefix.argtypes = [P, I, I, P, P, I, I, P]
         L.ptts_b200_kv_copy_stream.argtypes = [P, I, P, I, P]
         L.ptts_b200_kv_check.argtypes = [P]
@@ -310,6 +310,18 @@ def attend(kv: KvState, layer: int, q, k, v, streams: Sequence[int], rows: Seque
     return out
 
 
+def set_tracing(on: bool):
+    """Process-wide: while on, Transformer.step runs un-graphed and it and attend() time every
+    decode-attention launch with CUDA events (one synchronisation per call)."""
+    _check(lib().ptts_b200_set_tracing(int(on)))
+
+
+def trace(reset: bool = False) -> dict:
+    t = Trace()
+    _check(lib().ptts_b200_trace_read(ctypes.byref(t), int(reset)))
+    return {n: getattr(t, n) for n, _ in Trace._fields_}
+
+
 def linear_i8(x, w, scale, stream=None):
     """y = x W^T with W = w * scale[:, None]: x [m, k] bf16, w [n, k] int8, scale [n] f32."""
     import torch
@@ -394,16 +406,6 @@ class Transformer:
                                        _dptr(out), _stream(stream)))
         return out
 
-    def set_tracing(self, on: bool):
-        """While on, step() times every decode-attention launch with CUDA events (un-graphed,
-        one synchronisation per step); read the counters with trace()."""
-        _check(lib().ptts_b200_model_set_tracing(self._h, int(on)))
-
-    def trace(self, reset: bool = False) -> dict:
-        t = Trace()
-        _check(lib().ptts_b200_model_trace(self._h, ctypes.byref(t), int(reset)))
-        return {n: getattr(t, n) for n, _ in Trace._fields_}
-
     def step(self, kv: KvState, streams: Sequence[int], x, *, out=None, stream=None):
         """StreamingTransformer::forward_step: one row per stream, positions on the device, one
         CUDA graph per stream set. x [n, d] bf16 and out [n, d] f32 may be CUDA or pinned host."""
@@ -443,9 +445,19 @@ class Weights:
                     norm1_bias=self.ln1_b[l], norm2_weight=self.ln2_g[l], norm2_bias=self.ln2_b[l])
 
 
-def random_weights(cfg: FlowLMConfig, seed: int, *, ln_random: bool = False) -> Weights:
-    """int8 ~ U{-127..127}, scales ~ U(0.005, 0.02) per output row, LN gamma 1 / beta 0 (or
-    random when ln_random, for tests)."""
+LN_GAIN = 1.0 / 16.0
+
+
+def random_weights(cfg: FlowLMConfig, seed: int, *, ln_random: bool = False,
+                   ln_gain: float = LN_GAIN) -> Weights:
+    """int8 ~ U{-127..127}, scales ~ U(0.005, 0.02) per output row, LayerNorm gain `ln_gain`
+    and bias 0 (or random affine parameters when ln_random, for tests).
+
+    The gain is 1/16 rather than 1: with these int8 scales a unit gain gives q and k entries of
+    std ~20 and attention logits of std ~430, an almost-argmax attention under which a one-ulp
+    bf16 difference anywhere flips near-tied keys and the hidden states of two correct
+    implementations part by O(1) within a few layers. Gain 1/16 gives logits of std ~1.7, the
+    regime of a trained model. The byte and flop counts are the same either way."""
     rng = np.random.default_rng(seed)
     L, d, hd = cfg.num_layers, cfg.d_model, cfg.num_heads * cfg.head_dim
     nqkv = hd + 2 * cfg.num_kv_heads * cfg.head_dim
@@ -465,6 +477,6 @@ def random_weights(cfg: FlowLMConfig, seed: int, *, ln_random: bool = False) -> 
         ln = [rng.uniform(0.5, 1.5, (L, d)).astype(np.float32), rng.normal(0, 0.1, (L, d)).astype(np.float32),
               rng.uniform(0.5, 1.5, (L, d)).astype(np.float32), rng.normal(0, 0.1, (L, d)).astype(np.float32)]
     else:
-        ln = [np.ones((L, d), np.float32), np.zeros((L, d), np.float32),
-              np.ones((L, d), np.float32), np.zeros((L, d), np.float32)]
+        ln = [np.full((L, d), ln_gain, np.float32), np.zeros((L, d), np.float32),
+              np.full((L, d), ln_gain, np.float32), np.zeros((L, d), np.float32)]
     return Weights(w_qkv, s_qkv, w_out, s_out, w_ff1, s_ff1, w_ff2, s_ff2, *ln)

@@ -5,6 +5,7 @@
 #include <cstring>
 #include <exception>
 #include <memory>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -90,27 +91,34 @@ struct DevBuf {
     }
 };
 
-// Pinned staging for small host -> device uploads; waits for the previous upload first.
+// Pinned staging for small host -> device uploads: a ring of slots, each reused only after its
+// previous copy has completed, so a call does not wait for the device's earlier work.
 struct Staging {
-    void* host = nullptr;
-    size_t bytes = 0;
-    cudaEvent_t done = nullptr;
+    static constexpr int kSlots = 16;
+    void* host[kSlots] = {};
+    size_t bytes[kSlots] = {};
+    cudaEvent_t done[kSlots] = {};
+    int next = 0;
     ~Staging() {
-        if (host) cudaFreeHost(host);
-        if (done) cudaEventDestroy(done);
+        for (int i = 0; i < kSlots; ++i) {
+            if (host[i]) cudaFreeHost(host[i]);
+            if (done[i]) cudaEventDestroy(done[i]);
+        }
     }
     void upload(void* dev, const void* src, size_t n, cudaStream_t s) {
-        if (!done) CK(cudaEventCreateWithFlags(&done, cudaEventDisableTiming));
-        CK(cudaEventSynchronize(done));
-        if (n > bytes) {
-            if (host) CK(cudaFreeHost(host));
-            host = nullptr;
-            CK(cudaMallocHost(&host, n));
-            bytes = n;
+        const int i = next;
+        next = (next + 1) % kSlots;
+        if (!done[i]) CK(cudaEventCreateWithFlags(&done[i], cudaEventDisableTiming));
+        CK(cudaEventSynchronize(done[i]));
+        if (n > bytes[i]) {
+            if (host[i]) CK(cudaFreeHost(host[i]));
+            host[i] = nullptr;
+            CK(cudaMallocHost(&host[i], n < 4096 ? 4096 : n));
+            bytes[i] = n < 4096 ? 4096 : n;
         }
-        std::memcpy(host, src, n);
-        CK(cudaMemcpyAsync(dev, host, n, cudaMemcpyHostToDevice, s));
-        CK(cudaEventRecord(done, s));
+        std::memcpy(host[i], src, n);
+        CK(cudaMemcpyAsync(dev, host[i], n, cudaMemcpyHostToDevice, s));
+        CK(cudaEventRecord(done[i], s));
     }
 };
 
@@ -128,6 +136,29 @@ void rope_inv_freq(int head_dim, float max_period, float* out) {
 
 constexpr float kLog2e = 1.4426950408889634f;
 
+// Process-wide tracing of decode-attention launches (ptts_b200_set_tracing).
+struct Tracer {
+    std::mutex mu;
+    bool on = false;
+    ptts_b200_trace t{};
+};
+Tracer& tracer() {
+    static Tracer t;
+    return t;
+}
+bool tracing_on() {
+    std::lock_guard<std::mutex> g(tracer().mu);
+    return tracer().on;
+}
+void trace_add(int64_t launches, double attn_ms, double attn_bytes, int64_t steps, double step_ms) {
+    std::lock_guard<std::mutex> g(tracer().mu);
+    tracer().t.attn_launches += launches;
+    tracer().t.attn_ms += attn_ms;
+    tracer().t.attn_bytes += attn_bytes;
+    tracer().t.steps += steps;
+    tracer().t.step_ms += step_ms;
+}
+
 }  // namespace
 
 struct ptts_b200_kv {
@@ -140,6 +171,11 @@ struct ptts_b200_kv {
     // scratch of the attention op
     DevBuf seq_stream, row_offsets, row_stream, row_pos, prefix, part, q_rot;
     Staging staging;
+    cudaEvent_t trace_ev[2] = {nullptr, nullptr};
+    ~ptts_b200_kv() {
+        for (cudaEvent_t e : trace_ev)
+            if (e) cudaEventDestroy(e);
+    }
 
     size_t layer_bytes() const { return (size_t)streams * capacity * row_bytes; }
     size_t stream_bytes() const { return (size_t)capacity * row_bytes; }
@@ -174,10 +210,7 @@ struct ptts_b200_model {
     Staging staging;
     std::unique_ptr<StepGraph> step;
     cudaStream_t capture_stream = nullptr;
-    // tracing
-    bool tracing = false;
-    std::vector<cudaEvent_t> events;  // [2 * layers] around attention, then step start / end
-    ptts_b200_trace trace{};
+    std::vector<cudaEvent_t> events;  // tracing: [2 * layers] around attention, step start / end
     ~ptts_b200_model() {
         step.reset();
         if (capture_stream) cudaStreamDestroy(capture_stream);
@@ -242,7 +275,7 @@ RowPlan make_plan(const ptts_b200_kv* kv, bool decode, const int32_t* d_seq_stre
 }
 
 void attention(const ptts_b200_kv* kv, int layer, bool decode, const RowPlan& plan, int n_rows,
-               const void* q_rot, void* out, bool out_bf16, DevBuf& part, cudaStream_t s) {
+               const float* q_rot, void* out, bool out_bf16, DevBuf& part, cudaStream_t s) {
     const bool bf16 = kv->dtype == PTTS_B200_BF16;
     const float qscale = (1.0f / sqrtf((float)kv->head_dim)) * kLog2e;  // transformer.rs:215
     if (decode) {
@@ -297,7 +330,7 @@ void check_model_kv(const ptts_b200_model* m, const ptts_b200_kv* kv) {
 
 struct LayerBuffers {
     float* resid;             // [rows][d_model] f32
-    __nv_bfloat16* q_rot;     // [rows][H*D]
+    float* q_rot;             // [rows][H*D] f32
     __nv_bfloat16* attn;      // [rows][H*D]
     __nv_bfloat16* ff;        // [rows][ff]
     DevBuf* part;
@@ -323,7 +356,7 @@ void run_layers(const ptts_b200_model* m, const ptts_b200_kv* kv, bool decode, c
         a.ln_b = L.ln1b.as<float>();
         a.w = L.w_qkv.as<int8_t>();
         a.scale = L.s_qkv.as<float>();
-        a.yb = b.q_rot;
+        a.yq = b.q_rot;
         a.row_stream = plan.row_stream;
         a.row_pos = plan.row_pos;
         a.k_cache = reinterpret_cast<__nv_bfloat16*>(kv->k_layer(l));
@@ -608,7 +641,7 @@ int ptts_b200_attend(ptts_b200_kv* kv, int layer, const void* q, const void* k, 
         ra.q = q;
         ra.k = k;
         ra.v = v;
-        ra.q_out = kv->q_rot.need((size_t)n_rows * kv->row_bytes);
+        ra.q_out = static_cast<float*>(kv->q_rot.need((size_t)n_rows * kRowWidth * sizeof(float)));
         ra.k_cache = kv->k_layer(layer);
         ra.v_cache = kv->v_layer(layer);
         ra.row_stream = plan.row_stream;
@@ -622,8 +655,25 @@ int ptts_b200_attend(ptts_b200_kv* kv, int layer, const void* q, const void* k, 
         ra.err = kv->err.as<uint32_t>();
         launch_rope_append(ra, in_dtype == PTTS_B200_BF16, kv->dtype == PTTS_B200_BF16, s);
         check_launch();
+        const bool trace = decode && tracing_on();
+        if (trace) {
+            for (auto& e : kv->trace_ev)
+                if (!e) CK(cudaEventCreate(&e));
+            CK(cudaEventRecord(kv->trace_ev[0], s));
+        }
         attention(kv, layer, decode, plan, n_rows, ra.q_out, out, out_dtype == PTTS_B200_BF16,
                   kv->part, s);
+        if (trace) {
+            CK(cudaEventRecord(kv->trace_ev[1], s));
+            CK(cudaEventSynchronize(kv->trace_ev[1]));
+            float ms = 0.f;
+            CK(cudaEventElapsedTime(&ms, kv->trace_ev[0], kv->trace_ev[1]));
+            double bytes = 0.0;
+            for (int i = 0; i < n_seq; ++i)
+                bytes += (double)(kv->h_len[streams_host[i]] + 1) * kv->row_bytes * 2;
+            bytes += (double)n_seq * kRowWidth * (4 + (out_dtype == PTTS_B200_BF16 ? 2 : 4));
+            trace_add(1, ms, bytes, 0, 0.0);
+        }
     });
 }
 
@@ -747,7 +797,7 @@ int ptts_b200_forward(ptts_b200_model* model, ptts_b200_kv* kv, const void* x,
         const size_t hd = (size_t)c.num_heads * c.head_dim;
         LayerBuffers b;
         b.resid = y;  // the residual stream lives in the caller's output
-        b.q_rot = static_cast<__nv_bfloat16*>(model->q_rot.need((size_t)rows * hd * 2));
+        b.q_rot = static_cast<float*>(model->q_rot.need((size_t)rows * hd * 4));
         b.attn = static_cast<__nv_bfloat16*>(model->attn.need((size_t)rows * hd * 2));
         b.ff = static_cast<__nv_bfloat16*>(model->ff.need((size_t)rows * c.dim_feedforward * 2));
         b.part = &model->part;
@@ -786,7 +836,7 @@ int ptts_b200_step(ptts_b200_model* model, ptts_b200_kv* kv, const int32_t* stre
             CK(cudaMemcpy(sid, streams_host, sizeof(int32_t) * n, cudaMemcpyHostToDevice));
             ng->x.need((size_t)n * c.d_model * 2);
             ng->resid.need((size_t)n * c.d_model * 4);
-            ng->q_rot.need((size_t)n * hd * 2);
+            ng->q_rot.need((size_t)n * hd * 4);
             ng->attn.need((size_t)n * hd * 2);
             ng->ff.need((size_t)n * c.dim_feedforward * 2);
             ng->part.need(sizeof(float) * decode_part_floats(n, sm_count(kv->device)));
@@ -801,7 +851,7 @@ int ptts_b200_step(ptts_b200_model* model, ptts_b200_kv* kv, const int32_t* stre
         plan.row_pos = g->row_pos.as<int32_t>();
         plan.prefix = g->prefix.as<int32_t>();
         const int32_t* sid = g->sid.as<int32_t>();
-        LayerBuffers b{g->resid.as<float>(), g->q_rot.as<__nv_bfloat16>(), g->attn.as<__nv_bfloat16>(),
+        LayerBuffers b{g->resid.as<float>(), g->q_rot.as<float>(), g->attn.as<__nv_bfloat16>(),
                        g->ff.as<__nv_bfloat16>(), &g->part};
         auto body = [&](cudaStream_t cs, cudaEvent_t* ev) {
             launch_plan_decode(kv->len.as<int32_t>(), sid, n, kv->streams, kv->capacity, plan,
@@ -813,7 +863,7 @@ int ptts_b200_step(ptts_b200_model* model, ptts_b200_kv* kv, const int32_t* stre
         };
         const size_t xb = (size_t)n * c.d_model * 2, yb = (size_t)n * c.d_model * 4;
         CK(cudaMemcpyAsync(g->x.p, x, xb, is_device_pointer(x) ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, s));
-        if (model->tracing) {
+        if (tracing_on()) {
             const int L = c.num_layers;
             if (model->events.size() < (size_t)(2 * L + 2)) {
                 for (cudaEvent_t e : model->events) cudaEventDestroy(e);
@@ -825,20 +875,18 @@ int ptts_b200_step(ptts_b200_model* model, ptts_b200_kv* kv, const int32_t* stre
             body(s, ev);
             CK(cudaEventRecord(ev[2 * L + 1], s));
             CK(cudaEventSynchronize(ev[2 * L + 1]));
-            double bytes = 0.0;
+            double bytes = 0.0;  // K and V rows read, f32 q read, bf16 output written
             for (int i = 0; i < n; ++i) bytes += (double)(kv->h_len[streams_host[i]] + 1) * kv->row_bytes * 2;
-            bytes += (double)n * kv->row_bytes * 2;  // q read, output written
+            bytes += (double)n * kRowWidth * (4 + 2);
+            double attn_ms = 0.0;
             for (int l = 0; l < L; ++l) {
                 float ms = 0.f;
                 CK(cudaEventElapsedTime(&ms, ev[2 * l], ev[2 * l + 1]));
-                model->trace.attn_ms += ms;
-                model->trace.attn_launches += 1;
-                model->trace.attn_bytes += bytes;
+                attn_ms += ms;
             }
             float ms = 0.f;
             CK(cudaEventElapsedTime(&ms, ev[2 * L], ev[2 * L + 1]));
-            model->trace.step_ms += ms;
-            model->trace.steps += 1;
+            trace_add(L, attn_ms, bytes * L, 1, ms);
         } else {
             if (!g->exec) {
                 cudaStream_t cs = model->capture_stream;
@@ -862,18 +910,19 @@ int ptts_b200_step(ptts_b200_model* model, ptts_b200_kv* kv, const int32_t* stre
     });
 }
 
-int ptts_b200_model_set_tracing(ptts_b200_model* model, int on) {
+int ptts_b200_set_tracing(int on) {
     return guarded([&] {
-        require(model != nullptr, PTTS_B200_ERR_ARG, "model is NULL");
-        model->tracing = on != 0;
+        std::lock_guard<std::mutex> g(tracer().mu);
+        tracer().on = on != 0;
     });
 }
 
-int ptts_b200_model_trace(ptts_b200_model* model, ptts_b200_trace* out, int reset) {
+int ptts_b200_trace_read(ptts_b200_trace* out, int reset) {
     return guarded([&] {
-        require(model != nullptr && out != nullptr, PTTS_B200_ERR_ARG, "NULL argument");
-        *out = model->trace;
-        if (reset) model->trace = ptts_b200_trace{};
+        require(out != nullptr, PTTS_B200_ERR_ARG, "out is NULL");
+        std::lock_guard<std::mutex> g(tracer().mu);
+        *out = tracer().t;
+        if (reset) tracer().t = ptts_b200_trace{};
     });
 }
 

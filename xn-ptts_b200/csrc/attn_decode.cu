@@ -78,6 +78,15 @@ __device__ __forceinline__ void load8(const unsigned char* head_row, int j, floa
     o[0] = a.x; o[1] = a.y; o[2] = a.z; o[3] = a.w;
     o[4] = b.x; o[5] = b.y; o[6] = b.z; o[7] = b.w;
 }
+// The f32 q slice that matches load8's dims for lane slice j.
+template <typename T>
+__device__ __forceinline__ void load_q(const float* qh, int j, float* o) {
+    const float4 a = *reinterpret_cast<const float4*>(qh + (sizeof(T) == 2 ? 8 * j : 4 * j));
+    const float4 b = *reinterpret_cast<const float4*>(qh + (sizeof(T) == 2 ? 8 * j + 4 : 32 + 4 * j));
+    o[0] = a.x; o[1] = a.y; o[2] = a.z; o[3] = a.w;
+    o[4] = b.x; o[5] = b.y; o[6] = b.z; o[7] = b.w;
+}
+
 template <typename T>
 __device__ __forceinline__ int dim_of(int j, int i) {
     if (sizeof(T) == 2) return 8 * j + i;
@@ -188,8 +197,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(DecodeArgs a) 
         const bool whole = pb >= start && pe <= end;
 
         float q[8];
-        load8(static_cast<const unsigned char*>(a.q) + ((long long)b * kHeads + h) * HB, j, q,
-              static_cast<T*>(nullptr));
+        load_q<T>(a.q + ((long long)b * kHeads + h) * kHeadDim, j, q);
 #pragma unroll
         for (int i = 0; i < 8; ++i) q[i] *= a.qscale;
         float m = -1e30f, l = 0.f, acc[8];

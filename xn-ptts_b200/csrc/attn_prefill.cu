@@ -55,7 +55,13 @@ __global__ void __launch_bounds__(256) prefill_attn_kernel(PrefillArgs a) {
     const T* kb = static_cast<const T*>(a.k_cache) + (long long)sid * a.stream_elems + h * kHeadDim;
     const T* vb = static_cast<const T*>(a.v_cache) + (long long)sid * a.stream_elems + h * kHeadDim;
     float q[8];
-    load8g(static_cast<const T*>(a.q) + ((long long)row * kHeads + h) * kHeadDim, j, q);
+    {
+        const float* qh = a.q + ((long long)row * kHeads + h) * kHeadDim;
+        const float4 x = *reinterpret_cast<const float4*>(qh + (sizeof(T) == 2 ? 8 * j : 4 * j));
+        const float4 y = *reinterpret_cast<const float4*>(qh + (sizeof(T) == 2 ? 8 * j + 4 : 32 + 4 * j));
+        q[0] = x.x; q[1] = x.y; q[2] = x.z; q[3] = x.w;
+        q[4] = y.x; q[5] = y.y; q[6] = y.z; q[7] = y.w;
+    }
 #pragma unroll
     for (int i = 0; i < 8; ++i) q[i] *= a.qscale;
     float m = -1e30f, l = 0.f, acc[8];

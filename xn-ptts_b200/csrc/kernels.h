@@ -61,7 +61,7 @@ struct RopeAppendArgs {
     const void* q;         // [rows][H][D] in_dtype
     const void* k;         // [rows][KVH][D]
     const void* v;
-    void* q_out;           // [rows][H][D] cache dtype, rotated
+    float* q_out;          // [rows][H][D] f32, rotated
     void* k_cache;         // layer base [S][cap][H][D]
     void* v_cache;
     const int32_t* row_stream;
@@ -80,7 +80,7 @@ struct DecodeArgs {
     long long stream_bytes;   // capacity * row bytes
     const int32_t* row_stream;  // [B] arena stream of each sequence
     const int32_t* prefix;      // [B + 1] prefix sums of attended keys
-    const void* q;            // [B][H][D] cache dtype, rotated
+    const float* q;           // [B][H][D] f32, rotated
     void* out;                // [B][H*D]
     int out_bf16;
     float* part;              // [(B + grid) * H * kPartStride]
@@ -100,7 +100,7 @@ struct PrefillArgs {
     long long stream_elems;   // capacity * H * D
     const int32_t* row_stream;
     const int32_t* row_pos;
-    const void* q;            // [rows][H][D] cache dtype, rotated
+    const float* q;           // [rows][H][D] f32, rotated
     void* out;                // [rows][H*D]
     int out_bf16;
     int rows;
@@ -123,7 +123,8 @@ struct LinearArgs {
     const int8_t* w;          // [N][K]
     const float* scale;       // [N]
     float* y;                 // EPI_F32: [M][N]; EPI_RESID: [M][N] +=
-    __nv_bfloat16* yb;        // EPI_GELU: [M][N]; EPI_QKV: q_rot [M][H*D]
+    __nv_bfloat16* yb;        // EPI_GELU: [M][N]
+    float* yq;                // EPI_QKV: rotated q [M][H*D] f32
     int gelu_tanh;
     // EPI_QKV
     const int32_t* row_stream;

@@ -13,7 +13,7 @@
 //             resid   y += acc * scale           (x + attn / x + ff, residual kept in f32)
 //             gelu    y = bf16(gelu(acc*scale))   (linear1 + activation)
 //             qkv     columns [q | k | v] (transformer.rs:197-211): q and k turned by RoPE at
-//                     the row's position (rope.rs:81-95), q stored bf16, k and v written into
+//                     the row's position (rope.rs:81-95), q kept f32, k and v written into
 //                     the cache slot of the row's stream (complete_kv, transformer.rs:84-91),
 //                     a KV head repeated over the query heads that share it.
 //
@@ -131,7 +131,7 @@ __device__ __forceinline__ void epilogue_pair(const LinearArgs& p, int m, int n,
         float x0 = v0, x1 = v1;
         if (n < hd) {
             rot(x0, x1, pos, p.inv_freq[d >> 1]);
-            *reinterpret_cast<uint32_t*>(p.yb + (long long)m * hd + n) = pack_bf16x2(x0, x1);
+            *reinterpret_cast<float2*>(p.yq + (long long)m * hd + n) = make_float2(x0, x1);
             return;
         }
         if (sid < 0 || sid >= p.num_streams || pos < 0 || pos >= p.capacity) {

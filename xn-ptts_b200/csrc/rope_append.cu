@@ -44,10 +44,10 @@ __global__ void rope_append_kernel(RopeAppendArgs a) {
         y0 = __fsub_rn(__fmul_rn(x0, cs), __fmul_rn(x1, sn));
         y1 = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, cs));
     }
-    if (slot < a.heads) {
-        T* dst = static_cast<T*>(a.q_out) + ((long long)row * a.heads + slot) * kHeadDim;
-        dst[2 * i] = from_f32<T>(y0);
-        dst[2 * i + 1] = from_f32<T>(y1);
+    if (slot < a.heads) {  // q stays f32: it is only read by this call's attention
+        float* dst = static_cast<float*>(a.q_out) + ((long long)row * a.heads + slot) * kHeadDim;
+        dst[2 * i] = y0;
+        dst[2 * i + 1] = y1;
         return;
     }
     const bool is_k = slot < a.heads + a.kv_heads;
