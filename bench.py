@@ -151,7 +151,7 @@ def cpu_baseline(ptts, wl, cfg, weights, steps: int | None = None, budget_s: flo
     lengths = np.zeros(n, np.int32)
     streams = np.arange(n, dtype=np.int32)
     threads = oracle.threads()
-    om.forward(x, kc, vc, lengths, streams, offs, store_bf16=True, n_threads=threads)
+    om.forward(x, kc, vc, lengths, streams, offs, store=oracle.ROUND_KV, n_threads=threads)
     lengths = prefixes.copy()
     one = np.arange(n + 1, dtype=np.int32)
     frames = [torch.randn(n, cfg.d_model, generator=g).bfloat16().float().numpy() for _ in range(8)]
@@ -159,7 +159,7 @@ def cpu_baseline(ptts, wl, cfg, weights, steps: int | None = None, budget_s: flo
     while True:
         if done and done % FRAMES == 0:
             lengths = prefixes.copy()
-        om.forward(frames[done % len(frames)], kc, vc, lengths, streams, one, store_bf16=True,
+        om.forward(frames[done % len(frames)], kc, vc, lengths, streams, one, store=oracle.ROUND_KV,
                    n_threads=threads)
         lengths += 1
         done += 1

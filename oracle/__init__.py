@@ -80,6 +80,11 @@ def _i32(a) -> np.ndarray:
     return np.ascontiguousarray(a, dtype=np.int32)
 
 
+# Storage modes of the oracle (bit mask): which tensors are rounded to bf16 where they are stored.
+ROUND_KV = 1        # the rotated k and the v rows entering the cache (the CUDA library's storage)
+ROUND_OPERANDS = 2  # the GEMM inputs: normalised rows, attention output, GELU output
+
+
 def threads() -> int:
     return len(os.sched_getaffinity(0))
 
@@ -120,7 +125,7 @@ def rope_table(head_dim: int, positions, max_period: float = 10000.0):
 
 
 def attend(q, k, v, k_cache, v_cache, lengths, streams, row_offsets, *, max_period=10000.0,
-           store_bf16=False, n_threads=None) -> np.ndarray:
+           store=0, n_threads=None) -> np.ndarray:
     """Rope + append + causal attention for a ragged batch (caches updated in place).
 
     q [rows, H, D], k/v [rows, KVH, D], caches [S, cap, H, D] float32 (modified in place).
@@ -136,7 +141,7 @@ def attend(q, k, v, k_cache, v_cache, lengths, streams, row_offsets, *, max_peri
     out = np.zeros((rows, H * D), np.float32)
     rc = lib().oracle_attend(_p(q), _p(k), _p(v), H, KVH, D, _p(k_cache), _p(v_cache), S, cap,
                              _p(lengths), _p(streams), _p(row_offsets), len(streams),
-                             max_period, int(store_bf16), _p(out), n_threads or threads())
+                             max_period, int(store), _p(out), n_threads or threads())
     if rc != 0:
         raise ValueError(f"oracle_attend failed with {rc}")
     return out
@@ -196,16 +201,16 @@ class Model:
             lib().oracle_model_free(self._h)
             self._h = None
 
-    def forward(self, x, k_cache, v_cache, lengths, streams, row_offsets, *, store_bf16=True,
+    def forward(self, x, k_cache, v_cache, lengths, streams, row_offsets, *, store=ROUND_KV,
                 n_threads=None) -> np.ndarray:
         """x [rows, d] (layer-0 input) -> last layer's output [rows, d]; caches
-        [L, S, cap, H, D] updated in place; lengths not advanced."""
+        [L, S, cap, H, D] updated in place; lengths not advanced. `store`: ROUND_* bit mask."""
         x = _f32(x).copy()
         S, cap = k_cache.shape[1:3]
         lengths, streams, row_offsets = _i32(lengths), _i32(streams), _i32(row_offsets)
         rc = lib().oracle_model_forward(self._h, _p(x), _p(k_cache), _p(v_cache), S, cap,
                                         _p(lengths), _p(streams), _p(row_offsets), len(streams),
-                                        int(store_bf16), n_threads or threads())
+                                        int(store), n_threads or threads())
         if rc != 0:
             raise ValueError(f"oracle_model_forward failed with {rc}")
         return x

@@ -74,7 +74,7 @@ def test_config2_prefill_256(ptts, oracle, cuda):
     for store, tol in ((True, TOL), (False, F32_TOL)):
         kc = np.zeros((1, 256, 8, 64), np.float32)
         vc = np.zeros_like(kc)
-        want = oracle.attend(_f32(q), _f32(k), _f32(v), kc, vc, [0], [0], offs, store_bf16=store)
+        want = oracle.attend(_f32(q), _f32(k), _f32(v), kc, vc, [0], [0], offs, store=oracle.ROUND_KV if store else 0)
         err = normwise(got, want)
         assert err < tol, (store, err)
         if store:
@@ -108,7 +108,7 @@ def test_config3_ragged_decode(ptts, oracle, cuda, steps, B):
         kv.advance(streams, np.ones(B, np.int32))
         got = _f32(out)
         offs = np.arange(B + 1, dtype=np.int32)
-        want = oracle.attend(_f32(q), _f32(k), _f32(v), kc, vc, lengths, streams, offs, store_bf16=True)
+        want = oracle.attend(_f32(q), _f32(k), _f32(v), kc, vc, lengths, streams, offs, store=oracle.ROUND_KV)
         want32 = oracle.attend(_f32(q), _f32(k), _f32(v), kc32, vc32, lengths, streams, offs)
         worst[True] = max(worst[True], normwise(got, want))
         worst[False] = max(worst[False], normwise(got, want32))
@@ -146,7 +146,7 @@ def test_split_kv_partition_edges(ptts, oracle, cuda):
         out = ptts.attend(kv, 0, q.to(cuda), k.to(cuda), v.to(cuda), streams, np.ones(B, np.int32),
                           out_dtype=out_dtype)
         want = oracle.attend(_f32(q), _f32(k), _f32(v), kv2_k, kv2_v, lengths, streams,
-                             np.arange(B + 1, dtype=np.int32), store_bf16=True)
+                             np.arange(B + 1, dtype=np.int32), store=oracle.ROUND_KV)
         tol = TOL if out_dtype == "f32" else TOL + 2 ** -8
         assert normwise(_f32(out), want) < tol, out_dtype
     kv.check()
@@ -205,7 +205,7 @@ def test_append_positions_are_exact_and_nothing_else_is_read(ptts, oracle, cuda)
     for s in range(S):
         kc[s, : lens[s]] = _f32(base[: lens[s]])
         vc[s, : lens[s]] = _f32(base[: lens[s]])
-    want = oracle.attend(_f32(q), _f32(k), _f32(v), kc, vc, lens, streams, [0, 1, 7, 10], store_bf16=True)
+    want = oracle.attend(_f32(q), _f32(k), _f32(v), kc, vc, lens, streams, [0, 1, 7, 10], store=oracle.ROUND_KV)
     assert normwise(_f32(out), want) < TOL
     vt = _f32(kv.tensors(0)[1])
     for s in range(S):

@@ -51,9 +51,9 @@ def test_prefill_then_decode_matches_the_oracle(ptts, oracle, cuda):
     kv.check()
     lengths = np.zeros(S, np.int32)
     kc32, vc32 = kc.copy(), vc.copy()
-    want = om.forward(_f32(x), kc, vc, lengths, streams, offs, store_bf16=True)
+    want = om.forward(_f32(x), kc, vc, lengths, streams, offs, store=oracle.ROUND_KV)
     err = _report("prefill vs mirror", _f32(y), want)
-    _report("prefill vs f32", _f32(y), om.forward(_f32(x), kc32, vc32, lengths, streams, offs, store_bf16=False))
+    _report("prefill vs f32", _f32(y), om.forward(_f32(x), kc32, vc32, lengths, streams, offs, store=0))
     assert err < TOL
     for i, s in enumerate(streams):
         lengths[s] += rows[i]
@@ -63,7 +63,7 @@ def test_prefill_then_decode_matches_the_oracle(ptts, oracle, cuda):
         xs = torch.randn(S, 512).bfloat16()
         order = list(range(S))
         y = model.forward(kv, xs.to(cuda), order, [1] * S)
-        want = om.forward(_f32(xs), kc, vc, lengths, order, np.arange(S + 1, dtype=np.int32), store_bf16=True)
+        want = om.forward(_f32(xs), kc, vc, lengths, order, np.arange(S + 1, dtype=np.int32), store=oracle.ROUND_KV)
         lengths += 1
         worst = max(worst, normwise(_f32(y), want))
     kv.check()
@@ -123,13 +123,13 @@ def test_config4_decode_frames(ptts, oracle, cuda):
     offs = np.arange(0, B * prefix + 1, prefix, dtype=np.int32)
     model.forward(kv, x.to(cuda), streams, [prefix] * B)
     lengths = np.zeros(B, np.int32)
-    om.forward(_f32(x), kc, vc, lengths, streams, offs, store_bf16=True)
+    om.forward(_f32(x), kc, vc, lengths, streams, offs, store=oracle.ROUND_KV)
     lengths += prefix
     errs = []
     for f in range(frames):
         xs = torch.randn(B, 512, generator=g).bfloat16()
         y = model.step(kv, streams, xs.to(cuda))
-        want = om.forward(_f32(xs), kc, vc, lengths, streams, np.arange(B + 1, dtype=np.int32), store_bf16=True)
+        want = om.forward(_f32(xs), kc, vc, lengths, streams, np.arange(B + 1, dtype=np.int32), store=oracle.ROUND_KV)
         lengths += 1
         errs.append(normwise(_f32(y), want))
     kv.check()

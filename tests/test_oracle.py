@@ -220,19 +220,19 @@ def test_model_forward_is_the_layer_composition(oracle, ptts):
     S, cap, rows = 2, 16, [3, 5]
     offs = np.array([0, 3, 8], np.int32)
     x = rng.normal(size=(8, 512)).astype(np.float32)
-    for store_bf16 in (False, True):
+    for store in (0, oracle.ROUND_KV, oracle.ROUND_KV | oracle.ROUND_OPERANDS):
         kc = np.zeros((2, S, cap, 8, 64), np.float32)
         vc = np.zeros_like(kc)
-        got = m.forward(x, kc, vc, [0, 0], [0, 1], offs, store_bf16=store_bf16)
+        got = m.forward(x, kc, vc, [0, 0], [0, 1], offs, store=store)
         h = x.copy()
         kc2, vc2 = np.zeros_like(kc), np.zeros_like(vc)
-        rb = oracle.round_bf16 if store_bf16 else (lambda a: a)
+        rb = oracle.round_bf16 if store & oracle.ROUND_OPERANDS else (lambda a: a)
         for l in range(2):
             n1 = rb(oracle.layer_norm(h, w.ln1_g[l], w.ln1_b[l]))
             qkv = oracle.linear_i8(n1, w.w_qkv[l], w.s_qkv[l])
             a = oracle.attend(qkv[:, :512].reshape(-1, 8, 64), qkv[:, 512:1024].reshape(-1, 8, 64),
                               qkv[:, 1024:].reshape(-1, 8, 64), kc2[l], vc2[l], [0, 0], [0, 1], offs,
-                              store_bf16=store_bf16)
+                              store=store & oracle.ROUND_KV)
             h = h + oracle.linear_i8(rb(a), w.w_out[l], w.s_out[l])
             n2 = rb(oracle.layer_norm(h, w.ln2_g[l], w.ln2_b[l]))
             f = oracle.linear_i8(n2, w.w_ff1[l], w.s_ff1[l])
