@@ -200,6 +200,32 @@ int ptts_b200_forward(ptts_b200_model* model, ptts_b200_kv* kv, const void* x,
 int ptts_b200_step(ptts_b200_model* model, ptts_b200_kv* kv, const int32_t* streams_host, int n,
                    const void* x, float* y, void* cuda_stream);
 
+/* ---------------------------------------------------------------------------------------
+ * Decode attention without allocation. No counterpart in the reference: it exists for callers
+ * that cannot call cudaMalloc/cudaFree while running (a real-time audio engine that plans every
+ * allocation ahead of the frame loop, a server that carves device memory out of its own pool, a
+ * host runtime that only hands over raw device pointers).
+ *
+ * Same arithmetic as ptts_b200_attend with one row per sequence, over a cache the caller owns:
+ * k_cache/v_cache [num_streams][capacity][8][64] (one layer, kv_dtype), lengths [num_streams]
+ * (device, read and NOT advanced), streams [n] (device), q [n][8][64], k and v [n][KVH][64]
+ * (in_dtype), out [n][512] (out_dtype). Row i is rotated at position lengths[streams[i]], its k
+ * and v are written to that slot, and it attends to keys 0..=that position. Kernels that find a
+ * position past `capacity` skip it and set bits in *err (device word, may be NULL).
+ *
+ * Working memory comes from one fixed array in the library (about 4.6 MB per GPU, held until
+ * the process exits); n above 1024 is refused with PTTS_B200_ERR_ARG. Every call on a device
+ * shares that array, so two calls whose kernels overlap on the GPU (different streams, no
+ * ordering between them) race and both results are undefined; order them on one stream. The
+ * first call on a device looks the array's address up (cudaGetSymbolAddress) with that device
+ * current; make that first call before any stream capture. No call allocates or frees memory.
+ * ------------------------------------------------------------------------------------- */
+int ptts_b200_attend_decode_noalloc(void* k_cache, void* v_cache, int num_streams, int capacity,
+                                    int kv_dtype, const int32_t* lengths, const int32_t* streams,
+                                    int n, const void* q, const void* k, const void* v,
+                                    int in_dtype, int num_kv_heads, float max_period, void* out,
+                                    int out_dtype, uint32_t* err, void* cuda_stream);
+
 /* Tracing, the counterpart of the reference's `attn` / `transformer-layer` spans
  * (transformer.rs:182, :590), process-wide: while on, ptts_b200_step runs its kernels outside
  * its CUDA graph and ptts_b200_attend (one row per sequence) runs as usual, both with CUDA events

@@ -41,7 +41,7 @@ EXPORTS = (
     "ptts_b200_kv_load_prefix", "ptts_b200_kv_copy_stream", "ptts_b200_kv_check",
     "ptts_b200_attend", "ptts_b200_linear_i8",
     "ptts_b200_model_create", "ptts_b200_model_destroy", "ptts_b200_model_load_layer",
-    "ptts_b200_forward", "ptts_b200_step",
+    "ptts_b200_forward", "ptts_b200_step", "ptts_b200_attend_decode_noalloc",
 )
 
 
@@ -125,6 +125,7 @@ def lib() -> ctypes.CDLL:
         L.ptts_b200_model_load_layer.argtypes = [P, I, ctypes.POINTER(LayerWeights)]
         L.ptts_b200_forward.argtypes = [P, P, P, IP, IP, I, P, P]
         L.ptts_b200_step.argtypes = [P, P, IP, I, P, P, P]
+        L.ptts_b200_attend_decode_noalloc.argtypes = [P, P, I, I, I, P, P, I, P, P, P, I, I, F, P, I, P, P]
         _lib = L
     return _lib
 
@@ -320,6 +321,23 @@ def trace(reset: bool = False) -> dict:
     t = Trace()
     _check(lib().ptts_b200_trace_read(ctypes.byref(t), int(reset)))
     return {n: getattr(t, n) for n, _ in Trace._fields_}
+
+
+def attend_decode_noalloc(k_cache, v_cache, lengths, streams, q, k, v, *, out, err=None,
+                          max_period: float = 10000.0, stream=None):
+    """ptts_b200_attend_decode_noalloc: one decode row per stream over a caller-owned cache,
+    with no device allocation inside the call (for hosts that cannot allocate while running).
+
+    k_cache/v_cache [S, cap, 8, 64] (CUDA, bf16 or f32), lengths [S] int32 (CUDA, not advanced),
+    streams [n] int32 (CUDA), q [n, 8, 64], k/v [n, KVH, 64], out [n, 512] (all preallocated by
+    the caller), err an optional CUDA uint32/int32 word for device-side range errors."""
+    S, cap = int(k_cache.shape[0]), int(k_cache.shape[1])
+    _check(lib().ptts_b200_attend_decode_noalloc(
+        _dptr(k_cache), _dptr(v_cache), S, cap, _dtype_code(k_cache), _dptr(lengths),
+        _dptr(streams), int(streams.shape[0]), _dptr(q), _dptr(k), _dptr(v), _dtype_code(q),
+        int(k.shape[1]), max_period, _dptr(out), _dtype_code(out),
+        _dptr(err) if err is not None else None, _stream(stream)))
+    return out
 
 
 def linear_i8(x, w, scale, stream=None):

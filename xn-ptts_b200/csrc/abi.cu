@@ -425,6 +425,9 @@ bool is_device_pointer(const void* p) {
 
 }  // namespace
 
+// Lets other translation units of the library set this thread's last error.
+void ptts_b200_set_last_error(const std::string& msg) { g_last_error = msg; }
+
 extern "C" {
 
 const char* ptts_b200_last_error(void) { return g_last_error.c_str(); }
