@@ -286,7 +286,8 @@ def run_ours(args):
     ms = timed(dev_src, y, args.steps)
     clocks = sampler.stop()
     value = world * B * args.steps / (ms / 1e3)
-    launches_per_step = 3 + 6 * L
+    launches_per_step = 3 + 8 * L  # plan, final reduce, advance + per layer LN1, in_proj,
+    #                                 attention, merge, out_proj, LN2, linear1, linear2
     gpu_launches = args.steps * launches_per_step + (args.warmup + args.steps) // FRAMES
 
     # ---- end to end through pinned host buffers ------------------------------------------------

@@ -122,6 +122,22 @@ struct Staging {
     }
 };
 
+// Per-call activations of the layer stack (device, sized for `rows` rows).
+struct Workspace {
+    DevBuf q_rot, h_hi, h_lo, attn_hi, attn_lo, ff_hi, ff_lo, split, part;
+    void size(const ptts_b200_config& c, int rows) {
+        const size_t r = (size_t)rows, hd = (size_t)c.num_heads * c.head_dim;
+        q_rot.need(r * hd * 4);
+        h_hi.need(r * c.d_model * 2);
+        h_lo.need(r * c.d_model * 2);
+        attn_hi.need(r * hd * 2);
+        attn_lo.need(r * hd * 2);
+        ff_hi.need(r * c.dim_feedforward * 2);
+        ff_lo.need(r * c.dim_feedforward * 2);
+        split.need(4 * r * c.d_model * 4);
+    }
+};
+
 int sm_count(int dev) {
     int n = 0;
     CK(cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev));
@@ -189,7 +205,8 @@ struct StepGraph {
     uint64_t kv_uid = 0;
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t exec = nullptr;
-    DevBuf sid, x, resid, q_rot, attn, ff, row_stream, row_pos, prefix, part;
+    DevBuf sid, x, resid, row_stream, row_pos, prefix;
+    Workspace ws;
     ~StepGraph() {
         if (exec) cudaGraphExecDestroy(exec);
         if (graph) cudaGraphDestroy(graph);
@@ -206,7 +223,8 @@ struct ptts_b200_model {
     };
     std::vector<std::unique_ptr<Layer>> layers;
     // forward() workspace
-    DevBuf seq_stream, row_offsets, row_stream, row_pos, prefix, part, q_rot, attn, ff;
+    DevBuf seq_stream, row_stream, row_pos, prefix;
+    Workspace ws;
     Staging staging;
     std::unique_ptr<StepGraph> step;
     cudaStream_t capture_stream = nullptr;
@@ -275,7 +293,8 @@ RowPlan make_plan(const ptts_b200_kv* kv, bool decode, const int32_t* d_seq_stre
 }
 
 void attention(const ptts_b200_kv* kv, int layer, bool decode, const RowPlan& plan, int n_rows,
-               const float* q_rot, void* out, bool out_bf16, DevBuf& part, cudaStream_t s) {
+               const float* q_rot, void* out, void* out_lo, int out_mode, DevBuf& part,
+               cudaStream_t s) {
     const bool bf16 = kv->dtype == PTTS_B200_BF16;
     const float qscale = (1.0f / sqrtf((float)kv->head_dim)) * kLog2e;  // transformer.rs:215
     if (decode) {
@@ -288,7 +307,8 @@ void attention(const ptts_b200_kv* kv, int layer, bool decode, const RowPlan& pl
         a.prefix = plan.prefix;
         a.q = q_rot;
         a.out = out;
-        a.out_bf16 = out_bf16;
+        a.out_lo = out_lo;
+        a.out_mode = out_mode;
         a.part = static_cast<float*>(part.need(sizeof(float) * decode_part_floats(n_rows, grid)));
         a.B = n_rows;
         a.qscale = qscale;
@@ -303,7 +323,8 @@ void attention(const ptts_b200_kv* kv, int layer, bool decode, const RowPlan& pl
         a.row_pos = plan.row_pos;
         a.q = q_rot;
         a.out = out;
-        a.out_bf16 = out_bf16;
+        a.out_lo = out_lo;
+        a.out_mode = out_mode;
         a.rows = n_rows;
         a.qscale = qscale;
         a.err = kv->err.as<uint32_t>();
@@ -328,35 +349,77 @@ void check_model_kv(const ptts_b200_model* m, const ptts_b200_kv* kv) {
                 "layer " + std::to_string(l) + " has no weights (ptts_b200_model_load_layer)");
 }
 
-struct LayerBuffers {
-    float* resid;             // [rows][d_model] f32
-    float* q_rot;             // [rows][H*D] f32
-    __nv_bfloat16* attn;      // [rows][H*D]
-    __nv_bfloat16* ff;        // [rows][ff]
-    DevBuf* part;
-};
+// Split-K slices of out_proj and linear2 at a row count: enough CTAs to fill the GPU at decode
+// sizes, none for prompts; K / splits stays a multiple of 64.
+int split_for(int rows, int k, int want) {
+    if (rows >= 1024) return 1;
+    int sp = want;
+    while (sp > 1 && (k % sp != 0 || (k / sp) % 64 != 0)) sp /= 2;
+    return sp;
+}
 
-// StreamingTransformerLayer::forward (transformer.rs:591-634) for every layer.
+// StreamingTransformer::forward / forward_step body (transformer.rs:591-634 for every layer):
+//   LN1 (+ previous layer's split-K slices) -> in_proj (RoPE + append) -> attention ->
+//   out_proj (split-K) -> LN2 (+ slices) -> linear1 + GELU -> linear2 (split-K),
+// then a last reduction into the residual. x_in (bf16) seeds the f32 residual `resid`.
 void run_layers(const ptts_b200_model* m, const ptts_b200_kv* kv, bool decode, const RowPlan& plan,
-                int rows, const LayerBuffers& b, cudaStream_t s, cudaEvent_t* attn_ev = nullptr) {
+                int rows, const __nv_bfloat16* x_in, float* resid, Workspace& w, cudaStream_t s,
+                cudaEvent_t* attn_ev = nullptr) {
     const ptts_b200_config& c = m->cfg;
     const int hd = c.num_heads * c.head_dim;
     const int nqkv = hd + 2 * c.num_kv_heads * c.head_dim;
+    const int s_out = split_for(rows, hd, 2), s_ff2 = split_for(rows, c.dim_feedforward, 4);
+    uint32_t* err = kv->err.as<uint32_t>();
+    auto* h_hi = w.h_hi.as<__nv_bfloat16>();
+    auto* h_lo = w.h_lo.as<__nv_bfloat16>();
+    auto* split = w.split.as<float>();
+    int pending = 0;  // split-K slices not yet added to the residual
+    auto ln = [&](const float* g, const float* b, const __nv_bfloat16* x_bf16, bool normalise) {
+        LnArgs a{};
+        a.M = rows;
+        a.d = c.d_model;
+        a.resid = resid;
+        a.x_bf16 = x_bf16;
+        a.part = split;
+        a.nsplit = pending;
+        a.gamma = g;
+        a.beta = b;
+        a.hi = normalise ? h_hi : nullptr;
+        a.lo = normalise ? h_lo : nullptr;
+        launch_ln(a, s);
+        check_launch();
+        pending = 0;
+    };
+    auto residual_gemm = [&](const __nv_bfloat16* a_hi, const __nv_bfloat16* a_lo, const DevBuf& wq,
+                             const DevBuf& sc, int k, int splits) {
+        LinearArgs o{};
+        o.M = rows;
+        o.N = c.d_model;
+        o.K = k;
+        o.splits = splits;
+        o.a = a_hi;
+        o.a_lo = a_lo;
+        o.w = wq.as<int8_t>();
+        o.scale = sc.as<float>();
+        o.y = splits > 1 ? split : resid;
+        o.err = err;
+        launch_linear(o, splits > 1 ? EPI_PARTIAL : EPI_RESID, s);
+        check_launch();
+        if (splits > 1) pending = splits;
+    };
     for (int l = 0; l < c.num_layers; ++l) {
         const auto& L = *m->layers[l];
+        ln(L.ln1g.as<float>(), L.ln1b.as<float>(), l == 0 ? x_in : nullptr, true);
+        // in_proj, RoPE + append epilogue
         LinearArgs a{};
         a.M = rows;
-        a.err = kv->err.as<uint32_t>();
-        a.gelu_tanh = c.gelu;
-        // in_proj with LN1 prologue, RoPE + append epilogue
         a.N = nqkv;
         a.K = c.d_model;
-        a.x = b.resid;
-        a.ln_g = L.ln1g.as<float>();
-        a.ln_b = L.ln1b.as<float>();
+        a.a = h_hi;
+        a.a_lo = h_lo;
         a.w = L.w_qkv.as<int8_t>();
         a.scale = L.s_qkv.as<float>();
-        a.yq = b.q_rot;
+        a.yq = w.q_rot.as<float>();
         a.row_stream = plan.row_stream;
         a.row_pos = plan.row_pos;
         a.k_cache = reinterpret_cast<__nv_bfloat16*>(kv->k_layer(l));
@@ -366,52 +429,38 @@ void run_layers(const ptts_b200_model* m, const ptts_b200_kv* kv, bool decode, c
         a.num_streams = kv->streams;
         a.capacity = kv->capacity;
         std::memcpy(a.inv_freq, m->inv_freq, sizeof(a.inv_freq));
-        launch_linear(a, true, EPI_QKV, s);
+        a.err = err;
+        launch_linear(a, EPI_QKV, s);
         check_launch();
         // attention over the cache
         if (attn_ev) CK(cudaEventRecord(attn_ev[2 * l], s));
-        attention(kv, l, decode, plan, rows, b.q_rot, b.attn, true, *b.part, s);
+        attention(kv, l, decode, plan, rows, w.q_rot.as<float>(), w.attn_hi.p, w.attn_lo.p,
+                  kOutHiLo, w.part, s);
         if (attn_ev) CK(cudaEventRecord(attn_ev[2 * l + 1], s));
         // out_proj + residual
-        LinearArgs o{};
-        o.M = rows;
-        o.N = c.d_model;
-        o.K = hd;
-        o.a = b.attn;
-        o.w = L.w_out.as<int8_t>();
-        o.scale = L.s_out.as<float>();
-        o.y = b.resid;
-        o.err = a.err;
-        launch_linear(o, false, EPI_RESID, s);
-        check_launch();
-        // linear1 with LN2 prologue and GELU
+        residual_gemm(w.attn_hi.as<__nv_bfloat16>(), w.attn_lo.as<__nv_bfloat16>(), L.w_out, L.s_out,
+                      hd, s_out);
+        // LN2, linear1 + GELU
+        ln(L.ln2g.as<float>(), L.ln2b.as<float>(), nullptr, true);
         LinearArgs f1{};
         f1.M = rows;
         f1.N = c.dim_feedforward;
         f1.K = c.d_model;
-        f1.x = b.resid;
-        f1.ln_g = L.ln2g.as<float>();
-        f1.ln_b = L.ln2b.as<float>();
+        f1.a = h_hi;
+        f1.a_lo = h_lo;
         f1.w = L.w1.as<int8_t>();
         f1.scale = L.s1.as<float>();
-        f1.yb = b.ff;
+        f1.yb = w.ff_hi.as<__nv_bfloat16>();
+        f1.yb_lo = w.ff_lo.as<__nv_bfloat16>();
         f1.gelu_tanh = c.gelu;
-        f1.err = a.err;
-        launch_linear(f1, true, EPI_GELU, s);
+        f1.err = err;
+        launch_linear(f1, EPI_GELU, s);
         check_launch();
         // linear2 + residual
-        LinearArgs f2{};
-        f2.M = rows;
-        f2.N = c.d_model;
-        f2.K = c.dim_feedforward;
-        f2.a = b.ff;
-        f2.w = L.w2.as<int8_t>();
-        f2.scale = L.s2.as<float>();
-        f2.y = b.resid;
-        f2.err = a.err;
-        launch_linear(f2, false, EPI_RESID, s);
-        check_launch();
+        residual_gemm(w.ff_hi.as<__nv_bfloat16>(), w.ff_lo.as<__nv_bfloat16>(), L.w2, L.s2,
+                      c.dim_feedforward, s_ff2);
     }
+    if (pending) ln(nullptr, nullptr, nullptr, false);
 }
 
 bool is_device_pointer(const void* p) {
@@ -664,8 +713,8 @@ int ptts_b200_attend(ptts_b200_kv* kv, int layer, const void* q, const void* k, 
                 if (!e) CK(cudaEventCreate(&e));
             CK(cudaEventRecord(kv->trace_ev[0], s));
         }
-        attention(kv, layer, decode, plan, n_rows, ra.q_out, out, out_dtype == PTTS_B200_BF16,
-                  kv->part, s);
+        attention(kv, layer, decode, plan, n_rows, ra.q_out, out, nullptr,
+                  out_dtype == PTTS_B200_BF16 ? kOutBf16 : kOutF32, kv->part, s);
         if (trace) {
             CK(cudaEventRecord(kv->trace_ev[1], s));
             CK(cudaEventSynchronize(kv->trace_ev[1]));
@@ -695,7 +744,7 @@ int ptts_b200_linear_i8(int device, const void* x, const int8_t* w, const float*
         a.w = w;
         a.scale = scale;
         a.y = y;
-        launch_linear(a, false, EPI_F32, as_stream(cuda_stream));
+        launch_linear(a, EPI_F32, as_stream(cuda_stream));
         check_launch();
     });
 }
@@ -797,16 +846,9 @@ int ptts_b200_forward(ptts_b200_model* model, ptts_b200_kv* kv, const void* x,
         const RowPlan plan = make_plan(kv, decode, d, d + n_seq, n_seq, rows, model->row_stream,
                                        model->row_pos, model->prefix, s);
         check_launch();
-        const size_t hd = (size_t)c.num_heads * c.head_dim;
-        LayerBuffers b;
-        b.resid = y;  // the residual stream lives in the caller's output
-        b.q_rot = static_cast<float*>(model->q_rot.need((size_t)rows * hd * 4));
-        b.attn = static_cast<__nv_bfloat16*>(model->attn.need((size_t)rows * hd * 2));
-        b.ff = static_cast<__nv_bfloat16*>(model->ff.need((size_t)rows * c.dim_feedforward * 2));
-        b.part = &model->part;
-        launch_bf16_to_f32(static_cast<const __nv_bfloat16*>(x), y, (long long)rows * c.d_model, s);
-        check_launch();
-        run_layers(model, kv, decode, plan, rows, b, s);
+        model->ws.size(c, rows);
+        // The residual stream lives in the caller's output y.
+        run_layers(model, kv, decode, plan, rows, static_cast<const __nv_bfloat16*>(x), y, model->ws, s);
         launch_advance(kv->len.as<int32_t>(), d, d + n_seq, n_seq, 0, s);
         check_launch();
         for (int i = 0; i < n_seq; ++i) kv->h_len[streams_host[i]] += rows_host[i];
@@ -823,7 +865,6 @@ int ptts_b200_step(ptts_b200_model* model, ptts_b200_kv* kv, const int32_t* stre
         DeviceScope scope(model->device);
         cudaStream_t s = as_stream(cuda_stream);
         const ptts_b200_config& c = model->cfg;
-        const size_t hd = (size_t)c.num_heads * c.head_dim;
         StepGraph* g = model->step.get();
         const bool same = g && g->kv == kv && g->kv_uid == kv->uid && g->streams.size() == (size_t)n &&
                           std::memcmp(g->streams.data(), streams_host, sizeof(int32_t) * n) == 0;
@@ -839,10 +880,8 @@ int ptts_b200_step(ptts_b200_model* model, ptts_b200_kv* kv, const int32_t* stre
             CK(cudaMemcpy(sid, streams_host, sizeof(int32_t) * n, cudaMemcpyHostToDevice));
             ng->x.need((size_t)n * c.d_model * 2);
             ng->resid.need((size_t)n * c.d_model * 4);
-            ng->q_rot.need((size_t)n * hd * 4);
-            ng->attn.need((size_t)n * hd * 2);
-            ng->ff.need((size_t)n * c.dim_feedforward * 2);
-            ng->part.need(sizeof(float) * decode_part_floats(n, sm_count(kv->device)));
+            ng->ws.size(c, n);
+            ng->ws.part.need(sizeof(float) * decode_part_floats(n, sm_count(kv->device)));
             ng->row_stream.need(sizeof(int32_t) * n);
             ng->row_pos.need(sizeof(int32_t) * n);
             ng->prefix.need(sizeof(int32_t) * (n + 1));
@@ -854,13 +893,11 @@ int ptts_b200_step(ptts_b200_model* model, ptts_b200_kv* kv, const int32_t* stre
         plan.row_pos = g->row_pos.as<int32_t>();
         plan.prefix = g->prefix.as<int32_t>();
         const int32_t* sid = g->sid.as<int32_t>();
-        LayerBuffers b{g->resid.as<float>(), g->q_rot.as<float>(), g->attn.as<__nv_bfloat16>(),
-                       g->ff.as<__nv_bfloat16>(), &g->part};
         auto body = [&](cudaStream_t cs, cudaEvent_t* ev) {
             launch_plan_decode(kv->len.as<int32_t>(), sid, n, kv->streams, kv->capacity, plan,
                                kv->err.as<uint32_t>(), cs);
-            launch_bf16_to_f32(g->x.as<__nv_bfloat16>(), g->resid.as<float>(), (long long)n * c.d_model, cs);
-            run_layers(model, kv, true, plan, n, b, cs, ev);
+            run_layers(model, kv, true, plan, n, g->x.as<__nv_bfloat16>(), g->resid.as<float>(), g->ws,
+                       cs, ev);
             launch_advance(kv->len.as<int32_t>(), sid, nullptr, n, 1, cs);
             check_launch();
         };

@@ -94,23 +94,20 @@ __device__ __forceinline__ int dim_of(int j, int i) {
 }
 
 template <typename T>
-__device__ __forceinline__ void store_out(void* out, int out_bf16, long long at, int j,
-                                          const float* v) {
-    if (out_bf16) {
-        __nv_bfloat16* o = static_cast<__nv_bfloat16*>(out) + at;
-        if (sizeof(T) == 2) {
-            uint4 u;
-            u.x = pack_bf16x2(v[0], v[1]); u.y = pack_bf16x2(v[2], v[3]);
-            u.z = pack_bf16x2(v[4], v[5]); u.w = pack_bf16x2(v[6], v[7]);
-            *reinterpret_cast<uint4*>(o + 8 * j) = u;
-        } else {
-#pragma unroll
-            for (int i = 0; i < 8; ++i) o[dim_of<T>(j, i)] = __float2bfloat16_rn(v[i]);
-        }
-    } else {
-        float* o = static_cast<float*>(out) + at;
+__device__ __forceinline__ void store_out(const DecodeArgs& a, long long at, int j, const float* v) {
+    if (a.out_mode == kOutF32) {
+        float* o = static_cast<float*>(a.out) + at;
 #pragma unroll
         for (int i = 0; i < 8; ++i) o[dim_of<T>(j, i)] = v[i];
+        return;
+    }
+    __nv_bfloat16* o = static_cast<__nv_bfloat16*>(a.out) + at;
+    __nv_bfloat16* ol = static_cast<__nv_bfloat16*>(a.out_lo) + at;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const __nv_bfloat16 h = __float2bfloat16_rn(v[i]);
+        o[dim_of<T>(j, i)] = h;
+        if (a.out_mode == kOutHiLo) ol[dim_of<T>(j, i)] = __float2bfloat16_rn(v[i] - __bfloat162float(h));
     }
 }
 
@@ -264,7 +261,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(DecodeArgs a) 
                 const float inv = 1.f / l;
 #pragma unroll
                 for (int i = 0; i < 8; ++i) acc[i] *= inv;
-                store_out<T>(a.out, a.out_bf16, (long long)b * kRowWidth + h * kHeadDim, j, acc);
+                store_out<T>(a, (long long)b * kRowWidth + h * kHeadDim, j, acc);
             } else {
                 float* rec = a.part + ((long long)(b + c) * kHeads + h) * kPartStride;
 #pragma unroll
@@ -300,12 +297,15 @@ __global__ void __launch_bounds__(256) decode_combine_kernel(DecodeArgs a, int g
     }
     const float inv = 1.f / den;
     const long long at = (long long)b * kRowWidth + h * kHeadDim + 2 * lane;
-    if (a.out_bf16) {
-        *reinterpret_cast<uint32_t*>(static_cast<__nv_bfloat16*>(a.out) + at) =
-            pack_bf16x2(n0 * inv, n1 * inv);
+    const float o0 = n0 * inv, o1 = n1 * inv;
+    if (a.out_mode == kOutF32) {
+        *reinterpret_cast<float2*>(static_cast<float*>(a.out) + at) = make_float2(o0, o1);
     } else {
-        float2 o = make_float2(n0 * inv, n1 * inv);
-        *reinterpret_cast<float2*>(static_cast<float*>(a.out) + at) = o;
+        const uint32_t hi = pack_bf16x2(o0, o1);
+        *reinterpret_cast<uint32_t*>(static_cast<__nv_bfloat16*>(a.out) + at) = hi;
+        if (a.out_mode == kOutHiLo)
+            *reinterpret_cast<uint32_t*>(static_cast<__nv_bfloat16*>(a.out_lo) + at) =
+                pack_bf16x2(o0 - bf16lo(hi), o1 - bf16hi(hi));
     }
 }
 

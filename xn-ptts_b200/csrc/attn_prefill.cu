@@ -110,14 +110,20 @@ __global__ void __launch_bounds__(256) prefill_attn_kernel(PrefillArgs a) {
     if (g != 0) return;
     const float inv = 1.f / l;
     const long long at = (long long)row * kRowWidth + h * kHeadDim;
-    if (a.out_bf16) {
-        __nv_bfloat16* o = static_cast<__nv_bfloat16*>(a.out) + at;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) o[dim_of<T>(j, i)] = __float2bfloat16_rn(acc[i] * inv);
-    } else {
+    if (a.out_mode == kOutF32) {
         float* o = static_cast<float*>(a.out) + at;
 #pragma unroll
         for (int i = 0; i < 8; ++i) o[dim_of<T>(j, i)] = acc[i] * inv;
+    } else {
+        __nv_bfloat16* o = static_cast<__nv_bfloat16*>(a.out) + at;
+        __nv_bfloat16* ol = static_cast<__nv_bfloat16*>(a.out_lo) + at;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const float y = acc[i] * inv;
+            const __nv_bfloat16 hb = __float2bfloat16_rn(y);
+            o[dim_of<T>(j, i)] = hb;
+            if (a.out_mode == kOutHiLo) ol[dim_of<T>(j, i)] = __float2bfloat16_rn(y - __bfloat162float(hb));
+        }
     }
 }
 

@@ -81,13 +81,16 @@ struct DecodeArgs {
     const int32_t* row_stream;  // [B] arena stream of each sequence
     const int32_t* prefix;      // [B + 1] prefix sums of attended keys
     const float* q;           // [B][H][D] f32, rotated
-    void* out;                // [B][H*D]
-    int out_bf16;
+    void* out;                // [B][H*D]: f32, bf16, or the hi plane (see out_mode)
+    void* out_lo;             // [B][H*D] bf16 lo plane when out_mode == kOutHiLo
+    int out_mode;
     float* part;              // [(B + grid) * H * kPartStride]
     int B;
     float qscale;             // 1/sqrt(D) * log2(e)
     uint32_t* err;
 };
+// Output forms of the attention kernels.
+constexpr int kOutF32 = 0, kOutBf16 = 1, kOutHiLo = 2;  // hi/lo: bf16(o) and bf16(o - hi)
 constexpr int kPartStride = 68;  // floats per (slot, head) partial: acc[64], m, l, pad
 // Split-KV decode over the balanced partition of all attended keys, then the merge of the
 // streams that span more than one CTA. `grid` CTAs at most (one per SM).
@@ -101,8 +104,9 @@ struct PrefillArgs {
     const int32_t* row_stream;
     const int32_t* row_pos;
     const float* q;           // [rows][H][D] f32, rotated
-    void* out;                // [rows][H*D]
-    int out_bf16;
+    void* out;                // [rows][H*D] (see out_mode)
+    void* out_lo;
+    int out_mode;
     int rows;
     float qscale;
     uint32_t* err;
@@ -112,18 +116,18 @@ void launch_prefill_attn(const PrefillArgs& a, bool cache_bf16, cudaStream_t s);
 
 // ---- int8 linear (linear.cu) ----------------------------------------------------------
 
-enum LinearEpi : int { EPI_F32 = 0, EPI_QKV = 1, EPI_RESID = 2, EPI_GELU = 3 };
+enum LinearEpi : int { EPI_F32 = 0, EPI_QKV = 1, EPI_RESID = 2, EPI_GELU = 3, EPI_PARTIAL = 4 };
 
 struct LinearArgs {
     int M, N, K;
-    const __nv_bfloat16* a;   // A from global bf16 [M][K] (ln == false)
-    const float* x;           // A = LN(x) [M][K] f32 (ln == true)
-    const float* ln_g;
-    const float* ln_b;
+    int splits = 1;           // split-K slices (gridDim.z); EPI_PARTIAL writes slice z
+    const __nv_bfloat16* a;   // A hi plane [M][K] bf16
+    const __nv_bfloat16* a_lo;  // A lo plane [M][K] bf16, or nullptr (A exact in bf16)
     const int8_t* w;          // [N][K]
     const float* scale;       // [N]
-    float* y;                 // EPI_F32: [M][N]; EPI_RESID: [M][N] +=
-    __nv_bfloat16* yb;        // EPI_GELU: [M][N]
+    float* y;                 // EPI_F32 / EPI_RESID: [M][N]; EPI_PARTIAL: [splits][M][N]
+    __nv_bfloat16* yb;        // EPI_GELU: hi plane [M][N]
+    __nv_bfloat16* yb_lo;     // EPI_GELU: lo plane [M][N]
     float* yq;                // EPI_QKV: rotated q [M][H*D] f32
     int gelu_tanh;
     // EPI_QKV
@@ -135,6 +139,23 @@ struct LinearArgs {
     float inv_freq[kMaxPairs];
     uint32_t* err;
 };
-void launch_linear(const LinearArgs& a, bool ln, LinearEpi epi, cudaStream_t s);
+// N must be a multiple of 64 and K / splits a multiple of 64.
+void launch_linear(const LinearArgs& a, LinearEpi epi, cudaStream_t s);
+
+// Residual update and LayerNorm, one warp per row: resid = (x_bf16 ? x_bf16 : resid)
+// + sum of `nsplit` partial slices [nsplit][M][d]; then, when hi != nullptr, LayerNorm(resid)
+// (gamma, beta, eps 1e-5) written as bf16 hi/lo planes. d in {128, 256, 512, 1024}.
+struct LnArgs {
+    int M, d;
+    float* resid;
+    const __nv_bfloat16* x_bf16;
+    const float* part;
+    int nsplit;
+    const float* gamma;
+    const float* beta;
+    __nv_bfloat16* hi;
+    __nv_bfloat16* lo;
+};
+void launch_ln(const LnArgs& a, cudaStream_t s);
 
 }  // namespace ptts

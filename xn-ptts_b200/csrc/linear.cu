@@ -1,27 +1,32 @@
 // int8-weight linears of the flow-LM layer with their neighbours fused in.
 //
 // Reference: Q::LinearQ::forward for in_proj, out_proj, linear1 and linear2
-// (ptts/src/transformer.rs:195, :224, :627) around LayerNorm (:602, :618), GELU (:620-625) and
-// the residual adds (:616, :634). Weights are int8 [out][in] with one f32 scale per output row,
-// so y[m][n] = scale[n] * sum_k a[m][k] * q[n][k]; int8 values are exact in bf16, so the
-// products run on the tensor cores with the scale applied once in the epilogue.
+// (ptts/src/transformer.rs:195, :224, :627), GELU (:620-625) and the residual adds (:616, :634).
+// Weights are int8 [out][in] with one f32 scale per output row, so
+// y[m][n] = scale[n] * sum_k a[m][k] * q[n][k]. int8 values are exact in bf16, so the products
+// run on the tensor cores and the scale is applied once in the epilogue.
 //
-// Prologues:  plain   A = bf16 rows from global memory, streamed with B;
-//             ln      A = LayerNorm(x) of f32 residual rows, computed once per CTA into a
-//                     resident bf16 tile (transformer.rs:547-548, eps 1e-5).
-// Epilogues:  f32     y = acc * scale
-//             resid   y += acc * scale           (x + attn / x + ff, residual kept in f32)
-//             gelu    y = bf16(gelu(acc*scale))   (linear1 + activation)
-//             qkv     columns [q | k | v] (transformer.rs:197-211): q and k turned by RoPE at
-//                     the row's position (rope.rs:81-95), q kept f32, k and v written into
-//                     the cache slot of the row's stream (complete_kv, transformer.rs:84-91),
-//                     a KV head repeated over the query heads that share it.
+// Activations. Every A operand arrives as two bf16 planes, hi = bf16(a) and lo = bf16(a - hi),
+// and each tile runs two MMAs (hi and lo) into one f32 accumulator: about 16 mantissa bits of
+// the f32 activation reach the product, so the GEMMs are f32-grade while the tensor cores stay on
+// bf16. (With the bf16 KV cache the only bf16 storage, two implementations of the stack agree
+// to ~1e-5 instead of parting by the ~1e-3 per layer that rounding GEMM inputs to bf16 causes.)
+//
+// Epilogues:  f32      y = acc * scale                 (the plain linear op, one A plane)
+//             partial  part[z] = acc * scale           (split-K slice z; summed into the
+//                                                      residual by the next LayerNorm kernel)
+//             resid    y += acc * scale                (residual update when not split)
+//             gelu     ff = gelu(acc * scale) as hi/lo planes (linear1 + activation)
+//             qkv      columns [q | k | v] (transformer.rs:197-211): q and k turned by RoPE at
+//                      the row's position (rope.rs:81-95), q kept f32, k and v written as bf16
+//                      into the cache slot of the row's stream (complete_kv,
+//                      transformer.rs:84-91), a KV head repeated over the query heads sharing it.
 //
 // Tensor-core mapping (mma.m16n8k16 bf16, f32 accumulate). Within each 16-wide k block the MMA's
 // k slots are bound to memory so that every thread's B operand is 4 consecutive int8 weights
-// (one 32-bit shared load, converted in registers) and its A operand is 4 consecutive bf16
-// (one 64-bit shared load): slot 2t,2t+1 -> k 4t,4t+1 and slot 2t+8,2t+9 -> k 4t+2,4t+3. A and
-// B use the same binding, so the dot product is unchanged.
+// (one 32-bit shared load, converted in registers) and its A operand 4 consecutive bf16 (one
+// 64-bit shared load): slot 2t,2t+1 -> k 4t,4t+1 and slot 2t+8,2t+9 -> k 4t+2,4t+3. A and B use
+// the same binding, so the dot product is unchanged.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -35,6 +40,8 @@ constexpr int kAStride = BK * 2 + 32;  // bytes per A row of a stage (160: confl
 constexpr int kBStride = BK + 16;      // bytes per int8 B row (80: conflict-free 4B loads)
 constexpr int kAStageBytes = BM * kAStride;
 constexpr int kBStageBytes = BN * kBStride;
+constexpr int kStageBytes = 2 * kAStageBytes + kBStageBytes;  // A hi, A lo, B
+constexpr int kSmemBytes = kStages * kStageBytes;
 
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem, bool valid) {
     const int n = valid ? 16 : 0;  // zero-fill rows past M
@@ -70,32 +77,39 @@ __device__ __forceinline__ float gelu(float x, int tanh_form) {
     return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f));
 }
 
-// One k-tile (BK) of the warp's 32x32 block: a_base/a_stride address A rows (k offset applied
-// by the caller), b_tile is the int8 stage.
-__device__ __forceinline__ void mma_tile(float (&acc)[2][4][4], const unsigned char* a_base,
-                                         int a_stride, const unsigned char* b_tile, int wm, int wn,
-                                         int g, int t) {
+__device__ __forceinline__ void load_afrag(uint32_t (&af)[2][4], const unsigned char* a, int wm,
+                                           int kk, int g, int t) {
+#pragma unroll
+    for (int mi = 0; mi < 2; ++mi) {
+        const int r = wm * 32 + mi * 16 + g;
+        const uint2 lo = *reinterpret_cast<const uint2*>(a + r * kAStride + kk * 32 + t * 8);
+        const uint2 hi = *reinterpret_cast<const uint2*>(a + (r + 8) * kAStride + kk * 32 + t * 8);
+        af[mi][0] = lo.x;
+        af[mi][1] = hi.x;
+        af[mi][2] = lo.y;
+        af[mi][3] = hi.y;
+    }
+}
+
+// One k-tile (BK) of the warp's 32x32 block, with the lo plane when present.
+__device__ __forceinline__ void mma_tile(float (&acc)[2][4][4], const unsigned char* a_hi,
+                                         const unsigned char* a_lo, bool has_lo,
+                                         const unsigned char* b_tile, int wm, int wn, int g, int t) {
 #pragma unroll
     for (int kk = 0; kk < BK / 16; ++kk) {
-        uint32_t af[2][4];
-#pragma unroll
-        for (int mi = 0; mi < 2; ++mi) {
-            const int r = wm * 32 + mi * 16 + g;
-            const uint2 lo = *reinterpret_cast<const uint2*>(a_base + r * a_stride + kk * 32 + t * 8);
-            const uint2 hi =
-                *reinterpret_cast<const uint2*>(a_base + (r + 8) * a_stride + kk * 32 + t * 8);
-            af[mi][0] = lo.x;
-            af[mi][1] = hi.x;
-            af[mi][2] = lo.y;
-            af[mi][3] = hi.y;
-        }
+        uint32_t ah[2][4], al[2][4];
+        load_afrag(ah, a_hi, wm, kk, g, t);
+        if (has_lo) load_afrag(al, a_lo, wm, kk, g, t);
 #pragma unroll
         for (int ni = 0; ni < 4; ++ni) {
             const int n = wn * 32 + ni * 8 + g;
             const uint32_t wq = *reinterpret_cast<const uint32_t*>(b_tile + n * kBStride + kk * 16 + t * 4);
             const uint32_t b0 = i8x2_to_bf16x2(wq, 0), b1 = i8x2_to_bf16x2(wq, 16);
 #pragma unroll
-            for (int mi = 0; mi < 2; ++mi) mma_bf16(acc[mi][ni], af[mi], b0, b1);
+            for (int mi = 0; mi < 2; ++mi) {
+                mma_bf16(acc[mi][ni], ah[mi], b0, b1);
+                if (has_lo) mma_bf16(acc[mi][ni], al[mi], b0, b1);
+            }
         }
     }
 }
@@ -109,21 +123,26 @@ __device__ __forceinline__ void rot(float& x0, float& x1, int pos, float inv_fre
     x1 = y1;
 }
 
-// Epilogue for one pair of adjacent output columns (n even) of row m.
+// Epilogue for one pair of adjacent output columns (n even) of row m, split slice z.
 template <int EPI>
-__device__ __forceinline__ void epilogue_pair(const LinearArgs& p, int m, int n, float c0,
+__device__ __forceinline__ void epilogue_pair(const LinearArgs& p, int m, int n, int z, float c0,
                                               float c1) {
     const float v0 = c0 * p.scale[n], v1 = c1 * p.scale[n + 1];
     const long long at = (long long)m * p.N + n;
     if (EPI == EPI_F32) {
         *reinterpret_cast<float2*>(p.y + at) = make_float2(v0, v1);
+    } else if (EPI == EPI_PARTIAL) {
+        *reinterpret_cast<float2*>(p.y + (long long)z * p.M * p.N + at) = make_float2(v0, v1);
     } else if (EPI == EPI_RESID) {
         float2* y = reinterpret_cast<float2*>(p.y + at);
         const float2 o = *y;
         *y = make_float2(o.x + v0, o.y + v1);
     } else if (EPI == EPI_GELU) {
-        *reinterpret_cast<uint32_t*>(p.yb + at) =
-            pack_bf16x2(gelu(v0, p.gelu_tanh), gelu(v1, p.gelu_tanh));
+        const float g0 = gelu(v0, p.gelu_tanh), g1 = gelu(v1, p.gelu_tanh);
+        const uint32_t hi = pack_bf16x2(g0, g1);
+        const uint32_t lo = pack_bf16x2(g0 - bf16lo(hi), g1 - bf16hi(hi));
+        *reinterpret_cast<uint32_t*>(p.yb + at) = hi;
+        *reinterpret_cast<uint32_t*>(p.yb_lo + at) = lo;
     } else {  // EPI_QKV
         const int hd = p.heads * kHeadDim, kvd = p.kv_heads * kHeadDim;
         const int sid = p.row_stream[m], pos = p.row_pos[m];
@@ -150,102 +169,47 @@ __device__ __forceinline__ void epilogue_pair(const LinearArgs& p, int m, int n,
     }
 }
 
-template <bool LN, int EPI>
+template <int EPI>
 __global__ void __launch_bounds__(kThreads) linear_kernel(LinearArgs p) {
     extern __shared__ __align__(128) unsigned char smem[];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int g = lane >> 2, t = lane & 3;
     const int wm = warp >> 1, wn = warp & 1;
-    const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM;
-    const int KT = p.K / BK;
-    const int a_res_stride = p.K * 2 + 32;  // resident LN tile
-    unsigned char* a_smem = smem;
-    unsigned char* b_smem = smem + (LN ? BM * a_res_stride : kStages * kAStageBytes);
+    const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM, z = blockIdx.z;
+    const int k_len = p.K / p.splits;
+    const int k0 = z * k_len;
+    const int KT = k_len / BK;
+    const bool has_lo = p.a_lo != nullptr;
 
-    auto load_b = [&](int kt, int st) {
-        unsigned char* dst = b_smem + st * kBStageBytes;
-#pragma unroll
-        for (int i = 0; i < (BN * BK / 16) / kThreads; ++i) {
-            const int c = tid + i * kThreads;
-            const int r = c >> 2, col = (c & 3) * 16;
-            cp_async16(dst + r * kBStride + col, p.w + (long long)(n0 + r) * p.K + kt * BK + col, true);
-        }
-    };
-    auto load_a = [&](int kt, int st) {
-        unsigned char* dst = a_smem + st * kAStageBytes;
+    auto load_stage = [&](int kt, int st) {
+        unsigned char* base = smem + st * kStageBytes;
+        const int kb = k0 + kt * BK;
 #pragma unroll
         for (int i = 0; i < (BM * BK * 2 / 16) / kThreads; ++i) {
             const int c = tid + i * kThreads;
             const int r = c >> 3, col = (c & 7) * 16;
             const int gm = m0 + r;
             const bool valid = gm < p.M;
-            const unsigned char* src = reinterpret_cast<const unsigned char*>(
-                p.a + (long long)(valid ? gm : 0) * p.K + kt * BK) + col;
-            cp_async16(dst + r * kAStride + col, src, valid);
+            const long long off = (long long)(valid ? gm : 0) * p.K + kb;
+            cp_async16(base + r * kAStride + col,
+                       reinterpret_cast<const unsigned char*>(p.a + off) + col, valid);
+            if (has_lo)
+                cp_async16(base + kAStageBytes + r * kAStride + col,
+                           reinterpret_cast<const unsigned char*>(p.a_lo + off) + col, valid);
+        }
+        unsigned char* bdst = base + 2 * kAStageBytes;
+#pragma unroll
+        for (int i = 0; i < (BN * BK / 16) / kThreads; ++i) {
+            const int c = tid + i * kThreads;
+            const int r = c >> 2, col = (c & 3) * 16;
+            cp_async16(bdst + r * kBStride + col, p.w + (long long)(n0 + r) * p.K + kb + col, true);
         }
     };
 
-    // Start the weight stream first; the LN prologue overlaps it.
 #pragma unroll
     for (int s = 0; s < kStages - 1; ++s) {
-        if (s < KT) {
-            if (!LN) load_a(s, s);
-            load_b(s, s);
-        }
+        if (s < KT) load_stage(s, s);
         cp_async_commit();
-    }
-
-    if (LN) {
-        // LayerNorm of this CTA's BM rows into the resident bf16 tile.
-        for (int r = warp; r < BM; r += kThreads / 32) {
-            const int gm = m0 + r;
-            unsigned char* dst = a_smem + r * a_res_stride;
-            if (gm >= p.M) {
-                for (int k = lane * 4; k < p.K; k += 128)
-                    *reinterpret_cast<uint2*>(dst + k * 2) = make_uint2(0, 0);
-                continue;
-            }
-            const float* xr = p.x + (long long)gm * p.K;
-            float xv[32];
-            float sum = 0.f;
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                const int k = lane * 4 + i * 128;
-                if (k < p.K) {
-                    const float4 v = *reinterpret_cast<const float4*>(xr + k);
-                    xv[4 * i] = v.x; xv[4 * i + 1] = v.y; xv[4 * i + 2] = v.z; xv[4 * i + 3] = v.w;
-                    sum += (v.x + v.y) + (v.z + v.w);
-                }
-            }
-            const float mean = warp_sum(sum) / (float)p.K;
-            float var = 0.f;
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                const int k = lane * 4 + i * 128;
-                if (k < p.K) {
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        const float c = xv[4 * i + e] - mean;
-                        var = fmaf(c, c, var);
-                    }
-                }
-            }
-            const float inv = 1.0f / sqrtf(warp_sum(var) / (float)p.K + 1e-5f);
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                const int k = lane * 4 + i * 128;
-                if (k < p.K) {
-                    const float4 gm4 = *reinterpret_cast<const float4*>(p.ln_g + k);
-                    const float4 bt4 = *reinterpret_cast<const float4*>(p.ln_b + k);
-                    const float y0 = (xv[4 * i] - mean) * inv * gm4.x + bt4.x;
-                    const float y1 = (xv[4 * i + 1] - mean) * inv * gm4.y + bt4.y;
-                    const float y2 = (xv[4 * i + 2] - mean) * inv * gm4.z + bt4.z;
-                    const float y3 = (xv[4 * i + 3] - mean) * inv * gm4.w + bt4.w;
-                    *reinterpret_cast<uint2*>(dst + k * 2) = make_uint2(pack_bf16x2(y0, y1), pack_bf16x2(y2, y3));
-                }
-            }
-        }
-        __syncthreads();
     }
 
     float acc[2][4][4];
@@ -260,16 +224,10 @@ __global__ void __launch_bounds__(kThreads) linear_kernel(LinearArgs p) {
         cp_async_wait<kStages - 2>();
         __syncthreads();
         const int nxt = kt + kStages - 1;
-        if (nxt < KT) {
-            if (!LN) load_a(nxt, nxt % kStages);
-            load_b(nxt, nxt % kStages);
-        }
+        if (nxt < KT) load_stage(nxt, nxt % kStages);
         cp_async_commit();
-        const int st = kt % kStages;
-        if (LN)
-            mma_tile(acc, a_smem + kt * BK * 2, a_res_stride, b_smem + st * kBStageBytes, wm, wn, g, t);
-        else
-            mma_tile(acc, a_smem + st * kAStageBytes, kAStride, b_smem + st * kBStageBytes, wm, wn, g, t);
+        const unsigned char* base = smem + (kt % kStages) * kStageBytes;
+        mma_tile(acc, base, base + kAStageBytes, has_lo, base + 2 * kAStageBytes, wm, wn, g, t);
     }
     cp_async_wait<0>();
 
@@ -279,39 +237,101 @@ __global__ void __launch_bounds__(kThreads) linear_kernel(LinearArgs p) {
         for (int ni = 0; ni < 4; ++ni) {
             const int m = m0 + wm * 32 + mi * 16 + g;
             const int n = n0 + wn * 32 + ni * 8 + 2 * t;
-            if (m < p.M) epilogue_pair<EPI>(p, m, n, acc[mi][ni][0], acc[mi][ni][1]);
-            if (m + 8 < p.M) epilogue_pair<EPI>(p, m + 8, n, acc[mi][ni][2], acc[mi][ni][3]);
+            if (m < p.M) epilogue_pair<EPI>(p, m, n, z, acc[mi][ni][0], acc[mi][ni][1]);
+            if (m + 8 < p.M) epilogue_pair<EPI>(p, m + 8, n, z, acc[mi][ni][2], acc[mi][ni][3]);
         }
     }
 }
 
-template <bool LN, int EPI>
+// One warp per row: residual (+ split-K partial slices) -> residual, then LayerNorm -> hi/lo.
+// transformer.rs:547-548 (eps 1e-5, biased variance); the row sum uses a warp reduction.
+// PER = d_model / 32 floats per lane.
+template <int PER>
+__global__ void __launch_bounds__(256) ln_kernel(LnArgs a) {
+    const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (row >= a.M) return;
+    constexpr int d = PER * 32;
+    float v[PER];
+    float* xr = a.resid + (long long)row * d;
+#pragma unroll
+    for (int i = 0; i < PER / 4; ++i) {
+        const int k = 4 * (lane + 32 * i);
+        float4 x;
+        if (a.x_bf16) {
+            const uint2 u = *reinterpret_cast<const uint2*>(a.x_bf16 + (long long)row * d + k);
+            x = make_float4(bf16lo(u.x), bf16hi(u.x), bf16lo(u.y), bf16hi(u.y));
+        } else {
+            x = *reinterpret_cast<const float4*>(xr + k);
+        }
+        for (int s = 0; s < a.nsplit; ++s) {
+            const float4 q = *reinterpret_cast<const float4*>(a.part + ((long long)s * a.M + row) * d + k);
+            x.x += q.x; x.y += q.y; x.z += q.z; x.w += q.w;
+        }
+        v[4 * i] = x.x; v[4 * i + 1] = x.y; v[4 * i + 2] = x.z; v[4 * i + 3] = x.w;
+        if (a.x_bf16 || a.nsplit) *reinterpret_cast<float4*>(xr + k) = x;
+    }
+    if (!a.hi) return;  // reduce only
+    float sum = 0.f;
+#pragma unroll
+    for (int i = 0; i < PER; ++i) sum += v[i];
+    const float mean = warp_sum(sum) / (float)d;
+    float var = 0.f;
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+        const float c = v[i] - mean;
+        var = fmaf(c, c, var);
+    }
+    const float inv = 1.0f / sqrtf(warp_sum(var) / (float)d + 1e-5f);
+#pragma unroll
+    for (int i = 0; i < PER / 4; ++i) {
+        const int k = 4 * (lane + 32 * i);
+        const float4 gm = *reinterpret_cast<const float4*>(a.gamma + k);
+        const float4 bt = *reinterpret_cast<const float4*>(a.beta + k);
+        const float y0 = (v[4 * i] - mean) * inv * gm.x + bt.x;
+        const float y1 = (v[4 * i + 1] - mean) * inv * gm.y + bt.y;
+        const float y2 = (v[4 * i + 2] - mean) * inv * gm.z + bt.z;
+        const float y3 = (v[4 * i + 3] - mean) * inv * gm.w + bt.w;
+        const uint32_t h01 = pack_bf16x2(y0, y1), h23 = pack_bf16x2(y2, y3);
+        const uint32_t l01 = pack_bf16x2(y0 - bf16lo(h01), y1 - bf16hi(h01));
+        const uint32_t l23 = pack_bf16x2(y2 - bf16lo(h23), y3 - bf16hi(h23));
+        *reinterpret_cast<uint2*>(a.hi + (long long)row * d + k) = make_uint2(h01, h23);
+        *reinterpret_cast<uint2*>(a.lo + (long long)row * d + k) = make_uint2(l01, l23);
+    }
+}
+
+template <int EPI>
 void launch_typed(const LinearArgs& a, cudaStream_t s) {
-    const size_t smem = (LN ? (size_t)BM * (a.K * 2 + 32) : (size_t)kStages * kAStageBytes) +
-                        (size_t)kStages * kBStageBytes;
-    cudaFuncSetAttribute(linear_kernel<LN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)smem);
-    dim3 grid(a.N / BN, (a.M + BM - 1) / BM);
-    linear_kernel<LN, EPI><<<grid, kThreads, smem, s>>>(a);
+    static int configured = -1;  // device whose attribute was set last
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (configured != dev) {
+        cudaFuncSetAttribute(linear_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+        configured = dev;
+    }
+    dim3 grid(a.N / BN, (a.M + BM - 1) / BM, a.splits);
+    linear_kernel<EPI><<<grid, kThreads, kSmemBytes, s>>>(a);
 }
 
 }  // namespace
 
-void launch_linear(const LinearArgs& a, bool ln, LinearEpi epi, cudaStream_t s) {
-    if (ln) {
-        switch (epi) {
-            case EPI_F32: launch_typed<true, EPI_F32>(a, s); break;
-            case EPI_QKV: launch_typed<true, EPI_QKV>(a, s); break;
-            case EPI_RESID: launch_typed<true, EPI_RESID>(a, s); break;
-            case EPI_GELU: launch_typed<true, EPI_GELU>(a, s); break;
-        }
-    } else {
-        switch (epi) {
-            case EPI_F32: launch_typed<false, EPI_F32>(a, s); break;
-            case EPI_QKV: launch_typed<false, EPI_QKV>(a, s); break;
-            case EPI_RESID: launch_typed<false, EPI_RESID>(a, s); break;
-            case EPI_GELU: launch_typed<false, EPI_GELU>(a, s); break;
-        }
+void launch_linear(const LinearArgs& a, LinearEpi epi, cudaStream_t s) {
+    switch (epi) {
+        case EPI_F32: launch_typed<EPI_F32>(a, s); break;
+        case EPI_QKV: launch_typed<EPI_QKV>(a, s); break;
+        case EPI_RESID: launch_typed<EPI_RESID>(a, s); break;
+        case EPI_GELU: launch_typed<EPI_GELU>(a, s); break;
+        case EPI_PARTIAL: launch_typed<EPI_PARTIAL>(a, s); break;
+    }
+}
+
+void launch_ln(const LnArgs& a, cudaStream_t s) {
+    const int blocks = (a.M + 7) / 8;
+    switch (a.d) {
+        case 128: ln_kernel<4><<<blocks, 256, 0, s>>>(a); break;
+        case 256: ln_kernel<8><<<blocks, 256, 0, s>>>(a); break;
+        case 512: ln_kernel<16><<<blocks, 256, 0, s>>>(a); break;
+        case 1024: ln_kernel<32><<<blocks, 256, 0, s>>>(a); break;
+        default: break;  // refused by the caller (d_model is checked at model creation)
     }
 }
 

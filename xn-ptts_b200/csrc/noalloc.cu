@@ -136,7 +136,7 @@ extern "C" int ptts_b200_attend_decode_noalloc(void* k_cache, void* v_cache, int
     a.prefix = plan.prefix;
     a.q = q_rot;
     a.out = out;
-    a.out_bf16 = out_dtype == PTTS_B200_BF16;
+    a.out_mode = out_dtype == PTTS_B200_BF16 ? kOutBf16 : kOutF32;
     a.part = part;
     a.B = n;
     a.qscale = (1.0f / sqrtf((float)kHeadDim)) * 1.4426950408889634f;
