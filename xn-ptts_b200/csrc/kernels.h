@@ -139,8 +139,12 @@ struct LinearArgs {
     float inv_freq[kMaxPairs];
     uint32_t* err;
 };
-// N must be a multiple of 64 and K / splits a multiple of 64.
+// N must be a multiple of 64 and K / splits a multiple of 64. launch_linear runs the mma.sync
+// kernel (linear.cu; faster at decode sizes, where 64x64 tiles keep 3-4 CTAs per SM) unless
+// PTTS_B200_GEMM=tc selects the tcgen05/TMEM kernel (linear_tc.cu).
 void launch_linear(const LinearArgs& a, LinearEpi epi, cudaStream_t s);
+void launch_linear_mma(const LinearArgs& a, LinearEpi epi, cudaStream_t s);
+void launch_linear_tc(const LinearArgs& a, LinearEpi epi, cudaStream_t s);
 
 // Residual update and LayerNorm, one warp per row: resid = (x_bf16 ? x_bf16 : resid)
 // + sum of `nsplit` partial slices [nsplit][M][d]; then, when hi != nullptr, LayerNorm(resid)

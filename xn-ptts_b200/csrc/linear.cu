@@ -27,6 +27,8 @@
 // (one 32-bit shared load, converted in registers) and its A operand 4 consecutive bf16 (one
 // 64-bit shared load): slot 2t,2t+1 -> k 4t,4t+1 and slot 2t+8,2t+9 -> k 4t+2,4t+3. A and B use
 // the same binding, so the dot product is unchanged.
+#include <cstdlib>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -315,6 +317,12 @@ void launch_typed(const LinearArgs& a, cudaStream_t s) {
 }  // namespace
 
 void launch_linear(const LinearArgs& a, LinearEpi epi, cudaStream_t s) {
+    const char* sel = getenv("PTTS_B200_GEMM");
+    if (sel && sel[0] == 't') launch_linear_tc(a, epi, s);
+    else launch_linear_mma(a, epi, s);
+}
+
+void launch_linear_mma(const LinearArgs& a, LinearEpi epi, cudaStream_t s) {
     switch (epi) {
         case EPI_F32: launch_typed<EPI_F32>(a, s); break;
         case EPI_QKV: launch_typed<EPI_QKV>(a, s); break;
