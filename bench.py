@@ -121,14 +121,43 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
+def shard_streams(rank: int, world: int):
+    """Stream ids of a rank: contiguous blocks of STREAMS_PER_GPU (GPU g gets 512g..512g+511)."""
+    if world * STREAMS_PER_GPU > TOTAL_STREAMS:
+        raise ValueError(f"{world} ranks x {STREAMS_PER_GPU} streams exceed {TOTAL_STREAMS}")
+    return list(range(rank * STREAMS_PER_GPU, (rank + 1) * STREAMS_PER_GPU))
+
+
+def barrier(dist, device_index=None):
+    """Start/stop barrier of the timed region (no-op on one process)."""
+    if dist is None:
+        return
+    if device_index is None:
+        dist.barrier()
+    else:
+        dist.barrier(device_ids=[device_index])
+
+
+def max_over_ranks(dist, ms: float, device) -> float:
+    """The slowest rank's duration: the job's time."""
+    if dist is None:
+        return ms
+    import torch
+    t = torch.tensor([ms], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
 def load():
     import __graft_entry__ as ge
     return ge.load_package(), ge.load_workloads()
 
 
 def shard_prefixes(wl, rank: int):
+    """Prefix lengths of a rank's streams, cut from the job-wide U{32..512} draw (seed 4)."""
     allp = wl.prefix_lengths(TOTAL_STREAMS, PREFIX_LO, PREFIX_HI, SEED)
-    return allp[rank * STREAMS_PER_GPU:(rank + 1) * STREAMS_PER_GPU]
+    ids = shard_streams(rank, 1 + rank)
+    return allp[ids[0]:ids[-1] + 1]
 
 
 def cpu_baseline(ptts, wl, cfg, weights, steps: int | None = None, budget_s: float = 12.0):
@@ -254,27 +283,16 @@ def run_ours(args):
         model.step(kv, streams, x_src(f % FRAMES), out=out)
         state["f"] = f + 1
 
-    def barrier():
-        if dist is not None:
-            dist.barrier(device_ids=[local])
-        torch.cuda.synchronize()
-
-    def max_over_ranks(ms: float) -> float:
-        if dist is None:
-            return ms
-        t = torch.tensor([ms], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
-
     def timed(x_src, out, k: int):
-        barrier()
+        barrier(dist, local)
+        torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
         for _ in range(k):
             step(x_src, out)
         e1.record(stream)
         e1.synchronize()
-        return max_over_ranks(e0.elapsed_time(e1))
+        return max_over_ranks(dist, e0.elapsed_time(e1), dev)
 
     # ---- device-resident inputs --------------------------------------------------------------
     dev_src = lambda f: x_frames[f]
@@ -356,7 +374,7 @@ def run_ours(args):
     kv.check()
     del kv
     if dist is not None:
-        dist.barrier(device_ids=[local])
+        barrier(dist, local)
         dist.destroy_process_group()
 
 
