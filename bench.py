@@ -230,6 +230,29 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def workload_spec(args, ptts, wl, rank):
+    """(cfg, streams per GPU, prefix lengths of this rank, seed, description) of the workload."""
+    import numpy as np
+    if args.workload == "config4":
+        cfg = ptts.PHONON_31M
+        B = 64
+        prefixes = np.full(B, 128, np.int32)
+        seed = 3
+        desc = ("config4: 31m flow LM (6 layers, d 512, 8x64 heads, ff 2048), 64 streams/GPU, "
+                "prefix 128, 250-frame decode window")
+    else:
+        cfg = ptts.PHONON_40M
+        B = STREAMS_PER_GPU
+        prefixes = shard_prefixes(wl, rank)
+        seed = SEED
+        desc = ("config5 shard: 40m flow LM (9 layers, d 512, 8x64 heads, ff 2048), 512 streams/GPU, "
+                "prefixes U{32..512}, 250-frame decode window")
+    if args.layers:
+        cfg = ptts.FlowLMConfig(num_layers=args.layers)
+        desc += f" [profiling override: {args.layers} layers]"
+    return cfg, B, prefixes, seed, desc
+
+
 def run_ours(args):
     import numpy as np
     import torch
@@ -246,20 +269,18 @@ def run_ours(args):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
 
     ptts, wl = load()
-    cfg = ptts.PHONON_40M
+    cfg, B, prefixes, seed, desc = workload_spec(args, ptts, wl, rank)
     L = cfg.num_layers
-    weights = ptts.random_weights(cfg, SEED)
+    weights = ptts.random_weights(cfg, seed)
     model = ptts.Transformer(cfg, local)
     model.load(weights)
-    prefixes = shard_prefixes(wl, rank)
-    B = STREAMS_PER_GPU
     cap = int(prefixes.max()) + FRAMES
     streams = np.arange(B, dtype=np.int32)
     stream = torch.cuda.current_stream()
 
     def fresh_state():
         kv = ptts.KvState(L, B, cap, dtype="bf16", device=local)
-        g = torch.Generator(device=dev).manual_seed(SEED * 1000 + rank)
+        g = torch.Generator(device=dev).manual_seed(seed * 1000 + rank)
         x = torch.randn(int(prefixes.sum()), cfg.d_model, generator=g, device=dev).bfloat16()
         t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         t0.record()
@@ -270,7 +291,7 @@ def run_ours(args):
         return kv, t0.elapsed_time(t1)
 
     kv, prefill_ms = fresh_state()
-    g = torch.Generator(device=dev).manual_seed(SEED * 2000 + rank)
+    g = torch.Generator(device=dev).manual_seed(seed * 2000 + rank)
     x_frames = torch.randn(FRAMES, B, cfg.d_model, generator=g, device=dev).bfloat16()
     y = torch.empty(B, cfg.d_model, dtype=torch.float32, device=dev)
 
@@ -296,11 +317,14 @@ def run_ours(args):
 
     # ---- device-resident inputs --------------------------------------------------------------
     dev_src = lambda f: x_frames[f]
+    # The sampler's process starts before the warm-up, so its start-up does not stall the host
+    # inside the timed region.
+    sampler = ClockSampler(local)
+    sampler.start()
+    time.sleep(0.5)
     for _ in range(args.warmup):
         step(dev_src, y)
     torch.cuda.synchronize()
-    sampler = ClockSampler(local)
-    sampler.start()
     ms = timed(dev_src, y, args.steps)
     clocks = sampler.stop()
     value = world * B * args.steps / (ms / 1e3)
@@ -351,7 +375,7 @@ def run_ours(args):
         roofline["traffic_source"] = "scaled from profiles/decode_attn_traffic.json: " + traffic.get("source", "")
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and args.workload == "config5" and not args.layers:
         cb = cpu_baseline(ptts, wl, cfg, weights)
         cpu = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
 
@@ -361,11 +385,11 @@ def run_ours(args):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded random-init int8 weights and N(0,1) hidden rows)",
-            "config": {"workload": "config5 shard: 40m flow LM (9 layers, d 512, 8x64 heads, ff 2048), "
-                                   "512 streams/GPU, prefixes U{32..512}, 250-frame decode window",
+            "config": {"workload": desc,
                        "streams_per_gpu": B, "total_streams": world * B, "layers": L,
                        "kv_capacity": cap, "parallelism": f"stream-sharded x{world}, no collectives",
-                       "l2": "inputs larger than L2: ~3.8 GB of KV read per step per GPU"},
+                       "l2": f"inputs larger than L2: {per_launch_bytes * L / 1e9:.2f} GB of KV read per step per GPU"
+                             if per_launch_bytes * L > 126e6 else "KV per step fits in L2 (no flush)"},
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": gpu_launches,
             "clocks": clocks, "prefill_ms": prefill_ms,
             "prefill_rows_per_s": world * float(prefixes.sum()) / (prefill_ms / 1e3),
@@ -418,13 +442,14 @@ def run_config3(args):
         state["s"] = s + 1
 
     junk = []
+    sampler = ClockSampler(0)
+    sampler.start()
+    time.sleep(0.5)
     for _ in range(args.warmup):
         step(junk)
     torch.cuda.synchronize()
     acc = []
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    sampler = ClockSampler(0)
-    sampler.start()
     e0.record()
     for _ in range(args.steps):
         step(acc)
@@ -465,8 +490,11 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["config5", "config3"], default="config5",
-                    help="config5: the flow-LM frame (default); config3: the attention op alone")
+    ap.add_argument("--workload", choices=["config5", "config4", "config3"], default="config5",
+                    help="config5: the flow-LM frame, 512 streams/GPU (default); config4: 31m, "
+                         "64 streams, prefix 128; config3: the attention op alone")
+    ap.add_argument("--layers", type=int, default=0,
+                    help="profiling aid: override the layer count (recorded in config.workload)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be at least 3")

@@ -89,6 +89,13 @@ struct DevBuf {
     T* as() const {
         return static_cast<T*>(p);
     }
+    // Like need(), and zero-filled whenever it is (re)allocated.
+    void* need_zeroed(size_t n) {
+        if (n <= bytes) return p;
+        need(n);
+        CK(cudaMemset(p, 0, n));
+        return p;
+    }
 };
 
 // Pinned staging for small host -> device uploads: a ring of slots, each reused only after its
@@ -124,7 +131,7 @@ struct Staging {
 
 // Per-call activations of the layer stack (device, sized for `rows` rows).
 struct Workspace {
-    DevBuf q_rot, h_hi, h_lo, attn_hi, attn_lo, ff_hi, ff_lo, split, part;
+    DevBuf q_rot, h_hi, h_lo, attn_hi, attn_lo, ff_hi, ff_lo, split, part, counters;
     void size(const ptts_b200_config& c, int rows) {
         const size_t r = (size_t)rows, hd = (size_t)c.num_heads * c.head_dim;
         q_rot.need(r * hd * 4);
@@ -135,6 +142,7 @@ struct Workspace {
         ff_hi.need(r * c.dim_feedforward * 2);
         ff_lo.need(r * c.dim_feedforward * 2);
         split.need(4 * r * c.d_model * 4);
+        counters.need_zeroed(r * sizeof(int));
     }
 };
 
@@ -185,7 +193,7 @@ struct ptts_b200_kv {
     DevBuf err;
     std::vector<int32_t> h_len;
     // scratch of the attention op
-    DevBuf seq_stream, row_offsets, row_stream, row_pos, prefix, part, q_rot;
+    DevBuf seq_stream, row_offsets, row_stream, row_pos, prefix, part, q_rot, counters;
     Staging staging;
     cudaEvent_t trace_ev[2] = {nullptr, nullptr};
     ~ptts_b200_kv() {
@@ -294,7 +302,7 @@ RowPlan make_plan(const ptts_b200_kv* kv, bool decode, const int32_t* d_seq_stre
 
 void attention(const ptts_b200_kv* kv, int layer, bool decode, const RowPlan& plan, int n_rows,
                const float* q_rot, void* out, void* out_lo, int out_mode, DevBuf& part,
-               cudaStream_t s) {
+               DevBuf& counters, cudaStream_t s) {
     const bool bf16 = kv->dtype == PTTS_B200_BF16;
     const float qscale = (1.0f / sqrtf((float)kv->head_dim)) * kLog2e;  // transformer.rs:215
     if (decode) {
@@ -310,6 +318,7 @@ void attention(const ptts_b200_kv* kv, int layer, bool decode, const RowPlan& pl
         a.out_lo = out_lo;
         a.out_mode = out_mode;
         a.part = static_cast<float*>(part.need(sizeof(float) * decode_part_floats(n_rows, grid)));
+        a.counters = static_cast<int*>(counters.need_zeroed(sizeof(int) * n_rows));
         a.B = n_rows;
         a.qscale = qscale;
         a.err = kv->err.as<uint32_t>();
@@ -435,7 +444,7 @@ void run_layers(const ptts_b200_model* m, const ptts_b200_kv* kv, bool decode, c
         // attention over the cache
         if (attn_ev) CK(cudaEventRecord(attn_ev[2 * l], s));
         attention(kv, l, decode, plan, rows, w.q_rot.as<float>(), w.attn_hi.p, w.attn_lo.p,
-                  kOutHiLo, w.part, s);
+                  kOutHiLo, w.part, w.counters, s);
         if (attn_ev) CK(cudaEventRecord(attn_ev[2 * l + 1], s));
         // out_proj + residual
         residual_gemm(w.attn_hi.as<__nv_bfloat16>(), w.attn_lo.as<__nv_bfloat16>(), L.w_out, L.s_out,
@@ -714,7 +723,7 @@ int ptts_b200_attend(ptts_b200_kv* kv, int layer, const void* q, const void* k, 
             CK(cudaEventRecord(kv->trace_ev[0], s));
         }
         attention(kv, layer, decode, plan, n_rows, ra.q_out, out, nullptr,
-                  out_dtype == PTTS_B200_BF16 ? kOutBf16 : kOutF32, kv->part, s);
+                  out_dtype == PTTS_B200_BF16 ? kOutBf16 : kOutF32, kv->part, kv->counters, s);
         if (trace) {
             CK(cudaEventRecord(kv->trace_ev[1], s));
             CK(cudaEventSynchronize(kv->trace_ev[1]));

@@ -12,7 +12,10 @@
 // bytes whatever the length mix. A CTA walks the streams its range touches. A stream that lies
 // wholly inside one range is finished there; the pieces of a stream cut by range ends leave
 // partial (max, sum, acc) records at slot b + c (unique: along the key order each new piece
-// increments b or c or both) and a small second kernel merges them.
+// increments b or c or both). The CTA that finishes a cut stream's last piece merges them: each
+// piece's CTA publishes its records (threadfence) and bumps the stream's counter; the one that
+// sees the count complete merges and resets the counter for the next launch. No CTA waits for
+// another.
 //
 // Data movement. Keys and values of consecutive positions of a stream are contiguous
 // (the cache is [stream][slot][head][dim]), so a chunk of positions is one 1-D bulk copy for K
@@ -111,6 +114,34 @@ __device__ __forceinline__ void store_out(const DecodeArgs& a, long long at, int
     }
 }
 
+// Merge the partial records of stream b, head h, written by CTAs c0..c1 (one warp; lane owns
+// dims 2*lane, 2*lane+1). Records of other CTAs are read past L1.
+__device__ __forceinline__ void merge_head(const DecodeArgs& a, int b, int h, int c0, int c1, int lane) {
+    float mx = -1e30f;
+    for (int c = c0; c <= c1; ++c)
+        mx = fmaxf(mx, __ldcg(a.part + ((long long)(b + c) * kHeads + h) * kPartStride + 64));
+    float n0 = 0.f, n1 = 0.f, den = 0.f;
+    for (int c = c0; c <= c1; ++c) {
+        const float* rec = a.part + ((long long)(b + c) * kHeads + h) * kPartStride;
+        const float f = fast_exp2(__ldcg(rec + 64) - mx);
+        den += f * __ldcg(rec + 65);
+        n0 += f * __ldcg(rec + 2 * lane);
+        n1 += f * __ldcg(rec + 2 * lane + 1);
+    }
+    const float inv = 1.f / den;
+    const long long at = (long long)b * kRowWidth + h * kHeadDim + 2 * lane;
+    const float o0 = n0 * inv, o1 = n1 * inv;
+    if (a.out_mode == kOutF32) {
+        *reinterpret_cast<float2*>(static_cast<float*>(a.out) + at) = make_float2(o0, o1);
+    } else {
+        const uint32_t hi = pack_bf16x2(o0, o1);
+        *reinterpret_cast<uint32_t*>(static_cast<__nv_bfloat16*>(a.out) + at) = hi;
+        if (a.out_mode == kOutHiLo)
+            *reinterpret_cast<uint32_t*>(static_cast<__nv_bfloat16*>(a.out_lo) + at) =
+                pack_bf16x2(o0 - bf16lo(hi), o1 - bf16hi(hi));
+    }
+}
+
 template <typename T>
 __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(DecodeArgs a) {
     constexpr int RB = Row<T>::kBytes;
@@ -121,6 +152,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(DecodeArgs a) 
     uint64_t* empty = full + kStages;
     __shared__ int s_b0;
 
+    __shared__ int s_last;
+    grid_dep_wait();
+    grid_dep_launch();
     const long long total = a.prefix[a.B];
     const int G = ctas_in_use(total, gridDim.x);
     const int c = blockIdx.x;
@@ -186,6 +220,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(DecodeArgs a) 
     const int g = lane >> 3;  // which of the 4 rows of a warp step
     const int j = lane & 7;   // which 16-byte slice of the head row
     int it = 0;
+    bool alive = true;  // cleared by a timed-out wait; the warp then skips work but keeps to the
+                        // named barriers below, so its peers never wait for it
     for (int b = b0; b < a.B; ++b) {
         const long long pb = a.prefix[b], pe = a.prefix[b + 1];
         if (pb >= end) break;
@@ -205,10 +241,11 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(DecodeArgs a) 
             const int n = min(CH, s1 - p);
             const int st = it % kStages;
             const uint32_t ph = (it / kStages) & 1;
-            if (!mbar_wait(&full[st], ph)) {
+            if (alive && !mbar_wait(&full[st], ph)) {
                 set_error(a.err, DEV_ERR_TIMEOUT);
-                return;
+                alive = false;
             }
+            if (!alive) continue;
             const unsigned char* ks = smem + st * kStageBytes + h * HB;
             const unsigned char* vs = ks + kStageBytes / 2;
             for (int r = 0; r < n; r += 8) {
@@ -256,7 +293,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(DecodeArgs a) 
             for (int i = 0; i < 8; ++i) acc[i] = acc[i] * fa + __shfl_xor_sync(0xffffffffu, acc[i], o) * fb;
             m = mn;
         }
-        if (g == 0) {
+        if (g == 0 && alive) {
             if (whole) {
                 const float inv = 1.f / l;
 #pragma unroll
@@ -272,53 +309,36 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(DecodeArgs a) 
                 }
             }
         }
-    }
-}
-
-// One warp per (stream, head): merge the partial records of streams cut by range ends.
-__global__ void __launch_bounds__(256) decode_combine_kernel(DecodeArgs a, int grid) {
-    const int w = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
-    if (w >= a.B * kHeads) return;
-    const int b = w / kHeads, h = w % kHeads;
-    const long long total = a.prefix[a.B];
-    const int G = ctas_in_use(total, grid);
-    const int c0 = cta_of(a.prefix[b], total, G), c1 = cta_of(a.prefix[b + 1] - 1, total, G);
-    if (c0 == c1) return;  // finished by its CTA
-    float mx = -1e30f;
-    for (int c = c0; c <= c1; ++c)
-        mx = fmaxf(mx, a.part[((long long)(b + c) * kHeads + h) * kPartStride + 64]);
-    float n0 = 0.f, n1 = 0.f, den = 0.f;
-    for (int c = c0; c <= c1; ++c) {
-        const float* rec = a.part + ((long long)(b + c) * kHeads + h) * kPartStride;
-        const float f = fast_exp2(rec[64] - mx);
-        den += f * rec[65];
-        n0 += f * rec[2 * lane];
-        n1 += f * rec[2 * lane + 1];
-    }
-    const float inv = 1.f / den;
-    const long long at = (long long)b * kRowWidth + h * kHeadDim + 2 * lane;
-    const float o0 = n0 * inv, o1 = n1 * inv;
-    if (a.out_mode == kOutF32) {
-        *reinterpret_cast<float2*>(static_cast<float*>(a.out) + at) = make_float2(o0, o1);
-    } else {
-        const uint32_t hi = pack_bf16x2(o0, o1);
-        *reinterpret_cast<uint32_t*>(static_cast<__nv_bfloat16*>(a.out) + at) = hi;
-        if (a.out_mode == kOutHiLo)
-            *reinterpret_cast<uint32_t*>(static_cast<__nv_bfloat16*>(a.out_lo) + at) =
-                pack_bf16x2(o0 - bf16lo(hi), o1 - bf16hi(hi));
+        if (!whole) {
+            // Publish this piece; the CTA that completes the stream's count merges all pieces.
+            __threadfence();
+            asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
+            const int c0 = cta_of(pb, total, G), c1 = cta_of(pe - 1, total, G);
+            if (threadIdx.x == 0) {
+                const int seen = atomicAdd(&a.counters[b], 1) + 1;
+                s_last = seen == c1 - c0 + 1;
+                if (s_last) a.counters[b] = 0;  // ready for the next launch
+            }
+            asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
+            if (s_last) {
+                __threadfence();
+                merge_head(a, b, h, c0, c1, lane);
+            }
+        }
     }
 }
 
 template <typename T>
 void launch_typed(const DecodeArgs& a, int grid, cudaStream_t s) {
-    static bool configured = false;  // per process; the attribute is per function and device
-    if (!configured) {
+    static int configured = -1;  // the device whose attribute was set last
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (configured != dev) {
         cudaFuncSetAttribute(decode_attn_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              kSmemBytes);
-        configured = true;
+        configured = dev;
     }
-    decode_attn_kernel<T><<<grid, kThreads, kSmemBytes, s>>>(a);
-    decode_combine_kernel<<<(a.B * kHeads + 7) / 8, 256, 0, s>>>(a, grid);
+    launch_k(decode_attn_kernel<T>, dim3(grid), dim3(kThreads), kSmemBytes, s, a);
 }
 
 }  // namespace

@@ -41,6 +41,8 @@ __device__ __forceinline__ int dim_of(int j, int i) {
 
 template <typename T>
 __global__ void __launch_bounds__(256) prefill_attn_kernel(PrefillArgs a) {
+    grid_dep_wait();
+    grid_dep_launch();
     const int w = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (w >= a.rows * kHeads) return;
     const int row = w / kHeads, h = w % kHeads;
@@ -131,8 +133,8 @@ __global__ void __launch_bounds__(256) prefill_attn_kernel(PrefillArgs a) {
 
 void launch_prefill_attn(const PrefillArgs& a, bool cache_bf16, cudaStream_t s) {
     const int blocks = (a.rows * kHeads + 7) / 8;
-    if (cache_bf16) prefill_attn_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>(a);
-    else prefill_attn_kernel<float><<<blocks, 256, 0, s>>>(a);
+    if (cache_bf16) launch_k(prefill_attn_kernel<__nv_bfloat16>, dim3(blocks), dim3(256), 0, s, a);
+    else launch_k(prefill_attn_kernel<float>, dim3(blocks), dim3(256), 0, s, a);
 }
 
 }  // namespace ptts

@@ -82,6 +82,16 @@ __device__ __forceinline__ uint64_t policy_evict_first() {
     return p;
 }
 
+// ---- programmatic dependent launch ------------------------------------------------------
+// A kernel launched with programmatic stream serialisation may start before its predecessor
+// has finished. grid_dep_wait() returns once the predecessor grid has completed and its
+// memory is visible (a no-op when the launch had no such attribute); everything read from
+// the predecessor comes after it. grid_dep_launch() lets the successor start launching.
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dep_launch() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ---- bf16 / packing ----------------------------------------------------------------------
 
 __device__ __forceinline__ float bf16lo(uint32_t u) { return __uint_as_float(u << 16); }

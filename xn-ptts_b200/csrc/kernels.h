@@ -5,6 +5,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <utility>
+
 namespace ptts {
 
 // Bits of the device-side error word. Kernels set these and return instead of trapping.
@@ -14,6 +16,26 @@ enum : uint32_t {
     DEV_ERR_TIMEOUT = 4u,   // a bounded mbarrier wait gave up
 };
 
+
+// Launch with programmatic stream serialisation (PTTS_B200_PDL=0 turns it off): the kernel may
+// start while its predecessor in the stream finishes; every kernel calls grid_dep_wait()
+// before it reads what a predecessor wrote.
+bool pdl_enabled();
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                            cudaStream_t s, Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 constexpr int kHeadDim = 64;   // D: the only head size the kernels implement
 constexpr int kRowWidth = 512; // H * D: one cache row of all heads
@@ -85,6 +107,7 @@ struct DecodeArgs {
     void* out_lo;             // [B][H*D] bf16 lo plane when out_mode == kOutHiLo
     int out_mode;
     float* part;              // [(B + grid) * H * kPartStride]
+    int* counters;            // [B], zero between launches (the merging CTA resets its entry)
     int B;
     float qscale;             // 1/sqrt(D) * log2(e)
     uint32_t* err;
@@ -92,8 +115,8 @@ struct DecodeArgs {
 // Output forms of the attention kernels.
 constexpr int kOutF32 = 0, kOutBf16 = 1, kOutHiLo = 2;  // hi/lo: bf16(o) and bf16(o - hi)
 constexpr int kPartStride = 68;  // floats per (slot, head) partial: acc[64], m, l, pad
-// Split-KV decode over the balanced partition of all attended keys, then the merge of the
-// streams that span more than one CTA. `grid` CTAs at most (one per SM).
+// Split-KV decode over the balanced partition of all attended keys; the streams that span more
+// than one CTA are merged by the CTA that finishes them last. `grid` CTAs at most (one per SM).
 void launch_decode_attn(const DecodeArgs& a, bool cache_bf16, int grid, cudaStream_t s);
 size_t decode_part_floats(int B, int grid);
 

@@ -35,15 +35,21 @@
 namespace ptts {
 namespace {
 
-constexpr int BM = 64, BN = 64, BK = 64;
+// Tiles: TM (64, or 32 below 1024 rows so decode sizes fill the GPU) x BN 64 x BK 64, four
+// warps: 2 x 2 warp tiles of 32 x 32 (TM 64) or 1 x 4 of 32 x 16 (TM 32).
+constexpr int BN = 64, BK = 64;
 constexpr int kThreads = 128;
 constexpr int kStages = 3;
 constexpr int kAStride = BK * 2 + 32;  // bytes per A row of a stage (160: conflict-free 8B loads)
 constexpr int kBStride = BK + 16;      // bytes per int8 B row (80: conflict-free 4B loads)
-constexpr int kAStageBytes = BM * kAStride;
 constexpr int kBStageBytes = BN * kBStride;
-constexpr int kStageBytes = 2 * kAStageBytes + kBStageBytes;  // A hi, A lo, B
-constexpr int kSmemBytes = kStages * kStageBytes;
+template <int TM>
+struct Tile {
+    static constexpr int kAStageBytes = TM * kAStride;
+    static constexpr int kStageBytes = 2 * kAStageBytes + kBStageBytes;  // A hi, A lo, B
+    static constexpr int kSmemBytes = kStages * kStageBytes;
+    static constexpr int NI = TM == 64 ? 4 : 2;  // 8-column fragments per warp
+};
 
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem, bool valid) {
     const int n = valid ? 16 : 0;  // zero-fill rows past M
@@ -57,10 +63,17 @@ __device__ __forceinline__ void cp_async_wait() {
     asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
-__device__ __forceinline__ uint32_t i8x2_to_bf16x2(uint32_t w, int shift) {
-    const float lo = (float)(int8_t)(w >> shift);
-    const float hi = (float)(int8_t)(w >> (shift + 8));
-    return pack_bf16x2(lo, hi);
+// Four int8 weights (one 32-bit word) -> two bf16x2 words, exactly, without int->float
+// conversions: with the sign bit flipped, byte u = v + 128 placed under the f32 exponent of 2^23
+// reads as 2^23 + u, and subtracting 2^23 + 128 leaves v.
+__device__ __forceinline__ void i8x4_to_bf16x4(uint32_t w, uint32_t& b01, uint32_t& b23) {
+    const uint32_t u = w ^ 0x80808080u;
+    const float f0 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7540)) - 8388736.0f;
+    const float f1 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7541)) - 8388736.0f;
+    const float f2 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7542)) - 8388736.0f;
+    const float f3 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7543)) - 8388736.0f;
+    b01 = pack_bf16x2(f0, f1);
+    b23 = pack_bf16x2(f2, f3);
 }
 
 __device__ __forceinline__ void mma_bf16(float* c, const uint32_t* a, uint32_t b0, uint32_t b1) {
@@ -79,11 +92,12 @@ __device__ __forceinline__ float gelu(float x, int tanh_form) {
     return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f));
 }
 
-__device__ __forceinline__ void load_afrag(uint32_t (&af)[2][4], const unsigned char* a, int wm,
+template <int MI>
+__device__ __forceinline__ void load_afrag(uint32_t (&af)[MI][4], const unsigned char* a, int row0,
                                            int kk, int g, int t) {
 #pragma unroll
-    for (int mi = 0; mi < 2; ++mi) {
-        const int r = wm * 32 + mi * 16 + g;
+    for (int mi = 0; mi < MI; ++mi) {
+        const int r = row0 + mi * 16 + g;
         const uint2 lo = *reinterpret_cast<const uint2*>(a + r * kAStride + kk * 32 + t * 8);
         const uint2 hi = *reinterpret_cast<const uint2*>(a + (r + 8) * kAStride + kk * 32 + t * 8);
         af[mi][0] = lo.x;
@@ -93,25 +107,34 @@ __device__ __forceinline__ void load_afrag(uint32_t (&af)[2][4], const unsigned 
     }
 }
 
-// One k-tile (BK) of the warp's 32x32 block, with the lo plane when present.
-__device__ __forceinline__ void mma_tile(float (&acc)[2][4][4], const unsigned char* a_hi,
+// One k-tile (BK) of the warp's (16 MI) x (8 NI) block at (row0, col0), with the lo plane when
+// present. The hi products of all fragments are issued before the lo ones, so no MMA waits on
+// the accumulator of the one just issued.
+template <int MI, int NI>
+__device__ __forceinline__ void mma_tile(float (&acc)[MI][NI][4], const unsigned char* a_hi,
                                          const unsigned char* a_lo, bool has_lo,
-                                         const unsigned char* b_tile, int wm, int wn, int g, int t) {
+                                         const unsigned char* b_tile, int row0, int col0, int g,
+                                         int t) {
 #pragma unroll
     for (int kk = 0; kk < BK / 16; ++kk) {
-        uint32_t ah[2][4], al[2][4];
-        load_afrag(ah, a_hi, wm, kk, g, t);
-        if (has_lo) load_afrag(al, a_lo, wm, kk, g, t);
+        uint32_t ah[MI][4], al[MI][4], b0[NI], b1[NI];
+        load_afrag<MI>(ah, a_hi, row0, kk, g, t);
 #pragma unroll
-        for (int ni = 0; ni < 4; ++ni) {
-            const int n = wn * 32 + ni * 8 + g;
+        for (int ni = 0; ni < NI; ++ni) {
+            const int n = col0 + ni * 8 + g;
             const uint32_t wq = *reinterpret_cast<const uint32_t*>(b_tile + n * kBStride + kk * 16 + t * 4);
-            const uint32_t b0 = i8x2_to_bf16x2(wq, 0), b1 = i8x2_to_bf16x2(wq, 16);
+            i8x4_to_bf16x4(wq, b0[ni], b1[ni]);
+        }
 #pragma unroll
-            for (int mi = 0; mi < 2; ++mi) {
-                mma_bf16(acc[mi][ni], ah[mi], b0, b1);
-                if (has_lo) mma_bf16(acc[mi][ni], al[mi], b0, b1);
-            }
+        for (int ni = 0; ni < NI; ++ni)
+#pragma unroll
+            for (int mi = 0; mi < MI; ++mi) mma_bf16(acc[mi][ni], ah[mi], b0[ni], b1[ni]);
+        if (has_lo) {
+            load_afrag<MI>(al, a_lo, row0, kk, g, t);
+#pragma unroll
+            for (int ni = 0; ni < NI; ++ni)
+#pragma unroll
+                for (int mi = 0; mi < MI; ++mi) mma_bf16(acc[mi][ni], al[mi], b0[ni], b1[ni]);
         }
     }
 }
@@ -171,23 +194,36 @@ __device__ __forceinline__ void epilogue_pair(const LinearArgs& p, int m, int n,
     }
 }
 
-template <int EPI>
+template <int EPI, int TM>
 __global__ void __launch_bounds__(kThreads) linear_kernel(LinearArgs p) {
+    using T = Tile<TM>;
+    constexpr int MI = 2, NI = T::NI;
     extern __shared__ __align__(128) unsigned char smem[];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int g = lane >> 2, t = lane & 3;
-    const int wm = warp >> 1, wn = warp & 1;
-    const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM, z = blockIdx.z;
+    const int row0 = TM == 64 ? (warp >> 1) * 32 : 0;
+    const int col0 = TM == 64 ? (warp & 1) * 32 : warp * 16;
+    const int n0 = blockIdx.x * BN, m0 = blockIdx.y * TM, z = blockIdx.z;
     const int k_len = p.K / p.splits;
     const int k0 = z * k_len;
     const int KT = k_len / BK;
     const bool has_lo = p.a_lo != nullptr;
 
-    auto load_stage = [&](int kt, int st) {
-        unsigned char* base = smem + st * kStageBytes;
+    auto load_b = [&](int kt, int st) {
+        unsigned char* bdst = smem + st * T::kStageBytes + 2 * T::kAStageBytes;
         const int kb = k0 + kt * BK;
 #pragma unroll
-        for (int i = 0; i < (BM * BK * 2 / 16) / kThreads; ++i) {
+        for (int i = 0; i < (BN * BK / 16) / kThreads; ++i) {
+            const int c = tid + i * kThreads;
+            const int r = c >> 2, col = (c & 3) * 16;
+            cp_async16(bdst + r * kBStride + col, p.w + (long long)(n0 + r) * p.K + kb + col, true);
+        }
+    };
+    auto load_a = [&](int kt, int st) {
+        unsigned char* base = smem + st * T::kStageBytes;
+        const int kb = k0 + kt * BK;
+#pragma unroll
+        for (int i = 0; i < (TM * BK * 2 / 16) / kThreads; ++i) {
             const int c = tid + i * kThreads;
             const int r = c >> 3, col = (c & 7) * 16;
             const int gm = m0 + r;
@@ -196,29 +232,29 @@ __global__ void __launch_bounds__(kThreads) linear_kernel(LinearArgs p) {
             cp_async16(base + r * kAStride + col,
                        reinterpret_cast<const unsigned char*>(p.a + off) + col, valid);
             if (has_lo)
-                cp_async16(base + kAStageBytes + r * kAStride + col,
+                cp_async16(base + T::kAStageBytes + r * kAStride + col,
                            reinterpret_cast<const unsigned char*>(p.a_lo + off) + col, valid);
-        }
-        unsigned char* bdst = base + 2 * kAStageBytes;
-#pragma unroll
-        for (int i = 0; i < (BN * BK / 16) / kThreads; ++i) {
-            const int c = tid + i * kThreads;
-            const int r = c >> 2, col = (c & 3) * 16;
-            cp_async16(bdst + r * kBStride + col, p.w + (long long)(n0 + r) * p.K + kb + col, true);
         }
     };
 
+    // The weights never change, so their first stages load before the wait on the kernel that
+    // produced A; the first commit group then holds them too.
+#pragma unroll
+    for (int s = 0; s < kStages - 1; ++s)
+        if (s < KT) load_b(s, s);
+    grid_dep_wait();
+    grid_dep_launch();
 #pragma unroll
     for (int s = 0; s < kStages - 1; ++s) {
-        if (s < KT) load_stage(s, s);
+        if (s < KT) load_a(s, s);
         cp_async_commit();
     }
 
-    float acc[2][4][4];
+    float acc[MI][NI][4];
 #pragma unroll
-    for (int mi = 0; mi < 2; ++mi)
+    for (int mi = 0; mi < MI; ++mi)
 #pragma unroll
-        for (int ni = 0; ni < 4; ++ni)
+        for (int ni = 0; ni < NI; ++ni)
 #pragma unroll
             for (int e = 0; e < 4; ++e) acc[mi][ni][e] = 0.f;
 
@@ -226,19 +262,23 @@ __global__ void __launch_bounds__(kThreads) linear_kernel(LinearArgs p) {
         cp_async_wait<kStages - 2>();
         __syncthreads();
         const int nxt = kt + kStages - 1;
-        if (nxt < KT) load_stage(nxt, nxt % kStages);
+        if (nxt < KT) {
+            load_a(nxt, nxt % kStages);
+            load_b(nxt, nxt % kStages);
+        }
         cp_async_commit();
-        const unsigned char* base = smem + (kt % kStages) * kStageBytes;
-        mma_tile(acc, base, base + kAStageBytes, has_lo, base + 2 * kAStageBytes, wm, wn, g, t);
+        const unsigned char* base = smem + (kt % kStages) * T::kStageBytes;
+        mma_tile<MI, NI>(acc, base, base + T::kAStageBytes, has_lo, base + 2 * T::kAStageBytes,
+                         row0, col0, g, t);
     }
     cp_async_wait<0>();
 
 #pragma unroll
-    for (int mi = 0; mi < 2; ++mi) {
+    for (int mi = 0; mi < MI; ++mi) {
 #pragma unroll
-        for (int ni = 0; ni < 4; ++ni) {
-            const int m = m0 + wm * 32 + mi * 16 + g;
-            const int n = n0 + wn * 32 + ni * 8 + 2 * t;
+        for (int ni = 0; ni < NI; ++ni) {
+            const int m = m0 + row0 + mi * 16 + g;
+            const int n = n0 + col0 + ni * 8 + 2 * t;
             if (m < p.M) epilogue_pair<EPI>(p, m, n, z, acc[mi][ni][0], acc[mi][ni][1]);
             if (m + 8 < p.M) epilogue_pair<EPI>(p, m + 8, n, z, acc[mi][ni][2], acc[mi][ni][3]);
         }
@@ -249,28 +289,45 @@ __global__ void __launch_bounds__(kThreads) linear_kernel(LinearArgs p) {
 // transformer.rs:547-548 (eps 1e-5, biased variance); the row sum uses a warp reduction.
 // PER = d_model / 32 floats per lane.
 template <int PER>
-__global__ void __launch_bounds__(256) ln_kernel(LnArgs a) {
-    const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+__global__ void __launch_bounds__(128) ln_kernel(LnArgs a) {
+    grid_dep_wait();
+    grid_dep_launch();
+    const int row = blockIdx.x * 4 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (row >= a.M) return;
     constexpr int d = PER * 32;
-    float v[PER];
+    constexpr int Q = PER / 4;  // float4 per lane
+    float4 x[Q];
     float* xr = a.resid + (long long)row * d;
+    // Every load of the row (input, or residual plus up to four split-K slices) is issued
+    // before any of them is used.
 #pragma unroll
-    for (int i = 0; i < PER / 4; ++i) {
+    for (int i = 0; i < Q; ++i) {
         const int k = 4 * (lane + 32 * i);
-        float4 x;
         if (a.x_bf16) {
             const uint2 u = *reinterpret_cast<const uint2*>(a.x_bf16 + (long long)row * d + k);
-            x = make_float4(bf16lo(u.x), bf16hi(u.x), bf16lo(u.y), bf16hi(u.y));
+            x[i] = make_float4(bf16lo(u.x), bf16hi(u.x), bf16lo(u.y), bf16hi(u.y));
         } else {
-            x = *reinterpret_cast<const float4*>(xr + k);
+            x[i] = *reinterpret_cast<const float4*>(xr + k);
         }
-        for (int s = 0; s < a.nsplit; ++s) {
-            const float4 q = *reinterpret_cast<const float4*>(a.part + ((long long)s * a.M + row) * d + k);
-            x.x += q.x; x.y += q.y; x.z += q.z; x.w += q.w;
+    }
+    float4 q[4][Q];
+#pragma unroll
+    for (int s = 0; s < 4; ++s)
+#pragma unroll
+        for (int i = 0; i < Q; ++i)
+            q[s][i] = s < a.nsplit
+                          ? *reinterpret_cast<const float4*>(a.part + ((long long)s * a.M + row) * d + 4 * (lane + 32 * i))
+                          : make_float4(0.f, 0.f, 0.f, 0.f);
+    float v[PER];
+#pragma unroll
+    for (int i = 0; i < Q; ++i) {
+        float4 y = x[i];
+#pragma unroll
+        for (int s = 0; s < 4; ++s) {
+            y.x += q[s][i].x; y.y += q[s][i].y; y.z += q[s][i].z; y.w += q[s][i].w;
         }
-        v[4 * i] = x.x; v[4 * i + 1] = x.y; v[4 * i + 2] = x.z; v[4 * i + 3] = x.w;
-        if (a.x_bf16 || a.nsplit) *reinterpret_cast<float4*>(xr + k) = x;
+        v[4 * i] = y.x; v[4 * i + 1] = y.y; v[4 * i + 2] = y.z; v[4 * i + 3] = y.w;
+        if (a.x_bf16 || a.nsplit) *reinterpret_cast<float4*>(xr + 4 * (lane + 32 * i)) = y;
     }
     if (!a.hi) return;  // reduce only
     float sum = 0.f;
@@ -285,7 +342,7 @@ __global__ void __launch_bounds__(256) ln_kernel(LnArgs a) {
     }
     const float inv = 1.0f / sqrtf(warp_sum(var) / (float)d + 1e-5f);
 #pragma unroll
-    for (int i = 0; i < PER / 4; ++i) {
+    for (int i = 0; i < Q; ++i) {
         const int k = 4 * (lane + 32 * i);
         const float4 gm = *reinterpret_cast<const float4*>(a.gamma + k);
         const float4 bt = *reinterpret_cast<const float4*>(a.beta + k);
@@ -301,17 +358,24 @@ __global__ void __launch_bounds__(256) ln_kernel(LnArgs a) {
     }
 }
 
-template <int EPI>
-void launch_typed(const LinearArgs& a, cudaStream_t s) {
+template <int EPI, int TM>
+void launch_tile(const LinearArgs& a, cudaStream_t s) {
     static int configured = -1;  // device whose attribute was set last
     int dev = 0;
     cudaGetDevice(&dev);
     if (configured != dev) {
-        cudaFuncSetAttribute(linear_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+        cudaFuncSetAttribute(linear_kernel<EPI, TM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             Tile<TM>::kSmemBytes);
         configured = dev;
     }
-    dim3 grid(a.N / BN, (a.M + BM - 1) / BM, a.splits);
-    linear_kernel<EPI><<<grid, kThreads, kSmemBytes, s>>>(a);
+    dim3 grid(a.N / BN, (a.M + TM - 1) / TM, a.splits);
+    launch_k(linear_kernel<EPI, TM>, grid, dim3(kThreads), Tile<TM>::kSmemBytes, s, a);
+}
+
+template <int EPI>
+void launch_typed(const LinearArgs& a, cudaStream_t s) {
+    if (a.M < 1024) launch_tile<EPI, 32>(a, s);
+    else launch_tile<EPI, 64>(a, s);
 }
 
 }  // namespace
@@ -333,12 +397,12 @@ void launch_linear_mma(const LinearArgs& a, LinearEpi epi, cudaStream_t s) {
 }
 
 void launch_ln(const LnArgs& a, cudaStream_t s) {
-    const int blocks = (a.M + 7) / 8;
+    const dim3 blocks((a.M + 3) / 4), threads(128);
     switch (a.d) {
-        case 128: ln_kernel<4><<<blocks, 256, 0, s>>>(a); break;
-        case 256: ln_kernel<8><<<blocks, 256, 0, s>>>(a); break;
-        case 512: ln_kernel<16><<<blocks, 256, 0, s>>>(a); break;
-        case 1024: ln_kernel<32><<<blocks, 256, 0, s>>>(a); break;
+        case 128: launch_k(ln_kernel<4>, blocks, threads, 0, s, a); break;
+        case 256: launch_k(ln_kernel<8>, blocks, threads, 0, s, a); break;
+        case 512: launch_k(ln_kernel<16>, blocks, threads, 0, s, a); break;
+        case 1024: launch_k(ln_kernel<32>, blocks, threads, 0, s, a); break;
         default: break;  // refused by the caller (d_model is checked at model creation)
     }
 }

@@ -198,6 +198,8 @@ __global__ void __launch_bounds__(kThreadsTc, 1) linear_tc_kernel(LinearArgs p) 
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    grid_dep_wait();
+    grid_dep_launch();
 
     if (warp < kLoaderWarps) {
         // ---- loaders -------------------------------------------------------------------------
@@ -334,7 +336,7 @@ void launch_tc_typed(const LinearArgs& a, cudaStream_t s) {
         configured = dev;
     }
     dim3 grid(a.N / TBN, (a.M + TBM - 1) / TBM, a.splits);
-    linear_tc_kernel<EPI><<<grid, kThreadsTc, kSmemTc, s>>>(a);
+    launch_k(linear_tc_kernel<EPI>, grid, dim3(kThreadsTc), kSmemTc, s, a);
 }
 
 }  // namespace

@@ -1,4 +1,6 @@
 // Row plans, length bookkeeping and small conversions.
+#include <cstdlib>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -14,6 +16,8 @@ __global__ void __launch_bounds__(kPlanThreads) plan_decode_kernel(
     __shared__ int warp_tot[kPlanThreads / 32];
     __shared__ int carry;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    grid_dep_wait();
+    grid_dep_launch();
     if (tid == 0) {
         carry = 0;
         plan.prefix[0] = 0;
@@ -65,6 +69,8 @@ __global__ void plan_rows_kernel(const int32_t* __restrict__ lengths,
                                  const int32_t* __restrict__ seq_stream,
                                  const int32_t* __restrict__ row_offsets, int n_seq, int n_rows,
                                  int num_streams, int capacity, RowPlan plan, uint32_t* err) {
+    grid_dep_wait();
+    grid_dep_launch();
     const int r = blockIdx.x * blockDim.x + threadIdx.x;
     if (r >= n_rows) return;
     int lo = 0, hi = n_seq - 1;
@@ -86,6 +92,8 @@ __global__ void plan_rows_kernel(const int32_t* __restrict__ lengths,
 
 __global__ void advance_kernel(int32_t* lengths, const int32_t* __restrict__ seq_stream,
                                const int32_t* __restrict__ row_offsets, int n_seq, int rows) {
+    grid_dep_wait();
+    grid_dep_launch();
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n_seq) return;
     const int add = row_offsets ? row_offsets[i + 1] - row_offsets[i] : rows;
@@ -94,6 +102,8 @@ __global__ void advance_kernel(int32_t* lengths, const int32_t* __restrict__ seq
 
 __global__ void set_lengths_kernel(int32_t* lengths, const int32_t* __restrict__ streams,
                                    const int32_t* __restrict__ values, int n) {
+    grid_dep_wait();
+    grid_dep_launch();
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i < n) lengths[streams[i]] = values[i];
 }
@@ -101,6 +111,8 @@ __global__ void set_lengths_kernel(int32_t* lengths, const int32_t* __restrict__
 __global__ void reset_streams_kernel(uint4* k, uint4* v, int32_t* lengths,
                                      const int32_t* __restrict__ streams, int n, int layers,
                                      long long layer_vec, long long stream_vec) {
+    grid_dep_wait();
+    grid_dep_launch();
     const long long per = stream_vec * layers;
     const long long total = per * n;
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
@@ -118,6 +130,8 @@ __global__ void reset_streams_kernel(uint4* k, uint4* v, int32_t* lengths,
 
 __global__ void bf16_to_f32_kernel(const __nv_bfloat16* __restrict__ x, float* __restrict__ y,
                                    long long n) {
+    grid_dep_wait();
+    grid_dep_launch();
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
          i += (long long)gridDim.x * blockDim.x)
         y[i] = __bfloat162float(x[i]);
@@ -127,39 +141,47 @@ __global__ void bf16_to_f32_kernel(const __nv_bfloat16* __restrict__ x, float* _
 
 void launch_plan_decode(const int32_t* lengths, const int32_t* streams, int n, int num_streams,
                         int capacity, RowPlan plan, uint32_t* err, cudaStream_t s) {
-    plan_decode_kernel<<<1, kPlanThreads, 0, s>>>(lengths, streams, n, num_streams, capacity,
-                                                   plan, err);
+    launch_k(plan_decode_kernel, dim3(1), dim3(kPlanThreads), 0, s, lengths, streams, n,
+             num_streams, capacity, plan, err);
 }
 
 void launch_plan_rows(const int32_t* lengths, const int32_t* seq_stream, const int32_t* row_offsets,
                       int n_seq, int n_rows, int num_streams, int capacity, RowPlan plan,
                       uint32_t* err, cudaStream_t s) {
-    plan_rows_kernel<<<(n_rows + 255) / 256, 256, 0, s>>>(lengths, seq_stream, row_offsets, n_seq,
-                                                          n_rows, num_streams, capacity, plan, err);
+    launch_k(plan_rows_kernel, dim3((n_rows + 255) / 256), dim3(256), 0, s, lengths, seq_stream,
+             row_offsets, n_seq, n_rows, num_streams, capacity, plan, err);
 }
 
 void launch_advance(int32_t* lengths, const int32_t* seq_stream, const int32_t* row_offsets,
                     int n_seq, int rows, cudaStream_t s) {
-    advance_kernel<<<(n_seq + 255) / 256, 256, 0, s>>>(lengths, seq_stream, row_offsets, n_seq,
-                                                       rows);
+    launch_k(advance_kernel, dim3((n_seq + 255) / 256), dim3(256), 0, s, lengths, seq_stream,
+             row_offsets, n_seq, rows);
 }
 
 void launch_set_lengths(int32_t* lengths, const int32_t* streams, const int32_t* values, int n,
                         cudaStream_t s) {
-    set_lengths_kernel<<<(n + 255) / 256, 256, 0, s>>>(lengths, streams, values, n);
+    launch_k(set_lengths_kernel, dim3((n + 255) / 256), dim3(256), 0, s, lengths, streams, values, n);
 }
 
 void launch_reset_streams(void* k, void* v, int32_t* lengths, const int32_t* streams, int n,
                           int layers, long long layer_bytes, long long stream_bytes,
                           cudaStream_t s) {
-    reset_streams_kernel<<<1184, 256, 0, s>>>(static_cast<uint4*>(k), static_cast<uint4*>(v),
-                                              lengths, streams, n, layers, layer_bytes / 16,
-                                              stream_bytes / 16);
+    launch_k(reset_streams_kernel, dim3(1184), dim3(256), 0, s, static_cast<uint4*>(k),
+             static_cast<uint4*>(v), lengths, streams, n, layers, layer_bytes / 16,
+             stream_bytes / 16);
 }
 
 void launch_bf16_to_f32(const __nv_bfloat16* x, float* y, long long n, cudaStream_t s) {
     const long long blocks = (n + 255) / 256;
-    bf16_to_f32_kernel<<<(int)(blocks < 4096 ? blocks : 4096), 256, 0, s>>>(x, y, n);
+    launch_k(bf16_to_f32_kernel, dim3((int)(blocks < 4096 ? blocks : 4096)), dim3(256), 0, s, x, y, n);
+}
+
+bool pdl_enabled() {
+    static const bool on = [] {
+        const char* e = getenv("PTTS_B200_PDL");
+        return !(e && e[0] == '0');
+    }();
+    return on;
 }
 
 }  // namespace ptts

@@ -31,12 +31,14 @@ constexpr size_t kPlanBytes = align256(sizeof(int32_t) * (3 * kNoAllocMaxRows + 
 constexpr size_t kQBytes = align256(sizeof(float) * kNoAllocMaxRows * kRowWidth);
 constexpr size_t kPartBytes =
     align256(sizeof(float) * (size_t)(kNoAllocMaxRows + kNoAllocMaxGrid) * (kRowWidth / kHeadDim) * kPartStride);
-// About 4.6 MB: plan (12 KB) + rotated q (2 MB) + partial records (2.6 MB).
-constexpr size_t kNoAllocScratchBytes = kPlanBytes + kQBytes + kPartBytes;
+constexpr size_t kCounterBytes = align256(sizeof(int) * kNoAllocMaxRows);
+// About 4.6 MB: plan (12 KB) + rotated q (2 MB) + partial records (2.6 MB) + counters (4 KB).
+constexpr size_t kNoAllocScratchBytes = kPlanBytes + kQBytes + kPartBytes + kCounterBytes;
 
-// Shared by every call on a device; it keeps whatever the last call left in it. Nothing in it
-// has to start at zero: each call writes the plan and the rotated q before reading them, and the
-// partial records it reads were written by the same call.
+// Shared by every call on a device; it keeps whatever the last call left in it. The plan, the
+// rotated q and the partial records are written by each call before it reads them. The merge
+// counters must start at zero: each call clears them first (a call cut short by a failed wait
+// could have left one set).
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
 struct DeviceScratch {
@@ -108,6 +110,9 @@ extern "C" int ptts_b200_attend_decode_noalloc(void* k_cache, void* v_cache, int
     plan.prefix = plan_base + 2 * kNoAllocMaxRows;
     float* q_rot = reinterpret_cast<float*>(sc.base + kPlanBytes);
     float* part = reinterpret_cast<float*>(sc.base + kPlanBytes + kQBytes);
+    int* counters = reinterpret_cast<int*>(sc.base + kPlanBytes + kQBytes + kPartBytes);
+    if (cudaMemsetAsync(counters, 0, sizeof(int) * n, s) != cudaSuccess)
+        return refuse(PTTS_B200_ERR_CUDA, "clearing the merge counters failed");
 
     launch_plan_decode(lengths, streams, n, num_streams, capacity, plan, err, s);
     RopeAppendArgs ra{};
@@ -138,6 +143,7 @@ extern "C" int ptts_b200_attend_decode_noalloc(void* k_cache, void* v_cache, int
     a.out = out;
     a.out_mode = out_dtype == PTTS_B200_BF16 ? kOutBf16 : kOutF32;
     a.part = part;
+    a.counters = counters;
     a.B = n;
     a.qscale = (1.0f / sqrtf((float)kHeadDim)) * 1.4426950408889634f;
     a.err = err;

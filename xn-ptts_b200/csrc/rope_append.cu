@@ -14,6 +14,8 @@ namespace {
 
 template <typename Tin, typename T>
 __global__ void rope_append_kernel(RopeAppendArgs a) {
+    grid_dep_wait();
+    grid_dep_launch();
     const int pairs = kHeadDim / 2;
     const int slots = a.heads + 2 * a.kv_heads;
     const long long total = (long long)a.rows * slots * pairs;
@@ -68,13 +70,13 @@ void launch_rope_append(const RopeAppendArgs& a, bool in_bf16, bool cache_bf16, 
     const long long total = (long long)a.rows * (a.heads + 2 * a.kv_heads) * (kHeadDim / 2);
     const int blocks = (int)((total + 255) / 256);
     if (in_bf16 && cache_bf16)
-        rope_append_kernel<__nv_bfloat16, __nv_bfloat16><<<blocks, 256, 0, s>>>(a);
+        launch_k(rope_append_kernel<__nv_bfloat16, __nv_bfloat16>, dim3(blocks), dim3(256), 0, s, a);
     else if (in_bf16)
-        rope_append_kernel<__nv_bfloat16, float><<<blocks, 256, 0, s>>>(a);
+        launch_k(rope_append_kernel<__nv_bfloat16, float>, dim3(blocks), dim3(256), 0, s, a);
     else if (cache_bf16)
-        rope_append_kernel<float, __nv_bfloat16><<<blocks, 256, 0, s>>>(a);
+        launch_k(rope_append_kernel<float, __nv_bfloat16>, dim3(blocks), dim3(256), 0, s, a);
     else
-        rope_append_kernel<float, float><<<blocks, 256, 0, s>>>(a);
+        launch_k(rope_append_kernel<float, float>, dim3(blocks), dim3(256), 0, s, a);
 }
 
 }  // namespace ptts
