@@ -39,12 +39,13 @@ namespace {
 // warps: 2 x 2 warp tiles of 32 x 32 (TM 64) or 1 x 4 of 32 x 16 (TM 32).
 constexpr int BN = 64, BK = 64;
 constexpr int kThreads = 128;
-constexpr int kStages = 3;
 constexpr int kAStride = BK * 2 + 32;  // bytes per A row of a stage (160: conflict-free 8B loads)
 constexpr int kBStride = BK + 16;      // bytes per int8 B row (80: conflict-free 4B loads)
 constexpr int kBStageBytes = BN * kBStride;
 template <int TM>
 struct Tile {
+    // Three stages: deeper rings (6 / 4) measured slower, as they cost CTAs per SM.
+    static constexpr int kStages = 3;
     static constexpr int kAStageBytes = TM * kAStride;
     static constexpr int kStageBytes = 2 * kAStageBytes + kBStageBytes;  // A hi, A lo, B
     static constexpr int kSmemBytes = kStages * kStageBytes;
@@ -198,6 +199,7 @@ template <int EPI, int TM>
 __global__ void __launch_bounds__(kThreads) linear_kernel(LinearArgs p) {
     using T = Tile<TM>;
     constexpr int MI = 2, NI = T::NI;
+    constexpr int kStages = T::kStages;
     extern __shared__ __align__(128) unsigned char smem[];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int g = lane >> 2, t = lane & 3;
