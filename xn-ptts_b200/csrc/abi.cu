@@ -1,7 +1,9 @@
 // The C ABI of ptts_b200 (include/ptts_b200.h): objects, argument checks, workspaces, launch
 // sequences and the per-stream-set CUDA graph of the device step.
+#include <algorithm>
 #include <cmath>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <exception>
 #include <memory>
@@ -160,6 +162,21 @@ void rope_inv_freq(int head_dim, float max_period, float* out) {
 
 constexpr float kLog2e = 1.4426950408889634f;
 
+// Host-side tile list of the tcgen05 prefill kernel: (first row, rows) per 128 rows of each
+// sequence.
+std::vector<int2> make_tiles(const std::vector<int32_t>& offsets) {
+    std::vector<int2> t;
+    for (size_t i = 0; i + 1 < offsets.size(); ++i)
+        for (int r = offsets[i]; r < offsets[i + 1]; r += 128)
+            t.push_back(make_int2(r, std::min(128, offsets[i + 1] - r)));
+    return t;
+}
+
+bool prefill_on_tensor_cores() {
+    const char* e = getenv("PTTS_B200_PREFILL");
+    return !(e && e[0] == 'c');  // PTTS_B200_PREFILL=core keeps the CUDA-core kernel
+}
+
 // Process-wide tracing of decode-attention launches (ptts_b200_set_tracing).
 struct Tracer {
     std::mutex mu;
@@ -193,7 +210,7 @@ struct ptts_b200_kv {
     DevBuf err;
     std::vector<int32_t> h_len;
     // scratch of the attention op
-    DevBuf seq_stream, row_offsets, row_stream, row_pos, prefix, part, q_rot, counters;
+    DevBuf seq_stream, row_offsets, row_stream, row_pos, prefix, part, q_rot, counters, tiles;
     Staging staging;
     cudaEvent_t trace_ev[2] = {nullptr, nullptr};
     ~ptts_b200_kv() {
@@ -231,7 +248,7 @@ struct ptts_b200_model {
     };
     std::vector<std::unique_ptr<Layer>> layers;
     // forward() workspace
-    DevBuf seq_stream, row_stream, row_pos, prefix;
+    DevBuf seq_stream, row_stream, row_pos, prefix, tiles;
     Workspace ws;
     Staging staging;
     std::unique_ptr<StepGraph> step;
@@ -300,9 +317,15 @@ RowPlan make_plan(const ptts_b200_kv* kv, bool decode, const int32_t* d_seq_stre
     return plan;
 }
 
+// Tiles of a prefill call (device list + count); empty for decode calls.
+struct Tiles {
+    const int2* dev = nullptr;
+    int n = 0;
+};
+
 void attention(const ptts_b200_kv* kv, int layer, bool decode, const RowPlan& plan, int n_rows,
                const float* q_rot, void* out, void* out_lo, int out_mode, DevBuf& part,
-               DevBuf& counters, cudaStream_t s) {
+               DevBuf& counters, const Tiles& tiles, cudaStream_t s) {
     const bool bf16 = kv->dtype == PTTS_B200_BF16;
     const float qscale = (1.0f / sqrtf((float)kv->head_dim)) * kLog2e;  // transformer.rs:215
     if (decode) {
@@ -337,7 +360,10 @@ void attention(const ptts_b200_kv* kv, int layer, bool decode, const RowPlan& pl
         a.rows = n_rows;
         a.qscale = qscale;
         a.err = kv->err.as<uint32_t>();
-        launch_prefill_attn(a, bf16, s);
+        if (bf16 && tiles.n > 0 && prefill_on_tensor_cores())
+            launch_prefill_attn_tc(a, tiles.dev, tiles.n, s);
+        else
+            launch_prefill_attn(a, bf16, s);
     }
     check_launch();
 }
@@ -373,7 +399,7 @@ int split_for(int rows, int k, int want) {
 // then a last reduction into the residual. x_in (bf16) seeds the f32 residual `resid`.
 void run_layers(const ptts_b200_model* m, const ptts_b200_kv* kv, bool decode, const RowPlan& plan,
                 int rows, const __nv_bfloat16* x_in, float* resid, Workspace& w, cudaStream_t s,
-                cudaEvent_t* attn_ev = nullptr) {
+                cudaEvent_t* attn_ev = nullptr, const Tiles& tiles = Tiles{}) {
     const ptts_b200_config& c = m->cfg;
     const int hd = c.num_heads * c.head_dim;
     const int nqkv = hd + 2 * c.num_kv_heads * c.head_dim;
@@ -444,7 +470,7 @@ void run_layers(const ptts_b200_model* m, const ptts_b200_kv* kv, bool decode, c
         // attention over the cache
         if (attn_ev) CK(cudaEventRecord(attn_ev[2 * l], s));
         attention(kv, l, decode, plan, rows, w.q_rot.as<float>(), w.attn_hi.p, w.attn_lo.p,
-                  kOutHiLo, w.part, w.counters, s);
+                  kOutHiLo, w.part, w.counters, tiles, s);
         if (attn_ev) CK(cudaEventRecord(attn_ev[2 * l + 1], s));
         // out_proj + residual
         residual_gemm(w.attn_hi.as<__nv_bfloat16>(), w.attn_lo.as<__nv_bfloat16>(), L.w_out, L.s_out,
@@ -722,8 +748,15 @@ int ptts_b200_attend(ptts_b200_kv* kv, int layer, const void* q, const void* k, 
                 if (!e) CK(cudaEventCreate(&e));
             CK(cudaEventRecord(kv->trace_ev[0], s));
         }
+        Tiles tiles;
+        if (!decode) {
+            const std::vector<int2> t = make_tiles(offsets);
+            tiles.dev = static_cast<int2*>(kv->tiles.need(sizeof(int2) * t.size()));
+            tiles.n = (int)t.size();
+            kv->staging.upload(const_cast<int2*>(tiles.dev), t.data(), sizeof(int2) * t.size(), s);
+        }
         attention(kv, layer, decode, plan, n_rows, ra.q_out, out, nullptr,
-                  out_dtype == PTTS_B200_BF16 ? kOutBf16 : kOutF32, kv->part, kv->counters, s);
+                  out_dtype == PTTS_B200_BF16 ? kOutBf16 : kOutF32, kv->part, kv->counters, tiles, s);
         if (trace) {
             CK(cudaEventRecord(kv->trace_ev[1], s));
             CK(cudaEventSynchronize(kv->trace_ev[1]));
@@ -856,8 +889,16 @@ int ptts_b200_forward(ptts_b200_model* model, ptts_b200_kv* kv, const void* x,
                                        model->row_pos, model->prefix, s);
         check_launch();
         model->ws.size(c, rows);
+        Tiles tiles;
+        if (!decode) {
+            const std::vector<int2> t = make_tiles(offsets);
+            tiles.dev = static_cast<int2*>(model->tiles.need(sizeof(int2) * t.size()));
+            tiles.n = (int)t.size();
+            model->staging.upload(const_cast<int2*>(tiles.dev), t.data(), sizeof(int2) * t.size(), s);
+        }
         // The residual stream lives in the caller's output y.
-        run_layers(model, kv, decode, plan, rows, static_cast<const __nv_bfloat16*>(x), y, model->ws, s);
+        run_layers(model, kv, decode, plan, rows, static_cast<const __nv_bfloat16*>(x), y, model->ws, s,
+                   nullptr, tiles);
         launch_advance(kv->len.as<int32_t>(), d, d + n_seq, n_seq, 0, s);
         check_launch();
         for (int i = 0; i < n_seq; ++i) kv->h_len[streams_host[i]] += rows_host[i];

@@ -136,6 +136,9 @@ struct PrefillArgs {
 };
 // Causal attention of every row over keys 0..=row_pos (CUDA cores, online softmax).
 void launch_prefill_attn(const PrefillArgs& a, bool cache_bf16, cudaStream_t s);
+// The same on tcgen05 tiles, bf16 caches: one CTA per (tile of up to 128 consecutive rows of
+// one sequence, head); tiles[i] = (first row, rows).
+void launch_prefill_attn_tc(const PrefillArgs& a, const int2* tiles, int n_tiles, cudaStream_t s);
 
 // ---- int8 linear (linear.cu) ----------------------------------------------------------
 
