@@ -405,8 +405,8 @@ void run_layers(const ptts_b200_model* m, const ptts_b200_kv* kv, bool decode, c
     const int nqkv = hd + 2 * c.num_kv_heads * c.head_dim;
     const int s_out = split_for(rows, hd, 2), s_ff2 = split_for(rows, c.dim_feedforward, 4);
     uint32_t* err = kv->err.as<uint32_t>();
-    auto* h_hi = w.h_hi.as<__nv_bfloat16>();
-    auto* h_lo = w.h_lo.as<__nv_bfloat16>();
+    auto* h_hi = w.h_hi.as<__half>();
+    auto* h_lo = w.h_lo.as<__half>();
     auto* split = w.split.as<float>();
     int pending = 0;  // split-K slices not yet added to the residual
     auto ln = [&](const float* g, const float* b, const __nv_bfloat16* x_bf16, bool normalise) {
@@ -425,7 +425,7 @@ void run_layers(const ptts_b200_model* m, const ptts_b200_kv* kv, bool decode, c
         check_launch();
         pending = 0;
     };
-    auto residual_gemm = [&](const __nv_bfloat16* a_hi, const __nv_bfloat16* a_lo, const DevBuf& wq,
+    auto residual_gemm = [&](const void* a_hi, const void* a_lo, const DevBuf& wq,
                              const DevBuf& sc, int k, int splits) {
         LinearArgs o{};
         o.M = rows;
@@ -473,7 +473,7 @@ void run_layers(const ptts_b200_model* m, const ptts_b200_kv* kv, bool decode, c
                   kOutHiLo, w.part, w.counters, tiles, s);
         if (attn_ev) CK(cudaEventRecord(attn_ev[2 * l + 1], s));
         // out_proj + residual
-        residual_gemm(w.attn_hi.as<__nv_bfloat16>(), w.attn_lo.as<__nv_bfloat16>(), L.w_out, L.s_out,
+        residual_gemm(w.attn_hi.as<__half>(), w.attn_lo.as<__half>(), L.w_out, L.s_out,
                       hd, s_out);
         // LN2, linear1 + GELU
         ln(L.ln2g.as<float>(), L.ln2b.as<float>(), nullptr, true);
@@ -485,14 +485,14 @@ void run_layers(const ptts_b200_model* m, const ptts_b200_kv* kv, bool decode, c
         f1.a_lo = h_lo;
         f1.w = L.w1.as<int8_t>();
         f1.scale = L.s1.as<float>();
-        f1.yb = w.ff_hi.as<__nv_bfloat16>();
-        f1.yb_lo = w.ff_lo.as<__nv_bfloat16>();
+        f1.yb = w.ff_hi.as<__half>();
+        f1.yb_lo = w.ff_lo.as<__half>();
         f1.gelu_tanh = c.gelu;
         f1.err = err;
         launch_linear(f1, EPI_GELU, s);
         check_launch();
         // linear2 + residual
-        residual_gemm(w.ff_hi.as<__nv_bfloat16>(), w.ff_lo.as<__nv_bfloat16>(), L.w2, L.s2,
+        residual_gemm(w.ff_hi.as<__half>(), w.ff_lo.as<__half>(), L.w2, L.s2,
                       c.dim_feedforward, s_ff2);
     }
     if (pending) ln(nullptr, nullptr, nullptr, false);
@@ -782,7 +782,8 @@ int ptts_b200_linear_i8(int device, const void* x, const int8_t* w, const float*
         a.M = m;
         a.N = n;
         a.K = k;
-        a.a = static_cast<const __nv_bfloat16*>(x);
+        a.a = x;
+        a.a_f16 = 0;  // one bf16 plane
         a.w = w;
         a.scale = scale;
         a.y = y;

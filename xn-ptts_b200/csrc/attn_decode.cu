@@ -104,13 +104,20 @@ __device__ __forceinline__ void store_out(const DecodeArgs& a, long long at, int
         for (int i = 0; i < 8; ++i) o[dim_of<T>(j, i)] = v[i];
         return;
     }
-    __nv_bfloat16* o = static_cast<__nv_bfloat16*>(a.out) + at;
-    __nv_bfloat16* ol = static_cast<__nv_bfloat16*>(a.out_lo) + at;
+    if (a.out_mode == kOutBf16) {
+        __nv_bfloat16* o = static_cast<__nv_bfloat16*>(a.out) + at;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) o[dim_of<T>(j, i)] = __float2bfloat16_rn(v[i]);
+        return;
+    }
+    __half* o = static_cast<__half*>(a.out) + at;
+    __half* ol = static_cast<__half*>(a.out_lo) + at;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-        const __nv_bfloat16 h = __float2bfloat16_rn(v[i]);
-        o[dim_of<T>(j, i)] = h;
-        if (a.out_mode == kOutHiLo) ol[dim_of<T>(j, i)] = __float2bfloat16_rn(v[i] - __bfloat162float(h));
+        float hf, lf;
+        split_f16(v[i], hf, lf);
+        o[dim_of<T>(j, i)] = __float2half_rn(hf);
+        ol[dim_of<T>(j, i)] = __float2half_rn(lf);
     }
 }
 
@@ -133,12 +140,13 @@ __device__ __forceinline__ void merge_head(const DecodeArgs& a, int b, int h, in
     const float o0 = n0 * inv, o1 = n1 * inv;
     if (a.out_mode == kOutF32) {
         *reinterpret_cast<float2*>(static_cast<float*>(a.out) + at) = make_float2(o0, o1);
+    } else if (a.out_mode == kOutBf16) {
+        *reinterpret_cast<uint32_t*>(static_cast<__nv_bfloat16*>(a.out) + at) = pack_bf16x2(o0, o1);
     } else {
-        const uint32_t hi = pack_bf16x2(o0, o1);
-        *reinterpret_cast<uint32_t*>(static_cast<__nv_bfloat16*>(a.out) + at) = hi;
-        if (a.out_mode == kOutHiLo)
-            *reinterpret_cast<uint32_t*>(static_cast<__nv_bfloat16*>(a.out_lo) + at) =
-                pack_bf16x2(o0 - bf16lo(hi), o1 - bf16hi(hi));
+        uint32_t hi, lo;
+        split_f16x2(o0, o1, hi, lo);
+        *reinterpret_cast<uint32_t*>(static_cast<__half*>(a.out) + at) = hi;
+        *reinterpret_cast<uint32_t*>(static_cast<__half*>(a.out_lo) + at) = lo;
     }
 }
 

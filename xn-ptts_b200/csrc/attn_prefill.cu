@@ -116,15 +116,19 @@ __global__ void __launch_bounds__(256) prefill_attn_kernel(PrefillArgs a) {
         float* o = static_cast<float*>(a.out) + at;
 #pragma unroll
         for (int i = 0; i < 8; ++i) o[dim_of<T>(j, i)] = acc[i] * inv;
-    } else {
+    } else if (a.out_mode == kOutBf16) {
         __nv_bfloat16* o = static_cast<__nv_bfloat16*>(a.out) + at;
-        __nv_bfloat16* ol = static_cast<__nv_bfloat16*>(a.out_lo) + at;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) o[dim_of<T>(j, i)] = __float2bfloat16_rn(acc[i] * inv);
+    } else {
+        __half* o = static_cast<__half*>(a.out) + at;
+        __half* ol = static_cast<__half*>(a.out_lo) + at;
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-            const float y = acc[i] * inv;
-            const __nv_bfloat16 hb = __float2bfloat16_rn(y);
-            o[dim_of<T>(j, i)] = hb;
-            if (a.out_mode == kOutHiLo) ol[dim_of<T>(j, i)] = __float2bfloat16_rn(y - __bfloat162float(hb));
+            float hf, lf;
+            split_f16(acc[i] * inv, hf, lf);
+            o[dim_of<T>(j, i)] = __float2half_rn(hf);
+            ol[dim_of<T>(j, i)] = __float2half_rn(lf);
         }
     }
 }

@@ -245,17 +245,15 @@ __global__ void __launch_bounds__(kThreadsP, 1) prefill_tc_kernel(PrefillArgs a,
                 for (int i = 0; i < 16; ++i)
                     *reinterpret_cast<float4*>(out + 4 * i) =
                         make_float4(o[4 * i] * inv, o[4 * i + 1] * inv, o[4 * i + 2] * inv, o[4 * i + 3] * inv);
-            } else {
-                __nv_bfloat16* oh = static_cast<__nv_bfloat16*>(a.out) + at;
-                __nv_bfloat16* ol = static_cast<__nv_bfloat16*>(a.out_lo) + at;
+            } else if (a.out_mode == kOutBf16) {
+                uint32_t* oh = reinterpret_cast<uint32_t*>(static_cast<__nv_bfloat16*>(a.out) + at);
 #pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                    const float x = o[2 * i] * inv, y = o[2 * i + 1] * inv;
-                    const uint32_t hb = pack_bf16x2(x, y);
-                    *reinterpret_cast<uint32_t*>(oh + 2 * i) = hb;
-                    if (a.out_mode == kOutHiLo)
-                        *reinterpret_cast<uint32_t*>(ol + 2 * i) = pack_bf16x2(x - bf16lo(hb), y - bf16hi(hb));
-                }
+                for (int i = 0; i < 32; ++i) oh[i] = pack_bf16x2(o[2 * i] * inv, o[2 * i + 1] * inv);
+            } else {
+                uint32_t* oh = reinterpret_cast<uint32_t*>(static_cast<__half*>(a.out) + at);
+                uint32_t* ol = reinterpret_cast<uint32_t*>(static_cast<__half*>(a.out_lo) + at);
+#pragma unroll
+                for (int i = 0; i < 32; ++i) split_f16x2(o[2 * i] * inv, o[2 * i + 1] * inv, oh[i], ol[i]);
             }
         }
     } else if (lane == 0) {

@@ -2,6 +2,7 @@
 #pragma once
 
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -100,6 +101,29 @@ __device__ __forceinline__ float bf16hi(uint32_t u) { return __uint_as_float(u &
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
     __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
     return *reinterpret_cast<uint32_t*>(&v);
+}
+
+// f16 pairs for the GEMM operands: values saturate at +-65504 instead of overflowing.
+__device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
+    __half2 v = __floats2half2_rn(fminf(fmaxf(lo, -65504.f), 65504.f), fminf(fmaxf(hi, -65504.f), 65504.f));
+    return *reinterpret_cast<uint32_t*>(&v);
+}
+__device__ __forceinline__ float f16lo(uint32_t u) {
+    return __half2float(__ushort_as_half((unsigned short)(u & 0xffffu)));
+}
+__device__ __forceinline__ float f16hi(uint32_t u) {
+    return __half2float(__ushort_as_half((unsigned short)(u >> 16)));
+}
+// Scalar form of split_f16x2: hi = f16(a) (saturated), lo = a - hi, both as floats.
+__device__ __forceinline__ void split_f16(float a, float& hi, float& lo) {
+    hi = __half2float(__float2half_rn(fminf(fmaxf(a, -65504.f), 65504.f)));
+    lo = a - hi;
+}
+
+// hi = f16(a), lo = f16(a - hi) for two values: the split every GEMM input is stored in.
+__device__ __forceinline__ void split_f16x2(float a, float b, uint32_t& hi, uint32_t& lo) {
+    hi = pack_f16x2(a, b);
+    lo = pack_f16x2(a - f16lo(hi), b - f16hi(hi));
 }
 
 __device__ __forceinline__ float to_f32(float x) { return x; }

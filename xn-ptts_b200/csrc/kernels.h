@@ -2,6 +2,7 @@
 #pragma once
 
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -113,7 +114,7 @@ struct DecodeArgs {
     uint32_t* err;
 };
 // Output forms of the attention kernels.
-constexpr int kOutF32 = 0, kOutBf16 = 1, kOutHiLo = 2;  // hi/lo: bf16(o) and bf16(o - hi)
+constexpr int kOutF32 = 0, kOutBf16 = 1, kOutHiLo = 2;  // hi/lo: f16(o) and f16(o - hi)
 constexpr int kPartStride = 68;  // floats per (slot, head) partial: acc[64], m, l, pad
 // Split-KV decode over the balanced partition of all attended keys; the streams that span more
 // than one CTA are merged by the CTA that finishes them last. `grid` CTAs at most (one per SM).
@@ -147,13 +148,14 @@ enum LinearEpi : int { EPI_F32 = 0, EPI_QKV = 1, EPI_RESID = 2, EPI_GELU = 3, EP
 struct LinearArgs {
     int M, N, K;
     int splits = 1;           // split-K slices (gridDim.z); EPI_PARTIAL writes slice z
-    const __nv_bfloat16* a;   // A hi plane [M][K] bf16
-    const __nv_bfloat16* a_lo;  // A lo plane [M][K] bf16, or nullptr (A exact in bf16)
+    const void* a;            // A hi plane [M][K]: f16 (a_f16) or bf16
+    const void* a_lo;         // A lo plane [M][K], or nullptr (A exact in one plane)
+    int a_f16 = 1;            // 1: f16 planes (the layer stack); 0: one bf16 plane
     const int8_t* w;          // [N][K]
     const float* scale;       // [N]
     float* y;                 // EPI_F32 / EPI_RESID: [M][N]; EPI_PARTIAL: [splits][M][N]
-    __nv_bfloat16* yb;        // EPI_GELU: hi plane [M][N]
-    __nv_bfloat16* yb_lo;     // EPI_GELU: lo plane [M][N]
+    void* yb;                 // EPI_GELU: f16 hi plane [M][N]
+    void* yb_lo;              // EPI_GELU: f16 lo plane [M][N]
     float* yq;                // EPI_QKV: rotated q [M][H*D] f32
     int gelu_tanh;
     // EPI_QKV
@@ -174,7 +176,7 @@ void launch_linear_tc(const LinearArgs& a, LinearEpi epi, cudaStream_t s);
 
 // Residual update and LayerNorm, one warp per row: resid = (x_bf16 ? x_bf16 : resid)
 // + sum of `nsplit` partial slices [nsplit][M][d]; then, when hi != nullptr, LayerNorm(resid)
-// (gamma, beta, eps 1e-5) written as bf16 hi/lo planes. d in {128, 256, 512, 1024}.
+// (gamma, beta, eps 1e-5) written as f16 hi/lo planes. d in {128, 256, 512, 1024}.
 struct LnArgs {
     int M, d;
     float* resid;
@@ -183,8 +185,8 @@ struct LnArgs {
     int nsplit;
     const float* gamma;
     const float* beta;
-    __nv_bfloat16* hi;
-    __nv_bfloat16* lo;
+    __half* hi;
+    __half* lo;
 };
 void launch_ln(const LnArgs& a, cudaStream_t s);
 

@@ -6,11 +6,13 @@
 // y[m][n] = scale[n] * sum_k a[m][k] * q[n][k]. int8 values are exact in bf16, so the products
 // run on the tensor cores and the scale is applied once in the epilogue.
 //
-// Activations. Every A operand arrives as two bf16 planes, hi = bf16(a) and lo = bf16(a - hi),
-// and each tile runs two MMAs (hi and lo) into one f32 accumulator: about 16 mantissa bits of
-// the f32 activation reach the product, so the GEMMs are f32-grade while the tensor cores stay on
-// bf16. (With the bf16 KV cache the only bf16 storage, two implementations of the stack agree
-// to ~1e-5 instead of parting by the ~1e-3 per layer that rounding GEMM inputs to bf16 causes.)
+// Activations. Every A operand of the layer stack arrives as two f16 planes, hi = f16(a) and
+// lo = f16(a - hi) (saturating at +-65504), and each tile runs two MMAs (hi and lo) into one f32
+// accumulator: about 22 mantissa bits of the f32 activation reach the product, so the GEMMs are
+// f32-grade. (With the bf16 KV cache the only rounding to 16-bit storage, two implementations of
+// the stack agree to ~1e-3 instead of parting by ~1e-3 per layer, as rounding GEMM inputs to
+// bf16 makes them.) int8 weights convert to f16 exactly with a byte permute and one packed
+// subtract. The plain linear op (ptts_b200_linear_i8) takes one bf16 plane and runs on bf16.
 //
 // Epilogues:  f32      y = acc * scale                 (the plain linear op, one A plane)
 //             partial  part[z] = acc * scale           (split-K slice z; summed into the
@@ -77,12 +79,40 @@ __device__ __forceinline__ void i8x4_to_bf16x4(uint32_t w, uint32_t& b01, uint32
     b23 = pack_bf16x2(f2, f3);
 }
 
-__device__ __forceinline__ void mma_bf16(float* c, const uint32_t* a, uint32_t b0, uint32_t b1) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
-        "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
-        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+// Four int8 weights -> two f16x2 words, exactly: with the sign bit flipped, byte u = v + 128
+// under the f16 exponent of 1024 reads as 1024 + u; one packed subtract of 1152 leaves v.
+__device__ __forceinline__ void i8x4_to_f16x4(uint32_t w, uint32_t& h01, uint32_t& h23) {
+    const uint32_t u = w ^ 0x80808080u;
+    const uint32_t p01 = __byte_perm(u, 0x64646464u, 0x5140);
+    const uint32_t p23 = __byte_perm(u, 0x64646464u, 0x7362);
+    const __half2 bias = __halves2half2(__ushort_as_half(0x6480), __ushort_as_half(0x6480));  // 1152
+    const __half2 r01 = __hsub2(*reinterpret_cast<const __half2*>(&p01), bias);
+    const __half2 r23 = __hsub2(*reinterpret_cast<const __half2*>(&p23), bias);
+    h01 = *reinterpret_cast<const uint32_t*>(&r01);
+    h23 = *reinterpret_cast<const uint32_t*>(&r23);
+}
+
+template <bool F16>
+__device__ __forceinline__ void i8x4_convert(uint32_t w, uint32_t& b01, uint32_t& b23) {
+    if (F16) i8x4_to_f16x4(w, b01, b23);
+    else i8x4_to_bf16x4(w, b01, b23);
+}
+
+// D += A B, m16n8k16, f32 accumulate; A and B both f16 (F16) or both bf16.
+template <bool F16>
+__device__ __forceinline__ void mma16(float* c, const uint32_t* a, uint32_t b0, uint32_t b1) {
+    if (F16)
+        asm volatile(
+            "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+            "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+            : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+            : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+    else
+        asm volatile(
+            "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
+            "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+            : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+            : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
 __device__ __forceinline__ float gelu(float x, int tanh_form) {
@@ -111,7 +141,7 @@ __device__ __forceinline__ void load_afrag(uint32_t (&af)[MI][4], const unsigned
 // One k-tile (BK) of the warp's (16 MI) x (8 NI) block at (row0, col0), with the lo plane when
 // present. The hi products of all fragments are issued before the lo ones, so no MMA waits on
 // the accumulator of the one just issued.
-template <int MI, int NI>
+template <int MI, int NI, bool F16>
 __device__ __forceinline__ void mma_tile(float (&acc)[MI][NI][4], const unsigned char* a_hi,
                                          const unsigned char* a_lo, bool has_lo,
                                          const unsigned char* b_tile, int row0, int col0, int g,
@@ -124,18 +154,18 @@ __device__ __forceinline__ void mma_tile(float (&acc)[MI][NI][4], const unsigned
         for (int ni = 0; ni < NI; ++ni) {
             const int n = col0 + ni * 8 + g;
             const uint32_t wq = *reinterpret_cast<const uint32_t*>(b_tile + n * kBStride + kk * 16 + t * 4);
-            i8x4_to_bf16x4(wq, b0[ni], b1[ni]);
+            i8x4_convert<F16>(wq, b0[ni], b1[ni]);
         }
 #pragma unroll
         for (int ni = 0; ni < NI; ++ni)
 #pragma unroll
-            for (int mi = 0; mi < MI; ++mi) mma_bf16(acc[mi][ni], ah[mi], b0[ni], b1[ni]);
+            for (int mi = 0; mi < MI; ++mi) mma16<F16>(acc[mi][ni], ah[mi], b0[ni], b1[ni]);
         if (has_lo) {
             load_afrag<MI>(al, a_lo, row0, kk, g, t);
 #pragma unroll
             for (int ni = 0; ni < NI; ++ni)
 #pragma unroll
-                for (int mi = 0; mi < MI; ++mi) mma_bf16(acc[mi][ni], al[mi], b0[ni], b1[ni]);
+                for (int mi = 0; mi < MI; ++mi) mma16<F16>(acc[mi][ni], al[mi], b0[ni], b1[ni]);
         }
     }
 }
@@ -164,11 +194,10 @@ __device__ __forceinline__ void epilogue_pair(const LinearArgs& p, int m, int n,
         const float2 o = *y;
         *y = make_float2(o.x + v0, o.y + v1);
     } else if (EPI == EPI_GELU) {
-        const float g0 = gelu(v0, p.gelu_tanh), g1 = gelu(v1, p.gelu_tanh);
-        const uint32_t hi = pack_bf16x2(g0, g1);
-        const uint32_t lo = pack_bf16x2(g0 - bf16lo(hi), g1 - bf16hi(hi));
-        *reinterpret_cast<uint32_t*>(p.yb + at) = hi;
-        *reinterpret_cast<uint32_t*>(p.yb_lo + at) = lo;
+        uint32_t hi, lo;
+        split_f16x2(gelu(v0, p.gelu_tanh), gelu(v1, p.gelu_tanh), hi, lo);
+        static_cast<uint32_t*>(p.yb)[at >> 1] = hi;
+        static_cast<uint32_t*>(p.yb_lo)[at >> 1] = lo;
     } else {  // EPI_QKV
         const int hd = p.heads * kHeadDim, kvd = p.kv_heads * kHeadDim;
         const int sid = p.row_stream[m], pos = p.row_pos[m];
@@ -195,7 +224,7 @@ __device__ __forceinline__ void epilogue_pair(const LinearArgs& p, int m, int n,
     }
 }
 
-template <int EPI, int TM>
+template <int EPI, int TM, bool F16>
 __global__ void __launch_bounds__(kThreads) linear_kernel(LinearArgs p) {
     using T = Tile<TM>;
     constexpr int MI = 2, NI = T::NI;
@@ -230,12 +259,12 @@ __global__ void __launch_bounds__(kThreads) linear_kernel(LinearArgs p) {
             const int r = c >> 3, col = (c & 7) * 16;
             const int gm = m0 + r;
             const bool valid = gm < p.M;
-            const long long off = (long long)(valid ? gm : 0) * p.K + kb;
+            const long long off = 2 * ((long long)(valid ? gm : 0) * p.K + kb);  // bytes
             cp_async16(base + r * kAStride + col,
-                       reinterpret_cast<const unsigned char*>(p.a + off) + col, valid);
+                       static_cast<const unsigned char*>(p.a) + off + col, valid);
             if (has_lo)
                 cp_async16(base + T::kAStageBytes + r * kAStride + col,
-                           reinterpret_cast<const unsigned char*>(p.a_lo + off) + col, valid);
+                           static_cast<const unsigned char*>(p.a_lo) + off + col, valid);
         }
     };
 
@@ -270,8 +299,8 @@ __global__ void __launch_bounds__(kThreads) linear_kernel(LinearArgs p) {
         }
         cp_async_commit();
         const unsigned char* base = smem + (kt % kStages) * T::kStageBytes;
-        mma_tile<MI, NI>(acc, base, base + T::kAStageBytes, has_lo, base + 2 * T::kAStageBytes,
-                         row0, col0, g, t);
+        mma_tile<MI, NI, F16>(acc, base, base + T::kAStageBytes, has_lo, base + 2 * T::kAStageBytes,
+                              row0, col0, g, t);
     }
     cp_async_wait<0>();
 
@@ -352,32 +381,37 @@ __global__ void __launch_bounds__(128) ln_kernel(LnArgs a) {
         const float y1 = (v[4 * i + 1] - mean) * inv * gm.y + bt.y;
         const float y2 = (v[4 * i + 2] - mean) * inv * gm.z + bt.z;
         const float y3 = (v[4 * i + 3] - mean) * inv * gm.w + bt.w;
-        const uint32_t h01 = pack_bf16x2(y0, y1), h23 = pack_bf16x2(y2, y3);
-        const uint32_t l01 = pack_bf16x2(y0 - bf16lo(h01), y1 - bf16hi(h01));
-        const uint32_t l23 = pack_bf16x2(y2 - bf16lo(h23), y3 - bf16hi(h23));
+        uint32_t h01, h23, l01, l23;
+        split_f16x2(y0, y1, h01, l01);
+        split_f16x2(y2, y3, h23, l23);
         *reinterpret_cast<uint2*>(a.hi + (long long)row * d + k) = make_uint2(h01, h23);
         *reinterpret_cast<uint2*>(a.lo + (long long)row * d + k) = make_uint2(l01, l23);
     }
 }
 
-template <int EPI, int TM>
+template <int EPI, int TM, bool F16>
 void launch_tile(const LinearArgs& a, cudaStream_t s) {
     static int configured = -1;  // device whose attribute was set last
     int dev = 0;
     cudaGetDevice(&dev);
     if (configured != dev) {
-        cudaFuncSetAttribute(linear_kernel<EPI, TM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        cudaFuncSetAttribute(linear_kernel<EPI, TM, F16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              Tile<TM>::kSmemBytes);
         configured = dev;
     }
     dim3 grid(a.N / BN, (a.M + TM - 1) / TM, a.splits);
-    launch_k(linear_kernel<EPI, TM>, grid, dim3(kThreads), Tile<TM>::kSmemBytes, s, a);
+    launch_k(linear_kernel<EPI, TM, F16>, grid, dim3(kThreads), Tile<TM>::kSmemBytes, s, a);
 }
 
 template <int EPI>
 void launch_typed(const LinearArgs& a, cudaStream_t s) {
-    if (a.M < 1024) launch_tile<EPI, 32>(a, s);
-    else launch_tile<EPI, 64>(a, s);
+    if (a.a_f16) {
+        if (a.M < 1024) launch_tile<EPI, 32, true>(a, s);
+        else launch_tile<EPI, 64, true>(a, s);
+    } else {
+        if (a.M < 1024) launch_tile<EPI, 32, false>(a, s);
+        else launch_tile<EPI, 64, false>(a, s);
+    }
 }
 
 }  // namespace

@@ -1,17 +1,18 @@
 // int8-weight linears on the 5th-generation tensor cores (tcgen05 + TMEM), sm_100a.
 //
-// Same contract as linear.cu (LinearArgs, the five epilogues, A as bf16 hi/lo planes, int8
-// weights with one f32 scale per output row); this file replaces its mma.sync main loop.
+// Same contract as linear.cu (LinearArgs, the five epilogues, A as f16 hi/lo planes or one bf16
+// plane, int8 weights with one f32 scale per output row); this file replaces its mma.sync main
+// loop.
 //
 // CTA tile 128 (rows) x 64 (output features), K in steps of 64, a 4-stage shared-memory ring:
 //   warps 0-3  loaders: cp.async the A hi and lo planes straight into the 128-byte-swizzled
 //              K-major layout the MMA reads (16-byte chunk c of row r lands at chunk c ^ (r & 7)),
-//              cp.async the int8 weight tile raw, then convert it in registers to bf16 (exact)
+//              cp.async the int8 weight tile raw, then convert it in registers to A's type (exact)
 //              into the same swizzled layout; fence.proxy.async, then arrive on the stage's
 //              `full` barrier. After the main loop they are the epilogue: warp w reads TMEM
 //              lanes 32w..32w+31 (one output row per thread) with tcgen05.ld.
-//   warp 4     one thread issues tcgen05.mma.cta_group::1.kind::f16 (M=128, N=64, K=16; bf16 x
-//              bf16 -> f32 in TMEM): per 64-wide K tile 4 steps x (hi, lo), then
+//   warp 4     one thread issues tcgen05.mma.cta_group::1.kind::f16 (M=128, N=64, K=16; f16 x
+//              f16 or bf16 x bf16 -> f32 in TMEM): per 64-wide K tile 4 steps x (hi, lo), then
 //              tcgen05.commit to the stage's `empty` barrier; after the last tile a commit to
 //              `done`.
 // TMEM: 64 columns (the 128x64 f32 accumulator), allocated and freed by warp 0.
@@ -36,10 +37,10 @@ constexpr int kBarOffset = kStagesTc * kStageTc;
 constexpr int kSmemTc = 1024 + kBarOffset + 256;  // + alignment slack + barriers/TMEM address
 constexpr uint32_t kTmemCols = TBN;
 
-// Instruction descriptor, kind::f16: D f32 (bits 4-5 = 1), A bf16 (bits 7-9 = 1),
-// B bf16 (bits 10-12 = 1), both K-major, N >> 3 at bit 17, M >> 4 at bit 24.
-constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(TBN >> 3) << 17) |
-                            ((uint32_t)(TBM >> 4) << 24);
+// Instruction descriptor, kind::f16: D f32 (bits 4-5 = 1), A and B both f16 (format 0) or both
+// bf16 (format 1, bits 7-9 and 10-12), both K-major, N >> 3 at bit 17, M >> 4 at bit 24.
+constexpr uint32_t kIdescF16 = (1u << 4) | ((uint32_t)(TBN >> 3) << 17) | ((uint32_t)(TBM >> 4) << 24);
+constexpr uint32_t kIdescBf16 = kIdescF16 | (1u << 7) | (1u << 10);
 
 // Shared-memory matrix descriptor of a K-major, 128-byte-swizzled tile at `addr` (1024-aligned):
 // start >> 4 in bits 0-13, leading byte offset 1 (unused when swizzled), stride byte offset
@@ -129,11 +130,10 @@ __device__ __forceinline__ void epi_pair(const LinearArgs& p, int m, int n, int 
         const float2 o = *y;
         *y = make_float2(o.x + v0, o.y + v1);
     } else if (EPI == EPI_GELU) {
-        const float g0 = gelu_tc(v0, p.gelu_tanh), g1 = gelu_tc(v1, p.gelu_tanh);
-        const uint32_t hi = pack_bf16x2(g0, g1);
-        const uint32_t lo = pack_bf16x2(g0 - bf16lo(hi), g1 - bf16hi(hi));
-        *reinterpret_cast<uint32_t*>(p.yb + at) = hi;
-        *reinterpret_cast<uint32_t*>(p.yb_lo + at) = lo;
+        uint32_t hi, lo;
+        split_f16x2(gelu_tc(v0, p.gelu_tanh), gelu_tc(v1, p.gelu_tanh), hi, lo);
+        static_cast<uint32_t*>(p.yb)[at >> 1] = hi;
+        static_cast<uint32_t*>(p.yb_lo)[at >> 1] = lo;
     } else {  // EPI_QKV
         const int hd = p.heads * kHeadDim, kvd = p.kv_heads * kHeadDim;
         const int sid = p.row_stream[m], pos = p.row_pos[m];
@@ -177,6 +177,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1) linear_tc_kernel(LinearArgs p) 
     const int k0 = z * k_len;
     const int KT = k_len / TBK;
     const bool has_lo = p.a_lo != nullptr;
+    const bool f16 = p.a_f16 != 0;
 
     if (tid == 0) {
         s_abort = 0;
@@ -217,10 +218,10 @@ __global__ void __launch_bounds__(kThreadsTc, 1) linear_tc_kernel(LinearArgs p) 
                 const int r = i * 16 + (lt >> 3);
                 const int gm = m0 + r;
                 const bool valid = gm < p.M;
-                const long long off = (long long)(valid ? gm : 0) * p.K + kb + c * 8;
+                const long long off = 2 * ((long long)(valid ? gm : 0) * p.K + kb + c * 8);  // bytes
                 const uint32_t dst = sa + r * 128 + ((c ^ (r & 7)) << 4);
-                cp_async16(dst, p.a + off, valid);
-                if (has_lo) cp_async16(dst + kATileBytes, p.a_lo + off, valid);
+                cp_async16(dst, static_cast<const unsigned char*>(p.a) + off, valid);
+                if (has_lo) cp_async16(dst + kATileBytes, static_cast<const unsigned char*>(p.a_lo) + off, valid);
             }
             // B raw: 64 rows x 4 chunks of 16 int8; thread lt takes chunks lt and lt + 128.
 #pragma unroll
@@ -231,7 +232,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1) linear_tc_kernel(LinearArgs p) 
                            p.w + (long long)(n0 + n) * p.K + kb + cc * 16, true);
             }
         };
-        // Convert this thread's two raw chunks of K tile `it` into the swizzled bf16 tile.
+        // Convert this thread's two raw chunks of K tile `it` into the swizzled f16/bf16 tile.
         auto convert = [&](int it) {
             const int st = it % kStagesTc;
             unsigned char* sp = smem + st * kStageTc;
@@ -244,12 +245,20 @@ __global__ void __launch_bounds__(kThreadsTc, 1) linear_tc_kernel(LinearArgs p) 
                 const uint4 u = *reinterpret_cast<const uint4*>(rawb + n * 64 + cc * 16);
                 const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
-                for (int h = 0; h < 2; ++h) {  // two 16-byte bf16 chunks: k-chunk 2cc + h
+                for (int h = 0; h < 2; ++h) {  // two 16-byte chunks: k-chunk 2cc + h
                     uint4 o;
-                    o.x = pack_bf16x2((float)(int8_t)(w[2 * h] & 0xff), (float)(int8_t)((w[2 * h] >> 8) & 0xff));
-                    o.y = pack_bf16x2((float)(int8_t)((w[2 * h] >> 16) & 0xff), (float)(int8_t)(w[2 * h] >> 24));
-                    o.z = pack_bf16x2((float)(int8_t)(w[2 * h + 1] & 0xff), (float)(int8_t)((w[2 * h + 1] >> 8) & 0xff));
-                    o.w = pack_bf16x2((float)(int8_t)((w[2 * h + 1] >> 16) & 0xff), (float)(int8_t)(w[2 * h + 1] >> 24));
+                    const float f[8] = {
+                        (float)(int8_t)(w[2 * h] & 0xff),         (float)(int8_t)((w[2 * h] >> 8) & 0xff),
+                        (float)(int8_t)((w[2 * h] >> 16) & 0xff), (float)(int8_t)(w[2 * h] >> 24),
+                        (float)(int8_t)(w[2 * h + 1] & 0xff),     (float)(int8_t)((w[2 * h + 1] >> 8) & 0xff),
+                        (float)(int8_t)((w[2 * h + 1] >> 16) & 0xff), (float)(int8_t)(w[2 * h + 1] >> 24)};
+                    if (f16) {
+                        o.x = pack_f16x2(f[0], f[1]); o.y = pack_f16x2(f[2], f[3]);
+                        o.z = pack_f16x2(f[4], f[5]); o.w = pack_f16x2(f[6], f[7]);
+                    } else {
+                        o.x = pack_bf16x2(f[0], f[1]); o.y = pack_bf16x2(f[2], f[3]);
+                        o.z = pack_bf16x2(f[4], f[5]); o.w = pack_bf16x2(f[6], f[7]);
+                    }
                     const int kc = 2 * cc + h;
                     *reinterpret_cast<uint4*>(bt + n * 128 + ((kc ^ (n & 7)) << 4)) = o;
                 }
@@ -306,10 +315,11 @@ __global__ void __launch_bounds__(kThreadsTc, 1) linear_tc_kernel(LinearArgs p) 
             const uint32_t sa = base + st * kStageTc;
             const uint64_t dhi = sw128_desc(sa), dlo = sw128_desc(sa + kATileBytes);
             const uint64_t db = sw128_desc(sa + 2 * kATileBytes);
+            const uint32_t idesc = f16 ? kIdescF16 : kIdescBf16;
 #pragma unroll
             for (int kk = 0; kk < TBK / 16; ++kk) {  // 32 bytes of K per MMA
-                tc_mma(tmem, dhi + 2 * kk, db + 2 * kk, kIdesc, (kt | kk) ? 1u : 0u);
-                if (has_lo) tc_mma(tmem, dlo + 2 * kk, db + 2 * kk, kIdesc, 1u);
+                tc_mma(tmem, dhi + 2 * kk, db + 2 * kk, idesc, (kt | kk) ? 1u : 0u);
+                if (has_lo) tc_mma(tmem, dlo + 2 * kk, db + 2 * kk, idesc, 1u);
             }
             tc_commit(&empty[st]);
             ++issued;
