@@ -279,11 +279,14 @@ def run_ours(args):
     stream = torch.cuda.current_stream()
 
     def fresh_state():
-        # A small prompt on a scratch state first loads every kernel, so the timed prefill
-        # does not include first-use module loading.
-        scratch = ptts.KvState(L, 4, 256, dtype="bf16", device=local)
-        model.forward(scratch, torch.zeros(4 * 130, cfg.d_model, device=dev).bfloat16(),
-                      [0, 1, 2, 3], [130, 130, 130, 130])
+        # Prompts on a scratch state first load every kernel (both GEMM kernels: the tcgen05 one
+        # below 4096 rows, the mma.sync one above) and build the RoPE table for this capacity,
+        # so the timed prefill includes no first-use module loading.
+        scratch = ptts.KvState(L, 4, max(cap, 1100), dtype="bf16", device=local)
+        for n in (130, 1100):
+            model.forward(scratch, torch.zeros(4 * n, cfg.d_model, device=dev).bfloat16(),
+                          [0, 1, 2, 3], [n] * 4)
+            scratch.reset([0, 1, 2, 3])
         torch.cuda.synchronize()
         scratch.close()
         kv = ptts.KvState(L, B, cap, dtype="bf16", device=local)

@@ -138,10 +138,10 @@ def test_config4_decode_frames(ptts, oracle, cuda):
     assert max(errs) < TOL
 
 
-@pytest.mark.parametrize("env", [{"PTTS_B200_GEMM": "tc"}, {"PTTS_B200_PREFILL": "core"}],
-                         ids=["tcgen05-linears", "cuda-core-prefill"])
+@pytest.mark.parametrize("env", [{"PTTS_B200_GEMM": "mma"}, {"PTTS_B200_PREFILL": "core"}],
+                         ids=["mma-sync-linears", "cuda-core-prefill"])
 def test_kernel_variants_match_the_oracle(ptts, oracle, cuda, monkeypatch, env):
-    """The opt-in variants (tcgen05 linears; the CUDA-core prefill attention) on the same
+    """The opt-in variants (mma.sync linears; the CUDA-core prefill attention) on the same
     prefill + decode as the default path, against the oracle."""
     import torch
     for k, v in env.items():

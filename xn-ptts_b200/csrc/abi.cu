@@ -244,9 +244,12 @@ struct ptts_b200_model {
     float inv_freq[kMaxPairs];
     struct Layer {
         DevBuf w_qkv, s_qkv, w_out, s_out, w1, s1, w2, s2, ln1g, ln1b, ln2g, ln2b;
+        DevBuf h_qkv, h_out, h1, h2;  // the int8 weights as f16 (exact), read by the tcgen05 linears
         bool loaded = false;
     };
     std::vector<std::unique_ptr<Layer>> layers;
+    DevBuf rope;        // RoPE (cos, sin) table [rope_rows][kMaxPairs]
+    int rope_rows = 0;
     // forward() workspace
     DevBuf seq_stream, row_stream, row_pos, prefix, tiles;
     Workspace ws;
@@ -425,7 +428,7 @@ void run_layers(const ptts_b200_model* m, const ptts_b200_kv* kv, bool decode, c
         check_launch();
         pending = 0;
     };
-    auto residual_gemm = [&](const void* a_hi, const void* a_lo, const DevBuf& wq,
+    auto residual_gemm = [&](const void* a_hi, const void* a_lo, const DevBuf& wq, const DevBuf& wh,
                              const DevBuf& sc, int k, int splits) {
         LinearArgs o{};
         o.M = rows;
@@ -435,6 +438,7 @@ void run_layers(const ptts_b200_model* m, const ptts_b200_kv* kv, bool decode, c
         o.a = a_hi;
         o.a_lo = a_lo;
         o.w = wq.as<int8_t>();
+        o.wh = wh.as<__half>();
         o.scale = sc.as<float>();
         o.y = splits > 1 ? split : resid;
         o.err = err;
@@ -453,6 +457,7 @@ void run_layers(const ptts_b200_model* m, const ptts_b200_kv* kv, bool decode, c
         a.a = h_hi;
         a.a_lo = h_lo;
         a.w = L.w_qkv.as<int8_t>();
+        a.wh = L.h_qkv.as<__half>();
         a.scale = L.s_qkv.as<float>();
         a.yq = w.q_rot.as<float>();
         a.row_stream = plan.row_stream;
@@ -463,7 +468,8 @@ void run_layers(const ptts_b200_model* m, const ptts_b200_kv* kv, bool decode, c
         a.kv_heads = c.num_kv_heads;
         a.num_streams = kv->streams;
         a.capacity = kv->capacity;
-        std::memcpy(a.inv_freq, m->inv_freq, sizeof(a.inv_freq));
+        require(m->rope_rows >= kv->capacity, PTTS_B200_ERR_STATE, "RoPE table shorter than the cache");
+        a.rope = m->rope.as<float2>();
         a.err = err;
         launch_linear(a, EPI_QKV, s);
         check_launch();
@@ -473,7 +479,7 @@ void run_layers(const ptts_b200_model* m, const ptts_b200_kv* kv, bool decode, c
                   kOutHiLo, w.part, w.counters, tiles, s);
         if (attn_ev) CK(cudaEventRecord(attn_ev[2 * l + 1], s));
         // out_proj + residual
-        residual_gemm(w.attn_hi.as<__half>(), w.attn_lo.as<__half>(), L.w_out, L.s_out,
+        residual_gemm(w.attn_hi.as<__half>(), w.attn_lo.as<__half>(), L.w_out, L.h_out, L.s_out,
                       hd, s_out);
         // LN2, linear1 + GELU
         ln(L.ln2g.as<float>(), L.ln2b.as<float>(), nullptr, true);
@@ -484,6 +490,7 @@ void run_layers(const ptts_b200_model* m, const ptts_b200_kv* kv, bool decode, c
         f1.a = h_hi;
         f1.a_lo = h_lo;
         f1.w = L.w1.as<int8_t>();
+        f1.wh = L.h1.as<__half>();
         f1.scale = L.s1.as<float>();
         f1.yb = w.ff_hi.as<__half>();
         f1.yb_lo = w.ff_lo.as<__half>();
@@ -492,10 +499,23 @@ void run_layers(const ptts_b200_model* m, const ptts_b200_kv* kv, bool decode, c
         launch_linear(f1, EPI_GELU, s);
         check_launch();
         // linear2 + residual
-        residual_gemm(w.ff_hi.as<__half>(), w.ff_lo.as<__half>(), L.w2, L.s2,
+        residual_gemm(w.ff_hi.as<__half>(), w.ff_lo.as<__half>(), L.w2, L.h2, L.s2,
                       c.dim_feedforward, s_ff2);
     }
     if (pending) ln(nullptr, nullptr, nullptr, false);
+}
+
+// Grows the RoPE table to `rows` positions. A captured step graph holds the old table's address,
+// so it is dropped when the table moves.
+void ensure_rope(ptts_b200_model* m, int rows, cudaStream_t s) {
+    if (m->rope_rows >= rows) return;
+    CK(cudaStreamSynchronize(s));
+    m->step.reset();
+    RopeFreqs f;
+    std::memcpy(f.inv_freq, m->inv_freq, sizeof(f.inv_freq));
+    launch_rope_table(f, static_cast<float2*>(m->rope.need(sizeof(float2) * kMaxPairs * (size_t)rows)), rows, s);
+    check_launch();
+    m->rope_rows = rows;
 }
 
 bool is_device_pointer(const void* p) {
@@ -865,6 +885,15 @@ int ptts_b200_model_load_layer(ptts_b200_model* model, int layer,
         put(L.ln1b, w->norm1_bias_host, dm * 4);
         put(L.ln2g, w->norm2_weight_host, dm * 4);
         put(L.ln2b, w->norm2_bias_host, dm * 4);
+        auto widen = [](DevBuf& h, const DevBuf& q, size_t n) {
+            launch_i8_to_f16(q.as<int8_t>(), static_cast<__half*>(h.need(n * 2)), (long long)n, nullptr);
+        };
+        widen(L.h_qkv, L.w_qkv, nqkv * dm);
+        widen(L.h_out, L.w_out, dm * hd);
+        widen(L.h1, L.w1, ff * dm);
+        widen(L.h2, L.w2, dm * ff);
+        check_launch();
+        CK(cudaDeviceSynchronize());
         L.loaded = true;
     });
 }
@@ -882,6 +911,7 @@ int ptts_b200_forward(ptts_b200_model* model, ptts_b200_kv* kv, const void* x,
         DeviceScope scope(model->device);
         cudaStream_t s = as_stream(cuda_stream);
         const ptts_b200_config& c = model->cfg;
+        ensure_rope(model, kv->capacity, s);
         std::vector<int32_t> packed(streams_host, streams_host + n_seq);
         packed.insert(packed.end(), offsets.begin(), offsets.end());
         int32_t* d = static_cast<int32_t*>(model->seq_stream.need(sizeof(int32_t) * packed.size()));
@@ -916,6 +946,7 @@ int ptts_b200_step(ptts_b200_model* model, ptts_b200_kv* kv, const int32_t* stre
         DeviceScope scope(model->device);
         cudaStream_t s = as_stream(cuda_stream);
         const ptts_b200_config& c = model->cfg;
+        ensure_rope(model, kv->capacity, s);
         StepGraph* g = model->step.get();
         const bool same = g && g->kv == kv && g->kv_uid == kv->uid && g->streams.size() == (size_t)n &&
                           std::memcmp(g->streams.data(), streams_host, sizeof(int32_t) * n) == 0;

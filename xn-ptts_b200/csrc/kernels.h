@@ -152,6 +152,7 @@ struct LinearArgs {
     const void* a_lo;         // A lo plane [M][K], or nullptr (A exact in one plane)
     int a_f16 = 1;            // 1: f16 planes (the layer stack); 0: one bf16 plane
     const int8_t* w;          // [N][K]
+    const __half* wh = nullptr;  // the same weights as f16 [N][K] (exact), for the tcgen05 kernel
     const float* scale;       // [N]
     float* y;                 // EPI_F32 / EPI_RESID: [M][N]; EPI_PARTIAL: [splits][M][N]
     void* yb;                 // EPI_GELU: f16 hi plane [M][N]
@@ -164,15 +165,28 @@ struct LinearArgs {
     __nv_bfloat16* k_cache;
     __nv_bfloat16* v_cache;
     int heads, kv_heads, num_streams, capacity;
-    float inv_freq[kMaxPairs];
+    // (cos, sin)(f32(pos) * inv_freq[i]) at [pos][i] for pos < capacity (launch_rope_table):
+    // the RoPE factors of the QKV epilogue, computed once per model instead of per element.
+    const float2* rope;
     uint32_t* err;
 };
-// N must be a multiple of 64 and K / splits a multiple of 64. launch_linear runs the mma.sync
-// kernel (linear.cu; faster at decode sizes, where 64x64 tiles keep 3-4 CTAs per SM) unless
-// PTTS_B200_GEMM=tc selects the tcgen05/TMEM kernel (linear_tc.cu).
+// N must be a multiple of 64 and K / splits a multiple of 64. launch_linear runs the TMA-fed
+// tcgen05/TMEM kernel (linear_tc.cu) for M < 4096 where linear_tc_supported holds (f16 hi/lo
+// activations, f16 weight copy present, N a multiple of 128) and the mma.sync kernel (linear.cu) otherwise. PTTS_B200_GEMM=mma forces the
+// mma.sync kernel, PTTS_B200_GEMM=tc the tcgen05 kernel at every M.
 void launch_linear(const LinearArgs& a, LinearEpi epi, cudaStream_t s);
 void launch_linear_mma(const LinearArgs& a, LinearEpi epi, cudaStream_t s);
-void launch_linear_tc(const LinearArgs& a, LinearEpi epi, cudaStream_t s);
+bool linear_tc_supported(const LinearArgs& a);
+bool launch_linear_tc(const LinearArgs& a, LinearEpi epi, cudaStream_t s);  // false: not launched
+
+// RoPE table: out[pos][i] = (cos, sin)(f32(pos) * inv_freq[i]) for pos < rows, i < kMaxPairs.
+struct RopeFreqs {
+    float inv_freq[kMaxPairs];
+};
+void launch_rope_table(RopeFreqs f, float2* out, int rows, cudaStream_t s);
+
+// int8 -> f16, exact (weights, once per layer load).
+void launch_i8_to_f16(const int8_t* x, __half* y, long long n, cudaStream_t s);
 
 // Residual update and LayerNorm, one warp per row: resid = (x_bf16 ? x_bf16 : resid)
 // + sum of `nsplit` partial slices [nsplit][M][d]; then, when hi != nullptr, LayerNorm(resid)

@@ -170,11 +170,10 @@ __device__ __forceinline__ void mma_tile(float (&acc)[MI][NI][4], const unsigned
     }
 }
 
-__device__ __forceinline__ void rot(float& x0, float& x1, int pos, float inv_freq) {
-    float sn, cs;
-    sincosf((float)pos * inv_freq, &sn, &cs);
-    const float y0 = __fsub_rn(__fmul_rn(x0, cs), __fmul_rn(x1, sn));
-    const float y1 = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, cs));
+// RoPE of the pair (x0, x1) by the table entry t = (cos, sin); rope.rs:37-95 rounding order.
+__device__ __forceinline__ void rot(float& x0, float& x1, float2 t) {
+    const float y0 = __fsub_rn(__fmul_rn(x0, t.x), __fmul_rn(x1, t.y));
+    const float y1 = __fadd_rn(__fmul_rn(x0, t.y), __fmul_rn(x1, t.x));
     x0 = y0;
     x1 = y1;
 }
@@ -198,30 +197,33 @@ __device__ __forceinline__ void epilogue_pair(const LinearArgs& p, int m, int n,
         split_f16x2(gelu(v0, p.gelu_tanh), gelu(v1, p.gelu_tanh), hi, lo);
         static_cast<uint32_t*>(p.yb)[at >> 1] = hi;
         static_cast<uint32_t*>(p.yb_lo)[at >> 1] = lo;
-    } else {  // EPI_QKV
-        const int hd = p.heads * kHeadDim, kvd = p.kv_heads * kHeadDim;
-        const int sid = p.row_stream[m], pos = p.row_pos[m];
-        const int d = n % kHeadDim;
-        float x0 = v0, x1 = v1;
-        if (n < hd) {
-            rot(x0, x1, pos, p.inv_freq[d >> 1]);
-            *reinterpret_cast<float2*>(p.yq + (long long)m * hd + n) = make_float2(x0, x1);
-            return;
-        }
-        if (sid < 0 || sid >= p.num_streams || pos < 0 || pos >= p.capacity) {
-            set_error(p.err, DEV_ERR_CAPACITY);
-            return;
-        }
-        const bool is_k = n < hd + kvd;
-        const int kvh = (n - hd - (is_k ? 0 : kvd)) / kHeadDim;
-        if (is_k) rot(x0, x1, pos, p.inv_freq[d >> 1]);
-        const uint32_t packed = pack_bf16x2(x0, x1);
-        const int group = p.heads / p.kv_heads;
-        __nv_bfloat16* base = (is_k ? p.k_cache : p.v_cache) +
-                              ((long long)sid * p.capacity + pos) * hd + d;
-        for (int rep = 0; rep < group; ++rep)
-            *reinterpret_cast<uint32_t*>(base + (kvh * group + rep) * kHeadDim) = packed;
     }
+}
+
+// EPI_QKV for the column pair (n, n+1) of row m at (sid, pos), with its RoPE table entry t
+// (loaded by the caller before any store, so no load waits behind the stores).
+__device__ __forceinline__ void qkv_pair(const LinearArgs& p, int m, int n, float c0, float c1, int sid,
+                                         int pos, float2 t) {
+    const int hd = p.heads * kHeadDim, kvd = p.kv_heads * kHeadDim;
+    const int d = n % kHeadDim;
+    float x0 = c0 * p.scale[n], x1 = c1 * p.scale[n + 1];
+    if (n < hd) {
+        rot(x0, x1, t);
+        *reinterpret_cast<float2*>(p.yq + (long long)m * hd + n) = make_float2(x0, x1);
+        return;
+    }
+    if (sid < 0 || sid >= p.num_streams || pos < 0 || pos >= p.capacity) {
+        set_error(p.err, DEV_ERR_CAPACITY);
+        return;
+    }
+    const bool is_k = n < hd + kvd;
+    const int kvh = (n - hd - (is_k ? 0 : kvd)) / kHeadDim;
+    if (is_k) rot(x0, x1, t);
+    const uint32_t packed = pack_bf16x2(x0, x1);
+    const int group = p.heads / p.kv_heads;
+    __nv_bfloat16* base = (is_k ? p.k_cache : p.v_cache) + ((long long)sid * p.capacity + pos) * hd + d;
+    for (int rep = 0; rep < group; ++rep)
+        *reinterpret_cast<uint32_t*>(base + (kvh * group + rep) * kHeadDim) = packed;
 }
 
 template <int EPI, int TM, bool F16>
@@ -304,6 +306,36 @@ __global__ void __launch_bounds__(kThreads) linear_kernel(LinearArgs p) {
     }
     cp_async_wait<0>();
 
+    if (EPI == EPI_QKV) {
+        // Row metadata and RoPE entries of all this thread's outputs first, then the stores.
+        int sid[MI][2], pos[MI][2];
+        float2 rt[MI][2][NI];
+        const bool rotated = n0 < (p.heads + p.kv_heads) * kHeadDim;  // q or k columns (BN | 64)
+#pragma unroll
+        for (int mi = 0; mi < MI; ++mi)
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int m = m0 + row0 + mi * 16 + g + 8 * h;
+                sid[mi][h] = m < p.M ? p.row_stream[m] : 0;
+                pos[mi][h] = m < p.M ? p.row_pos[m] : 0;
+                const long long trow = (long long)min(max(pos[mi][h], 0), p.capacity - 1) * kMaxPairs;
+#pragma unroll
+                for (int ni = 0; ni < NI; ++ni)
+                    rt[mi][h][ni] = rotated ? __ldg(p.rope + trow + ((n0 + col0 + ni * 8 + 2 * t) % kHeadDim) / 2)
+                                            : make_float2(1.f, 0.f);
+            }
+#pragma unroll
+        for (int mi = 0; mi < MI; ++mi)
+#pragma unroll
+            for (int ni = 0; ni < NI; ++ni) {
+                const int m = m0 + row0 + mi * 16 + g;
+                const int n = n0 + col0 + ni * 8 + 2 * t;
+                if (m < p.M) qkv_pair(p, m, n, acc[mi][ni][0], acc[mi][ni][1], sid[mi][0], pos[mi][0], rt[mi][0][ni]);
+                if (m + 8 < p.M)
+                    qkv_pair(p, m + 8, n, acc[mi][ni][2], acc[mi][ni][3], sid[mi][1], pos[mi][1], rt[mi][1][ni]);
+            }
+        return;
+    }
 #pragma unroll
     for (int mi = 0; mi < MI; ++mi) {
 #pragma unroll
@@ -417,9 +449,12 @@ void launch_typed(const LinearArgs& a, cudaStream_t s) {
 }  // namespace
 
 void launch_linear(const LinearArgs& a, LinearEpi epi, cudaStream_t s) {
+    // Default: tcgen05 below 4096 rows (decode and short prompts), mma.sync above, where its four
+    // CTAs per SM overlap epilogues with main loops. PTTS_B200_GEMM=mma / =tc force one kernel.
     const char* sel = getenv("PTTS_B200_GEMM");
-    if (sel && sel[0] == 't') launch_linear_tc(a, epi, s);
-    else launch_linear_mma(a, epi, s);
+    const bool use_tc = sel && sel[0] == 'm' ? false : (sel && sel[0] == 't') || a.M < 4096;
+    if (use_tc && launch_linear_tc(a, epi, s)) return;
+    launch_linear_mma(a, epi, s);
 }
 
 void launch_linear_mma(const LinearArgs& a, LinearEpi epi, cudaStream_t s) {

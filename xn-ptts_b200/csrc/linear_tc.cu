@@ -1,71 +1,74 @@
-// int8-weight linears on the 5th-generation tensor cores (tcgen05 + TMEM), sm_100a.
+// int8-weight linears on the 5th-generation tensor cores (tcgen05 + TMEM), fed by TMA, sm_100a.
 //
-// Same contract as linear.cu (LinearArgs, the five epilogues, A as f16 hi/lo planes or one bf16
-// plane, int8 weights with one f32 scale per output row); this file replaces its mma.sync main
-// loop.
+// Same contract as linear.cu (LinearArgs, the five epilogues, split-K slices) for the layer
+// stack's f16 hi/lo activations. The int8 weights are read through their exact f16 copy
+// (LinearArgs::wh, made once when a layer is loaded), so both operands reach shared memory by
+// TMA (cp.async.bulk.tensor, 128-byte swizzle) with no conversion on the way.
 //
-// CTA tile 128 (rows) x 64 (output features), K in steps of 64, a 4-stage shared-memory ring:
-//   warps 0-3  loaders: cp.async the A hi and lo planes straight into the 128-byte-swizzled
-//              K-major layout the MMA reads (16-byte chunk c of row r lands at chunk c ^ (r & 7)),
-//              cp.async the int8 weight tile raw, then convert it in registers to A's type (exact)
-//              into the same swizzled layout; fence.proxy.async, then arrive on the stage's
-//              `full` barrier. After the main loop they are the epilogue: warp w reads TMEM
-//              lanes 32w..32w+31 (one output row per thread) with tcgen05.ld.
-//   warp 4     one thread issues tcgen05.mma.cta_group::1.kind::f16 (M=128, N=64, K=16; f16 x
-//              f16 or bf16 x bf16 -> f32 in TMEM): per 64-wide K tile 4 steps x (hi, lo), then
-//              tcgen05.commit to the stage's `empty` barrier; after the last tile a commit to
-//              `done`.
-// TMEM: 64 columns (the 128x64 f32 accumulator), allocated and freed by warp 0.
-// Every mbarrier wait is bounded and sets DEV_ERR_TIMEOUT; on a timeout the CTA still waits
-// (bounded) for its copies and MMAs in flight and frees its TMEM before returning.
-// No cluster launch, no multicast.
+// Roles are swapped against the row-major view: the MMA's M side (128 TMEM lanes) is 128 output
+// features and its N side is RT activation rows, D^T[f][r] = sum_k W[f][k] X[r][k]. Per 16 k
+// that is one tcgen05.mma.cta_group::1.kind::f16 per activation plane (hi, lo) with A = the
+// weight tile and B = the activation tile, both K-major. A decode batch of 512 rows gives
+// (N / 128) x 16 CTAs of RT = 32 rows, two CTAs per SM by shared memory; prompts use RT = 128.
+//
+// CTA: 128 threads.
+//   thread 0:   TMA producer over a kStages ring of {W 128x64, X hi RTx64, X lo RTx64} f16
+//               tiles. The weight tiles of the first stages are requested before the wait on
+//               the grid that wrote X (weights never change).
+//   thread 32:  MMA issuer; tcgen05.commit frees each stage and finally signals `done`.
+//   all warps:  epilogue: warp w reads TMEM lanes 32w..32w+31 (features n0 + 32w + lane), 32
+//               rows per tcgen05.ld, and stores each row's 32 features as one coalesced run.
+// Every wait is bounded (DEV_ERR_TIMEOUT); after a timeout the CTA still waits, bounded, for the
+// copies it issued and frees its TMEM. No clusters, no multicast.
+#include <cuda.h>
+
+#include <map>
+#include <mutex>
+#include <tuple>
+
 #include "common.cuh"
 #include "kernels.h"
 
 namespace ptts {
 namespace {
 
-constexpr int TBM = 128, TBN = 64, TBK = 64;
-constexpr int kLoaderWarps = 4;
-constexpr int kThreadsTc = (kLoaderWarps + 1) * 32;
-constexpr int kStagesTc = 4;
-constexpr int kATileBytes = TBM * TBK * 2;   // 16 KB, 128-byte rows
-constexpr int kBTileBytes = TBN * TBK * 2;   // 8 KB
-constexpr int kBRawBytes = TBN * TBK;        // 4 KB int8
-constexpr int kStageTc = 2 * kATileBytes + kBTileBytes + kBRawBytes;  // 44 KB, 1024-aligned
-constexpr int kBarOffset = kStagesTc * kStageTc;
-constexpr int kSmemTc = 1024 + kBarOffset + 256;  // + alignment slack + barriers/TMEM address
-constexpr uint32_t kTmemCols = TBN;
+constexpr int FT = 128;  // output features per CTA (MMA M)
+constexpr int KS = 64;   // k per stage: one 128-byte swizzle row of f16
+constexpr int kThreadsTma = 128;
 
-// Instruction descriptor, kind::f16: D f32 (bits 4-5 = 1), A and B both f16 (format 0) or both
-// bf16 (format 1, bits 7-9 and 10-12), both K-major, N >> 3 at bit 17, M >> 4 at bit 24.
-constexpr uint32_t kIdescF16 = (1u << 4) | ((uint32_t)(TBN >> 3) << 17) | ((uint32_t)(TBM >> 4) << 24);
-constexpr uint32_t kIdescBf16 = kIdescF16 | (1u << 7) | (1u << 10);
+template <int RT>
+struct TmaTile {
+    static constexpr int kStages = 4;
+    static constexpr int kWBytes = FT * KS * 2;  // 16 KB
+    static constexpr int kXBytes = RT * KS * 2;  // per plane
+    static constexpr int kStageBytes = kWBytes + 2 * kXBytes;
+    static constexpr int kBarOffset = kStages * kStageBytes;
+    static constexpr int kSmem = 1024 + kBarOffset + 256;  // + alignment slack + barriers
+    static constexpr uint32_t kTmemCols = RT < 32 ? 32 : RT;
+    static_assert(RT % 32 == 0 && RT >= 32 && RT <= 256, "RT: 32..256 in steps of 32");
+    static_assert(kStageBytes % 1024 == 0, "stages stay 1024-byte aligned");
+    static_assert(32 * (FT + 4) * 4 <= kBarOffset, "the QKV staging tile fits in the ring");
+};
+
+// Instruction descriptor, kind::f16: D f32 (bits 4-5 = 1), A and B f16 (formats 0), both
+// K-major, N >> 3 at bit 17, M >> 4 at bit 24.
+template <int RT>
+constexpr uint32_t idesc_f16() {
+    return (1u << 4) | ((uint32_t)(RT >> 3) << 17) | ((uint32_t)(FT >> 4) << 24);
+}
 
 // Shared-memory matrix descriptor of a K-major, 128-byte-swizzled tile at `addr` (1024-aligned):
 // start >> 4 in bits 0-13, leading byte offset 1 (unused when swizzled), stride byte offset
-// 1024 B (8 rows of 128 B) >> 4 in bits 32-45, version 1 at bit 46, layout SWIZZLE_128B (2) at
-// bits 61-63.
+// 1024 B (8 rows of 128 B) >> 4 in bits 32-45, version 1 at bit 46, SWIZZLE_128B (2) at 61-63.
 __device__ __forceinline__ uint64_t sw128_desc(uint32_t addr) {
     return (uint64_t)((addr >> 4) & 0x3FFFu) | ((uint64_t)1u << 16) | ((uint64_t)(1024 >> 4) << 32) |
            ((uint64_t)1u << 46) | ((uint64_t)2u << 61);
 }
 
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
-    const int n = valid ? 16 : 0;
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(n) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
-__device__ __forceinline__ void fence_proxy_async() {
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
+// D (TMEM) += A (smem) x B (smem), or D = A x B when accumulate is 0.
 __device__ __forceinline__ void tc_mma(uint32_t tmem_d, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
                                        uint32_t accumulate) {
     asm volatile(
@@ -75,6 +78,7 @@ __device__ __forceinline__ void tc_mma(uint32_t tmem_d, uint64_t a_desc, uint64_
         ::"r"(tmem_d), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
         : "memory");
 }
+// Arrives on `bar` once every MMA this thread issued before has completed.
 __device__ __forceinline__ void tc_commit(uint64_t* bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
                      smem_u32(bar))
@@ -99,6 +103,31 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
     for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+__device__ __forceinline__ uint64_t policy_evict_last() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+
+// 2-D tiled TMA load of the box at (x = k, y = row) into shared memory, completing its bytes on
+// `bar`. x is a multiple of 64 f16 (128 bytes), so the 16-byte rule on x always holds.
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y,
+                                            uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+__device__ __forceinline__ void tma_load_2d_hint(uint32_t dst, const CUtensorMap* map, int x, int y,
+                                                 uint64_t* bar, uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar)), "l"(policy)
+        : "memory");
+}
+
 __device__ __forceinline__ float gelu_tc(float x, int tanh_form) {
     if (tanh_form) {
         const float u2 = (x * x * 0.07135482f + 1.595769f) * x;
@@ -107,91 +136,138 @@ __device__ __forceinline__ float gelu_tc(float x, int tanh_form) {
     return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f));
 }
 
-__device__ __forceinline__ void rot_tc(float& x0, float& x1, int pos, float inv_freq) {
-    float sn, cs;
-    sincosf((float)pos * inv_freq, &sn, &cs);
-    const float y0 = __fsub_rn(__fmul_rn(x0, cs), __fmul_rn(x1, sn));
-    const float y1 = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, cs));
-    x0 = y0;
-    x1 = y1;
+__device__ __forceinline__ __half f16_sat(float x) {
+    return __float2half_rn(fminf(fmaxf(x, -65504.f), 65504.f));
 }
 
-// Same arithmetic as linear.cu's epilogue for the column pair (n, n+1) of row m.
+// Epilogue of 32 rows (mbase .. mbase+31) of this thread's feature f; v[j] is row mbase + j.
+// Arithmetic as linear.cu's epilogue_pair (scale, then the epilogue's own operation).
+// EPI_QKV goes through qkv_rows instead.
 template <int EPI>
-__device__ __forceinline__ void epi_pair(const LinearArgs& p, int m, int n, int z, float c0, float c1) {
-    const float v0 = c0 * p.scale[n], v1 = c1 * p.scale[n + 1];
-    const long long at = (long long)m * p.N + n;
-    if (EPI == EPI_F32) {
-        *reinterpret_cast<float2*>(p.y + at) = make_float2(v0, v1);
-    } else if (EPI == EPI_PARTIAL) {
-        *reinterpret_cast<float2*>(p.y + (long long)z * p.M * p.N + at) = make_float2(v0, v1);
-    } else if (EPI == EPI_RESID) {
-        float2* y = reinterpret_cast<float2*>(p.y + at);
-        const float2 o = *y;
-        *y = make_float2(o.x + v0, o.y + v1);
-    } else if (EPI == EPI_GELU) {
-        uint32_t hi, lo;
-        split_f16x2(gelu_tc(v0, p.gelu_tanh), gelu_tc(v1, p.gelu_tanh), hi, lo);
-        static_cast<uint32_t*>(p.yb)[at >> 1] = hi;
-        static_cast<uint32_t*>(p.yb_lo)[at >> 1] = lo;
-    } else {  // EPI_QKV
-        const int hd = p.heads * kHeadDim, kvd = p.kv_heads * kHeadDim;
-        const int sid = p.row_stream[m], pos = p.row_pos[m];
-        const int d = n % kHeadDim;
-        float x0 = v0, x1 = v1;
-        if (n < hd) {
-            rot_tc(x0, x1, pos, p.inv_freq[d >> 1]);
-            *reinterpret_cast<float2*>(p.yq + (long long)m * hd + n) = make_float2(x0, x1);
-            return;
+__device__ __forceinline__ void epi_rows(const LinearArgs& p, int f, int mbase, int z, const float (&v)[32]) {
+    const float sc = __ldg(p.scale + f);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+        const int m = mbase + j;
+        if (m >= p.M) break;
+        const float x = v[j] * sc;
+        const long long at = (long long)m * p.N + f;
+        if (EPI == EPI_F32) {
+            p.y[at] = x;
+        } else if (EPI == EPI_PARTIAL) {
+            p.y[(long long)z * p.M * p.N + at] = x;
+        } else if (EPI == EPI_RESID) {
+            p.y[at] += x;
+        } else {  // EPI_GELU: f16 hi/lo planes
+            float hi, lo;
+            split_f16(gelu_tc(x, p.gelu_tanh), hi, lo);
+            static_cast<__half*>(p.yb)[at] = __float2half_rn(hi);
+            static_cast<__half*>(p.yb_lo)[at] = f16_sat(lo);
         }
-        if (sid < 0 || sid >= p.num_streams || pos < 0 || pos >= p.capacity) {
-            set_error(p.err, DEV_ERR_CAPACITY);
-            return;
-        }
-        const bool is_k = n < hd + kvd;
-        const int kvh = (n - hd - (is_k ? 0 : kvd)) / kHeadDim;
-        if (is_k) rot_tc(x0, x1, pos, p.inv_freq[d >> 1]);
-        const uint32_t packed = pack_bf16x2(x0, x1);
-        const int group = p.heads / p.kv_heads;
-        __nv_bfloat16* base = (is_k ? p.k_cache : p.v_cache) + ((long long)sid * p.capacity + pos) * hd + d;
-        for (int rep = 0; rep < group; ++rep)
-            *reinterpret_cast<uint32_t*>(base + (kvh * group + rep) * kHeadDim) = packed;
     }
 }
 
-template <int EPI>
-__global__ void __launch_bounds__(kThreadsTc, 1) linear_tc_kernel(LinearArgs p) {
-    extern __shared__ unsigned char smem_raw[];
+// Staged tile row stride in floats: 128 features + 4 (keeps float4 alignment, spreads banks).
+constexpr int kStageStride = FT + 4;
+
+// EPI_QKV of 32 staged rows: st[j * kStageStride + c] = accumulator of row mbase + j, tile
+// feature c. Warp w takes rows w, w + 4, ..., lane l features n0 + 4l .. 4l + 3, i.e. the RoPE
+// pairs (4l, 4l+1) and (4l+2, 4l+3) (rope.rs:37-95), with the arithmetic of linear.cu's qkv_pair.
+// Row metadata and every RoPE entry are loaded before the first store.
+__device__ __forceinline__ void qkv_rows(const LinearArgs& p, const float* st, int n0, int mbase) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int hd = p.heads * kHeadDim, kvd = p.kv_heads * kHeadDim;
+    const int f = n0 + 4 * lane, d = f % kHeadDim;
+    const int region = f < hd ? 0 : (f < hd + kvd ? 1 : 2);
+    const int group = p.heads / p.kv_heads;
+    const float4 sc = __ldg(reinterpret_cast<const float4*>(p.scale + f));
+    const int ml = mbase + lane;
+    const int pos_l = ml < p.M ? __ldg(p.row_pos + ml) : 0;
+    const int sid_l = ml < p.M ? __ldg(p.row_stream + ml) : 0;
+    float4 t[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const int pos = __shfl_sync(0xffffffffu, pos_l, warp + 4 * i);
+        t[i] = region != 2 ? __ldg(reinterpret_cast<const float4*>(
+                                 p.rope + (long long)min(max(pos, 0), p.capacity - 1) * kMaxPairs + (d >> 1)))
+                           : make_float4(1.f, 0.f, 1.f, 0.f);
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const int j = warp + 4 * i, m = mbase + j;
+        const int pos = __shfl_sync(0xffffffffu, pos_l, j);
+        const int sid = __shfl_sync(0xffffffffu, sid_l, j);
+        const float4 a = *reinterpret_cast<const float4*>(st + j * kStageStride + 4 * lane);
+        float x0 = a.x * sc.x, x1 = a.y * sc.y, x2 = a.z * sc.z, x3 = a.w * sc.w;
+        if (region != 2) {
+            const float y0 = __fsub_rn(__fmul_rn(x0, t[i].x), __fmul_rn(x1, t[i].y));
+            const float y1 = __fadd_rn(__fmul_rn(x0, t[i].y), __fmul_rn(x1, t[i].x));
+            const float y2 = __fsub_rn(__fmul_rn(x2, t[i].z), __fmul_rn(x3, t[i].w));
+            const float y3 = __fadd_rn(__fmul_rn(x2, t[i].w), __fmul_rn(x3, t[i].z));
+            x0 = y0;
+            x1 = y1;
+            x2 = y2;
+            x3 = y3;
+        }
+        if (m >= p.M) continue;
+        if (region == 0) {
+            *reinterpret_cast<float4*>(p.yq + (long long)m * hd + f) = make_float4(x0, x1, x2, x3);
+            continue;
+        }
+        if (sid < 0 || sid >= p.num_streams || pos < 0 || pos >= p.capacity) {
+            set_error(p.err, DEV_ERR_CAPACITY);
+            continue;
+        }
+        const bool is_k = region == 1;
+        const int kvh = (f - hd - (is_k ? 0 : kvd)) / kHeadDim;
+        const uint2 packed = make_uint2(pack_bf16x2(x0, x1), pack_bf16x2(x2, x3));
+        __nv_bfloat16* base = (is_k ? p.k_cache : p.v_cache) + ((long long)sid * p.capacity + pos) * hd + d;
+        for (int rep = 0; rep < group; ++rep)
+            *reinterpret_cast<uint2*>(base + (kvh * group + rep) * kHeadDim) = packed;
+    }
+}
+
+template <int EPI, int RT>
+__global__ void __launch_bounds__(kThreadsTma) linear_tma_kernel(const __grid_constant__ LinearArgs p,
+                                                                 const __grid_constant__ CUtensorMap tm_w,
+                                                                 const __grid_constant__ CUtensorMap tm_x,
+                                                                 const __grid_constant__ CUtensorMap tm_xlo) {
+    using T = TmaTile<RT>;
+    constexpr int S = T::kStages;
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
-    const uint32_t base = (raw + 1023u) & ~1023u;  // 1024-aligned for the 128-byte swizzle
+    const uint32_t base = (raw + 1023u) & ~1023u;
     unsigned char* smem = smem_raw + (base - raw);
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kBarOffset);
-    uint64_t* empty = full + kStagesTc;
-    uint64_t* done = empty + kStagesTc;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + T::kBarOffset);
+    uint64_t* empty = full + S;
+    uint64_t* done = empty + S;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
-    __shared__ int s_abort;
+    __shared__ int s_issued, s_consumed;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int n0 = blockIdx.x * TBN, m0 = blockIdx.y * TBM, z = blockIdx.z;
+    const int n0 = blockIdx.x * FT, m0 = blockIdx.y * RT, z = blockIdx.z;
     const int k_len = p.K / p.splits;
     const int k0 = z * k_len;
-    const int KT = k_len / TBK;
+    const int KT = k_len / KS;
     const bool has_lo = p.a_lo != nullptr;
-    const bool f16 = p.a_f16 != 0;
+    const uint32_t stage_tx = T::kWBytes + (has_lo ? 2u : 1u) * T::kXBytes;
 
     if (tid == 0) {
-        s_abort = 0;
-        for (int s = 0; s < kStagesTc; ++s) {
-            mbar_init(&full[s], kLoaderWarps);
+        s_issued = 0;
+        s_consumed = 0;
+        for (int s = 0; s < S; ++s) {
+            mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
         }
         mbar_init(done, 1);
         fence_mbar_init();
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tm_w)) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tm_x)) : "memory");
     }
     if (warp == 0) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                          smem_u32(tmem_slot)),
-                     "r"(kTmemCols)
+                     "r"(T::kTmemCols)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
@@ -199,166 +275,193 @@ __global__ void __launch_bounds__(kThreadsTc, 1) linear_tc_kernel(LinearArgs p) 
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    grid_dep_wait();
-    grid_dep_launch();
 
-    if (warp < kLoaderWarps) {
-        // ---- loaders -------------------------------------------------------------------------
-        const int lt = tid;  // 0..127
-        bool ok = true;
-        // Issue the loads of K tile `it` into its stage.
-        auto issue = [&](int it) {
-            const int st = it % kStagesTc;
-            const uint32_t sa = base + st * kStageTc;
-            const int kb = k0 + it * TBK;
-            // A: 128 rows x 8 chunks of 16 B per plane; 8 consecutive threads cover one row.
-            const int c = lt & 7;
-#pragma unroll
-            for (int i = 0; i < TBM / 16; ++i) {
-                const int r = i * 16 + (lt >> 3);
-                const int gm = m0 + r;
-                const bool valid = gm < p.M;
-                const long long off = 2 * ((long long)(valid ? gm : 0) * p.K + kb + c * 8);  // bytes
-                const uint32_t dst = sa + r * 128 + ((c ^ (r & 7)) << 4);
-                cp_async16(dst, static_cast<const unsigned char*>(p.a) + off, valid);
-                if (has_lo) cp_async16(dst + kATileBytes, static_cast<const unsigned char*>(p.a_lo) + off, valid);
-            }
-            // B raw: 64 rows x 4 chunks of 16 int8; thread lt takes chunks lt and lt + 128.
-#pragma unroll
-            for (int q = 0; q < 2; ++q) {
-                const int c = lt + 128 * q;
-                const int n = c >> 2, cc = c & 3;
-                cp_async16(sa + 2 * kATileBytes + kBTileBytes + n * 64 + cc * 16,
-                           p.w + (long long)(n0 + n) * p.K + kb + cc * 16, true);
-            }
-        };
-        // Convert this thread's two raw chunks of K tile `it` into the swizzled f16/bf16 tile.
-        auto convert = [&](int it) {
-            const int st = it % kStagesTc;
-            unsigned char* sp = smem + st * kStageTc;
-            const unsigned char* rawb = sp + 2 * kATileBytes + kBTileBytes;
-            unsigned char* bt = sp + 2 * kATileBytes;
-#pragma unroll
-            for (int q = 0; q < 2; ++q) {
-                const int c = lt + 128 * q;  // the chunks this thread loaded
-                const int n = c >> 2, cc = c & 3;  // 16 weights k = 16cc .. 16cc+15 of row n
-                const uint4 u = *reinterpret_cast<const uint4*>(rawb + n * 64 + cc * 16);
-                const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {  // two 16-byte chunks: k-chunk 2cc + h
-                    uint4 o;
-                    const float f[8] = {
-                        (float)(int8_t)(w[2 * h] & 0xff),         (float)(int8_t)((w[2 * h] >> 8) & 0xff),
-                        (float)(int8_t)((w[2 * h] >> 16) & 0xff), (float)(int8_t)(w[2 * h] >> 24),
-                        (float)(int8_t)(w[2 * h + 1] & 0xff),     (float)(int8_t)((w[2 * h + 1] >> 8) & 0xff),
-                        (float)(int8_t)((w[2 * h + 1] >> 16) & 0xff), (float)(int8_t)(w[2 * h + 1] >> 24)};
-                    if (f16) {
-                        o.x = pack_f16x2(f[0], f[1]); o.y = pack_f16x2(f[2], f[3]);
-                        o.z = pack_f16x2(f[4], f[5]); o.w = pack_f16x2(f[6], f[7]);
-                    } else {
-                        o.x = pack_bf16x2(f[0], f[1]); o.y = pack_bf16x2(f[2], f[3]);
-                        o.z = pack_bf16x2(f[4], f[5]); o.w = pack_bf16x2(f[6], f[7]);
-                    }
-                    const int kc = 2 * cc + h;
-                    *reinterpret_cast<uint4*>(bt + n * 128 + ((kc ^ (n & 7)) << 4)) = o;
-                }
-            }
-        };
-        // Software pipeline: loads run kStagesTc - 1 tiles ahead of the conversions.
-        for (int it = 0; it < KT + kStagesTc - 1 && ok; ++it) {
-            if (it < KT) {
-                const int st = it % kStagesTc;
-                if (!mbar_wait(&empty[st], ((it / kStagesTc) & 1) ^ 1)) {
-                    set_error(p.err, DEV_ERR_TIMEOUT);
-                    ok = false;
-                }
-                if (ok) issue(it);
-            }
-            cp_async_commit();
-            const int j = it - (kStagesTc - 1);
-            if (j >= 0 && ok) {
-                cp_async_wait<kStagesTc - 1>();
-                convert(j);
-                fence_proxy_async();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&full[j % kStagesTc]);
-            }
+    if (tid == 0) {
+        // ---- TMA producer ----------------------------------------------------------------------
+        const uint64_t pol_w = policy_evict_last();  // weights: reread every frame
+        const int pre = KT < S ? KT : S;
+        for (int kt = 0; kt < pre; ++kt) {
+            mbar_arrive_expect_tx(&full[kt], stage_tx);
+            tma_load_2d_hint(base + kt * T::kStageBytes, &tm_w, k0 + kt * KS, n0, &full[kt], pol_w);
         }
-        cp_async_wait<0>();
-        if (!ok) s_abort = 1;
-        // ---- epilogue: this warp's 32 TMEM lanes = rows 32w .. 32w+31 of the tile ------------
-        const bool got = mbar_wait(done, 0);
-        if (!got) set_error(p.err, DEV_ERR_TIMEOUT);
-        tc_fence_after();
-        const int m = m0 + 32 * warp + lane;
-#pragma unroll
-        for (int c = 0; c < TBN; c += 32) {
-            float v[32];
-            tmem_ld32(tmem + ((uint32_t)(32 * warp) << 16) + (uint32_t)c, v);
-            if (got && m < p.M) {
-#pragma unroll
-                for (int j = 0; j < 32; j += 2) epi_pair<EPI>(p, m, n0 + c + j, z, v[j], v[j + 1]);
-            }
-        }
-    } else if (lane == 0) {
-        // ---- MMA issuer ----------------------------------------------------------------------
-        bool ok = true;
-        int issued = 0;
+        grid_dep_wait();
+        grid_dep_launch();
         for (int kt = 0; kt < KT; ++kt) {
-            const int st = kt % kStagesTc;
-            if (!mbar_wait(&full[st], (kt / kStagesTc) & 1)) {
-                set_error(p.err, DEV_ERR_TIMEOUT);
-                ok = false;
-                break;
+            const int st = kt % S;
+            const uint32_t sa = base + st * T::kStageBytes;
+            if (kt >= pre) {
+                if (!mbar_wait(&empty[st], ((kt / S) & 1) ^ 1)) {
+                    set_error(p.err, DEV_ERR_TIMEOUT);
+                    break;
+                }
+                mbar_arrive_expect_tx(&full[st], stage_tx);
+                tma_load_2d_hint(sa, &tm_w, k0 + kt * KS, n0, &full[st], pol_w);
             }
-            tc_fence_after();
-            const uint32_t sa = base + st * kStageTc;
-            const uint64_t dhi = sw128_desc(sa), dlo = sw128_desc(sa + kATileBytes);
-            const uint64_t db = sw128_desc(sa + 2 * kATileBytes);
-            const uint32_t idesc = f16 ? kIdescF16 : kIdescBf16;
-#pragma unroll
-            for (int kk = 0; kk < TBK / 16; ++kk) {  // 32 bytes of K per MMA
-                tc_mma(tmem, dhi + 2 * kk, db + 2 * kk, idesc, (kt | kk) ? 1u : 0u);
-                if (has_lo) tc_mma(tmem, dlo + 2 * kk, db + 2 * kk, idesc, 1u);
-            }
-            tc_commit(&empty[st]);
-            ++issued;
+            tma_load_2d(sa + T::kWBytes, &tm_x, k0 + kt * KS, m0, &full[st]);
+            if (has_lo) tma_load_2d(sa + T::kWBytes + T::kXBytes, &tm_xlo, k0 + kt * KS, m0, &full[st]);
+            s_issued = kt + 1;
         }
-        (void)ok;
-        tc_commit(done);  // arrives once every MMA issued above has completed
+    } else {
+        grid_dep_wait();
+        grid_dep_launch();
+        if (tid == 32) {
+            // ---- MMA issuer --------------------------------------------------------------------
+            constexpr uint32_t idesc = idesc_f16<RT>();
+            for (int kt = 0; kt < KT; ++kt) {
+                const int st = kt % S;
+                if (!mbar_wait(&full[st], (kt / S) & 1)) {
+                    set_error(p.err, DEV_ERR_TIMEOUT);
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t sa = base + st * T::kStageBytes;
+                const uint64_t dw = sw128_desc(sa), dx = sw128_desc(sa + T::kWBytes);
+                const uint64_t dxl = sw128_desc(sa + T::kWBytes + T::kXBytes);
+#pragma unroll
+                for (int kk = 0; kk < KS / 16; ++kk) {  // 32 bytes of K per MMA
+                    tc_mma(tmem, dw + 2 * kk, dx + 2 * kk, idesc, (kt | kk) ? 1u : 0u);
+                    if (has_lo) tc_mma(tmem, dw + 2 * kk, dxl + 2 * kk, idesc, 1u);
+                }
+                tc_commit(&empty[st]);
+                s_consumed = kt + 1;
+            }
+            tc_commit(done);  // arrives once every MMA issued above has completed
+        }
     }
+    __syncwarp();
+
+    // ---- epilogue: feature n0 + 32w + lane, rows m0 .. m0 + RT - 1 ------------------------------
+    const bool got = mbar_wait(done, 0);
+    if (!got) set_error(p.err, DEV_ERR_TIMEOUT);
+    __syncwarp();  // tcgen05.ld below is warp-collective
+    tc_fence_after();
+    const int f = n0 + 32 * warp + lane;
+#pragma unroll 1
+    for (int c = 0; c < RT; c += 32) {
+        float v[32];
+        tmem_ld32(tmem + ((uint32_t)(32 * warp) << 16) + (uint32_t)c, v);
+        if (EPI == EPI_QKV) {
+            // Transpose through shared memory (the drained ring): lanes then own feature quads.
+            float* st = reinterpret_cast<float*>(smem);
+            __syncthreads();  // the previous chunk's readers are done
+#pragma unroll
+            for (int j = 0; j < 32; ++j) st[j * kStageStride + 32 * warp + lane] = v[j];
+            __syncthreads();
+            if (got) qkv_rows(p, st, n0, m0 + c);
+        } else if (got) {
+            epi_rows<EPI>(p, f, m0 + c, z, v);
+        }
+    }
+
     tc_fence_before();
     __syncthreads();
+    if (tid == 0) {
+        // Copies issued but never consumed (only after a timeout): let them land before exit.
+        for (int kt = s_consumed; kt < s_issued; ++kt) mbar_wait(&full[kt % S], (kt / S) & 1);
+    }
     if (warp == 0) {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                     "r"(T::kTmemCols)
                      : "memory");
     }
 }
 
-template <int EPI>
-void launch_tc_typed(const LinearArgs& a, cudaStream_t s) {
+// ---- tensor maps ---------------------------------------------------------------------------
+
+using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                 const cuuint64_t*, const cuuint32_t*, const cuuint32_t*,
+                                 CUtensorMapInterleave, CUtensorMapSwizzle, CUtensorMapL2promotion,
+                                 CUtensorMapFloatOOBfill);
+
+EncodeTiled encoder() {
+    static const EncodeTiled fn = [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &f, 12000, cudaEnableDefault, &q) !=
+                cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            f = nullptr;
+        return reinterpret_cast<EncodeTiled>(f);
+    }();
+    return fn;
+}
+
+// Tensor map of a row-major [rows][cols] f16 matrix, box 64 (k) x box_rows, 128-byte swizzle,
+// zero fill past the last row. A map is a pure function of its key, so cached maps never go
+// stale; the cache is cleared when it grows large (prompt lengths vary).
+bool f16_map(CUtensorMap* out, const void* ptr, int rows, int cols, int box_rows) {
+    using Key = std::tuple<const void*, int, int, int>;
+    static std::mutex mu;
+    static std::map<Key, CUtensorMap> cache;
+    const Key key{ptr, rows, cols, box_rows};
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) {
+        *out = it->second;
+        return true;
+    }
+    EncodeTiled enc = encoder();
+    if (!enc) return false;
+    const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
+    const cuuint32_t box[2] = {(cuuint32_t)KS, (cuuint32_t)box_rows};
+    const cuuint32_t elem[2] = {1, 1};
+    CUtensorMap m;
+    if (enc(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, elem,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return false;
+    if (cache.size() > 4096) cache.clear();
+    cache.emplace(key, m);
+    *out = m;
+    return true;
+}
+
+template <int EPI, int RT>
+bool launch_tma(const LinearArgs& a, cudaStream_t s) {
+    using T = TmaTile<RT>;
+    CUtensorMap mw, mx, mxl;
+    if (!f16_map(&mw, a.wh, a.N, a.K, FT) || !f16_map(&mx, a.a, a.M, a.K, RT)) return false;
+    if (a.a_lo) {
+        if (!f16_map(&mxl, a.a_lo, a.M, a.K, RT)) return false;
+    } else {
+        mxl = mx;
+    }
     static int configured = -1;
     int dev = 0;
     cudaGetDevice(&dev);
     if (configured != dev) {
-        cudaFuncSetAttribute(linear_tc_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemTc);
+        cudaFuncSetAttribute(linear_tma_kernel<EPI, RT>, cudaFuncAttributeMaxDynamicSharedMemorySize, T::kSmem);
         configured = dev;
     }
-    dim3 grid(a.N / TBN, (a.M + TBM - 1) / TBM, a.splits);
-    launch_k(linear_tc_kernel<EPI>, grid, dim3(kThreadsTc), kSmemTc, s, a);
+    dim3 grid(a.N / FT, (a.M + RT - 1) / RT, a.splits);
+    launch_k(linear_tma_kernel<EPI, RT>, grid, dim3(kThreadsTma), T::kSmem, s, a, mw, mx, mxl);
+    return true;
+}
+
+template <int EPI>
+bool launch_tma_rows(const LinearArgs& a, cudaStream_t s) {
+    return a.M < 4096 ? launch_tma<EPI, 32>(a, s) : launch_tma<EPI, 128>(a, s);
 }
 
 }  // namespace
 
-void launch_linear_tc(const LinearArgs& a, LinearEpi epi, cudaStream_t s) {
+bool linear_tc_supported(const LinearArgs& a) {
+    return a.wh != nullptr && a.a_f16 && a.M > 0 && a.N % FT == 0 && a.K % 8 == 0 && a.splits >= 1 &&
+           a.K % a.splits == 0 && (a.K / a.splits) % KS == 0;
+}
+
+bool launch_linear_tc(const LinearArgs& a, LinearEpi epi, cudaStream_t s) {
+    if (!linear_tc_supported(a)) return false;
     switch (epi) {
-        case EPI_F32: launch_tc_typed<EPI_F32>(a, s); break;
-        case EPI_QKV: launch_tc_typed<EPI_QKV>(a, s); break;
-        case EPI_RESID: launch_tc_typed<EPI_RESID>(a, s); break;
-        case EPI_GELU: launch_tc_typed<EPI_GELU>(a, s); break;
-        case EPI_PARTIAL: launch_tc_typed<EPI_PARTIAL>(a, s); break;
+        case EPI_F32: return launch_tma_rows<EPI_F32>(a, s);
+        case EPI_QKV: return launch_tma_rows<EPI_QKV>(a, s);
+        case EPI_RESID: return launch_tma_rows<EPI_RESID>(a, s);
+        case EPI_GELU: return launch_tma_rows<EPI_GELU>(a, s);
+        case EPI_PARTIAL: return launch_tma_rows<EPI_PARTIAL>(a, s);
     }
+    return false;
 }
 
 }  // namespace ptts

@@ -171,6 +171,31 @@ void launch_reset_streams(void* k, void* v, int32_t* lengths, const int32_t* str
              stream_bytes / 16);
 }
 
+__global__ void rope_table_kernel(RopeFreqs f, float2* __restrict__ out, int rows) {
+    const long long n = (long long)rows * kMaxPairs;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+        const int pos = (int)(i / kMaxPairs), k = (int)(i % kMaxPairs);
+        float sn, cs;
+        sincosf((float)pos * f.inv_freq[k], &sn, &cs);
+        out[i] = make_float2(cs, sn);
+    }
+}
+
+void launch_rope_table(RopeFreqs f, float2* out, int rows, cudaStream_t s) {
+    const long long blocks = ((long long)rows * kMaxPairs + 255) / 256;
+    rope_table_kernel<<<(int)(blocks < 4096 ? blocks : 4096), 256, 0, s>>>(f, out, rows);
+}
+
+__global__ void i8_to_f16_kernel(const int8_t* __restrict__ x, __half* __restrict__ y, long long n) {
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
+        y[i] = __short2half_rn((short)x[i]);
+}
+
+void launch_i8_to_f16(const int8_t* x, __half* y, long long n, cudaStream_t s) {
+    const long long blocks = (n + 255) / 256;
+    i8_to_f16_kernel<<<(int)(blocks < 4096 ? blocks : 4096), 256, 0, s>>>(x, y, n);
+}
+
 void launch_bf16_to_f32(const __nv_bfloat16* x, float* y, long long n, cudaStream_t s) {
     const long long blocks = (n + 255) / 256;
     launch_k(bf16_to_f32_kernel, dim3((int)(blocks < 4096 ? blocks : 4096)), dim3(256), 0, s, x, y, n);
