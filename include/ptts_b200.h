@@ -243,6 +243,64 @@ int ptts_b200_set_tracing(int on);
 /* Read (and with reset != 0, clear) the counters. */
 int ptts_b200_trace_read(ptts_b200_trace* out, int reset);
 
+/* ---- Flow head: the rest of a frame -------------------------------------------------------
+ * FlowLM's per-frame tail (flow_lm.rs:296-324, :360-410) and its flow net SimpleMLPAdaLN
+ * (mlp.rs): out_norm -> EOS logit (out_eos) and the latent from the solver's starting point
+ * (LSD: `lsd_steps` Euler steps of the flow net, each conditioned on the times (i/N, (i+1)/N);
+ * drifting: one evaluation; pointwise: noise + one evaluation), plus input_linear, which turns
+ * the previous latent (or bos_emb) into the next backbone input. z_proj is not supported: the
+ * head reads the d_model-wide backbone output (z_dim absent, as in the phonon checkpoints). */
+typedef struct ptts_b200_flow ptts_b200_flow;
+
+enum { PTTS_B200_FLOW_LSD = 0, PTTS_B200_FLOW_DRIFTING = 1, PTTS_B200_FLOW_POINTWISE = 2 };
+enum { PTTS_B200_TIME_RMS = 0, PTTS_B200_TIME_RMS_VAR = 1 };
+
+typedef struct {
+    int d_model;     /* backbone width (512); the flow net's cond_channels */
+    int flow_dim;    /* flow net width (512), a multiple of 128 */
+    int flow_depth;  /* residual blocks (6) */
+    int ldim;        /* latent width (32), at most 64 */
+    int freq_dim;    /* time embedders' frequency width (256) */
+    int flow_type;   /* PTTS_B200_FLOW_* */
+    int lsd_steps;   /* LSD solver steps (1) */
+    int time_norm;   /* PTTS_B200_TIME_RMS (audiocraft / phonon) or _RMS_VAR (pocket-tts) */
+} ptts_b200_flow_config;
+
+/* Weights are set one tensor at a time under the checkpoint's own names (FlowLM::load,
+ * flow_lm.rs:196-283, and the SimpleMLPAdaLN paths of mlp.rs), as f32 host arrays of `numel`
+ * elements, row-major with Linear weights [out][in]:
+ *   input_linear.weight [d_model][ldim]       out_norm.weight, out_norm.bias [d_model]
+ *   out_eos.weight [1][d_model], out_eos.bias [1]          bos_emb [ldim]
+ *   flow_net.input_proj.{weight [flow_dim][ldim], bias}    flow_net.cond_embed.{weight [flow_dim][d_model], bias}
+ *   flow_net.time_embed.{i}.freqs [freq_dim/2]  .mlp.0.{weight [flow_dim][freq_dim], bias}
+ *   flow_net.time_embed.{i}.mlp.2.{weight [flow_dim][flow_dim], bias}  .mlp.3.alpha [flow_dim]
+ *   flow_net.res_blocks.{i}.in_ln.{weight, bias} [flow_dim]   .mlp.0.{weight, bias}  .mlp.2.{weight, bias}
+ *   flow_net.res_blocks.{i}.adaLN_modulation.1.{weight [3 flow_dim][flow_dim], bias}
+ *   flow_net.final_layer.adaLN_modulation.1.{weight [2 flow_dim][flow_dim], bias}
+ *   flow_net.final_layer.linear.{weight [ldim][flow_dim], bias}
+ *   condition [d_model] (optional: the summed condition providers added to every input row)
+ * (time_embed.{i} for i < 2 with LSD, none otherwise.) ptts_b200_flow_finish checks that every
+ * tensor is present, uploads them (large linears as bf16 hi + lo planes, so f32 weights stay
+ * exact to 16 bits) and computes the solver steps' time embeddings once, as FlowLM::load does. */
+int ptts_b200_flow_create(int device, const ptts_b200_flow_config* config, ptts_b200_flow** out);
+void ptts_b200_flow_destroy(ptts_b200_flow* flow);
+int ptts_b200_flow_set_tensor(ptts_b200_flow* flow, const char* name, const float* host, int64_t numel);
+int ptts_b200_flow_finish(ptts_b200_flow* flow);
+
+/* FlowLM::sample_from_noise (flow_lm.rs:360-384): t_out [n][d_model] f32 (the backbone output
+ * after out_norm), noise [n][ldim] f32 -> latent [n][ldim] f32 and eos [n] f32 (raw logits).
+ * Device pointers, stream-ordered. */
+int ptts_b200_flow_sample(ptts_b200_flow* flow, const float* t_out, int n, const float* noise,
+                          float* latent, float* eos, void* cuda_stream);
+
+/* One frame (FlowLM::sample_next_latent_step, flow_lm.rs:392-410): input_linear(latent) (+
+ * condition) as the bf16 backbone input, ptts_b200_step over `streams_host`, out_norm, then
+ * ptts_b200_flow_sample. latent_in NULL starts from bos_emb (StepInput::Bos). Device pointers
+ * [n][ldim] f32 for latent_in, noise and latent_out, [n] f32 for eos. */
+int ptts_b200_frame(ptts_b200_model* model, ptts_b200_flow* flow, ptts_b200_kv* kv,
+                    const int32_t* streams_host, int n, const float* latent_in, const float* noise,
+                    float* latent_out, float* eos, void* cuda_stream);
+
 #ifdef __cplusplus
 }
 #endif

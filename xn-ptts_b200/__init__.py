@@ -42,6 +42,8 @@ EXPORTS = (
     "ptts_b200_attend", "ptts_b200_linear_i8",
     "ptts_b200_model_create", "ptts_b200_model_destroy", "ptts_b200_model_load_layer",
     "ptts_b200_forward", "ptts_b200_step", "ptts_b200_attend_decode_noalloc",
+    "ptts_b200_flow_create", "ptts_b200_flow_destroy", "ptts_b200_flow_set_tensor",
+    "ptts_b200_flow_finish", "ptts_b200_flow_sample", "ptts_b200_frame",
 )
 
 
@@ -68,6 +70,12 @@ class Config(ctypes.Structure):
                 ("num_kv_heads", ctypes.c_int32), ("head_dim", ctypes.c_int32),
                 ("num_layers", ctypes.c_int32), ("dim_feedforward", ctypes.c_int32),
                 ("max_period", ctypes.c_float), ("gelu", ctypes.c_int32)]
+
+
+class FlowConfigC(ctypes.Structure):
+    _fields_ = [("d_model", ctypes.c_int), ("flow_dim", ctypes.c_int), ("flow_depth", ctypes.c_int),
+                ("ldim", ctypes.c_int), ("freq_dim", ctypes.c_int), ("flow_type", ctypes.c_int),
+                ("lsd_steps", ctypes.c_int), ("time_norm", ctypes.c_int)]
 
 
 class Trace(ctypes.Structure):
@@ -126,6 +134,13 @@ def lib() -> ctypes.CDLL:
         L.ptts_b200_forward.argtypes = [P, P, P, IP, IP, I, P, P]
         L.ptts_b200_step.argtypes = [P, P, IP, I, P, P, P]
         L.ptts_b200_attend_decode_noalloc.argtypes = [P, P, I, I, I, P, P, I, P, P, P, I, I, F, P, I, P, P]
+        L.ptts_b200_flow_create.argtypes = [I, ctypes.POINTER(FlowConfigC), ctypes.POINTER(P)]
+        L.ptts_b200_flow_destroy.argtypes = [P]
+        L.ptts_b200_flow_destroy.restype = None
+        L.ptts_b200_flow_set_tensor.argtypes = [P, ctypes.c_char_p, P, ctypes.c_int64]
+        L.ptts_b200_flow_finish.argtypes = [P]
+        L.ptts_b200_flow_sample.argtypes = [P, P, I, P, P, P, P]
+        L.ptts_b200_frame.argtypes = [P, P, P, IP, I, P, P, P, P, P]
         _lib = L
     return _lib
 
@@ -498,3 +513,150 @@ def random_weights(cfg: FlowLMConfig, seed: int, *, ln_random: bool = False,
         ln = [np.full((L, d), ln_gain, np.float32), np.zeros((L, d), np.float32),
               np.full((L, d), ln_gain, np.float32), np.zeros((L, d), np.float32)]
     return Weights(w_qkv, s_qkv, w_out, s_out, w_ff1, s_ff1, w_ff2, s_ff2, *ln)
+
+
+# --------------------------------------------------------------------------------------------
+# flow head (FlowLM's frame tail, flow_lm.rs:296-410; SimpleMLPAdaLN, mlp.rs)
+# --------------------------------------------------------------------------------------------
+
+FLOW_TYPES = {"lsd": 0, "drifting": 1, "pointwise": 2}
+TIME_NORMS = {"rms": 0, "rms_var": 1}
+
+
+@dataclass
+class FlowConfig:
+    """The flow head's shape (FlowLMConfig flow_* fields, flow_lm.rs:114-146). Phonon: flow_dim
+    512, depth 6, ldim 32, one LSD step, the uncentred RMS time norm."""
+    d_model: int = 512
+    flow_dim: int = 512
+    flow_depth: int = 6
+    ldim: int = 32
+    freq_dim: int = 256
+    flow_type: str = "lsd"
+    lsd_steps: int = 1
+    time_norm: str = "rms"
+
+    @property
+    def time_conds(self) -> int:
+        return 2 if self.flow_type == "lsd" else 0
+
+    def c_struct(self) -> FlowConfigC:
+        return FlowConfigC(self.d_model, self.flow_dim, self.flow_depth, self.ldim, self.freq_dim,
+                           FLOW_TYPES[self.flow_type], self.lsd_steps, TIME_NORMS[self.time_norm])
+
+    def shapes(self) -> dict:
+        """Every tensor ptts_b200_flow_set_tensor takes, name -> shape (the checkpoint's keys)."""
+        d, C, L, F = self.d_model, self.flow_dim, self.ldim, self.freq_dim
+        sh = {"input_linear.weight": (d, L), "out_norm.weight": (d,), "out_norm.bias": (d,),
+              "out_eos.weight": (1, d), "out_eos.bias": (1,), "bos_emb": (L,),
+              "flow_net.input_proj.weight": (C, L), "flow_net.input_proj.bias": (C,),
+              "flow_net.cond_embed.weight": (C, d), "flow_net.cond_embed.bias": (C,),
+              "flow_net.final_layer.adaLN_modulation.1.weight": (2 * C, C),
+              "flow_net.final_layer.adaLN_modulation.1.bias": (2 * C,),
+              "flow_net.final_layer.linear.weight": (L, C), "flow_net.final_layer.linear.bias": (L,)}
+        for i in range(self.time_conds):
+            p = f"flow_net.time_embed.{i}."
+            sh.update({p + "freqs": (F // 2,), p + "mlp.0.weight": (C, F), p + "mlp.0.bias": (C,),
+                       p + "mlp.2.weight": (C, C), p + "mlp.2.bias": (C,), p + "mlp.3.alpha": (C,)})
+        for b in range(self.flow_depth):
+            p = f"flow_net.res_blocks.{b}."
+            sh.update({p + "in_ln.weight": (C,), p + "in_ln.bias": (C,), p + "mlp.0.weight": (C, C),
+                       p + "mlp.0.bias": (C,), p + "mlp.2.weight": (C, C), p + "mlp.2.bias": (C,),
+                       p + "adaLN_modulation.1.weight": (3 * C, C), p + "adaLN_modulation.1.bias": (3 * C,)})
+        return sh
+
+
+PHONON_FLOW = FlowConfig()
+
+
+def random_flow_weights(cfg: FlowConfig, seed: int, *, bf16_exact: bool = False,
+                        condition: bool = False) -> dict:
+    """Random-init flow-head tensors under the checkpoint's names: Linear weights and biases
+    U(-1/sqrt(in), 1/sqrt(in)) (torch's default init), LayerNorm gains near 1, time-embedder
+    frequencies exp(-ln(10^4) j / (F/2)) and alphas near 1. bf16_exact rounds the large linears'
+    weights to bf16 (the form the reference's CUDA backend holds them in)."""
+    rng = np.random.default_rng(seed)
+    out = {}
+    for name, shape in cfg.shapes().items():
+        if name.endswith(".freqs"):
+            half = shape[0]
+            v = np.exp(-np.log(10000.0) * np.arange(half) / half)
+        elif name.endswith("alpha") or name.endswith("in_ln.weight") or name == "out_norm.weight":
+            v = rng.uniform(0.8, 1.2, shape)
+        elif name.endswith("in_ln.bias") or name == "out_norm.bias":
+            v = rng.normal(0.0, 0.05, shape)
+        elif name == "bos_emb":
+            v = rng.normal(0.0, 1.0, shape)
+        else:
+            fan_in = shape[1] if len(shape) == 2 else cfg.shapes()[name[:-len("bias")] + "weight"][1]
+            bound = 1.0 / np.sqrt(fan_in)
+            v = rng.uniform(-bound, bound, shape)
+        v = v.astype(np.float32)
+        if bf16_exact and len(shape) == 2 and shape[0] >= 128 and shape[1] >= 128:
+            v = round_bf16_np(v)
+        out[name] = v
+    if condition:
+        out["condition"] = rng.normal(0.0, 0.5, (cfg.d_model,)).astype(np.float32)
+    return out
+
+
+def round_bf16_np(x: np.ndarray) -> np.ndarray:
+    """f32 -> nearest-even bf16 -> f32 (finite values)."""
+    u = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32).astype(np.uint64)
+    u = (u + 0x7FFF + ((u >> 16) & 1)) & 0xFFFF0000
+    return u.astype(np.uint32).view(np.float32)
+
+
+class Flow:
+    """The flow head on one device: ptts_b200_flow_* and ptts_b200_frame."""
+
+    def __init__(self, cfg: FlowConfig, device: int = 0):
+        self.cfg, self.device = cfg, device
+        h = P()
+        st = cfg.c_struct()
+        _check(lib().ptts_b200_flow_create(device, ctypes.byref(st), ctypes.byref(h)))
+        self._h = h
+
+    def close(self):
+        if getattr(self, "_h", None):
+            lib().ptts_b200_flow_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def set(self, name: str, value: np.ndarray):
+        a = np.ascontiguousarray(value, dtype=np.float32)
+        _check(lib().ptts_b200_flow_set_tensor(self._h, name.encode(), a.ctypes.data_as(P), a.size))
+
+    def load(self, tensors: dict):
+        for k, v in tensors.items():
+            self.set(k, v)
+        _check(lib().ptts_b200_flow_finish(self._h))
+
+    def sample(self, t_out, noise, *, stream=None):
+        """FlowLM::sample_from_noise: t_out [n, d] f32, noise [n, ldim] f32 (CUDA) -> (latent, eos)."""
+        import torch
+        n = t_out.shape[0]
+        latent = torch.empty((n, self.cfg.ldim), dtype=torch.float32, device=t_out.device)
+        eos = torch.empty((n,), dtype=torch.float32, device=t_out.device)
+        _check(lib().ptts_b200_flow_sample(self._h, _dptr(t_out), n, _dptr(noise), _dptr(latent),
+                                           _dptr(eos), _stream(stream)))
+        return latent, eos
+
+    def frame(self, model: Transformer, kv: KvState, streams: Sequence[int], latent, noise, *,
+              stream=None):
+        """One frame: latent [n, ldim] f32 (None: bos_emb) and noise [n, ldim] f32 on the device
+        -> (next latent, eos logits). Lengths advance by one."""
+        import torch
+        s = _i32(streams)
+        n = len(s)
+        out = torch.empty((n, self.cfg.ldim), dtype=torch.float32, device=noise.device)
+        eos = torch.empty((n,), dtype=torch.float32, device=noise.device)
+        lat = _dptr(latent) if latent is not None else P()
+        _check(lib().ptts_b200_frame(model._h, self._h, kv.handle, _ip(s), n, lat, _dptr(noise),
+                                     _dptr(out), _dptr(eos), _stream(stream)))
+        return out, eos

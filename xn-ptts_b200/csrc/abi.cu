@@ -11,125 +11,14 @@
 #include <string>
 #include <vector>
 
+#include "host.h"
 #include "kernels.h"
 #include "ptts_b200.h"
 
 namespace {
 
 using namespace ptts;
-
-thread_local std::string g_last_error;
-
-struct Error {
-    int code;
-    std::string msg;
-};
-
-[[noreturn]] void fail(int code, const std::string& msg) { throw Error{code, msg}; }
-
-#define CK(call)                                                                             \
-    do {                                                                                     \
-        cudaError_t e_ = (call);                                                             \
-        if (e_ != cudaSuccess) fail(PTTS_B200_ERR_CUDA, std::string(#call) + ": " + cudaGetErrorString(e_)); \
-    } while (0)
-
-template <class F>
-int guarded(F&& f) {
-    try {
-        f();
-        return PTTS_B200_OK;
-    } catch (const Error& e) {
-        g_last_error = e.msg;
-        return e.code;
-    } catch (const std::exception& e) {
-        g_last_error = std::string("internal error: ") + e.what();
-        return PTTS_B200_ERR_STATE;
-    } catch (...) {
-        g_last_error = "internal error: unknown exception";
-        return PTTS_B200_ERR_STATE;
-    }
-}
-
-void require(bool ok, int code, const std::string& msg) {
-    if (!ok) fail(code, msg);
-}
-
-struct DeviceScope {
-    int prev = -1;
-    explicit DeviceScope(int dev) {
-        CK(cudaGetDevice(&prev));
-        if (prev != dev) CK(cudaSetDevice(dev));
-    }
-    ~DeviceScope() {
-        if (prev >= 0) cudaSetDevice(prev);
-    }
-};
-
-// Grow-only device buffer.
-struct DevBuf {
-    void* p = nullptr;
-    size_t bytes = 0;
-    DevBuf() = default;
-    DevBuf(const DevBuf&) = delete;
-    DevBuf& operator=(const DevBuf&) = delete;
-    ~DevBuf() {
-        if (p) cudaFree(p);
-    }
-    void* need(size_t n) {
-        if (n <= bytes) return p;
-        if (p) {
-            CK(cudaDeviceSynchronize());
-            CK(cudaFree(p));
-            p = nullptr;
-            bytes = 0;
-        }
-        CK(cudaMalloc(&p, n));
-        bytes = n;
-        return p;
-    }
-    template <class T>
-    T* as() const {
-        return static_cast<T*>(p);
-    }
-    // Like need(), and zero-filled whenever it is (re)allocated.
-    void* need_zeroed(size_t n) {
-        if (n <= bytes) return p;
-        need(n);
-        CK(cudaMemset(p, 0, n));
-        return p;
-    }
-};
-
-// Pinned staging for small host -> device uploads: a ring of slots, each reused only after its
-// previous copy has completed, so a call does not wait for the device's earlier work.
-struct Staging {
-    static constexpr int kSlots = 16;
-    void* host[kSlots] = {};
-    size_t bytes[kSlots] = {};
-    cudaEvent_t done[kSlots] = {};
-    int next = 0;
-    ~Staging() {
-        for (int i = 0; i < kSlots; ++i) {
-            if (host[i]) cudaFreeHost(host[i]);
-            if (done[i]) cudaEventDestroy(done[i]);
-        }
-    }
-    void upload(void* dev, const void* src, size_t n, cudaStream_t s) {
-        const int i = next;
-        next = (next + 1) % kSlots;
-        if (!done[i]) CK(cudaEventCreateWithFlags(&done[i], cudaEventDisableTiming));
-        CK(cudaEventSynchronize(done[i]));
-        if (n > bytes[i]) {
-            if (host[i]) CK(cudaFreeHost(host[i]));
-            host[i] = nullptr;
-            CK(cudaMallocHost(&host[i], n < 4096 ? 4096 : n));
-            bytes[i] = n < 4096 ? 4096 : n;
-        }
-        std::memcpy(host[i], src, n);
-        CK(cudaMemcpyAsync(dev, host[i], n, cudaMemcpyHostToDevice, s));
-        CK(cudaEventRecord(done[i], s));
-    }
-};
+using namespace ptts::host;
 
 // Per-call activations of the layer stack (device, sized for `rows` rows).
 struct Workspace {

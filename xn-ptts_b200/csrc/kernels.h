@@ -143,7 +143,12 @@ void launch_prefill_attn_tc(const PrefillArgs& a, const int2* tiles, int n_tiles
 
 // ---- int8 linear (linear.cu) ----------------------------------------------------------
 
-enum LinearEpi : int { EPI_F32 = 0, EPI_QKV = 1, EPI_RESID = 2, EPI_GELU = 3, EPI_PARTIAL = 4 };
+enum LinearEpi : int {
+    EPI_F32 = 0, EPI_QKV = 1, EPI_RESID = 2, EPI_GELU = 3, EPI_PARTIAL = 4,
+    // Flow net (bf16 planes, tcgen05 kernel only): y = W x + b; bf16 hi/lo of silu(W x + b + aux[n]);
+    // bf16 hi/lo of silu(W x + b); y += aux[m * aux_stride + n] * (W x + b).
+    EPI_BIAS = 5, EPI_COND = 6, EPI_BIAS_SILU = 7, EPI_GATE_RESID = 8
+};
 
 struct LinearArgs {
     int M, N, K;
@@ -152,8 +157,13 @@ struct LinearArgs {
     const void* a_lo;         // A lo plane [M][K], or nullptr (A exact in one plane)
     int a_f16 = 1;            // 1: f16 planes (the layer stack); 0: one bf16 plane
     const int8_t* w;          // [N][K]
-    const __half* wh = nullptr;  // the same weights as f16 [N][K] (exact), for the tcgen05 kernel
-    const float* scale;       // [N]
+    const void* wh = nullptr;    // 16-bit weights [N][K] for the tcgen05 kernel: the int8 ones as
+                                 // f16 (exact), or the flow net's bf16 hi plane
+    const void* wh_lo = nullptr; // flow net: bf16 lo plane of the weights, or nullptr
+    const float* scale;       // [N], or nullptr (1) for the flow net
+    const float* bias = nullptr;  // flow epilogues: [N] or nullptr
+    const float* aux = nullptr;   // EPI_COND: time embedding [N]; EPI_GATE_RESID: gates
+    int aux_stride = 0;           // EPI_GATE_RESID: row stride of aux
     float* y;                 // EPI_F32 / EPI_RESID: [M][N]; EPI_PARTIAL: [splits][M][N]
     void* yb;                 // EPI_GELU: f16 hi plane [M][N]
     void* yb_lo;              // EPI_GELU: f16 lo plane [M][N]
@@ -178,6 +188,67 @@ void launch_linear(const LinearArgs& a, LinearEpi epi, cudaStream_t s);
 void launch_linear_mma(const LinearArgs& a, LinearEpi epi, cudaStream_t s);
 bool linear_tc_supported(const LinearArgs& a);
 bool launch_linear_tc(const LinearArgs& a, LinearEpi epi, cudaStream_t s);  // false: not launched
+
+// ---- flow head (flow.cu) ----------------------------------------------------------------
+// y = a W^T + bias + add for K <= 64: a [M][K] (or every row a_row [K]), W [N][K] f32; output
+// f32 y or bf16 yb.
+struct FlowSmallArgs {
+    int M, N, K;
+    const float* a;
+    const float* a_row;
+    const float* w;
+    const float* bias;
+    const float* add;
+    float* y;
+    __nv_bfloat16* yb;
+};
+void launch_flow_small(const FlowSmallArgs& a, cudaStream_t s);
+
+// Rows x [M][d] (LayerNorm with gamma/beta/eps first when gamma != nullptr) -> bf16 hi/lo planes
+// and eos[m] = row . eos_w + eos_b. d in {128, 256, 512, 1024}.
+struct FlowNormArgs {
+    int M, d;
+    const float* x;
+    const float* gamma;
+    const float* beta;
+    float eps;
+    const float* eos_w;
+    float eos_b;
+    float* eos;
+    __nv_bfloat16* hi;
+    __nv_bfloat16* lo;
+};
+void launch_flow_norm_eos(const FlowNormArgs& a, cudaStream_t s);
+
+// LayerNorm(x) (eps; affine when gamma != nullptr) * (1 + scale) + shift, shift and scale rows
+// at shift + m * stride, scale + m * stride; out f32 y, or bf16 hi/lo. C in {128, ..., 1024}.
+struct FlowModArgs {
+    int M, C;
+    const float* x;
+    const float* gamma;
+    const float* beta;
+    float eps;
+    const float* shift;
+    const float* scale;
+    int stride;
+    float* y;
+    __nv_bfloat16* hi;
+    __nv_bfloat16* lo;
+};
+void launch_flow_ln_mod(const FlowModArgs& a, cudaStream_t s);
+
+// out[m][j] = cur[m][j] + step_scale * (h[m] . w[j] + bias[j]) (or the bare product when cur is
+// nullptr); h [M][C], w [L][C], L <= 64, C * L * 4 <= 200 KB.
+struct FlowOutArgs {
+    int M, C, L;
+    const float* h;
+    const float* w;
+    const float* bias;
+    const float* cur;
+    float step_scale;
+    float* out;
+};
+void launch_flow_out(const FlowOutArgs& a, cudaStream_t s);
 
 // RoPE table: out[pos][i] = (cos, sin)(f32(pos) * inv_freq[i]) for pos < rows, i < kMaxPairs.
 struct RopeFreqs {

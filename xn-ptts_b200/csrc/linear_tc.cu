@@ -17,7 +17,8 @@
 //               the grid that wrote X (weights never change).
 //   thread 32:  MMA issuer; tcgen05.commit frees each stage and finally signals `done`.
 //   all warps:  epilogue: warp w reads TMEM lanes 32w..32w+31 (features n0 + 32w + lane), 32
-//               rows per tcgen05.ld, and stores each row's 32 features as one coalesced run.
+//               rows per tcgen05.ld, into a shared-memory tile; then each warp takes whole rows,
+//               lane l the features 4l..4l+3, so stores are 16 bytes and RoPE pairs in-lane.
 // Every wait is bounded (DEV_ERR_TIMEOUT); after a timeout the CTA still waits, bounded, for the
 // copies it issued and frees its TMEM. No clusters, no multicast.
 #include <cuda.h>
@@ -36,12 +37,14 @@ constexpr int FT = 128;  // output features per CTA (MMA M)
 constexpr int KS = 64;   // k per stage: one 128-byte swizzle row of f16
 constexpr int kThreadsTma = 128;
 
-template <int RT>
+// WLO: the weights come as two planes too (hi, lo), and each k step runs a third MMA.
+template <int RT, bool WLO>
 struct TmaTile {
-    static constexpr int kStages = 4;
-    static constexpr int kWBytes = FT * KS * 2;  // 16 KB
-    static constexpr int kXBytes = RT * KS * 2;  // per plane
-    static constexpr int kStageBytes = kWBytes + 2 * kXBytes;
+    static constexpr int kStages = WLO ? 3 : 4;
+    static constexpr int kWBytes = FT * KS * 2;  // 16 KB per weight plane
+    static constexpr int kXBytes = RT * KS * 2;  // per activation plane
+    static constexpr int kStageBytes = (WLO ? 2 : 1) * kWBytes + 2 * kXBytes;
+    static constexpr int kXOffset = (WLO ? 2 : 1) * kWBytes;  // X hi, then X lo
     static constexpr int kBarOffset = kStages * kStageBytes;
     static constexpr int kSmem = 1024 + kBarOffset + 256;  // + alignment slack + barriers
     static constexpr uint32_t kTmemCols = RT < 32 ? 32 : RT;
@@ -50,12 +53,18 @@ struct TmaTile {
     static_assert(32 * (FT + 4) * 4 <= kBarOffset, "the QKV staging tile fits in the ring");
 };
 
-// Instruction descriptor, kind::f16: D f32 (bits 4-5 = 1), A and B f16 (formats 0), both
-// K-major, N >> 3 at bit 17, M >> 4 at bit 24.
+// Instruction descriptor, kind::f16: D f32 (bits 4-5 = 1), A and B both f16 (formats 0) or both
+// bf16 (format 1 at bits 7-9 and 10-12), both K-major, N >> 3 at bit 17, M >> 4 at bit 24.
 template <int RT>
 constexpr uint32_t idesc_f16() {
     return (1u << 4) | ((uint32_t)(RT >> 3) << 17) | ((uint32_t)(FT >> 4) << 24);
 }
+template <int RT>
+constexpr uint32_t idesc_bf16() {
+    return idesc_f16<RT>() | (1u << 7) | (1u << 10);
+}
+
+__device__ __forceinline__ float silu(float x) { return x / (1.0f + expf(-x)); }
 
 // Shared-memory matrix descriptor of a K-major, 128-byte-swizzled tile at `addr` (1024-aligned):
 // start >> 4 in bits 0-13, leading byte offset 1 (unused when swizzled), stride byte offset
@@ -140,33 +149,6 @@ __device__ __forceinline__ __half f16_sat(float x) {
     return __float2half_rn(fminf(fmaxf(x, -65504.f), 65504.f));
 }
 
-// Epilogue of 32 rows (mbase .. mbase+31) of this thread's feature f; v[j] is row mbase + j.
-// Arithmetic as linear.cu's epilogue_pair (scale, then the epilogue's own operation).
-// EPI_QKV goes through qkv_rows instead.
-template <int EPI>
-__device__ __forceinline__ void epi_rows(const LinearArgs& p, int f, int mbase, int z, const float (&v)[32]) {
-    const float sc = __ldg(p.scale + f);
-#pragma unroll
-    for (int j = 0; j < 32; ++j) {
-        const int m = mbase + j;
-        if (m >= p.M) break;
-        const float x = v[j] * sc;
-        const long long at = (long long)m * p.N + f;
-        if (EPI == EPI_F32) {
-            p.y[at] = x;
-        } else if (EPI == EPI_PARTIAL) {
-            p.y[(long long)z * p.M * p.N + at] = x;
-        } else if (EPI == EPI_RESID) {
-            p.y[at] += x;
-        } else {  // EPI_GELU: f16 hi/lo planes
-            float hi, lo;
-            split_f16(gelu_tc(x, p.gelu_tanh), hi, lo);
-            static_cast<__half*>(p.yb)[at] = __float2half_rn(hi);
-            static_cast<__half*>(p.yb_lo)[at] = f16_sat(lo);
-        }
-    }
-}
-
 // Staged tile row stride in floats: 128 features + 4 (keeps float4 alignment, spreads banks).
 constexpr int kStageStride = FT + 4;
 
@@ -227,12 +209,78 @@ __device__ __forceinline__ void qkv_rows(const LinearArgs& p, const float* st, i
     }
 }
 
-template <int EPI, int RT>
+// The other epilogues on the same staged layout (warp w rows w + 4i, lane l features
+// n0 + 4l .. 4l + 3), with linear.cu's epilogue_pair arithmetic. EPI_RESID reads all its old
+// values before its first store.
+template <int EPI>
+__device__ __forceinline__ void plain_rows(const LinearArgs& p, const float* st, int n0, int mbase, int z) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int f = n0 + 4 * lane;
+    const float4 sc = p.scale ? __ldg(reinterpret_cast<const float4*>(p.scale + f)) : make_float4(1.f, 1.f, 1.f, 1.f);
+    float4 bias = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (EPI >= EPI_BIAS && p.bias) bias = __ldg(reinterpret_cast<const float4*>(p.bias + f));
+    if (EPI == EPI_COND) {  // the step's time embedding joins the bias
+        const float4 t = __ldg(reinterpret_cast<const float4*>(p.aux + f));
+        bias = make_float4(bias.x + t.x, bias.y + t.y, bias.z + t.z, bias.w + t.w);
+    }
+    float4 old[8], gate[8];
+    if (EPI == EPI_RESID || EPI == EPI_GATE_RESID) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int m = mbase + warp + 4 * i;
+            const bool live = m < p.M;
+            old[i] = live ? *reinterpret_cast<const float4*>(p.y + (long long)m * p.N + f) : make_float4(0.f, 0.f, 0.f, 0.f);
+            if (EPI == EPI_GATE_RESID)
+                gate[i] = live ? *reinterpret_cast<const float4*>(p.aux + (long long)m * p.aux_stride + f)
+                               : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const int j = warp + 4 * i, m = mbase + j;
+        if (m >= p.M) break;
+        const float4 a = *reinterpret_cast<const float4*>(st + j * kStageStride + 4 * lane);
+        const float x0 = a.x * sc.x, x1 = a.y * sc.y, x2 = a.z * sc.z, x3 = a.w * sc.w;
+        const long long at = (long long)m * p.N + f;
+        if (EPI == EPI_F32) {
+            *reinterpret_cast<float4*>(p.y + at) = make_float4(x0, x1, x2, x3);
+        } else if (EPI == EPI_PARTIAL) {
+            *reinterpret_cast<float4*>(p.y + (long long)z * p.M * p.N + at) = make_float4(x0, x1, x2, x3);
+        } else if (EPI == EPI_RESID) {
+            *reinterpret_cast<float4*>(p.y + at) =
+                make_float4(old[i].x + x0, old[i].y + x1, old[i].z + x2, old[i].w + x3);
+        } else if (EPI == EPI_BIAS) {
+            *reinterpret_cast<float4*>(p.y + at) = make_float4(x0 + bias.x, x1 + bias.y, x2 + bias.z, x3 + bias.w);
+        } else if (EPI == EPI_GATE_RESID) {  // x += gate * (W h + b)
+            *reinterpret_cast<float4*>(p.y + at) =
+                make_float4(old[i].x + gate[i].x * (x0 + bias.x), old[i].y + gate[i].y * (x1 + bias.y),
+                            old[i].z + gate[i].z * (x2 + bias.z), old[i].w + gate[i].w * (x3 + bias.w));
+        } else if (EPI == EPI_COND || EPI == EPI_BIAS_SILU) {  // bf16 hi/lo of silu(W x + b [+ t])
+            uint2 hi, lo;
+            const float y0 = silu(x0 + bias.x), y1 = silu(x1 + bias.y), y2 = silu(x2 + bias.z), y3 = silu(x3 + bias.w);
+            hi.x = pack_bf16x2(y0, y1);
+            hi.y = pack_bf16x2(y2, y3);
+            lo.x = pack_bf16x2(y0 - bf16lo(hi.x), y1 - bf16hi(hi.x));
+            lo.y = pack_bf16x2(y2 - bf16lo(hi.y), y3 - bf16hi(hi.y));
+            *reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(p.yb) + at) = hi;
+            *reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(p.yb_lo) + at) = lo;
+        } else {  // EPI_GELU: f16 hi/lo planes
+            uint2 hi, lo;
+            split_f16x2(gelu_tc(x0, p.gelu_tanh), gelu_tc(x1, p.gelu_tanh), hi.x, lo.x);
+            split_f16x2(gelu_tc(x2, p.gelu_tanh), gelu_tc(x3, p.gelu_tanh), hi.y, lo.y);
+            *reinterpret_cast<uint2*>(static_cast<__half*>(p.yb) + at) = hi;
+            *reinterpret_cast<uint2*>(static_cast<__half*>(p.yb_lo) + at) = lo;
+        }
+    }
+}
+
+template <int EPI, int RT, bool WLO>
 __global__ void __launch_bounds__(kThreadsTma) linear_tma_kernel(const __grid_constant__ LinearArgs p,
                                                                  const __grid_constant__ CUtensorMap tm_w,
+                                                                 const __grid_constant__ CUtensorMap tm_wlo,
                                                                  const __grid_constant__ CUtensorMap tm_x,
                                                                  const __grid_constant__ CUtensorMap tm_xlo) {
-    using T = TmaTile<RT>;
+    using T = TmaTile<RT, WLO>;
     constexpr int S = T::kStages;
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
@@ -250,7 +298,7 @@ __global__ void __launch_bounds__(kThreadsTma) linear_tma_kernel(const __grid_co
     const int k0 = z * k_len;
     const int KT = k_len / KS;
     const bool has_lo = p.a_lo != nullptr;
-    const uint32_t stage_tx = T::kWBytes + (has_lo ? 2u : 1u) * T::kXBytes;
+    const uint32_t stage_tx = (WLO ? 2u : 1u) * T::kWBytes + (has_lo ? 2u : 1u) * T::kXBytes;
 
     if (tid == 0) {
         s_issued = 0;
@@ -283,6 +331,7 @@ __global__ void __launch_bounds__(kThreadsTma) linear_tma_kernel(const __grid_co
         for (int kt = 0; kt < pre; ++kt) {
             mbar_arrive_expect_tx(&full[kt], stage_tx);
             tma_load_2d_hint(base + kt * T::kStageBytes, &tm_w, k0 + kt * KS, n0, &full[kt], pol_w);
+            if (WLO) tma_load_2d_hint(base + kt * T::kStageBytes + T::kWBytes, &tm_wlo, k0 + kt * KS, n0, &full[kt], pol_w);
         }
         grid_dep_wait();
         grid_dep_launch();
@@ -296,9 +345,10 @@ __global__ void __launch_bounds__(kThreadsTma) linear_tma_kernel(const __grid_co
                 }
                 mbar_arrive_expect_tx(&full[st], stage_tx);
                 tma_load_2d_hint(sa, &tm_w, k0 + kt * KS, n0, &full[st], pol_w);
+                if (WLO) tma_load_2d_hint(sa + T::kWBytes, &tm_wlo, k0 + kt * KS, n0, &full[st], pol_w);
             }
-            tma_load_2d(sa + T::kWBytes, &tm_x, k0 + kt * KS, m0, &full[st]);
-            if (has_lo) tma_load_2d(sa + T::kWBytes + T::kXBytes, &tm_xlo, k0 + kt * KS, m0, &full[st]);
+            tma_load_2d(sa + T::kXOffset, &tm_x, k0 + kt * KS, m0, &full[st]);
+            if (has_lo) tma_load_2d(sa + T::kXOffset + T::kXBytes, &tm_xlo, k0 + kt * KS, m0, &full[st]);
             s_issued = kt + 1;
         }
     } else {
@@ -306,7 +356,7 @@ __global__ void __launch_bounds__(kThreadsTma) linear_tma_kernel(const __grid_co
         grid_dep_launch();
         if (tid == 32) {
             // ---- MMA issuer --------------------------------------------------------------------
-            constexpr uint32_t idesc = idesc_f16<RT>();
+            const uint32_t idesc = p.a_f16 ? idesc_f16<RT>() : idesc_bf16<RT>();
             for (int kt = 0; kt < KT; ++kt) {
                 const int st = kt % S;
                 if (!mbar_wait(&full[st], (kt / S) & 1)) {
@@ -315,12 +365,13 @@ __global__ void __launch_bounds__(kThreadsTma) linear_tma_kernel(const __grid_co
                 }
                 tc_fence_after();
                 const uint32_t sa = base + st * T::kStageBytes;
-                const uint64_t dw = sw128_desc(sa), dx = sw128_desc(sa + T::kWBytes);
-                const uint64_t dxl = sw128_desc(sa + T::kWBytes + T::kXBytes);
+                const uint64_t dw = sw128_desc(sa), dwl = sw128_desc(sa + T::kWBytes);
+                const uint64_t dx = sw128_desc(sa + T::kXOffset), dxl = sw128_desc(sa + T::kXOffset + T::kXBytes);
 #pragma unroll
                 for (int kk = 0; kk < KS / 16; ++kk) {  // 32 bytes of K per MMA
                     tc_mma(tmem, dw + 2 * kk, dx + 2 * kk, idesc, (kt | kk) ? 1u : 0u);
                     if (has_lo) tc_mma(tmem, dw + 2 * kk, dxl + 2 * kk, idesc, 1u);
+                    if (WLO) tc_mma(tmem, dwl + 2 * kk, dx + 2 * kk, idesc, 1u);
                 }
                 tc_commit(&empty[st]);
                 s_consumed = kt + 1;
@@ -335,21 +386,20 @@ __global__ void __launch_bounds__(kThreadsTma) linear_tma_kernel(const __grid_co
     if (!got) set_error(p.err, DEV_ERR_TIMEOUT);
     __syncwarp();  // tcgen05.ld below is warp-collective
     tc_fence_after();
-    const int f = n0 + 32 * warp + lane;
 #pragma unroll 1
     for (int c = 0; c < RT; c += 32) {
         float v[32];
         tmem_ld32(tmem + ((uint32_t)(32 * warp) << 16) + (uint32_t)c, v);
-        if (EPI == EPI_QKV) {
-            // Transpose through shared memory (the drained ring): lanes then own feature quads.
-            float* st = reinterpret_cast<float*>(smem);
-            __syncthreads();  // the previous chunk's readers are done
+        // Transpose through shared memory (the drained ring): lanes then own feature quads and
+        // store 16 bytes per row.
+        float* st = reinterpret_cast<float*>(smem);
+        __syncthreads();  // the previous chunk's readers are done
 #pragma unroll
-            for (int j = 0; j < 32; ++j) st[j * kStageStride + 32 * warp + lane] = v[j];
-            __syncthreads();
-            if (got) qkv_rows(p, st, n0, m0 + c);
-        } else if (got) {
-            epi_rows<EPI>(p, f, m0 + c, z, v);
+        for (int j = 0; j < 32; ++j) st[j * kStageStride + 32 * warp + lane] = v[j];
+        __syncthreads();
+        if (got) {
+            if (EPI == EPI_QKV) qkv_rows(p, st, n0, m0 + c);
+            else plain_rows<EPI>(p, st, n0, m0 + c, z);
         }
     }
 
@@ -387,14 +437,14 @@ EncodeTiled encoder() {
     return fn;
 }
 
-// Tensor map of a row-major [rows][cols] f16 matrix, box 64 (k) x box_rows, 128-byte swizzle,
-// zero fill past the last row. A map is a pure function of its key, so cached maps never go
-// stale; the cache is cleared when it grows large (prompt lengths vary).
-bool f16_map(CUtensorMap* out, const void* ptr, int rows, int cols, int box_rows) {
-    using Key = std::tuple<const void*, int, int, int>;
+// Tensor map of a row-major [rows][cols] f16 (or bf16) matrix, box 64 (k) x box_rows, 128-byte
+// swizzle, zero fill past the last row. A map is a pure function of its key, so cached maps never
+// go stale; the cache is cleared when it grows large (prompt lengths vary).
+bool f16_map(CUtensorMap* out, const void* ptr, int rows, int cols, int box_rows, bool bf16 = false) {
+    using Key = std::tuple<const void*, int, int, int, bool>;
     static std::mutex mu;
     static std::map<Key, CUtensorMap> cache;
-    const Key key{ptr, rows, cols, box_rows};
+    const Key key{ptr, rows, cols, box_rows, bf16};
     std::lock_guard<std::mutex> lock(mu);
     auto it = cache.find(key);
     if (it != cache.end()) {
@@ -408,7 +458,8 @@ bool f16_map(CUtensorMap* out, const void* ptr, int rows, int cols, int box_rows
     const cuuint32_t box[2] = {(cuuint32_t)KS, (cuuint32_t)box_rows};
     const cuuint32_t elem[2] = {1, 1};
     CUtensorMap m;
-    if (enc(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, elem,
+    if (enc(&m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+            const_cast<void*>(ptr), dims, strides, box, elem,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
         return false;
@@ -418,13 +469,19 @@ bool f16_map(CUtensorMap* out, const void* ptr, int rows, int cols, int box_rows
     return true;
 }
 
-template <int EPI, int RT>
+template <int EPI, int RT, bool WLO>
 bool launch_tma(const LinearArgs& a, cudaStream_t s) {
-    using T = TmaTile<RT>;
-    CUtensorMap mw, mx, mxl;
-    if (!f16_map(&mw, a.wh, a.N, a.K, FT) || !f16_map(&mx, a.a, a.M, a.K, RT)) return false;
+    using T = TmaTile<RT, WLO>;
+    const bool bf = !a.a_f16;
+    CUtensorMap mw, mwl, mx, mxl;
+    if (!f16_map(&mw, a.wh, a.N, a.K, FT, bf) || !f16_map(&mx, a.a, a.M, a.K, RT, bf)) return false;
+    if (WLO) {
+        if (!f16_map(&mwl, a.wh_lo, a.N, a.K, FT, bf)) return false;
+    } else {
+        mwl = mw;
+    }
     if (a.a_lo) {
-        if (!f16_map(&mxl, a.a_lo, a.M, a.K, RT)) return false;
+        if (!f16_map(&mxl, a.a_lo, a.M, a.K, RT, bf)) return false;
     } else {
         mxl = mx;
     }
@@ -432,34 +489,46 @@ bool launch_tma(const LinearArgs& a, cudaStream_t s) {
     int dev = 0;
     cudaGetDevice(&dev);
     if (configured != dev) {
-        cudaFuncSetAttribute(linear_tma_kernel<EPI, RT>, cudaFuncAttributeMaxDynamicSharedMemorySize, T::kSmem);
+        cudaFuncSetAttribute(linear_tma_kernel<EPI, RT, WLO>, cudaFuncAttributeMaxDynamicSharedMemorySize, T::kSmem);
         configured = dev;
     }
     dim3 grid(a.N / FT, (a.M + RT - 1) / RT, a.splits);
-    launch_k(linear_tma_kernel<EPI, RT>, grid, dim3(kThreadsTma), T::kSmem, s, a, mw, mx, mxl);
+    launch_k(linear_tma_kernel<EPI, RT, WLO>, grid, dim3(kThreadsTma), T::kSmem, s, a, mw, mwl, mx, mxl);
     return true;
 }
 
 template <int EPI>
 bool launch_tma_rows(const LinearArgs& a, cudaStream_t s) {
-    return a.M < 4096 ? launch_tma<EPI, 32>(a, s) : launch_tma<EPI, 128>(a, s);
+    return a.M < 4096 ? launch_tma<EPI, 32, false>(a, s) : launch_tma<EPI, 128, false>(a, s);
+}
+
+// The flow net's linears (bf16 planes, optional weight lo plane), decode-size rows only.
+template <int EPI>
+bool launch_tma_flow(const LinearArgs& a, cudaStream_t s) {
+    return a.wh_lo ? launch_tma<EPI, 32, true>(a, s) : launch_tma<EPI, 32, false>(a, s);
 }
 
 }  // namespace
 
 bool linear_tc_supported(const LinearArgs& a) {
-    return a.wh != nullptr && a.a_f16 && a.M > 0 && a.N % FT == 0 && a.K % 8 == 0 && a.splits >= 1 &&
+    return a.wh != nullptr && a.M > 0 && a.N % FT == 0 && a.K % 8 == 0 && a.splits >= 1 &&
            a.K % a.splits == 0 && (a.K / a.splits) % KS == 0;
 }
 
 bool launch_linear_tc(const LinearArgs& a, LinearEpi epi, cudaStream_t s) {
     if (!linear_tc_supported(a)) return false;
+    const bool flow_epi = epi >= EPI_BIAS;
+    if (!flow_epi && (!a.a_f16 || a.wh_lo)) return false;  // the layer stack's linears: f16, one weight plane
     switch (epi) {
         case EPI_F32: return launch_tma_rows<EPI_F32>(a, s);
         case EPI_QKV: return launch_tma_rows<EPI_QKV>(a, s);
         case EPI_RESID: return launch_tma_rows<EPI_RESID>(a, s);
         case EPI_GELU: return launch_tma_rows<EPI_GELU>(a, s);
         case EPI_PARTIAL: return launch_tma_rows<EPI_PARTIAL>(a, s);
+        case EPI_BIAS: return launch_tma_flow<EPI_BIAS>(a, s);
+        case EPI_COND: return launch_tma_flow<EPI_COND>(a, s);
+        case EPI_BIAS_SILU: return launch_tma_flow<EPI_BIAS_SILU>(a, s);
+        case EPI_GATE_RESID: return launch_tma_flow<EPI_GATE_RESID>(a, s);
     }
     return false;
 }
