@@ -384,6 +384,43 @@ def run_ours(args):
     if traffic:
         roofline["traffic_source"] = "scaled from profiles/decode_attn_traffic.json: " + traffic.get("source", "")
 
+    # ---- whole frames: input_linear -> step -> out_norm -> EOS + flow net (ptts_b200_frame) ----
+    # An extra line item (the headline value above is the backbone step the configs define):
+    # each frame feeds its latent back as the next input, as FlowLM's sampler does.
+    flow_frame = None
+    if args.workload == "config5" and not args.no_flow:
+        fcfg = ptts.PHONON_FLOW
+        flow = ptts.Flow(fcfg, device=local)
+        flow.load(ptts.random_flow_weights(fcfg, seed, bf16_exact=True))
+        noise = torch.randn(FRAMES, B, fcfg.ldim, generator=g, device=dev)
+        fstate = {"f": 0, "lat": None}
+
+        def frame():
+            f = fstate["f"]
+            if f and f % FRAMES == 0:
+                kv.set_lengths(streams, prefixes)
+            fstate["lat"], _ = flow.frame(model, kv, streams, fstate["lat"], noise[f % FRAMES])
+            fstate["f"] = f + 1
+
+        kv.set_lengths(streams, prefixes)
+        for _ in range(args.warmup):
+            frame()
+        k = min(args.steps, FRAMES)
+        barrier(dist, local)
+        torch.cuda.synchronize()
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0.record(stream)
+        for _ in range(k):
+            frame()
+        f1.record(stream)
+        f1.synchronize()
+        fms = max_over_ranks(dist, f0.elapsed_time(f1), dev)
+        flow_frame = {"value": world * B * k / (fms / 1e3), "unit": "frames/s", "frames": k,
+                      "ms_per_frame": fms / k, "ms_head_per_frame": fms / k - ms / args.steps,
+                      "head": "flow_dim 512, depth 6, ldim 32, LSD 1 step (phonon shape), bf16 weights, "
+                              "latent fed back each frame"}
+        flow.close()
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline and args.workload == "config5" and not args.layers:
         cb = cpu_baseline(ptts, wl, cfg, weights)
@@ -401,7 +438,7 @@ def run_ours(args):
                        "l2": f"inputs larger than L2: {per_launch_bytes * L / 1e9:.2f} GB of KV read per step per GPU"
                              if per_launch_bytes * L > 126e6 else "KV per step fits in L2 (no flush)"},
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": gpu_launches,
-            "clocks": clocks, "prefill_ms": prefill_ms,
+            "clocks": clocks, "prefill_ms": prefill_ms, "frame_with_flow_head": flow_frame,
             "prefill_rows_per_s": world * float(prefixes.sum()) / (prefill_ms / 1e3),
         }
         print(json.dumps(line), flush=True)
@@ -550,6 +587,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-flow", action="store_true",
+                    help="skip the extra line item: whole frames with the flow head (ptts_b200_frame)")
     ap.add_argument("--workload", choices=["config5", "config4", "config3", "config2"], default="config5",
                     help="config5: the flow-LM frame, 512 streams/GPU (default); config4: 31m, "
                          "64 streams, prefix 128; config3: the attention op alone")
