@@ -143,6 +143,27 @@ int ptts_b200_kv_copy_stream(ptts_b200_kv* dst, int dst_stream, const ptts_b200_
  * timeouts of bounded waits). Synchronises the device. Clears the word. */
 int ptts_b200_kv_check(ptts_b200_kv* kv);
 
+/* ---- Ring caches: sliding windows (StreamingTransformer::start_ring / set_ring_slot / evict,
+ * transformer.rs:840-929) ----------------------------------------------------------------
+ * A ring stream keeps every row in the slot it was written to. Its next row goes to the write
+ * slot (set_ring_slot), which must not hold a row, at RoPE position = its length; it attends
+ * slots 0..max(filled, write + 1) - 1 where a row is held or being written. Evicting hides
+ * rows without moving anything, rotates every kept key past `prefix` back by the number of
+ * rows evicted (so all distances between kept rows stay) and lowers the length by that many.
+ * Ring streams take one row per call, in calls where every sequence has one row (forward,
+ * step, attend + kv_advance); prompts, load_prefix, copy_stream and set_lengths refuse them;
+ * kv_reset turns them back into appended streams. Refusals leave the cache as it was. */
+
+/* Every listed stream becomes a ring: its rows so far stay, the write slot is its length. */
+int ptts_b200_kv_start_ring(ptts_b200_kv* kv, const int32_t* streams_host, int n, void* cuda_stream);
+/* The slot of a ring stream's next row, 0 <= slot < capacity. */
+int ptts_b200_kv_set_ring_slot(ptts_b200_kv* kv, int stream, int slot, void* cuda_stream);
+/* Drop the rows in slots[0..n) of a ring stream (each at or past `prefix` and holding a row,
+ * no repeats, n at most the length); keys past `prefix` are rotated back by n positions with
+ * the RoPE of max_period (RotaryEmbedding::shift_back, rope.rs:26-35), in every layer. */
+int ptts_b200_kv_evict(ptts_b200_kv* kv, int stream, int prefix, const int32_t* slots_host, int n,
+                       float max_period, void* cuda_stream);
+
 /* ---------------------------------------------------------------------------------------
  * Attention op: the body of StreamingMultiheadAttention::forward after in_proj
  * (transformer.rs:197-248): GQA repeat, RoPE, append, then causal attention.

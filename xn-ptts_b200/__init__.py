@@ -44,6 +44,7 @@ EXPORTS = (
     "ptts_b200_forward", "ptts_b200_step", "ptts_b200_attend_decode_noalloc",
     "ptts_b200_flow_create", "ptts_b200_flow_destroy", "ptts_b200_flow_set_tensor",
     "ptts_b200_flow_finish", "ptts_b200_flow_sample", "ptts_b200_frame",
+    "ptts_b200_kv_start_ring", "ptts_b200_kv_set_ring_slot", "ptts_b200_kv_evict",
 )
 
 
@@ -134,6 +135,9 @@ def lib() -> ctypes.CDLL:
         L.ptts_b200_forward.argtypes = [P, P, P, IP, IP, I, P, P]
         L.ptts_b200_step.argtypes = [P, P, IP, I, P, P, P]
         L.ptts_b200_attend_decode_noalloc.argtypes = [P, P, I, I, I, P, P, I, P, P, P, I, I, F, P, I, P, P]
+        L.ptts_b200_kv_start_ring.argtypes = [P, IP, I, P]
+        L.ptts_b200_kv_set_ring_slot.argtypes = [P, I, I, P]
+        L.ptts_b200_kv_evict.argtypes = [P, I, I, IP, I, F, P]
         L.ptts_b200_flow_create.argtypes = [I, ctypes.POINTER(FlowConfigC), ctypes.POINTER(P)]
         L.ptts_b200_flow_destroy.argtypes = [P]
         L.ptts_b200_flow_destroy.restype = None
@@ -242,6 +246,21 @@ class KvState:
     def reset(self, streams: Sequence[int], stream=None):
         s = _i32(streams)
         _check(lib().ptts_b200_kv_reset(self._h, _ip(s), len(s), _stream(stream)))
+
+    def start_ring(self, streams: Sequence[int], stream=None):
+        """StreamingTransformer::start_ring for these streams (ptts_b200_kv_start_ring)."""
+        st = _i32(streams)
+        _check(lib().ptts_b200_kv_start_ring(self._h, _ip(st), len(st), _stream(stream)))
+
+    def set_ring_slot(self, stream_index: int, slot: int, stream=None):
+        _check(lib().ptts_b200_kv_set_ring_slot(self._h, stream_index, slot, _stream(stream)))
+
+    def evict(self, stream_index: int, prefix: int, slots: Sequence[int], max_period: float = 10000.0,
+              stream=None):
+        """StreamingTransformer::evict: hide `slots`, rotate kept keys past `prefix` back."""
+        sl = _i32(slots)
+        _check(lib().ptts_b200_kv_evict(self._h, stream_index, prefix, _ip(sl), len(sl), max_period,
+                                        _stream(stream)))
 
     def set_lengths(self, streams: Sequence[int], lengths: Sequence[int], stream=None):
         """Lower (or raise, up to capacity) stream lengths, keeping the slots."""

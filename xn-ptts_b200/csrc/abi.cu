@@ -98,6 +98,12 @@ struct ptts_b200_kv {
     DevBuf k, v, len;
     DevBuf err;
     std::vector<int32_t> h_len;
+    // Ring streams (start_ring / set_ring_slot / evict, transformer.rs:840-929), on the device
+    // and mirrored here: the slot the next row goes to (-1: not a ring), one past the highest
+    // slot written, and which slots hold a row attention may see.
+    DevBuf ring_write, ring_filled, ring_valid;
+    std::vector<int32_t> h_ring_write, h_ring_filled;
+    std::vector<uint8_t> h_ring_valid;
     // scratch of the attention op
     DevBuf seq_stream, row_offsets, row_stream, row_pos, prefix, part, q_rot, counters, tiles;
     Staging staging;
@@ -107,6 +113,21 @@ struct ptts_b200_kv {
             if (e) cudaEventDestroy(e);
     }
 
+    RingArgs ring() const {
+        RingArgs r;
+        r.write = ring_write.as<int32_t>();
+        r.filled = ring_filled.as<int32_t>();
+        r.valid = ring_valid.as<uint8_t>();
+        return r;
+    }
+    bool is_ring(int s) const { return h_ring_write[s] >= 0; }
+    // The host mirror after a row went into stream s's write slot (RingSlots in complete_kv).
+    void ring_commit(int s) {
+        const int w = h_ring_write[s];
+        if (w < 0) return;
+        h_ring_valid[(size_t)s * capacity + w] = 1;
+        h_ring_filled[s] = std::max(h_ring_filled[s], w + 1);
+    }
     size_t layer_bytes() const { return (size_t)streams * capacity * row_bytes; }
     size_t stream_bytes() const { return (size_t)capacity * row_bytes; }
     char* k_layer(int l) const { return k.as<char>() + l * layer_bytes(); }
@@ -179,6 +200,17 @@ int check_sequences(const ptts_b200_kv* kv, const int32_t* streams, const int32_
         require(!seen[s], PTTS_B200_ERR_ARG, "stream " + std::to_string(s) + " appears twice");
         seen[s] = 1;
         require(rows[i] >= 1, PTTS_B200_ERR_ARG, "every sequence needs at least one row");
+        if (kv->is_ring(s)) {  // StreamingMHAState::complete_kv, transformer.rs:67-73
+            require(rows[i] == 1, PTTS_B200_ERR_ARG,
+                    "a ring cache takes one row at a time, not " + std::to_string(rows[i]) + " (stream " +
+                        std::to_string(s) + ")");
+            const int w = kv->h_ring_write[s];
+            require(w < kv->capacity, PTTS_B200_ERR_CAPACITY,
+                    "ring slot " + std::to_string(w) + " of a " + std::to_string(kv->capacity) + "-slot ring");
+            require(!kv->h_ring_valid[(size_t)s * kv->capacity + w], PTTS_B200_ERR_STATE,
+                    "ring slot " + std::to_string(w) + " still holds a row, evict it first (stream " +
+                        std::to_string(s) + ")");
+        }
         const long long need = (long long)kv->h_len[s] + rows[i];
         if (need > kv->capacity)
             fail(PTTS_B200_ERR_CAPACITY, "cannot fit " + std::to_string(need) +
@@ -192,17 +224,41 @@ int check_sequences(const ptts_b200_kv* kv, const int32_t* streams, const int32_
     return (int)total;
 }
 
-// Decode (every sequence one row) or ragged plan into the given buffers.
+// A call with a prompt (some sequence of more than one row) plans rows by position; a ring
+// stream's row must go to its write slot, so ring streams only join all-decode calls.
+void refuse_ring_prompt(const ptts_b200_kv* kv, const int32_t* streams, int n, bool decode) {
+    if (decode) return;
+    for (int i = 0; i < n; ++i)
+        require(!kv->is_ring(streams[i]), PTTS_B200_ERR_ARG,
+                "a ring cache takes one row at a time, in calls where every sequence has one row (stream " +
+                    std::to_string(streams[i]) + ")");
+}
+
+// Ring state of stream st back to "not a ring" (kv_reset).
+void ring_clear(ptts_b200_kv* kv, int st, cudaStream_t s) {
+    kv->h_ring_write[st] = -1;
+    kv->h_ring_filled[st] = 0;
+    std::fill(kv->h_ring_valid.begin() + (size_t)st * kv->capacity,
+              kv->h_ring_valid.begin() + (size_t)(st + 1) * kv->capacity, 0);
+    const int32_t wf[2] = {-1, 0};
+    kv->staging.upload(kv->ring_write.as<int32_t>() + st, &wf[0], sizeof(int32_t), s);
+    kv->staging.upload(kv->ring_filled.as<int32_t>() + st, &wf[1], sizeof(int32_t), s);
+    CK(cudaMemsetAsync(kv->ring_valid.as<uint8_t>() + (size_t)st * kv->capacity, 0, kv->capacity, s));
+}
+
+// Decode (every sequence one row) or ragged plan into the given buffers; `row_pos` holds the
+// positions and then the slots.
 RowPlan make_plan(const ptts_b200_kv* kv, bool decode, const int32_t* d_seq_stream,
                   const int32_t* d_row_offsets, int n_seq, int n_rows, DevBuf& row_stream,
                   DevBuf& row_pos, DevBuf& prefix, cudaStream_t s) {
     RowPlan plan;
     plan.row_stream = static_cast<int32_t*>(row_stream.need(sizeof(int32_t) * n_rows));
-    plan.row_pos = static_cast<int32_t*>(row_pos.need(sizeof(int32_t) * n_rows));
+    plan.row_pos = static_cast<int32_t*>(row_pos.need(2 * sizeof(int32_t) * n_rows));
+    plan.row_slot = plan.row_pos + n_rows;
     plan.prefix = static_cast<int32_t*>(prefix.need(sizeof(int32_t) * (n_rows + 1)));
     if (decode)
         launch_plan_decode(kv->len.as<int32_t>(), d_seq_stream, n_seq, kv->streams, kv->capacity,
-                           plan, kv->err.as<uint32_t>(), s);
+                           plan, kv->ring(), kv->err.as<uint32_t>(), s);
     else
         launch_plan_rows(kv->len.as<int32_t>(), d_seq_stream, d_row_offsets, n_seq, n_rows,
                          kv->streams, kv->capacity, plan, kv->err.as<uint32_t>(), s);
@@ -237,6 +293,9 @@ void attention(const ptts_b200_kv* kv, int layer, bool decode, const RowPlan& pl
         a.B = n_rows;
         a.qscale = qscale;
         a.err = kv->err.as<uint32_t>();
+        a.ring_write = kv->ring_write.as<int32_t>();
+        a.ring_valid = kv->ring_valid.as<uint8_t>();
+        a.capacity = kv->capacity;
         launch_decode_attn(a, bf16, grid, s);
     } else {
         PrefillArgs a{};
@@ -351,6 +410,7 @@ void run_layers(const ptts_b200_model* m, const ptts_b200_kv* kv, bool decode, c
         a.yq = w.q_rot.as<float>();
         a.row_stream = plan.row_stream;
         a.row_pos = plan.row_pos;
+        a.row_slot = plan.row_slot;
         a.k_cache = reinterpret_cast<__nv_bfloat16*>(kv->k_layer(l));
         a.v_cache = reinterpret_cast<__nv_bfloat16*>(kv->v_layer(l));
         a.heads = c.num_heads;
@@ -455,6 +515,12 @@ int ptts_b200_kv_create(int device, int num_layers, int num_streams, int capacit
         CK(cudaMemset(kv->len.need(sizeof(int32_t) * num_streams), 0, sizeof(int32_t) * num_streams));
         CK(cudaMemset(kv->err.need(sizeof(uint32_t)), 0, sizeof(uint32_t)));
         kv->h_len.assign(num_streams, 0);
+        CK(cudaMemset(kv->ring_write.need(sizeof(int32_t) * num_streams), 0xFF, sizeof(int32_t) * num_streams));
+        CK(cudaMemset(kv->ring_filled.need(sizeof(int32_t) * num_streams), 0, sizeof(int32_t) * num_streams));
+        CK(cudaMemset(kv->ring_valid.need((size_t)num_streams * capacity), 0, (size_t)num_streams * capacity));
+        kv->h_ring_write.assign(num_streams, -1);
+        kv->h_ring_filled.assign(num_streams, 0);
+        kv->h_ring_valid.assign((size_t)num_streams * capacity, 0);
         CK(cudaDeviceSynchronize());
         *out = kv.release();
     });
@@ -501,9 +567,12 @@ int ptts_b200_kv_advance(ptts_b200_kv* kv, const int32_t* streams_host, const in
         packed.insert(packed.end(), offsets.begin(), offsets.end());
         int32_t* d = static_cast<int32_t*>(kv->seq_stream.need(sizeof(int32_t) * packed.size()));
         kv->staging.upload(d, packed.data(), sizeof(int32_t) * packed.size(), s);
-        launch_advance(kv->len.as<int32_t>(), d, d + n, n, 0, s);
+        launch_advance(kv->len.as<int32_t>(), d, d + n, n, 0, kv->ring(), kv->capacity, s);
         check_launch();
-        for (int i = 0; i < n; ++i) kv->h_len[streams_host[i]] += rows_host[i];
+        for (int i = 0; i < n; ++i) {
+            kv->h_len[streams_host[i]] += rows_host[i];
+            kv->ring_commit(streams_host[i]);
+        }
     });
 }
 
@@ -521,7 +590,11 @@ int ptts_b200_kv_reset(ptts_b200_kv* kv, const int32_t* streams_host, int n, voi
         launch_reset_streams(kv->k.p, kv->v.p, kv->len.as<int32_t>(), d, n, kv->layers,
                              (long long)kv->layer_bytes(), (long long)kv->stream_bytes(), s);
         check_launch();
-        for (int i = 0; i < n; ++i) kv->h_len[streams_host[i]] = 0;
+        for (int i = 0; i < n; ++i) {
+            const int st = streams_host[i];
+            kv->h_len[st] = 0;
+            if (kv->is_ring(st)) ring_clear(kv, st, s);  // back to an appended cache
+        }
     });
 }
 
@@ -532,6 +605,7 @@ int ptts_b200_kv_load_prefix(ptts_b200_kv* kv, int layer, int stream, const void
         require(layer >= 0 && layer < kv->layers, PTTS_B200_ERR_ARG, "layer out of range");
         require(stream >= 0 && stream < kv->streams, PTTS_B200_ERR_ARG, "stream out of range");
         require(len >= 0, PTTS_B200_ERR_ARG, "negative length");
+        require(!kv->is_ring(stream), PTTS_B200_ERR_STATE, "a ring cache cannot load a prefix");
         if (len > kv->capacity)
             fail(PTTS_B200_ERR_CAPACITY, "cannot fit " + std::to_string(len) +
                                              " filled KV positions into a budget of " +
@@ -563,6 +637,8 @@ int ptts_b200_kv_copy_stream(ptts_b200_kv* dst, int dst_stream, const ptts_b200_
         require(dst_stream >= 0 && dst_stream < dst->streams && src_stream >= 0 &&
                     src_stream < src->streams,
                 PTTS_B200_ERR_ARG, "stream out of range");
+        require(!src->is_ring(src_stream) && !dst->is_ring(dst_stream), PTTS_B200_ERR_STATE,
+                "a ring cache cannot be resized");  // transformer.rs:356-357
         const int used = src->h_len[src_stream];
         if (used > dst->capacity)
             fail(PTTS_B200_ERR_CAPACITY, "cannot fit " + std::to_string(used) +
@@ -624,6 +700,7 @@ int ptts_b200_attend(ptts_b200_kv* kv, int layer, const void* q, const void* k, 
         const int n_rows = check_sequences(kv, streams_host, rows_host, n_seq, offsets);
         bool decode = true;
         for (int i = 0; i < n_seq; ++i) decode = decode && rows_host[i] == 1;
+        refuse_ring_prompt(kv, streams_host, n_seq, decode);
         DeviceScope scope(kv->device);
         cudaStream_t s = as_stream(cuda_stream);
         std::vector<int32_t> packed(streams_host, streams_host + n_seq);
@@ -642,6 +719,7 @@ int ptts_b200_attend(ptts_b200_kv* kv, int layer, const void* q, const void* k, 
         ra.v_cache = kv->v_layer(layer);
         ra.row_stream = plan.row_stream;
         ra.row_pos = plan.row_pos;
+        ra.row_slot = plan.row_slot;
         ra.rows = n_rows;
         ra.heads = kv->heads;
         ra.kv_heads = num_kv_heads;
@@ -797,6 +875,7 @@ int ptts_b200_forward(ptts_b200_model* model, ptts_b200_kv* kv, const void* x,
         const int rows = check_sequences(kv, streams_host, rows_host, n_seq, offsets);
         bool decode = true;
         for (int i = 0; i < n_seq; ++i) decode = decode && rows_host[i] == 1;
+        refuse_ring_prompt(kv, streams_host, n_seq, decode);
         DeviceScope scope(model->device);
         cudaStream_t s = as_stream(cuda_stream);
         const ptts_b200_config& c = model->cfg;
@@ -819,9 +898,12 @@ int ptts_b200_forward(ptts_b200_model* model, ptts_b200_kv* kv, const void* x,
         // The residual stream lives in the caller's output y.
         run_layers(model, kv, decode, plan, rows, static_cast<const __nv_bfloat16*>(x), y, model->ws, s,
                    nullptr, tiles);
-        launch_advance(kv->len.as<int32_t>(), d, d + n_seq, n_seq, 0, s);
+        launch_advance(kv->len.as<int32_t>(), d, d + n_seq, n_seq, 0, kv->ring(), kv->capacity, s);
         check_launch();
-        for (int i = 0; i < n_seq; ++i) kv->h_len[streams_host[i]] += rows_host[i];
+        for (int i = 0; i < n_seq; ++i) {
+            kv->h_len[streams_host[i]] += rows_host[i];
+            kv->ring_commit(streams_host[i]);
+        }
     });
 }
 
@@ -854,7 +936,7 @@ int ptts_b200_step(ptts_b200_model* model, ptts_b200_kv* kv, const int32_t* stre
             ng->ws.size(c, n);
             ng->ws.part.need(sizeof(float) * decode_part_floats(n, sm_count(kv->device)));
             ng->row_stream.need(sizeof(int32_t) * n);
-            ng->row_pos.need(sizeof(int32_t) * n);
+            ng->row_pos.need(2 * sizeof(int32_t) * n);  // positions, then slots
             ng->prefix.need(sizeof(int32_t) * (n + 1));
             model->step = std::move(ng);
             g = model->step.get();
@@ -862,14 +944,15 @@ int ptts_b200_step(ptts_b200_model* model, ptts_b200_kv* kv, const int32_t* stre
         RowPlan plan;
         plan.row_stream = g->row_stream.as<int32_t>();
         plan.row_pos = g->row_pos.as<int32_t>();
+        plan.row_slot = plan.row_pos + n;
         plan.prefix = g->prefix.as<int32_t>();
         const int32_t* sid = g->sid.as<int32_t>();
         auto body = [&](cudaStream_t cs, cudaEvent_t* ev) {
-            launch_plan_decode(kv->len.as<int32_t>(), sid, n, kv->streams, kv->capacity, plan,
+            launch_plan_decode(kv->len.as<int32_t>(), sid, n, kv->streams, kv->capacity, plan, kv->ring(),
                                kv->err.as<uint32_t>(), cs);
             run_layers(model, kv, true, plan, n, g->x.as<__nv_bfloat16>(), g->resid.as<float>(), g->ws,
                        cs, ev);
-            launch_advance(kv->len.as<int32_t>(), sid, nullptr, n, 1, cs);
+            launch_advance(kv->len.as<int32_t>(), sid, nullptr, n, 1, kv->ring(), kv->capacity, cs);
             check_launch();
         };
         const size_t xb = (size_t)n * c.d_model * 2, yb = (size_t)n * c.d_model * 4;
@@ -917,7 +1000,10 @@ int ptts_b200_step(ptts_b200_model* model, ptts_b200_kv* kv, const int32_t* stre
             CK(cudaGraphLaunch(g->exec, s));
         }
         CK(cudaMemcpyAsync(y, g->resid.p, yb, is_device_pointer(y) ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost, s));
-        for (int i = 0; i < n; ++i) kv->h_len[streams_host[i]] += 1;
+        for (int i = 0; i < n; ++i) {
+            kv->h_len[streams_host[i]] += 1;
+            kv->ring_commit(streams_host[i]);
+        }
     });
 }
 
@@ -937,6 +1023,98 @@ int ptts_b200_trace_read(ptts_b200_trace* out, int reset) {
     });
 }
 
+int ptts_b200_kv_start_ring(ptts_b200_kv* kv, const int32_t* streams_host, int n, void* cuda_stream) {
+    return guarded([&] {
+        check_kv(kv);
+        require(n > 0 && streams_host, PTTS_B200_ERR_ARG, "no streams");
+        for (int i = 0; i < n; ++i) {
+            const int st = streams_host[i];
+            require(st >= 0 && st < kv->streams, PTTS_B200_ERR_ARG, "stream out of range");
+            require(!kv->is_ring(st), PTTS_B200_ERR_STATE, "stream " + std::to_string(st) + " is already a ring");
+        }
+        DeviceScope scope(kv->device);
+        cudaStream_t s = as_stream(cuda_stream);
+        for (int i = 0; i < n; ++i) {
+            // start_ring (transformer.rs:842-852): the rows so far stay, the next goes after them.
+            const int st = streams_host[i], used = kv->h_len[st];
+            kv->h_ring_write[st] = used;
+            kv->h_ring_filled[st] = used;
+            uint8_t* hv = kv->h_ring_valid.data() + (size_t)st * kv->capacity;
+            std::fill(hv, hv + kv->capacity, 0);
+            std::fill(hv, hv + used, 1);
+            kv->staging.upload(kv->ring_write.as<int32_t>() + st, &kv->h_ring_write[st], sizeof(int32_t), s);
+            kv->staging.upload(kv->ring_filled.as<int32_t>() + st, &kv->h_ring_filled[st], sizeof(int32_t), s);
+            uint8_t* dv = kv->ring_valid.as<uint8_t>() + (size_t)st * kv->capacity;
+            if (used > 0) CK(cudaMemsetAsync(dv, 1, used, s));
+            if (used < kv->capacity) CK(cudaMemsetAsync(dv + used, 0, kv->capacity - used, s));
+        }
+    });
+}
+
+int ptts_b200_kv_set_ring_slot(ptts_b200_kv* kv, int stream, int slot, void* cuda_stream) {
+    return guarded([&] {
+        check_kv(kv);
+        require(stream >= 0 && stream < kv->streams, PTTS_B200_ERR_ARG, "stream out of range");
+        require(kv->is_ring(stream), PTTS_B200_ERR_STATE, "not a ring cache, see ptts_b200_kv_start_ring");
+        require(slot >= 0 && slot < kv->capacity, PTTS_B200_ERR_ARG,
+                "slot " + std::to_string(slot) + " of a " + std::to_string(kv->capacity) + "-slot ring");
+        DeviceScope scope(kv->device);
+        kv->h_ring_write[stream] = slot;
+        kv->staging.upload(kv->ring_write.as<int32_t>() + stream, &kv->h_ring_write[stream], sizeof(int32_t),
+                           as_stream(cuda_stream));
+    });
+}
+
+int ptts_b200_kv_evict(ptts_b200_kv* kv, int stream, int prefix, const int32_t* slots_host, int n,
+                       float max_period, void* cuda_stream) {
+    return guarded([&] {
+        check_kv(kv);
+        require(stream >= 0 && stream < kv->streams, PTTS_B200_ERR_ARG, "stream out of range");
+        require(kv->is_ring(stream), PTTS_B200_ERR_STATE, "not a ring cache, see ptts_b200_kv_start_ring");
+        require(n >= 0 && (n == 0 || slots_host), PTTS_B200_ERR_ARG, "slots are NULL");
+        require(prefix >= 0, PTTS_B200_ERR_ARG, "negative prefix");
+        require(max_period > 1.0f, PTTS_B200_ERR_ARG, "max_period must be above 1");
+        require(n <= kv->h_len[stream], PTTS_B200_ERR_ARG,
+                "cannot evict " + std::to_string(n) + " of " + std::to_string(kv->h_len[stream]) + " positions");
+        // Every slot is checked before anything changes, so a refused call leaves the cache as is.
+        uint8_t* hv = kv->h_ring_valid.data() + (size_t)stream * kv->capacity;
+        std::vector<char> seen(kv->capacity, 0);
+        for (int i = 0; i < n; ++i) {
+            const int sl = slots_host[i];
+            require(sl >= prefix && sl < kv->capacity && hv[sl] && !seen[sl], PTTS_B200_ERR_ARG,
+                    "slot " + std::to_string(sl) + " holds no row past the prefix");
+            seen[sl] = 1;
+        }
+        if (n == 0) return;
+        DeviceScope scope(kv->device);
+        cudaStream_t s = as_stream(cuda_stream);
+        RingEvictArgs a{};
+        int32_t* d = static_cast<int32_t*>(kv->seq_stream.need(sizeof(int32_t) * n));
+        kv->staging.upload(d, slots_host, sizeof(int32_t) * n, s);
+        a.k_cache = kv->k.p;
+        a.layers = kv->layers;
+        const long long elem = kv->dtype == PTTS_B200_BF16 ? 2 : 4;
+        a.layer_elems = (long long)kv->layer_bytes() / elem;
+        a.stream_elems = (long long)kv->stream_bytes() / elem;
+        a.row_elems = kv->heads * kv->head_dim;
+        a.capacity = kv->capacity;
+        a.sid = stream;
+        a.prefix = prefix;
+        a.filled = kv->h_ring_filled[stream];
+        a.shift = n;
+        a.bf16 = kv->dtype == PTTS_B200_BF16;
+        rope_inv_freq(kv->head_dim, max_period, a.inv_freq);
+        a.slots = d;
+        a.n = n;
+        a.ring = kv->ring();
+        a.lengths = kv->len.as<int32_t>();
+        launch_ring_evict(a, s);
+        check_launch();
+        for (int i = 0; i < n; ++i) hv[slots_host[i]] = 0;
+        kv->h_len[stream] -= n;
+    });
+}
+
 int ptts_b200_kv_set_lengths(ptts_b200_kv* kv, const int32_t* streams_host,
                              const int32_t* lengths_host, int n, void* cuda_stream) {
     return guarded([&] {
@@ -945,6 +1123,8 @@ int ptts_b200_kv_set_lengths(ptts_b200_kv* kv, const int32_t* streams_host,
         for (int i = 0; i < n; ++i) {
             require(streams_host[i] >= 0 && streams_host[i] < kv->streams, PTTS_B200_ERR_ARG,
                     "stream out of range");
+            require(!kv->is_ring(streams_host[i]), PTTS_B200_ERR_STATE,
+                    "a ring cache drops rows by eviction (ptts_b200_kv_evict), not by length");
             if (lengths_host[i] < 0 || lengths_host[i] > kv->capacity)
                 fail(PTTS_B200_ERR_CAPACITY, "cannot fit " + std::to_string(lengths_host[i]) +
                                                  " filled KV positions into a budget of " +

@@ -1,5 +1,7 @@
 // Split-KV decode attention: one query row per stream over that stream's cached keys
-// 0..=pos, for a batch of streams with ragged lengths.
+// 0..=pos, for a batch of streams with ragged lengths. A ring stream attends its slots
+// 0..max(filled, write + 1) - 1 with the slots of evicted rows masked (RingSlots::decode_mask,
+// transformer.rs:39-53).
 //
 // Reference: the t == 1 branch of StreamingMultiheadAttention::forward, `q.sdpa_decode(k, v,
 // mask, 1/sqrt(d))` (ptts/src/transformer.rs:229-230), and its device-position twin at
@@ -236,6 +238,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(DecodeArgs a) 
         const int s0 = (int)((start > pb ? start : pb) - pb);
         const int s1 = (int)((end < pe ? end : pe) - pb);
         const bool whole = pb >= start && pe <= end;
+        // Ring stream: slot s is visible iff valid[s] or s is the slot being written.
+        const int sid = a.row_stream[b];
+        const int ring_w = a.ring_write ? a.ring_write[sid] : -1;
+        const uint8_t* vis = ring_w >= 0 ? a.ring_valid + (long long)sid * a.capacity : nullptr;
 
         float q[8];
         load_q<T>(a.q + ((long long)b * kHeads + h) * kHeadDim, j, q);
@@ -275,6 +281,11 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(DecodeArgs a) 
                 }
                 if (r0 >= n) d0 = -INFINITY;
                 if (r1 >= n) d1 = -INFINITY;
+                if (vis) {
+                    const int s0 = p + rr0, s1 = p + rr1;
+                    if (!vis[s0] && s0 != ring_w) d0 = -INFINITY;
+                    if (!vis[s1] && s1 != ring_w) d1 = -INFINITY;
+                }
                 const float mn = fmaxf(m, fmaxf(d0, d1));
                 const float corr = fast_exp2(m - mn);
                 const float e0 = fast_exp2(d0 - mn), e1 = fast_exp2(d1 - mn);

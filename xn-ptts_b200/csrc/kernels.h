@@ -42,19 +42,32 @@ constexpr int kHeadDim = 64;   // D: the only head size the kernels implement
 constexpr int kRowWidth = 512; // H * D: one cache row of all heads
 constexpr int kMaxPairs = kHeadDim / 2;
 
-// Per-call row plan on the device: which arena stream and position each row has.
+// Per-call row plan on the device: which arena stream, position and cache slot each row has.
 struct RowPlan {
     int32_t* row_stream = nullptr;  // [rows]
-    int32_t* row_pos = nullptr;     // [rows]
+    int32_t* row_pos = nullptr;     // [rows] RoPE position
+    int32_t* row_slot = nullptr;    // [rows] cache slot written (the position, except in a ring)
     int32_t* prefix = nullptr;      // [rows + 1] decode only: prefix sums of attended keys
+};
+
+// Ring caches (StreamingTransformer::start_ring / set_ring_slot / evict, transformer.rs:840-929):
+// per stream the slot the next row goes to (-1: not a ring), one past the highest slot written,
+// and which slots hold a row attention may see. nullptr members: no stream is a ring.
+struct RingArgs {
+    int32_t* write = nullptr;   // [streams]
+    int32_t* filled = nullptr;  // [streams]
+    uint8_t* valid = nullptr;   // [streams][capacity]
 };
 
 // ---- plans and bookkeeping (misc.cu) ---------------------------------------------------
 
-// Decode plan: one row per sequence. row_pos[i] = lengths[streams[i]]; prefix[i+1] =
-// sum_{j<=i} min(row_pos[j] + 1, capacity). Sets DEV_ERR_CAPACITY / DEV_ERR_BOUNDS.
+// Decode plan: one row per sequence. row_pos[i] = lengths[streams[i]]; the row is written at
+// slot row_pos[i] and attends keys 0..row_pos[i], or, for a ring stream, written at its write
+// slot w and attends slots 0..max(filled, w + 1) - 1 (the invisible ones masked by the decode
+// kernel). prefix[i+1] = sum of attended keys, clamped to capacity. Sets DEV_ERR_CAPACITY /
+// DEV_ERR_BOUNDS.
 void launch_plan_decode(const int32_t* lengths, const int32_t* streams, int n, int num_streams,
-                        int capacity, RowPlan plan, uint32_t* err, cudaStream_t s);
+                        int capacity, RowPlan plan, const RingArgs& ring, uint32_t* err, cudaStream_t s);
 
 // Ragged plan: sequence i (stream seq_stream[i]) owns rows row_offsets[i]..row_offsets[i+1];
 // row r of it sits at lengths[stream] + (r - row_offsets[i]).
@@ -62,9 +75,30 @@ void launch_plan_rows(const int32_t* lengths, const int32_t* seq_stream, const i
                       int n_seq, int n_rows, int num_streams, int capacity, RowPlan plan,
                       uint32_t* err, cudaStream_t s);
 
-// lengths[seq_stream[i]] += rows (row_offsets == nullptr) or row_offsets[i+1]-row_offsets[i].
+// lengths[seq_stream[i]] += rows (row_offsets == nullptr) or row_offsets[i+1]-row_offsets[i];
+// for a ring stream also valid[write] = 1 and filled = max(filled, write + 1).
 void launch_advance(int32_t* lengths, const int32_t* seq_stream, const int32_t* row_offsets,
-                    int n_seq, int rows, cudaStream_t s);
+                    int n_seq, int rows, const RingArgs& ring, int capacity, cudaStream_t s);
+
+// Ring eviction of stream `sid` (transformer.rs:873-928): slots[0..n) become invisible, every
+// still-visible key in slots [prefix, filled) of every layer is rotated back by n positions
+// (RotaryEmbedding::shift_back, rope.rs:26-35: the rotation by -n, angle f32(-n) * inv_freq[i]),
+// and lengths[sid] -= n.
+struct RingEvictArgs {
+    void* k_cache;            // all layers
+    int layers;
+    long long layer_elems;    // elements per layer
+    long long stream_elems;   // elements per stream (capacity * H * D)
+    int row_elems;            // H * D
+    int capacity, sid, prefix, filled, shift;
+    bool bf16;
+    float inv_freq[kMaxPairs];
+    const int32_t* slots;     // [n] device
+    int n;
+    RingArgs ring;
+    int32_t* lengths;
+};
+void launch_ring_evict(const RingEvictArgs& a, cudaStream_t s);
 
 // lengths[streams[i]] = values[i].
 void launch_set_lengths(int32_t* lengths, const int32_t* streams, const int32_t* values, int n,
@@ -89,6 +123,7 @@ struct RopeAppendArgs {
     void* v_cache;
     const int32_t* row_stream;
     const int32_t* row_pos;
+    const int32_t* row_slot;   // cache slot of each row
     int rows, heads, kv_heads, num_streams, capacity;
     float inv_freq[kMaxPairs];
     uint32_t* err;
@@ -112,6 +147,11 @@ struct DecodeArgs {
     int B;
     float qscale;             // 1/sqrt(D) * log2(e)
     uint32_t* err;
+    // Ring streams: key slot s is visible iff valid[s] or s == write (RingSlots::decode_mask,
+    // transformer.rs:39-53). ring_write nullptr: no ring in the arena.
+    const int32_t* ring_write = nullptr;
+    const uint8_t* ring_valid = nullptr;
+    int capacity = 0;
 };
 // Output forms of the attention kernels.
 constexpr int kOutF32 = 0, kOutBf16 = 1, kOutHiLo = 2;  // hi/lo: f16(o) and f16(o - hi)
@@ -172,6 +212,7 @@ struct LinearArgs {
     // EPI_QKV
     const int32_t* row_stream;
     const int32_t* row_pos;
+    const int32_t* row_slot;   // EPI_QKV: cache slot of each row
     __nv_bfloat16* k_cache;
     __nv_bfloat16* v_cache;
     int heads, kv_heads, num_streams, capacity;

@@ -204,6 +204,7 @@ __device__ __forceinline__ void epilogue_pair(const LinearArgs& p, int m, int n,
 // (loaded by the caller before any store, so no load waits behind the stores).
 __device__ __forceinline__ void qkv_pair(const LinearArgs& p, int m, int n, float c0, float c1, int sid,
                                          int pos, float2 t) {
+    // `pos` is the row's cache slot here (the RoPE factors t come from its position).
     const int hd = p.heads * kHeadDim, kvd = p.kv_heads * kHeadDim;
     const int d = n % kHeadDim;
     float x0 = c0 * p.scale[n], x1 = c1 * p.scale[n + 1];
@@ -317,8 +318,9 @@ __global__ void __launch_bounds__(kThreads) linear_kernel(LinearArgs p) {
             for (int h = 0; h < 2; ++h) {
                 const int m = m0 + row0 + mi * 16 + g + 8 * h;
                 sid[mi][h] = m < p.M ? p.row_stream[m] : 0;
-                pos[mi][h] = m < p.M ? p.row_pos[m] : 0;
-                const long long trow = (long long)min(max(pos[mi][h], 0), p.capacity - 1) * kMaxPairs;
+                const int rpos = m < p.M ? p.row_pos[m] : 0;
+                pos[mi][h] = m < p.M ? p.row_slot[m] : 0;  // cache slot
+                const long long trow = (long long)min(max(rpos, 0), p.capacity - 1) * kMaxPairs;
 #pragma unroll
                 for (int ni = 0; ni < NI; ++ni)
                     rt[mi][h][ni] = rotated ? __ldg(p.rope + trow + ((n0 + col0 + ni * 8 + 2 * t) % kHeadDim) / 2)

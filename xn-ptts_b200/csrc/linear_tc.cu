@@ -164,7 +164,8 @@ __device__ __forceinline__ void qkv_rows(const LinearArgs& p, const float* st, i
     const int group = p.heads / p.kv_heads;
     const float4 sc = __ldg(reinterpret_cast<const float4*>(p.scale + f));
     const int ml = mbase + lane;
-    const int pos_l = ml < p.M ? __ldg(p.row_pos + ml) : 0;
+    const int pos_l = ml < p.M ? __ldg(p.row_pos + ml) : 0;     // RoPE position
+    const int slot_l = ml < p.M ? __ldg(p.row_slot + ml) : 0;   // cache slot
     const int sid_l = ml < p.M ? __ldg(p.row_stream + ml) : 0;
     float4 t[8];
 #pragma unroll
@@ -177,7 +178,7 @@ __device__ __forceinline__ void qkv_rows(const LinearArgs& p, const float* st, i
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
         const int j = warp + 4 * i, m = mbase + j;
-        const int pos = __shfl_sync(0xffffffffu, pos_l, j);
+        const int pos = __shfl_sync(0xffffffffu, slot_l, j);
         const int sid = __shfl_sync(0xffffffffu, sid_l, j);
         const float4 a = *reinterpret_cast<const float4*>(st + j * kStageStride + 4 * lane);
         float x0 = a.x * sc.x, x1 = a.y * sc.y, x2 = a.z * sc.z, x3 = a.w * sc.w;

@@ -12,7 +12,7 @@ constexpr int kPlanThreads = 1024;
 // One CTA: a running block scan over the sequences, 1024 at a time.
 __global__ void __launch_bounds__(kPlanThreads) plan_decode_kernel(
     const int32_t* __restrict__ lengths, const int32_t* __restrict__ streams, int n,
-    int num_streams, int capacity, RowPlan plan, uint32_t* err) {
+    int num_streams, int capacity, RowPlan plan, RingArgs ring, uint32_t* err) {
     __shared__ int warp_tot[kPlanThreads / 32];
     __shared__ int carry;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -34,10 +34,18 @@ __global__ void __launch_bounds__(kPlanThreads) plan_decode_kernel(
             }
             const int len = lengths[sid];
             if (len < 0 || len + 1 > capacity) set_error(err, DEV_ERR_CAPACITY);
-            plan.row_stream[i] = sid;
-            plan.row_pos[i] = len;
+            int slot = len;
             // Clamped so that a refused row never makes a kernel read past the stream's slots.
             keys = min(max(len, 0) + 1, capacity);
+            const int w = ring.write ? ring.write[sid] : -1;
+            if (w >= 0) {
+                if (w >= capacity) set_error(err, DEV_ERR_CAPACITY);
+                slot = min(w, capacity - 1);
+                keys = min(max(ring.filled[sid], slot + 1), capacity);
+            }
+            plan.row_stream[i] = sid;
+            plan.row_pos[i] = len;
+            plan.row_slot[i] = slot;
         }
         int v = keys;
 #pragma unroll
@@ -88,16 +96,59 @@ __global__ void plan_rows_kernel(const int32_t* __restrict__ lengths,
     if (pos < 0 || pos >= capacity) set_error(err, DEV_ERR_CAPACITY);
     plan.row_stream[r] = sid;
     plan.row_pos[r] = pos;
+    plan.row_slot[r] = pos;
 }
 
 __global__ void advance_kernel(int32_t* lengths, const int32_t* __restrict__ seq_stream,
-                               const int32_t* __restrict__ row_offsets, int n_seq, int rows) {
+                               const int32_t* __restrict__ row_offsets, int n_seq, int rows,
+                               RingArgs ring, int capacity) {
     grid_dep_wait();
     grid_dep_launch();
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n_seq) return;
     const int add = row_offsets ? row_offsets[i + 1] - row_offsets[i] : rows;
-    lengths[seq_stream[i]] += add;
+    const int sid = seq_stream[i];
+    const int w = ring.write ? ring.write[sid] : -1;
+    if (w >= 0 && w < capacity) {
+        ring.valid[(long long)sid * capacity + w] = 1;
+        ring.filled[sid] = max(ring.filled[sid], w + 1);
+    }
+    lengths[sid] += add;
+}
+
+__global__ void ring_hide_kernel(RingEvictArgs a) {
+    grid_dep_wait();
+    grid_dep_launch();
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < a.n) a.ring.valid[(long long)a.sid * a.capacity + a.slots[i]] = 0;
+    if (i == 0) a.lengths[a.sid] -= a.n;
+}
+
+// One thread per (layer, slot, pair); rotation arithmetic as the RoPE epilogues (rope.rs order).
+template <typename T>
+__global__ void ring_rotate_kernel(RingEvictArgs a) {
+    grid_dep_wait();
+    grid_dep_launch();
+    const int pairs = a.row_elems / 2, slots = a.filled - a.prefix;
+    const long long total = (long long)a.layers * slots * pairs;
+    const uint8_t* valid = a.ring.valid + (long long)a.sid * a.capacity;
+    T* k = static_cast<T*>(a.k_cache);
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+         i += (long long)gridDim.x * blockDim.x) {
+        const int pr = (int)(i % pairs);
+        const long long ls = i / pairs;
+        const int slot = a.prefix + (int)(ls % slots), layer = (int)(ls / slots);
+        if (!valid[slot]) continue;
+        const int d2 = pr % (kHeadDim / 2);  // pair index within the head
+        float sn, cs;
+        sincosf((float)(-a.shift) * a.inv_freq[d2], &sn, &cs);
+        T* e = k + layer * a.layer_elems + a.sid * a.stream_elems + (long long)slot * a.row_elems + 2 * pr;
+        const float x0 = (float)e[0], x1 = (float)e[1];
+        const float y0 = __fsub_rn(__fmul_rn(x0, cs), __fmul_rn(x1, sn));
+        const float y1 = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, cs));
+        e[0] = (T)y0;
+        e[1] = (T)y1;
+    }
 }
 
 __global__ void set_lengths_kernel(int32_t* lengths, const int32_t* __restrict__ streams,
@@ -140,9 +191,9 @@ __global__ void bf16_to_f32_kernel(const __nv_bfloat16* __restrict__ x, float* _
 }  // namespace
 
 void launch_plan_decode(const int32_t* lengths, const int32_t* streams, int n, int num_streams,
-                        int capacity, RowPlan plan, uint32_t* err, cudaStream_t s) {
+                        int capacity, RowPlan plan, const RingArgs& ring, uint32_t* err, cudaStream_t s) {
     launch_k(plan_decode_kernel, dim3(1), dim3(kPlanThreads), 0, s, lengths, streams, n,
-             num_streams, capacity, plan, err);
+             num_streams, capacity, plan, ring, err);
 }
 
 void launch_plan_rows(const int32_t* lengths, const int32_t* seq_stream, const int32_t* row_offsets,
@@ -153,9 +204,18 @@ void launch_plan_rows(const int32_t* lengths, const int32_t* seq_stream, const i
 }
 
 void launch_advance(int32_t* lengths, const int32_t* seq_stream, const int32_t* row_offsets,
-                    int n_seq, int rows, cudaStream_t s) {
+                    int n_seq, int rows, const RingArgs& ring, int capacity, cudaStream_t s) {
     launch_k(advance_kernel, dim3((n_seq + 255) / 256), dim3(256), 0, s, lengths, seq_stream,
-             row_offsets, n_seq, rows);
+             row_offsets, n_seq, rows, ring, capacity);
+}
+
+void launch_ring_evict(const RingEvictArgs& a, cudaStream_t s) {
+    launch_k(ring_hide_kernel, dim3((a.n + 255) / 256 > 0 ? (a.n + 255) / 256 : 1), dim3(256), 0, s, a);
+    if (a.filled <= a.prefix) return;
+    const long long total = (long long)a.layers * (a.filled - a.prefix) * (a.row_elems / 2);
+    const int blocks = (int)((total + 255) / 256 < 4096 ? (total + 255) / 256 : 4096);
+    if (a.bf16) launch_k(ring_rotate_kernel<__nv_bfloat16>, dim3(blocks), dim3(256), 0, s, a);
+    else launch_k(ring_rotate_kernel<float>, dim3(blocks), dim3(256), 0, s, a);
 }
 
 void launch_set_lengths(int32_t* lengths, const int32_t* streams, const int32_t* values, int n,

@@ -107,6 +107,7 @@ extern "C" int ptts_b200_attend_decode_noalloc(void* k_cache, void* v_cache, int
     RowPlan plan;
     plan.row_stream = plan_base;
     plan.row_pos = plan_base + kNoAllocMaxRows;
+    plan.row_slot = plan.row_pos;  // no ring here: every row is written at its position
     plan.prefix = plan_base + 2 * kNoAllocMaxRows;
     float* q_rot = reinterpret_cast<float*>(sc.base + kPlanBytes);
     float* part = reinterpret_cast<float*>(sc.base + kPlanBytes + kQBytes);
@@ -114,7 +115,7 @@ extern "C" int ptts_b200_attend_decode_noalloc(void* k_cache, void* v_cache, int
     if (cudaMemsetAsync(counters, 0, sizeof(int) * n, s) != cudaSuccess)
         return refuse(PTTS_B200_ERR_CUDA, "clearing the merge counters failed");
 
-    launch_plan_decode(lengths, streams, n, num_streams, capacity, plan, err, s);
+    launch_plan_decode(lengths, streams, n, num_streams, capacity, plan, RingArgs{}, err, s);
     RopeAppendArgs ra{};
     ra.q = q;
     ra.k = k;
@@ -124,6 +125,7 @@ extern "C" int ptts_b200_attend_decode_noalloc(void* k_cache, void* v_cache, int
     ra.v_cache = v_cache;
     ra.row_stream = plan.row_stream;
     ra.row_pos = plan.row_pos;
+    ra.row_slot = plan.row_slot;
     ra.rows = n;
     ra.heads = heads;
     ra.kv_heads = num_kv_heads;

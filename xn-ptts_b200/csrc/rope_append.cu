@@ -25,8 +25,8 @@ __global__ void rope_append_kernel(RopeAppendArgs a) {
     const int slot = (int)((idx / pairs) % slots);
     const int row = (int)(idx / ((long long)pairs * slots));
     const int sid = a.row_stream[row];
-    const int pos = a.row_pos[row];
-    if (sid < 0 || sid >= a.num_streams || pos < 0 || pos >= a.capacity) {
+    const int pos = a.row_pos[row], cslot = a.row_slot[row];  // RoPE position, cache slot
+    if (sid < 0 || sid >= a.num_streams || pos < 0 || pos >= a.capacity || cslot < 0 || cslot >= a.capacity) {
         set_error(a.err, DEV_ERR_CAPACITY);
         return;
     }
@@ -56,7 +56,7 @@ __global__ void rope_append_kernel(RopeAppendArgs a) {
     const int g = is_k ? slot - a.heads : slot - a.heads - a.kv_heads;
     const int group = a.heads / a.kv_heads;
     T* base = static_cast<T*>(is_k ? a.k_cache : a.v_cache) +
-              ((long long)sid * a.capacity + pos) * a.heads * kHeadDim;
+              ((long long)sid * a.capacity + cslot) * a.heads * kHeadDim;
     for (int rep = 0; rep < group; ++rep) {
         T* dst = base + (long long)(g * group + rep) * kHeadDim;
         dst[2 * i] = from_f32<T>(y0);
