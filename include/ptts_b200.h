@@ -54,6 +54,7 @@ extern "C" {
 
 typedef struct ptts_b200_kv ptts_b200_kv;
 typedef struct ptts_b200_model ptts_b200_model;
+typedef struct ptts_b200_flow ptts_b200_flow; /* the flow head, see "Flow head" below */
 
 /* Shape of a flow-LM transformer: FlowLMConfig (ptts/src/flow_lm.rs:114-146) and the
  * transformer arguments of StreamingTransformer::load (transformer.rs:680-717). */
@@ -201,8 +202,55 @@ int ptts_b200_linear_i8(int device, const void* x, const int8_t* w, const float*
  * (transformer.rs:699-707). */
 int ptts_b200_model_create(int device, const ptts_b200_config* config, ptts_b200_model** out);
 void ptts_b200_model_destroy(ptts_b200_model* model);
+/* The shape the model was created with. */
+int ptts_b200_model_config(const ptts_b200_model* model, ptts_b200_config* out);
 int ptts_b200_model_load_layer(ptts_b200_model* model, int layer,
                                const ptts_b200_layer_weights* weights);
+
+/* A layer from dense f32 linears [out][in] (HOST pointers), e.g. a safetensors checkpoint. The
+ * device keeps two f16 planes per linear, f16(W / s) and f16(W / s - hi) with s a power of two
+ * per output row: exact to 22 significant bits (every q8_0 weight exactly). Such layers run on
+ * the tcgen05 linears at every row count. */
+typedef struct {
+    const float* in_proj_host;
+    const float* out_proj_host;
+    const float* linear1_host;
+    const float* linear2_host;
+    const float* norm1_weight_host;
+    const float* norm1_bias_host;
+    const float* norm2_weight_host;
+    const float* norm2_bias_host;
+} ptts_b200_layer_weights_f32;
+int ptts_b200_model_load_layer_f32(ptts_b200_model* model, int layer,
+                                   const ptts_b200_layer_weights_f32* weights);
+
+/* A layer from GGUF q8_0 linears (the reference's model.q8.gguf, examples/quantize.rs:46-47):
+ * each weight [out][in] as rows of in/32 blocks of 34 bytes, an f16 scale d then 32 int8 q,
+ * W = q * d (kernels.js:252, :302). Dequantized exactly into the planes above. */
+typedef struct {
+    const void* in_proj_q8_0;
+    const void* out_proj_q8_0;
+    const void* linear1_q8_0;
+    const void* linear2_q8_0;
+    const float* norm1_weight_host;
+    const float* norm1_bias_host;
+    const float* norm2_weight_host;
+    const float* norm2_bias_host;
+} ptts_b200_layer_weights_q8_0;
+int ptts_b200_model_load_layer_q8_0(ptts_b200_model* model, int layer,
+                                    const ptts_b200_layer_weights_q8_0* weights);
+
+/* Load a GGUF checkpoint (load_weights, loader.rs:58-67): keys go through the reference's
+ * remap_key (loader.rs:15-39: flow_lm.backbone. -> flow_lm.transformer., flow_lm.flow. ->
+ * flow_lm.flow_net., ...). Every layer of `model` from flow_lm.transformer.layers.{i}.{self_attn.
+ * in_proj, self_attn.out_proj, linear1, linear2}.weight (q8_0, f32, f16 or bf16) and norm1/2;
+ * when `flow` is not NULL, every flow-head tensor from flow_lm.<name> and then
+ * ptts_b200_flow_finish. Refused, naming the tensor, when one is missing or misshaped. */
+int ptts_b200_load_gguf(ptts_b200_model* model, ptts_b200_flow* flow, const char* path);
+/* remap_key alone (no device needed): 1 and the new name in `out` (NUL-terminated, at most
+ * out_size bytes) when the tensor is kept, 0 when it is dropped, PTTS_B200_ERR_ARG when `out`
+ * is too small. */
+int ptts_b200_gguf_remap_key(const char* name, char* out, int out_size);
 
 /* StreamingTransformer::forward (transformer.rs:742-808) for a ragged batch of independent
  * streams: x [n_rows][d_model] bf16 (device) -> y [n_rows][d_model] f32 (device); per layer
@@ -271,7 +319,6 @@ int ptts_b200_trace_read(ptts_b200_trace* out, int reset);
  * drifting: one evaluation; pointwise: noise + one evaluation), plus input_linear, which turns
  * the previous latent (or bos_emb) into the next backbone input. z_proj is not supported: the
  * head reads the d_model-wide backbone output (z_dim absent, as in the phonon checkpoints). */
-typedef struct ptts_b200_flow ptts_b200_flow;
 
 enum { PTTS_B200_FLOW_LSD = 0, PTTS_B200_FLOW_DRIFTING = 1, PTTS_B200_FLOW_POINTWISE = 2 };
 enum { PTTS_B200_TIME_RMS = 0, PTTS_B200_TIME_RMS_VAR = 1 };

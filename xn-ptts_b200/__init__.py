@@ -45,6 +45,8 @@ EXPORTS = (
     "ptts_b200_flow_create", "ptts_b200_flow_destroy", "ptts_b200_flow_set_tensor",
     "ptts_b200_flow_finish", "ptts_b200_flow_sample", "ptts_b200_frame",
     "ptts_b200_kv_start_ring", "ptts_b200_kv_set_ring_slot", "ptts_b200_kv_evict",
+    "ptts_b200_model_config", "ptts_b200_model_load_layer_f32", "ptts_b200_model_load_layer_q8_0",
+    "ptts_b200_load_gguf", "ptts_b200_gguf_remap_key",
 )
 
 
@@ -71,6 +73,16 @@ class Config(ctypes.Structure):
                 ("num_kv_heads", ctypes.c_int32), ("head_dim", ctypes.c_int32),
                 ("num_layers", ctypes.c_int32), ("dim_feedforward", ctypes.c_int32),
                 ("max_period", ctypes.c_float), ("gelu", ctypes.c_int32)]
+
+
+class LayerWeightsF32(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_void_p) for n in (
+        "in_proj", "out_proj", "linear1", "linear2", "norm1_weight", "norm1_bias", "norm2_weight", "norm2_bias")]
+
+
+class LayerWeightsQ8(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_void_p) for n in (
+        "in_proj", "out_proj", "linear1", "linear2", "norm1_weight", "norm1_bias", "norm2_weight", "norm2_bias")]
 
 
 class FlowConfigC(ctypes.Structure):
@@ -135,6 +147,11 @@ def lib() -> ctypes.CDLL:
         L.ptts_b200_forward.argtypes = [P, P, P, IP, IP, I, P, P]
         L.ptts_b200_step.argtypes = [P, P, IP, I, P, P, P]
         L.ptts_b200_attend_decode_noalloc.argtypes = [P, P, I, I, I, P, P, I, P, P, P, I, I, F, P, I, P, P]
+        L.ptts_b200_model_config.argtypes = [P, ctypes.POINTER(Config)]
+        L.ptts_b200_model_load_layer_f32.argtypes = [P, I, ctypes.POINTER(LayerWeightsF32)]
+        L.ptts_b200_model_load_layer_q8_0.argtypes = [P, I, ctypes.POINTER(LayerWeightsQ8)]
+        L.ptts_b200_load_gguf.argtypes = [P, P, ctypes.c_char_p]
+        L.ptts_b200_gguf_remap_key.argtypes = [ctypes.c_char_p, ctypes.c_char_p, I]
         L.ptts_b200_kv_start_ring.argtypes = [P, IP, I, P]
         L.ptts_b200_kv_set_ring_slot.argtypes = [P, I, I, P]
         L.ptts_b200_kv_evict.argtypes = [P, I, I, IP, I, F, P]
@@ -447,6 +464,25 @@ class Transformer:
         for l in range(self.cfg.num_layers):
             self.load_layer(l, weights.layer(l))
 
+    _DENSE = ("in_proj", "out_proj", "linear1", "linear2", "norm1_weight", "norm1_bias", "norm2_weight",
+              "norm2_bias")
+
+    def load_layer_f32(self, layer: int, w: dict):
+        """Dense f32 linears [out][in] (ptts_b200_model_load_layer_f32); keys as load_layer's."""
+        keep = {k: np.ascontiguousarray(w[k], dtype=np.float32) for k in self._DENSE}
+        lw = LayerWeightsF32(*[keep[n].ctypes.data for n in self._DENSE])
+        _check(lib().ptts_b200_model_load_layer_f32(self._h, layer, ctypes.byref(lw)))
+
+    def load_layer_q8_0(self, layer: int, w: dict):
+        """GGUF q8_0 block bytes for the four linears (uint8 arrays), f32 norms."""
+        keep = {k: np.ascontiguousarray(w[k]) for k in self._DENSE}
+        lw = LayerWeightsQ8(*[keep[n].ctypes.data for n in self._DENSE])
+        _check(lib().ptts_b200_model_load_layer_q8_0(self._h, layer, ctypes.byref(lw)))
+
+    def load_gguf(self, path: str, flow: "Flow" = None):
+        """ptts_b200_load_gguf: every layer (and the flow head's tensors) from a GGUF file."""
+        _check(lib().ptts_b200_load_gguf(self._h, flow._h if flow is not None else P(), path.encode()))
+
     def forward(self, kv: KvState, x, streams: Sequence[int], rows: Sequence[int], *, out=None,
                 stream=None):
         """StreamingTransformer::forward: x [n_rows, d] bf16 -> [n_rows, d] f32; lengths advance."""
@@ -679,3 +715,12 @@ class Flow:
         _check(lib().ptts_b200_frame(model._h, self._h, kv.handle, _ip(s), n, lat, _dptr(noise),
                                      _dptr(out), _dptr(eos), _stream(stream)))
         return out, eos
+
+
+def gguf_remap_key(name: str):
+    """loader.rs remap_key through the library: the new name, or None when dropped."""
+    buf = ctypes.create_string_buffer(4096)
+    rc = lib().ptts_b200_gguf_remap_key(name.encode(), buf, len(buf))
+    if rc < 0:
+        _check(rc)
+    return buf.value.decode() if rc == 1 else None

@@ -155,6 +155,9 @@ struct ptts_b200_model {
     struct Layer {
         DevBuf w_qkv, s_qkv, w_out, s_out, w1, s1, w2, s2, ln1g, ln1b, ln2g, ln2b;
         DevBuf h_qkv, h_out, h1, h2;  // the int8 weights as f16 (exact), read by the tcgen05 linears
+        // Layers loaded from f32 or q8_0 weights have no int8 copy: h_* hold f16(W / s_row) and
+        // l_* the f16 remainders, s_row a power of two per output row (in s_*).
+        DevBuf l_qkv, l_out, l1, l2;
         bool loaded = false;
     };
     std::vector<std::unique_ptr<Layer>> layers;
@@ -377,7 +380,7 @@ void run_layers(const ptts_b200_model* m, const ptts_b200_kv* kv, bool decode, c
         pending = 0;
     };
     auto residual_gemm = [&](const void* a_hi, const void* a_lo, const DevBuf& wq, const DevBuf& wh,
-                             const DevBuf& sc, int k, int splits) {
+                             const DevBuf& wl, const DevBuf& sc, int k, int splits) {
         LinearArgs o{};
         o.M = rows;
         o.N = c.d_model;
@@ -387,10 +390,12 @@ void run_layers(const ptts_b200_model* m, const ptts_b200_kv* kv, bool decode, c
         o.a_lo = a_lo;
         o.w = wq.as<int8_t>();
         o.wh = wh.as<__half>();
+        o.wh_lo = wl.p;
         o.scale = sc.as<float>();
         o.y = splits > 1 ? split : resid;
         o.err = err;
-        launch_linear(o, splits > 1 ? EPI_PARTIAL : EPI_RESID, s);
+        require(launch_linear(o, splits > 1 ? EPI_PARTIAL : EPI_RESID, s), PTTS_B200_ERR_UNSUPPORTED,
+                "no kernel for this linear's shape");
         check_launch();
         if (splits > 1) pending = splits;
     };
@@ -406,6 +411,7 @@ void run_layers(const ptts_b200_model* m, const ptts_b200_kv* kv, bool decode, c
         a.a_lo = h_lo;
         a.w = L.w_qkv.as<int8_t>();
         a.wh = L.h_qkv.as<__half>();
+        a.wh_lo = L.l_qkv.p;
         a.scale = L.s_qkv.as<float>();
         a.yq = w.q_rot.as<float>();
         a.row_stream = plan.row_stream;
@@ -420,7 +426,7 @@ void run_layers(const ptts_b200_model* m, const ptts_b200_kv* kv, bool decode, c
         require(m->rope_rows >= kv->capacity, PTTS_B200_ERR_STATE, "RoPE table shorter than the cache");
         a.rope = m->rope.as<float2>();
         a.err = err;
-        launch_linear(a, EPI_QKV, s);
+        require(launch_linear(a, EPI_QKV, s), PTTS_B200_ERR_UNSUPPORTED, "no kernel for in_proj's shape");
         check_launch();
         // attention over the cache
         if (attn_ev) CK(cudaEventRecord(attn_ev[2 * l], s));
@@ -428,7 +434,7 @@ void run_layers(const ptts_b200_model* m, const ptts_b200_kv* kv, bool decode, c
                   kOutHiLo, w.part, w.counters, tiles, s);
         if (attn_ev) CK(cudaEventRecord(attn_ev[2 * l + 1], s));
         // out_proj + residual
-        residual_gemm(w.attn_hi.as<__half>(), w.attn_lo.as<__half>(), L.w_out, L.h_out, L.s_out,
+        residual_gemm(w.attn_hi.as<__half>(), w.attn_lo.as<__half>(), L.w_out, L.h_out, L.l_out, L.s_out,
                       hd, s_out);
         // LN2, linear1 + GELU
         ln(L.ln2g.as<float>(), L.ln2b.as<float>(), nullptr, true);
@@ -440,15 +446,16 @@ void run_layers(const ptts_b200_model* m, const ptts_b200_kv* kv, bool decode, c
         f1.a_lo = h_lo;
         f1.w = L.w1.as<int8_t>();
         f1.wh = L.h1.as<__half>();
+        f1.wh_lo = L.l1.p;
         f1.scale = L.s1.as<float>();
         f1.yb = w.ff_hi.as<__half>();
         f1.yb_lo = w.ff_lo.as<__half>();
         f1.gelu_tanh = c.gelu;
         f1.err = err;
-        launch_linear(f1, EPI_GELU, s);
+        require(launch_linear(f1, EPI_GELU, s), PTTS_B200_ERR_UNSUPPORTED, "no kernel for linear1's shape");
         check_launch();
         // linear2 + residual
-        residual_gemm(w.ff_hi.as<__half>(), w.ff_lo.as<__half>(), L.w2, L.h2, L.s2,
+        residual_gemm(w.ff_hi.as<__half>(), w.ff_lo.as<__half>(), L.w2, L.h2, L.l2, L.s2,
                       c.dim_feedforward, s_ff2);
     }
     if (pending) ln(nullptr, nullptr, nullptr, false);
@@ -465,6 +472,95 @@ void ensure_rope(ptts_b200_model* m, int rows, cudaStream_t s) {
     launch_rope_table(f, static_cast<float2*>(m->rope.need(sizeof(float2) * kMaxPairs * (size_t)rows)), rows, s);
     check_launch();
     m->rope_rows = rows;
+}
+
+// f32 -> f16 bits, round to nearest even, subnormals included (|x| <= 65504 here).
+uint16_t f16_bits(float f) {
+    uint32_t u;
+    std::memcpy(&u, &f, 4);
+    const uint32_t sign = (u >> 16) & 0x8000u;
+    const int exp = (int)((u >> 23) & 0xFF) - 127 + 15;
+    uint32_t man = u & 0x7FFFFFu;
+    if (((u >> 23) & 0xFF) == 0) return (uint16_t)sign;  // f32 zero or subnormal -> 0
+    if (exp >= 31) return (uint16_t)(sign | 0x7C00u);
+    if (exp <= 0) {  // f16 subnormal: value = man16 * 2^-24
+        if (exp < -10) return (uint16_t)sign;
+        man |= 0x800000u;
+        const int shift = 14 - exp;  // bits dropped from the 24-bit significand
+        uint32_t q = man >> shift;
+        const uint32_t rem = man & ((1u << shift) - 1), half = 1u << (shift - 1);
+        if (rem > half || (rem == half && (q & 1u))) ++q;
+        return (uint16_t)(sign | q);
+    }
+    uint32_t q = ((uint32_t)exp << 10) | (man >> 13);
+    const uint32_t rem = man & 0x1FFFu;
+    if (rem > 0x1000u || (rem == 0x1000u && (q & 1u))) ++q;  // may carry into the exponent
+    return (uint16_t)(sign | q);
+}
+// A linear of f32 weights [n][k] as f16 planes: hi = f16(W / s), lo = f16(W / s - hi) with
+// s = 2^ceil(log2(max |W_row|)) per row, so W/s is exact to 22 significant bits for weights
+// within 2^-14 of their row's largest (q8_0 weights, 18 bits, are exact); lo is dropped when it
+// is all zero.
+void upload_dense(DevBuf& hi, DevBuf& lo, DevBuf& scale, const float* w, size_t n, size_t k) {
+    std::vector<uint16_t> h(n * k), l(n * k);
+    std::vector<float> sc(n);
+    bool any_lo = false;
+    for (size_t r = 0; r < n; ++r) {
+        float amax = 0.f;
+        for (size_t c = 0; c < k; ++c) amax = std::max(amax, std::fabs(w[r * k + c]));
+        require(std::isfinite(amax), PTTS_B200_ERR_ARG, "a weight is not finite");
+        int e = 0;
+        if (amax > 0.f) std::frexp(amax, &e);  // amax = f * 2^e, 0.5 <= f < 1
+        sc[r] = std::ldexp(1.0f, e);
+        for (size_t c = 0; c < k; ++c) {
+            const float x = std::ldexp(w[r * k + c], -e);
+            h[r * k + c] = f16_bits(x);
+            l[r * k + c] = f16_bits(x - f16_value(h[r * k + c]));
+            any_lo = any_lo || (l[r * k + c] & 0x7FFFu) != 0;
+        }
+    }
+    CK(cudaMemcpy(hi.need(n * k * 2), h.data(), n * k * 2, cudaMemcpyHostToDevice));
+    if (any_lo) CK(cudaMemcpy(lo.need(n * k * 2), l.data(), n * k * 2, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(scale.need(n * 4), sc.data(), n * 4, cudaMemcpyHostToDevice));
+}
+
+// GGUF q8_0 blocks (34 bytes: f16 d, then 32 int8 q) of an [n][k] weight -> f32 W = q * d.
+std::vector<float> dequant_q8_0(const void* blocks, size_t n, size_t k) {
+    std::vector<float> w(n * k);
+    const unsigned char* b = static_cast<const unsigned char*>(blocks);
+    for (size_t i = 0; i < n * k / 32; ++i, b += 34) {
+        uint16_t d16;
+        std::memcpy(&d16, b, 2);
+        const float d = f16_value(d16);
+        for (int j = 0; j < 32; ++j) w[i * 32 + j] = (float)(int8_t)b[2 + j] * d;
+    }
+    return w;
+}
+
+// A layer from f32 linears: the f16 planes above, no int8 copy.
+void load_dense_layer(ptts_b200_model* model, int layer, const float* in_proj, const float* out_proj,
+                      const float* linear1, const float* linear2, const float* n1w, const float* n1b,
+                      const float* n2w, const float* n2b) {
+    require(layer >= 0 && layer < model->cfg.num_layers, PTTS_B200_ERR_ARG, "layer out of range");
+    require(in_proj && out_proj && linear1 && linear2 && n1w && n1b && n2w && n2b, PTTS_B200_ERR_ARG,
+            "a weight pointer is NULL");
+    const ptts_b200_config& c = model->cfg;
+    const size_t dm = c.d_model, hd = (size_t)c.num_heads * c.head_dim;
+    const size_t nqkv = hd + 2 * (size_t)c.num_kv_heads * c.head_dim, ff = c.dim_feedforward;
+    DeviceScope scope(model->device);
+    auto& L = *model->layers[layer];
+    for (DevBuf* b : {&L.w_qkv, &L.w_out, &L.w1, &L.w2, &L.l_qkv, &L.l_out, &L.l1, &L.l2}) b->release();
+    upload_dense(L.h_qkv, L.l_qkv, L.s_qkv, in_proj, nqkv, dm);
+    upload_dense(L.h_out, L.l_out, L.s_out, out_proj, dm, hd);
+    upload_dense(L.h1, L.l1, L.s1, linear1, ff, dm);
+    upload_dense(L.h2, L.l2, L.s2, linear2, dm, ff);
+    auto put = [](DevBuf& b, const void* src, size_t n) { CK(cudaMemcpy(b.need(n), src, n, cudaMemcpyHostToDevice)); };
+    put(L.ln1g, n1w, dm * 4);
+    put(L.ln1b, n1b, dm * 4);
+    put(L.ln2g, n2w, dm * 4);
+    put(L.ln2b, n2b, dm * 4);
+    CK(cudaDeviceSynchronize());
+    L.loaded = true;
 }
 
 bool is_device_pointer(const void* p) {
@@ -774,7 +870,8 @@ int ptts_b200_linear_i8(int device, const void* x, const int8_t* w, const float*
         a.w = w;
         a.scale = scale;
         a.y = y;
-        launch_linear(a, EPI_F32, as_stream(cuda_stream));
+        require(launch_linear(a, EPI_F32, as_stream(cuda_stream)), PTTS_B200_ERR_UNSUPPORTED,
+                "no kernel for this linear's shape");
         check_launch();
     });
 }
@@ -852,6 +949,7 @@ int ptts_b200_model_load_layer(ptts_b200_model* model, int layer,
         put(L.ln1b, w->norm1_bias_host, dm * 4);
         put(L.ln2g, w->norm2_weight_host, dm * 4);
         put(L.ln2b, w->norm2_bias_host, dm * 4);
+        for (DevBuf* b : {&L.l_qkv, &L.l_out, &L.l1, &L.l2}) b->release();  // int8 layers: one plane
         auto widen = [](DevBuf& h, const DevBuf& q, size_t n) {
             launch_i8_to_f16(q.as<int8_t>(), static_cast<__half*>(h.need(n * 2)), (long long)n, nullptr);
         };
@@ -862,6 +960,38 @@ int ptts_b200_model_load_layer(ptts_b200_model* model, int layer,
         check_launch();
         CK(cudaDeviceSynchronize());
         L.loaded = true;
+    });
+}
+
+int ptts_b200_model_config(const ptts_b200_model* model, ptts_b200_config* out) {
+    return guarded([&] {
+        require(model && out, PTTS_B200_ERR_ARG, "NULL argument");
+        *out = model->cfg;
+    });
+}
+
+int ptts_b200_model_load_layer_f32(ptts_b200_model* model, int layer, const ptts_b200_layer_weights_f32* w) {
+    return guarded([&] {
+        require(model && w, PTTS_B200_ERR_ARG, "NULL argument");
+        load_dense_layer(model, layer, w->in_proj_host, w->out_proj_host, w->linear1_host, w->linear2_host,
+                         w->norm1_weight_host, w->norm1_bias_host, w->norm2_weight_host, w->norm2_bias_host);
+    });
+}
+
+int ptts_b200_model_load_layer_q8_0(ptts_b200_model* model, int layer, const ptts_b200_layer_weights_q8_0* w) {
+    return guarded([&] {
+        require(model && w, PTTS_B200_ERR_ARG, "NULL argument");
+        require(w->in_proj_q8_0 && w->out_proj_q8_0 && w->linear1_q8_0 && w->linear2_q8_0, PTTS_B200_ERR_ARG,
+                "a weight pointer is NULL");
+        const ptts_b200_config& c = model->cfg;
+        const size_t dm = c.d_model, hd = (size_t)c.num_heads * c.head_dim;
+        const size_t nqkv = hd + 2 * (size_t)c.num_kv_heads * c.head_dim, ff = c.dim_feedforward;
+        require(dm % 32 == 0 && hd % 32 == 0 && ff % 32 == 0, PTTS_B200_ERR_UNSUPPORTED,
+                "q8_0 needs every input width to be a multiple of 32");
+        const auto qkv = dequant_q8_0(w->in_proj_q8_0, nqkv, dm), out = dequant_q8_0(w->out_proj_q8_0, dm, hd);
+        const auto l1 = dequant_q8_0(w->linear1_q8_0, ff, dm), l2 = dequant_q8_0(w->linear2_q8_0, dm, ff);
+        load_dense_layer(model, layer, qkv.data(), out.data(), l1.data(), l2.data(), w->norm1_weight_host,
+                         w->norm1_bias_host, w->norm2_weight_host, w->norm2_bias_host);
     });
 }
 

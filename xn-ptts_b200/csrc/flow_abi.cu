@@ -284,6 +284,11 @@ void sample(ptts_b200_flow* f, const float* src, bool normalise, int n, const fl
 
 }  // namespace
 
+// Whether `name` is one of this flow head's tensors (for the GGUF loader, gguf.cu).
+bool ptts_b200_flow_wants(const ptts_b200_flow* flow, const std::string& name) {
+    return flow && (name == "condition" || flow->expected.count(name) != 0);
+}
+
 extern "C" {
 
 int ptts_b200_flow_create(int device, const ptts_b200_flow_config* config, ptts_b200_flow** out) {

@@ -5,6 +5,8 @@
 
 #include <cuda_runtime.h>
 
+#include <cmath>
+#include <cstdint>
 #include <cstring>
 #include <exception>
 #include <string>
@@ -84,6 +86,15 @@ struct DevBuf {
         bytes = n;
         return p;
     }
+    // Free the memory (the buffer reads as empty again).
+    void release() {
+        if (p) {
+            CK(cudaDeviceSynchronize());
+            CK(cudaFree(p));
+        }
+        p = nullptr;
+        bytes = 0;
+    }
     template <class T>
     T* as() const {
         return static_cast<T*>(p);
@@ -127,6 +138,20 @@ struct Staging {
         CK(cudaEventRecord(done[i], s));
     }
 };
+
+// f16 bits -> f32 (exact; subnormals, infinities and NaN included).
+inline float f16_value(uint16_t h) {
+    const uint32_t sign = (uint32_t)(h & 0x8000u) << 16, exp = (h >> 10) & 0x1F, man = h & 0x3FFu;
+    float v;
+    if (exp == 0) v = std::ldexp((float)man, -24);
+    else if (exp == 31) v = man ? NAN : INFINITY;
+    else v = std::ldexp((float)(man | 0x400u), (int)exp - 25);
+    uint32_t u;
+    std::memcpy(&u, &v, 4);
+    u |= sign;
+    std::memcpy(&v, &u, 4);
+    return v;
+}
 
 }  // namespace host
 }  // namespace ptts

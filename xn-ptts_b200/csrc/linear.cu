@@ -450,13 +450,17 @@ void launch_typed(const LinearArgs& a, cudaStream_t s) {
 
 }  // namespace
 
-void launch_linear(const LinearArgs& a, LinearEpi epi, cudaStream_t s) {
-    // Default: tcgen05 below 4096 rows (decode and short prompts), mma.sync above, where its four
-    // CTAs per SM overlap epilogues with main loops. PTTS_B200_GEMM=mma / =tc force one kernel.
+bool launch_linear(const LinearArgs& a, LinearEpi epi, cudaStream_t s) {
+    // Weights without an int8 copy (f32 or q8_0 layers: two f16 planes) only have the tcgen05
+    // kernel. Otherwise: tcgen05 below 4096 rows (decode and short prompts), mma.sync above,
+    // where its four CTAs per SM overlap epilogues with main loops. PTTS_B200_GEMM=mma / =tc
+    // force one kernel where both exist.
+    if (a.w == nullptr) return launch_linear_tc(a, epi, s);
     const char* sel = getenv("PTTS_B200_GEMM");
     const bool use_tc = sel && sel[0] == 'm' ? false : (sel && sel[0] == 't') || a.M < 4096;
-    if (use_tc && launch_linear_tc(a, epi, s)) return;
+    if (use_tc && launch_linear_tc(a, epi, s)) return true;
     launch_linear_mma(a, epi, s);
+    return true;
 }
 
 void launch_linear_mma(const LinearArgs& a, LinearEpi epi, cudaStream_t s) {

@@ -500,6 +500,8 @@ bool launch_tma(const LinearArgs& a, cudaStream_t s) {
 
 template <int EPI>
 bool launch_tma_rows(const LinearArgs& a, cudaStream_t s) {
+    if (a.wh_lo)  // f16 hi/lo weight planes (f32 or q8_0 layers)
+        return a.M < 4096 ? launch_tma<EPI, 32, true>(a, s) : launch_tma<EPI, 128, true>(a, s);
     return a.M < 4096 ? launch_tma<EPI, 32, false>(a, s) : launch_tma<EPI, 128, false>(a, s);
 }
 
@@ -519,7 +521,7 @@ bool linear_tc_supported(const LinearArgs& a) {
 bool launch_linear_tc(const LinearArgs& a, LinearEpi epi, cudaStream_t s) {
     if (!linear_tc_supported(a)) return false;
     const bool flow_epi = epi >= EPI_BIAS;
-    if (!flow_epi && (!a.a_f16 || a.wh_lo)) return false;  // the layer stack's linears: f16, one weight plane
+    if (!flow_epi && !a.a_f16) return false;  // the layer stack's linears read f16 planes
     switch (epi) {
         case EPI_F32: return launch_tma_rows<EPI_F32>(a, s);
         case EPI_QKV: return launch_tma_rows<EPI_QKV>(a, s);
