@@ -155,6 +155,17 @@ int ptts_b200_kv_check(ptts_b200_kv* kv);
  * step, attend + kv_advance); prompts, load_prefix, copy_stream and set_lengths refuse them;
  * kv_reset turns them back into appended streams. Refusals leave the cache as it was. */
 
+/* ---- Windowed streams: Mimi's KvCache with a context (transformer.rs:257-317, :395-468) -----
+ * A windowed stream's position (its length) grows without bound; position p is stored at slot
+ * p % capacity and a query at p attends positions max(0, p - context + 1) .. p (the mask of
+ * transformer.rs:762-785, with the cache trimmed to context - 1 rows between calls). A call
+ * adds at most capacity - context + 1 rows to it, so no row a query reads is overwritten.
+ * Windowed streams run through ptts_b200_attend (+ kv_advance); the layer stack, rings,
+ * load_prefix and set_lengths refuse them; copy_stream copies them whole into a stream of the
+ * same capacity; kv_reset makes them appended streams again. */
+int ptts_b200_kv_set_window(ptts_b200_kv* kv, const int32_t* streams_host, int n, int context,
+                            void* cuda_stream);
+
 /* Every listed stream becomes a ring: its rows so far stay, the write slot is its length. */
 int ptts_b200_kv_start_ring(ptts_b200_kv* kv, const int32_t* streams_host, int n, void* cuda_stream);
 /* The slot of a ring stream's next row, 0 <= slot < capacity. */

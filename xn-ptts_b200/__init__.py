@@ -46,7 +46,7 @@ EXPORTS = (
     "ptts_b200_flow_finish", "ptts_b200_flow_sample", "ptts_b200_frame",
     "ptts_b200_kv_start_ring", "ptts_b200_kv_set_ring_slot", "ptts_b200_kv_evict",
     "ptts_b200_model_config", "ptts_b200_model_load_layer_f32", "ptts_b200_model_load_layer_q8_0",
-    "ptts_b200_load_gguf", "ptts_b200_gguf_remap_key",
+    "ptts_b200_load_gguf", "ptts_b200_gguf_remap_key", "ptts_b200_kv_set_window",
 )
 
 
@@ -152,6 +152,7 @@ def lib() -> ctypes.CDLL:
         L.ptts_b200_model_load_layer_q8_0.argtypes = [P, I, ctypes.POINTER(LayerWeightsQ8)]
         L.ptts_b200_load_gguf.argtypes = [P, P, ctypes.c_char_p]
         L.ptts_b200_gguf_remap_key.argtypes = [ctypes.c_char_p, ctypes.c_char_p, I]
+        L.ptts_b200_kv_set_window.argtypes = [P, IP, I, I, P]
         L.ptts_b200_kv_start_ring.argtypes = [P, IP, I, P]
         L.ptts_b200_kv_set_ring_slot.argtypes = [P, I, I, P]
         L.ptts_b200_kv_evict.argtypes = [P, I, I, IP, I, F, P]
@@ -263,6 +264,11 @@ class KvState:
     def reset(self, streams: Sequence[int], stream=None):
         s = _i32(streams)
         _check(lib().ptts_b200_kv_reset(self._h, _ip(s), len(s), _stream(stream)))
+
+    def set_window(self, streams: Sequence[int], context: int, stream=None):
+        """Mimi's KvCache::new(context) for these (empty) streams (ptts_b200_kv_set_window)."""
+        st = _i32(streams)
+        _check(lib().ptts_b200_kv_set_window(self._h, _ip(st), len(st), context, _stream(stream)))
 
     def start_ring(self, streams: Sequence[int], stream=None):
         """StreamingTransformer::start_ring for these streams (ptts_b200_kv_start_ring)."""

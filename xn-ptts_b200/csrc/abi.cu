@@ -104,6 +104,9 @@ struct ptts_b200_kv {
     DevBuf ring_write, ring_filled, ring_valid;
     std::vector<int32_t> h_ring_write, h_ring_filled;
     std::vector<uint8_t> h_ring_valid;
+    // Windowed streams (Mimi's KvCache, transformer.rs:257-317): the context, 0 = none.
+    DevBuf window;
+    std::vector<int32_t> h_window;
     // scratch of the attention op
     DevBuf seq_stream, row_offsets, row_stream, row_pos, prefix, part, q_rot, counters, tiles;
     Staging staging;
@@ -118,9 +121,11 @@ struct ptts_b200_kv {
         r.write = ring_write.as<int32_t>();
         r.filled = ring_filled.as<int32_t>();
         r.valid = ring_valid.as<uint8_t>();
+        r.window = window.as<int32_t>();
         return r;
     }
     bool is_ring(int s) const { return h_ring_write[s] >= 0; }
+    bool is_window(int s) const { return h_window[s] > 0; }
     // The host mirror after a row went into stream s's write slot (RingSlots in complete_kv).
     void ring_commit(int s) {
         const int w = h_ring_write[s];
@@ -215,7 +220,15 @@ int check_sequences(const ptts_b200_kv* kv, const int32_t* streams, const int32_
                         std::to_string(s) + ")");
         }
         const long long need = (long long)kv->h_len[s] + rows[i];
-        if (need > kv->capacity)
+        if (kv->is_window(s)) {  // positions grow past the capacity; the window must not wrap
+            const int w = kv->h_window[s];      // onto keys the call still reads
+            if (rows[i] > kv->capacity - w + 1)
+                fail(PTTS_B200_ERR_CAPACITY, "a window of " + std::to_string(w) + " positions over " +
+                                                 std::to_string(kv->capacity) + " slots takes at most " +
+                                                 std::to_string(kv->capacity - w + 1) + " rows per call, not " +
+                                                 std::to_string(rows[i]) + " (stream " + std::to_string(s) + ")");
+            require(need < (1LL << 31), PTTS_B200_ERR_CAPACITY, "stream position overflow");
+        } else if (need > kv->capacity)
             fail(PTTS_B200_ERR_CAPACITY, "cannot fit " + std::to_string(need) +
                                              " filled KV positions into a budget of " +
                                              std::to_string(kv->capacity) + " (stream " +
@@ -229,6 +242,23 @@ int check_sequences(const ptts_b200_kv* kv, const int32_t* streams, const int32_
 
 // A call with a prompt (some sequence of more than one row) plans rows by position; a ring
 // stream's row must go to its write slot, so ring streams only join all-decode calls.
+// Keys the next decode row of stream st attends (the decode plan's count; tracing only).
+long long attended_keys(const ptts_b200_kv* kv, int st) {
+    const long long len = kv->h_len[st];
+    if (kv->is_window(st)) return std::min<long long>(len + 1, kv->h_window[st]);
+    if (kv->is_ring(st)) return std::max<long long>(kv->h_ring_filled[st], kv->h_ring_write[st] + 1);
+    return len + 1;
+}
+
+// The layer stack reads RoPE factors from a table of `capacity` positions, while a windowed
+// stream's position grows without bound: windowed streams run through the attention op.
+void refuse_window(const ptts_b200_kv* kv, const int32_t* streams, int n) {
+    for (int i = 0; i < n; ++i)
+        require(!kv->is_window(streams[i]), PTTS_B200_ERR_UNSUPPORTED,
+                "stream " + std::to_string(streams[i]) +
+                    " is windowed: windowed streams run through ptts_b200_attend, not the layer stack");
+}
+
 void refuse_ring_prompt(const ptts_b200_kv* kv, const int32_t* streams, int n, bool decode) {
     if (decode) return;
     for (int i = 0; i < n; ++i)
@@ -264,7 +294,7 @@ RowPlan make_plan(const ptts_b200_kv* kv, bool decode, const int32_t* d_seq_stre
                            plan, kv->ring(), kv->err.as<uint32_t>(), s);
     else
         launch_plan_rows(kv->len.as<int32_t>(), d_seq_stream, d_row_offsets, n_seq, n_rows,
-                         kv->streams, kv->capacity, plan, kv->err.as<uint32_t>(), s);
+                         kv->streams, kv->capacity, plan, kv->window.as<int32_t>(), kv->err.as<uint32_t>(), s);
     return plan;
 }
 
@@ -272,6 +302,7 @@ RowPlan make_plan(const ptts_b200_kv* kv, bool decode, const int32_t* d_seq_stre
 struct Tiles {
     const int2* dev = nullptr;
     int n = 0;
+    bool windowed = false;  // a windowed stream is in the call: the CUDA-core kernel maps its slots
 };
 
 void attention(const ptts_b200_kv* kv, int layer, bool decode, const RowPlan& plan, int n_rows,
@@ -299,6 +330,8 @@ void attention(const ptts_b200_kv* kv, int layer, bool decode, const RowPlan& pl
         a.ring_write = kv->ring_write.as<int32_t>();
         a.ring_valid = kv->ring_valid.as<uint8_t>();
         a.capacity = kv->capacity;
+        a.window = kv->window.as<int32_t>();
+        a.row_pos = plan.row_pos;
         launch_decode_attn(a, bf16, grid, s);
     } else {
         PrefillArgs a{};
@@ -307,6 +340,7 @@ void attention(const ptts_b200_kv* kv, int layer, bool decode, const RowPlan& pl
         a.stream_elems = (long long)kv->capacity * kRowWidth;
         a.row_stream = plan.row_stream;
         a.row_pos = plan.row_pos;
+        a.window = kv->window.as<int32_t>();
         a.q = q_rot;
         a.out = out;
         a.out_lo = out_lo;
@@ -314,7 +348,7 @@ void attention(const ptts_b200_kv* kv, int layer, bool decode, const RowPlan& pl
         a.rows = n_rows;
         a.qscale = qscale;
         a.err = kv->err.as<uint32_t>();
-        if (bf16 && tiles.n > 0 && prefill_on_tensor_cores())
+        if (bf16 && tiles.n > 0 && prefill_on_tensor_cores() && !tiles.windowed)
             launch_prefill_attn_tc(a, tiles.dev, tiles.n, s);
         else
             launch_prefill_attn(a, bf16, s);
@@ -617,6 +651,8 @@ int ptts_b200_kv_create(int device, int num_layers, int num_streams, int capacit
         kv->h_ring_write.assign(num_streams, -1);
         kv->h_ring_filled.assign(num_streams, 0);
         kv->h_ring_valid.assign((size_t)num_streams * capacity, 0);
+        CK(cudaMemset(kv->window.need(sizeof(int32_t) * num_streams), 0, sizeof(int32_t) * num_streams));
+        kv->h_window.assign(num_streams, 0);
         CK(cudaDeviceSynchronize());
         *out = kv.release();
     });
@@ -690,6 +726,10 @@ int ptts_b200_kv_reset(ptts_b200_kv* kv, const int32_t* streams_host, int n, voi
             const int st = streams_host[i];
             kv->h_len[st] = 0;
             if (kv->is_ring(st)) ring_clear(kv, st, s);  // back to an appended cache
+            if (kv->is_window(st)) {
+                kv->h_window[st] = 0;
+                kv->staging.upload(kv->window.as<int32_t>() + st, &kv->h_window[st], sizeof(int32_t), s);
+            }
         }
     });
 }
@@ -701,7 +741,8 @@ int ptts_b200_kv_load_prefix(ptts_b200_kv* kv, int layer, int stream, const void
         require(layer >= 0 && layer < kv->layers, PTTS_B200_ERR_ARG, "layer out of range");
         require(stream >= 0 && stream < kv->streams, PTTS_B200_ERR_ARG, "stream out of range");
         require(len >= 0, PTTS_B200_ERR_ARG, "negative length");
-        require(!kv->is_ring(stream), PTTS_B200_ERR_STATE, "a ring cache cannot load a prefix");
+        require(!kv->is_ring(stream) && !kv->is_window(stream), PTTS_B200_ERR_STATE,
+                "a ring or windowed cache cannot load a prefix");
         if (len > kv->capacity)
             fail(PTTS_B200_ERR_CAPACITY, "cannot fit " + std::to_string(len) +
                                              " filled KV positions into a budget of " +
@@ -735,6 +776,28 @@ int ptts_b200_kv_copy_stream(ptts_b200_kv* dst, int dst_stream, const ptts_b200_
                 PTTS_B200_ERR_ARG, "stream out of range");
         require(!src->is_ring(src_stream) && !dst->is_ring(dst_stream), PTTS_B200_ERR_STATE,
                 "a ring cache cannot be resized");  // transformer.rs:356-357
+        require(!dst->is_window(dst_stream), PTTS_B200_ERR_STATE, "the destination stream is windowed");
+        if (src->is_window(src_stream)) {
+            // Mimi caches are cloned as they are (transformer.rs:348-355): every slot, the
+            // position and the window, so the capacities must match.
+            require(dst->capacity == src->capacity, PTTS_B200_ERR_STATE,
+                    "a windowed cache is copied whole, into a stream of the same capacity");
+            DeviceScope scope(dst->device);
+            cudaStream_t s = as_stream(cuda_stream);
+            for (int l = 0; l < dst->layers; ++l) {
+                CK(cudaMemcpyAsync(dst->k_layer(l) + (size_t)dst_stream * dst->stream_bytes(),
+                                   src->k_layer(l) + (size_t)src_stream * src->stream_bytes(), dst->stream_bytes(),
+                                   cudaMemcpyDeviceToDevice, s));
+                CK(cudaMemcpyAsync(dst->v_layer(l) + (size_t)dst_stream * dst->stream_bytes(),
+                                   src->v_layer(l) + (size_t)src_stream * src->stream_bytes(), dst->stream_bytes(),
+                                   cudaMemcpyDeviceToDevice, s));
+            }
+            dst->h_len[dst_stream] = src->h_len[src_stream];
+            dst->h_window[dst_stream] = src->h_window[src_stream];
+            dst->staging.upload(dst->len.as<int32_t>() + dst_stream, &dst->h_len[dst_stream], sizeof(int32_t), s);
+            dst->staging.upload(dst->window.as<int32_t>() + dst_stream, &dst->h_window[dst_stream], sizeof(int32_t), s);
+            return;
+        }
         const int used = src->h_len[src_stream];
         if (used > dst->capacity)
             fail(PTTS_B200_ERR_CAPACITY, "cannot fit " + std::to_string(used) +
@@ -837,6 +900,7 @@ int ptts_b200_attend(ptts_b200_kv* kv, int layer, const void* q, const void* k, 
             tiles.dev = static_cast<int2*>(kv->tiles.need(sizeof(int2) * t.size()));
             tiles.n = (int)t.size();
             kv->staging.upload(const_cast<int2*>(tiles.dev), t.data(), sizeof(int2) * t.size(), s);
+            for (int i = 0; i < n_seq; ++i) tiles.windowed = tiles.windowed || kv->is_window(streams_host[i]);
         }
         attention(kv, layer, decode, plan, n_rows, ra.q_out, out, nullptr,
                   out_dtype == PTTS_B200_BF16 ? kOutBf16 : kOutF32, kv->part, kv->counters, tiles, s);
@@ -847,7 +911,7 @@ int ptts_b200_attend(ptts_b200_kv* kv, int layer, const void* q, const void* k, 
             CK(cudaEventElapsedTime(&ms, kv->trace_ev[0], kv->trace_ev[1]));
             double bytes = 0.0;
             for (int i = 0; i < n_seq; ++i)
-                bytes += (double)(kv->h_len[streams_host[i]] + 1) * kv->row_bytes * 2;
+                bytes += (double)attended_keys(kv, streams_host[i]) * kv->row_bytes * 2;
             bytes += (double)n_seq * kRowWidth * (4 + (out_dtype == PTTS_B200_BF16 ? 2 : 4));
             trace_add(1, ms, bytes, 0, 0.0);
         }
@@ -1006,6 +1070,7 @@ int ptts_b200_forward(ptts_b200_model* model, ptts_b200_kv* kv, const void* x,
         bool decode = true;
         for (int i = 0; i < n_seq; ++i) decode = decode && rows_host[i] == 1;
         refuse_ring_prompt(kv, streams_host, n_seq, decode);
+        refuse_window(kv, streams_host, n_seq);
         DeviceScope scope(model->device);
         cudaStream_t s = as_stream(cuda_stream);
         const ptts_b200_config& c = model->cfg;
@@ -1044,6 +1109,7 @@ int ptts_b200_step(ptts_b200_model* model, ptts_b200_kv* kv, const int32_t* stre
         require(x && y, PTTS_B200_ERR_ARG, "x/y are NULL");
         std::vector<int32_t> ones(n > 0 ? n : 0, 1), offsets;
         check_sequences(kv, streams_host, ones.data(), n, offsets);  // capacity for one more row
+        refuse_window(kv, streams_host, n);
         DeviceScope scope(model->device);
         cudaStream_t s = as_stream(cuda_stream);
         const ptts_b200_config& c = model->cfg;
@@ -1100,7 +1166,7 @@ int ptts_b200_step(ptts_b200_model* model, ptts_b200_kv* kv, const int32_t* stre
             CK(cudaEventRecord(ev[2 * L + 1], s));
             CK(cudaEventSynchronize(ev[2 * L + 1]));
             double bytes = 0.0;  // K and V rows read, f32 q read, bf16 output written
-            for (int i = 0; i < n; ++i) bytes += (double)(kv->h_len[streams_host[i]] + 1) * kv->row_bytes * 2;
+            for (int i = 0; i < n; ++i) bytes += (double)attended_keys(kv, streams_host[i]) * kv->row_bytes * 2;
             bytes += (double)n * kRowWidth * (4 + 2);
             double attn_ms = 0.0;
             for (int l = 0; l < L; ++l) {
@@ -1161,6 +1227,7 @@ int ptts_b200_kv_start_ring(ptts_b200_kv* kv, const int32_t* streams_host, int n
             const int st = streams_host[i];
             require(st >= 0 && st < kv->streams, PTTS_B200_ERR_ARG, "stream out of range");
             require(!kv->is_ring(st), PTTS_B200_ERR_STATE, "stream " + std::to_string(st) + " is already a ring");
+            require(!kv->is_window(st), PTTS_B200_ERR_STATE, "stream " + std::to_string(st) + " is windowed");
         }
         DeviceScope scope(kv->device);
         cudaStream_t s = as_stream(cuda_stream);
@@ -1177,6 +1244,29 @@ int ptts_b200_kv_start_ring(ptts_b200_kv* kv, const int32_t* streams_host, int n
             uint8_t* dv = kv->ring_valid.as<uint8_t>() + (size_t)st * kv->capacity;
             if (used > 0) CK(cudaMemsetAsync(dv, 1, used, s));
             if (used < kv->capacity) CK(cudaMemsetAsync(dv + used, 0, kv->capacity - used, s));
+        }
+    });
+}
+
+int ptts_b200_kv_set_window(ptts_b200_kv* kv, const int32_t* streams_host, int n, int context,
+                            void* cuda_stream) {
+    return guarded([&] {
+        check_kv(kv);
+        require(n > 0 && streams_host, PTTS_B200_ERR_ARG, "no streams");
+        require(context >= 1 && context <= kv->capacity, PTTS_B200_ERR_ARG,
+                "context must be in 1.." + std::to_string(kv->capacity) + " (the capacity)");
+        for (int i = 0; i < n; ++i) {
+            const int st = streams_host[i];
+            require(st >= 0 && st < kv->streams, PTTS_B200_ERR_ARG, "stream out of range");
+            require(!kv->is_ring(st), PTTS_B200_ERR_STATE, "stream " + std::to_string(st) + " is a ring");
+            require(kv->h_len[st] == 0, PTTS_B200_ERR_STATE,
+                    "stream " + std::to_string(st) + " is not empty (KvCache::new starts a window)");
+        }
+        DeviceScope scope(kv->device);
+        cudaStream_t s = as_stream(cuda_stream);
+        for (int i = 0; i < n; ++i) {
+            kv->h_window[streams_host[i]] = context;
+            kv->staging.upload(kv->window.as<int32_t>() + streams_host[i], &context, sizeof(int32_t), s);
         }
     });
 }
@@ -1255,6 +1345,8 @@ int ptts_b200_kv_set_lengths(ptts_b200_kv* kv, const int32_t* streams_host,
                     "stream out of range");
             require(!kv->is_ring(streams_host[i]), PTTS_B200_ERR_STATE,
                     "a ring cache drops rows by eviction (ptts_b200_kv_evict), not by length");
+            require(!kv->is_window(streams_host[i]), PTTS_B200_ERR_STATE,
+                    "a windowed cache keeps its position; reset it to start over");
             if (lengths_host[i] < 0 || lengths_host[i] > kv->capacity)
                 fail(PTTS_B200_ERR_CAPACITY, "cannot fit " + std::to_string(lengths_host[i]) +
                                                  " filled KV positions into a budget of " +

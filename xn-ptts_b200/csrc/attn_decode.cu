@@ -1,7 +1,9 @@
 // Split-KV decode attention: one query row per stream over that stream's cached keys
 // 0..=pos, for a batch of streams with ragged lengths. A ring stream attends its slots
 // 0..max(filled, write + 1) - 1 with the slots of evicted rows masked (RingSlots::decode_mask,
-// transformer.rs:39-53).
+// transformer.rs:39-53). A windowed stream (Mimi's KvCache, transformer.rs:257-317) attends
+// its last `context` positions, stored at slots modulo the capacity: a chunk that crosses the
+// end of the slots is copied in two pieces.
 //
 // Reference: the t == 1 branch of StreamingMultiheadAttention::forward, `q.sdpa_decode(k, v,
 // mask, 1/sqrt(d))` (ptts/src/transformer.rs:229-230), and its device-position twin at
@@ -202,7 +204,12 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(DecodeArgs a) 
             if (pb >= end) break;
             const int s0 = (int)((start > pb ? start : pb) - pb);
             const int s1 = (int)((end < pe ? end : pe) - pb);
-            const long long base = (long long)a.row_stream[b] * a.stream_bytes;
+            const int sid = a.row_stream[b];
+            const long long base = (long long)sid * a.stream_bytes;
+            // Key i of the stream sits at slot i, or for a windowed stream at slot
+            // (first + i) % capacity, first being the oldest attended position.
+            const bool wrap = a.window && a.capacity > 0 && a.window[sid] > 0;
+            const int first = wrap ? (int)(((long long)a.row_pos[b] + 1 - (pe - pb)) % a.capacity) : 0;
             for (int p = s0; p < s1; p += CH, ++it) {
                 const int n = min(CH, s1 - p);
                 const int st = it % kStages;
@@ -214,8 +221,14 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(DecodeArgs a) 
                 }
                 unsigned char* ks = smem + st * kStageBytes;
                 mbar_arrive_expect_tx(&full[st], 2u * n * RB);
-                bulk_g2s(ks, kc + base + (long long)p * RB, n * RB, &full[st], pol);
-                bulk_g2s(ks + kStageBytes / 2, vc + base + (long long)p * RB, n * RB, &full[st], pol);
+                const int slot = wrap ? (first + p) % a.capacity : p;
+                const int n0 = wrap ? min(n, a.capacity - slot) : n;  // rows before the wrap
+                bulk_g2s(ks, kc + base + (long long)slot * RB, n0 * RB, &full[st], pol);
+                bulk_g2s(ks + kStageBytes / 2, vc + base + (long long)slot * RB, n0 * RB, &full[st], pol);
+                if (n0 < n) {
+                    bulk_g2s(ks + n0 * RB, kc + base, (n - n0) * RB, &full[st], pol);
+                    bulk_g2s(ks + kStageBytes / 2 + n0 * RB, vc + base, (n - n0) * RB, &full[st], pol);
+                }
             }
         }
         // Before leaving, let every copy still in flight land (bounded) so none writes into

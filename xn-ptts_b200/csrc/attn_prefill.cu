@@ -48,9 +48,14 @@ __global__ void __launch_bounds__(256) prefill_attn_kernel(PrefillArgs a) {
     const int row = w / kHeads, h = w % kHeads;
     const int g = lane >> 3, j = lane & 7;
     const int sid = a.row_stream[row];
-    const int nk = a.row_pos[row] + 1;
+    const int pos = a.row_pos[row];
     const long long cap_rows = a.stream_elems / kRowWidth;
-    if (sid < 0 || a.row_pos[row] < 0 || nk > cap_rows) {
+    // Keys: positions first..pos; a windowed stream keeps its last `context` (Mimi's mask,
+    // transformer.rs:762-785: 0 <= pos - key < context) at slots modulo the capacity.
+    const int ctx = a.window ? a.window[sid] : 0;
+    const int first = ctx > 0 ? max(0, pos - ctx + 1) : 0;
+    const int nk = pos - first + 1;
+    if (sid < 0 || pos < 0 || nk > cap_rows || (ctx == 0 && pos + 1 > cap_rows)) {
         set_error(a.err, DEV_ERR_BOUNDS);
         return;
     }
@@ -73,10 +78,11 @@ __global__ void __launch_bounds__(256) prefill_attn_kernel(PrefillArgs a) {
         const int r0 = r + g, r1 = r + 4 + g;
         const int rr0 = r0 < nk ? r0 : nk - 1, rr1 = r1 < nk ? r1 : nk - 1;
         float k0[8], k1[8], v0[8], v1[8];
-        load8g(kb + (long long)rr0 * kRowWidth, j, k0);
-        load8g(kb + (long long)rr1 * kRowWidth, j, k1);
-        load8g(vb + (long long)rr0 * kRowWidth, j, v0);
-        load8g(vb + (long long)rr1 * kRowWidth, j, v1);
+        const long long sl0 = (first + rr0) % cap_rows, sl1 = (first + rr1) % cap_rows;
+        load8g(kb + sl0 * kRowWidth, j, k0);
+        load8g(kb + sl1 * kRowWidth, j, k1);
+        load8g(vb + sl0 * kRowWidth, j, v0);
+        load8g(vb + sl1 * kRowWidth, j, v1);
         float d0 = 0.f, d1 = 0.f;
 #pragma unroll
         for (int i = 0; i < 8; ++i) {

@@ -57,23 +57,29 @@ struct RingArgs {
     int32_t* write = nullptr;   // [streams]
     int32_t* filled = nullptr;  // [streams]
     uint8_t* valid = nullptr;   // [streams][capacity]
+    // Windowed streams (Mimi's KvCache, transformer.rs:257-317): [streams] context, 0 = none. A
+    // windowed stream writes position p at slot p % capacity and attends positions
+    // max(0, p - context + 1) .. p.
+    int32_t* window = nullptr;
 };
 
 // ---- plans and bookkeeping (misc.cu) ---------------------------------------------------
 
 // Decode plan: one row per sequence. row_pos[i] = lengths[streams[i]]; the row is written at
-// slot row_pos[i] and attends keys 0..row_pos[i], or, for a ring stream, written at its write
-// slot w and attends slots 0..max(filled, w + 1) - 1 (the invisible ones masked by the decode
-// kernel). prefix[i+1] = sum of attended keys, clamped to capacity. Sets DEV_ERR_CAPACITY /
+// slot row_pos[i] and attends keys 0..row_pos[i]; a ring stream writes at its write slot w and
+// attends slots 0..max(filled, w + 1) - 1 (the invisible ones masked by the decode kernel); a
+// windowed stream writes at row_pos[i] % capacity and attends its last min(pos + 1, context)
+// positions. prefix[i+1] = sum of attended keys, clamped to capacity. Sets DEV_ERR_CAPACITY /
 // DEV_ERR_BOUNDS.
 void launch_plan_decode(const int32_t* lengths, const int32_t* streams, int n, int num_streams,
                         int capacity, RowPlan plan, const RingArgs& ring, uint32_t* err, cudaStream_t s);
 
 // Ragged plan: sequence i (stream seq_stream[i]) owns rows row_offsets[i]..row_offsets[i+1];
 // row r of it sits at lengths[stream] + (r - row_offsets[i]).
+// A windowed stream's row r sits at slot pos % capacity (window: [streams] contexts or nullptr).
 void launch_plan_rows(const int32_t* lengths, const int32_t* seq_stream, const int32_t* row_offsets,
                       int n_seq, int n_rows, int num_streams, int capacity, RowPlan plan,
-                      uint32_t* err, cudaStream_t s);
+                      const int32_t* window, uint32_t* err, cudaStream_t s);
 
 // lengths[seq_stream[i]] += rows (row_offsets == nullptr) or row_offsets[i+1]-row_offsets[i];
 // for a ring stream also valid[write] = 1 and filled = max(filled, write + 1).
@@ -152,6 +158,10 @@ struct DecodeArgs {
     const int32_t* ring_write = nullptr;
     const uint8_t* ring_valid = nullptr;
     int capacity = 0;
+    // Windowed streams: the attended keys are positions pos + 1 - n .. pos of the row, at slots
+    // modulo capacity (n = the row's key count). window nullptr: none in the arena.
+    const int32_t* window = nullptr;
+    const int32_t* row_pos = nullptr;
 };
 // Output forms of the attention kernels.
 constexpr int kOutF32 = 0, kOutBf16 = 1, kOutHiLo = 2;  // hi/lo: f16(o) and f16(o - hi)
@@ -167,6 +177,7 @@ struct PrefillArgs {
     long long stream_elems;   // capacity * H * D
     const int32_t* row_stream;
     const int32_t* row_pos;
+    const int32_t* window = nullptr;  // [streams] context of windowed streams (0: none)
     const float* q;           // [rows][H][D] f32, rotated
     void* out;                // [rows][H*D] (see out_mode)
     void* out_lo;
@@ -175,7 +186,8 @@ struct PrefillArgs {
     float qscale;
     uint32_t* err;
 };
-// Causal attention of every row over keys 0..=row_pos (CUDA cores, online softmax).
+// Causal attention of every row over keys 0..=row_pos, or over the last `context` positions
+// (slots pos % capacity) for windowed streams (CUDA cores, online softmax).
 void launch_prefill_attn(const PrefillArgs& a, bool cache_bf16, cudaStream_t s);
 // The same on tcgen05 tiles, bf16 caches: one CTA per (tile of up to 128 consecutive rows of
 // one sequence, head); tiles[i] = (first row, rows).

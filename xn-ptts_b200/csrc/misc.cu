@@ -33,15 +33,21 @@ __global__ void __launch_bounds__(kPlanThreads) plan_decode_kernel(
                 sid = 0;
             }
             const int len = lengths[sid];
-            if (len < 0 || len + 1 > capacity) set_error(err, DEV_ERR_CAPACITY);
+            if (len < 0) set_error(err, DEV_ERR_CAPACITY);
             int slot = len;
             // Clamped so that a refused row never makes a kernel read past the stream's slots.
             keys = min(max(len, 0) + 1, capacity);
             const int w = ring.write ? ring.write[sid] : -1;
+            const int ctx = ring.window ? ring.window[sid] : 0;
             if (w >= 0) {
                 if (w >= capacity) set_error(err, DEV_ERR_CAPACITY);
                 slot = min(w, capacity - 1);
                 keys = min(max(ring.filled[sid], slot + 1), capacity);
+            } else if (ctx > 0) {  // the position grows past the capacity; slots wrap
+                slot = max(len, 0) % capacity;
+                keys = min(min(max(len, 0) + 1, ctx), capacity);
+            } else if (len < 0 || len + 1 > capacity) {
+                set_error(err, DEV_ERR_CAPACITY);
             }
             plan.row_stream[i] = sid;
             plan.row_pos[i] = len;
@@ -76,7 +82,8 @@ __global__ void __launch_bounds__(kPlanThreads) plan_decode_kernel(
 __global__ void plan_rows_kernel(const int32_t* __restrict__ lengths,
                                  const int32_t* __restrict__ seq_stream,
                                  const int32_t* __restrict__ row_offsets, int n_seq, int n_rows,
-                                 int num_streams, int capacity, RowPlan plan, uint32_t* err) {
+                                 int num_streams, int capacity, RowPlan plan, const int32_t* window,
+                                 uint32_t* err) {
     grid_dep_wait();
     grid_dep_launch();
     const int r = blockIdx.x * blockDim.x + threadIdx.x;
@@ -93,10 +100,11 @@ __global__ void plan_rows_kernel(const int32_t* __restrict__ lengths,
         sid = 0;
     }
     const int pos = lengths[sid] + (r - row_offsets[lo]);
-    if (pos < 0 || pos >= capacity) set_error(err, DEV_ERR_CAPACITY);
+    const bool windowed = window && window[sid] > 0;
+    if (pos < 0 || (!windowed && pos >= capacity)) set_error(err, DEV_ERR_CAPACITY);
     plan.row_stream[r] = sid;
     plan.row_pos[r] = pos;
-    plan.row_slot[r] = pos;
+    plan.row_slot[r] = windowed ? max(pos, 0) % capacity : pos;
 }
 
 __global__ void advance_kernel(int32_t* lengths, const int32_t* __restrict__ seq_stream,
@@ -198,9 +206,9 @@ void launch_plan_decode(const int32_t* lengths, const int32_t* streams, int n, i
 
 void launch_plan_rows(const int32_t* lengths, const int32_t* seq_stream, const int32_t* row_offsets,
                       int n_seq, int n_rows, int num_streams, int capacity, RowPlan plan,
-                      uint32_t* err, cudaStream_t s) {
+                      const int32_t* window, uint32_t* err, cudaStream_t s) {
     launch_k(plan_rows_kernel, dim3((n_rows + 255) / 256), dim3(256), 0, s, lengths, seq_stream,
-             row_offsets, n_seq, n_rows, num_streams, capacity, plan, err);
+             row_offsets, n_seq, n_rows, num_streams, capacity, plan, window, err);
 }
 
 void launch_advance(int32_t* lengths, const int32_t* seq_stream, const int32_t* row_offsets,
