@@ -33,7 +33,7 @@ struct Workspace {
         ff_hi.need(r * c.dim_feedforward * 2);
         ff_lo.need(r * c.dim_feedforward * 2);
         split.need(4 * r * c.d_model * 4);
-        counters.need_zeroed(r * sizeof(int));
+        counters.need_zeroed(decode_counter_ints(r) * sizeof(int));
     }
 };
 
@@ -288,10 +288,11 @@ RowPlan make_plan(const ptts_b200_kv* kv, bool decode, const int32_t* d_seq_stre
     plan.row_stream = static_cast<int32_t*>(row_stream.need(sizeof(int32_t) * n_rows));
     plan.row_pos = static_cast<int32_t*>(row_pos.need(2 * sizeof(int32_t) * n_rows));
     plan.row_slot = plan.row_pos + n_rows;
-    plan.prefix = static_cast<int32_t*>(prefix.need(sizeof(int32_t) * (n_rows + 1)));
+    plan.prefix = static_cast<int32_t*>(prefix.need(sizeof(int32_t) * (n_rows + 1 + kMaxDecodeGrid)));
+    plan.cta_first = plan.prefix + n_rows + 1;
     if (decode)
         launch_plan_decode(kv->len.as<int32_t>(), d_seq_stream, n_seq, kv->streams, kv->capacity,
-                           plan, kv->ring(), kv->err.as<uint32_t>(), s);
+                           plan, kv->ring(), sm_count(kv->device), kv->err.as<uint32_t>(), s);
     else
         launch_plan_rows(kv->len.as<int32_t>(), d_seq_stream, d_row_offsets, n_seq, n_rows,
                          kv->streams, kv->capacity, plan, kv->window.as<int32_t>(), kv->err.as<uint32_t>(), s);
@@ -323,7 +324,8 @@ void attention(const ptts_b200_kv* kv, int layer, bool decode, const RowPlan& pl
         a.out_lo = out_lo;
         a.out_mode = out_mode;
         a.part = static_cast<float*>(part.need(sizeof(float) * decode_part_floats(n_rows, grid)));
-        a.counters = static_cast<int*>(counters.need_zeroed(sizeof(int) * n_rows));
+        a.counters = static_cast<int*>(counters.need_zeroed(sizeof(int) * decode_counter_ints(n_rows)));
+        a.cta_first = plan.cta_first;
         a.B = n_rows;
         a.qscale = qscale;
         a.err = kv->err.as<uint32_t>();
@@ -1133,7 +1135,7 @@ int ptts_b200_step(ptts_b200_model* model, ptts_b200_kv* kv, const int32_t* stre
             ng->ws.part.need(sizeof(float) * decode_part_floats(n, sm_count(kv->device)));
             ng->row_stream.need(sizeof(int32_t) * n);
             ng->row_pos.need(2 * sizeof(int32_t) * n);  // positions, then slots
-            ng->prefix.need(sizeof(int32_t) * (n + 1));
+            ng->prefix.need(sizeof(int32_t) * (n + 1 + kMaxDecodeGrid));
             model->step = std::move(ng);
             g = model->step.get();
         }
@@ -1142,10 +1144,11 @@ int ptts_b200_step(ptts_b200_model* model, ptts_b200_kv* kv, const int32_t* stre
         plan.row_pos = g->row_pos.as<int32_t>();
         plan.row_slot = plan.row_pos + n;
         plan.prefix = g->prefix.as<int32_t>();
+        plan.cta_first = plan.prefix + n + 1;
         const int32_t* sid = g->sid.as<int32_t>();
         auto body = [&](cudaStream_t cs, cudaEvent_t* ev) {
             launch_plan_decode(kv->len.as<int32_t>(), sid, n, kv->streams, kv->capacity, plan, kv->ring(),
-                               kv->err.as<uint32_t>(), cs);
+                               sm_count(kv->device), kv->err.as<uint32_t>(), cs);
             run_layers(model, kv, true, plan, n, g->x.as<__nv_bfloat16>(), g->resid.as<float>(), g->ws,
                        cs, ev);
             launch_advance(kv->len.as<int32_t>(), sid, nullptr, n, 1, kv->ring(), kv->capacity, cs);

@@ -37,9 +37,22 @@ constexpr int kHeads = kRowWidth / kHeadDim;  // 8
 constexpr int kConsumerWarps = kHeads;
 constexpr int kThreads = (kConsumerWarps + 1) * 32;
 constexpr int kStages = 3;
-constexpr int kStageBytes = 64 * 1024;  // K half + V half
-constexpr int kMinKeysPerCta = 32;
+constexpr int kDataBytes = 64 * 1024;                   // K half + V half of a chunk
+constexpr int kQStageBytes = kHeads * kHeadDim * 4;      // the f32 q of a stream a piece starts
+constexpr int kHdrBytes = 128;                           // the chunk's header
+constexpr int kStageBytes = kDataBytes + kQStageBytes + kHdrBytes;
 constexpr int kSmemBytes = kStages * kStageBytes + 2 * kStages * 8;
+static_assert(kStageBytes % 128 == 0, "stages stay 128-byte aligned");
+
+// What the producer tells the consumers about a chunk (written before the stage's arrive, read
+// after its wait): stream b of the batch, rows p .. p + n - 1 of its attended keys.
+struct ChunkHdr {
+    int b, p, n, flags;
+    int sid;         // arena stream
+    int ring_w;      // ring write slot, or -1
+    int c0, c1;      // the CTAs holding pieces of a cut stream
+};
+constexpr int kFirst = 1, kLast = 2, kWhole = 4, kEnd = 8;
 
 template <typename T>
 struct Row;
@@ -56,19 +69,6 @@ __device__ __forceinline__ float fast_exp2(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
     return y;
-}
-
-__device__ __forceinline__ int ctas_in_use(long long total, int grid) {
-    const long long g = (total + kMinKeysPerCta - 1) / kMinKeysPerCta;
-    return (int)(g < 1 ? 1 : (g > grid ? grid : g));
-}
-__device__ __forceinline__ long long cta_start(int c, long long total, int g) {
-    return (long long)c * total / g;
-}
-// The CTA whose range holds key p: the largest c with cta_start(c) <= p.
-__device__ __forceinline__ int cta_of(long long p, long long total, int g) {
-    const long long c = ((p + 1) * g + total - 1) / total - 1;
-    return (int)(c < g - 1 ? c : g - 1);
 }
 
 // Eight elements of a head row for lane slice j: bf16 dims 8j..8j+7; f32 dims 4j..4j+3 and
@@ -158,30 +158,19 @@ template <typename T>
 __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(DecodeArgs a) {
     constexpr int RB = Row<T>::kBytes;
     constexpr int HB = RB / kHeads;              // one head of one row: 128 or 256 bytes
-    constexpr int CH = kStageBytes / 2 / RB;     // rows per chunk: 32 (bf16) or 16 (f32)
+    constexpr int CH = kDataBytes / 2 / RB;      // rows per chunk: 32 (bf16) or 16 (f32)
     extern __shared__ __align__(128) unsigned char smem[];
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
     uint64_t* empty = full + kStages;
-    __shared__ int s_b0;
-
-    __shared__ int s_last;
     grid_dep_wait();
     grid_dep_launch();
     const long long total = a.prefix[a.B];
     const int G = ctas_in_use(total, gridDim.x);
     const int c = blockIdx.x;
     if (c >= G) return;
-    const long long start = cta_start(c, total, G), end = cta_start(c + 1, total, G);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
     if (threadIdx.x == 0) {
-        int lo = 0, hi = a.B - 1;  // the last stream whose keys begin at or before `start`
-        while (lo < hi) {
-            const int mid = (lo + hi + 1) >> 1;
-            if (a.prefix[mid] <= start) lo = mid;
-            else hi = mid - 1;
-        }
-        s_b0 = lo;
         for (int s = 0; s < kStages; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], kConsumerWarps);
@@ -189,47 +178,76 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(DecodeArgs a) 
         fence_mbar_init();
     }
     __syncthreads();
-    const int b0 = s_b0;
-    const unsigned char* kc = static_cast<const unsigned char*>(a.k_cache);
-    const unsigned char* vc = static_cast<const unsigned char*>(a.v_cache);
 
     if (warp == kConsumerWarps) {
-        // ---- producer: one lane issues the bulk copies -------------------------------
+        // ---- producer: one lane walks this CTA's key range and issues the bulk copies -------
         if (lane != 0) return;
+        const long long start = cta_start(c, total, G), end = cta_start(c + 1, total, G);
+        int b0 = a.cta_first ? a.cta_first[c] : 0;
+        if (!a.cta_first) {  // the last stream whose keys begin at or before `start`
+            int lo = 0, hi = a.B - 1;
+            while (lo < hi) {
+                const int mid = (lo + hi + 1) >> 1;
+                if (a.prefix[mid] <= start) lo = mid;
+                else hi = mid - 1;
+            }
+            b0 = lo;
+        }
         const uint64_t pol = policy_evict_first();
+        const unsigned char* kc = static_cast<const unsigned char*>(a.k_cache);
+        const unsigned char* vc = static_cast<const unsigned char*>(a.v_cache);
         int it = 0;
         bool ok = true;
+        auto stage_free = [&](int k) {  // wait until the consumers have released stage k % S
+            if (mbar_wait(&empty[k % kStages], ((k / kStages) & 1) ^ 1)) return true;
+            set_error(a.err, DEV_ERR_TIMEOUT);
+            return false;
+        };
         for (int b = b0; b < a.B && ok; ++b) {
             const long long pb = a.prefix[b], pe = a.prefix[b + 1];
             if (pb >= end) break;
             const int s0 = (int)((start > pb ? start : pb) - pb);
             const int s1 = (int)((end < pe ? end : pe) - pb);
+            const bool whole = pb >= start && pe <= end;
             const int sid = a.row_stream[b];
             const long long base = (long long)sid * a.stream_bytes;
             // Key i of the stream sits at slot i, or for a windowed stream at slot
             // (first + i) % capacity, first being the oldest attended position.
             const bool wrap = a.window && a.capacity > 0 && a.window[sid] > 0;
             const int first = wrap ? (int)(((long long)a.row_pos[b] + 1 - (pe - pb)) % a.capacity) : 0;
+            ChunkHdr proto;
+            proto.b = b;
+            proto.sid = sid;
+            proto.ring_w = a.ring_write ? a.ring_write[sid] : -1;
+            proto.c0 = whole ? c : cta_of(pb, total, G);
+            proto.c1 = whole ? c : cta_of(pe - 1, total, G);
             for (int p = s0; p < s1; p += CH, ++it) {
                 const int n = min(CH, s1 - p);
                 const int st = it % kStages;
-                const uint32_t ph = (it / kStages) & 1;
-                if (!mbar_wait(&empty[st], ph ^ 1)) {
-                    set_error(a.err, DEV_ERR_TIMEOUT);
-                    ok = false;
-                    break;
-                }
-                unsigned char* ks = smem + st * kStageBytes;
-                mbar_arrive_expect_tx(&full[st], 2u * n * RB);
+                if (!(ok = stage_free(it))) break;
+                unsigned char* sb = smem + st * kStageBytes;
+                ChunkHdr hd = proto;
+                hd.p = p;
+                hd.n = n;
+                hd.flags = (p == s0 ? kFirst : 0) | (p + n >= s1 ? kLast : 0) | (whole ? kWhole : 0);
+                *reinterpret_cast<ChunkHdr*>(sb + kDataBytes + kQStageBytes) = hd;
+                mbar_arrive_expect_tx(&full[st], 2u * n * RB + (p == s0 ? (uint32_t)kQStageBytes : 0u));
+                if (p == s0) bulk_g2s(sb + kDataBytes, a.q + (long long)b * kRowWidth, kQStageBytes, &full[st], pol);
                 const int slot = wrap ? (first + p) % a.capacity : p;
                 const int n0 = wrap ? min(n, a.capacity - slot) : n;  // rows before the wrap
-                bulk_g2s(ks, kc + base + (long long)slot * RB, n0 * RB, &full[st], pol);
-                bulk_g2s(ks + kStageBytes / 2, vc + base + (long long)slot * RB, n0 * RB, &full[st], pol);
+                bulk_g2s(sb, kc + base + (long long)slot * RB, n0 * RB, &full[st], pol);
+                bulk_g2s(sb + kDataBytes / 2, vc + base + (long long)slot * RB, n0 * RB, &full[st], pol);
                 if (n0 < n) {
-                    bulk_g2s(ks + n0 * RB, kc + base, (n - n0) * RB, &full[st], pol);
-                    bulk_g2s(ks + kStageBytes / 2 + n0 * RB, vc + base, (n - n0) * RB, &full[st], pol);
+                    bulk_g2s(sb + n0 * RB, kc + base, (n - n0) * RB, &full[st], pol);
+                    bulk_g2s(sb + kDataBytes / 2 + n0 * RB, vc + base, (n - n0) * RB, &full[st], pol);
                 }
             }
+        }
+        if (ok && stage_free(it)) {  // the end of the range: a header alone
+            const int st = it % kStages;
+            reinterpret_cast<ChunkHdr*>(smem + st * kStageBytes + kDataBytes + kQStageBytes)->flags = kEnd;
+            mbar_arrive(&full[st]);
+            ++it;
         }
         // Before leaving, let every copy still in flight land (bounded) so none writes into
         // shared memory of a CTA that has gone.
@@ -238,124 +256,121 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(DecodeArgs a) 
         return;
     }
 
-    // ---- consumers: warp h owns head h ---------------------------------------------------
+    // ---- consumers: warp h owns head h and follows the producer's chunks --------------------
+    // No CTA-wide barrier after the start: a warp whose wait times out leaves on its own.
     const int h = warp;
     const int g = lane >> 3;  // which of the 4 rows of a warp step
     const int j = lane & 7;   // which 16-byte slice of the head row
-    int it = 0;
-    bool alive = true;  // cleared by a timed-out wait; the warp then skips work but keeps to the
-                        // named barriers below, so its peers never wait for it
-    for (int b = b0; b < a.B; ++b) {
-        const long long pb = a.prefix[b], pe = a.prefix[b + 1];
-        if (pb >= end) break;
-        const int s0 = (int)((start > pb ? start : pb) - pb);
-        const int s1 = (int)((end < pe ? end : pe) - pb);
-        const bool whole = pb >= start && pe <= end;
-        // Ring stream: slot s is visible iff valid[s] or s is the slot being written.
-        const int sid = a.row_stream[b];
-        const int ring_w = a.ring_write ? a.ring_write[sid] : -1;
-        const uint8_t* vis = ring_w >= 0 ? a.ring_valid + (long long)sid * a.capacity : nullptr;
-
-        float q[8];
-        load_q<T>(a.q + ((long long)b * kHeads + h) * kHeadDim, j, q);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) q[i] *= a.qscale;
-        float m = -1e30f, l = 0.f, acc[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) acc[i] = 0.f;
-
-        for (int p = s0; p < s1; p += CH, ++it) {
-            const int n = min(CH, s1 - p);
-            const int st = it % kStages;
-            const uint32_t ph = (it / kStages) & 1;
-            if (alive && !mbar_wait(&full[st], ph)) {
-                set_error(a.err, DEV_ERR_TIMEOUT);
-                alive = false;
-            }
-            if (!alive) continue;
-            const unsigned char* ks = smem + st * kStageBytes + h * HB;
-            const unsigned char* vs = ks + kStageBytes / 2;
-            for (int r = 0; r < n; r += 8) {
-                const int r0 = r + g, r1 = r + 4 + g;
-                const int rr0 = r0 < n ? r0 : n - 1, rr1 = r1 < n ? r1 : n - 1;
-                float k0[8], k1[8];
-                load8(ks + rr0 * RB, j, k0, static_cast<T*>(nullptr));
-                load8(ks + rr1 * RB, j, k1, static_cast<T*>(nullptr));
-                float d0 = 0.f, d1 = 0.f;
-#pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    d0 = fmaf(q[i], k0[i], d0);
-                    d1 = fmaf(q[i], k1[i], d1);
-                }
-#pragma unroll
-                for (int o = 1; o < 8; o <<= 1) {
-                    d0 += __shfl_xor_sync(0xffffffffu, d0, o);
-                    d1 += __shfl_xor_sync(0xffffffffu, d1, o);
-                }
-                if (r0 >= n) d0 = -INFINITY;
-                if (r1 >= n) d1 = -INFINITY;
-                if (vis) {
-                    const int s0 = p + rr0, s1 = p + rr1;
-                    if (!vis[s0] && s0 != ring_w) d0 = -INFINITY;
-                    if (!vis[s1] && s1 != ring_w) d1 = -INFINITY;
-                }
-                const float mn = fmaxf(m, fmaxf(d0, d1));
-                const float corr = fast_exp2(m - mn);
-                const float e0 = fast_exp2(d0 - mn), e1 = fast_exp2(d1 - mn);
-                l = fmaf(l, corr, e0 + e1);
-                float v0[8], v1[8];
-                load8(vs + rr0 * RB, j, v0, static_cast<T*>(nullptr));
-                load8(vs + rr1 * RB, j, v1, static_cast<T*>(nullptr));
-#pragma unroll
-                for (int i = 0; i < 8; ++i) acc[i] = fmaf(e1, v1[i], fmaf(e0, v0[i], acc[i] * corr));
-                m = mn;
-            }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[st]);
+    float q[8], m = -1e30f, l = 0.f, acc[8];
+    for (int it = 0;; ++it) {
+        const int st = it % kStages;
+        if (!mbar_wait(&full[st], (it / kStages) & 1)) {
+            set_error(a.err, DEV_ERR_TIMEOUT);
+            break;
         }
-        // Merge the four row groups (lanes j, j+8, j+16, j+24 hold the same dims).
+        const unsigned char* sb = smem + st * kStageBytes;
+        const ChunkHdr hd = *reinterpret_cast<const ChunkHdr*>(sb + kDataBytes + kQStageBytes);
+        if (hd.flags & kEnd) break;
+        if (hd.flags & kFirst) {
+            load_q<T>(reinterpret_cast<const float*>(sb + kDataBytes) + h * kHeadDim, j, q);
 #pragma unroll
-        for (int o = 8; o <= 16; o <<= 1) {
-            const float mo = __shfl_xor_sync(0xffffffffu, m, o);
-            const float lo = __shfl_xor_sync(0xffffffffu, l, o);
-            const float mn = fmaxf(m, mo);
-            const float fa = fast_exp2(m - mn), fb = fast_exp2(mo - mn);
-            l = l * fa + lo * fb;
+            for (int i = 0; i < 8; ++i) q[i] *= a.qscale;
+            m = -1e30f;
+            l = 0.f;
 #pragma unroll
-            for (int i = 0; i < 8; ++i) acc[i] = acc[i] * fa + __shfl_xor_sync(0xffffffffu, acc[i], o) * fb;
+            for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+        }
+        // Ring stream: slot s is visible iff valid[s] or s is the slot being written.
+        const uint8_t* vis = hd.ring_w >= 0 ? a.ring_valid + (long long)hd.sid * a.capacity : nullptr;
+        const int n = hd.n, p = hd.p;
+        const unsigned char* ks = sb + h * HB;
+        const unsigned char* vs = ks + kDataBytes / 2;
+        for (int r = 0; r < n; r += 8) {
+            const int r0 = r + g, r1 = r + 4 + g;
+            const int rr0 = r0 < n ? r0 : n - 1, rr1 = r1 < n ? r1 : n - 1;
+            float k0[8], k1[8];
+            load8(ks + rr0 * RB, j, k0, static_cast<T*>(nullptr));
+            load8(ks + rr1 * RB, j, k1, static_cast<T*>(nullptr));
+            float d0 = 0.f, d1 = 0.f;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                d0 = fmaf(q[i], k0[i], d0);
+                d1 = fmaf(q[i], k1[i], d1);
+            }
+#pragma unroll
+            for (int o = 1; o < 8; o <<= 1) {
+                d0 += __shfl_xor_sync(0xffffffffu, d0, o);
+                d1 += __shfl_xor_sync(0xffffffffu, d1, o);
+            }
+            if (r0 >= n) d0 = -INFINITY;
+            if (r1 >= n) d1 = -INFINITY;
+            if (vis) {
+                const int s0 = p + rr0, s1 = p + rr1;
+                if (!vis[s0] && s0 != hd.ring_w) d0 = -INFINITY;
+                if (!vis[s1] && s1 != hd.ring_w) d1 = -INFINITY;
+            }
+            const float mn = fmaxf(m, fmaxf(d0, d1));
+            const float corr = fast_exp2(m - mn);
+            const float e0 = fast_exp2(d0 - mn), e1 = fast_exp2(d1 - mn);
+            l = fmaf(l, corr, e0 + e1);
+            float v0[8], v1[8];
+            load8(vs + rr0 * RB, j, v0, static_cast<T*>(nullptr));
+            load8(vs + rr1 * RB, j, v1, static_cast<T*>(nullptr));
+#pragma unroll
+            for (int i = 0; i < 8; ++i) acc[i] = fmaf(e1, v1[i], fmaf(e0, v0[i], acc[i] * corr));
             m = mn;
         }
-        if (g == 0 && alive) {
-            if (whole) {
-                const float inv = 1.f / l;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[st]);
+        if (!(hd.flags & kLast)) continue;
+        // The end of this CTA's piece of stream b: merge the four row groups (lanes j, j+8,
+        // j+16, j+24 hold the same dims).
+        float mm = m, ll = l, aa[8];
 #pragma unroll
-                for (int i = 0; i < 8; ++i) acc[i] *= inv;
-                store_out<T>(a, (long long)b * kRowWidth + h * kHeadDim, j, acc);
-            } else {
-                float* rec = a.part + ((long long)(b + c) * kHeads + h) * kPartStride;
+        for (int i = 0; i < 8; ++i) aa[i] = acc[i];
 #pragma unroll
-                for (int i = 0; i < 8; ++i) rec[dim_of<T>(j, i)] = acc[i];
-                if (j == 0) {
-                    rec[64] = m;
-                    rec[65] = l;
-                }
+        for (int o = 8; o <= 16; o <<= 1) {
+            const float mo = __shfl_xor_sync(0xffffffffu, mm, o);
+            const float lo = __shfl_xor_sync(0xffffffffu, ll, o);
+            const float mn = fmaxf(mm, mo);
+            const float fa = fast_exp2(mm - mn), fb = fast_exp2(mo - mn);
+            ll = ll * fa + lo * fb;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) aa[i] = aa[i] * fa + __shfl_xor_sync(0xffffffffu, aa[i], o) * fb;
+            mm = mn;
+        }
+        const int b = hd.b;
+        if (hd.flags & kWhole) {
+            if (g == 0) {
+                const float inv = 1.f / ll;
+#pragma unroll
+                for (int i = 0; i < 8; ++i) aa[i] *= inv;
+                store_out<T>(a, (long long)b * kRowWidth + h * kHeadDim, j, aa);
+            }
+            continue;
+        }
+        // A cut stream: publish this head's piece; the warp that completes the head's count
+        // over the stream's pieces merges them and resets the count for the next launch.
+        if (g == 0) {
+            float* rec = a.part + ((long long)(b + c) * kHeads + h) * kPartStride;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) rec[dim_of<T>(j, i)] = aa[i];
+            if (j == 0) {
+                rec[64] = mm;
+                rec[65] = ll;
             }
         }
-        if (!whole) {
-            // Publish this piece; the CTA that completes the stream's count merges all pieces.
+        __threadfence();
+        __syncwarp();
+        int last = 0;
+        if (lane == 0) {
+            int* cnt = a.counters + (long long)b * kHeads + h;
+            last = atomicAdd(cnt, 1) + 1 == hd.c1 - hd.c0 + 1;
+            if (last) *cnt = 0;
+        }
+        if (__shfl_sync(0xffffffffu, last, 0)) {
             __threadfence();
-            asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
-            const int c0 = cta_of(pb, total, G), c1 = cta_of(pe - 1, total, G);
-            if (threadIdx.x == 0) {
-                const int seen = atomicAdd(&a.counters[b], 1) + 1;
-                s_last = seen == c1 - c0 + 1;
-                if (s_last) a.counters[b] = 0;  // ready for the next launch
-            }
-            asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
-            if (s_last) {
-                __threadfence();
-                merge_head(a, b, h, c0, c1, lane);
-            }
+            merge_head(a, b, h, hd.c0, hd.c1, lane);
         }
     }
 }
@@ -374,6 +389,8 @@ void launch_typed(const DecodeArgs& a, int grid, cudaStream_t s) {
 }
 
 }  // namespace
+
+size_t decode_counter_ints(int B) { return (size_t)B * kHeads; }
 
 size_t decode_part_floats(int B, int grid) {
     return (size_t)(B + grid) * kHeads * kPartStride;

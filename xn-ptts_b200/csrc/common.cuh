@@ -83,6 +83,23 @@ __device__ __forceinline__ uint64_t policy_evict_first() {
     return p;
 }
 
+// ---- the split-KV partition (plan and decode kernels) --------------------------------------
+// All attended keys of a decode batch lie end to end (prefix sums); `ctas_in_use` CTAs take
+// equal ranges of them, at least kMinKeysPerCta keys each.
+constexpr int kMinKeysPerCta = 32;
+__device__ __forceinline__ int ctas_in_use(long long total, int grid) {
+    const long long g = (total + kMinKeysPerCta - 1) / kMinKeysPerCta;
+    return (int)(g < 1 ? 1 : (g > grid ? grid : g));
+}
+__device__ __forceinline__ long long cta_start(int c, long long total, int g) {
+    return (long long)c * total / g;
+}
+// The CTA whose range holds key p: the largest c with cta_start(c) <= p.
+__device__ __forceinline__ int cta_of(long long p, long long total, int g) {
+    const long long c = ((p + 1) * g + total - 1) / total - 1;
+    return (int)(c < g - 1 ? c : g - 1);
+}
+
 // ---- programmatic dependent launch ------------------------------------------------------
 // A kernel launched with programmatic stream serialisation may start before its predecessor
 // has finished. grid_dep_wait() returns once the predecessor grid has completed and its

@@ -48,7 +48,9 @@ struct RowPlan {
     int32_t* row_pos = nullptr;     // [rows] RoPE position
     int32_t* row_slot = nullptr;    // [rows] cache slot written (the position, except in a ring)
     int32_t* prefix = nullptr;      // [rows + 1] decode only: prefix sums of attended keys
+    int32_t* cta_first = nullptr;   // [kMaxDecodeGrid] decode only: the stream each CTA starts in
 };
+constexpr int kMaxDecodeGrid = 256;  // >= SMs of the GPU; the decode kernel's CTAs
 
 // Ring caches (StreamingTransformer::start_ring / set_ring_slot / evict, transformer.rs:840-929):
 // per stream the slot the next row goes to (-1: not a ring), one past the highest slot written,
@@ -71,8 +73,11 @@ struct RingArgs {
 // windowed stream writes at row_pos[i] % capacity and attends its last min(pos + 1, context)
 // positions. prefix[i+1] = sum of attended keys, clamped to capacity. Sets DEV_ERR_CAPACITY /
 // DEV_ERR_BOUNDS.
+// With plan.cta_first set, also cta_first[c] = the stream in which CTA c of a `grid`-CTA decode
+// launch starts (the split-KV partition of the prefix sums), so no CTA searches for it.
 void launch_plan_decode(const int32_t* lengths, const int32_t* streams, int n, int num_streams,
-                        int capacity, RowPlan plan, const RingArgs& ring, uint32_t* err, cudaStream_t s);
+                        int capacity, RowPlan plan, const RingArgs& ring, int grid, uint32_t* err,
+                        cudaStream_t s);
 
 // Ragged plan: sequence i (stream seq_stream[i]) owns rows row_offsets[i]..row_offsets[i+1];
 // row r of it sits at lengths[stream] + (r - row_offsets[i]).
@@ -149,7 +154,8 @@ struct DecodeArgs {
     void* out_lo;             // [B][H*D] bf16 lo plane when out_mode == kOutHiLo
     int out_mode;
     float* part;              // [(B + grid) * H * kPartStride]
-    int* counters;            // [B], zero between launches (the merging CTA resets its entry)
+    int* counters;            // [B * H], zero between launches (the merging warp resets its entry)
+    const int32_t* cta_first = nullptr;  // [grid] the stream each CTA starts in, or nullptr (search)
     int B;
     float qscale;             // 1/sqrt(D) * log2(e)
     uint32_t* err;
@@ -170,6 +176,7 @@ constexpr int kPartStride = 68;  // floats per (slot, head) partial: acc[64], m,
 // than one CTA are merged by the CTA that finishes them last. `grid` CTAs at most (one per SM).
 void launch_decode_attn(const DecodeArgs& a, bool cache_bf16, int grid, cudaStream_t s);
 size_t decode_part_floats(int B, int grid);
+size_t decode_counter_ints(int B);
 
 struct PrefillArgs {
     const void* k_cache;

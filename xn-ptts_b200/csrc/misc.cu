@@ -12,7 +12,7 @@ constexpr int kPlanThreads = 1024;
 // One CTA: a running block scan over the sequences, 1024 at a time.
 __global__ void __launch_bounds__(kPlanThreads) plan_decode_kernel(
     const int32_t* __restrict__ lengths, const int32_t* __restrict__ streams, int n,
-    int num_streams, int capacity, RowPlan plan, RingArgs ring, uint32_t* err) {
+    int num_streams, int capacity, RowPlan plan, RingArgs ring, int grid, uint32_t* err) {
     __shared__ int warp_tot[kPlanThreads / 32];
     __shared__ int carry;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -76,6 +76,16 @@ __global__ void __launch_bounds__(kPlanThreads) plan_decode_kernel(
         __syncthreads();
         if (tid == 0) carry += warp_tot[kPlanThreads / 32 - 1];
         __syncthreads();
+    }
+    if (!plan.cta_first) return;
+    // The CTAs of the decode launch: each starts in the stream holding its first key.
+    const long long total = plan.prefix[n];
+    const int G = ctas_in_use(total, grid);
+    for (int b = tid; b < n; b += kPlanThreads) {
+        const long long pb = plan.prefix[b], pe = plan.prefix[b + 1];
+        if (pe <= pb) continue;
+        for (int c = cta_of(pb, total, G); c <= cta_of(pe - 1, total, G); ++c)
+            if (cta_start(c, total, G) >= pb) plan.cta_first[c] = b;
     }
 }
 
@@ -199,9 +209,10 @@ __global__ void bf16_to_f32_kernel(const __nv_bfloat16* __restrict__ x, float* _
 }  // namespace
 
 void launch_plan_decode(const int32_t* lengths, const int32_t* streams, int n, int num_streams,
-                        int capacity, RowPlan plan, const RingArgs& ring, uint32_t* err, cudaStream_t s) {
+                        int capacity, RowPlan plan, const RingArgs& ring, int grid, uint32_t* err,
+                        cudaStream_t s) {
     launch_k(plan_decode_kernel, dim3(1), dim3(kPlanThreads), 0, s, lengths, streams, n,
-             num_streams, capacity, plan, ring, err);
+             num_streams, capacity, plan, ring, grid < kMaxDecodeGrid ? grid : kMaxDecodeGrid, err);
 }
 
 void launch_plan_rows(const int32_t* lengths, const int32_t* seq_stream, const int32_t* row_offsets,

@@ -27,11 +27,11 @@ constexpr int kNoAllocMaxGrid = 160;   // decode CTAs (one per SM; a B200 has 14
 constexpr int kMaxDevices = 64;
 
 constexpr size_t align256(size_t n) { return (n + 255) / 256 * 256; }
-constexpr size_t kPlanBytes = align256(sizeof(int32_t) * (3 * kNoAllocMaxRows + 1));
+constexpr size_t kPlanBytes = align256(sizeof(int32_t) * (3 * kNoAllocMaxRows + 1 + kMaxDecodeGrid));
 constexpr size_t kQBytes = align256(sizeof(float) * kNoAllocMaxRows * kRowWidth);
 constexpr size_t kPartBytes =
     align256(sizeof(float) * (size_t)(kNoAllocMaxRows + kNoAllocMaxGrid) * (kRowWidth / kHeadDim) * kPartStride);
-constexpr size_t kCounterBytes = align256(sizeof(int) * kNoAllocMaxRows);
+constexpr size_t kCounterBytes = align256(sizeof(int) * kNoAllocMaxRows * (kRowWidth / kHeadDim));
 // About 4.6 MB: plan (12 KB) + rotated q (2 MB) + partial records (2.6 MB) + counters (4 KB).
 constexpr size_t kNoAllocScratchBytes = kPlanBytes + kQBytes + kPartBytes + kCounterBytes;
 
@@ -109,13 +109,14 @@ extern "C" int ptts_b200_attend_decode_noalloc(void* k_cache, void* v_cache, int
     plan.row_pos = plan_base + kNoAllocMaxRows;
     plan.row_slot = plan.row_pos;  // no ring here: every row is written at its position
     plan.prefix = plan_base + 2 * kNoAllocMaxRows;
+    plan.cta_first = plan.prefix + n + 1;
     float* q_rot = reinterpret_cast<float*>(sc.base + kPlanBytes);
     float* part = reinterpret_cast<float*>(sc.base + kPlanBytes + kQBytes);
     int* counters = reinterpret_cast<int*>(sc.base + kPlanBytes + kQBytes + kPartBytes);
-    if (cudaMemsetAsync(counters, 0, sizeof(int) * n, s) != cudaSuccess)
+    if (cudaMemsetAsync(counters, 0, sizeof(int) * decode_counter_ints(n), s) != cudaSuccess)
         return refuse(PTTS_B200_ERR_CUDA, "clearing the merge counters failed");
 
-    launch_plan_decode(lengths, streams, n, num_streams, capacity, plan, RingArgs{}, err, s);
+    launch_plan_decode(lengths, streams, n, num_streams, capacity, plan, RingArgs{}, sc.grid, err, s);
     RopeAppendArgs ra{};
     ra.q = q;
     ra.k = k;
@@ -150,6 +151,7 @@ extern "C" int ptts_b200_attend_decode_noalloc(void* k_cache, void* v_cache, int
     a.qscale = (1.0f / sqrtf((float)kHeadDim)) * 1.4426950408889634f;
     a.err = err;
     a.capacity = capacity;  // no ring or windowed stream here (ring_write and window stay null)
+    a.cta_first = plan.cta_first;
     launch_decode_attn(a, kv_dtype == PTTS_B200_BF16, sc.grid, s);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return refuse(PTTS_B200_ERR_CUDA, std::string("kernel launch: ") + cudaGetErrorString(e));
