@@ -279,9 +279,9 @@ def run_ours(args):
     stream = torch.cuda.current_stream()
 
     def fresh_state():
-        # Prompts on a scratch state first load every kernel (both GEMM kernels: the tcgen05 one
-        # below 4096 rows, the mma.sync one above) and build the RoPE table for this capacity,
-        # so the timed prefill includes no first-use module loading.
+        # Prompts on a scratch state first load every kernel (the linears' 32- and 128-row
+        # tiles) and build the RoPE table for this capacity, so the timed prefill includes no
+        # first-use module loading.
         scratch = ptts.KvState(L, 4, max(cap, 1100), dtype="bf16", device=local)
         for n in (130, 1100):
             model.forward(scratch, torch.zeros(4 * n, cfg.d_model, device=dev).bfloat16(),

@@ -170,3 +170,31 @@ def test_kernel_variants_match_the_oracle(ptts, oracle, cuda, monkeypatch, env):
     kv.check()
     print(env, "normwise:", ["%.2e" % e for e in errs])
     assert max(errs) < TOL
+
+
+def test_long_prompts_match_the_oracle(ptts, oracle, cuda):
+    """Prompts of 4096+ rows in one call (the linears' 128-row tcgen05 tiles, the tcgen05
+    prefill attention over 1000+ keys), then a decode step."""
+    import torch
+    cfg = ptts.FlowLMConfig(num_layers=2)
+    rows = [1100, 1003, 1200, 900]
+    S, cap = len(rows), max(rows) + 4
+    model, om, kv, kc, vc = _setup(ptts, oracle, cfg, 17, S, cap, cuda)
+    g = torch.Generator().manual_seed(18)
+    streams = [2, 0, 3, 1]
+    offs = np.concatenate([[0], np.cumsum(rows)]).astype(np.int32)
+    x = torch.randn(int(offs[-1]), 512, generator=g).bfloat16()
+    y = model.forward(kv, x.to(cuda), streams, rows)
+    lengths = np.zeros(S, np.int32)
+    want = om.forward(_f32(x), kc, vc, lengths, streams, offs, store=oracle.ROUND_KV)
+    errs = [normwise(_f32(y), want)]
+    for i, s in enumerate(streams):
+        lengths[s] += rows[i]
+    xs = torch.randn(S, 512, generator=g).bfloat16()
+    y = model.step(kv, list(range(S)), xs.to(cuda))
+    want = om.forward(_f32(xs), kc, vc, lengths, list(range(S)), np.arange(S + 1, dtype=np.int32),
+                      store=oracle.ROUND_KV)
+    errs.append(normwise(_f32(y), want))
+    kv.check()
+    print("long prompts", ["%.2e" % e for e in errs])
+    assert max(errs) < TOL

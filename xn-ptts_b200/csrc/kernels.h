@@ -240,12 +240,11 @@ struct LinearArgs {
     const float2* rope;
     uint32_t* err;
 };
-// N must be a multiple of 64 and K / splits a multiple of 64. Layers loaded from f32 or q8_0
-// weights have no int8 copy (w == nullptr) and two f16 weight planes (wh, wh_lo); they run on
-// the tcgen05 kernel at every M. Otherwise launch_linear runs the TMA-fed
-// tcgen05/TMEM kernel (linear_tc.cu) for M < 4096 where linear_tc_supported holds (f16 hi/lo
-// activations, f16 weight copy present, N a multiple of 128) and the mma.sync kernel (linear.cu) otherwise. PTTS_B200_GEMM=mma forces the
-// mma.sync kernel, PTTS_B200_GEMM=tc the tcgen05 kernel at every M.
+// N must be a multiple of 64 and K / splits a multiple of 64. launch_linear runs the TMA-fed
+// tcgen05/TMEM kernel (linear_tc.cu) wherever linear_tc_supported holds (f16 hi/lo activations,
+// an f16 weight copy, N a multiple of 128), and the mma.sync kernel (linear.cu) otherwise or when
+// PTTS_B200_GEMM=mma. Layers loaded from f32 or q8_0 weights have no int8 copy (w == nullptr)
+// and two f16 weight planes (wh, wh_lo): only the tcgen05 kernel takes them.
 bool launch_linear(const LinearArgs& a, LinearEpi epi, cudaStream_t s);  // false: nothing launched
 void launch_linear_mma(const LinearArgs& a, LinearEpi epi, cudaStream_t s);
 bool linear_tc_supported(const LinearArgs& a);

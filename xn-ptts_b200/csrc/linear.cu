@@ -451,13 +451,12 @@ void launch_typed(const LinearArgs& a, cudaStream_t s) {
 }  // namespace
 
 bool launch_linear(const LinearArgs& a, LinearEpi epi, cudaStream_t s) {
-    // Weights without an int8 copy (f32 or q8_0 layers: two f16 planes) only have the tcgen05
-    // kernel. Otherwise: tcgen05 below 4096 rows (decode and short prompts), mma.sync above,
-    // where its four CTAs per SM overlap epilogues with main loops. PTTS_B200_GEMM=mma / =tc
-    // force one kernel where both exist.
+    // The tcgen05 kernel wherever it applies (decode batches and prompts alike: 56 ms against
+    // 90 ms for config 5's 139k-row prefill); weights without an int8 copy (f32 or q8_0
+    // layers) only have it. PTTS_B200_GEMM=mma selects the mma.sync kernel where both exist.
     if (a.w == nullptr) return launch_linear_tc(a, epi, s);
     const char* sel = getenv("PTTS_B200_GEMM");
-    const bool use_tc = sel && sel[0] == 'm' ? false : (sel && sel[0] == 't') || a.M < 4096;
+    const bool use_tc = !(sel && sel[0] == 'm');
     if (use_tc && launch_linear_tc(a, epi, s)) return true;
     launch_linear_mma(a, epi, s);
     return true;
