@@ -198,3 +198,31 @@ def test_long_prompts_match_the_oracle(ptts, oracle, cuda):
     kv.check()
     print("long prompts", ["%.2e" % e for e in errs])
     assert max(errs) < TOL
+
+
+def test_grouped_query_attention_in_the_stack(ptts, oracle, cuda):
+    """num_kv_heads < num_heads through the whole stack (transformer.rs:1112-1164's equivalence,
+    here against the oracle's GQA): a ragged prompt and decode steps."""
+    import torch
+    cfg = ptts.FlowLMConfig(num_layers=2, num_kv_heads=4)
+    S, cap = 4, 64
+    model, om, kv, kc, vc = _setup(ptts, oracle, cfg, 23, S, cap, cuda)
+    g = torch.Generator().manual_seed(24)
+    rows = [20, 3, 33, 9]
+    streams = [1, 3, 0, 2]
+    offs = np.concatenate([[0], np.cumsum(rows)]).astype(np.int32)
+    x = torch.randn(int(offs[-1]), 512, generator=g).bfloat16()
+    y = model.forward(kv, x.to(cuda), streams, rows)
+    lengths = np.zeros(S, np.int32)
+    errs = [normwise(_f32(y), om.forward(_f32(x), kc, vc, lengths, streams, offs, store=oracle.ROUND_KV))]
+    for i, s in enumerate(streams):
+        lengths[s] += rows[i]
+    for _ in range(3):
+        xs = torch.randn(S, 512, generator=g).bfloat16()
+        y = model.step(kv, list(range(S)), xs.to(cuda))
+        errs.append(normwise(_f32(y), om.forward(_f32(xs), kc, vc, lengths, list(range(S)),
+                                                 np.arange(S + 1, dtype=np.int32), store=oracle.ROUND_KV)))
+        lengths += 1
+    kv.check()
+    print("gqa", ["%.2e" % e for e in errs])
+    assert max(errs) < TOL

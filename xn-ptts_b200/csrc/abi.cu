@@ -9,11 +9,18 @@
 #include <memory>
 #include <mutex>
 #include <string>
+#include <type_traits>
 #include <vector>
 
 #include "host.h"
 #include "kernels.h"
 #include "ptts_b200.h"
+
+uint64_t ptts_b200_flow_prepare(ptts_b200_flow* f, int n, int d_model);
+int ptts_b200_flow_ldim(const ptts_b200_flow* f);
+void ptts_b200_flow_input(ptts_b200_flow* f, const float* latent, __nv_bfloat16* x, int n, cudaStream_t s);
+void ptts_b200_flow_head(ptts_b200_flow* f, const float* hidden, int n, const float* noise, float* latent,
+                         float* eos, cudaStream_t s);
 
 namespace {
 
@@ -139,6 +146,14 @@ struct ptts_b200_kv {
     char* v_layer(int l) const { return v.as<char>() + l * layer_bytes(); }
 };
 
+// What besides the stream set a recorded step graph depends on: a frame graph also records the
+// flow head (its workspace generation) and whether the frame starts from bos_emb.
+struct GraphKey {
+    uint64_t flow = 0;  // the flow head's identity and workspace generation (0: a plain step)
+    bool bos = false;
+    bool operator==(const GraphKey& o) const { return flow == o.flow && bos == o.bos; }
+};
+
 struct StepGraph {
     std::vector<int32_t> streams;
     const ptts_b200_kv* kv = nullptr;
@@ -147,6 +162,8 @@ struct StepGraph {
     cudaGraphExec_t exec = nullptr;
     DevBuf sid, x, resid, row_stream, row_pos, prefix;
     Workspace ws;
+    GraphKey key;
+    DevBuf lat_in, noise, lat_out, eos;  // a frame graph's own inputs and outputs
     ~StepGraph() {
         if (exec) cudaGraphExecDestroy(exec);
         if (graph) cudaGraphDestroy(graph);
@@ -173,10 +190,12 @@ struct ptts_b200_model {
     Workspace ws;
     Staging staging;
     std::unique_ptr<StepGraph> step;
+    std::unique_ptr<StepGraph> frame;  // ptts_b200_frame's graph (the step with the flow head)
     cudaStream_t capture_stream = nullptr;
     std::vector<cudaEvent_t> events;  // tracing: [2 * layers] around attention, step start / end
     ~ptts_b200_model() {
         step.reset();
+        frame.reset();
         if (capture_stream) cudaStreamDestroy(capture_stream);
         for (cudaEvent_t e : events) cudaEventDestroy(e);
     }
@@ -503,6 +522,7 @@ void ensure_rope(ptts_b200_model* m, int rows, cudaStream_t s) {
     if (m->rope_rows >= rows) return;
     CK(cudaStreamSynchronize(s));
     m->step.reset();
+    m->frame.reset();
     RopeFreqs f;
     std::memcpy(f.inv_freq, m->inv_freq, sizeof(f.inv_freq));
     launch_rope_table(f, static_cast<float2*>(m->rope.need(sizeof(float2) * kMaxPairs * (size_t)rows)), rows, s);
@@ -609,6 +629,108 @@ bool is_device_pointer(const void* p) {
 }
 
 }  // namespace
+
+// One decode step of the stack for `streams` (transformer.rs:822-838 with DeviceStep), recorded
+// once per stream set as a CUDA graph in `slot` and replayed: `inputs` fills the graph's input
+// buffers (before the replay), `pre` and `post` launch extra kernels before and after the layers
+// inside the recorded body. With tracing on, the body runs un-recorded, timed per attention.
+template <class Inputs, class Pre, class Post>
+void run_step(ptts_b200_model* model, ptts_b200_kv* kv, const int32_t* streams_host, int n,
+              std::unique_ptr<StepGraph>& slot, const GraphKey& key, cudaStream_t s, Inputs&& inputs,
+              Pre&& pre, Post&& post) {
+    std::vector<int32_t> ones(n > 0 ? n : 0, 1), offsets;
+    check_sequences(kv, streams_host, ones.data(), n, offsets);  // capacity for one more row
+    refuse_window(kv, streams_host, n);
+    const ptts_b200_config& c = model->cfg;
+    ensure_rope(model, kv->capacity, s);
+    StepGraph* g = slot.get();
+    const bool same = g && g->kv == kv && g->kv_uid == kv->uid && g->key == key && g->streams.size() == (size_t)n &&
+                      std::memcmp(g->streams.data(), streams_host, sizeof(int32_t) * n) == 0;
+    if (!same) {
+        // Buffers of this stream set.
+        CK(cudaStreamSynchronize(s));
+        slot.reset();
+        auto ng = std::make_unique<StepGraph>();
+        ng->streams.assign(streams_host, streams_host + n);
+        ng->kv = kv;
+        ng->kv_uid = kv->uid;
+        ng->key = key;
+        int32_t* sid = static_cast<int32_t*>(ng->sid.need(sizeof(int32_t) * n));
+        CK(cudaMemcpy(sid, streams_host, sizeof(int32_t) * n, cudaMemcpyHostToDevice));
+        ng->x.need((size_t)n * c.d_model * 2);
+        ng->resid.need((size_t)n * c.d_model * 4);
+        ng->ws.size(c, n);
+        ng->ws.part.need(sizeof(float) * decode_part_floats(n, sm_count(kv->device)));
+        ng->row_stream.need(sizeof(int32_t) * n);
+        ng->row_pos.need(2 * sizeof(int32_t) * n);  // positions, then slots
+        ng->prefix.need(sizeof(int32_t) * (n + 1 + kMaxDecodeGrid));
+        slot = std::move(ng);
+        g = slot.get();
+    }
+    RowPlan plan;
+    plan.row_stream = g->row_stream.as<int32_t>();
+    plan.row_pos = g->row_pos.as<int32_t>();
+    plan.row_slot = plan.row_pos + n;
+    plan.prefix = g->prefix.as<int32_t>();
+    plan.cta_first = plan.prefix + n + 1;
+    const int32_t* sid = g->sid.as<int32_t>();
+    inputs(g);
+    auto body = [&](cudaStream_t cs, cudaEvent_t* ev) {
+        if constexpr (!std::is_same_v<std::decay_t<Pre>, std::nullptr_t>) pre(cs);
+        launch_plan_decode(kv->len.as<int32_t>(), sid, n, kv->streams, kv->capacity, plan, kv->ring(),
+                           sm_count(kv->device), kv->err.as<uint32_t>(), cs);
+        run_layers(model, kv, true, plan, n, g->x.as<__nv_bfloat16>(), g->resid.as<float>(), g->ws, cs, ev);
+        launch_advance(kv->len.as<int32_t>(), sid, nullptr, n, 1, kv->ring(), kv->capacity, cs);
+        check_launch();
+        if constexpr (!std::is_same_v<std::decay_t<Post>, std::nullptr_t>) post(cs);
+    };
+    if (tracing_on()) {
+        const int L = c.num_layers;
+        if (model->events.size() < (size_t)(2 * L + 2)) {
+            for (cudaEvent_t e : model->events) cudaEventDestroy(e);
+            model->events.assign(2 * L + 2, nullptr);
+            for (auto& e : model->events) CK(cudaEventCreate(&e));
+        }
+        cudaEvent_t* ev = model->events.data();
+        CK(cudaEventRecord(ev[2 * L], s));
+        body(s, ev);
+        CK(cudaEventRecord(ev[2 * L + 1], s));
+        CK(cudaEventSynchronize(ev[2 * L + 1]));
+        double bytes = 0.0;  // K and V rows read, f32 q read, bf16 output written
+        for (int i = 0; i < n; ++i) bytes += (double)attended_keys(kv, streams_host[i]) * kv->row_bytes * 2;
+        bytes += (double)n * kRowWidth * (4 + 2);
+        double attn_ms = 0.0;
+        for (int l = 0; l < L; ++l) {
+            float ms = 0.f;
+            CK(cudaEventElapsedTime(&ms, ev[2 * l], ev[2 * l + 1]));
+            attn_ms += ms;
+        }
+        float ms = 0.f;
+        CK(cudaEventElapsedTime(&ms, ev[2 * L], ev[2 * L + 1]));
+        trace_add(L, attn_ms, bytes * L, 1, ms);
+    } else {
+        if (!g->exec) {
+            cudaStream_t cs = model->capture_stream;
+            CK(cudaStreamSynchronize(s));
+            CK(cudaStreamBeginCapture(cs, cudaStreamCaptureModeRelaxed));
+            try {
+                body(cs, nullptr);
+            } catch (...) {
+                cudaGraph_t junk = nullptr;
+                cudaStreamEndCapture(cs, &junk);
+                if (junk) cudaGraphDestroy(junk);
+                throw;
+            }
+            CK(cudaStreamEndCapture(cs, &g->graph));
+            CK(cudaGraphInstantiate(&g->exec, g->graph, 0));
+        }
+        CK(cudaGraphLaunch(g->exec, s));
+    }
+    for (int i = 0; i < n; ++i) {
+        kv->h_len[streams_host[i]] += 1;
+        kv->ring_commit(streams_host[i]);
+    }
+}
 
 // Lets other translation units of the library set this thread's last error.
 void ptts_b200_set_last_error(const std::string& msg) { g_last_error = msg; }
@@ -1109,100 +1231,62 @@ int ptts_b200_step(ptts_b200_model* model, ptts_b200_kv* kv, const int32_t* stre
     return guarded([&] {
         check_model_kv(model, kv);
         require(x && y, PTTS_B200_ERR_ARG, "x/y are NULL");
-        std::vector<int32_t> ones(n > 0 ? n : 0, 1), offsets;
-        check_sequences(kv, streams_host, ones.data(), n, offsets);  // capacity for one more row
-        refuse_window(kv, streams_host, n);
         DeviceScope scope(model->device);
         cudaStream_t s = as_stream(cuda_stream);
         const ptts_b200_config& c = model->cfg;
-        ensure_rope(model, kv->capacity, s);
-        StepGraph* g = model->step.get();
-        const bool same = g && g->kv == kv && g->kv_uid == kv->uid && g->streams.size() == (size_t)n &&
-                          std::memcmp(g->streams.data(), streams_host, sizeof(int32_t) * n) == 0;
-        if (!same) {
-            // Buffers of this stream set (transformer.rs:822-838 with DeviceStep).
-            CK(cudaStreamSynchronize(s));
-            model->step.reset();
-            auto ng = std::make_unique<StepGraph>();
-            ng->streams.assign(streams_host, streams_host + n);
-            ng->kv = kv;
-            ng->kv_uid = kv->uid;
-            int32_t* sid = static_cast<int32_t*>(ng->sid.need(sizeof(int32_t) * n));
-            CK(cudaMemcpy(sid, streams_host, sizeof(int32_t) * n, cudaMemcpyHostToDevice));
-            ng->x.need((size_t)n * c.d_model * 2);
-            ng->resid.need((size_t)n * c.d_model * 4);
-            ng->ws.size(c, n);
-            ng->ws.part.need(sizeof(float) * decode_part_floats(n, sm_count(kv->device)));
-            ng->row_stream.need(sizeof(int32_t) * n);
-            ng->row_pos.need(2 * sizeof(int32_t) * n);  // positions, then slots
-            ng->prefix.need(sizeof(int32_t) * (n + 1 + kMaxDecodeGrid));
-            model->step = std::move(ng);
-            g = model->step.get();
-        }
-        RowPlan plan;
-        plan.row_stream = g->row_stream.as<int32_t>();
-        plan.row_pos = g->row_pos.as<int32_t>();
-        plan.row_slot = plan.row_pos + n;
-        plan.prefix = g->prefix.as<int32_t>();
-        plan.cta_first = plan.prefix + n + 1;
-        const int32_t* sid = g->sid.as<int32_t>();
-        auto body = [&](cudaStream_t cs, cudaEvent_t* ev) {
-            launch_plan_decode(kv->len.as<int32_t>(), sid, n, kv->streams, kv->capacity, plan, kv->ring(),
-                               sm_count(kv->device), kv->err.as<uint32_t>(), cs);
-            run_layers(model, kv, true, plan, n, g->x.as<__nv_bfloat16>(), g->resid.as<float>(), g->ws,
-                       cs, ev);
-            launch_advance(kv->len.as<int32_t>(), sid, nullptr, n, 1, kv->ring(), kv->capacity, cs);
-            check_launch();
-        };
         const size_t xb = (size_t)n * c.d_model * 2, yb = (size_t)n * c.d_model * 4;
-        CK(cudaMemcpyAsync(g->x.p, x, xb, is_device_pointer(x) ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, s));
-        if (tracing_on()) {
-            const int L = c.num_layers;
-            if (model->events.size() < (size_t)(2 * L + 2)) {
-                for (cudaEvent_t e : model->events) cudaEventDestroy(e);
-                model->events.assign(2 * L + 2, nullptr);
-                for (auto& e : model->events) CK(cudaEventCreate(&e));
-            }
-            cudaEvent_t* ev = model->events.data();
-            CK(cudaEventRecord(ev[2 * L], s));
-            body(s, ev);
-            CK(cudaEventRecord(ev[2 * L + 1], s));
-            CK(cudaEventSynchronize(ev[2 * L + 1]));
-            double bytes = 0.0;  // K and V rows read, f32 q read, bf16 output written
-            for (int i = 0; i < n; ++i) bytes += (double)attended_keys(kv, streams_host[i]) * kv->row_bytes * 2;
-            bytes += (double)n * kRowWidth * (4 + 2);
-            double attn_ms = 0.0;
-            for (int l = 0; l < L; ++l) {
-                float ms = 0.f;
-                CK(cudaEventElapsedTime(&ms, ev[2 * l], ev[2 * l + 1]));
-                attn_ms += ms;
-            }
-            float ms = 0.f;
-            CK(cudaEventElapsedTime(&ms, ev[2 * L], ev[2 * L + 1]));
-            trace_add(L, attn_ms, bytes * L, 1, ms);
-        } else {
-            if (!g->exec) {
-                cudaStream_t cs = model->capture_stream;
-                CK(cudaStreamSynchronize(s));
-                CK(cudaStreamBeginCapture(cs, cudaStreamCaptureModeRelaxed));
-                try {
-                    body(cs, nullptr);
-                } catch (...) {
-                    cudaGraph_t junk = nullptr;
-                    cudaStreamEndCapture(cs, &junk);
-                    if (junk) cudaGraphDestroy(junk);
-                    throw;
-                }
-                CK(cudaStreamEndCapture(cs, &g->graph));
-                CK(cudaGraphInstantiate(&g->exec, g->graph, 0));
-            }
-            CK(cudaGraphLaunch(g->exec, s));
-        }
+        StepGraph* g = nullptr;
+        run_step(model, kv, streams_host, n, model->step, GraphKey{}, s,
+                 [&](StepGraph* sg) {
+                     g = sg;
+                     CK(cudaMemcpyAsync(g->x.p, x, xb,
+                                        is_device_pointer(x) ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, s));
+                 },
+                 nullptr, nullptr);
         CK(cudaMemcpyAsync(y, g->resid.p, yb, is_device_pointer(y) ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost, s));
-        for (int i = 0; i < n; ++i) {
-            kv->h_len[streams_host[i]] += 1;
-            kv->ring_commit(streams_host[i]);
-        }
+    });
+}
+
+int ptts_b200_frame(ptts_b200_model* model, ptts_b200_flow* flow, ptts_b200_kv* kv, const int32_t* streams_host,
+                    int n, const float* latent_in, const float* noise, float* latent_out, float* eos,
+                    void* cuda_stream) {
+    return guarded([&] {
+        check_model_kv(model, kv);
+        require(flow && noise && latent_out && eos, PTTS_B200_ERR_ARG, "NULL argument");
+        DeviceScope scope(model->device);
+        cudaStream_t s = as_stream(cuda_stream);
+        const uint64_t version = ptts_b200_flow_prepare(flow, n > 0 ? n : 1, model->cfg.d_model);
+        const size_t lb = (size_t)n * ptts_b200_flow_ldim(flow) * 4;
+        const bool bos = latent_in == nullptr;
+        GraphKey key;
+        key.flow = version;
+        key.bos = bos;
+        auto kind = [](const void* p) {
+            return is_device_pointer(p) ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
+        };
+        StepGraph* g = nullptr;
+        run_step(model, kv, streams_host, n, model->frame, key, s,
+                 [&](StepGraph* sg) {  // inputs into the graph's own buffers
+                     g = sg;
+                     g->lat_in.need(lb);
+                     g->noise.need(lb);
+                     g->lat_out.need(lb);
+                     g->eos.need((size_t)n * 4);
+                     if (!bos) CK(cudaMemcpyAsync(g->lat_in.p, latent_in, lb, kind(latent_in), s));
+                     CK(cudaMemcpyAsync(g->noise.p, noise, lb, kind(noise), s));
+                 },
+                 [&](cudaStream_t cs) {  // input_linear, inside the recorded body
+                     ptts_b200_flow_input(flow, bos ? nullptr : g->lat_in.as<float>(), g->x.as<__nv_bfloat16>(), n, cs);
+                 },
+                 [&](cudaStream_t cs) {  // out_norm, EOS and the flow net
+                     ptts_b200_flow_head(flow, g->resid.as<float>(), n, g->noise.as<float>(), g->lat_out.as<float>(),
+                                         g->eos.as<float>(), cs);
+                 });
+        auto back = [](const void* p) {
+            return is_device_pointer(p) ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost;
+        };
+        CK(cudaMemcpyAsync(latent_out, g->lat_out.p, lb, back(latent_out), s));
+        CK(cudaMemcpyAsync(eos, g->eos.p, (size_t)n * 4, back(eos), s));
     });
 }
 

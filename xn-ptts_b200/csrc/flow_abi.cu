@@ -79,9 +79,12 @@ struct ptts_b200_flow {
     int rows = 0;
     DevBuf x_in, hidden, t_hi, t_lo, y_hi, y_lo, ada_out, xf, h_hi, h_lo, h1_hi, h1_lo, hf, cur_a, cur_b;
 
-    int ada_width() const { return cfg.flow_depth * 3 * cfg.flow_dim + 2 * cfg.flow_dim; }
+    uint64_t uid = 0;  // distinguishes a new flow head at a recycled address
+    int gen = 0;       // bumped whenever the workspace moves (a recorded frame graph is then stale)
+    int ada_width() const { return cfg.flow_dim * (3 * cfg.flow_depth + 2); }
     void size(int n) {
         if (n <= rows) return;
+        ++gen;
         const size_t d = cfg.d_model, C = cfg.flow_dim, L = cfg.ldim;
         x_in.need(n * d * 2);
         hidden.need(n * d * 4);
@@ -284,6 +287,41 @@ void sample(ptts_b200_flow* f, const float* src, bool normalise, int n, const fl
 
 }  // namespace
 
+// ---- pieces of ptts_b200_frame (abi.cu records them with the step in one CUDA graph) ---------
+
+// The flow head is ready for `n` rows: its workspace sized (outside any capture). Returns what
+// a recorded frame graph depends on: the object's identity and its workspace generation.
+uint64_t ptts_b200_flow_prepare(ptts_b200_flow* f, int n, int d_model) {
+    check_flow(f);
+    require(f->cfg.d_model == d_model, PTTS_B200_ERR_STATE, "the flow head and the model differ in d_model");
+    DeviceScope scope(f->device);
+    f->size(n);
+    return (f->uid << 32) | (uint64_t)(uint32_t)f->gen;
+}
+int ptts_b200_flow_ldim(const ptts_b200_flow* f) { return f->cfg.ldim; }
+
+// input_linear(latent) (+ condition) -> the backbone's bf16 input rows x [n][d_model]; latent
+// nullptr: every row from bos_emb (StepInput::Bos).
+void ptts_b200_flow_input(ptts_b200_flow* f, const float* latent, __nv_bfloat16* x, int n, cudaStream_t s) {
+    FlowSmallArgs in{};
+    in.M = n;
+    in.N = f->cfg.d_model;
+    in.K = f->cfg.ldim;
+    in.a = latent;
+    in.a_row = f->bos.as<float>();
+    in.w = f->input_linear.as<float>();
+    in.add = f->has_condition ? f->condition.as<float>() : nullptr;
+    in.yb = x;
+    launch_flow_small(in, s);
+    CK(cudaGetLastError());
+}
+
+// out_norm of the backbone's output rows, then sample_from_noise.
+void ptts_b200_flow_head(ptts_b200_flow* f, const float* hidden, int n, const float* noise, float* latent,
+                         float* eos, cudaStream_t s) {
+    sample(f, hidden, true, n, noise, latent, eos, s);
+}
+
 // Whether `name` is one of this flow head's tensors (for the GGUF loader, gguf.cu).
 bool ptts_b200_flow_wants(const ptts_b200_flow* flow, const std::string& name) {
     return flow && (name == "condition" || flow->expected.count(name) != 0);
@@ -311,7 +349,9 @@ int ptts_b200_flow_create(int device, const ptts_b200_flow_config* config, ptts_
         int count = 0;
         CK(cudaGetDeviceCount(&count));
         require(device >= 0 && device < count, PTTS_B200_ERR_ARG, "no such device");
+        static uint64_t next_uid = 1;
         auto f = std::make_unique<ptts_b200_flow>();
+        f->uid = next_uid++;
         f->device = device;
         f->cfg = c;
         f->time_conds = c.flow_type == PTTS_B200_FLOW_LSD ? 2 : 0;
@@ -455,34 +495,6 @@ int ptts_b200_flow_sample(ptts_b200_flow* flow, const float* t_out, int n, const
         require(n >= 1, PTTS_B200_ERR_ARG, "n must be >= 1");
         DeviceScope scope(flow->device);
         sample(flow, t_out, false, n, noise, latent, eos, static_cast<cudaStream_t>(cuda_stream));
-    });
-}
-
-int ptts_b200_frame(ptts_b200_model* model, ptts_b200_flow* flow, ptts_b200_kv* kv, const int32_t* streams_host,
-                    int n, const float* latent_in, const float* noise, float* latent_out, float* eos,
-                    void* cuda_stream) {
-    return guarded([&] {
-        check_flow(flow);
-        require(noise && latent_out && eos && streams_host, PTTS_B200_ERR_ARG, "NULL argument");
-        require(n >= 1, PTTS_B200_ERR_ARG, "n must be >= 1");
-        DeviceScope scope(flow->device);
-        cudaStream_t s = static_cast<cudaStream_t>(cuda_stream);
-        flow->size(n);
-        // input_linear(latent) (+ condition), the backbone's bf16 input rows
-        FlowSmallArgs in{};
-        in.M = n;
-        in.N = flow->cfg.d_model;
-        in.K = flow->cfg.ldim;
-        in.a = latent_in;
-        in.a_row = flow->bos.as<float>();
-        in.w = flow->input_linear.as<float>();
-        in.add = flow->has_condition ? flow->condition.as<float>() : nullptr;
-        in.yb = flow->x_in.as<__nv_bfloat16>();
-        launch_flow_small(in, s);
-        CK(cudaGetLastError());
-        const int rc = ptts_b200_step(model, kv, streams_host, n, flow->x_in.p, flow->hidden.as<float>(), cuda_stream);
-        if (rc != PTTS_B200_OK) fail(rc, ptts_b200_last_error());
-        sample(flow, flow->hidden.as<float>(), true, n, noise, latent_out, eos, s);
     });
 }
 
