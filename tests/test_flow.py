@@ -85,9 +85,11 @@ def test_flow_sample_matches_the_oracle(ptts, cuda, kind, exact):
 
 
 @pytest.mark.gpu
-def test_frames_match_the_oracle(ptts, oracle, cuda):
+@pytest.mark.parametrize("S", [6, 200])
+def test_frames_match_the_oracle(ptts, oracle, cuda, S):
     """A prompt, then frames from bos_emb: input_linear -> device step -> out_norm -> flow
-    sample, per frame against the oracle fed the same latents (flow_lm.rs:392-410)."""
+    sample, per frame against the oracle fed the same latents (flow_lm.rs:392-410). 200 streams
+    run the step as two lanes."""
     import torch
     from oracle import flow as of
     mcfg = ptts.FlowLMConfig(num_layers=2)
@@ -97,7 +99,7 @@ def test_frames_match_the_oracle(ptts, oracle, cuda):
     model.load(w)
     om = oracle.Model(mcfg, w)
     f, W = _flow(ptts, fcfg, 8, condition=True)
-    S, P, cap = 6, 20, 40
+    P, cap = 20, 40
     kv = ptts.KvState(mcfg.num_layers, S, cap, dtype="bf16")
     shape = (mcfg.num_layers, S, cap, mcfg.num_heads, mcfg.head_dim)
     kc, vc = np.zeros(shape, np.float32), np.zeros(shape, np.float32)

@@ -138,6 +138,38 @@ def test_config4_decode_frames(ptts, oracle, cuda):
     assert max(errs) < TOL
 
 
+def test_two_lane_steps_match_the_oracle(ptts, oracle, cuda):
+    """Decode steps of 200 streams, which run as two lanes (rows 0-95 and 96-199 on two CUDA
+    streams inside the step graph): ragged prefixes and a permuted subset of the arena's
+    streams, per step against the oracle."""
+    import torch
+    cfg = ptts.FlowLMConfig(num_layers=2)
+    S, cap = 240, 48
+    model, om, kv, kc, vc = _setup(ptts, oracle, cfg, 41, S, cap, cuda)
+    rng = np.random.default_rng(41)
+    rows = rng.integers(1, 40, size=S).astype(np.int32)
+    offs = np.concatenate([[0], np.cumsum(rows)]).astype(np.int32)
+    g = torch.Generator().manual_seed(41)
+    x = torch.randn(int(offs[-1]), 512, generator=g).bfloat16()
+    model.forward(kv, x.to(cuda), list(range(S)), rows.tolist())
+    lengths = np.zeros(S, np.int32)
+    om.forward(_f32(x), kc, vc, lengths, list(range(S)), offs, store=oracle.ROUND_KV)
+    lengths += rows
+    streams = [int(v) for v in rng.permutation(S)[:200]]
+    errs = []
+    for _ in range(3):
+        xs = torch.randn(len(streams), 512, generator=g).bfloat16()
+        y = model.step(kv, streams, xs.to(cuda))
+        want = om.forward(_f32(xs), kc, vc, lengths, streams, np.arange(len(streams) + 1, dtype=np.int32),
+                          store=oracle.ROUND_KV)
+        lengths[streams] += 1
+        errs.append(normwise(_f32(y), want))
+    kv.check()
+    np.testing.assert_array_equal(kv.lengths(), lengths)
+    print("two-lane steps normwise:", ["%.2e" % e for e in errs])
+    assert max(errs) < TOL
+
+
 @pytest.mark.parametrize("env", [{"PTTS_B200_GEMM": "mma"}, {"PTTS_B200_PREFILL": "core"}],
                          ids=["mma-sync-linears", "cuda-core-prefill"])
 def test_kernel_variants_match_the_oracle(ptts, oracle, cuda, monkeypatch, env):

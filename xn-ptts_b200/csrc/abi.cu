@@ -154,14 +154,23 @@ struct GraphKey {
     bool operator==(const GraphKey& o) const { return flow == o.flow && bos == o.bos; }
 };
 
+// One lane of a decode step: rows off .. off + n - 1 of the stream set, with its own row plan
+// and workspace so that two lanes can run at the same time.
+struct StepLane {
+    int off = 0, n = 0;
+    DevBuf row_stream, row_pos, prefix;
+    Workspace ws;
+};
+
 struct StepGraph {
     std::vector<int32_t> streams;
     const ptts_b200_kv* kv = nullptr;
     uint64_t kv_uid = 0;
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t exec = nullptr;
-    DevBuf sid, x, resid, row_stream, row_pos, prefix;
-    Workspace ws;
+    DevBuf sid, x, resid;
+    StepLane lanes[2];
+    int n_lanes = 0;
     GraphKey key;
     DevBuf lat_in, noise, lat_out, eos;  // a frame graph's own inputs and outputs
     ~StepGraph() {
@@ -191,12 +200,16 @@ struct ptts_b200_model {
     Staging staging;
     std::unique_ptr<StepGraph> step;
     std::unique_ptr<StepGraph> frame;  // ptts_b200_frame's graph (the step with the flow head)
-    cudaStream_t capture_stream = nullptr;
-    std::vector<cudaEvent_t> events;  // tracing: [2 * layers] around attention, step start / end
+    cudaStream_t capture_stream = nullptr, lane_stream = nullptr;
+    cudaEvent_t lane_start = nullptr, lane_join = nullptr;  // fork / join of a two-lane step
+    std::vector<cudaEvent_t> events;  // tracing: [2 * layers] per lane around attention, step start / end
     ~ptts_b200_model() {
         step.reset();
         frame.reset();
         if (capture_stream) cudaStreamDestroy(capture_stream);
+        if (lane_stream) cudaStreamDestroy(lane_stream);
+        if (lane_start) cudaEventDestroy(lane_start);
+        if (lane_join) cudaEventDestroy(lane_join);
         for (cudaEvent_t e : events) cudaEventDestroy(e);
     }
 };
@@ -327,7 +340,7 @@ struct Tiles {
 
 void attention(const ptts_b200_kv* kv, int layer, bool decode, const RowPlan& plan, int n_rows,
                const float* q_rot, void* out, void* out_lo, int out_mode, DevBuf& part,
-               DevBuf& counters, const Tiles& tiles, cudaStream_t s) {
+               DevBuf& counters, const Tiles& tiles, cudaStream_t s, bool compact = false) {
     const bool bf16 = kv->dtype == PTTS_B200_BF16;
     const float qscale = (1.0f / sqrtf((float)kv->head_dim)) * kLog2e;  // transformer.rs:215
     if (decode) {
@@ -353,7 +366,8 @@ void attention(const ptts_b200_kv* kv, int layer, bool decode, const RowPlan& pl
         a.capacity = kv->capacity;
         a.window = kv->window.as<int32_t>();
         a.row_pos = plan.row_pos;
-        launch_decode_attn(a, bf16, grid, s);
+        a.prestart = true;  // the in_proj or rope_append launch sits between the plan and this one
+        launch_decode_attn(a, bf16, grid, s, compact);
     } else {
         PrefillArgs a{};
         a.k_cache = kv->k_layer(layer);
@@ -406,9 +420,15 @@ int split_for(int rows, int k, int want) {
 //   LN1 (+ previous layer's split-K slices) -> in_proj (RoPE + append) -> attention ->
 //   out_proj (split-K) -> LN2 (+ slices) -> linear1 + GELU -> linear2 (split-K),
 // then a last reduction into the residual. x_in (bf16) seeds the f32 residual `resid`.
+// `lane`: this is one of two lanes of a decode step running side by side; the attention takes
+// its compact ring, and `after_qkv0` (if set) is recorded once the first in_proj is launched.
+struct LaneOpts {
+    bool lane = false;
+    cudaEvent_t after_qkv0 = nullptr;
+};
 void run_layers(const ptts_b200_model* m, const ptts_b200_kv* kv, bool decode, const RowPlan& plan,
                 int rows, const __nv_bfloat16* x_in, float* resid, Workspace& w, cudaStream_t s,
-                cudaEvent_t* attn_ev = nullptr, const Tiles& tiles = Tiles{}) {
+                cudaEvent_t* attn_ev = nullptr, const Tiles& tiles = Tiles{}, const LaneOpts& lo = LaneOpts{}) {
     const ptts_b200_config& c = m->cfg;
     const int hd = c.num_heads * c.head_dim;
     const int nqkv = hd + 2 * c.num_kv_heads * c.head_dim;
@@ -483,10 +503,11 @@ void run_layers(const ptts_b200_model* m, const ptts_b200_kv* kv, bool decode, c
         a.err = err;
         require(launch_linear(a, EPI_QKV, s), PTTS_B200_ERR_UNSUPPORTED, "no kernel for in_proj's shape");
         check_launch();
+        if (l == 0 && lo.after_qkv0) CK(cudaEventRecord(lo.after_qkv0, s));
         // attention over the cache
         if (attn_ev) CK(cudaEventRecord(attn_ev[2 * l], s));
         attention(kv, l, decode, plan, rows, w.q_rot.as<float>(), w.attn_hi.p, w.attn_lo.p,
-                  kOutHiLo, w.part, w.counters, tiles, s);
+                  kOutHiLo, w.part, w.counters, tiles, s, lo.lane);
         if (attn_ev) CK(cudaEventRecord(attn_ev[2 * l + 1], s));
         // out_proj + residual
         residual_gemm(w.attn_hi.as<__half>(), w.attn_lo.as<__half>(), L.w_out, L.h_out, L.l_out, L.s_out,
@@ -630,10 +651,26 @@ bool is_device_pointer(const void* p) {
 
 }  // namespace
 
+// How many lanes a decode step of n rows runs in. Two lanes (two halves of the stream set on two
+// streams inside the graph) let one half's latency-bound linears run beside the other half's
+// HBM-bound attention; below 128 rows a step runs as one. PTTS_B200_LANES=1 keeps one lane.
+int step_lanes(int n) {
+    static const bool one = [] {
+        const char* e = getenv("PTTS_B200_LANES");
+        return e && e[0] == '1';
+    }();
+    return (!one && n >= 128) ? 2 : 1;
+}
+
 // One decode step of the stack for `streams` (transformer.rs:822-838 with DeviceStep), recorded
 // once per stream set as a CUDA graph in `slot` and replayed: `inputs` fills the graph's input
 // buffers (before the replay), `pre` and `post` launch extra kernels before and after the layers
-// inside the recorded body. With tracing on, the body runs un-recorded, timed per attention.
+// inside the recorded body. With tracing on, the body runs un-recorded on one stream (the lanes
+// one after the other), timed per attention.
+//
+// Two lanes: rows [0, n0) run on the capture stream, rows [n0, n) on a second stream forked
+// from it. The second lane starts once the first has launched its first in_proj, so the first
+// lane's attention meets the second lane's linears; both join before `post`.
 template <class Inputs, class Pre, class Post>
 void run_step(ptts_b200_model* model, ptts_b200_kv* kv, const int32_t* streams_host, int n,
               std::unique_ptr<StepGraph>& slot, const GraphKey& key, cudaStream_t s, Inputs&& inputs,
@@ -643,8 +680,11 @@ void run_step(ptts_b200_model* model, ptts_b200_kv* kv, const int32_t* streams_h
     refuse_window(kv, streams_host, n);
     const ptts_b200_config& c = model->cfg;
     ensure_rope(model, kv->capacity, s);
+    const int grid = sm_count(kv->device);
+    const int n_lanes = step_lanes(n);
     StepGraph* g = slot.get();
     const bool same = g && g->kv == kv && g->kv_uid == kv->uid && g->key == key && g->streams.size() == (size_t)n &&
+                      g->n_lanes == n_lanes &&
                       std::memcmp(g->streams.data(), streams_host, sizeof(int32_t) * n) == 0;
     if (!same) {
         // Buffers of this stream set.
@@ -659,62 +699,95 @@ void run_step(ptts_b200_model* model, ptts_b200_kv* kv, const int32_t* streams_h
         CK(cudaMemcpy(sid, streams_host, sizeof(int32_t) * n, cudaMemcpyHostToDevice));
         ng->x.need((size_t)n * c.d_model * 2);
         ng->resid.need((size_t)n * c.d_model * 4);
-        ng->ws.size(c, n);
-        ng->ws.part.need(sizeof(float) * decode_part_floats(n, sm_count(kv->device)));
-        ng->row_stream.need(sizeof(int32_t) * n);
-        ng->row_pos.need(2 * sizeof(int32_t) * n);  // positions, then slots
-        ng->prefix.need(sizeof(int32_t) * (n + 1 + kMaxDecodeGrid));
+        // Lane 0 takes half the rows rounded to the 32-row tiles of the linears.
+        const int n0 = n_lanes == 1 ? n : std::max(1, ((n / 2 + 16) / 32) * 32);
+        ng->n_lanes = n_lanes;
+        for (int i = 0; i < n_lanes; ++i) {
+            StepLane& ln = ng->lanes[i];
+            ln.off = i == 0 ? 0 : n0;
+            ln.n = i == 0 ? n0 : n - n0;
+            const int r = std::max(ln.n, 1);
+            ln.ws.size(c, r);
+            ln.ws.part.need(sizeof(float) * decode_part_floats(r, grid));
+            ln.row_stream.need(sizeof(int32_t) * r);
+            ln.row_pos.need(2 * sizeof(int32_t) * r);  // positions, then slots
+            ln.prefix.need(sizeof(int32_t) * (r + 1 + kMaxDecodeGrid));
+        }
         slot = std::move(ng);
         g = slot.get();
     }
-    RowPlan plan;
-    plan.row_stream = g->row_stream.as<int32_t>();
-    plan.row_pos = g->row_pos.as<int32_t>();
-    plan.row_slot = plan.row_pos + n;
-    plan.prefix = g->prefix.as<int32_t>();
-    plan.cta_first = plan.prefix + n + 1;
     const int32_t* sid = g->sid.as<int32_t>();
+    auto plan_of = [](StepLane& ln) {
+        RowPlan plan;
+        plan.row_stream = ln.row_stream.as<int32_t>();
+        plan.row_pos = ln.row_pos.as<int32_t>();
+        plan.row_slot = plan.row_pos + ln.n;
+        plan.prefix = ln.prefix.as<int32_t>();
+        plan.cta_first = plan.prefix + ln.n + 1;
+        return plan;
+    };
     inputs(g);
-    auto body = [&](cudaStream_t cs, cudaEvent_t* ev) {
+    if (n_lanes > 1 && !model->lane_stream) {
+        CK(cudaStreamCreateWithFlags(&model->lane_stream, cudaStreamNonBlocking));
+        CK(cudaEventCreateWithFlags(&model->lane_start, cudaEventDisableTiming));
+        CK(cudaEventCreateWithFlags(&model->lane_join, cudaEventDisableTiming));
+    }
+    // `cs2` is the second lane's stream (== cs when the lanes run one after the other).
+    auto body = [&](cudaStream_t cs, cudaStream_t cs2, cudaEvent_t* ev) {
         if constexpr (!std::is_same_v<std::decay_t<Pre>, std::nullptr_t>) pre(cs);
-        launch_plan_decode(kv->len.as<int32_t>(), sid, n, kv->streams, kv->capacity, plan, kv->ring(),
-                           sm_count(kv->device), kv->err.as<uint32_t>(), cs);
-        run_layers(model, kv, true, plan, n, g->x.as<__nv_bfloat16>(), g->resid.as<float>(), g->ws, cs, ev);
+        for (int i = 0; i < n_lanes; ++i) {
+            StepLane& ln = g->lanes[i];
+            const cudaStream_t ls = i == 0 ? cs : cs2;
+            if (i == 1 && cs2 != cs) CK(cudaStreamWaitEvent(cs2, model->lane_start, 0));
+            const RowPlan plan = plan_of(ln);
+            launch_plan_decode(kv->len.as<int32_t>(), sid + ln.off, ln.n, kv->streams, kv->capacity, plan,
+                               kv->ring(), grid, kv->err.as<uint32_t>(), ls);
+            LaneOpts lo;
+            lo.lane = n_lanes > 1;
+            lo.after_qkv0 = (i == 0 && n_lanes > 1 && cs2 != cs) ? model->lane_start : nullptr;
+            run_layers(model, kv, true, plan, ln.n, g->x.as<__nv_bfloat16>() + (size_t)ln.off * c.d_model,
+                       g->resid.as<float>() + (size_t)ln.off * c.d_model, ln.ws, ls,
+                       ev ? ev + 2 * c.num_layers * i : nullptr, Tiles{}, lo);
+        }
+        if (n_lanes > 1 && cs2 != cs) {
+            CK(cudaEventRecord(model->lane_join, cs2));
+            CK(cudaStreamWaitEvent(cs, model->lane_join, 0));
+        }
         launch_advance(kv->len.as<int32_t>(), sid, nullptr, n, 1, kv->ring(), kv->capacity, cs);
         check_launch();
         if constexpr (!std::is_same_v<std::decay_t<Post>, std::nullptr_t>) post(cs);
     };
     if (tracing_on()) {
-        const int L = c.num_layers;
-        if (model->events.size() < (size_t)(2 * L + 2)) {
+        const int L = c.num_layers, E = 2 * L * n_lanes;
+        if (model->events.size() < (size_t)(E + 2)) {
             for (cudaEvent_t e : model->events) cudaEventDestroy(e);
-            model->events.assign(2 * L + 2, nullptr);
+            model->events.assign(E + 2, nullptr);
             for (auto& e : model->events) CK(cudaEventCreate(&e));
         }
         cudaEvent_t* ev = model->events.data();
-        CK(cudaEventRecord(ev[2 * L], s));
-        body(s, ev);
-        CK(cudaEventRecord(ev[2 * L + 1], s));
-        CK(cudaEventSynchronize(ev[2 * L + 1]));
+        CK(cudaEventRecord(ev[E], s));
+        body(s, s, ev);
+        CK(cudaEventRecord(ev[E + 1], s));
+        CK(cudaEventSynchronize(ev[E + 1]));
         double bytes = 0.0;  // K and V rows read, f32 q read, bf16 output written
         for (int i = 0; i < n; ++i) bytes += (double)attended_keys(kv, streams_host[i]) * kv->row_bytes * 2;
         bytes += (double)n * kRowWidth * (4 + 2);
         double attn_ms = 0.0;
-        for (int l = 0; l < L; ++l) {
+        for (int l = 0; l < L * n_lanes; ++l) {
             float ms = 0.f;
             CK(cudaEventElapsedTime(&ms, ev[2 * l], ev[2 * l + 1]));
             attn_ms += ms;
         }
         float ms = 0.f;
-        CK(cudaEventElapsedTime(&ms, ev[2 * L], ev[2 * L + 1]));
-        trace_add(L, attn_ms, bytes * L, 1, ms);
+        CK(cudaEventElapsedTime(&ms, ev[E], ev[E + 1]));
+        trace_add((int64_t)L * n_lanes, attn_ms, bytes * L, 1, ms);
     } else {
         if (!g->exec) {
             cudaStream_t cs = model->capture_stream;
             CK(cudaStreamSynchronize(s));
             CK(cudaStreamBeginCapture(cs, cudaStreamCaptureModeRelaxed));
             try {
-                body(cs, nullptr);
+                body(cs, n_lanes > 1 ? model->lane_stream : cs, nullptr);
             } catch (...) {
                 cudaGraph_t junk = nullptr;
                 cudaStreamEndCapture(cs, &junk);

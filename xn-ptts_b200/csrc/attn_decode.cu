@@ -36,13 +36,23 @@ namespace {
 constexpr int kHeads = kRowWidth / kHeadDim;  // 8
 constexpr int kConsumerWarps = kHeads;
 constexpr int kThreads = (kConsumerWarps + 1) * 32;
-constexpr int kStages = 3;
-constexpr int kDataBytes = 64 * 1024;                   // K half + V half of a chunk
 constexpr int kQStageBytes = kHeads * kHeadDim * 4;      // the f32 q of a stream a piece starts
 constexpr int kHdrBytes = 128;                           // the chunk's header
-constexpr int kStageBytes = kDataBytes + kQStageBytes + kHdrBytes;
-constexpr int kSmemBytes = kStages * kStageBytes + 2 * kStages * 8;
-static_assert(kStageBytes % 128 == 0, "stages stay 128-byte aligned");
+
+// The shared-memory ring: STAGES stages of DATA bytes (K half + V half of a chunk) plus the q
+// and header slots. The wide ring (3 x 64 KB) is for a kernel that has the SMs to itself; the
+// compact one (4 x 32 KB, 137 KB) leaves room on every SM for a linear's CTA (74 KB) of a
+// step's other lane, so the two run side by side.
+template <int STAGES, int DATA>
+struct Ring {
+    static constexpr int kStages = STAGES;
+    static constexpr int kDataBytes = DATA;
+    static constexpr int kStageBytes = DATA + kQStageBytes + kHdrBytes;
+    static constexpr int kSmemBytes = STAGES * kStageBytes + 2 * STAGES * 8;
+    static_assert(kStageBytes % 128 == 0, "stages stay 128-byte aligned");
+};
+using WideRing = Ring<3, 64 * 1024>;
+using CompactRing = Ring<4, 32 * 1024>;
 
 // What the producer tells the consumers about a chunk (written before the stage's arrive, read
 // after its wait): stream b of the batch, rows p .. p + n - 1 of its attended keys.
@@ -154,16 +164,19 @@ __device__ __forceinline__ void merge_head(const DecodeArgs& a, int b, int h, in
     }
 }
 
-template <typename T>
+template <typename T, class R>
 __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(DecodeArgs a) {
+    constexpr int kStages = R::kStages, kDataBytes = R::kDataBytes, kStageBytes = R::kStageBytes;
     constexpr int RB = Row<T>::kBytes;
     constexpr int HB = RB / kHeads;              // one head of one row: 128 or 256 bytes
     constexpr int CH = kDataBytes / 2 / RB;      // rows per chunk: 32 (bf16) or 16 (f32)
     extern __shared__ __align__(128) unsigned char smem[];
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
     uint64_t* empty = full + kStages;
-    grid_dep_wait();
-    grid_dep_launch();
+    // With `prestart` the plan is complete before the predecessor began, so it is read now; the
+    // producer waits for the predecessor (which writes q and this step's cache rows) only before
+    // the first copy that needs either.
+    if (!a.prestart) grid_dep_wait();
     const long long total = a.prefix[a.B];
     const int G = ctas_in_use(total, gridDim.x);
     const int c = blockIdx.x;
@@ -203,6 +216,16 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(DecodeArgs a) 
             set_error(a.err, DEV_ERR_TIMEOUT);
             return false;
         };
+        // Before the wait: the stages (at most kStages) whose q copy is still to be issued.
+        bool waited = !a.prestart;
+        int q_stage[kStages], q_row[kStages], n_deferred = 0;
+        auto wait_predecessor = [&]() {
+            grid_dep_wait();
+            waited = true;
+            for (int i = 0; i < n_deferred; ++i)
+                bulk_g2s(smem + q_stage[i] * kStageBytes + kDataBytes, a.q + (long long)q_row[i] * kRowWidth,
+                         kQStageBytes, &full[q_stage[i]], pol);
+        };
         for (int b = b0; b < a.B && ok; ++b) {
             const long long pb = a.prefix[b], pe = a.prefix[b + 1];
             if (pb >= end) break;
@@ -224,6 +247,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(DecodeArgs a) 
             for (int p = s0; p < s1; p += CH, ++it) {
                 const int n = min(CH, s1 - p);
                 const int st = it % kStages;
+                // The row this step appends: the ring's write slot, else the stream's last key.
+                const bool new_row = proto.ring_w >= 0 ? (p <= proto.ring_w && proto.ring_w < p + n)
+                                                       : p + n == (int)(pe - pb);
+                if (!waited && (it >= kStages || new_row)) wait_predecessor();
                 if (!(ok = stage_free(it))) break;
                 unsigned char* sb = smem + st * kStageBytes;
                 ChunkHdr hd = proto;
@@ -232,7 +259,14 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(DecodeArgs a) 
                 hd.flags = (p == s0 ? kFirst : 0) | (p + n >= s1 ? kLast : 0) | (whole ? kWhole : 0);
                 *reinterpret_cast<ChunkHdr*>(sb + kDataBytes + kQStageBytes) = hd;
                 mbar_arrive_expect_tx(&full[st], 2u * n * RB + (p == s0 ? (uint32_t)kQStageBytes : 0u));
-                if (p == s0) bulk_g2s(sb + kDataBytes, a.q + (long long)b * kRowWidth, kQStageBytes, &full[st], pol);
+                if (p == s0) {
+                    if (waited) {
+                        bulk_g2s(sb + kDataBytes, a.q + (long long)b * kRowWidth, kQStageBytes, &full[st], pol);
+                    } else {
+                        q_stage[n_deferred] = st;
+                        q_row[n_deferred++] = b;
+                    }
+                }
                 const int slot = wrap ? (first + p) % a.capacity : p;
                 const int n0 = wrap ? min(n, a.capacity - slot) : n;  // rows before the wrap
                 bulk_g2s(sb, kc + base + (long long)slot * RB, n0 * RB, &full[st], pol);
@@ -243,12 +277,15 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(DecodeArgs a) 
                 }
             }
         }
+        if (!waited) wait_predecessor();
         if (ok && stage_free(it)) {  // the end of the range: a header alone
             const int st = it % kStages;
             reinterpret_cast<ChunkHdr*>(smem + st * kStageBytes + kDataBytes + kQStageBytes)->flags = kEnd;
             mbar_arrive(&full[st]);
             ++it;
         }
+        // Every copy is issued: the next kernel may launch (its CTAs wait for this grid).
+        grid_dep_launch();
         // Before leaving, let every copy still in flight land (bounded) so none writes into
         // shared memory of a CTA that has gone.
         for (int k = (it > kStages ? it - kStages : 0); k < it; ++k)
@@ -258,6 +295,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(DecodeArgs a) 
 
     // ---- consumers: warp h owns head h and follows the producer's chunks --------------------
     // No CTA-wide barrier after the start: a warp whose wait times out leaves on its own.
+    if (a.prestart) grid_dep_wait();
     const int h = warp;
     const int g = lane >> 3;  // which of the 4 rows of a warp step
     const int j = lane & 7;   // which 16-byte slice of the head row
@@ -375,17 +413,17 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(DecodeArgs a) 
     }
 }
 
-template <typename T>
+template <typename T, class R>
 void launch_typed(const DecodeArgs& a, int grid, cudaStream_t s) {
-    static int configured = -1;  // the device whose attribute was set last
+    static int configured = -1;  // the device whose attributes were set last
     int dev = 0;
     cudaGetDevice(&dev);
     if (configured != dev) {
-        cudaFuncSetAttribute(decode_attn_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             kSmemBytes);
+        cudaFuncSetAttribute(decode_attn_kernel<T, R>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             R::kSmemBytes);
         configured = dev;
     }
-    launch_k(decode_attn_kernel<T>, dim3(grid), dim3(kThreads), kSmemBytes, s, a);
+    launch_k(decode_attn_kernel<T, R>, dim3(grid), dim3(kThreads), R::kSmemBytes, s, a);
 }
 
 }  // namespace
@@ -396,9 +434,14 @@ size_t decode_part_floats(int B, int grid) {
     return (size_t)(B + grid) * kHeads * kPartStride;
 }
 
-void launch_decode_attn(const DecodeArgs& a, bool cache_bf16, int grid, cudaStream_t s) {
-    if (cache_bf16) launch_typed<__nv_bfloat16>(a, grid, s);
-    else launch_typed<float>(a, grid, s);
+void launch_decode_attn(const DecodeArgs& a, bool cache_bf16, int grid, cudaStream_t s, bool compact) {
+    if (compact) {
+        if (cache_bf16) launch_typed<__nv_bfloat16, CompactRing>(a, grid, s);
+        else launch_typed<float, CompactRing>(a, grid, s);
+    } else {
+        if (cache_bf16) launch_typed<__nv_bfloat16, WideRing>(a, grid, s);
+        else launch_typed<float, WideRing>(a, grid, s);
+    }
 }
 
 }  // namespace ptts

@@ -22,9 +22,13 @@ enum : uint32_t {
 // start while its predecessor in the stream finishes; every kernel calls grid_dep_wait()
 // before it reads what a predecessor wrote.
 bool pdl_enabled();
+// Asks, once per kernel and device, for the largest shared-memory carveout. Kernels of the two
+// lanes of a step share SMs, and an SM runs CTAs side by side only under one carveout.
+void prefer_max_shared(const void* kernel);
 template <typename... KArgs, typename... Args>
 inline cudaError_t launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
                             cudaStream_t s, Args&&... args) {
+    prefer_max_shared(reinterpret_cast<const void*>(kernel));
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
     cfg.blockDim = block;
@@ -168,13 +172,18 @@ struct DecodeArgs {
     // modulo capacity (n = the row's key count). window nullptr: none in the arena.
     const int32_t* window = nullptr;
     const int32_t* row_pos = nullptr;
+    // The plan and every cache row but the ones this launch's predecessor appends were written
+    // before that predecessor began (it is not the plan kernel): the kernel reads the plan and
+    // copies those rows before it waits for the predecessor.
+    bool prestart = false;
 };
 // Output forms of the attention kernels.
 constexpr int kOutF32 = 0, kOutBf16 = 1, kOutHiLo = 2;  // hi/lo: f16(o) and f16(o - hi)
 constexpr int kPartStride = 68;  // floats per (slot, head) partial: acc[64], m, l, pad
 // Split-KV decode over the balanced partition of all attended keys; the streams that span more
 // than one CTA are merged by the CTA that finishes them last. `grid` CTAs at most (one per SM).
-void launch_decode_attn(const DecodeArgs& a, bool cache_bf16, int grid, cudaStream_t s);
+// `compact`: the smaller shared-memory ring, which leaves room on each SM for a linear's CTA.
+void launch_decode_attn(const DecodeArgs& a, bool cache_bf16, int grid, cudaStream_t s, bool compact = false);
 size_t decode_part_floats(int B, int grid);
 size_t decode_counter_ints(int B);
 

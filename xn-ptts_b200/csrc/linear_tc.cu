@@ -40,7 +40,8 @@ constexpr int kThreadsTma = 128;
 // WLO: the weights come as two planes too (hi, lo), and each k step runs a third MMA.
 template <int RT, bool WLO>
 struct TmaTile {
-    static constexpr int kStages = WLO ? 3 : 4;
+    // 3 stages: 74 KB for f16 weights, so a CTA fits beside the decode attention's compact ring.
+    static constexpr int kStages = 3;
     static constexpr int kWBytes = FT * KS * 2;  // 16 KB per weight plane
     static constexpr int kXBytes = RT * KS * 2;  // per activation plane
     static constexpr int kStageBytes = (WLO ? 2 : 1) * kWBytes + 2 * kXBytes;
@@ -335,7 +336,6 @@ __global__ void __launch_bounds__(kThreadsTma) linear_tma_kernel(const __grid_co
             if (WLO) tma_load_2d_hint(base + kt * T::kStageBytes + T::kWBytes, &tm_wlo, k0 + kt * KS, n0, &full[kt], pol_w);
         }
         grid_dep_wait();
-        grid_dep_launch();
         for (int kt = 0; kt < KT; ++kt) {
             const int st = kt % S;
             const uint32_t sa = base + st * T::kStageBytes;
@@ -354,7 +354,6 @@ __global__ void __launch_bounds__(kThreadsTma) linear_tma_kernel(const __grid_co
         }
     } else {
         grid_dep_wait();
-        grid_dep_launch();
         if (tid == 32) {
             // ---- MMA issuer --------------------------------------------------------------------
             const uint32_t idesc = p.a_f16 ? idesc_f16<RT>() : idesc_bf16<RT>();
@@ -385,6 +384,9 @@ __global__ void __launch_bounds__(kThreadsTma) linear_tma_kernel(const __grid_co
     // ---- epilogue: feature n0 + 32w + lane, rows m0 .. m0 + RT - 1 ------------------------------
     const bool got = mbar_wait(done, 0);
     if (!got) set_error(p.err, DEV_ERR_TIMEOUT);
+    // The next kernel may launch now: its CTAs take SM room only while this epilogue runs, not
+    // through the whole pipeline (room a concurrent lane's kernels can use).
+    if (tid == 0) grid_dep_launch();
     __syncwarp();  // tcgen05.ld below is warp-collective
     tc_fence_after();
 #pragma unroll 1

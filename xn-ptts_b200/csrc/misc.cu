@@ -1,5 +1,8 @@
 // Row plans, length bookkeeping and small conversions.
 #include <cstdlib>
+#include <mutex>
+#include <set>
+#include <utility>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -278,6 +281,16 @@ void launch_i8_to_f16(const int8_t* x, __half* y, long long n, cudaStream_t s) {
 void launch_bf16_to_f32(const __nv_bfloat16* x, float* y, long long n, cudaStream_t s) {
     const long long blocks = (n + 255) / 256;
     launch_k(bf16_to_f32_kernel, dim3((int)(blocks < 4096 ? blocks : 4096)), dim3(256), 0, s, x, y, n);
+}
+
+void prefer_max_shared(const void* kernel) {
+    static std::mutex mu;
+    static std::set<std::pair<int, const void*>> done;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> g(mu);
+    if (done.insert({dev, kernel}).second)
+        cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
 }
 
 bool pdl_enabled() {

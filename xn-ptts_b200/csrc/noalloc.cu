@@ -152,6 +152,7 @@ extern "C" int ptts_b200_attend_decode_noalloc(void* k_cache, void* v_cache, int
     a.err = err;
     a.capacity = capacity;  // no ring or windowed stream here (ring_write and window stay null)
     a.cta_first = plan.cta_first;
+    a.prestart = true;  // rope_append sits between the plan and this launch
     launch_decode_attn(a, kv_dtype == PTTS_B200_BF16, sc.grid, s);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return refuse(PTTS_B200_ERR_CUDA, std::string("kernel launch: ") + cudaGetErrorString(e));
