@@ -40,8 +40,9 @@ constexpr int kThreadsTma = 128;
 // WLO: the weights come as two planes too (hi, lo), and each k step runs a third MMA.
 template <int RT, bool WLO>
 struct TmaTile {
-    // 3 stages: 74 KB for f16 weights, so a CTA fits beside the decode attention's compact ring.
-    static constexpr int kStages = 3;
+    // Decode tiles (RT 32) of f16 weights take 3 stages (74 KB) so that a CTA fits beside the
+    // decode attention's compact ring (137 KB) on one SM; prompt tiles take 4.
+    static constexpr int kStages = (WLO || RT == 32) ? 3 : 4;
     static constexpr int kWBytes = FT * KS * 2;  // 16 KB per weight plane
     static constexpr int kXBytes = RT * KS * 2;  // per activation plane
     static constexpr int kStageBytes = (WLO ? 2 : 1) * kWBytes + 2 * kXBytes;
