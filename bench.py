@@ -343,8 +343,9 @@ def run_ours(args):
     ms = timed(dev_src, y, args.steps)
     clocks = sampler.stop()
     value = world * B * args.steps / (ms / 1e3)
-    launches_per_step = 3 + 7 * L  # plan, final reduce, advance + per layer LN1, in_proj,
-    #                                 attention (merge fused), out_proj, LN2, linear1, linear2
+    lanes = ptts.step_lanes(B)
+    launches_per_step = 1 + lanes * (2 + 7 * L)  # advance + per lane: plan, final reduce and per
+    #                       layer LN1, in_proj, attention (merge fused), out_proj, LN2, linear1, linear2
     gpu_launches = args.steps * launches_per_step + (args.warmup + args.steps) // FRAMES
 
     # ---- end to end through pinned host buffers ------------------------------------------------
@@ -388,6 +389,43 @@ def run_ours(args):
                 "attn_share_of_traced_step": tr["attn_ms"] / max(tr["step_ms"], 1e-9)}
     if traffic:
         roofline["traffic_source"] = "scaled from profiles/decode_attn_traffic.json: " + traffic.get("source", "")
+    kv_bytes_per_step = tr["attn_bytes"] / max(tr["steps"], 1)
+
+    # ---- kernel timeline inside the graph (device stamps), for the attention as it runs there --
+    # Events around a launch cut it off from its neighbours; the stamps do not. The last of a few
+    # graph-replayed steps is read: per attention launch, from its first CTA past the wait on its
+    # predecessor to its last CTA done (and from its first CTA's start, which also counts the
+    # copies issued before that wait).
+    kv.set_lengths(streams, prefixes)
+    state["f"] = 0
+    model.stamps(lanes * (2 + 8 * L))
+    stamped = 12
+    for _ in range(stamped):
+        step(dev_src, y)
+    torch.cuda.synchronize()
+    stamps = model.read_stamps()
+    model.stamps(0)
+    att = [e for e in stamps if e["kernel"] == "attention"]
+    kv_rows = float(prefixes.sum()) + B * stamped  # attended keys of the stamped step
+    bytes_stamped = L * (kv_rows * 2 * 1024 + B * 512 * 6)
+    busy = sum(e["end_us"] - e["start_us"] for e in att)
+    busy_entry = sum(e["end_us"] - e["entry_us"] for e in att)
+    if att and busy > 0:
+        roofline["in_frame"] = {
+            "source": "device stamps (globaltimer) of the attention launches of one graph-replayed step "
+                      f"(frame {stamped} of the window)",
+            "launches": len(att), "us_per_launch": busy / len(att),
+            "achieved": bytes_stamped / (busy / 1e6) / 1e9,
+            "frac": bytes_stamped / (busy / 1e6) / 1e9 / peak,
+            "us_per_launch_from_first_cta": busy_entry / len(att),
+            "frac_from_first_cta": bytes_stamped / (busy_entry / 1e6) / 1e9 / peak,
+            "step_us": max(e["end_us"] for e in stamps)}
+    if args.timeline:
+        with open(args.timeline, "w") as f:
+            f.write("lane layer kernel       entry_us  start_us    end_us\n")
+            for e in stamps:
+                f.write(f"{e['lane']:4d} {e['layer']:5d} {e['kernel']:10s} {e['entry_us']:9.2f} "
+                        f"{e['start_us']:9.2f} {e['end_us']:9.2f}\n")
 
     # ---- whole frames: input_linear -> step -> out_norm -> EOS + flow net (ptts_b200_frame) ----
     # An extra line item (the headline value above is the backbone step the configs define):
@@ -440,8 +478,9 @@ def run_ours(args):
             "config": {"workload": desc,
                        "streams_per_gpu": B, "total_streams": world * B, "layers": L,
                        "kv_capacity": cap, "parallelism": f"stream-sharded x{world}, no collectives",
-                       "l2": f"inputs larger than L2: {per_launch_bytes * L / 1e9:.2f} GB of KV read per step per GPU"
-                             if per_launch_bytes * L > 126e6 else "KV per step fits in L2 (no flush)"},
+                       "lanes": lanes,
+                       "l2": f"inputs larger than L2: {kv_bytes_per_step / 1e9:.2f} GB of KV read per step per GPU"
+                             if kv_bytes_per_step > 126e6 else "KV per step fits in L2 (no flush)"},
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": gpu_launches,
             "clocks": clocks, "prefill_ms": prefill_ms, "frame_with_flow_head": flow_frame,
             "prefill_rows_per_s": world * float(prefixes.sum()) / (prefill_ms / 1e3),
@@ -592,6 +631,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--timeline", default="",
+                    help="write the kernel timeline (device stamps) of one decode step to this file")
     ap.add_argument("--no-flow", action="store_true",
                     help="skip the extra line item: whole frames with the flow head (ptts_b200_frame)")
     ap.add_argument("--workload", choices=["config5", "config4", "config3", "config2"], default="config5",

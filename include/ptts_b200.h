@@ -323,6 +323,24 @@ int ptts_b200_set_tracing(int on);
 /* Read (and with reset != 0, clear) the counters. */
 int ptts_b200_trace_read(ptts_b200_trace* out, int reset);
 
+/* Kernel timeline of a model's decode steps, taken inside its CUDA graph (where events cannot
+ * time single kernels without changing how they overlap). While on, every kernel of the layer
+ * stack stamps the GPU's global timer when its first CTA starts, when its first CTA is past its
+ * wait on the predecessor kernel, and when its last CTA is done; read returns the launches of
+ * the last step, in launch order per lane. A step records a separate graph while stamps are on.
+ * max_launches 0 turns stamps off. */
+typedef struct {
+    char kernel[16];   /* "ln1", "in_proj", "attention", "out_proj", "ln2", "linear1", "linear2",
+                          "ln_out" (the last residual reduction) */
+    int lane;          /* 0, or 1 for the second lane of a two-lane step */
+    int layer;
+    double entry_us;   /* first CTA started, from the step's first stamp */
+    double start_us;   /* first CTA past its wait on the predecessor */
+    double end_us;     /* last CTA done */
+} ptts_b200_stamp;
+int ptts_b200_model_stamps(ptts_b200_model* model, int max_launches);
+int ptts_b200_model_stamps_read(ptts_b200_model* model, ptts_b200_stamp* out, int max, int* n);
+
 /* ---- Flow head: the rest of a frame -------------------------------------------------------
  * FlowLM's per-frame tail (flow_lm.rs:296-324, :360-410) and its flow net SimpleMLPAdaLN
  * (mlp.rs): out_norm -> EOS logit (out_eos) and the latent from the solver's starting point

@@ -258,3 +258,39 @@ def test_grouped_query_attention_in_the_stack(ptts, oracle, cuda):
     kv.check()
     print("gqa", ["%.2e" % e for e in errs])
     assert max(errs) < TOL
+
+
+def test_kernel_stamps_of_a_two_lane_step(ptts, cuda):
+    """The kernel timeline (ptts_b200_model_stamps) of a two-lane step: every launch of both
+    lanes is stamped, each kernel starts after its predecessor in the lane ended, and the
+    stamped step's output equals an unstamped step's bit for bit."""
+    import torch
+    cfg = ptts.FlowLMConfig(num_layers=2)
+    S, P = 160, 12
+    w = ptts.random_weights(cfg, 61)
+    model = ptts.Transformer(cfg)
+    model.load(w)
+    kvs = [ptts.KvState(cfg.num_layers, S, 32, dtype="bf16") for _ in range(2)]
+    g = torch.Generator().manual_seed(61)
+    x = torch.randn(S * P, 512, generator=g).bfloat16().to(cuda)
+    for kv in kvs:
+        model.forward(kv, x, list(range(S)), [P] * S)
+    xs = torch.randn(S, 512, generator=g).bfloat16().to(cuda)
+    plain = model.step(kvs[0], list(range(S)), xs).clone()
+    model.stamps(64)
+    stamped = model.step(kvs[1], list(range(S)), xs).clone()
+    st = model.read_stamps()
+    model.stamps(0)
+    assert torch.equal(plain, stamped)
+    kernels = ["ln1", "in_proj", "attention", "out_proj", "ln2", "linear1", "linear2"]
+    for lane in (0, 1):
+        seq = [e for e in st if e["lane"] == lane]
+        assert [e["kernel"] for e in seq] == kernels * cfg.num_layers + ["ln_out"]
+        assert [e["layer"] for e in seq[:-1]] == [l for l in range(cfg.num_layers) for _ in kernels]
+        for a, b in zip(seq, seq[1:]):
+            assert 0 <= b["entry_us"] <= b["start_us"] <= b["end_us"]
+            assert b["start_us"] >= a["end_us"] - 0.1, (a, b)
+    with pytest.raises(ptts.PttsError, match="stamps are off"):
+        model.read_stamps()
+    model.step(kvs[0], list(range(S)), xs)  # the unstamped graph again
+    kvs[0].check()

@@ -47,6 +47,7 @@ EXPORTS = (
     "ptts_b200_kv_start_ring", "ptts_b200_kv_set_ring_slot", "ptts_b200_kv_evict",
     "ptts_b200_model_config", "ptts_b200_model_load_layer_f32", "ptts_b200_model_load_layer_q8_0",
     "ptts_b200_load_gguf", "ptts_b200_gguf_remap_key", "ptts_b200_kv_set_window",
+    "ptts_b200_model_stamps", "ptts_b200_model_stamps_read",
 )
 
 
@@ -98,6 +99,12 @@ class Trace(ctypes.Structure):
                 ("step_ms", ctypes.c_double)]
 
 
+class Stamp(ctypes.Structure):
+    """ptts_b200_stamp: one launch of the kernel timeline (see Transformer.stamps)."""
+    _fields_ = [("kernel", ctypes.c_char * 16), ("lane", ctypes.c_int), ("layer", ctypes.c_int),
+                ("entry_us", ctypes.c_double), ("start_us", ctypes.c_double), ("end_us", ctypes.c_double)]
+
+
 class LayerWeights(ctypes.Structure):
     _fields_ = [(n, P) for n in (
         "in_proj_host", "in_proj_scale_host", "out_proj_host", "out_proj_scale_host",
@@ -135,6 +142,8 @@ def lib() -> ctypes.CDLL:
         L.ptts_b200_kv_set_lengths.argtypes = [P, IP, IP, I, P]
         L.ptts_b200_set_tracing.argtypes = [I]
         L.ptts_b200_trace_read.argtypes = [ctypes.POINTER(Trace), I]
+        L.ptts_b200_model_stamps.argtypes = [P, I]
+        L.ptts_b200_model_stamps_read.argtypes = [P, ctypes.POINTER(Stamp), I, IP]
         L.ptts_b200_kv_load_prefix.argtypes = [P, I, I, P, P, I, I, P]
         L.ptts_b200_kv_copy_stream.argtypes = [P, I, P, I, P]
         L.ptts_b200_kv_check.argtypes = [P]
@@ -368,6 +377,12 @@ def attend(kv: KvState, layer: int, q, k, v, streams: Sequence[int], rows: Seque
     return out
 
 
+def step_lanes(n: int) -> int:
+    """How many lanes a decode step of n rows runs in (the library's rule: two from 128 rows,
+    one with PTTS_B200_LANES=1)."""
+    return 1 if os.environ.get("PTTS_B200_LANES", "").startswith("1") or n < 128 else 2
+
+
 def set_tracing(on: bool):
     """Process-wide: while on, Transformer.step runs un-graphed and it and attend() time every
     decode-attention launch with CUDA events (one synchronisation per call)."""
@@ -510,6 +525,18 @@ class Transformer:
         _check(lib().ptts_b200_step(self._h, kv.handle, _ip(s), len(s), ctypes.c_void_p(x.data_ptr()),
                                     ctypes.c_void_p(out.data_ptr()), _stream(stream)))
         return out
+
+    def stamps(self, max_launches: int):
+        """ptts_b200_model_stamps: kernel timeline of decode steps on (max_launches slots) or off (0)."""
+        _check(lib().ptts_b200_model_stamps(self._h, int(max_launches)))
+
+    def read_stamps(self) -> list:
+        """The last step's launches: dicts of kernel, lane, layer and entry/start/end in µs."""
+        buf = (Stamp * 4096)()
+        n = ctypes.c_int(0)
+        _check(lib().ptts_b200_model_stamps_read(self._h, buf, 4096, ctypes.byref(n)))
+        return [{"kernel": b.kernel.decode(), "lane": b.lane, "layer": b.layer, "entry_us": b.entry_us,
+                 "start_us": b.start_us, "end_us": b.end_us} for b in buf[:n.value]]
 
 
 # --------------------------------------------------------------------------------------------

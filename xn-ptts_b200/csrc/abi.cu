@@ -151,7 +151,25 @@ struct ptts_b200_kv {
 struct GraphKey {
     uint64_t flow = 0;  // the flow head's identity and workspace generation (0: a plain step)
     bool bos = false;
-    bool operator==(const GraphKey& o) const { return flow == o.flow && bos == o.bos; }
+    bool stamps = false;  // recorded with kernel timeline stamps
+    bool operator==(const GraphKey& o) const { return flow == o.flow && bos == o.bos && stamps == o.stamps; }
+};
+
+// Kernel timeline of the last step (ptts_b200_model_stamps): four u64 words per launch slot,
+// filled by the kernels (stamp_mark), and each slot's kernel, lane and layer.
+struct StampLog {
+    DevBuf buf;
+    int cap = 0, next = 0;
+    std::vector<ptts_b200_stamp> meta;
+    unsigned long long* words() const { return buf.as<unsigned long long>(); }
+    int take(const char* kernel, int lane, int layer) {
+        if (next >= cap) return -1;
+        ptts_b200_stamp& m = meta[next];
+        std::snprintf(m.kernel, sizeof m.kernel, "%s", kernel);
+        m.lane = lane;
+        m.layer = layer;
+        return next++;
+    }
 };
 
 // One lane of a decode step: rows off .. off + n - 1 of the stream set, with its own row plan
@@ -203,6 +221,7 @@ struct ptts_b200_model {
     cudaStream_t capture_stream = nullptr, lane_stream = nullptr;
     cudaEvent_t lane_start = nullptr, lane_join = nullptr;  // fork / join of a two-lane step
     std::vector<cudaEvent_t> events;  // tracing: [2 * layers] per lane around attention, step start / end
+    StampLog stamps;
     ~ptts_b200_model() {
         step.reset();
         frame.reset();
@@ -340,7 +359,8 @@ struct Tiles {
 
 void attention(const ptts_b200_kv* kv, int layer, bool decode, const RowPlan& plan, int n_rows,
                const float* q_rot, void* out, void* out_lo, int out_mode, DevBuf& part,
-               DevBuf& counters, const Tiles& tiles, cudaStream_t s, bool compact = false) {
+               DevBuf& counters, const Tiles& tiles, cudaStream_t s, bool compact = false,
+               unsigned long long* stamps = nullptr, int stamp = -1) {
     const bool bf16 = kv->dtype == PTTS_B200_BF16;
     const float qscale = (1.0f / sqrtf((float)kv->head_dim)) * kLog2e;  // transformer.rs:215
     if (decode) {
@@ -367,6 +387,8 @@ void attention(const ptts_b200_kv* kv, int layer, bool decode, const RowPlan& pl
         a.window = kv->window.as<int32_t>();
         a.row_pos = plan.row_pos;
         a.prestart = true;  // the in_proj or rope_append launch sits between the plan and this one
+        a.stamps = stamps;
+        a.stamp = stamp;
         launch_decode_attn(a, bf16, grid, s, compact);
     } else {
         PrefillArgs a{};
@@ -423,8 +445,10 @@ int split_for(int rows, int k, int want) {
 // `lane`: this is one of two lanes of a decode step running side by side; the attention takes
 // its compact ring, and `after_qkv0` (if set) is recorded once the first in_proj is launched.
 struct LaneOpts {
+    int id = 0;
     bool lane = false;
     cudaEvent_t after_qkv0 = nullptr;
+    StampLog* stamps = nullptr;  // kernel timeline, or none
 };
 void run_layers(const ptts_b200_model* m, const ptts_b200_kv* kv, bool decode, const RowPlan& plan,
                 int rows, const __nv_bfloat16* x_in, float* resid, Workspace& w, cudaStream_t s,
@@ -438,7 +462,14 @@ void run_layers(const ptts_b200_model* m, const ptts_b200_kv* kv, bool decode, c
     auto* h_lo = w.h_lo.as<__half>();
     auto* split = w.split.as<float>();
     int pending = 0;  // split-K slices not yet added to the residual
-    auto ln = [&](const float* g, const float* b, const __nv_bfloat16* x_bf16, bool normalise) {
+    int layer = 0;
+    // A timeline slot for the next launch, when stamps are on.
+    auto stamp = [&](auto& args, const char* kernel) {
+        if (!lo.stamps) return;
+        args.stamps = lo.stamps->words();
+        args.stamp = lo.stamps->take(kernel, lo.id, layer);
+    };
+    auto ln = [&](const float* g, const float* b, const __nv_bfloat16* x_bf16, bool normalise, const char* name) {
         LnArgs a{};
         a.M = rows;
         a.d = c.d_model;
@@ -450,6 +481,7 @@ void run_layers(const ptts_b200_model* m, const ptts_b200_kv* kv, bool decode, c
         a.beta = b;
         a.hi = normalise ? h_hi : nullptr;
         a.lo = normalise ? h_lo : nullptr;
+        stamp(a, name);
         launch_ln(a, s);
         check_launch();
         pending = 0;
@@ -469,14 +501,16 @@ void run_layers(const ptts_b200_model* m, const ptts_b200_kv* kv, bool decode, c
         o.scale = sc.as<float>();
         o.y = splits > 1 ? split : resid;
         o.err = err;
+        stamp(o, k == c.d_model ? "out_proj" : "linear2");
         require(launch_linear(o, splits > 1 ? EPI_PARTIAL : EPI_RESID, s), PTTS_B200_ERR_UNSUPPORTED,
                 "no kernel for this linear's shape");
         check_launch();
         if (splits > 1) pending = splits;
     };
     for (int l = 0; l < c.num_layers; ++l) {
+        layer = l;
         const auto& L = *m->layers[l];
-        ln(L.ln1g.as<float>(), L.ln1b.as<float>(), l == 0 ? x_in : nullptr, true);
+        ln(L.ln1g.as<float>(), L.ln1b.as<float>(), l == 0 ? x_in : nullptr, true, "ln1");
         // in_proj, RoPE + append epilogue
         LinearArgs a{};
         a.M = rows;
@@ -501,19 +535,22 @@ void run_layers(const ptts_b200_model* m, const ptts_b200_kv* kv, bool decode, c
         require(m->rope_rows >= kv->capacity, PTTS_B200_ERR_STATE, "RoPE table shorter than the cache");
         a.rope = m->rope.as<float2>();
         a.err = err;
+        stamp(a, "in_proj");
         require(launch_linear(a, EPI_QKV, s), PTTS_B200_ERR_UNSUPPORTED, "no kernel for in_proj's shape");
         check_launch();
         if (l == 0 && lo.after_qkv0) CK(cudaEventRecord(lo.after_qkv0, s));
         // attention over the cache
         if (attn_ev) CK(cudaEventRecord(attn_ev[2 * l], s));
+        DecodeArgs stamped;  // carries the attention's timeline slot
+        stamp(stamped, "attention");
         attention(kv, l, decode, plan, rows, w.q_rot.as<float>(), w.attn_hi.p, w.attn_lo.p,
-                  kOutHiLo, w.part, w.counters, tiles, s, lo.lane);
+                  kOutHiLo, w.part, w.counters, tiles, s, lo.lane, stamped.stamps, stamped.stamp);
         if (attn_ev) CK(cudaEventRecord(attn_ev[2 * l + 1], s));
         // out_proj + residual
         residual_gemm(w.attn_hi.as<__half>(), w.attn_lo.as<__half>(), L.w_out, L.h_out, L.l_out, L.s_out,
                       hd, s_out);
         // LN2, linear1 + GELU
-        ln(L.ln2g.as<float>(), L.ln2b.as<float>(), nullptr, true);
+        ln(L.ln2g.as<float>(), L.ln2b.as<float>(), nullptr, true, "ln2");
         LinearArgs f1{};
         f1.M = rows;
         f1.N = c.dim_feedforward;
@@ -528,13 +565,14 @@ void run_layers(const ptts_b200_model* m, const ptts_b200_kv* kv, bool decode, c
         f1.yb_lo = w.ff_lo.as<__half>();
         f1.gelu_tanh = c.gelu;
         f1.err = err;
+        stamp(f1, "linear1");
         require(launch_linear(f1, EPI_GELU, s), PTTS_B200_ERR_UNSUPPORTED, "no kernel for linear1's shape");
         check_launch();
         // linear2 + residual
         residual_gemm(w.ff_hi.as<__half>(), w.ff_lo.as<__half>(), L.w2, L.h2, L.l2, L.s2,
                       c.dim_feedforward, s_ff2);
     }
-    if (pending) ln(nullptr, nullptr, nullptr, false);
+    if (pending) ln(nullptr, nullptr, nullptr, false, "ln_out");
 }
 
 // Grows the RoPE table to `rows` positions. A captured step graph holds the old table's address,
@@ -682,8 +720,10 @@ void run_step(ptts_b200_model* model, ptts_b200_kv* kv, const int32_t* streams_h
     ensure_rope(model, kv->capacity, s);
     const int grid = sm_count(kv->device);
     const int n_lanes = step_lanes(n);
+    GraphKey gkey = key;
+    gkey.stamps = model->stamps.cap > 0;
     StepGraph* g = slot.get();
-    const bool same = g && g->kv == kv && g->kv_uid == kv->uid && g->key == key && g->streams.size() == (size_t)n &&
+    const bool same = g && g->kv == kv && g->kv_uid == kv->uid && g->key == gkey && g->streams.size() == (size_t)n &&
                       g->n_lanes == n_lanes &&
                       std::memcmp(g->streams.data(), streams_host, sizeof(int32_t) * n) == 0;
     if (!same) {
@@ -694,7 +734,7 @@ void run_step(ptts_b200_model* model, ptts_b200_kv* kv, const int32_t* streams_h
         ng->streams.assign(streams_host, streams_host + n);
         ng->kv = kv;
         ng->kv_uid = kv->uid;
-        ng->key = key;
+        ng->key = gkey;
         int32_t* sid = static_cast<int32_t*>(ng->sid.need(sizeof(int32_t) * n));
         CK(cudaMemcpy(sid, streams_host, sizeof(int32_t) * n, cudaMemcpyHostToDevice));
         ng->x.need((size_t)n * c.d_model * 2);
@@ -734,6 +774,11 @@ void run_step(ptts_b200_model* model, ptts_b200_kv* kv, const int32_t* streams_h
     }
     // `cs2` is the second lane's stream (== cs when the lanes run one after the other).
     auto body = [&](cudaStream_t cs, cudaStream_t cs2, cudaEvent_t* ev) {
+        StampLog* stamps = gkey.stamps ? &model->stamps : nullptr;
+        if (stamps) {
+            CK(cudaMemsetAsync(stamps->buf.p, 0xFF, sizeof(unsigned long long) * 4 * stamps->cap, cs));
+            stamps->next = 0;
+        }
         if constexpr (!std::is_same_v<std::decay_t<Pre>, std::nullptr_t>) pre(cs);
         for (int i = 0; i < n_lanes; ++i) {
             StepLane& ln = g->lanes[i];
@@ -743,7 +788,9 @@ void run_step(ptts_b200_model* model, ptts_b200_kv* kv, const int32_t* streams_h
             launch_plan_decode(kv->len.as<int32_t>(), sid + ln.off, ln.n, kv->streams, kv->capacity, plan,
                                kv->ring(), grid, kv->err.as<uint32_t>(), ls);
             LaneOpts lo;
+            lo.id = i;
             lo.lane = n_lanes > 1;
+            lo.stamps = stamps;
             lo.after_qkv0 = (i == 0 && n_lanes > 1 && cs2 != cs) ? model->lane_start : nullptr;
             run_layers(model, kv, true, plan, ln.n, g->x.as<__nv_bfloat16>() + (size_t)ln.off * c.d_model,
                        g->resid.as<float>() + (size_t)ln.off * c.d_model, ln.ws, ls,
@@ -1360,6 +1407,44 @@ int ptts_b200_frame(ptts_b200_model* model, ptts_b200_flow* flow, ptts_b200_kv* 
         };
         CK(cudaMemcpyAsync(latent_out, g->lat_out.p, lb, back(latent_out), s));
         CK(cudaMemcpyAsync(eos, g->eos.p, (size_t)n * 4, back(eos), s));
+    });
+}
+
+int ptts_b200_model_stamps(ptts_b200_model* model, int max_launches) {
+    return guarded([&] {
+        require(model != nullptr, PTTS_B200_ERR_ARG, "model is NULL");
+        require(max_launches >= 0, PTTS_B200_ERR_ARG, "max_launches must be >= 0");
+        DeviceScope scope(model->device);
+        CK(cudaDeviceSynchronize());
+        StampLog& st = model->stamps;
+        if (max_launches > 0) st.buf.need(sizeof(unsigned long long) * 4 * (size_t)max_launches);
+        st.cap = max_launches;
+        st.next = 0;
+        st.meta.assign((size_t)max_launches, ptts_b200_stamp{});
+    });
+}
+
+int ptts_b200_model_stamps_read(ptts_b200_model* model, ptts_b200_stamp* out, int max, int* n) {
+    return guarded([&] {
+        require(model != nullptr && out != nullptr && n != nullptr, PTTS_B200_ERR_ARG, "NULL argument");
+        DeviceScope scope(model->device);
+        const StampLog& st = model->stamps;
+        require(st.cap > 0, PTTS_B200_ERR_STATE, "stamps are off (ptts_b200_model_stamps)");
+        CK(cudaDeviceSynchronize());
+        std::vector<unsigned long long> w((size_t)4 * st.next);
+        if (st.next > 0) CK(cudaMemcpy(w.data(), st.buf.p, w.size() * 8, cudaMemcpyDeviceToHost));
+        unsigned long long t0 = ~0ull;
+        for (int i = 0; i < st.next; ++i) t0 = std::min(t0, w[4 * i + STAMP_ENTRY]);
+        auto us = [&](unsigned long long t) { return t == ~0ull ? -1.0 : (double)(t - t0) / 1000.0; };
+        const int k = std::min(max, st.next);
+        for (int i = 0; i < k; ++i) {
+            out[i] = st.meta[i];
+            out[i].entry_us = us(w[4 * i + STAMP_ENTRY]);
+            out[i].start_us = us(w[4 * i + STAMP_START]);
+            const unsigned long long e = w[4 * i + STAMP_END];
+            out[i].end_us = e == ~0ull ? -1.0 : us(~e);
+        }
+        *n = k;
     });
 }
 

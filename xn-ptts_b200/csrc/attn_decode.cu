@@ -195,7 +195,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(DecodeArgs a) 
     // With `prestart` the plan is complete before the predecessor began, so it is read now; the
     // producer waits for the predecessor (which writes q and this step's cache rows) only before
     // the first copy that needs either.
+    if (threadIdx.x == 0) stamp_mark(a.stamps, a.stamp, STAMP_ENTRY);
     if (!a.prestart) grid_dep_wait();
+    if (!a.prestart && threadIdx.x == 0) stamp_mark(a.stamps, a.stamp, STAMP_START);
     const long long total = a.prefix[a.B];
     const int G = ctas_in_use(total, gridDim.x);
     const int c = blockIdx.x;
@@ -240,6 +242,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(DecodeArgs a) 
         int q_stage[kStages], q_row[kStages], n_deferred = 0;
         auto wait_predecessor = [&]() {
             grid_dep_wait();
+            stamp_mark(a.stamps, a.stamp, STAMP_START);
             waited = true;
             for (int i = 0; i < n_deferred; ++i)
                 bulk_g2s(smem + q_stage[i] * kStageBytes + kDataBytes, a.q + (long long)q_row[i] * kRowWidth,
@@ -462,6 +465,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(DecodeArgs a) 
             merge_head(a, b, h, hd.c0, hd.c1, lane);
         }
     }
+    if (lane == 0) stamp_mark(a.stamps, a.stamp, STAMP_END);
 }
 
 template <typename T, class R>

@@ -77,6 +77,17 @@ __device__ __forceinline__ void bulk_g2s(void* smem_dst, const void* gmem_src, u
         : "memory");
 }
 
+// Kernel timeline: slot s of `stamps` holds four u64 words, each the minimum over the CTAs that
+// mark it: [0] global timer at entry, [1] after the wait on the predecessor, [2] the bitwise
+// complement of the timer at the end (so the minimum is the last end). The host fills the slots
+// with all-ones before the step.
+__device__ __forceinline__ void stamp_mark(unsigned long long* stamps, int slot, int field) {
+    if (!stamps || slot < 0) return;
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    atomicMin(stamps + 4 * slot + field, field == STAMP_END ? ~t : t);
+}
+
 __device__ __forceinline__ uint64_t policy_evict_first() {
     uint64_t p;
     asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));

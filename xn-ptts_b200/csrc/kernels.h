@@ -42,6 +42,10 @@ inline cudaError_t launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, siz
     return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
+// Words of a kernel-timeline slot (stamp_mark): first entry, first start past the wait on the
+// predecessor, and the complement of the last end.
+enum { STAMP_ENTRY = 0, STAMP_START = 1, STAMP_END = 2 };
+
 constexpr int kHeadDim = 64;   // D: the only head size the kernels implement
 constexpr int kRowWidth = 512; // H * D: one cache row of all heads
 constexpr int kMaxPairs = kHeadDim / 2;
@@ -148,6 +152,8 @@ void launch_rope_append(const RopeAppendArgs& a, bool in_bf16, bool cache_bf16, 
 // ---- attention (attn_decode.cu, attn_prefill.cu) -----------------------------------------
 
 struct DecodeArgs {
+    unsigned long long* stamps = nullptr;  // kernel timeline slot (see stamp_mark), or none
+    int stamp = -1;
     const void* k_cache;      // layer base [S][cap][H][D]
     const void* v_cache;
     long long stream_bytes;   // capacity * row bytes
@@ -219,6 +225,8 @@ enum LinearEpi : int {
 };
 
 struct LinearArgs {
+    unsigned long long* stamps = nullptr;  // kernel timeline slot (see stamp_mark), or none
+    int stamp = -1;
     int M, N, K;
     int splits = 1;           // split-K slices (gridDim.z); EPI_PARTIAL writes slice z
     const void* a;            // A hi plane [M][K]: f16 (a_f16) or bf16
@@ -333,6 +341,8 @@ void launch_i8_to_f16(const int8_t* x, __half* y, long long n, cudaStream_t s);
 // + sum of `nsplit` partial slices [nsplit][M][d]; then, when hi != nullptr, LayerNorm(resid)
 // (gamma, beta, eps 1e-5) written as f16 hi/lo planes. d in {128, 256, 512, 1024}.
 struct LnArgs {
+    unsigned long long* stamps = nullptr;  // kernel timeline slot (see stamp_mark), or none
+    int stamp = -1;
     int M, d;
     float* resid;
     const __nv_bfloat16* x_bf16;

@@ -355,7 +355,9 @@ __global__ void __launch_bounds__(kThreads) linear_kernel(LinearArgs p) {
 // PER = d_model / 32 floats per lane.
 template <int PER>
 __global__ void __launch_bounds__(128) ln_kernel(LnArgs a) {
+    if (threadIdx.x == 0) stamp_mark(a.stamps, a.stamp, STAMP_ENTRY);
     grid_dep_wait();
+    if (threadIdx.x == 0) stamp_mark(a.stamps, a.stamp, STAMP_START);
     grid_dep_launch();
     const int row = blockIdx.x * 4 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (row >= a.M) return;
@@ -394,7 +396,10 @@ __global__ void __launch_bounds__(128) ln_kernel(LnArgs a) {
         v[4 * i] = y.x; v[4 * i + 1] = y.y; v[4 * i + 2] = y.z; v[4 * i + 3] = y.w;
         if (a.x_bf16 || a.nsplit) *reinterpret_cast<float4*>(xr + 4 * (lane + 32 * i)) = y;
     }
-    if (!a.hi) return;  // reduce only
+    if (!a.hi) {  // reduce only
+        if (lane == 0) stamp_mark(a.stamps, a.stamp, STAMP_END);
+        return;
+    }
     float sum = 0.f;
 #pragma unroll
     for (int i = 0; i < PER; ++i) sum += v[i];
@@ -421,6 +426,7 @@ __global__ void __launch_bounds__(128) ln_kernel(LnArgs a) {
         *reinterpret_cast<uint2*>(a.hi + (long long)row * d + k) = make_uint2(h01, h23);
         *reinterpret_cast<uint2*>(a.lo + (long long)row * d + k) = make_uint2(l01, l23);
     }
+    if (lane == 0) stamp_mark(a.stamps, a.stamp, STAMP_END);
 }
 
 template <int EPI, int TM, bool F16>

@@ -327,6 +327,7 @@ __global__ void __launch_bounds__(kThreadsTma) linear_tma_kernel(const __grid_co
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
+    if (tid == 0) stamp_mark(p.stamps, p.stamp, STAMP_ENTRY);
     if (tid == 0) {
         // ---- TMA producer ----------------------------------------------------------------------
         const uint64_t pol_w = policy_evict_last();  // weights: reread every frame
@@ -337,6 +338,7 @@ __global__ void __launch_bounds__(kThreadsTma) linear_tma_kernel(const __grid_co
             if (WLO) tma_load_2d_hint(base + kt * T::kStageBytes + T::kWBytes, &tm_wlo, k0 + kt * KS, n0, &full[kt], pol_w);
         }
         grid_dep_wait();
+        stamp_mark(p.stamps, p.stamp, STAMP_START);
         for (int kt = 0; kt < KT; ++kt) {
             const int st = kt % S;
             const uint32_t sa = base + st * T::kStageBytes;
@@ -407,6 +409,7 @@ __global__ void __launch_bounds__(kThreadsTma) linear_tma_kernel(const __grid_co
         }
     }
 
+    if (tid == 0) stamp_mark(p.stamps, p.stamp, STAMP_END);
     tc_fence_before();
     __syncthreads();
     if (tid == 0) {
