@@ -456,7 +456,7 @@ void run_layers(const ptts_b200_model* m, const ptts_b200_kv* kv, bool decode, c
     const ptts_b200_config& c = m->cfg;
     const int hd = c.num_heads * c.head_dim;
     const int nqkv = hd + 2 * c.num_kv_heads * c.head_dim;
-    const int s_out = split_for(rows, hd, 2), s_ff2 = split_for(rows, c.dim_feedforward, 4);
+    const int s_out = split_for(rows, hd, 4), s_ff2 = split_for(rows, c.dim_feedforward, 4);
     uint32_t* err = kv->err.as<uint32_t>();
     auto* h_hi = w.h_hi.as<__half>();
     auto* h_lo = w.h_lo.as<__half>();

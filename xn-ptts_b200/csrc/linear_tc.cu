@@ -11,14 +11,16 @@
 // weight tile and B = the activation tile, both K-major. A decode batch of 512 rows gives
 // (N / 128) x 16 CTAs of RT = 32 rows, two CTAs per SM by shared memory; prompts use RT = 128.
 //
-// CTA: 128 threads.
+// CTA: 256 threads (8 warps).
 //   thread 0:   TMA producer over a kStages ring of {W 128x64, X hi RTx64, X lo RTx64} f16
 //               tiles. The weight tiles of the first stages are requested before the wait on
 //               the grid that wrote X (weights never change).
 //   thread 32:  MMA issuer; tcgen05.commit frees each stage and finally signals `done`.
-//   all warps:  epilogue: warp w reads TMEM lanes 32w..32w+31 (features n0 + 32w + lane), 32
-//               rows per tcgen05.ld, into a shared-memory tile; then each warp takes whole rows,
-//               lane l the features 4l..4l+3, so stores are 16 bytes and RoPE pairs in-lane.
+//   all warps:  epilogue: warp w reads TMEM lanes 32 (w % 4) .. + 31 (features n0 + 32 (w % 4)
+//               + lane), 16 rows per tcgen05.ld, into a shared-memory tile; then each warp takes
+//               4 whole rows, lane l the features 4l..4l+3, so stores are 16 bytes and RoPE
+//               pairs in-lane. Eight warps instead of four halve each warp's serial share of
+//               the epilogue (GELU, RoPE), which bounds the decode-size launches.
 // Every wait is bounded (DEV_ERR_TIMEOUT); after a timeout the CTA still waits, bounded, for the
 // copies it issued and frees its TMEM. No clusters, no multicast.
 #include <cuda.h>
@@ -35,7 +37,11 @@ namespace {
 
 constexpr int FT = 128;  // output features per CTA (MMA M)
 constexpr int KS = 64;   // k per stage: one 128-byte swizzle row of f16
-constexpr int kThreadsTma = 128;
+// 8 warps: the MMA-side roles take threads 0 and 32; all eight run the epilogue, two per TMEM
+// lane quarter (warp w reads lanes 32 (w % 4) ..), each then storing 4 of the 32 staged rows.
+constexpr int kEpiWarps = 8;
+constexpr int kThreadsTma = 32 * kEpiWarps;
+constexpr int kRowsPerWarp = 32 / kEpiWarps;
 
 // WLO: the weights come as two planes too (hi, lo), and each k step runs a third MMA.
 template <int RT, bool WLO>
@@ -97,6 +103,21 @@ __device__ __forceinline__ void tc_commit(uint64_t* bar) {
 }
 
 // 32 consecutive f32 columns of this thread's TMEM lane.
+// 16 consecutive TMEM columns of this warp's 32 lanes (tcgen05.ld.32x32b.x16).
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+          "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
     uint32_t r[32];
     asm volatile(
@@ -155,7 +176,7 @@ __device__ __forceinline__ __half f16_sat(float x) {
 constexpr int kStageStride = FT + 4;
 
 // EPI_QKV of 32 staged rows: st[j * kStageStride + c] = accumulator of row mbase + j, tile
-// feature c. Warp w takes rows w, w + 4, ..., lane l features n0 + 4l .. 4l + 3, i.e. the RoPE
+// feature c. Warp w takes rows w, w + 8, ..., lane l features n0 + 4l .. 4l + 3, i.e. the RoPE
 // pairs (4l, 4l+1) and (4l+2, 4l+3) (rope.rs:37-95), with the arithmetic of linear.cu's qkv_pair.
 // Row metadata and every RoPE entry are loaded before the first store.
 __device__ __forceinline__ void qkv_rows(const LinearArgs& p, const float* st, int n0, int mbase) {
@@ -169,17 +190,17 @@ __device__ __forceinline__ void qkv_rows(const LinearArgs& p, const float* st, i
     const int pos_l = ml < p.M ? __ldg(p.row_pos + ml) : 0;     // RoPE position
     const int slot_l = ml < p.M ? __ldg(p.row_slot + ml) : 0;   // cache slot
     const int sid_l = ml < p.M ? __ldg(p.row_stream + ml) : 0;
-    float4 t[8];
+    float4 t[kRowsPerWarp];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        const int pos = __shfl_sync(0xffffffffu, pos_l, warp + 4 * i);
+    for (int i = 0; i < kRowsPerWarp; ++i) {
+        const int pos = __shfl_sync(0xffffffffu, pos_l, warp + kEpiWarps * i);
         t[i] = region != 2 ? __ldg(reinterpret_cast<const float4*>(
                                  p.rope + (long long)min(max(pos, 0), p.capacity - 1) * kMaxPairs + (d >> 1)))
                            : make_float4(1.f, 0.f, 1.f, 0.f);
     }
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        const int j = warp + 4 * i, m = mbase + j;
+    for (int i = 0; i < kRowsPerWarp; ++i) {
+        const int j = warp + kEpiWarps * i, m = mbase + j;
         const int pos = __shfl_sync(0xffffffffu, slot_l, j);
         const int sid = __shfl_sync(0xffffffffu, sid_l, j);
         const float4 a = *reinterpret_cast<const float4*>(st + j * kStageStride + 4 * lane);
@@ -212,7 +233,7 @@ __device__ __forceinline__ void qkv_rows(const LinearArgs& p, const float* st, i
     }
 }
 
-// The other epilogues on the same staged layout (warp w rows w + 4i, lane l features
+// The other epilogues on the same staged layout (warp w rows w + 8i, lane l features
 // n0 + 4l .. 4l + 3), with linear.cu's epilogue_pair arithmetic. EPI_RESID reads all its old
 // values before its first store.
 template <int EPI>
@@ -226,11 +247,11 @@ __device__ __forceinline__ void plain_rows(const LinearArgs& p, const float* st,
         const float4 t = __ldg(reinterpret_cast<const float4*>(p.aux + f));
         bias = make_float4(bias.x + t.x, bias.y + t.y, bias.z + t.z, bias.w + t.w);
     }
-    float4 old[8], gate[8];
+    float4 old[kRowsPerWarp], gate[kRowsPerWarp];
     if (EPI == EPI_RESID || EPI == EPI_GATE_RESID) {
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const int m = mbase + warp + 4 * i;
+        for (int i = 0; i < kRowsPerWarp; ++i) {
+            const int m = mbase + warp + kEpiWarps * i;
             const bool live = m < p.M;
             old[i] = live ? *reinterpret_cast<const float4*>(p.y + (long long)m * p.N + f) : make_float4(0.f, 0.f, 0.f, 0.f);
             if (EPI == EPI_GATE_RESID)
@@ -239,8 +260,8 @@ __device__ __forceinline__ void plain_rows(const LinearArgs& p, const float* st,
         }
     }
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        const int j = warp + 4 * i, m = mbase + j;
+    for (int i = 0; i < kRowsPerWarp; ++i) {
+        const int j = warp + kEpiWarps * i, m = mbase + j;
         if (m >= p.M) break;
         const float4 a = *reinterpret_cast<const float4*>(st + j * kStageStride + 4 * lane);
         const float x0 = a.x * sc.x, x1 = a.y * sc.y, x2 = a.z * sc.z, x3 = a.w * sc.w;
@@ -394,14 +415,16 @@ __global__ void __launch_bounds__(kThreadsTma) linear_tma_kernel(const __grid_co
     tc_fence_after();
 #pragma unroll 1
     for (int c = 0; c < RT; c += 32) {
-        float v[32];
-        tmem_ld32(tmem + ((uint32_t)(32 * warp) << 16) + (uint32_t)c, v);
-        // Transpose through shared memory (the drained ring): lanes then own feature quads and
-        // store 16 bytes per row.
+        // Warp w reads lane quarter w % 4, columns (rows) c + 16 (w / 4) .. + 15, and
+        // transposes them through shared memory (the drained ring): lanes then own feature
+        // quads and store 16 bytes per row.
+        const int quarter = warp & 3, half = warp >> 2;
+        float v[16];
+        tmem_ld16(tmem + ((uint32_t)(32 * quarter) << 16) + (uint32_t)(c + 16 * half), v);
         float* st = reinterpret_cast<float*>(smem);
         __syncthreads();  // the previous chunk's readers are done
 #pragma unroll
-        for (int j = 0; j < 32; ++j) st[j * kStageStride + 32 * warp + lane] = v[j];
+        for (int j = 0; j < 16; ++j) st[(16 * half + j) * kStageStride + 32 * quarter + lane] = v[j];
         __syncthreads();
         if (got) {
             if (EPI == EPI_QKV) qkv_rows(p, st, n0, m0 + c);
