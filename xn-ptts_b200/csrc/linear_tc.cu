@@ -39,7 +39,7 @@ constexpr int FT = 128;  // output features per CTA (MMA M)
 constexpr int KS = 64;   // k per stage: one 128-byte swizzle row of f16
 // 8 warps: the MMA-side roles take threads 0 and 32; all eight run the epilogue, two per TMEM
 // lane quarter (warp w reads lanes 32 (w % 4) ..), each then storing 4 of the 32 staged rows.
-constexpr int kEpiWarps = 8;
+constexpr int kEpiWarps = 16;
 constexpr int kThreadsTma = 32 * kEpiWarps;
 constexpr int kRowsPerWarp = 32 / kEpiWarps;
 
@@ -103,6 +103,18 @@ __device__ __forceinline__ void tc_commit(uint64_t* bar) {
 }
 
 // 32 consecutive f32 columns of this thread's TMEM lane.
+// 8 consecutive TMEM columns of this warp's 32 lanes (tcgen05.ld.32x32b.x8).
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, float (&v)[8]) {
+    uint32_t r[8];
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+                   "=r"(r[7])
+                 : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
+}
+
 // 16 consecutive TMEM columns of this warp's 32 lanes (tcgen05.ld.32x32b.x16).
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
     uint32_t r[16];
@@ -116,6 +128,12 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
     for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+template <int N>
+__device__ __forceinline__ void tmem_ld(uint32_t taddr, float (&v)[N]) {
+    if constexpr (N == 8) tmem_ld8(taddr, v);
+    else tmem_ld16(taddr, v);
 }
 
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
@@ -418,13 +436,14 @@ __global__ void __launch_bounds__(kThreadsTma) linear_tma_kernel(const __grid_co
         // Warp w reads lane quarter w % 4, columns (rows) c + 16 (w / 4) .. + 15, and
         // transposes them through shared memory (the drained ring): lanes then own feature
         // quads and store 16 bytes per row.
-        const int quarter = warp & 3, half = warp >> 2;
-        float v[16];
-        tmem_ld16(tmem + ((uint32_t)(32 * quarter) << 16) + (uint32_t)(c + 16 * half), v);
+        constexpr int CW = 32 / (kEpiWarps / 4);  // columns (rows) per warp
+        const int quarter = warp & 3, part = warp >> 2;
+        float v[CW];
+        tmem_ld<CW>(tmem + ((uint32_t)(32 * quarter) << 16) + (uint32_t)(c + CW * part), v);
         float* st = reinterpret_cast<float*>(smem);
         __syncthreads();  // the previous chunk's readers are done
 #pragma unroll
-        for (int j = 0; j < 16; ++j) st[(16 * half + j) * kStageStride + 32 * quarter + lane] = v[j];
+        for (int j = 0; j < CW; ++j) st[(CW * part + j) * kStageStride + 32 * quarter + lane] = v[j];
         __syncthreads();
         if (got) {
             if (EPI == EPI_QKV) qkv_rows(p, st, n0, m0 + c);
