@@ -422,10 +422,10 @@ def run_ours(args):
             "step_us": max(e["end_us"] for e in stamps)}
     if args.timeline:
         with open(args.timeline, "w") as f:
-            f.write("lane layer kernel       entry_us  start_us    end_us\n")
+            f.write("lane layer kernel       entry_us  start_us    end_us last_entry_us\n")
             for e in stamps:
                 f.write(f"{e['lane']:4d} {e['layer']:5d} {e['kernel']:10s} {e['entry_us']:9.2f} "
-                        f"{e['start_us']:9.2f} {e['end_us']:9.2f}\n")
+                        f"{e['start_us']:9.2f} {e['end_us']:9.2f} {e['last_entry_us']:9.2f}\n")
 
     # ---- whole frames: input_linear -> step -> out_norm -> EOS + flow net (ptts_b200_frame) ----
     # An extra line item (the headline value above is the backbone step the configs define):

@@ -337,6 +337,7 @@ typedef struct {
     double entry_us;   /* first CTA started, from the step's first stamp */
     double start_us;   /* first CTA past its wait on the predecessor */
     double end_us;     /* last CTA done */
+    double last_entry_us; /* last CTA started (a late one waited for room on its SM) */
 } ptts_b200_stamp;
 int ptts_b200_model_stamps(ptts_b200_model* model, int max_launches);
 int ptts_b200_model_stamps_read(ptts_b200_model* model, ptts_b200_stamp* out, int max, int* n);

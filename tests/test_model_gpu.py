@@ -289,6 +289,7 @@ def test_kernel_stamps_of_a_two_lane_step(ptts, cuda):
         assert [e["layer"] for e in seq[:-1]] == [l for l in range(cfg.num_layers) for _ in kernels]
         for a, b in zip(seq, seq[1:]):
             assert 0 <= b["entry_us"] <= b["start_us"] <= b["end_us"]
+            assert b["entry_us"] <= b["last_entry_us"] <= b["end_us"]
             assert b["start_us"] >= a["end_us"] - 0.1, (a, b)
     with pytest.raises(ptts.PttsError, match="stamps are off"):
         model.read_stamps()

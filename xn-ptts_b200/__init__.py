@@ -102,7 +102,8 @@ class Trace(ctypes.Structure):
 class Stamp(ctypes.Structure):
     """ptts_b200_stamp: one launch of the kernel timeline (see Transformer.stamps)."""
     _fields_ = [("kernel", ctypes.c_char * 16), ("lane", ctypes.c_int), ("layer", ctypes.c_int),
-                ("entry_us", ctypes.c_double), ("start_us", ctypes.c_double), ("end_us", ctypes.c_double)]
+                ("entry_us", ctypes.c_double), ("start_us", ctypes.c_double), ("end_us", ctypes.c_double),
+                ("last_entry_us", ctypes.c_double)]
 
 
 class LayerWeights(ctypes.Structure):
@@ -536,7 +537,8 @@ class Transformer:
         n = ctypes.c_int(0)
         _check(lib().ptts_b200_model_stamps_read(self._h, buf, 4096, ctypes.byref(n)))
         return [{"kernel": b.kernel.decode(), "lane": b.lane, "layer": b.layer, "entry_us": b.entry_us,
-                 "start_us": b.start_us, "end_us": b.end_us} for b in buf[:n.value]]
+                 "start_us": b.start_us, "end_us": b.end_us, "last_entry_us": b.last_entry_us}
+                for b in buf[:n.value]]
 
 
 # --------------------------------------------------------------------------------------------

@@ -1441,8 +1441,9 @@ int ptts_b200_model_stamps_read(ptts_b200_model* model, ptts_b200_stamp* out, in
             out[i] = st.meta[i];
             out[i].entry_us = us(w[4 * i + STAMP_ENTRY]);
             out[i].start_us = us(w[4 * i + STAMP_START]);
-            const unsigned long long e = w[4 * i + STAMP_END];
+            const unsigned long long e = w[4 * i + STAMP_END], le = w[4 * i + STAMP_LAST_ENTRY];
             out[i].end_us = e == ~0ull ? -1.0 : us(~e);
+            out[i].last_entry_us = le == ~0ull ? -1.0 : us(~le);
         }
         *n = k;
     });

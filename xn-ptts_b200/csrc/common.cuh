@@ -78,14 +78,16 @@ __device__ __forceinline__ void bulk_g2s(void* smem_dst, const void* gmem_src, u
 }
 
 // Kernel timeline: slot s of `stamps` holds four u64 words, each the minimum over the CTAs that
-// mark it: [0] global timer at entry, [1] after the wait on the predecessor, [2] the bitwise
-// complement of the timer at the end (so the minimum is the last end). The host fills the slots
-// with all-ones before the step.
+// mark it: [0] global timer at entry, [1] after the wait on the predecessor, [2] and [3] the
+// bitwise complements of the timer at the end and at entry (so the minimum is the last end and
+// the last entry). The host fills the slots with all-ones before the step. An entry mark also
+// records the last entry.
 __device__ __forceinline__ void stamp_mark(unsigned long long* stamps, int slot, int field) {
     if (!stamps || slot < 0) return;
     unsigned long long t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
     atomicMin(stamps + 4 * slot + field, field == STAMP_END ? ~t : t);
+    if (field == STAMP_ENTRY) atomicMin(stamps + 4 * slot + STAMP_LAST_ENTRY, ~t);
 }
 
 __device__ __forceinline__ uint64_t policy_evict_first() {

@@ -43,8 +43,8 @@ inline cudaError_t launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, siz
 }
 
 // Words of a kernel-timeline slot (stamp_mark): first entry, first start past the wait on the
-// predecessor, and the complement of the last end.
-enum { STAMP_ENTRY = 0, STAMP_START = 1, STAMP_END = 2 };
+// predecessor, and the complements of the last end and of the last entry.
+enum { STAMP_ENTRY = 0, STAMP_START = 1, STAMP_END = 2, STAMP_LAST_ENTRY = 3 };
 
 constexpr int kHeadDim = 64;   // D: the only head size the kernels implement
 constexpr int kRowWidth = 512; // H * D: one cache row of all heads
