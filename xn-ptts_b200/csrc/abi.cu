@@ -20,7 +20,7 @@ uint64_t ptts_b200_flow_prepare(ptts_b200_flow* f, int n, int d_model);
 int ptts_b200_flow_ldim(const ptts_b200_flow* f);
 void ptts_b200_flow_input(ptts_b200_flow* f, const float* latent, __nv_bfloat16* x, int n, cudaStream_t s);
 void ptts_b200_flow_head(ptts_b200_flow* f, const float* hidden, int n, const float* noise, float* latent,
-                         float* eos, cudaStream_t s);
+                         float* eos, cudaStream_t s, int row_off);
 
 namespace {
 
@@ -702,9 +702,10 @@ int step_lanes(int n) {
 
 // One decode step of the stack for `streams` (transformer.rs:822-838 with DeviceStep), recorded
 // once per stream set as a CUDA graph in `slot` and replayed: `inputs` fills the graph's input
-// buffers (before the replay), `pre` and `post` launch extra kernels before and after the layers
-// inside the recorded body. With tracing on, the body runs un-recorded on one stream (the lanes
-// one after the other), timed per attention.
+// buffers (before the replay), `pre` launches extra kernels before the layers and `post(stream,
+// row_off, rows)` after each lane's layers, on that lane's stream, inside the recorded body.
+// With tracing on, the body runs un-recorded on one stream (the lanes one after the other),
+// timed per attention.
 //
 // Two lanes: rows [0, n0) run on the capture stream, rows [n0, n) on a second stream forked
 // from it. The second lane starts once the first has launched its first in_proj, so the first
@@ -795,6 +796,7 @@ void run_step(ptts_b200_model* model, ptts_b200_kv* kv, const int32_t* streams_h
             run_layers(model, kv, true, plan, ln.n, g->x.as<__nv_bfloat16>() + (size_t)ln.off * c.d_model,
                        g->resid.as<float>() + (size_t)ln.off * c.d_model, ln.ws, ls,
                        ev ? ev + 2 * c.num_layers * i : nullptr, Tiles{}, lo);
+            if constexpr (!std::is_same_v<std::decay_t<Post>, std::nullptr_t>) post(ls, ln.off, ln.n);
         }
         if (n_lanes > 1 && cs2 != cs) {
             CK(cudaEventRecord(model->lane_join, cs2));
@@ -802,7 +804,6 @@ void run_step(ptts_b200_model* model, ptts_b200_kv* kv, const int32_t* streams_h
         }
         launch_advance(kv->len.as<int32_t>(), sid, nullptr, n, 1, kv->ring(), kv->capacity, cs);
         check_launch();
-        if constexpr (!std::is_same_v<std::decay_t<Post>, std::nullptr_t>) post(cs);
     };
     if (tracing_on()) {
         const int L = c.num_layers, E = 2 * L * n_lanes;
@@ -1398,9 +1399,11 @@ int ptts_b200_frame(ptts_b200_model* model, ptts_b200_flow* flow, ptts_b200_kv* 
                  [&](cudaStream_t cs) {  // input_linear, inside the recorded body
                      ptts_b200_flow_input(flow, bos ? nullptr : g->lat_in.as<float>(), g->x.as<__nv_bfloat16>(), n, cs);
                  },
-                 [&](cudaStream_t cs) {  // out_norm, EOS and the flow net
-                     ptts_b200_flow_head(flow, g->resid.as<float>(), n, g->noise.as<float>(), g->lat_out.as<float>(),
-                                         g->eos.as<float>(), cs);
+                 [&](cudaStream_t cs, int off, int rows) {  // out_norm, EOS and the flow net, per lane
+                     const int ld = ptts_b200_flow_ldim(flow);
+                     ptts_b200_flow_head(flow, g->resid.as<float>() + (size_t)off * model->cfg.d_model, rows,
+                                         g->noise.as<float>() + (size_t)off * ld,
+                                         g->lat_out.as<float>() + (size_t)off * ld, g->eos.as<float>() + off, cs, off);
                  });
         auto back = [](const void* p) {
             return is_device_pointer(p) ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost;

@@ -194,12 +194,29 @@ void gemm(const ptts_b200_flow* f, LinearEpi epi, int rows, const void* a_hi, co
 }
 
 // FlowLM::sample_from_noise from `src` rows [n][d_model] f32: out_norm first when `normalise`
-// (the backbone output), else `src` is already t_out.
+// (the backbone output), else `src` is already t_out. The rows use workspace rows row_off ..
+// row_off + n - 1, so calls on disjoint row ranges may run at the same time (the two lanes of a
+// frame); the workspace must already hold row_off + n rows.
 void sample(ptts_b200_flow* f, const float* src, bool normalise, int n, const float* noise, float* latent,
-            float* eos, cudaStream_t s) {
+            float* eos, cudaStream_t s, int row_off = 0) {
     const auto& c = f->cfg;
     const int C = c.flow_dim, L = c.ldim, W = f->ada_width();
-    f->size(n);
+    if (row_off == 0) f->size(n);
+    require(row_off + n <= f->rows, PTTS_B200_ERR_STATE, "flow workspace smaller than the rows asked for");
+    const size_t o = (size_t)row_off;
+    __nv_bfloat16* t_hi = f->t_hi.as<__nv_bfloat16>() + o * c.d_model;
+    __nv_bfloat16* t_lo = f->t_lo.as<__nv_bfloat16>() + o * c.d_model;
+    __nv_bfloat16* y_hi = f->y_hi.as<__nv_bfloat16>() + o * C;
+    __nv_bfloat16* y_lo = f->y_lo.as<__nv_bfloat16>() + o * C;
+    float* ada = f->ada_out.as<float>() + o * W;
+    float* xf = f->xf.as<float>() + o * C;
+    __nv_bfloat16* h_hi = f->h_hi.as<__nv_bfloat16>() + o * C;
+    __nv_bfloat16* h_lo = f->h_lo.as<__nv_bfloat16>() + o * C;
+    __nv_bfloat16* h1_hi = f->h1_hi.as<__nv_bfloat16>() + o * C;
+    __nv_bfloat16* h1_lo = f->h1_lo.as<__nv_bfloat16>() + o * C;
+    float* hf = f->hf.as<float>() + o * C;
+    float* cur_a = f->cur_a.as<float>() + o * L;
+    float* cur_b = f->cur_b.as<float>() + o * L;
     FlowNormArgs na{};
     na.M = n;
     na.d = c.d_model;
@@ -210,8 +227,8 @@ void sample(ptts_b200_flow* f, const float* src, bool normalise, int n, const fl
     na.eos_w = f->eos_w.as<float>();
     na.eos_b = f->eos_b;
     na.eos = eos;
-    na.hi = f->t_hi.as<__nv_bfloat16>();
-    na.lo = f->t_lo.as<__nv_bfloat16>();
+    na.hi = t_hi;
+    na.lo = t_lo;
     launch_flow_norm_eos(na, s);
     CK(cudaGetLastError());
     const int steps = c.flow_type == PTTS_B200_FLOW_LSD ? c.lsd_steps : 1;
@@ -225,59 +242,56 @@ void sample(ptts_b200_flow* f, const float* src, bool normalise, int n, const fl
         ip.a = cur;
         ip.w = f->in_proj_w.as<float>();
         ip.bias = f->in_proj_b.as<float>();
-        ip.y = f->xf.as<float>();
+        ip.y = xf;
         launch_flow_small(ip, s);
         CK(cudaGetLastError());
         // y_act = silu(cond_embed(t_out) + t_emb): one linear, both biases in its epilogue
         if (f->time_conds > 0)
-            gemm(f, EPI_COND, n, f->t_hi.p, f->t_lo.p, f->cond, nullptr, f->y_hi.p, f->y_lo.p,
-                 f->temb.as<float>() + (size_t)i * C, 0, s);
+            gemm(f, EPI_COND, n, t_hi, t_lo, f->cond, nullptr, y_hi, y_lo, f->temb.as<float>() + (size_t)i * C, 0, s);
         else
-            gemm(f, EPI_BIAS_SILU, n, f->t_hi.p, f->t_lo.p, f->cond, nullptr, f->y_hi.p, f->y_lo.p, nullptr, 0, s);
+            gemm(f, EPI_BIAS_SILU, n, t_hi, t_lo, f->cond, nullptr, y_hi, y_lo, nullptr, 0, s);
         // every block's adaLN modulation (and the final layer's) in one linear
-        float* ada = f->ada_out.as<float>();
-        gemm(f, EPI_BIAS, n, f->y_hi.p, f->y_lo.p, f->ada, ada, nullptr, nullptr, nullptr, 0, s);
+        gemm(f, EPI_BIAS, n, y_hi, y_lo, f->ada, ada, nullptr, nullptr, nullptr, 0, s);
         for (int b = 0; b < c.flow_depth; ++b) {
             FlowModArgs m{};
             m.M = n;
             m.C = C;
-            m.x = f->xf.as<float>();
+            m.x = xf;
             m.gamma = f->ln_w[b]->as<float>();
             m.beta = f->ln_b[b]->as<float>();
             m.eps = 1e-6f;
             m.shift = ada + (size_t)b * 3 * C;
             m.scale = ada + (size_t)b * 3 * C + C;
             m.stride = W;
-            m.hi = f->h_hi.as<__nv_bfloat16>();
-            m.lo = f->h_lo.as<__nv_bfloat16>();
+            m.hi = h_hi;
+            m.lo = h_lo;
             launch_flow_ln_mod(m, s);
             CK(cudaGetLastError());
-            gemm(f, EPI_BIAS_SILU, n, f->h_hi.p, f->h_lo.p, *f->lin1[b], nullptr, f->h1_hi.p, f->h1_lo.p,
-                 nullptr, 0, s);
-            gemm(f, EPI_GATE_RESID, n, f->h1_hi.p, f->h1_lo.p, *f->lin2[b], f->xf.as<float>(), nullptr,
-                 nullptr, ada + (size_t)b * 3 * C + 2 * C, W, s);
+            gemm(f, EPI_BIAS_SILU, n, h_hi, h_lo, *f->lin1[b], nullptr, h1_hi, h1_lo, nullptr, 0, s);
+            gemm(f, EPI_GATE_RESID, n, h1_hi, h1_lo, *f->lin2[b], xf, nullptr, nullptr,
+                 ada + (size_t)b * 3 * C + 2 * C, W, s);
         }
         FlowModArgs m{};
         m.M = n;
         m.C = C;
-        m.x = f->xf.as<float>();
+        m.x = xf;
         m.eps = 1e-6f;
         m.shift = ada + (size_t)c.flow_depth * 3 * C;
         m.scale = ada + (size_t)c.flow_depth * 3 * C + C;
         m.stride = W;
-        m.y = f->hf.as<float>();
+        m.y = hf;
         launch_flow_ln_mod(m, s);
         CK(cudaGetLastError());
         FlowOutArgs o{};
         o.M = n;
         o.C = C;
         o.L = L;
-        o.h = f->hf.as<float>();
+        o.h = hf;
         o.w = f->final_w.as<float>();
         o.bias = f->final_b.as<float>();
         o.cur = c.flow_type == PTTS_B200_FLOW_DRIFTING ? nullptr : cur;
         o.step_scale = c.flow_type == PTTS_B200_FLOW_LSD ? 1.0f / (float)steps : 1.0f;
-        float* next = i + 1 == steps ? latent : (i % 2 == 0 ? f->cur_a.as<float>() : f->cur_b.as<float>());
+        float* next = i + 1 == steps ? latent : (i % 2 == 0 ? cur_a : cur_b);
         o.out = next;
         launch_flow_out(o, s);
         CK(cudaGetLastError());
@@ -316,10 +330,11 @@ void ptts_b200_flow_input(ptts_b200_flow* f, const float* latent, __nv_bfloat16*
     CK(cudaGetLastError());
 }
 
-// out_norm of the backbone's output rows, then sample_from_noise.
+// out_norm of the backbone's output rows, then sample_from_noise, for rows row_off ..
+// row_off + n - 1 of the frame (the pointers are those rows' own; the workspace rows match).
 void ptts_b200_flow_head(ptts_b200_flow* f, const float* hidden, int n, const float* noise, float* latent,
-                         float* eos, cudaStream_t s) {
-    sample(f, hidden, true, n, noise, latent, eos, s);
+                         float* eos, cudaStream_t s, int row_off) {
+    sample(f, hidden, true, n, noise, latent, eos, s, row_off);
 }
 
 // Whether `name` is one of this flow head's tensors (for the GGUF loader, gguf.cu).
