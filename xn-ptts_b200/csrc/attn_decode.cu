@@ -67,6 +67,7 @@ struct ChunkHdr {
     int c0, c1;      // the CTAs holding pieces of a cut stream
 };
 constexpr int kFirst = 1, kLast = 2, kWhole = 4, kEnd = 8;
+constexpr int kQLoaded = 16;  // the consumers loaded this piece's q themselves (none in the stage)
 
 template <typename T>
 struct Row;
@@ -237,7 +238,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(DecodeArgs a) 
             set_error(a.err, DEV_ERR_TIMEOUT);
             return false;
         };
-        // Before the wait: the stages (at most kStages) whose q copy is still to be issued.
+        // Before the wait: the stages (at most kStages) whose q copy is still to be issued. The
+        // consumers load the q of the CTA's first piece themselves as soon as they are past the
+        // wait (plain loads, not queued behind the K/V copies), so that piece has none staged.
+        const bool q_first_loaded = a.prestart && a.cta_first != nullptr;
         bool waited = !a.prestart;
         int q_stage[kStages], q_row[kStages], n_deferred = 0;
         auto wait_predecessor = [&]() {
@@ -278,10 +282,12 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(DecodeArgs a) 
                 ChunkHdr hd = proto;
                 hd.p = p;
                 hd.n = n;
-                hd.flags = (p == s0 ? kFirst : 0) | (p + n >= s1 ? kLast : 0) | (whole ? kWhole : 0);
+                const bool q_loaded = it == 0 && q_first_loaded;  // the CTA's first chunk: stream b0
+                hd.flags = (p == s0 ? kFirst : 0) | (p + n >= s1 ? kLast : 0) | (whole ? kWhole : 0) |
+                           (q_loaded ? kQLoaded : 0);
                 *reinterpret_cast<ChunkHdr*>(sb + kDataBytes + kQStageBytes) = hd;
-                mbar_arrive_expect_tx(&full[st], 2u * n * RB + (p == s0 ? (uint32_t)kQStageBytes : 0u));
-                if (p == s0) {
+                mbar_arrive_expect_tx(&full[st], 2u * n * RB + (p == s0 && !q_loaded ? (uint32_t)kQStageBytes : 0u));
+                if (p == s0 && !q_loaded) {
                     if (waited) {
                         bulk_g2s(sb + kDataBytes, a.q + (long long)b * kRowWidth, kQStageBytes, &full[st], pol);
                     } else {
@@ -322,6 +328,12 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(DecodeArgs a) 
     const int g = lane >> 3;  // which of the 4 rows of a warp step
     const int j = lane & 7;   // which 16-byte slice of the head row
     float q[8], m = -1e30f, l = 0.f, acc[8];
+    // The q of the CTA's first piece (stream cta_first[c]), loaded now rather than staged.
+    float q_first[8];
+    if (a.prestart && a.cta_first) {
+        const int b0 = min(max(a.cta_first[c], 0), max(a.B - 1, 0));
+        load_q<T>(a.q + (long long)b0 * kRowWidth + h * kHeadDim, j, q_first);
+    }
     for (int it = 0;; ++it) {
         const int st = it % kStages;
         if (!mbar_wait(&full[st], (it / kStages) & 1)) {
@@ -332,7 +344,12 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(DecodeArgs a) 
         const ChunkHdr hd = *reinterpret_cast<const ChunkHdr*>(sb + kDataBytes + kQStageBytes);
         if (hd.flags & kEnd) break;
         if (hd.flags & kFirst) {
-            load_q<T>(reinterpret_cast<const float*>(sb + kDataBytes) + h * kHeadDim, j, q);
+            if (hd.flags & kQLoaded) {
+#pragma unroll
+                for (int i = 0; i < 8; ++i) q[i] = q_first[i];
+            } else {
+                load_q<T>(reinterpret_cast<const float*>(sb + kDataBytes) + h * kHeadDim, j, q);
+            }
 #pragma unroll
             for (int i = 0; i < 8; ++i) q[i] *= a.qscale;
             m = -1e30f;
