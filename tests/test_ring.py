@@ -102,52 +102,57 @@ def test_evicting_leaves_the_cache_of_a_sequence_without_them(ptts, oracle, cuda
     assert worst_sem < 1e-2
 
 
-def test_ring_and_appended_streams_share_a_batch(ptts, oracle, cuda):
-    """A decode batch mixing a ring stream (with a hole from an eviction) and appended streams:
-    every row against the oracle (the ring stream on its kept rows)."""
+@pytest.mark.parametrize("S,rings", [(3, [1]), (160, [1, 130])], ids=["one-lane", "two-lanes"])
+def test_ring_and_appended_streams_share_a_batch(ptts, oracle, cuda, S, rings):
+    """A decode batch mixing ring streams (each with a hole from an eviction) and appended
+    streams: every row against the oracle (a ring stream on its kept rows). 160 streams run the
+    step as two lanes, with a ring stream in each."""
     import torch
     cfg = ptts.FlowLMConfig(num_layers=2)
     w = ptts.random_weights(cfg, 21)
     model = ptts.Transformer(cfg)
     model.load(w)
     om = oracle.Model(cfg, w)
-    S, P, cap = 3, 8, 16
+    P, cap = 8, 16
+    streams = list(range(S))
     g = torch.Generator().manual_seed(22)
     kv = ptts.KvState(cfg.num_layers, S, cap, dtype="bf16")
     prompt = torch.randn(S * P, 512, generator=g).bfloat16()
-    model.forward(kv, prompt.to(cuda), [0, 1, 2], [P] * S)
+    model.forward(kv, prompt.to(cuda), streams, [P] * S)
     shape = (cfg.num_layers, S, cap, 8, 64)
     kc, vc = np.zeros(shape, np.float32), np.zeros(shape, np.float32)
     lengths = np.zeros(S, np.int32)
-    om.forward(prompt.float().numpy(), kc, vc, lengths, [0, 1, 2], np.arange(0, S * P + 1, P, dtype=np.int32),
+    om.forward(prompt.float().numpy(), kc, vc, lengths, streams, np.arange(0, S * P + 1, P, dtype=np.int32),
                store=oracle.ROUND_KV)
     lengths += P
-    kv.start_ring([1])
-    # Evict slots 5 and 6 of stream 1 (past a prefix of 4): rows 5, 6 go, 7 rotates back by 2.
-    kv.evict(1, 4, [5, 6])
+    kv.start_ring(rings)
+    # Evict slots 5 and 6 of each ring stream (past a prefix of 4): rows 5, 6 go, 7 rotates back by 2.
     keep = [0, 1, 2, 3, 4, 7]
-    for l in range(cfg.num_layers):
-        k_kept, v_kept = kc[l, 1, keep].copy(), vc[l, 1, keep].copy()
-        k_kept[4:] = _rotate_back(oracle, k_kept[4:], 2)
-        kc[l, 1] = 0
-        vc[l, 1] = 0
-        kc[l, 1, :6] = k_kept
-        vc[l, 1, :6] = v_kept
-    lengths[1] -= 2
-    kv.set_ring_slot(1, 5)
+    for r in rings:
+        kv.evict(r, 4, [5, 6])
+        for l in range(cfg.num_layers):
+            k_kept, v_kept = kc[l, r, keep].copy(), vc[l, r, keep].copy()
+            k_kept[4:] = _rotate_back(oracle, k_kept[4:], 2)
+            kc[l, r] = 0
+            vc[l, r] = 0
+            kc[l, r, :6] = k_kept
+            vc[l, r, :6] = v_kept
+        lengths[r] -= 2
+        kv.set_ring_slot(r, 5)
     worst = 0.0
     for frame in range(3):
         if frame:
-            kv.set_ring_slot(1, 8 + frame)  # fresh slots past the filled ones
+            for r in rings:
+                kv.set_ring_slot(r, 8 + frame)  # fresh slots past the filled ones
         x = torch.randn(S, 512, generator=g).bfloat16()
-        got = model.step(kv, [0, 1, 2], x.to(cuda)).float().cpu().numpy()
-        want = om.forward(x.float().numpy(), kc, vc, lengths, [0, 1, 2], np.arange(S + 1, dtype=np.int32),
+        got = model.step(kv, streams, x.to(cuda)).float().cpu().numpy()
+        want = om.forward(x.float().numpy(), kc, vc, lengths, streams, np.arange(S + 1, dtype=np.int32),
                           store=oracle.ROUND_KV)
         lengths += 1
         worst = max(worst, normwise(got, want))
     kv.check()
     np.testing.assert_array_equal(kv.lengths(), lengths)
-    print("mixed batch", worst)
+    print("mixed batch", S, worst)
     assert worst < TOL
 
 
