@@ -205,7 +205,7 @@ def test_kernel_variants_match_the_oracle(ptts, oracle, cuda, monkeypatch, env):
 
 
 def test_long_prompts_match_the_oracle(ptts, oracle, cuda):
-    """Prompts of 4096+ rows in one call (the linears' 128-row tcgen05 tiles, the tcgen05
+    """Prompts of 4096+ rows in one call (the linears' 64-row tcgen05 tiles, the tcgen05
     prefill attention over 1000+ keys), then a decode step."""
     import torch
     cfg = ptts.FlowLMConfig(num_layers=2)

@@ -9,7 +9,7 @@
 // features and its N side is RT activation rows, D^T[f][r] = sum_k W[f][k] X[r][k]. Per 16 k
 // that is one tcgen05.mma.cta_group::1.kind::f16 per activation plane (hi, lo) with A = the
 // weight tile and B = the activation tile, both K-major. A decode batch of 512 rows gives
-// (N / 128) x 16 CTAs of RT = 32 rows, two CTAs per SM by shared memory; prompts use RT = 128.
+// (N / 128) x 16 CTAs of RT = 32 rows; prompts of 4096+ rows use RT = 64, two CTAs per SM.
 //
 // CTA: 256 threads (8 warps).
 //   thread 0:   TMA producer over a kStages ring of {W 128x64, X hi RTx64, X lo RTx64} f16
@@ -46,9 +46,10 @@ constexpr int kRowsPerWarp = 32 / kEpiWarps;
 // WLO: the weights come as two planes too (hi, lo), and each k step runs a third MMA.
 template <int RT, bool WLO>
 struct TmaTile {
-    // Decode tiles (RT 32) of f16 weights take 3 stages (74 KB) so that a CTA fits beside the
-    // decode attention's compact ring (137 KB) on one SM; prompt tiles take 4.
-    static constexpr int kStages = (WLO || RT == 32) ? 3 : 4;
+    // 3 stages: a decode tile (RT 32, 74 KB) fits beside the decode attention's compact ring
+    // (137 KB) on one SM, and two prompt tiles (RT 64, 97 KB) share an SM, so that one's epilogue
+    // overlaps the other's loads and MMAs.
+    static constexpr int kStages = (WLO || RT <= 64) ? 3 : 4;
     static constexpr int kWBytes = FT * KS * 2;  // 16 KB per weight plane
     static constexpr int kXBytes = RT * KS * 2;  // per activation plane
     static constexpr int kStageBytes = (WLO ? 2 : 1) * kWBytes + 2 * kXBytes;
@@ -549,8 +550,8 @@ bool launch_tma(const LinearArgs& a, cudaStream_t s) {
 template <int EPI>
 bool launch_tma_rows(const LinearArgs& a, cudaStream_t s) {
     if (a.wh_lo)  // f16 hi/lo weight planes (f32 or q8_0 layers)
-        return a.M < 4096 ? launch_tma<EPI, 32, true>(a, s) : launch_tma<EPI, 128, true>(a, s);
-    return a.M < 4096 ? launch_tma<EPI, 32, false>(a, s) : launch_tma<EPI, 128, false>(a, s);
+        return a.M < 4096 ? launch_tma<EPI, 32, true>(a, s) : launch_tma<EPI, 64, true>(a, s);
+    return a.M < 4096 ? launch_tma<EPI, 32, false>(a, s) : launch_tma<EPI, 64, false>(a, s);
 }
 
 // The flow net's linears (bf16 planes, optional weight lo plane), decode-size rows only.
