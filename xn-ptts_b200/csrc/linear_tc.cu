@@ -198,8 +198,9 @@ constexpr int kStageStride = FT + 4;
 // feature c. Warp w takes rows w, w + 8, ..., lane l features n0 + 4l .. 4l + 3, i.e. the RoPE
 // pairs (4l, 4l+1) and (4l+2, 4l+3) (rope.rs:37-95), with the arithmetic of linear.cu's qkv_pair.
 // Row metadata and every RoPE entry are loaded before the first store.
-__device__ __forceinline__ void qkv_rows(const LinearArgs& p, const float* st, int n0, int mbase) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+__device__ __forceinline__ void qkv_rows(const LinearArgs& p, const float* st, int n0, int mbase,
+                                         int warp = threadIdx.x >> 5) {
+    const int lane = threadIdx.x & 31;
     const int hd = p.heads * kHeadDim, kvd = p.kv_heads * kHeadDim;
     const int f = n0 + 4 * lane, d = f % kHeadDim;
     const int region = f < hd ? 0 : (f < hd + kvd ? 1 : 2);
@@ -256,8 +257,9 @@ __device__ __forceinline__ void qkv_rows(const LinearArgs& p, const float* st, i
 // n0 + 4l .. 4l + 3), with linear.cu's epilogue_pair arithmetic. EPI_RESID reads all its old
 // values before its first store.
 template <int EPI>
-__device__ __forceinline__ void plain_rows(const LinearArgs& p, const float* st, int n0, int mbase, int z) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+__device__ __forceinline__ void plain_rows(const LinearArgs& p, const float* st, int n0, int mbase, int z,
+                                           int warp = threadIdx.x >> 5) {
+    const int lane = threadIdx.x & 31;
     const int f = n0 + 4 * lane;
     const float4 sc = p.scale ? __ldg(reinterpret_cast<const float4*>(p.scale + f)) : make_float4(1.f, 1.f, 1.f, 1.f);
     float4 bias = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -467,6 +469,218 @@ __global__ void __launch_bounds__(kThreadsTma) linear_tma_kernel(const __grid_co
     }
 }
 
+// ---- persistent prompt-size linears ----------------------------------------------------------
+//
+// One CTA per SM walks 128-feature x 128-row tiles (tile t = blockIdx.x + i * gridDim.x,
+// feature tile t % NT, row tile t / NT) with two TMEM accumulators, so the epilogue of one tile
+// runs while the next tile's loads and MMAs do:
+//   warp 0, lane 0: TMA producer over a PS-stage ring of {W 128x64 (+ lo), X hi 128x64, X lo}
+//   warp 1, lane 0: MMA issuer, tcgen05.commit frees each stage and fills an accumulator
+//   warps 2..17:    epilogue, two accumulators in turn: 4 x 32-row chunks through a staging
+//                   tile (warp w reads TMEM lane quarter w % 4, 8 columns), then the same
+//                   row epilogues as linear_tma_kernel (2 rows per warp and chunk)
+// Every wait is bounded; a timed-out wait sets DEV_ERR_TIMEOUT and a shared abort flag that
+// ends every role's loop.
+constexpr int PT = 128;   // rows per tile (MMA N)
+constexpr int PS = 3;     // ring stages
+constexpr int kPersistWarps = 2 + kEpiWarps;
+constexpr int kPersistThreads = 32 * kPersistWarps;
+
+template <bool WLO>
+struct PersistTile {
+    static constexpr int kWBytes = FT * KS * 2;
+    static constexpr int kXBytes = PT * KS * 2;
+    static constexpr int kStageBytes = (WLO ? 2 : 1) * kWBytes + 2 * kXBytes;
+    static constexpr int kXOffset = (WLO ? 2 : 1) * kWBytes;
+    static constexpr int kStageOffset = PS * kStageBytes;              // the epilogue's staging tile
+    static constexpr int kBarOffset = kStageOffset + 32 * kStageStride * 4;
+    static constexpr int kSmem = 1024 + kBarOffset + 256;
+    static_assert(kStageBytes % 1024 == 0, "stages stay 1024-byte aligned");
+    static_assert(kSmem <= 227 * 1024, "fits one CTA per SM");
+};
+
+__device__ __forceinline__ void epi_bar_sync() {  // the 16 epilogue warps only
+    asm volatile("bar.sync 1, %0;" ::"r"(32 * kEpiWarps) : "memory");
+}
+// The same barrier, returning whether `v` held in any epilogue thread (one answer for all).
+__device__ __forceinline__ bool epi_bar_any(bool v) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 p, %1, 0;\n\t"
+        "barrier.red.or.pred q, 1, %2, p;\n\t"
+        "selp.u32 %0, 1, 0, q;\n\t}"
+        : "=r"(r)
+        : "r"((uint32_t)v), "r"(32 * kEpiWarps)
+        : "memory");
+    return r != 0;
+}
+
+template <int EPI, bool WLO>
+__global__ void __launch_bounds__(kPersistThreads, 1) linear_persist_kernel(
+    const __grid_constant__ LinearArgs p, const __grid_constant__ CUtensorMap tm_w,
+    const __grid_constant__ CUtensorMap tm_wlo, const __grid_constant__ CUtensorMap tm_x,
+    const __grid_constant__ CUtensorMap tm_xlo) {
+    using T = PersistTile<WLO>;
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    const uint32_t raw = smem_u32(smem_raw);
+    const uint32_t base = (raw + 1023u) & ~1023u;
+    unsigned char* smem = smem_raw + (base - raw);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + T::kBarOffset);
+    uint64_t* empty = full + PS;
+    uint64_t* acc_full = empty + PS;
+    uint64_t* acc_empty = acc_full + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+    __shared__ int s_abort, s_issued, s_consumed;
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int NT = p.N / FT, MT = (p.M + PT - 1) / PT, tiles = NT * MT, KT = p.K / KS;
+    const bool has_lo = p.a_lo != nullptr;
+    const uint32_t stage_tx = (WLO ? 2u : 1u) * T::kWBytes + (has_lo ? 2u : 1u) * T::kXBytes;
+
+    if (tid == 0) {
+        s_abort = 0;
+        s_issued = 0;
+        s_consumed = 0;
+        for (int i = 0; i < PS; ++i) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&acc_full[i], 1);
+            mbar_init(&acc_empty[i], kEpiWarps);
+        }
+        fence_mbar_init();
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tm_w)) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tm_x)) : "memory");
+    }
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(2 * PT)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    if (tid == 0) stamp_mark(p.stamps, p.stamp, STAMP_ENTRY);
+    auto fail = [&]() {
+        set_error(p.err, DEV_ERR_TIMEOUT);
+        atomicExch(&s_abort, 1);
+    };
+    auto aborted = [&]() { return *reinterpret_cast<volatile int*>(&s_abort) != 0; };
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ---- TMA producer ------------------------------------------------------------------
+            const uint64_t pol_w = policy_evict_last();
+            grid_dep_wait();
+            stamp_mark(p.stamps, p.stamp, STAMP_START);
+            int kk = 0;
+            for (int t = blockIdx.x; t < tiles && !aborted(); t += gridDim.x) {
+                const int n0 = (t % NT) * FT, m0 = (t / NT) * PT;
+                for (int kt = 0; kt < KT; ++kt, ++kk) {
+                    const int st = kk % PS;
+                    if (kk >= PS && !mbar_wait(&empty[st], ((kk / PS) & 1) ^ 1)) {
+                        fail();
+                        break;
+                    }
+                    const uint32_t sa = base + st * T::kStageBytes;
+                    mbar_arrive_expect_tx(&full[st], stage_tx);
+                    tma_load_2d_hint(sa, &tm_w, kt * KS, n0, &full[st], pol_w);
+                    if (WLO) tma_load_2d_hint(sa + T::kWBytes, &tm_wlo, kt * KS, n0, &full[st], pol_w);
+                    tma_load_2d(sa + T::kXOffset, &tm_x, kt * KS, m0, &full[st]);
+                    if (has_lo) tma_load_2d(sa + T::kXOffset + T::kXBytes, &tm_xlo, kt * KS, m0, &full[st]);
+                    s_issued = kk + 1;
+                }
+            }
+            grid_dep_launch();
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // ---- MMA issuer --------------------------------------------------------------------
+            const uint32_t idesc = p.a_f16 ? idesc_f16<PT>() : idesc_bf16<PT>();
+            int kk = 0, i = 0;
+            for (int t = blockIdx.x; t < tiles && !aborted(); t += gridDim.x, ++i) {
+                const int acc = i & 1, use = i >> 1;
+                if (use > 0 && !mbar_wait(&acc_empty[acc], (use - 1) & 1)) {
+                    fail();
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d = tmem + (uint32_t)(acc * PT);
+                bool ok = true;
+                for (int kt = 0; kt < KT; ++kt, ++kk) {
+                    const int st = kk % PS;
+                    if (!mbar_wait(&full[st], (kk / PS) & 1)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t sa = base + st * T::kStageBytes;
+                    const uint64_t dw = sw128_desc(sa), dwl = sw128_desc(sa + T::kWBytes);
+                    const uint64_t dx = sw128_desc(sa + T::kXOffset), dxl = sw128_desc(sa + T::kXOffset + T::kXBytes);
+#pragma unroll
+                    for (int k2 = 0; k2 < KS / 16; ++k2) {
+                        tc_mma(d, dw + 2 * k2, dx + 2 * k2, idesc, (kt | k2) ? 1u : 0u);
+                        if (has_lo) tc_mma(d, dw + 2 * k2, dxl + 2 * k2, idesc, 1u);
+                        if (WLO) tc_mma(d, dwl + 2 * k2, dx + 2 * k2, idesc, 1u);
+                    }
+                    tc_commit(&empty[st]);
+                    s_consumed = kk + 1;
+                }
+                if (!ok) {
+                    fail();
+                    break;
+                }
+                tc_commit(&acc_full[acc]);
+            }
+        }
+    } else {
+        // ---- epilogue ------------------------------------------------------------------------
+        grid_dep_wait();  // the residual epilogues read what predecessors wrote
+        const int ew = warp - 2, quarter = warp & 3, part = ew >> 2;
+        float* stg = reinterpret_cast<float*>(smem + T::kStageOffset);
+        int i = 0;
+        for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++i) {
+            const int acc = i & 1, use = i >> 1;
+            const int n0 = (t % NT) * FT, m0 = (t / NT) * PT;
+            const bool got = !aborted() && mbar_wait(&acc_full[acc], use & 1);
+            if (!got) fail();
+            if (epi_bar_any(!got)) break;  // every epilogue warp leaves together
+            __syncwarp();
+            tc_fence_after();
+#pragma unroll 1
+            for (int c = 0; c < PT; c += 32) {
+                float v[8];
+                tmem_ld8(tmem + ((uint32_t)(32 * quarter) << 16) + (uint32_t)(acc * PT + c + 8 * part), v);
+                epi_bar_sync();  // the previous chunk's readers are done with the staging tile
+#pragma unroll
+                for (int j = 0; j < 8; ++j) stg[(8 * part + j) * kStageStride + 32 * quarter + lane] = v[j];
+                epi_bar_sync();
+                if (EPI == EPI_QKV) qkv_rows(p, stg, n0, m0 + c, ew);
+                else plain_rows<EPI>(p, stg, n0, m0 + c, 0, ew);
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty[acc]);
+        }
+        if (tid == 64) stamp_mark(p.stamps, p.stamp, STAMP_END);
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (tid == 0) {
+        // Copies issued but never consumed (only after a timeout): let them land before exit.
+        for (int kk = s_consumed; kk < s_issued; ++kk) mbar_wait(&full[kk % PS], (kk / PS) & 1);
+    }
+    if (warp == 0) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * PT) : "memory");
+    }
+}
+
 // ---- tensor maps ---------------------------------------------------------------------------
 
 using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -547,11 +761,37 @@ bool launch_tma(const LinearArgs& a, cudaStream_t s) {
     return true;
 }
 
+// Prompt sizes: the persistent kernel, one CTA per SM over all tiles.
+template <int EPI, bool WLO>
+bool launch_persist(const LinearArgs& a, cudaStream_t s) {
+    using T = PersistTile<WLO>;
+    const bool bf = !a.a_f16;
+    CUtensorMap mw, mwl, mx, mxl;
+    if (!f16_map(&mw, a.wh, a.N, a.K, FT, bf) || !f16_map(&mx, a.a, a.M, a.K, PT, bf)) return false;
+    mwl = mw;
+    if (WLO && !f16_map(&mwl, a.wh_lo, a.N, a.K, FT, bf)) return false;
+    mxl = mx;
+    if (a.a_lo && !f16_map(&mxl, a.a_lo, a.M, a.K, PT, bf)) return false;
+    static int configured = -1;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    static int sms = 0;
+    if (configured != dev) {
+        cudaFuncSetAttribute(linear_persist_kernel<EPI, WLO>, cudaFuncAttributeMaxDynamicSharedMemorySize, T::kSmem);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        configured = dev;
+    }
+    const int tiles = (a.N / FT) * ((a.M + PT - 1) / PT);
+    launch_k(linear_persist_kernel<EPI, WLO>, dim3(tiles < sms ? tiles : sms), dim3(kPersistThreads), T::kSmem, s, a,
+             mw, mwl, mx, mxl);
+    return true;
+}
+
 template <int EPI>
 bool launch_tma_rows(const LinearArgs& a, cudaStream_t s) {
-    if (a.wh_lo)  // f16 hi/lo weight planes (f32 or q8_0 layers)
-        return a.M < 4096 ? launch_tma<EPI, 32, true>(a, s) : launch_tma<EPI, 64, true>(a, s);
-    return a.M < 4096 ? launch_tma<EPI, 32, false>(a, s) : launch_tma<EPI, 64, false>(a, s);
+    if (a.M >= 4096 && a.splits == 1 && EPI != EPI_PARTIAL)
+        return a.wh_lo ? launch_persist<EPI, true>(a, s) : launch_persist<EPI, false>(a, s);
+    return a.wh_lo ? launch_tma<EPI, 32, true>(a, s) : launch_tma<EPI, 32, false>(a, s);
 }
 
 // The flow net's linears (bf16 planes, optional weight lo plane), decode-size rows only.
