@@ -474,7 +474,8 @@ __global__ void __launch_bounds__(kThreadsTma) linear_tma_kernel(const __grid_co
 // One CTA per SM walks 128-feature x 128-row tiles (tile t = blockIdx.x + i * gridDim.x,
 // feature tile t % NT, row tile t / NT) with two TMEM accumulators, so the epilogue of one tile
 // runs while the next tile's loads and MMAs do:
-//   warp 0, lane 0: TMA producer over a PS-stage ring of {W 128x64 (+ lo), X hi 128x64, X lo}
+//   warp 0, lane 0: TMA producer over a 4-stage (3 with a weight lo plane) ring of
+//                   {W 128x64 (+ lo), X hi 128x64, X lo}
 //   warp 1, lane 0: MMA issuer, tcgen05.commit frees each stage and fills an accumulator
 //   warps 2..17:    epilogue, two accumulators in turn: 4 x 32-row chunks through a staging
 //                   tile (warp w reads TMEM lane quarter w % 4, 8 columns), then the same
@@ -482,12 +483,12 @@ __global__ void __launch_bounds__(kThreadsTma) linear_tma_kernel(const __grid_co
 // Every wait is bounded; a timed-out wait sets DEV_ERR_TIMEOUT and a shared abort flag that
 // ends every role's loop.
 constexpr int PT = 128;   // rows per tile (MMA N)
-constexpr int PS = 3;     // ring stages
 constexpr int kPersistWarps = 2 + kEpiWarps;
 constexpr int kPersistThreads = 32 * kPersistWarps;
 
 template <bool WLO>
 struct PersistTile {
+    static constexpr int PS = WLO ? 3 : 4;  // ring stages: 192 KB either way
     static constexpr int kWBytes = FT * KS * 2;
     static constexpr int kXBytes = PT * KS * 2;
     static constexpr int kStageBytes = (WLO ? 2 : 1) * kWBytes + 2 * kXBytes;
@@ -522,6 +523,7 @@ __global__ void __launch_bounds__(kPersistThreads, 1) linear_persist_kernel(
     const __grid_constant__ CUtensorMap tm_wlo, const __grid_constant__ CUtensorMap tm_x,
     const __grid_constant__ CUtensorMap tm_xlo) {
     using T = PersistTile<WLO>;
+    constexpr int PS = T::PS;
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t base = (raw + 1023u) & ~1023u;
