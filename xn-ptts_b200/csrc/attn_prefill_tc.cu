@@ -29,9 +29,12 @@ constexpr int kThreadsP = kWarps * 32;
 constexpr int kQBytes = QT * 128;  // 64 bf16 per row
 constexpr int kKVBytes = KT * 128;
 constexpr int kPBytes = QT * 128;  // 64 keys per row
-// Shared layout (1024-aligned tiles): Q_hi, Q_lo, K, V, P_hi, P_lo, barriers, TMEM slot.
+// Shared layout (1024-aligned tiles): Q_hi, Q_lo, two K/V buffers (K, V each), P_hi, P_lo,
+// barriers, TMEM slot. Key tile kt uses buffer kt % 2, so the next tile's copies run while
+// this one's MMAs and softmax do.
 constexpr int kOffQh = 0, kOffQl = kQBytes, kOffK = 2 * kQBytes, kOffV = kOffK + kKVBytes;
-constexpr int kOffPh = kOffV + kKVBytes, kOffPl = kOffPh + kPBytes;
+constexpr int kKVBuf = 2 * kKVBytes;  // from one buffer's K to the next one's
+constexpr int kOffPh = kOffK + 2 * kKVBuf, kOffPl = kOffPh + kPBytes;
 constexpr int kOffBar = kOffPl + kPBytes;
 constexpr int kSmemP = 1024 + kOffBar + 128;
 constexpr uint32_t kTmemColsP = 128;
@@ -159,6 +162,24 @@ __global__ void __launch_bounds__(kThreadsP, 1) prefill_tc_kernel(PrefillArgs a,
         const bool active = r < nrows;
         const int pos = active ? a.row_pos[row0 + r] : -1;
         bool ok = true;
+        // K and V tiles of keys kt*64 .. kt*64+63 into buffer kt % 2: 64 rows x 8 chunks each,
+        // 2 rows per thread, one cp.async group per tile.
+        auto load_kv = [&](int kt) {
+            const uint32_t buf = (uint32_t)((kt & 1) * kKVBuf);
+#pragma unroll
+            for (int i = 0; i < (KT * 8) / 128; ++i) {
+                const int c = tid + 128 * i;
+                const int kr = c >> 3, ch = c & 7;
+                const int key = kt * KT + kr;
+                const bool valid = key <= pos_max;
+                const long long off = (long long)(valid ? key : 0) * kRowWidth + ch * 8;
+                const uint32_t dst = buf + (uint32_t)(kr * 128 + ((ch ^ (kr & 7)) << 4));
+                cp_async16(base + kOffK + dst, kc + off, valid);
+                cp_async16(base + kOffV + dst, vc + off, valid);
+            }
+            asm volatile("cp.async.commit_group;" ::: "memory");
+        };
+        if (n_kt > 0) load_kv(0);
         // Q (rotated, f32) -> bf16 hi/lo tiles.
         {
             float q[64];
@@ -176,19 +197,14 @@ __global__ void __launch_bounds__(kThreadsP, 1) prefill_tc_kernel(PrefillArgs a,
         float m = -1e30f, l = 0.f;
         for (int kt = 0; kt < n_kt && ok; ++kt) {
             const uint32_t par = kt & 1;
-            // K and V tiles of keys kt*64 .. kt*64+63: 64 rows x 8 chunks each; 2 rows per thread.
-#pragma unroll
-            for (int i = 0; i < (KT * 8) / 128; ++i) {
-                const int c = tid + 128 * i;
-                const int kr = c >> 3, ch = c & 7;
-                const int key = kt * KT + kr;
-                const bool valid = key <= pos_max;
-                const long long off = (long long)(valid ? key : 0) * kRowWidth + ch * 8;
-                const uint32_t dst = (uint32_t)(kr * 128 + ((ch ^ (kr & 7)) << 4));
-                cp_async16(base + kOffK + dst, kc + off, valid);
-                cp_async16(base + kOffV + dst, vc + off, valid);
+            // Tile kt + 1 goes to the other buffer, last read by tile kt - 1's MMAs, which are
+            // complete: this thread waited for its P.V product at the end of the last iteration.
+            if (kt + 1 < n_kt) {
+                load_kv(kt + 1);
+                asm volatile("cp.async.wait_group 1;" ::: "memory");  // tile kt has landed
+            } else {
+                asm volatile("cp.async.wait_group 0;" ::: "memory");
             }
-            asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
             fence_proxy_async();
             tc_before();
             __syncwarp();
@@ -259,7 +275,8 @@ __global__ void __launch_bounds__(kThreadsP, 1) prefill_tc_kernel(PrefillArgs a,
     } else if (lane == 0) {
         // MMA issuer.
         const uint64_t dqh = desc_kmajor(base + kOffQh), dql = desc_kmajor(base + kOffQl);
-        const uint64_t dk = desc_kmajor(base + kOffK), dv = desc_mnmajor(base + kOffV);
+        const uint64_t dk0 = desc_kmajor(base + kOffK), dv0 = desc_mnmajor(base + kOffV);
+        const uint64_t dk1 = desc_kmajor(base + kOffK + kKVBuf), dv1 = desc_mnmajor(base + kOffV + kKVBuf);
         const uint64_t dph = desc_kmajor(base + kOffPh), dpl = desc_kmajor(base + kOffPl);
         for (int kt = 0; kt < n_kt; ++kt) {
             const uint32_t par = kt & 1;
@@ -268,6 +285,7 @@ __global__ void __launch_bounds__(kThreadsP, 1) prefill_tc_kernel(PrefillArgs a,
                 break;
             }
             tc_after();
+            const uint64_t dk = (kt & 1) ? dk1 : dk0, dv = (kt & 1) ? dv1 : dv0;
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk) {  // head dim 64 = 4 x 16: 32 bytes per step
                 tc_mma(tmem, dqh + 2 * kk, dk + 2 * kk, kIdescS, kk ? 1u : 0u);
