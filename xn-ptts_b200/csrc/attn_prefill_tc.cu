@@ -195,20 +195,23 @@ __global__ void __launch_bounds__(kThreadsP, 1) prefill_tc_kernel(PrefillArgs a,
 #pragma unroll
         for (int i = 0; i < 64; ++i) o[i] = 0.f;
         float m = -1e30f, l = 0.f;
+        // Key tile kt: [S(kt) ready] softmax -> P(kt) -> [tile kt + 1's K/V landed: the MMA
+        // thread computes S(kt + 1) right after P(kt).V] -> [P(kt).V ready] fold. The copies of
+        // tile kt + 1 run during tile kt's softmax.
+        float corr = 1.f;
         for (int kt = 0; kt < n_kt && ok; ++kt) {
             const uint32_t par = kt & 1;
+            auto kv_ready = [&]() {  // this thread's copies so far have landed: tell the MMA thread
+                asm volatile("cp.async.wait_group 0;" ::: "memory");
+                fence_proxy_async();
+                tc_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&bar[0]);
+            };
+            if (kt == 0) kv_ready();  // tile 0 (and the Q tiles)
             // Tile kt + 1 goes to the other buffer, last read by tile kt - 1's MMAs, which are
             // complete: this thread waited for its P.V product at the end of the last iteration.
-            if (kt + 1 < n_kt) {
-                load_kv(kt + 1);
-                asm volatile("cp.async.wait_group 1;" ::: "memory");  // tile kt has landed
-            } else {
-                asm volatile("cp.async.wait_group 0;" ::: "memory");
-            }
-            fence_proxy_async();
-            tc_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&bar[0]);
+            if (kt + 1 < n_kt) load_kv(kt + 1);
             // S from TMEM: this thread's row, 64 keys.
             if (!mbar_wait(&bar[1], par)) {
                 set_error(a.err, DEV_ERR_TIMEOUT);
@@ -225,7 +228,7 @@ __global__ void __launch_bounds__(kThreadsP, 1) prefill_tc_kernel(PrefillArgs a,
                 s[j] = key <= pos ? s[j] * a.qscale : -INFINITY;
                 mt = fmaxf(mt, s[j]);
             }
-            const float corr = fast_exp2(m - mt);
+            corr = fast_exp2(m - mt);
             float rs = 0.f;
 #pragma unroll
             for (int j = 0; j < 64; ++j) {
@@ -237,6 +240,7 @@ __global__ void __launch_bounds__(kThreadsP, 1) prefill_tc_kernel(PrefillArgs a,
             tc_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&bar[2]);
+            if (kt + 1 < n_kt) kv_ready();
             // O tile from TMEM, folded into the running accumulator.
             if (ok && !mbar_wait(&bar[3], par)) {
                 set_error(a.err, DEV_ERR_TIMEOUT);
@@ -278,32 +282,38 @@ __global__ void __launch_bounds__(kThreadsP, 1) prefill_tc_kernel(PrefillArgs a,
         const uint64_t dk0 = desc_kmajor(base + kOffK), dv0 = desc_mnmajor(base + kOffV);
         const uint64_t dk1 = desc_kmajor(base + kOffK + kKVBuf), dv1 = desc_mnmajor(base + kOffV + kKVBuf);
         const uint64_t dph = desc_kmajor(base + kOffPh), dpl = desc_kmajor(base + kOffPl);
-        for (int kt = 0; kt < n_kt; ++kt) {
-            const uint32_t par = kt & 1;
-            if (!mbar_wait(&bar[0], par)) {
-                set_error(a.err, DEV_ERR_TIMEOUT);
-                break;
-            }
+        // S(kt) = Q K(kt)^T once tile kt's K/V have landed; P(kt).V once P(kt) is written, then
+        // at once S(kt + 1), so that it runs while the warps fold P(kt).V.
+        auto issue_s = [&](int kt) -> bool {
+            if (!mbar_wait(&bar[0], kt & 1)) return false;
             tc_after();
-            const uint64_t dk = (kt & 1) ? dk1 : dk0, dv = (kt & 1) ? dv1 : dv0;
+            const uint64_t dk = (kt & 1) ? dk1 : dk0;
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk) {  // head dim 64 = 4 x 16: 32 bytes per step
                 tc_mma(tmem, dqh + 2 * kk, dk + 2 * kk, kIdescS, kk ? 1u : 0u);
                 tc_mma(tmem, dql + 2 * kk, dk + 2 * kk, kIdescS, 1u);
             }
             tc_commit(&bar[1]);
+            return true;
+        };
+        bool ok = n_kt == 0 || issue_s(0);
+        for (int kt = 0; kt < n_kt && ok; ++kt) {
+            const uint32_t par = kt & 1;
             if (!mbar_wait(&bar[2], par)) {
-                set_error(a.err, DEV_ERR_TIMEOUT);
+                ok = false;
                 break;
             }
             tc_after();
+            const uint64_t dv = (kt & 1) ? dv1 : dv0;
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk) {  // 64 keys = 4 x 16: P 32 bytes, V 2 x 1024 bytes
                 tc_mma(tmem + 64u, dph + 2 * kk, dv + 128 * kk, kIdescPV, kk ? 1u : 0u);
                 tc_mma(tmem + 64u, dpl + 2 * kk, dv + 128 * kk, kIdescPV, 1u);
             }
             tc_commit(&bar[3]);
+            if (kt + 1 < n_kt) ok = issue_s(kt + 1);
         }
+        if (!ok) set_error(a.err, DEV_ERR_TIMEOUT);
     }
     tc_before();
     __syncthreads();
