@@ -150,15 +150,18 @@ __global__ void __launch_bounds__(128) flow_ln_mod_kernel(FlowModArgs p) {
     }
 }
 
-// Eight rows per block (one per warp); the weights sit transposed in shared memory, [C][L], so
-// lane j reads output j's column without bank conflicts. L <= 64 (lanes j and j + 32).
+// Eight rows per block (one per warp); the weights sit transposed in shared memory, [C][L + 1]
+// (the extra column keeps both the transposing stores and the reads free of bank conflicts),
+// so lane j reads output j's column. L <= 64 (lanes j and j + 32).
 __global__ void __launch_bounds__(256) flow_out_kernel(FlowOutArgs p) {
-    extern __shared__ float wt[];  // [C][L]
+    extern __shared__ float wt[];  // [C][L + 1]
+    const int ld = p.L + 1;
     grid_dep_wait();
     grid_dep_launch();
-    for (int i = threadIdx.x; i < p.C * p.L; i += blockDim.x) {
-        const int j = i / p.C, k = i - j * p.C;  // coalesced read of w[j][k]
-        wt[k * p.L + j] = p.w[i];
+    {
+        const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+        for (int j = warp; j < p.L; j += blockDim.x >> 5)   // w[j][k]: coalesced along k
+            for (int k = lane; k < p.C; k += 32) wt[k * ld + j] = __ldg(p.w + (long long)j * p.C + k);
     }
     __syncthreads();
     const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
@@ -171,7 +174,7 @@ __global__ void __launch_bounds__(256) flow_out_kernel(FlowOutArgs p) {
 #pragma unroll 8
         for (int i = 0; i < 32; ++i) {
             const float hk = __shfl_sync(0xffffffffu, hv, i);
-            const float* wr = wt + (k0 + i) * p.L;
+            const float* wr = wt + (k0 + i) * ld;
             a0 = fmaf(hk, wr[j0], a0);
             if (p.L > 32) a1 = fmaf(hk, wr[j1], a1);
         }
@@ -216,7 +219,7 @@ void launch_flow_ln_mod(const FlowModArgs& a, cudaStream_t s) {
 }
 
 void launch_flow_out(const FlowOutArgs& a, cudaStream_t s) {
-    const size_t smem = sizeof(float) * a.C * a.L;
+    const size_t smem = sizeof(float) * a.C * (a.L + 1);
     static int configured = -1;
     int dev = 0;
     cudaGetDevice(&dev);

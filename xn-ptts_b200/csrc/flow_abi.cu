@@ -353,6 +353,8 @@ int ptts_b200_flow_create(int device, const ptts_b200_flow_config* config, ptts_
         require(wide(c.flow_dim), PTTS_B200_ERR_UNSUPPORTED, "flow_dim must be 128, 256, 512 or 1024");
         require(c.flow_depth >= 1, PTTS_B200_ERR_ARG, "flow_depth must be >= 1");
         require(c.ldim >= 1 && c.ldim <= 64, PTTS_B200_ERR_UNSUPPORTED, "ldim must be in 1..64");
+        require((size_t)c.flow_dim * (c.ldim + 1) * 4 <= 200 * 1024, PTTS_B200_ERR_UNSUPPORTED,
+                "flow_dim x (ldim + 1) floats must fit the final layer's 200 KB of shared memory");
         require((size_t)c.flow_dim * c.ldim * 4 <= 200 * 1024, PTTS_B200_ERR_UNSUPPORTED,
                 "flow_dim * ldim too large for the final layer's kernel");
         require(c.flow_type >= 0 && c.flow_type <= 2, PTTS_B200_ERR_ARG, "unknown flow_type");
