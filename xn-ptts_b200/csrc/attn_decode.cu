@@ -23,10 +23,11 @@
 //
 // Data movement. Keys and values of consecutive positions of a stream are contiguous
 // (the cache is [stream][slot][head][dim]), so a chunk of positions is one 1-D bulk copy for K
-// and one for V, issued by a producer warp into a 3-stage shared-memory ring guarded by
-// mbarriers. Eight consumer warps, one per head, read their head's 128-byte slice of every row
-// with 16-byte shared loads (8 lanes per row, 4 rows per warp instruction) and keep an online
-// softmax in the exp2 domain. Every wait is bounded and reports DEV_ERR_TIMEOUT.
+// and one for V, issued by a producer warp into a shared-memory ring guarded by mbarriers (the
+// wide or the compact ring, below). Eight consumer warps, one per head, read their head's
+// 128-byte slice of every row with 16-byte shared loads (8 lanes per row, 4 rows per warp
+// instruction) and keep an online softmax in the exp2 domain. Every wait is bounded and reports
+// DEV_ERR_TIMEOUT.
 #include "common.cuh"
 #include "kernels.h"
 

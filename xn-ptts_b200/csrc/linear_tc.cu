@@ -8,18 +8,20 @@
 // Roles are swapped against the row-major view: the MMA's M side (128 TMEM lanes) is 128 output
 // features and its N side is RT activation rows, D^T[f][r] = sum_k W[f][k] X[r][k]. Per 16 k
 // that is one tcgen05.mma.cta_group::1.kind::f16 per activation plane (hi, lo) with A = the
-// weight tile and B = the activation tile, both K-major. A decode batch of 512 rows gives
-// (N / 128) x 16 CTAs of RT = 32 rows; prompts of 4096+ rows use RT = 64, two CTAs per SM.
+// weight tile and B = the activation tile, both K-major. Up to 4095 rows, linear_tma_kernel
+// takes one 128-feature x 32-row tile per CTA (a 512-row decode batch gives (N / 128) x 16
+// CTAs); prompts of 4096+ rows go to linear_persist_kernel (below), one CTA per SM over all
+// 128 x 128 tiles.
 //
-// CTA: 256 threads (8 warps).
+// linear_tma_kernel CTA: 512 threads (16 warps).
 //   thread 0:   TMA producer over a kStages ring of {W 128x64, X hi RTx64, X lo RTx64} f16
 //               tiles. The weight tiles of the first stages are requested before the wait on
 //               the grid that wrote X (weights never change).
 //   thread 32:  MMA issuer; tcgen05.commit frees each stage and finally signals `done`.
 //   all warps:  epilogue: warp w reads TMEM lanes 32 (w % 4) .. + 31 (features n0 + 32 (w % 4)
-//               + lane), 16 rows per tcgen05.ld, into a shared-memory tile; then each warp takes
-//               4 whole rows, lane l the features 4l..4l+3, so stores are 16 bytes and RoPE
-//               pairs in-lane. Eight warps instead of four halve each warp's serial share of
+//               + lane), 8 rows per tcgen05.ld, into a shared-memory tile; then each warp takes
+//               2 whole rows, lane l the features 4l..4l+3, so stores are 16 bytes and RoPE
+//               pairs in-lane. Sixteen warps instead of four cut each warp's serial share of
 //               the epilogue (GELU, RoPE), which bounds the decode-size launches.
 // Every wait is bounded (DEV_ERR_TIMEOUT); after a timeout the CTA still waits, bounded, for the
 // copies it issued and frees its TMEM. No clusters, no multicast.
@@ -37,8 +39,8 @@ namespace {
 
 constexpr int FT = 128;  // output features per CTA (MMA M)
 constexpr int KS = 64;   // k per stage: one 128-byte swizzle row of f16
-// 8 warps: the MMA-side roles take threads 0 and 32; all eight run the epilogue, two per TMEM
-// lane quarter (warp w reads lanes 32 (w % 4) ..), each then storing 4 of the 32 staged rows.
+// 16 warps: the MMA-side roles take threads 0 and 32; all sixteen run the epilogue, four per
+// TMEM lane quarter (warp w reads lanes 32 (w % 4) ..), each then storing 2 of the 32 staged rows.
 constexpr int kEpiWarps = 16;
 constexpr int kThreadsTma = 32 * kEpiWarps;
 constexpr int kRowsPerWarp = 32 / kEpiWarps;
