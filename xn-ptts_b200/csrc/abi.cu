@@ -117,6 +117,11 @@ struct ptts_b200_kv {
     // scratch of the attention op
     DevBuf seq_stream, row_offsets, row_stream, row_pos, prefix, part, q_rot, counters, tiles;
     Staging staging;
+    // What seq_stream holds after the last upload_seq, and on which CUDA stream it was copied: a
+    // decode loop that attends and advances the same streams step after step copies the list
+    // once, not twice a step (each copy is a DMA round trip between the step's kernels).
+    std::vector<int32_t> seq_shadow;
+    cudaStream_t seq_shadow_stream = nullptr;
     cudaEvent_t trace_ev[2] = {nullptr, nullptr};
     ~ptts_b200_kv() {
         for (cudaEvent_t e : trace_ev)
@@ -132,6 +137,24 @@ struct ptts_b200_kv {
         return r;
     }
     bool is_ring(int s) const { return h_ring_write[s] >= 0; }
+    // The per-sequence list (streams, then offsets) of an attend or advance call, on the device.
+    const int32_t* upload_seq(const std::vector<int32_t>& packed, cudaStream_t s) {
+        const size_t n = sizeof(int32_t) * packed.size();
+        if (s == seq_shadow_stream && packed == seq_shadow && seq_stream.bytes >= n)
+            return seq_stream.as<int32_t>();
+        int32_t* d = static_cast<int32_t*>(seq_stream.need(n));
+        staging.upload(d, packed.data(), n, s);
+        seq_shadow = packed;
+        seq_shadow_stream = s;
+        return d;
+    }
+    // Any other list through seq_stream (reset, evict, set_lengths).
+    int32_t* upload_scratch(const void* src, size_t n, cudaStream_t s) {
+        seq_shadow.clear();
+        int32_t* d = static_cast<int32_t*>(seq_stream.need(n));
+        staging.upload(d, src, n, s);
+        return d;
+    }
     bool is_window(int s) const { return h_window[s] > 0; }
     // The host mirror after a row went into stream s's write slot (RingSlots in complete_kv).
     void ring_commit(int s) {
@@ -254,21 +277,23 @@ int check_sequences(const ptts_b200_kv* kv, const int32_t* streams, const int32_
     long long total = 0;
     for (int i = 0; i < n_seq; ++i) {
         const int s = streams[i];
-        require(s >= 0 && s < kv->streams, PTTS_B200_ERR_ARG,
-                "stream " + std::to_string(s) + " is outside 0.." + std::to_string(kv->streams - 1));
-        require(!seen[s], PTTS_B200_ERR_ARG, "stream " + std::to_string(s) + " appears twice");
+        if (s < 0 || s >= kv->streams)
+            fail(PTTS_B200_ERR_ARG,
+                 "stream " + std::to_string(s) + " is outside 0.." + std::to_string(kv->streams - 1));
+        if (seen[s]) fail(PTTS_B200_ERR_ARG, "stream " + std::to_string(s) + " appears twice");
         seen[s] = 1;
         require(rows[i] >= 1, PTTS_B200_ERR_ARG, "every sequence needs at least one row");
         if (kv->is_ring(s)) {  // StreamingMHAState::complete_kv, transformer.rs:67-73
-            require(rows[i] == 1, PTTS_B200_ERR_ARG,
-                    "a ring cache takes one row at a time, not " + std::to_string(rows[i]) + " (stream " +
-                        std::to_string(s) + ")");
+            if (rows[i] != 1)
+                fail(PTTS_B200_ERR_ARG, "a ring cache takes one row at a time, not " + std::to_string(rows[i]) +
+                                            " (stream " + std::to_string(s) + ")");
             const int w = kv->h_ring_write[s];
-            require(w < kv->capacity, PTTS_B200_ERR_CAPACITY,
-                    "ring slot " + std::to_string(w) + " of a " + std::to_string(kv->capacity) + "-slot ring");
-            require(!kv->h_ring_valid[(size_t)s * kv->capacity + w], PTTS_B200_ERR_STATE,
-                    "ring slot " + std::to_string(w) + " still holds a row, evict it first (stream " +
-                        std::to_string(s) + ")");
+            if (w >= kv->capacity)
+                fail(PTTS_B200_ERR_CAPACITY,
+                     "ring slot " + std::to_string(w) + " of a " + std::to_string(kv->capacity) + "-slot ring");
+            if (kv->h_ring_valid[(size_t)s * kv->capacity + w])
+                fail(PTTS_B200_ERR_STATE, "ring slot " + std::to_string(w) +
+                                              " still holds a row, evict it first (stream " + std::to_string(s) + ")");
         }
         const long long need = (long long)kv->h_len[s] + rows[i];
         if (kv->is_window(s)) {  // positions grow past the capacity; the window must not wrap
@@ -305,17 +330,19 @@ long long attended_keys(const ptts_b200_kv* kv, int st) {
 // stream's position grows without bound: windowed streams run through the attention op.
 void refuse_window(const ptts_b200_kv* kv, const int32_t* streams, int n) {
     for (int i = 0; i < n; ++i)
-        require(!kv->is_window(streams[i]), PTTS_B200_ERR_UNSUPPORTED,
-                "stream " + std::to_string(streams[i]) +
-                    " is windowed: windowed streams run through ptts_b200_attend, not the layer stack");
+        if (kv->is_window(streams[i]))
+            fail(PTTS_B200_ERR_UNSUPPORTED,
+                 "stream " + std::to_string(streams[i]) +
+                     " is windowed: windowed streams run through ptts_b200_attend, not the layer stack");
 }
 
 void refuse_ring_prompt(const ptts_b200_kv* kv, const int32_t* streams, int n, bool decode) {
     if (decode) return;
     for (int i = 0; i < n; ++i)
-        require(!kv->is_ring(streams[i]), PTTS_B200_ERR_ARG,
-                "a ring cache takes one row at a time, in calls where every sequence has one row (stream " +
-                    std::to_string(streams[i]) + ")");
+        if (kv->is_ring(streams[i]))
+            fail(PTTS_B200_ERR_ARG,
+                 "a ring cache takes one row at a time, in calls where every sequence has one row (stream " +
+                     std::to_string(streams[i]) + ")");
 }
 
 // Ring state of stream st back to "not a ring" (kv_reset).
@@ -942,8 +969,7 @@ int ptts_b200_kv_advance(ptts_b200_kv* kv, const int32_t* streams_host, const in
         cudaStream_t s = as_stream(cuda_stream);
         std::vector<int32_t> packed(streams_host, streams_host + n);
         packed.insert(packed.end(), offsets.begin(), offsets.end());
-        int32_t* d = static_cast<int32_t*>(kv->seq_stream.need(sizeof(int32_t) * packed.size()));
-        kv->staging.upload(d, packed.data(), sizeof(int32_t) * packed.size(), s);
+        const int32_t* d = kv->upload_seq(packed, s);
         launch_advance(kv->len.as<int32_t>(), d, d + n, n, 0, kv->ring(), kv->capacity, s);
         check_launch();
         for (int i = 0; i < n; ++i) {
@@ -962,8 +988,7 @@ int ptts_b200_kv_reset(ptts_b200_kv* kv, const int32_t* streams_host, int n, voi
                     "stream out of range");
         DeviceScope scope(kv->device);
         cudaStream_t s = as_stream(cuda_stream);
-        int32_t* d = static_cast<int32_t*>(kv->seq_stream.need(sizeof(int32_t) * n));
-        kv->staging.upload(d, streams_host, sizeof(int32_t) * n, s);
+        const int32_t* d = kv->upload_scratch(streams_host, sizeof(int32_t) * n, s);
         launch_reset_streams(kv->k.p, kv->v.p, kv->len.as<int32_t>(), d, n, kv->layers,
                              (long long)kv->layer_bytes(), (long long)kv->stream_bytes(), s);
         check_launch();
@@ -1109,8 +1134,7 @@ int ptts_b200_attend(ptts_b200_kv* kv, int layer, const void* q, const void* k, 
         cudaStream_t s = as_stream(cuda_stream);
         std::vector<int32_t> packed(streams_host, streams_host + n_seq);
         packed.insert(packed.end(), offsets.begin(), offsets.end());
-        int32_t* d = static_cast<int32_t*>(kv->seq_stream.need(sizeof(int32_t) * packed.size()));
-        kv->staging.upload(d, packed.data(), sizeof(int32_t) * packed.size(), s);
+        const int32_t* d = kv->upload_seq(packed, s);
         const RowPlan plan = make_plan(kv, decode, d, d + n_seq, n_seq, n_rows, kv->row_stream,
                                        kv->row_pos, kv->prefix, s);
         check_launch();
@@ -1475,8 +1499,8 @@ int ptts_b200_kv_start_ring(ptts_b200_kv* kv, const int32_t* streams_host, int n
         for (int i = 0; i < n; ++i) {
             const int st = streams_host[i];
             require(st >= 0 && st < kv->streams, PTTS_B200_ERR_ARG, "stream out of range");
-            require(!kv->is_ring(st), PTTS_B200_ERR_STATE, "stream " + std::to_string(st) + " is already a ring");
-            require(!kv->is_window(st), PTTS_B200_ERR_STATE, "stream " + std::to_string(st) + " is windowed");
+            if (kv->is_ring(st)) fail(PTTS_B200_ERR_STATE, "stream " + std::to_string(st) + " is already a ring");
+            if (kv->is_window(st)) fail(PTTS_B200_ERR_STATE, "stream " + std::to_string(st) + " is windowed");
         }
         DeviceScope scope(kv->device);
         cudaStream_t s = as_stream(cuda_stream);
@@ -1507,9 +1531,9 @@ int ptts_b200_kv_set_window(ptts_b200_kv* kv, const int32_t* streams_host, int n
         for (int i = 0; i < n; ++i) {
             const int st = streams_host[i];
             require(st >= 0 && st < kv->streams, PTTS_B200_ERR_ARG, "stream out of range");
-            require(!kv->is_ring(st), PTTS_B200_ERR_STATE, "stream " + std::to_string(st) + " is a ring");
-            require(kv->h_len[st] == 0, PTTS_B200_ERR_STATE,
-                    "stream " + std::to_string(st) + " is not empty (KvCache::new starts a window)");
+            if (kv->is_ring(st)) fail(PTTS_B200_ERR_STATE, "stream " + std::to_string(st) + " is a ring");
+            if (kv->h_len[st] != 0)
+                fail(PTTS_B200_ERR_STATE, "stream " + std::to_string(st) + " is not empty (KvCache::new starts a window)");
         }
         DeviceScope scope(kv->device);
         cudaStream_t s = as_stream(cuda_stream);
@@ -1550,16 +1574,15 @@ int ptts_b200_kv_evict(ptts_b200_kv* kv, int stream, int prefix, const int32_t* 
         std::vector<char> seen(kv->capacity, 0);
         for (int i = 0; i < n; ++i) {
             const int sl = slots_host[i];
-            require(sl >= prefix && sl < kv->capacity && hv[sl] && !seen[sl], PTTS_B200_ERR_ARG,
-                    "slot " + std::to_string(sl) + " holds no row past the prefix");
+            if (sl < prefix || sl >= kv->capacity || !hv[sl] || seen[sl])
+                fail(PTTS_B200_ERR_ARG, "slot " + std::to_string(sl) + " holds no row past the prefix");
             seen[sl] = 1;
         }
         if (n == 0) return;
         DeviceScope scope(kv->device);
         cudaStream_t s = as_stream(cuda_stream);
         RingEvictArgs a{};
-        int32_t* d = static_cast<int32_t*>(kv->seq_stream.need(sizeof(int32_t) * n));
-        kv->staging.upload(d, slots_host, sizeof(int32_t) * n, s);
+        const int32_t* d = kv->upload_scratch(slots_host, sizeof(int32_t) * n, s);
         a.k_cache = kv->k.p;
         a.layers = kv->layers;
         const long long elem = kv->dtype == PTTS_B200_BF16 ? 2 : 4;
@@ -1605,8 +1628,7 @@ int ptts_b200_kv_set_lengths(ptts_b200_kv* kv, const int32_t* streams_host,
         cudaStream_t s = as_stream(cuda_stream);
         std::vector<int32_t> packed(streams_host, streams_host + n);
         packed.insert(packed.end(), lengths_host, lengths_host + n);
-        int32_t* d = static_cast<int32_t*>(kv->seq_stream.need(sizeof(int32_t) * packed.size()));
-        kv->staging.upload(d, packed.data(), sizeof(int32_t) * packed.size(), s);
+        const int32_t* d = kv->upload_scratch(packed.data(), sizeof(int32_t) * packed.size(), s);
         launch_set_lengths(kv->len.as<int32_t>(), d, d + n, n, s);
         check_launch();
         for (int i = 0; i < n; ++i) kv->h_len[streams_host[i]] = lengths_host[i];

@@ -49,6 +49,11 @@ int guarded(F&& f) {
     }
 }
 
+// Checks that run per stream build their message only on failure (`if (!ok) fail(...)`): a
+// message assembled before the test costs an allocation per stream per call.
+inline void require(bool ok, int code, const char* msg) {
+    if (!ok) fail(code, msg);
+}
 inline void require(bool ok, int code, const std::string& msg) {
     if (!ok) fail(code, msg);
 }
