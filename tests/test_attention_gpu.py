@@ -152,6 +152,55 @@ def test_split_kv_partition_edges(ptts, oracle, cuda):
     kv.check()
 
 
+def test_stream_list_copy_is_reused_only_while_it_holds(ptts, oracle, cuda):
+    """attend and advance of an unchanged stream list on one CUDA stream share one device copy
+    of the list; set_lengths, reset, another CUDA stream or another list take a fresh copy.
+    Every call's output is checked against the oracle."""
+    import torch
+    rng = np.random.default_rng(4)
+    S, cap = 8, 64
+    lens = rng.integers(1, 20, S).astype(np.int32)
+    kv = ptts.KvState(1, S, cap, dtype="bf16")
+    kc = np.zeros((S, cap, 8, 64), np.float32)
+    vc = np.zeros_like(kc)
+    for s in range(S):
+        k = torch.randn(int(lens[s]), 8, 64).bfloat16()
+        v = torch.randn(int(lens[s]), 8, 64).bfloat16()
+        kv.load_prefix(0, s, k.to(cuda), v.to(cuda))
+        kc[s, : lens[s]], vc[s, : lens[s]] = _f32(k), _f32(v)
+
+    def step(streams, stream=None):
+        streams = np.asarray(streams, np.int32)
+        B = len(streams)
+        ones = np.ones(B, np.int32)
+        q, k, v = (torch.randn(B, 8, 64).bfloat16() for _ in range(3))
+        qd, kd, vd = q.to(cuda), k.to(cuda), v.to(cuda)
+        if stream is not None:
+            stream.wait_stream(torch.cuda.current_stream())
+        out = ptts.attend(kv, 0, qd, kd, vd, streams, ones, out_dtype="f32", stream=stream)
+        kv.advance(streams, ones, stream=stream)
+        torch.cuda.synchronize()
+        want = oracle.attend(_f32(q), _f32(k), _f32(v), kc, vc, lens, streams,
+                             np.arange(B + 1, dtype=np.int32), store=oracle.ROUND_KV)
+        lens[streams] += 1
+        assert normwise(_f32(out), want) < TOL, list(streams)
+        np.testing.assert_array_equal(kv.lengths(), lens)
+
+    a = [3, 1, 5]
+    step(a)
+    step(a)  # the list's copy from the call before
+    lens -= 1
+    kv.set_lengths(np.arange(S, dtype=np.int32), lens)  # the scratch list is overwritten
+    step(a)
+    kv.reset([5])
+    lens[5] = 0
+    step(a)
+    step(a, stream=torch.cuda.Stream(device=cuda))
+    step([5, 3, 1])
+    step([3, 1, 5, 0])
+    kv.check()
+
+
 def test_gqa_is_attention_with_repeated_kv_heads(ptts, cuda):
     """transformer.rs:1112-1164 on the device: 2 KV heads shared by 8 query heads give the
     same outputs and cache as the 8 heads repeated, over a prompt and two single steps."""
