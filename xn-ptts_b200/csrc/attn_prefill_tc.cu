@@ -115,7 +115,9 @@ __device__ __forceinline__ void store_row_hilo(unsigned char* hi, unsigned char*
     }
 }
 
-__global__ void __launch_bounds__(kThreadsP, 1) prefill_tc_kernel(PrefillArgs a, const int2* tiles) {
+// Two CTAs per SM (shared memory allows two): ten warps put three on one SM sub-partition, whose
+// 16K registers hold three warps only at 168 registers a thread or fewer (0 spills at 168).
+__global__ void __maxnreg__(168) prefill_tc_kernel(PrefillArgs a, const int2* tiles) {
     extern __shared__ unsigned char smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t base = (raw + 1023u) & ~1023u;
