@@ -232,6 +232,56 @@ def test_long_prompts_match_the_oracle(ptts, oracle, cuda):
     assert max(errs) < TOL
 
 
+def test_full_config5_shard_on_sampled_streams(ptts, oracle, cuda):
+    """The benchmark's whole per-GPU workload: the 40m stack (9 layers), 512 streams with
+    prompts of U{32..512} rows (seed 4, 139k rows in one prefill: the persistent prompt
+    linears and the tcgen05 prefill attention), then decode steps of all 512 streams (two
+    lanes, compact-ring attention). Streams never interact, so the oracle runs only a sample of
+    them, on their own prompts and inputs, and every sampled stream's rows are compared."""
+    import importlib
+    import torch
+    wl = importlib.import_module("xn_ptts_b200.workloads")
+    cfg = ptts.PHONON_40M
+    B = 512
+    prefixes = np.asarray(wl.prefix_lengths(4096, 32, 512, 4)[:B], np.int32)
+    cap = int(prefixes.max()) + 4
+    w = ptts.random_weights(cfg, 4)
+    model = ptts.Transformer(cfg)
+    model.load(w)
+    kv = ptts.KvState(cfg.num_layers, B, cap, dtype="bf16")
+    offs = np.concatenate([[0], np.cumsum(prefixes)]).astype(np.int32)
+    g = torch.Generator().manual_seed(4)
+    x = torch.randn(int(offs[-1]), 512, generator=g).bfloat16()
+    y = model.forward(kv, x.to(cuda), list(range(B)), prefixes.tolist())
+    y = _f32(y)
+    steps = [torch.randn(B, 512, generator=g).bfloat16() for _ in range(3)]
+    ys = [_f32(model.step(kv, list(range(B)), xs.to(cuda))) for xs in steps]
+    kv.check()
+    np.testing.assert_array_equal(kv.lengths(), prefixes + len(steps))
+
+    sample = np.random.default_rng(4).choice(B, size=8, replace=False)
+    sample.sort()
+    om = oracle.Model(cfg, w)
+    shape = (cfg.num_layers, len(sample), cap, cfg.num_heads, cfg.head_dim)
+    kc, vc = np.zeros(shape, np.float32), np.zeros(shape, np.float32)
+    xf = _f32(x)
+    rows = prefixes[sample]
+    o_offs = np.concatenate([[0], np.cumsum(rows)]).astype(np.int32)
+    xin = np.concatenate([xf[offs[b]:offs[b + 1]] for b in sample])
+    lengths = np.zeros(len(sample), np.int32)
+    local = list(range(len(sample)))
+    want = om.forward(xin, kc, vc, lengths, local, o_offs, store=oracle.ROUND_KV)
+    got = np.concatenate([y[offs[b]:offs[b + 1]] for b in sample])
+    errs = [_report("config-5 prefill (sampled streams)", got, want)]
+    lengths += rows
+    for i, xs in enumerate(steps):
+        want = om.forward(_f32(xs)[sample], kc, vc, lengths, local,
+                          np.arange(len(sample) + 1, dtype=np.int32), store=oracle.ROUND_KV)
+        lengths += 1
+        errs.append(_report(f"config-5 step {i}", ys[i][sample], want))
+    assert max(errs) < TOL
+
+
 def test_grouped_query_attention_in_the_stack(ptts, oracle, cuda):
     """num_kv_heads < num_heads through the whole stack (transformer.rs:1112-1164's equivalence,
     here against the oracle's GQA): a ragged prompt and decode steps."""
