@@ -79,3 +79,37 @@ def test_no_cpu_fallback_without_the_library(ptts, monkeypatch, tmp_path):
     monkeypatch.setattr(ptts, "_lib", None)
     with pytest.raises(ptts.PttsError):
         ptts.lib()
+
+
+def test_header_is_plain_c_and_links(ptts, tmp_path):
+    """The header compiles as C99 (no C++ in the boundary), every declared entry point links
+    against the built library, and a C host gets the version and an error message without a
+    GPU (a NULL handle is refused before any device work)."""
+    import shutil
+    import subprocess
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    names = _declared()
+    src = tmp_path / "abi_check.c"
+    src.write_text(
+        "#include <stdio.h>\n#include <string.h>\n#include \"ptts_b200.h\"\n"
+        "typedef void (*any_fn)(void);\n"
+        "static any_fn table[] = {\n" + "".join(f"    (any_fn){n},\n" for n in names) + "};\n"
+        "int main(void) {\n"
+        "    size_t n = sizeof(table) / sizeof(table[0]);\n"
+        "    for (size_t i = 0; i < n; ++i) if (!table[i]) return 2;\n"
+        "    if (strncmp(ptts_b200_version(), \"ptts_b200\", 9) != 0) return 3;\n"
+        "    if (ptts_b200_kv_create(0, 1, 1, 1, 8, 64, 1, NULL) == 0) return 4;\n"
+        "    if (strlen(ptts_b200_last_error()) == 0) return 5;\n"
+        "    printf(\"%zu entry points; last error: %s\\n\", n, ptts_b200_last_error());\n"
+        "    return 0;\n}\n")
+    lib = os.path.abspath(ptts.lib()._name)
+    exe = tmp_path / "abi_check"
+    r = subprocess.run([cc, "-std=c99", "-Wall", "-Werror", "-I", os.path.join(ROOT, "include"), str(src),
+                        "-o", str(exe), lib, "-Wl,-rpath," + os.path.dirname(lib)],
+                       capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=120)
+    assert r.returncode == 0, (r.returncode, r.stdout, r.stderr)
+    assert "entry points" in r.stdout
