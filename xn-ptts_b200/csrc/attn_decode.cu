@@ -488,14 +488,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(DecodeArgs a) 
 
 template <typename T, class R>
 void launch_typed(const DecodeArgs& a, int grid, cudaStream_t s) {
-    static int configured = -1;  // the device whose attributes were set last
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (configured != dev) {
-        cudaFuncSetAttribute(decode_attn_kernel<T, R>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             R::kSmemBytes);
-        configured = dev;
-    }
+    set_max_dynamic_smem(reinterpret_cast<const void*>(decode_attn_kernel<T, R>), R::kSmemBytes);
     launch_k(decode_attn_kernel<T, R>, dim3(grid), dim3(kThreads), R::kSmemBytes, s, a);
 }
 

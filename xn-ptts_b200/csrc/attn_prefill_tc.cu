@@ -328,13 +328,7 @@ __global__ void __maxnreg__(168) prefill_tc_kernel(PrefillArgs a, const int2* ti
 }  // namespace
 
 void launch_prefill_attn_tc(const PrefillArgs& a, const int2* tiles, int n_tiles, cudaStream_t s) {
-    static int configured = -1;
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (configured != dev) {
-        cudaFuncSetAttribute(prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemP);
-        configured = dev;
-    }
+    set_max_dynamic_smem(reinterpret_cast<const void*>(prefill_tc_kernel), kSmemP);
     launch_k(prefill_tc_kernel, dim3(n_tiles, kRowWidth / kHeadDim), dim3(kThreadsP), kSmemP, s, a, tiles);
 }
 

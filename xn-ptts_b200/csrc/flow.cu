@@ -220,13 +220,7 @@ void launch_flow_ln_mod(const FlowModArgs& a, cudaStream_t s) {
 
 void launch_flow_out(const FlowOutArgs& a, cudaStream_t s) {
     const size_t smem = sizeof(float) * a.C * (a.L + 1);
-    static int configured = -1;
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (configured != dev) {
-        cudaFuncSetAttribute(flow_out_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-        configured = dev;
-    }
+    set_max_dynamic_smem(reinterpret_cast<const void*>(flow_out_kernel), 200 * 1024);
     launch_k(flow_out_kernel, dim3((a.M + 7) / 8), dim3(256), smem, s, a);
 }
 

@@ -25,6 +25,9 @@ bool pdl_enabled();
 // Asks, once per kernel and device, for the largest shared-memory carveout. Kernels of the two
 // lanes of a step share SMs, and an SM runs CTAs side by side only under one carveout.
 void prefer_max_shared(const void* kernel);
+// Raises a kernel's dynamic shared-memory limit to `bytes`, once per kernel and device. Safe when
+// host threads drive different devices at once (one object per device, one thread each).
+void set_max_dynamic_smem(const void* kernel, int bytes);
 template <typename... KArgs, typename... Args>
 inline cudaError_t launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
                             cudaStream_t s, Args&&... args) {

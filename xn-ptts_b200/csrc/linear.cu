@@ -431,14 +431,7 @@ __global__ void __launch_bounds__(128) ln_kernel(LnArgs a) {
 
 template <int EPI, int TM, bool F16>
 void launch_tile(const LinearArgs& a, cudaStream_t s) {
-    static int configured = -1;  // device whose attribute was set last
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (configured != dev) {
-        cudaFuncSetAttribute(linear_kernel<EPI, TM, F16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             Tile<TM>::kSmemBytes);
-        configured = dev;
-    }
+    set_max_dynamic_smem(reinterpret_cast<const void*>(linear_kernel<EPI, TM, F16>), Tile<TM>::kSmemBytes);
     dim3 grid(a.N / BN, (a.M + TM - 1) / TM, a.splits);
     launch_k(linear_kernel<EPI, TM, F16>, grid, dim3(kThreads), Tile<TM>::kSmemBytes, s, a);
 }

@@ -753,13 +753,7 @@ bool launch_tma(const LinearArgs& a, cudaStream_t s) {
     } else {
         mxl = mx;
     }
-    static int configured = -1;
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (configured != dev) {
-        cudaFuncSetAttribute(linear_tma_kernel<EPI, RT, WLO>, cudaFuncAttributeMaxDynamicSharedMemorySize, T::kSmem);
-        configured = dev;
-    }
+    set_max_dynamic_smem(reinterpret_cast<const void*>(linear_tma_kernel<EPI, RT, WLO>), T::kSmem);
     dim3 grid(a.N / FT, (a.M + RT - 1) / RT, a.splits);
     launch_k(linear_tma_kernel<EPI, RT, WLO>, grid, dim3(kThreadsTma), T::kSmem, s, a, mw, mwl, mx, mxl);
     return true;
@@ -776,15 +770,10 @@ bool launch_persist(const LinearArgs& a, cudaStream_t s) {
     if (WLO && !f16_map(&mwl, a.wh_lo, a.N, a.K, FT, bf)) return false;
     mxl = mx;
     if (a.a_lo && !f16_map(&mxl, a.a_lo, a.M, a.K, PT, bf)) return false;
-    static int configured = -1;
-    int dev = 0;
+    set_max_dynamic_smem(reinterpret_cast<const void*>(linear_persist_kernel<EPI, WLO>), T::kSmem);
+    int dev = 0, sms = 0;
     cudaGetDevice(&dev);
-    static int sms = 0;
-    if (configured != dev) {
-        cudaFuncSetAttribute(linear_persist_kernel<EPI, WLO>, cudaFuncAttributeMaxDynamicSharedMemorySize, T::kSmem);
-        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-        configured = dev;
-    }
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms < 1) sms = 1;
     const int tiles = (a.N / FT) * ((a.M + PT - 1) / PT);
     launch_k(linear_persist_kernel<EPI, WLO>, dim3(tiles < sms ? tiles : sms), dim3(kPersistThreads), T::kSmem, s, a,
              mw, mwl, mx, mxl);

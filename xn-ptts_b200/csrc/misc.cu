@@ -293,6 +293,18 @@ void prefer_max_shared(const void* kernel) {
         cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
 }
 
+void set_max_dynamic_smem(const void* kernel, int bytes) {
+    static std::mutex mu;
+    static std::set<std::pair<int, const void*>> done;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> g(mu);
+    if (done.count({dev, kernel})) return;
+    // Recorded only once set, so a launch on this device never precedes the attribute.
+    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) == cudaSuccess)
+        done.insert({dev, kernel});
+}
+
 bool pdl_enabled() {
     static const bool on = [] {
         const char* e = getenv("PTTS_B200_PDL");
