@@ -1,25 +1,35 @@
 """Benchmark: flow-LM decode frames/s (config 5 shard) with decode-attention GB/s vs HBM peak.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--repeats R] [--impl ours|reference]
 
 Workload (the largest single-GPU configuration): the 40m flow LM shape
 (9 layers, d_model 512, 8 heads of 64, ff 2048), random-init int8 per-output-channel weights
 (scales U(0.005, 0.02), seed 4), 512 independent streams per GPU (GPU g holds streams
 512g..512g+511 of 4096), prefixes U{32..512} prefilled before timing, then decode frames: one
 row per stream per frame through all layers (QKV + RoPE + KV append + split-KV attention +
-out_proj + FFN) replayed as one CUDA graph. Config 5 runs 250 frames; steps beyond that cycle
-the 250-frame window (lengths return to the prefixes), so every timed step is a frame of the
-same length distribution. A step = one frame for all streams of a GPU.
+out_proj + FFN) replayed as one CUDA graph. A step = one frame for all streams of a GPU.
+
+Timed window. Config 5 runs 250 frames, and a frame's KV read grows with its index (2.7 GB at
+frame 5, 3.8 GB on average, 4.8 GB at frame 249 per GPU). K < 250 timed frames sit in the middle
+of the window (frames (250 - K) / 2 ..), with the W warm-up frames just before them, so they see
+the window's average KV; the K-frame region is timed R times from that same start (lengths set
+back between repeats, outside the timed region) and ms_per_step is the median, with min and
+max beside it. K >= 250 frames cycle the whole window from frame 0 (lengths return to the
+prefixes every 250 frames), timed once.
 
 value  = stream-frames per second over all GPUs, inputs resident in HBM.
 e2e    = the same through ptts_b200_step with pinned HOST input/output (H2D + D2H per step).
 roofline = the decode-attention kernel: algorithmic bytes (K and V rows read for every
            attended position, q read, output written) / its CUDA-event duration in a traced
            pass over the same frames, against MEASURED_PEAKS.json's HBM copy bandwidth.
+decode_attn = config 3 (256 ragged streams, lengths U{64..2048}, bf16 KV, 100-step window) run
+           through the attention op in the same process: the op's algorithmic GB/s and the
+           decode kernel's own fraction of the HBM peak.
 cpu_baseline = the C oracle (a port of the reference's CPU path) on the host cores, on a
            sample of 16 streams of the same workload.
-Multi-GPU: one process per GPU (torchrun), independent shards, no data-path collective; NCCL
-only for the start barrier and the max over ranks of the timed duration.
+Multi-GPU: one process per GPU (torchrun), independent shards, no data-path collective and no
+NCCL: the start/stop barriers and the max over ranks of the timed duration go through a gloo
+process group on host tensors.
 """
 from __future__ import annotations
 
@@ -128,24 +138,47 @@ def shard_streams(rank: int, world: int):
     return list(range(rank * STREAMS_PER_GPU, (rank + 1) * STREAMS_PER_GPU))
 
 
-def barrier(dist, device_index=None):
-    """Start/stop barrier of the timed region (no-op on one process)."""
+def barrier(dist):
+    """Start/stop barrier of the timed region (no-op on one process; gloo, host side)."""
     if dist is None:
         return
-    if device_index is None:
-        dist.barrier()
-    else:
-        dist.barrier(device_ids=[device_index])
+    dist.barrier()
 
 
-def max_over_ranks(dist, ms: float, device) -> float:
-    """The slowest rank's duration: the job's time."""
+def max_over_ranks(dist, ms: float) -> float:
+    """The slowest rank's duration: the job's time (a host tensor through gloo)."""
     if dist is None:
         return ms
     import torch
-    t = torch.tensor([ms], dtype=torch.float64, device=device)
+    t = torch.tensor([ms], dtype=torch.float64)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
+
+
+def gather_over_ranks(dist, v: float) -> list:
+    """Every rank's value, in rank order (one element on one process)."""
+    if dist is None:
+        return [v]
+    import torch
+    t = torch.tensor([v], dtype=torch.float64)
+    out = [torch.zeros_like(t) for _ in range(dist.get_world_size())]
+    dist.all_gather(out, t)
+    return [float(x.item()) for x in out]
+
+
+def timing_window(steps: int, warmup: int):
+    """(first warm-up frame, first timed frame) in the 250-frame window. K < 250 timed frames
+    are centred in the window, the warm-up frames just before them; K >= 250 cycle the window
+    from frame 0 (warm-up frames first)."""
+    if steps >= FRAMES:
+        return 0, warmup % FRAMES
+    first = (FRAMES - steps) // 2
+    return max(first - warmup, 0), first
+
+
+def spread(values) -> dict:
+    vs = sorted(values)
+    return {"min": vs[0], "median": statistics.median(vs), "max": vs[-1]}
 
 
 def load():
@@ -160,9 +193,13 @@ def shard_prefixes(wl, rank: int):
     return allp[ids[0]:ids[-1] + 1]
 
 
-def cpu_baseline(ptts, wl, cfg, weights, steps: int | None = None, budget_s: float = 12.0):
+def cpu_baseline(ptts, wl, cfg, weights, steps: int | None = None, warmup: int = 0, start: int = 0,
+                 budget_s: float = 12.0):
     """The oracle on the host cores: a sample of CPU_SAMPLE_STREAMS streams of rank 0's shard,
-    prefilled (untimed), then decode frames timed until `steps` frames or `budget_s` seconds."""
+    prefilled (untimed), then decode frames from frame `start` of the window (lengths set to
+    prefix + start; the cache rows of the frames skipped stay zero, which changes no arithmetic
+    count), `warmup` untimed frames, then frames timed until `steps` frames or `budget_s`
+    seconds. Frames past the window's end cycle it (lengths return to the prefixes)."""
     import numpy as np
     import torch
     import oracle
@@ -181,16 +218,22 @@ def cpu_baseline(ptts, wl, cfg, weights, steps: int | None = None, budget_s: flo
     streams = np.arange(n, dtype=np.int32)
     threads = oracle.threads()
     om.forward(x, kc, vc, lengths, streams, offs, store=oracle.ROUND_KV, n_threads=threads)
-    lengths = prefixes.copy()
     one = np.arange(n + 1, dtype=np.int32)
     frames = [torch.randn(n, cfg.d_model, generator=g).bfloat16().float().numpy() for _ in range(8)]
+    state = {"f": start % FRAMES}
+
+    def frame():
+        f = state["f"]
+        lengths = prefixes + f
+        om.forward(frames[f % len(frames)], kc, vc, lengths, streams, one, store=oracle.ROUND_KV,
+                   n_threads=threads)
+        state["f"] = (f + 1) % FRAMES
+
+    for _ in range(warmup):
+        frame()
     done, t0 = 0, time.perf_counter()
     while True:
-        if done and done % FRAMES == 0:
-            lengths = prefixes.copy()
-        om.forward(frames[done % len(frames)], kc, vc, lengths, streams, one, store=oracle.ROUND_KV,
-                   n_threads=threads)
-        lengths += 1
+        frame()
         done += 1
         el = time.perf_counter() - t0
         if (steps is not None and done >= steps) or (steps is None and el >= budget_s) or done >= 4 * FRAMES:
@@ -198,12 +241,14 @@ def cpu_baseline(ptts, wl, cfg, weights, steps: int | None = None, budget_s: flo
     el = time.perf_counter() - t0
     return {"value": n * done / el, "unit": "frames/s", "cores": threads, "kind": "port",
             "sample": f"{n} streams of the config-5 shard (prefixes U{{32..512}}), {done} decode frames "
-                      f"of the 40m stack after an untimed prefill, C oracle with OpenMP",
+                      f"of the 40m stack from frame {start % FRAMES} of the 250-frame window, after an "
+                      f"untimed prefill and {warmup} untimed frames; C oracle with OpenMP",
             "seconds": el, "frames": done}
 
 
 def run_reference(args):
-    """--impl reference: the reference's CPU path (the C oracle port) on the host cores."""
+    """--impl reference: the reference's CPU path (the C oracle port) on the host cores, over
+    the same timed frames of the window as the GPU arm (see timing_window)."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
@@ -212,8 +257,9 @@ def run_reference(args):
     weights = ptts.random_weights(cfg, SEED)
     import oracle
     oracle.lib()
-    # Warm-up frames are part of the same sampled run; time exactly `steps` frames after them.
-    cb = cpu_baseline(ptts, wl, cfg, weights, steps=args.warmup + args.steps)
+    w0, t0 = timing_window(args.steps, args.warmup)
+    cb = cpu_baseline(ptts, wl, cfg, weights, steps=args.steps, warmup=t0 - w0 if args.steps < FRAMES else args.warmup,
+                      start=w0)
     per_frame = cb["seconds"] / cb["frames"]
     value = CPU_SAMPLE_STREAMS / per_frame
     line = {
@@ -222,7 +268,11 @@ def run_reference(args):
         "ms_per_step": per_frame * 1e3, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32 (bf16-rounded storage)", "data": "synthetic",
         "config": {"workload": "config5 shard: 40m flow LM, prefixes U{32..512}, decode frames",
-                   "streams_sampled": CPU_SAMPLE_STREAMS},
+                   "streams_sampled": CPU_SAMPLE_STREAMS, "timed_frames": [t0, t0 + args.steps],
+                   "extrapolated": f"stream-frames/s of {CPU_SAMPLE_STREAMS} sampled streams of the "
+                                   f"{STREAMS_PER_GPU}-stream shard: streams never interact, so the "
+                                   "per-stream rate is the shard's; ms_per_step is the time of one "
+                                   f"frame of the {CPU_SAMPLE_STREAMS} sampled streams"},
         "cpu_baseline": {"value": value, "unit": "frames/s", "cores": cb["cores"], "kind": "port",
                          "sample": cb["sample"]},
         "e2e": {"value": value, "unit": "frames/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -264,9 +314,11 @@ def run_ours(args):
     dev = torch.device(f"cuda:{local}")
     dist = None
     if world > 1:
+        # Host-side plumbing only (barriers, the max over ranks): the data path has no
+        # collective, so no NCCL communicator is created.
         import datetime
         import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=120))
 
     ptts, wl = load()
     cfg, B, prefixes, seed, desc = workload_spec(args, ptts, wl, rank)
@@ -312,15 +364,23 @@ def run_ours(args):
 
     state = {"f": 0}
 
+    def goto(f):
+        """Window position f: every stream's length prefix + f (a host call, outside timing)."""
+        kv.set_lengths(streams, prefixes + (f % FRAMES))
+        state["f"] = f % FRAMES
+        torch.cuda.synchronize()
+
     def step(x_src, out):
         f = state["f"]
-        if f and f % FRAMES == 0:
+        if f == FRAMES:
             kv.set_lengths(streams, prefixes)
-        model.step(kv, streams, x_src(f % FRAMES), out=out)
+            f = 0
+        model.step(kv, streams, x_src(f), out=out)
         state["f"] = f + 1
 
-    def timed(x_src, out, k: int):
-        barrier(dist, local)
+    def timed(x_src, out, k: int, start: int):
+        goto(start)
+        barrier(dist)
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
@@ -328,7 +388,49 @@ def run_ours(args):
             step(x_src, out)
         e1.record(stream)
         e1.synchronize()
-        return max_over_ranks(dist, e0.elapsed_time(e1), dev)
+        mine = e0.elapsed_time(e1)
+        return max_over_ranks(dist, mine), mine
+
+    w0, t0 = timing_window(args.steps, args.warmup)
+    cycling = args.steps >= FRAMES
+
+    def run_repeats(x_src, out, min_repeats):
+        """Warm-up frames (before the timed start), then R timed regions of K frames, each from
+        the same start. Returns per-repeat job times (max over ranks) and this rank's own."""
+        goto(w0)
+        for _ in range(args.warmup):
+            step(x_src, out)
+        torch.cuda.synchronize()
+        if cycling:
+            job, mine = timed_cycle(x_src, out)
+            return [job], [mine]
+        jobs, mine = [], []
+        r = 0
+        target = args.repeats if args.repeats > 0 else min_repeats
+        while r < target:
+            j, m = timed(x_src, out, args.steps, t0)
+            jobs.append(j)
+            mine.append(m)
+            r += 1
+            if args.repeats <= 0 and r == min_repeats:
+                # Auto: at least min_repeats, and at least ~1 s of timed work in all, so the
+                # 200 ms clock sampler sees the timed region (the same count on every rank).
+                want = int(np.ceil(1000.0 / max(statistics.median(jobs), 1e-3)))
+                target = max(min_repeats, min(want, 200))
+        return jobs, mine
+
+    def timed_cycle(x_src, out):
+        # K >= 250: one region, frames cycling the whole window from the warm-up's end.
+        barrier(dist)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            step(x_src, out)
+        e1.record(stream)
+        e1.synchronize()
+        m = e0.elapsed_time(e1)
+        return max_over_ranks(dist, m), m
 
     # ---- device-resident inputs --------------------------------------------------------------
     dev_src = lambda f: x_frames[f]
@@ -337,38 +439,38 @@ def run_ours(args):
     sampler = ClockSampler(local)
     sampler.start()
     time.sleep(0.5)
-    for _ in range(args.warmup):
-        step(dev_src, y)
-    torch.cuda.synchronize()
-    ms = timed(dev_src, y, args.steps)
+    jobs, mine = run_repeats(dev_src, y, 15)
     clocks = sampler.stop()
+    ms = statistics.median(jobs)
     value = world * B * args.steps / (ms / 1e3)
     lanes = ptts.step_lanes(B)
     launches_per_step = 1 + lanes * (2 + 7 * L)  # advance + per lane: plan, final reduce and per
     #                       layer LN1, in_proj, attention (merge fused), out_proj, LN2, linear1, linear2
-    gpu_launches = args.steps * launches_per_step + (args.warmup + args.steps) // FRAMES
+    wraps = (t0 + args.steps - 1) // FRAMES if not cycling else (args.warmup + args.steps) // FRAMES
+    gpu_launches = len(jobs) * (args.steps * launches_per_step + wraps)
+    per_rank = gather_over_ranks(dist, statistics.median(mine) / args.steps)
 
     # ---- end to end through pinned host buffers ------------------------------------------------
     x_host = x_frames.cpu().pin_memory()
     y_host = torch.empty(B, cfg.d_model, dtype=torch.float32).pin_memory()
-    kv.set_lengths(streams, prefixes)
-    state["f"] = 0
     host_src = lambda f: x_host[f]
-    for _ in range(args.warmup):
-        step(host_src, y_host)
-    torch.cuda.synchronize()
-    ms_e2e = timed(host_src, y_host, args.steps)
+    ejobs, _ = run_repeats(host_src, y_host, 15)
+    ms_e2e = statistics.median(ejobs)
     e2e = {"value": world * B * args.steps / (ms_e2e / 1e3), "unit": "frames/s",
            "h2d_bytes_per_step": B * cfg.d_model * 2, "d2h_bytes_per_step": B * cfg.d_model * 4,
-           "ms_per_step": ms_e2e / args.steps}
+           "ms_per_step": ms_e2e / args.steps, "repeats": len(ejobs)}
 
     # ---- traced pass: decode-attention launch durations with CUDA events ------------------------
-    kv.set_lengths(streams, prefixes)
-    state["f"] = 0
+    # The same frames as the timed region (its first repeat).
+    goto(w0)
+    for _ in range(args.warmup):
+        step(dev_src, y)
+    if not cycling:
+        goto(t0)
+    torch.cuda.synchronize()
     ptts.set_tracing(True)
     ptts.trace(reset=True)
-    traced = min(args.steps + args.warmup, FRAMES)
-    for _ in range(traced):
+    for _ in range(min(args.steps, FRAMES)):
         step(dev_src, y)
     torch.cuda.synchronize()
     tr = ptts.trace(reset=True)
@@ -393,28 +495,28 @@ def run_ours(args):
 
     # ---- kernel timeline inside the graph (device stamps), for the attention as it runs there --
     # Events around a launch cut it off from its neighbours; the stamps do not. The last of a few
-    # graph-replayed steps is read: per attention launch, from its first CTA past the wait on its
-    # predecessor to its last CTA done (and from its first CTA's start, which also counts the
-    # copies issued before that wait).
-    kv.set_lengths(streams, prefixes)
-    state["f"] = 0
+    # graph-replayed steps is read, at the middle of the timed frames: per attention launch, from
+    # its first CTA past the wait on its predecessor to its last CTA done (and from its first
+    # CTA's start, which also counts the copies issued before that wait).
+    mid = (t0 + args.steps // 2) % FRAMES if not cycling else FRAMES // 2
+    goto(max(mid - 2, 0))
     model.stamps(lanes * (2 + 8 * L))
-    stamped = 12
-    for _ in range(stamped):
+    while state["f"] <= mid:
         step(dev_src, y)
     torch.cuda.synchronize()
     stamps = model.read_stamps()
     model.stamps(0)
     att = [e for e in stamps if e["kernel"] == "attention"]
-    kv_rows = float(prefixes.sum()) + B * stamped  # attended keys of the stamped step
+    kv_rows = float(prefixes.sum()) + B * (mid + 1)  # attended keys of the stamped step
     bytes_stamped = L * (kv_rows * 2 * 1024 + B * 512 * 6)
     busy = sum(e["end_us"] - e["start_us"] for e in att)
     busy_entry = sum(e["end_us"] - e["entry_us"] for e in att)
     if att and busy > 0:
         roofline["in_frame"] = {
             "source": "device stamps (globaltimer) of the attention launches of one graph-replayed step "
-                      f"(frame {stamped} of the window)",
+                      f"(frame {mid} of the window)",
             "launches": len(att), "us_per_launch": busy / len(att),
+            "bytes_per_launch": bytes_stamped / len(att),
             "achieved": bytes_stamped / (busy / 1e6) / 1e9,
             "frac": bytes_stamped / (busy / 1e6) / 1e9 / peak,
             "us_per_launch_from_first_cta": busy_entry / len(att),
@@ -436,20 +538,22 @@ def run_ours(args):
         flow = ptts.Flow(fcfg, device=local)
         flow.load(ptts.random_flow_weights(fcfg, seed, bf16_exact=True))
         noise = torch.randn(FRAMES, B, fcfg.ldim, generator=g, device=dev)
-        fstate = {"f": 0, "lat": None}
+        fstate = {"lat": None}
 
         def frame():
-            f = fstate["f"]
-            if f and f % FRAMES == 0:
+            f = state["f"]
+            if f == FRAMES:
                 kv.set_lengths(streams, prefixes)
-            fstate["lat"], _ = flow.frame(model, kv, streams, fstate["lat"], noise[f % FRAMES])
-            fstate["f"] = f + 1
+                f = 0
+            fstate["lat"], _ = flow.frame(model, kv, streams, fstate["lat"], noise[f])
+            state["f"] = f + 1
 
-        kv.set_lengths(streams, prefixes)
+        k = min(args.steps, FRAMES)
+        goto(w0)
         for _ in range(args.warmup):
             frame()
-        k = min(args.steps, FRAMES)
-        barrier(dist, local)
+        goto(t0 if not cycling else 0)
+        barrier(dist)
         torch.cuda.synchronize()
         f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         f0.record(stream)
@@ -457,16 +561,23 @@ def run_ours(args):
             frame()
         f1.record(stream)
         f1.synchronize()
-        fms = max_over_ranks(dist, f0.elapsed_time(f1), dev)
+        fms = max_over_ranks(dist, f0.elapsed_time(f1))
         flow_frame = {"value": world * B * k / (fms / 1e3), "unit": "frames/s", "frames": k,
                       "ms_per_frame": fms / k, "ms_head_per_frame": fms / k - ms / args.steps,
                       "head": "flow_dim 512, depth 6, ldim 32, LSD 1 step (phonon shape), bf16 weights, "
                               "latent fed back each frame"}
         flow.close()
+    kv.check()
+    del kv
+
+    # ---- config 3 through the attention op: the north star's decode-attention figure ------------
+    decode_attn = None
+    if args.workload == "config5" and not args.no_config3 and rank == 0 and world == 1:
+        decode_attn = config3_attention(ptts, 200, args.warmup, local)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline and args.workload == "config5" and not args.layers:
-        cb = cpu_baseline(ptts, wl, cfg, weights)
+        cb = cpu_baseline(ptts, wl, cfg, weights, warmup=t0 - w0 if not cycling else args.warmup, start=w0)
         cpu = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
 
     if rank == 0:
@@ -479,35 +590,39 @@ def run_ours(args):
                        "streams_per_gpu": B, "total_streams": world * B, "layers": L,
                        "kv_capacity": cap, "parallelism": f"stream-sharded x{world}, no collectives",
                        "lanes": lanes,
+                       "timed_frames": "whole window, cycled from frame 0" if cycling else [t0, t0 + args.steps],
+                       "repeats": len(jobs),
                        "l2": f"inputs larger than L2: {kv_bytes_per_step / 1e9:.2f} GB of KV read per step per GPU"
                              if kv_bytes_per_step > 126e6 else "KV per step fits in L2 (no flush)"},
+            "ms_per_step_spread": {k: v / args.steps for k, v in spread(jobs).items()},
+            "ms_per_step_per_rank": {**spread(per_rank), "ranks": per_rank},
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": gpu_launches,
+            "gpu_launches_per_step": launches_per_step,
             "clocks": clocks, "prefill_ms": prefill_ms, "frame_with_flow_head": flow_frame,
             "prefill_rows_per_s": world * float(prefixes.sum()) / (prefill_ms / 1e3),
+            "decode_attn": decode_attn,
         }
         print(json.dumps(line), flush=True)
-    kv.check()
-    del kv
     if dist is not None:
-        barrier(dist, local)
+        barrier(dist)
         dist.destroy_process_group()
 
 
-def run_config3(args):
-    """Config 3 (seed 2): the attention op alone over 256 ragged streams (prefilled lengths
-    U{64..2048}, bf16 cache), one query per stream per step: RoPE + append + split-KV attention.
-    Steps cycle a 100-step window. value = algorithmic GB/s of the op (bytes per step: K and V
-    rows of every attended position + per stream 1 KB q, 2 KB appended k/v, 1 KB output)."""
+def config3_attention(ptts, steps: int, warmup: int, device: int) -> dict:
+    """Config 3 (seed 2) through the attention op, for the bench line's `decode_attn` object:
+    256 ragged streams (prefilled lengths U{64..2048}, bf16 cache), one query per stream per
+    step (RoPE + append + split-KV attention, then kv_advance), `steps` steps cycling the 100-step
+    window. Reports the op's algorithmic GB/s (CUDA events around all steps), the decode
+    kernel's own GB/s and fraction of the HBM peak (CUDA events around each launch, a traced
+    pass over the same steps) and the clocks sampled meanwhile."""
     import numpy as np
     import torch
 
-    ptts, wl = load()
-    torch.cuda.set_device(0)
-    dev = torch.device("cuda:0")
+    dev = torch.device(f"cuda:{device}")
     B, window = 256, 100
     lengths = torch.randint(64, 2049, (B,), generator=torch.Generator().manual_seed(2)).numpy().astype(np.int32)
     cap = int(lengths.max()) + window
-    kv = ptts.KvState(1, B, cap, dtype="bf16")
+    kv = ptts.KvState(1, B, cap, dtype="bf16", device=device)
     g = torch.Generator(device=dev).manual_seed(2)
     kt, vt, _ = kv.tensors(0)
     kt.normal_(generator=g)
@@ -533,45 +648,64 @@ def run_config3(args):
         state["s"] = s + 1
 
     junk = []
-    sampler = ClockSampler(0)
+    sampler = ClockSampler(device)
     sampler.start()
     time.sleep(0.5)
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         step(junk)
+    kv.set_lengths(streams, lengths)
+    state["s"] = 0
     torch.cuda.synchronize()
     acc = []
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
-    for _ in range(args.steps):
+    for _ in range(steps):
         step(acc)
     e1.record()
     e1.synchronize()
     clocks = sampler.stop()
     ms = e0.elapsed_time(e1)
-    gbs = sum(acc) / (ms / 1e3) / 1e9
     kv.set_lengths(streams, lengths)
     state["s"] = 0
     ptts.set_tracing(True)
     ptts.trace(reset=True)
-    for _ in range(min(args.steps, window)):
+    for _ in range(steps):
         step(junk)
     tr = ptts.trace(reset=True)
     ptts.set_tracing(False)
+    kv.check()
+    kv.close()
     peak, kind = peaks()
     per_bytes = tr["attn_bytes"] / max(tr["attn_launches"], 1)
     per_ms = tr["attn_ms"] / max(tr["attn_launches"], 1)
     achieved = per_bytes / (per_ms / 1e3) / 1e9
+    return {"workload": "config3: 256 ragged streams, lengths U{64..2048} (seed 2), bf16 KV, one query "
+                        "per stream per step, 100-step window",
+            "steps": steps, "op_gbs": sum(acc) / (ms / 1e3) / 1e9, "op_ms_per_step": ms / steps,
+            "kernel": "decode_attn_kernel<bf16> (split-KV, wide ring)", "achieved": achieved,
+            "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+            "peak_kind": f"{kind} (MEASURED_PEAKS.json hbm_gbs)" if kind == "measured" else "fallback 6.65 TB/s",
+            "launch_ms": per_ms, "algorithmic_bytes_per_launch": per_bytes,
+            "launches_timed": tr["attn_launches"], "clocks": clocks}
+
+
+def run_config3(args):
+    """--workload config3: the attention op alone over config 3 (see config3_attention), K steps
+    after W warm-up steps; value = the op's algorithmic GB/s."""
+    import torch
+    ptts, _ = load()
+    torch.cuda.set_device(0)
+    d = config3_attention(ptts, args.steps, args.warmup, 0)
     print(json.dumps({
         "metric": "decode attn GB/s (config 3: 256 ragged streams, L0 U{64..2048}, bf16 KV)",
-        "value": gbs, "unit": "GB/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": ms / args.steps, "higher_is_better": True, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": "config3", "streams": B, "window": window},
-        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                     "frac": achieved / peak, "peak_kind": kind, "launch_ms": per_ms,
-                     "algorithmic_bytes_per_launch": per_bytes,
-                     "kernel": "decode_attn_kernel<bf16> + combine"},
-        "clocks": clocks}), flush=True)
-    kv.check()
+        "value": d["op_gbs"], "unit": "GB/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": d["op_ms_per_step"], "higher_is_better": True, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "config3", "streams": 256, "window": 100},
+        "roofline": {"bound": "hbm", "achieved": d["achieved"], "peak": d["peak"], "unit": "GB/s",
+                     "frac": d["frac"], "peak_kind": d["peak_kind"], "launch_ms": d["launch_ms"],
+                     "algorithmic_bytes_per_launch": d["algorithmic_bytes_per_launch"],
+                     "kernel": d["kernel"]},
+        "clocks": d["clocks"]}), flush=True)
 
 
 def run_config2(args):
@@ -627,8 +761,13 @@ def run_config2(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=1000)
+    ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--repeats", type=int, default=0,
+                    help="timed regions of K frames from the same centred start (0: at least 15 and "
+                         "at least 1 s of timed work); K >= 250 frames are timed once")
+    ap.add_argument("--no-config3", action="store_true",
+                    help="skip the decode_attn object (config 3 through the attention op)")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--timeline", default="",

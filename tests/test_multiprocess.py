@@ -31,13 +31,14 @@ def _worker(rank, world, port, mode, q):
             got = [torch.zeros_like(mine) for _ in range(world)]
             dist.all_gather(got, mine)
             bench.barrier(dist)
-            slowest = bench.max_over_ranks(dist, 10.0 + rank, "cpu")
-            q.put((rank, sorted(torch.cat(got).tolist()), slowest))
+            slowest = bench.max_over_ranks(dist, 10.0 + rank)
+            each = bench.gather_over_ranks(dist, 10.0 + rank)
+            q.put((rank, sorted(torch.cat(got).tolist()), slowest, each))
         elif mode == "dead_peer":
             if rank == 1:
                 os._exit(0)  # leaves between steps, nothing in flight
             try:
-                bench.max_over_ranks(dist, 1.0, "cpu")
+                bench.max_over_ranks(dist, 1.0)
                 q.put((rank, "no error"))
             except Exception as e:  # the collective ends with an error instead of hanging
                 q.put((rank, type(e).__name__))
@@ -68,14 +69,30 @@ def _run(mode, world=2, timeout=60):
 def test_ranks_own_disjoint_contiguous_shards_and_time_is_the_slowest_rank():
     res = _run("shards")
     assert len(res) == 2
-    for rank, all_ids, slowest in res:
+    for rank, all_ids, slowest, each in res:
         assert all_ids == list(range(2 * 512))
         assert slowest == 11.0
+        assert each == [10.0, 11.0]
 
 
 def test_a_rank_that_leaves_does_not_hang_its_peer():
     res = _run("dead_peer")
     assert [r for r in res if r[0] == 0][0][1] != "no error"
+
+
+def test_timed_frames_sit_in_the_middle_of_the_window():
+    """K < 250 timed frames are centred in config 5's 250-frame window (the window's average KV
+    read), with the warm-up frames just before them; K >= 250 cycle the window from frame 0."""
+    import sys
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    import bench
+    assert bench.timing_window(20, 5) == (110, 115)
+    w0, t0 = bench.timing_window(20, 5)
+    assert t0 + 20 / 2 == bench.FRAMES / 2
+    assert bench.timing_window(248, 5) == (0, 1)
+    assert bench.timing_window(250, 5) == (0, 5)
+    assert bench.timing_window(1000, 3) == (0, 3)
+    assert bench.spread([3.0, 1.0, 2.0]) == {"min": 1.0, "median": 2.0, "max": 3.0}
 
 
 def test_more_ranks_than_streams_is_refused():
