@@ -54,6 +54,19 @@ def cuda(ptts):
     return torch.device("cuda:0")
 
 
+def elementwise(got: np.ndarray, want: np.ndarray, floor: float = 1e-2) -> float:
+    """max_i |got_i - want_i| / max(|want_i|, floor * ||want||_inf): the element-wise relative
+    error, with an absolute floor at `floor` of the largest magnitude (elements near zero are
+    measured against the floor, not against themselves). Reported beside the normwise gate:
+    after a bf16 store (unit roundoff 2^-8) no element-wise bound below 2e-3 can hold without
+    such a floor."""
+    got = np.asarray(got, np.float64)
+    want = np.asarray(want, np.float64)
+    top = np.abs(want).max()
+    den = np.maximum(np.abs(want), floor * (top if top > 0 else 1.0))
+    return float((np.abs(got - want) / den).max())
+
+
 def normwise(got: np.ndarray, want: np.ndarray) -> float:
     """||got - want||_inf / ||want||_inf, the parity metric of every test here."""
     got = np.asarray(got, np.float64)

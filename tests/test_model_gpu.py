@@ -11,7 +11,7 @@ from __future__ import annotations
 import numpy as np
 import pytest
 
-from conftest import normwise
+from conftest import elementwise, normwise
 
 pytestmark = pytest.mark.gpu
 TOL = 2e-3
@@ -33,9 +33,49 @@ def _setup(ptts, oracle, cfg, seed, S, cap, cuda):
 
 def _report(name, got, want):
     rowerr = np.abs(got - want).max(1) / np.abs(want).max()
-    print(f"{name}: normwise {normwise(got, want):.3e}, median row {np.median(rowerr):.2e}, "
+    print(f"{name}: normwise {normwise(got, want):.3e}, element-wise (floor 1e-2) "
+          f"{elementwise(got, want):.2e}, median row {np.median(rowerr):.2e}, "
           f"rows > 1e-3: {(rowerr > 1e-3).sum()}/{len(rowerr)}")
     return normwise(got, want)
+
+
+def _check_frames(name, errs, elem):
+    """Every frame under TOL; prints the worst frame and its index."""
+    worst = int(np.argmax(errs))
+    print(f"{name}: {len(errs)} frames, worst normwise {errs[worst]:.2e} at frame {worst}, "
+          f"median {np.median(errs):.2e}, worst element-wise (floor 1e-2) {max(elem):.2e}")
+    for i, e in enumerate(errs):
+        assert e < TOL, (name, i, e)
+
+
+# Bound on the free-running drift (the oracle and the GPU each evolving their own cache over
+# hundreds of frames). A one-ulp change of the inputs moves the oracle from itself by 1.7e-3
+# over config 4's 250 frames: every bf16 rounding of a cached k or v element that flips goes on
+# steering later frames. The per-frame gate (TOL) applies to frames run from the same cache.
+DRIFT_TOL = 1e-2
+# Appended cache rows, GPU against oracle (same inputs, each side's arithmetic rounded to bf16).
+ROW_TOL = 2 ** -5
+
+
+def _sync_rows(kv, kc, vc, gpu_streams, oracle_streams, first, count):
+    """Copy the GPU cache's rows first[i] .. first[i] + count[i] - 1 of stream gpu_streams[i]
+    into the oracle's caches kc/vc [layer][stream][slot][8][64] (stream oracle_streams[i]), so
+    the next frame of both sides starts from the same cache. Returns the largest difference
+    between the replaced oracle rows and the GPU's, relative to the largest entry of the row
+    block: the rows hold the same arithmetic rounded to bf16, so they agree to a few bf16
+    roundings (2^-8 each); a row at a wrong slot would differ by O(1)."""
+    worst = 0.0
+    for l in range(kc.shape[0]):
+        kt, vt, _ = kv.tensors(l)
+        for g, o, a, n in zip(gpu_streams, oracle_streams, first, count):
+            gk = _f32(kt[int(g), int(a):int(a) + int(n)])
+            gv = _f32(vt[int(g), int(a):int(a) + int(n)])
+            ok, ov = kc[l, o, a:a + n], vc[l, o, a:a + n]
+            den = max(np.abs(ok).max(), 1e-30)
+            worst = max(worst, float(np.abs(gk - ok).max() / den), float(np.abs(gv - ov).max() / den))
+            kc[l, o, a:a + n] = gk
+            vc[l, o, a:a + n] = gv
+    return worst
 
 
 def test_prefill_then_decode_matches_the_oracle(ptts, oracle, cuda):
@@ -112,11 +152,14 @@ def test_a_device_step_is_the_host_step(ptts, cuda):
 
 
 def test_config4_decode_frames(ptts, oracle, cuda):
-    """Config 4 (seed 3) shortened to 12 frames: 31m shape, 64 streams, prefix 128, per-frame
-    hidden states of the device step against the oracle."""
+    """Config 4 (seed 3) at full length: 31m shape, 64 streams, prefix 128, all 250 frames.
+    Every frame's hidden states from the device step are checked against the oracle run on the
+    same cache (after the prefill and after each frame the GPU's appended rows replace the
+    oracle's, whose own rows must agree with them to one bf16 rounding); a second oracle runs
+    free from the prompt on, and its drift from the GPU is reported and bounded."""
     import torch
     cfg = ptts.PHONON_31M
-    B, prefix, frames = 64, 128, 12
+    B, prefix, frames = 64, 128, 250
     model, om, kv, kc, vc = _setup(ptts, oracle, cfg, 3, B, prefix + frames, cuda)
     g = torch.Generator().manual_seed(3)
     x = torch.randn(B * prefix, 512, generator=g).bfloat16()
@@ -125,17 +168,28 @@ def test_config4_decode_frames(ptts, oracle, cuda):
     model.forward(kv, x.to(cuda), streams, [prefix] * B)
     lengths = np.zeros(B, np.int32)
     om.forward(_f32(x), kc, vc, lengths, streams, offs, store=oracle.ROUND_KV)
+    fkc, fvc = kc.copy(), vc.copy()
+    rows_dev = _sync_rows(kv, kc, vc, streams, streams, lengths, np.full(B, prefix))
     lengths += prefix
-    errs = []
+    errs, elem, drift = [], [], []
+    one = np.arange(B + 1, dtype=np.int32)
     for f in range(frames):
         xs = torch.randn(B, 512, generator=g).bfloat16()
-        y = model.step(kv, streams, xs.to(cuda))
-        want = om.forward(_f32(xs), kc, vc, lengths, streams, np.arange(B + 1, dtype=np.int32), store=oracle.ROUND_KV)
+        y = _f32(model.step(kv, streams, xs.to(cuda)))
+        want = om.forward(_f32(xs), kc, vc, lengths, streams, one, store=oracle.ROUND_KV)
+        free = om.forward(_f32(xs), fkc, fvc, lengths, streams, one, store=oracle.ROUND_KV)
+        rows_dev = max(rows_dev, _sync_rows(kv, kc, vc, streams, streams, lengths, np.ones(B, np.int32)))
         lengths += 1
-        errs.append(normwise(_f32(y), want))
+        errs.append(normwise(y, want))
+        elem.append(elementwise(y, want))
+        drift.append(normwise(y, free))
     kv.check()
-    print("config4 per-frame normwise:", ["%.2e" % e for e in errs])
-    assert max(errs) < TOL
+    np.testing.assert_array_equal(kv.lengths(), lengths)
+    print(f"config4: appended cache rows vs the oracle's: {rows_dev:.2e}; free-running drift: worst "
+          f"{max(drift):.2e} at frame {int(np.argmax(drift))}, median {np.median(drift):.2e}")
+    _check_frames("config4 (same cache)", errs, elem)
+    assert rows_dev < ROW_TOL
+    assert max(drift) < DRIFT_TOL
 
 
 def test_two_lane_steps_match_the_oracle(ptts, oracle, cuda):
@@ -233,18 +287,19 @@ def test_long_prompts_match_the_oracle(ptts, oracle, cuda):
 
 
 def test_full_config5_shard_on_sampled_streams(ptts, oracle, cuda):
-    """The benchmark's whole per-GPU workload: the 40m stack (9 layers), 512 streams with
-    prompts of U{32..512} rows (seed 4, 139k rows in one prefill: the persistent prompt
-    linears and the tcgen05 prefill attention), then decode steps of all 512 streams (two
-    lanes, compact-ring attention). Streams never interact, so the oracle runs only a sample of
-    them, on their own prompts and inputs, and every sampled stream's rows are compared."""
+    """The benchmark's whole per-GPU workload at full length: the 40m stack (9 layers), 512
+    streams with prompts of U{32..512} rows (seed 4, 139k rows in one prefill: the persistent
+    prompt linears and the tcgen05 prefill attention), then all 250 decode frames of all 512
+    streams (two lanes, compact-ring attention; KV lengths up to prefix + 249). Streams never
+    interact, so the oracle runs only a sample of them, on their own prompts and inputs, and
+    every sampled stream's rows are compared, frame by frame."""
     import importlib
     import torch
     wl = importlib.import_module("xn_ptts_b200.workloads")
     cfg = ptts.PHONON_40M
-    B = 512
+    B, frames = 512, 250
     prefixes = np.asarray(wl.prefix_lengths(4096, 32, 512, 4)[:B], np.int32)
-    cap = int(prefixes.max()) + 4
+    cap = int(prefixes.max()) + frames
     w = ptts.random_weights(cfg, 4)
     model = ptts.Transformer(cfg)
     model.load(w)
@@ -254,10 +309,6 @@ def test_full_config5_shard_on_sampled_streams(ptts, oracle, cuda):
     x = torch.randn(int(offs[-1]), 512, generator=g).bfloat16()
     y = model.forward(kv, x.to(cuda), list(range(B)), prefixes.tolist())
     y = _f32(y)
-    steps = [torch.randn(B, 512, generator=g).bfloat16() for _ in range(3)]
-    ys = [_f32(model.step(kv, list(range(B)), xs.to(cuda))) for xs in steps]
-    kv.check()
-    np.testing.assert_array_equal(kv.lengths(), prefixes + len(steps))
 
     sample = np.random.default_rng(4).choice(B, size=8, replace=False)
     sample.sort()
@@ -272,14 +323,67 @@ def test_full_config5_shard_on_sampled_streams(ptts, oracle, cuda):
     local = list(range(len(sample)))
     want = om.forward(xin, kc, vc, lengths, local, o_offs, store=oracle.ROUND_KV)
     got = np.concatenate([y[offs[b]:offs[b + 1]] for b in sample])
-    errs = [_report("config-5 prefill (sampled streams)", got, want)]
+    assert _report("config-5 prefill (sampled streams)", got, want) < TOL
+    rows_dev = _sync_rows(kv, kc, vc, sample, local, lengths, rows)
     lengths += rows
-    for i, xs in enumerate(steps):
-        want = om.forward(_f32(xs)[sample], kc, vc, lengths, local,
-                          np.arange(len(sample) + 1, dtype=np.int32), store=oracle.ROUND_KV)
+    errs, elem = [], []
+    one = np.arange(len(sample) + 1, dtype=np.int32)
+    for f in range(frames):
+        xs = torch.randn(B, 512, generator=g).bfloat16()
+        ys = _f32(model.step(kv, list(range(B)), xs.to(cuda)))[sample]
+        want = om.forward(_f32(xs)[sample], kc, vc, lengths, local, one, store=oracle.ROUND_KV)
+        rows_dev = max(rows_dev, _sync_rows(kv, kc, vc, sample, local, lengths, np.ones(len(sample), np.int32)))
         lengths += 1
-        errs.append(_report(f"config-5 step {i}", ys[i][sample], want))
-    assert max(errs) < TOL
+        errs.append(normwise(ys, want))
+        elem.append(elementwise(ys, want))
+    kv.check()
+    np.testing.assert_array_equal(kv.lengths(), prefixes + frames)
+    print(f"config-5: appended cache rows vs the oracle's: {rows_dev:.2e}")
+    _check_frames("config-5 decode (sampled streams, same cache)", errs, elem)
+    assert rows_dev < ROW_TOL
+
+
+def test_one_layer_at_layer_norm_gain_one(ptts, oracle, cuda):
+    """One layer with the LayerNorm gain at 1 (the 1/16 of the other synthetic stacks keeps
+    attention logits at a trained model's scale over many layers; a single layer has no depth
+    for rounding differences to grow through). Ragged prompts, then 20 device steps, each from
+    the same cache on both sides. Logits are ~430 wide here (near-argmax attention), so one
+    bf16 rounding flip of a cached key moves a near-tied query by O(1): the oracle's own bf16
+    and f32 modes differ by 3-15 % per step."""
+    import torch
+    cfg = ptts.FlowLMConfig(num_layers=1)
+    S, cap = 16, 160
+    w = ptts.random_weights(cfg, 71, ln_gain=1.0)
+    model = ptts.Transformer(cfg)
+    model.load(w)
+    om = oracle.Model(cfg, w)
+    kv = ptts.KvState(1, S, cap, dtype="bf16")
+    kc = np.zeros((1, S, cap, 8, 64), np.float32)
+    vc = np.zeros_like(kc)
+    rng = np.random.default_rng(71)
+    rows = rng.integers(1, 120, size=S).astype(np.int32)
+    offs = np.concatenate([[0], np.cumsum(rows)]).astype(np.int32)
+    g = torch.Generator().manual_seed(71)
+    x = torch.randn(int(offs[-1]), 512, generator=g).bfloat16()
+    streams = list(range(S))
+    y = _f32(model.forward(kv, x.to(cuda), streams, rows.tolist()))
+    lengths = np.zeros(S, np.int32)
+    want = om.forward(_f32(x), kc, vc, lengths, streams, offs, store=oracle.ROUND_KV)
+    errs = [_report("gain-1 layer prompt", y, want)]
+    elem = [elementwise(y, want)]
+    _sync_rows(kv, kc, vc, streams, streams, lengths, rows)
+    lengths += rows
+    for _ in range(20):
+        xs = torch.randn(S, 512, generator=g).bfloat16()
+        ys = _f32(model.step(kv, streams, xs.to(cuda)))
+        want = om.forward(_f32(xs), kc, vc, lengths, streams, np.arange(S + 1, dtype=np.int32),
+                          store=oracle.ROUND_KV)
+        _sync_rows(kv, kc, vc, streams, streams, lengths, np.ones(S, np.int32))
+        lengths += 1
+        errs.append(normwise(ys, want))
+        elem.append(elementwise(ys, want))
+    kv.check()
+    _check_frames("gain-1 layer (prompt, then steps from the same cache)", errs, elem)
 
 
 def test_grouped_query_attention_in_the_stack(ptts, oracle, cuda):
