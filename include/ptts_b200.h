@@ -48,6 +48,13 @@ extern "C" {
 #define PTTS_B200_ERR_UNSUPPORTED (-5) /* a shape or type these kernels do not implement */
 #define PTTS_B200_ERR_DEVICE (-6)      /* a kernel's own bounds check or bounded wait tripped */
 
+/* Bits of the device-side error word (ptts_b200_kv_check reads the kv's own word;
+ * ptts_b200_attend_decode_noalloc ORs them into the caller's). */
+#define PTTS_B200_DEVERR_BOUNDS 1u    /* a stream index outside the cache's streams */
+#define PTTS_B200_DEVERR_CAPACITY 2u  /* a row's position outside its stream's slots */
+#define PTTS_B200_DEVERR_TIMEOUT 4u   /* a bounded wait inside a kernel gave up */
+#define PTTS_B200_DEVERR_DUPLICATE 8u /* a stream named by two rows of one decode call */
+
 /* Element types of caches, inputs and outputs. */
 #define PTTS_B200_F32 0
 #define PTTS_B200_BF16 1
@@ -290,15 +297,24 @@ int ptts_b200_step(ptts_b200_model* model, ptts_b200_kv* kv, const int32_t* stre
  * k_cache/v_cache [num_streams][capacity][8][64] (one layer, kv_dtype), lengths [num_streams]
  * (device, read and NOT advanced), streams [n] (device), q [n][8][64], k and v [n][KVH][64]
  * (in_dtype), out [n][512] (out_dtype). Row i is rotated at position lengths[streams[i]], its k
- * and v are written to that slot, and it attends to keys 0..=that position. Kernels that find a
- * position past `capacity` skip it and set bits in *err (device word, may be NULL).
+ * and v are written to that slot, and it attends to keys 0..=that position.
+ *
+ * The stream list lives on the device, so the host cannot check it: the kernels do. A row is
+ * refused when streams[i] is outside 0..num_streams-1 (err bit PTTS_B200_DEVERR_BOUNDS), when an
+ * earlier row names the same stream (PTTS_B200_DEVERR_DUPLICATE; the first row of that stream
+ * proceeds), or when its position lengths[streams[i]] is negative or not below `capacity`
+ * (PTTS_B200_DEVERR_CAPACITY). A refused row writes no cache row, reads nothing, and its row of
+ * `out` is set to zeros. The bits are ORed into *err (a device word the caller clears; may be
+ * NULL, in which case a refused row is visible only as its zero output row).
  *
  * Working memory comes from one fixed array in the library (about 4.6 MB per GPU, held until
  * the process exits); n above 1024 is refused with PTTS_B200_ERR_ARG. Every call on a device
  * shares that array, so two calls whose kernels overlap on the GPU (different streams, no
  * ordering between them) race and both results are undefined; order them on one stream. The
  * first call on a device looks the array's address up (cudaGetSymbolAddress) with that device
- * current; make that first call before any stream capture. No call allocates or frees memory.
+ * current; make that first call before any stream capture. The address is kept for the rest of
+ * the process: do not call this on a device after cudaDeviceReset of that device. No call
+ * allocates or frees memory.
  * ------------------------------------------------------------------------------------- */
 int ptts_b200_attend_decode_noalloc(void* k_cache, void* v_cache, int num_streams, int capacity,
                                     int kv_dtype, const int32_t* lengths, const int32_t* streams,

@@ -30,6 +30,8 @@ LIB_PATH = os.path.join(HERE, "libptts_b200.so")
 OK = 0
 ERR_ARG, ERR_CAPACITY, ERR_CUDA, ERR_STATE, ERR_UNSUPPORTED, ERR_DEVICE = -1, -2, -3, -4, -5, -6
 F32, BF16 = 0, 1
+# Bits of a device-side error word (PTTS_B200_DEVERR_*).
+DEVERR_BOUNDS, DEVERR_CAPACITY, DEVERR_TIMEOUT, DEVERR_DUPLICATE = 1, 2, 4, 8
 _DTYPES = {"f32": F32, "float32": F32, "bf16": BF16, "bfloat16": BF16}
 
 # Every symbol include/ptts_b200.h declares.

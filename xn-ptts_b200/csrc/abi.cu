@@ -1106,6 +1106,7 @@ int ptts_b200_kv_check(ptts_b200_kv* kv) {
             if (e & DEV_ERR_BOUNDS) what += " bounds";
             if (e & DEV_ERR_CAPACITY) what += " capacity";
             if (e & DEV_ERR_TIMEOUT) what += " timeout";
+            if (e & DEV_ERR_DUPLICATE) what += " duplicate";
             fail(PTTS_B200_ERR_DEVICE, "device-side check tripped:" + what);
         }
     });

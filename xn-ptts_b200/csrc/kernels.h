@@ -8,6 +8,8 @@
 
 #include <utility>
 
+#include "ptts_b200.h"
+
 namespace ptts {
 
 // Bits of the device-side error word. Kernels set these and return instead of trapping.
@@ -15,7 +17,11 @@ enum : uint32_t {
     DEV_ERR_BOUNDS = 1u,    // an index or position fell outside its buffer
     DEV_ERR_CAPACITY = 2u,  // a stream's rows did not fit its capacity
     DEV_ERR_TIMEOUT = 4u,   // a bounded mbarrier wait gave up
+    DEV_ERR_DUPLICATE = 8u, // a stream appeared twice among one decode call's rows
 };
+static_assert(DEV_ERR_BOUNDS == PTTS_B200_DEVERR_BOUNDS && DEV_ERR_CAPACITY == PTTS_B200_DEVERR_CAPACITY &&
+                  DEV_ERR_TIMEOUT == PTTS_B200_DEVERR_TIMEOUT && DEV_ERR_DUPLICATE == PTTS_B200_DEVERR_DUPLICATE,
+              "device error bits match the C header");
 
 
 // Launch with programmatic stream serialisation (PTTS_B200_PDL=0 turns it off): the kernel may
@@ -82,13 +88,24 @@ struct RingArgs {
 // slot row_pos[i] and attends keys 0..row_pos[i]; a ring stream writes at its write slot w and
 // attends slots 0..max(filled, w + 1) - 1 (the invisible ones masked by the decode kernel); a
 // windowed stream writes at row_pos[i] % capacity and attends its last min(pos + 1, context)
-// positions. prefix[i+1] = sum of attended keys, clamped to capacity. Sets DEV_ERR_CAPACITY /
-// DEV_ERR_BOUNDS.
+// positions. prefix[i+1] = sum of attended keys.
 // With plan.cta_first set, also cta_first[c] = the stream in which CTA c of a `grid`-CTA decode
 // launch starts (the split-KV partition of the prefix sums), so no CTA searches for it.
+//
+// A row is refused when its stream index is out of range (DEV_ERR_BOUNDS), when, with
+// PlanChecks::unique, an earlier row of the call names the same stream (DEV_ERR_DUPLICATE), or
+// when its position does not fit the stream's slots (DEV_ERR_CAPACITY). A refused row attends
+// no keys and writes no cache row (row_stream 0, row_pos and row_slot -1: the RoPE/append
+// kernels and the QKV epilogues skip it), and with PlanChecks::zero_out its output row is
+// written as zeros (no other kernel writes it).
+struct PlanChecks {
+    int unique = 0;            // check rows for repeated streams (n <= 1024 only)
+    void* zero_out = nullptr;  // [n] rows of zero_row_bytes (a multiple of 4), or nullptr
+    int zero_row_bytes = 0;
+};
 void launch_plan_decode(const int32_t* lengths, const int32_t* streams, int n, int num_streams,
                         int capacity, RowPlan plan, const RingArgs& ring, int grid, uint32_t* err,
-                        cudaStream_t s);
+                        cudaStream_t s, const PlanChecks& checks = PlanChecks{});
 
 // Ragged plan: sequence i (stream seq_stream[i]) owns rows row_offsets[i]..row_offsets[i+1];
 // row r of it sits at lengths[stream] + (r - row_offsets[i]).

@@ -12,12 +12,20 @@ namespace {
 
 constexpr int kPlanThreads = 1024;
 
+// Open-addressing table of the repeated-stream check: keys, then the lowest row per key (dynamic
+// shared memory, only in launches that ask for the check).
+constexpr int kDupSlots = 2 * kPlanThreads;
+constexpr int kDupSmemBytes = 2 * kDupSlots * (int)sizeof(int);
+
 // One CTA: a running block scan over the sequences, 1024 at a time.
 __global__ void __launch_bounds__(kPlanThreads) plan_decode_kernel(
     const int32_t* __restrict__ lengths, const int32_t* __restrict__ streams, int n,
-    int num_streams, int capacity, RowPlan plan, RingArgs ring, int grid, uint32_t* err) {
+    int num_streams, int capacity, RowPlan plan, RingArgs ring, int grid, uint32_t* err,
+    PlanChecks chk) {
     __shared__ int warp_tot[kPlanThreads / 32];
     __shared__ int carry;
+    extern __shared__ int dup_key[];
+    int* dup_first = dup_key + kDupSlots;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     grid_dep_wait();
     grid_dep_launch();
@@ -25,36 +33,84 @@ __global__ void __launch_bounds__(kPlanThreads) plan_decode_kernel(
         carry = 0;
         plan.prefix[0] = 0;
     }
+    // Repeated streams (n <= kPlanThreads): every row's stream goes into an open-addressing
+    // table that keeps the lowest row index per stream; a row whose index is not the lowest
+    // repeats an earlier row's stream. Probing ends within kDupSlots steps (at most n < kDupSlots
+    // keys are ever inserted, so a free slot or the row's own key is always found).
+    const bool unique = chk.unique && n <= kPlanThreads;
+    int dup_slot = -1;
+    if (unique) {
+        for (int t = tid; t < kDupSlots; t += kPlanThreads) {
+            dup_key[t] = -1;
+            dup_first[t] = 0x7fffffff;
+        }
+        __syncthreads();
+        if (tid < n) {
+            const int sid = streams[tid];
+            if (sid >= 0 && sid < num_streams) {
+                int h = (int)(((unsigned)sid * 2654435761u) % (unsigned)kDupSlots);
+                for (int t = 0; t < kDupSlots; ++t) {
+                    const int prev = atomicCAS(&dup_key[h], -1, sid);
+                    if (prev == -1 || prev == sid) {
+                        atomicMin(&dup_first[h], tid);
+                        dup_slot = h;
+                        break;
+                    }
+                    h = h + 1 == kDupSlots ? 0 : h + 1;
+                }
+            }
+        }
+    }
     __syncthreads();
     for (int base = 0; base < n; base += kPlanThreads) {
         const int i = base + tid;
         int keys = 0;
         if (i < n) {
-            int sid = streams[i];
+            const int sid = streams[i];
+            bool refused = false;
             if (sid < 0 || sid >= num_streams) {
                 set_error(err, DEV_ERR_BOUNDS);
-                sid = 0;
+                refused = true;
+            } else if (unique && dup_slot >= 0 && dup_first[dup_slot] != i) {
+                set_error(err, DEV_ERR_DUPLICATE);
+                refused = true;
             }
-            const int len = lengths[sid];
-            if (len < 0) set_error(err, DEV_ERR_CAPACITY);
-            int slot = len;
-            // Clamped so that a refused row never makes a kernel read past the stream's slots.
-            keys = min(max(len, 0) + 1, capacity);
-            const int w = ring.write ? ring.write[sid] : -1;
-            const int ctx = ring.window ? ring.window[sid] : 0;
-            if (w >= 0) {
-                if (w >= capacity) set_error(err, DEV_ERR_CAPACITY);
-                slot = min(w, capacity - 1);
-                keys = min(max(ring.filled[sid], slot + 1), capacity);
-            } else if (ctx > 0) {  // the position grows past the capacity; slots wrap
-                slot = max(len, 0) % capacity;
-                keys = min(min(max(len, 0) + 1, ctx), capacity);
-            } else if (len < 0 || len + 1 > capacity) {
-                set_error(err, DEV_ERR_CAPACITY);
+            int len = 0, slot = 0;
+            if (!refused) {
+                len = lengths[sid];
+                slot = len;
+                keys = len + 1;
+                const int w = ring.write ? ring.write[sid] : -1;
+                const int ctx = ring.window ? ring.window[sid] : 0;
+                if (len < 0) {
+                    refused = true;
+                } else if (w >= 0) {
+                    if (w >= capacity) refused = true;
+                    slot = w;
+                    keys = min(max(ring.filled[sid], slot + 1), capacity);
+                } else if (ctx > 0) {  // the position grows past the capacity; slots wrap
+                    slot = len % capacity;
+                    keys = min(min(len + 1, ctx), capacity);
+                } else if (len + 1 > capacity) {
+                    refused = true;
+                }
+                if (refused) set_error(err, DEV_ERR_CAPACITY);
             }
-            plan.row_stream[i] = sid;
-            plan.row_pos[i] = len;
-            plan.row_slot[i] = slot;
+            if (refused) {
+                keys = 0;
+                plan.row_stream[i] = 0;
+                plan.row_pos[i] = -1;
+                plan.row_slot[i] = -1;
+                if (chk.zero_out) {  // 4-byte stores: the decode kernel's own output alignment
+                    uint32_t* o = reinterpret_cast<uint32_t*>(static_cast<unsigned char*>(chk.zero_out) +
+                                                              (long long)i * chk.zero_row_bytes);
+                    for (int t = 0; t < chk.zero_row_bytes / 4; ++t) o[t] = 0u;
+                }
+            } else {
+                plan.row_stream[i] = sid;
+                plan.row_pos[i] = len;
+                plan.row_slot[i] = slot;
+            }
         }
         int v = keys;
 #pragma unroll
@@ -213,9 +269,12 @@ __global__ void bf16_to_f32_kernel(const __nv_bfloat16* __restrict__ x, float* _
 
 void launch_plan_decode(const int32_t* lengths, const int32_t* streams, int n, int num_streams,
                         int capacity, RowPlan plan, const RingArgs& ring, int grid, uint32_t* err,
-                        cudaStream_t s) {
-    launch_k(plan_decode_kernel, dim3(1), dim3(kPlanThreads), 0, s, lengths, streams, n,
-             num_streams, capacity, plan, ring, grid < kMaxDecodeGrid ? grid : kMaxDecodeGrid, err);
+                        cudaStream_t s, const PlanChecks& checks) {
+    PlanChecks c = checks;
+    c.unique = c.unique && n <= kPlanThreads;
+    launch_k(plan_decode_kernel, dim3(1), dim3(kPlanThreads), c.unique ? kDupSmemBytes : 0, s, lengths,
+             streams, n, num_streams, capacity, plan, ring, grid < kMaxDecodeGrid ? grid : kMaxDecodeGrid,
+             err, c);
 }
 
 void launch_plan_rows(const int32_t* lengths, const int32_t* seq_stream, const int32_t* row_offsets,

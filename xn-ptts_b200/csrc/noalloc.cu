@@ -11,7 +11,14 @@
 // The array is a file-scope __device__ variable: every GPU that loads this library holds its own
 // copy, kNoAllocScratchBytes long, until the process exits. Host code cannot use the variable's
 // name as a device address, so the first call on each device looks the address up with
-// cudaGetSymbolAddress (with that device current) and keeps it.
+// cudaGetSymbolAddress (with that device current) and keeps it for the rest of the process. A
+// cudaDeviceReset destroys the context that address belongs to: the entry point must not be
+// called on a device after that device was reset.
+//
+// The stream list is device memory the host never reads, so the checks the allocating path makes
+// on the host run in the plan kernel here: a row whose stream index is out of range, that repeats
+// an earlier row's stream, or whose position does not fit the capacity is refused. It writes no
+// cache row, attends nothing, and its output row is written as zeros; a bit in *err says why.
 #include <mutex>
 #include <string>
 
@@ -116,7 +123,11 @@ extern "C" int ptts_b200_attend_decode_noalloc(void* k_cache, void* v_cache, int
     if (cudaMemsetAsync(counters, 0, sizeof(int) * decode_counter_ints(n), s) != cudaSuccess)
         return refuse(PTTS_B200_ERR_CUDA, "clearing the merge counters failed");
 
-    launch_plan_decode(lengths, streams, n, num_streams, capacity, plan, RingArgs{}, sc.grid, err, s);
+    PlanChecks checks;
+    checks.unique = 1;  // n <= 1024
+    checks.zero_out = out;
+    checks.zero_row_bytes = kRowWidth * (out_dtype == PTTS_B200_BF16 ? 2 : 4);
+    launch_plan_decode(lengths, streams, n, num_streams, capacity, plan, RingArgs{}, sc.grid, err, s, checks);
     RopeAppendArgs ra{};
     ra.q = q;
     ra.k = k;

@@ -26,6 +26,8 @@ __global__ void rope_append_kernel(RopeAppendArgs a) {
     const int row = (int)(idx / ((long long)pairs * slots));
     const int sid = a.row_stream[row];
     const int pos = a.row_pos[row], cslot = a.row_slot[row];  // RoPE position, cache slot
+    // A row the plan refused (its error bit is set already) writes nothing.
+    if (pos == -1 && cslot == -1) return;
     // A windowed stream's position runs past the capacity; its slot never does.
     if (sid < 0 || sid >= a.num_streams || pos < 0 || cslot < 0 || cslot >= a.capacity) {
         set_error(a.err, DEV_ERR_CAPACITY);
