@@ -206,7 +206,9 @@ int ptts_b200_attend(ptts_b200_kv* kv, int layer, const void* q, const void* k, 
  * Quantised linear: Q::LinearQ::forward (transformer.rs:195, :224, :627) for int8 weights with
  * one f32 scale per output row. y[m][n] = scale[n] * sum_k x[m][k] * w[n][k].
  * x [m][k] bf16, w [n][k] int8, scale [n] f32, y [m][n] f32; all device pointers.
- * k and n must be multiples of 64.
+ * k and n must be multiples of 64. With n a multiple of 128 it runs on the tcgen05 tensor cores
+ * (the int8 weights widened to bf16 in shared memory, exactly; the scale applied to the f32
+ * accumulator); other n on the mma.sync kernel.
  * ------------------------------------------------------------------------------------- */
 int ptts_b200_linear_i8(int device, const void* x, const int8_t* w, const float* scale, int m,
                         int n, int k, float* y, void* cuda_stream);

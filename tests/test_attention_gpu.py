@@ -321,7 +321,9 @@ def test_with_seq_budget_known_answers(ptts, cuda):
 def test_linear_i8_matches_the_oracle(ptts, oracle, cuda):
     import torch
     rng = np.random.default_rng(7)
-    for m, n, k in ((1, 64, 64), (100, 1536, 512), (64, 512, 2048), (129, 2048, 512)):
+    # n a multiple of 128: tcgen05 with the int8 weights widened to bf16 on chip (one CTA per
+    # tile up to 4095 rows, the persistent kernel from 4096); n = 64: the mma.sync kernel.
+    for m, n, k in ((1, 64, 64), (100, 1536, 512), (64, 512, 2048), (129, 2048, 512), (4100, 512, 512)):
         x = torch.from_numpy(rng.normal(size=(m, k)).astype(np.float32)).bfloat16()
         w = rng.integers(-127, 128, size=(n, k), dtype=np.int8)
         s = rng.uniform(0.005, 0.02, n).astype(np.float32)

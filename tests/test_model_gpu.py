@@ -258,6 +258,40 @@ def test_kernel_variants_match_the_oracle(ptts, oracle, cuda, monkeypatch, env):
     assert max(errs) < TOL
 
 
+def test_int8_weights_widened_on_chip_equal_the_f16_copy(ptts, cuda, monkeypatch):
+    """The tcgen05 linears read the int8 weights and widen them to f16 in shared memory; with
+    PTTS_B200_WEIGHTS=f16 they read an exact f16 copy made at load time instead. Both feed the
+    MMAs the same f16 values in the same order, so a prompt (the persistent prompt kernel, 4096+
+    rows, and the per-tile kernel) and decode steps (split-K partial epilogues, two lanes) give
+    bit-identical hidden states and caches."""
+    import torch
+    cfg = ptts.FlowLMConfig(num_layers=2)
+    w = ptts.random_weights(cfg, 81)
+    models = []
+    for form in ("i8", "f16"):
+        if form == "f16":
+            monkeypatch.setenv("PTTS_B200_WEIGHTS", "f16")
+        m = ptts.Transformer(cfg)
+        m.load(w)
+        models.append(m)
+    S = 160
+    rows = [30] * (S - 2) + [2100, 40]
+    g = torch.Generator().manual_seed(81)
+    x = torch.randn(sum(rows), 512, generator=g).bfloat16().to(cuda)
+    kvs = [ptts.KvState(cfg.num_layers, S, 2200, dtype="bf16") for _ in models]
+    ys = [m.forward(kv, x, list(range(S)), rows) for m, kv in zip(models, kvs)]
+    assert torch.equal(ys[0], ys[1])
+    for _ in range(3):
+        xs = torch.randn(S, 512, generator=g).bfloat16().to(cuda)
+        ys = [m.step(kv, list(range(S)), xs) for m, kv in zip(models, kvs)]
+        assert torch.equal(ys[0], ys[1])
+    for l in range(cfg.num_layers):
+        assert torch.equal(kvs[0].tensors(l)[0], kvs[1].tensors(l)[0])
+        assert torch.equal(kvs[0].tensors(l)[1], kvs[1].tensors(l)[1])
+    for kv in kvs:
+        kv.check()
+
+
 def test_long_prompts_match_the_oracle(ptts, oracle, cuda):
     """Prompts of 4096+ rows in one call (the linears' 64-row tcgen05 tiles, the tcgen05
     prefill attention over 1000+ keys), then a decode step."""

@@ -30,6 +30,10 @@ using namespace ptts::host;
 // Per-call activations of the layer stack (device, sized for `rows` rows).
 struct Workspace {
     DevBuf q_rot, h_hi, h_lo, attn_hi, attn_lo, ff_hi, ff_lo, split, part, counters;
+    // Prompts of kPersistMinRows+ rows: the current layer's int8 weights widened to f16 (the
+    // persistent linears reread every weight tile for each row tile; widening once per call
+    // beats widening every tile on chip). Four matrices, 256-byte aligned slices.
+    DevBuf wconv;
     void size(const ptts_b200_config& c, int rows) {
         const size_t r = (size_t)rows, hd = (size_t)c.num_heads * c.head_dim;
         q_rot.need(r * hd * 4);
@@ -48,6 +52,29 @@ int sm_count(int dev) {
     int n = 0;
     CK(cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev));
     return n;
+}
+
+// The decode attention's ring: the compact one for the lanes of a two-lane step (room for a
+// linear CTA beside it), else the wide one; PTTS_B200_RING=wide or =compact overrides both.
+bool decode_ring_compact(bool lane) {
+    static const int force = [] {
+        const char* e = getenv("PTTS_B200_RING");
+        return !e ? 0 : (e[0] == 'w' ? 1 : (e[0] == 'c' ? 2 : 0));
+    }();
+    return force == 0 ? lane : force == 2;
+}
+
+// CTAs of a split-KV decode launch: one per SM, or for the attention of a two-lane step (which
+// shares the SMs with the other lane's linears) PTTS_B200_LANE_CTAS if set (1..SMs). The plan
+// and the attention of one launch must use the same count.
+int decode_grid(int dev, bool lane) {
+    const int sms = sm_count(dev);
+    if (!lane) return sms;
+    static const int want = [] {
+        const char* e = getenv("PTTS_B200_LANE_CTAS");
+        return e ? atoi(e) : 0;
+    }();
+    return want >= 1 && want < sms ? want : sms;
 }
 
 void rope_inv_freq(int head_dim, float max_period, float* out) {
@@ -226,7 +253,9 @@ struct ptts_b200_model {
     float inv_freq[kMaxPairs];
     struct Layer {
         DevBuf w_qkv, s_qkv, w_out, s_out, w1, s1, w2, s2, ln1g, ln1b, ln2g, ln2b;
-        DevBuf h_qkv, h_out, h1, h2;  // the int8 weights as f16 (exact), read by the tcgen05 linears
+        // int8 layers: empty (the tcgen05 linears widen the int8 weights on chip), or with
+        // PTTS_B200_WEIGHTS=f16 an exact f16 copy of them that those linears read instead.
+        DevBuf h_qkv, h_out, h1, h2;
         // Layers loaded from f32 or q8_0 weights have no int8 copy: h_* hold f16(W / s_row) and
         // l_* the f16 remainders, s_row a power of two per output row (in s_*).
         DevBuf l_qkv, l_out, l1, l2;
@@ -391,7 +420,7 @@ void attention(const ptts_b200_kv* kv, int layer, bool decode, const RowPlan& pl
     const bool bf16 = kv->dtype == PTTS_B200_BF16;
     const float qscale = (1.0f / sqrtf((float)kv->head_dim)) * kLog2e;  // transformer.rs:215
     if (decode) {
-        const int grid = sm_count(kv->device);
+        const int grid = decode_grid(kv->device, compact);
         DecodeArgs a{};
         a.k_cache = kv->k_layer(layer);
         a.v_cache = kv->v_layer(layer);
@@ -416,7 +445,7 @@ void attention(const ptts_b200_kv* kv, int layer, bool decode, const RowPlan& pl
         a.prestart = true;  // the in_proj or rope_append launch sits between the plan and this one
         a.stamps = stamps;
         a.stamp = stamp;
-        launch_decode_attn(a, bf16, grid, s, compact);
+        launch_decode_attn(a, bf16, grid, s, decode_ring_compact(compact));
     } else {
         PrefillArgs a{};
         a.k_cache = kv->k_layer(layer);
@@ -513,7 +542,7 @@ void run_layers(const ptts_b200_model* m, const ptts_b200_kv* kv, bool decode, c
         check_launch();
         pending = 0;
     };
-    auto residual_gemm = [&](const void* a_hi, const void* a_lo, const DevBuf& wq, const DevBuf& wh,
+    auto residual_gemm = [&](const void* a_hi, const void* a_lo, const DevBuf& wq, const void* wh,
                              const DevBuf& wl, const DevBuf& sc, int k, int splits) {
         LinearArgs o{};
         o.M = rows;
@@ -523,7 +552,7 @@ void run_layers(const ptts_b200_model* m, const ptts_b200_kv* kv, bool decode, c
         o.a = a_hi;
         o.a_lo = a_lo;
         o.w = wq.as<int8_t>();
-        o.wh = wh.as<__half>();
+        o.wh = wh;
         o.wh_lo = wl.p;
         o.scale = sc.as<float>();
         o.y = splits > 1 ? split : resid;
@@ -534,9 +563,35 @@ void run_layers(const ptts_b200_model* m, const ptts_b200_kv* kv, bool decode, c
         check_launch();
         if (splits > 1) pending = splits;
     };
+    // Prompt-size calls on int8 layers read their weights widened once per layer (see wconv).
+    // Prompts only: decode steps are recorded into graphs, where the workspace cannot grow.
+    const bool widen = !decode && rows >= kPersistMinRows && s_out == 1 && s_ff2 == 1;
+    const size_t n_qkv = (size_t)nqkv * c.d_model, n_out = (size_t)c.d_model * hd;
+    const size_t n_ff1 = (size_t)c.dim_feedforward * c.d_model, n_ff2 = n_ff1;
+    auto al = [](size_t bytes) { return (bytes + 255) / 256 * 256; };
+    const size_t o_out = al(2 * n_qkv), o_ff1 = o_out + al(2 * n_out), o_ff2 = o_ff1 + al(2 * n_ff1);
     for (int l = 0; l < c.num_layers; ++l) {
         layer = l;
         const auto& L = *m->layers[l];
+        // Per-linear 16-bit weights: the layer's own planes, the widened prompt copy, or none.
+        const void *wh_qkv = L.h_qkv.p, *wh_out = L.h_out.p, *wh_1 = L.h1.p, *wh_2 = L.h2.p;
+        if (widen && L.w_qkv.p && !L.h_qkv.p) {
+            unsigned char* base = static_cast<unsigned char*>(w.wconv.need(o_ff2 + al(2 * n_ff2)));
+            I8Widen wd;
+            const DevBuf* src[4] = {&L.w_qkv, &L.w_out, &L.w1, &L.w2};
+            const size_t off[4] = {0, o_out, o_ff1, o_ff2}, n[4] = {n_qkv, n_out, n_ff1, n_ff2};
+            for (int i = 0; i < 4; ++i) {
+                wd.src[i] = src[i]->as<int8_t>();
+                wd.dst[i] = reinterpret_cast<__half*>(base + off[i]);
+                wd.n[i] = (long long)n[i];
+            }
+            launch_widen_i8(wd, s);
+            check_launch();
+            wh_qkv = wd.dst[0];
+            wh_out = wd.dst[1];
+            wh_1 = wd.dst[2];
+            wh_2 = wd.dst[3];
+        }
         ln(L.ln1g.as<float>(), L.ln1b.as<float>(), l == 0 ? x_in : nullptr, true, "ln1");
         // in_proj, RoPE + append epilogue
         LinearArgs a{};
@@ -546,7 +601,7 @@ void run_layers(const ptts_b200_model* m, const ptts_b200_kv* kv, bool decode, c
         a.a = h_hi;
         a.a_lo = h_lo;
         a.w = L.w_qkv.as<int8_t>();
-        a.wh = L.h_qkv.as<__half>();
+        a.wh = wh_qkv;
         a.wh_lo = L.l_qkv.p;
         a.scale = L.s_qkv.as<float>();
         a.yq = w.q_rot.as<float>();
@@ -574,7 +629,7 @@ void run_layers(const ptts_b200_model* m, const ptts_b200_kv* kv, bool decode, c
                   kOutHiLo, w.part, w.counters, tiles, s, lo.lane, stamped.stamps, stamped.stamp);
         if (attn_ev) CK(cudaEventRecord(attn_ev[2 * l + 1], s));
         // out_proj + residual
-        residual_gemm(w.attn_hi.as<__half>(), w.attn_lo.as<__half>(), L.w_out, L.h_out, L.l_out, L.s_out,
+        residual_gemm(w.attn_hi.as<__half>(), w.attn_lo.as<__half>(), L.w_out, wh_out, L.l_out, L.s_out,
                       hd, s_out);
         // LN2, linear1 + GELU
         ln(L.ln2g.as<float>(), L.ln2b.as<float>(), nullptr, true, "ln2");
@@ -585,7 +640,7 @@ void run_layers(const ptts_b200_model* m, const ptts_b200_kv* kv, bool decode, c
         f1.a = h_hi;
         f1.a_lo = h_lo;
         f1.w = L.w1.as<int8_t>();
-        f1.wh = L.h1.as<__half>();
+        f1.wh = wh_1;
         f1.wh_lo = L.l1.p;
         f1.scale = L.s1.as<float>();
         f1.yb = w.ff_hi.as<__half>();
@@ -596,7 +651,7 @@ void run_layers(const ptts_b200_model* m, const ptts_b200_kv* kv, bool decode, c
         require(launch_linear(f1, EPI_GELU, s), PTTS_B200_ERR_UNSUPPORTED, "no kernel for linear1's shape");
         check_launch();
         // linear2 + residual
-        residual_gemm(w.ff_hi.as<__half>(), w.ff_lo.as<__half>(), L.w2, L.h2, L.l2, L.s2,
+        residual_gemm(w.ff_hi.as<__half>(), w.ff_lo.as<__half>(), L.w2, wh_2, L.l2, L.s2,
                       c.dim_feedforward, s_ff2);
     }
     if (pending) ln(nullptr, nullptr, nullptr, false, "ln_out");
@@ -746,8 +801,8 @@ void run_step(ptts_b200_model* model, ptts_b200_kv* kv, const int32_t* streams_h
     refuse_window(kv, streams_host, n);
     const ptts_b200_config& c = model->cfg;
     ensure_rope(model, kv->capacity, s);
-    const int grid = sm_count(kv->device);
     const int n_lanes = step_lanes(n);
+    const int grid = decode_grid(kv->device, n_lanes > 1);
     GraphKey gkey = key;
     gkey.stamps = model->stamps.cap > 0;
     StepGraph* g = slot.get();
@@ -1284,13 +1339,20 @@ int ptts_b200_model_load_layer(ptts_b200_model* model, int layer,
         put(L.ln2g, w->norm2_weight_host, dm * 4);
         put(L.ln2b, w->norm2_bias_host, dm * 4);
         for (DevBuf* b : {&L.l_qkv, &L.l_out, &L.l1, &L.l2}) b->release();  // int8 layers: one plane
-        auto widen = [](DevBuf& h, const DevBuf& q, size_t n) {
-            launch_i8_to_f16(q.as<int8_t>(), static_cast<__half*>(h.need(n * 2)), (long long)n, nullptr);
-        };
-        widen(L.h_qkv, L.w_qkv, nqkv * dm);
-        widen(L.h_out, L.w_out, dm * hd);
-        widen(L.h1, L.w1, ff * dm);
-        widen(L.h2, L.w2, dm * ff);
+        // The tcgen05 linears read the int8 weights and widen them on chip. An exact f16 copy of
+        // every weight, read instead (twice the bytes), is kept only with PTTS_B200_WEIGHTS=f16.
+        const char* wsel = getenv("PTTS_B200_WEIGHTS");
+        if (wsel && wsel[0] == 'f') {
+            auto widen = [](DevBuf& h, const DevBuf& q, size_t n) {
+                launch_i8_to_f16(q.as<int8_t>(), static_cast<__half*>(h.need(n * 2)), (long long)n, nullptr);
+            };
+            widen(L.h_qkv, L.w_qkv, nqkv * dm);
+            widen(L.h_out, L.w_out, dm * hd);
+            widen(L.h1, L.w1, ff * dm);
+            widen(L.h2, L.w2, dm * ff);
+        } else {
+            for (DevBuf* b : {&L.h_qkv, &L.h_out, &L.h1, &L.h2}) b->release();
+        }
         check_launch();
         CK(cudaDeviceSynchronize());
         L.loaded = true;

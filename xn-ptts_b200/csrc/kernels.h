@@ -253,8 +253,9 @@ struct LinearArgs {
     const void* a_lo;         // A lo plane [M][K], or nullptr (A exact in one plane)
     int a_f16 = 1;            // 1: f16 planes (the layer stack); 0: one bf16 plane
     const int8_t* w;          // [N][K]
-    const void* wh = nullptr;    // 16-bit weights [N][K] for the tcgen05 kernel: the int8 ones as
-                                 // f16 (exact), or the flow net's bf16 hi plane
+    const void* wh = nullptr;    // 16-bit weights [N][K] for the tcgen05 kernel (the f32 / q8_0 layers'
+                                 // hi plane, the flow net's bf16 hi plane, or an f16 copy of w);
+                                 // nullptr: the tcgen05 kernel widens the int8 `w` on chip
     const void* wh_lo = nullptr; // flow net: bf16 lo plane of the weights, or nullptr
     const float* scale;       // [N], or nullptr (1) for the flow net
     const float* bias = nullptr;  // flow epilogues: [N] or nullptr
@@ -278,10 +279,14 @@ struct LinearArgs {
     uint32_t* err;
 };
 // N must be a multiple of 64 and K / splits a multiple of 64. launch_linear runs the TMA-fed
-// tcgen05/TMEM kernel (linear_tc.cu) wherever linear_tc_supported holds (f16 hi/lo activations,
-// an f16 weight copy, N a multiple of 128), and the mma.sync kernel (linear.cu) otherwise or when
-// PTTS_B200_GEMM=mma. Layers loaded from f32 or q8_0 weights have no int8 copy (w == nullptr)
-// and two f16 weight planes (wh, wh_lo): only the tcgen05 kernel takes them.
+// tcgen05/TMEM kernel (linear_tc.cu) wherever linear_tc_supported holds (N a multiple of 128;
+// int8 weights widened on chip, or 16-bit weight planes of the activations' type), and the
+// mma.sync kernel (linear.cu) otherwise or when PTTS_B200_GEMM=mma. Layers loaded from f32 or
+// q8_0 weights have no int8 copy (w == nullptr) and two f16 weight planes (wh, wh_lo): only the
+// tcgen05 kernel takes them.
+// From this many rows (one slice, not EPI_PARTIAL) the tcgen05 linears run the persistent
+// kernel, which reads its weights only after the wait on its predecessor grid.
+constexpr int kPersistMinRows = 4096;
 bool launch_linear(const LinearArgs& a, LinearEpi epi, cudaStream_t s);  // false: nothing launched
 void launch_linear_mma(const LinearArgs& a, LinearEpi epi, cudaStream_t s);
 bool linear_tc_supported(const LinearArgs& a);
@@ -356,6 +361,15 @@ void launch_rope_table(RopeFreqs f, float2* out, int rows, cudaStream_t s);
 
 // int8 -> f16, exact (weights, once per layer load).
 void launch_i8_to_f16(const int8_t* x, __half* y, long long n, cudaStream_t s);
+// Up to four int8 matrices widened to f16 (exact) in one launch: n[i] a multiple of 16, src and
+// dst 16-byte aligned. A plain launch (no programmatic serialisation): it starts after its
+// predecessor in the stream has finished and its successor starts after it has.
+struct I8Widen {
+    const int8_t* src[4] = {};
+    __half* dst[4] = {};
+    long long n[4] = {};
+};
+void launch_widen_i8(const I8Widen& w, cudaStream_t s);
 
 // Residual update and LayerNorm, one warp per row: resid = (x_bf16 ? x_bf16 : resid)
 // + sum of `nsplit` partial slices [nsplit][M][d]; then, when hi != nullptr, LayerNorm(resid)

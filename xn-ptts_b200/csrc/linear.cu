@@ -66,37 +66,6 @@ __device__ __forceinline__ void cp_async_wait() {
     asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
-// Four int8 weights (one 32-bit word) -> two bf16x2 words, exactly, without int->float
-// conversions: with the sign bit flipped, byte u = v + 128 placed under the f32 exponent of 2^23
-// reads as 2^23 + u, and subtracting 2^23 + 128 leaves v.
-__device__ __forceinline__ void i8x4_to_bf16x4(uint32_t w, uint32_t& b01, uint32_t& b23) {
-    const uint32_t u = w ^ 0x80808080u;
-    const float f0 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7540)) - 8388736.0f;
-    const float f1 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7541)) - 8388736.0f;
-    const float f2 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7542)) - 8388736.0f;
-    const float f3 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7543)) - 8388736.0f;
-    b01 = pack_bf16x2(f0, f1);
-    b23 = pack_bf16x2(f2, f3);
-}
-
-// Four int8 weights -> two f16x2 words, exactly: with the sign bit flipped, byte u = v + 128
-// under the f16 exponent of 1024 reads as 1024 + u; one packed subtract of 1152 leaves v.
-__device__ __forceinline__ void i8x4_to_f16x4(uint32_t w, uint32_t& h01, uint32_t& h23) {
-    const uint32_t u = w ^ 0x80808080u;
-    const uint32_t p01 = __byte_perm(u, 0x64646464u, 0x5140);
-    const uint32_t p23 = __byte_perm(u, 0x64646464u, 0x7362);
-    const __half2 bias = __halves2half2(__ushort_as_half(0x6480), __ushort_as_half(0x6480));  // 1152
-    const __half2 r01 = __hsub2(*reinterpret_cast<const __half2*>(&p01), bias);
-    const __half2 r23 = __hsub2(*reinterpret_cast<const __half2*>(&p23), bias);
-    h01 = *reinterpret_cast<const uint32_t*>(&r01);
-    h23 = *reinterpret_cast<const uint32_t*>(&r23);
-}
-
-template <bool F16>
-__device__ __forceinline__ void i8x4_convert(uint32_t w, uint32_t& b01, uint32_t& b23) {
-    if (F16) i8x4_to_f16x4(w, b01, b23);
-    else i8x4_to_bf16x4(w, b01, b23);
-}
 
 // D += A B, m16n8k16, f32 accumulate; A and B both f16 (F16) or both bf16.
 template <bool F16>

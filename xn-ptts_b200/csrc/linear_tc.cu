@@ -1,28 +1,36 @@
 // int8-weight linears on the 5th-generation tensor cores (tcgen05 + TMEM), fed by TMA, sm_100a.
 //
-// Same contract as linear.cu (LinearArgs, the five epilogues, split-K slices) for the layer
-// stack's f16 hi/lo activations. The int8 weights are read through their exact f16 copy
-// (LinearArgs::wh, made once when a layer is loaded), so both operands reach shared memory by
-// TMA (cp.async.bulk.tensor, 128-byte swizzle) with no conversion on the way.
+// Same contract as linear.cu (LinearArgs, the epilogues, split-K slices). Three weight forms:
+//   kW8    the layer's int8 weights themselves (the default for int8 layers), copied by TMA as
+//          int8 and widened in registers to the 16-bit type of the activations (f16 for the
+//          layer stack's hi/lo planes, bf16 for a single bf16 plane) in the 128-byte-swizzled
+//          K-major layout the MMA reads; int8 values are exact in both types, and the per-row
+//          scale is applied to the f32 accumulator in the epilogue;
+//   kW16   one 16-bit plane read as it is (the flow net's bf16 weights, a prompt's weights
+//          widened once per call, or an f16 copy made at load time with PTTS_B200_WEIGHTS=f16);
+//   kW16Lo two 16-bit planes (hi, lo) for f32 and q8_0 layers and the flow net's f32 weights.
 //
 // Roles are swapped against the row-major view: the MMA's M side (128 TMEM lanes) is 128 output
 // features and its N side is RT activation rows, D^T[f][r] = sum_k W[f][k] X[r][k]. Per 16 k
 // that is one tcgen05.mma.cta_group::1.kind::f16 per activation plane (hi, lo) with A = the
-// weight tile and B = the activation tile, both K-major. Up to 4095 rows, linear_tma_kernel
-// takes one 128-feature x 32-row tile per CTA (a 512-row decode batch gives (N / 128) x 16
-// CTAs); prompts of 4096+ rows go to linear_persist_kernel (below), one CTA per SM over all
-// 128 x 128 tiles.
+// weight tile and B = the activation tile, both K-major. Kernels:
+//   linear_tma_kernel    one 128-feature x 32-row tile per CTA (decode sizes up to 4095 rows:
+//                        a 512-row batch gives (N / 128) x 16 CTAs);
+//   linear_persist_kernel prompts of 4096+ rows: one CTA per SM over all 128 x 128 tiles.
 //
 // linear_tma_kernel CTA: 512 threads (16 warps).
-//   thread 0:   TMA producer over a kStages ring of {W 128x64, X hi RTx64, X lo RTx64} f16
-//               tiles. The weight tiles of the first stages are requested before the wait on
-//               the grid that wrote X (weights never change).
+//   thread 0:   TMA producer over a kStages ring of {W 128x64, X hi RTx64, X lo RTx64} tiles,
+//               weights and activations on separate barriers. The weight tiles of the first
+//               stages are requested before the wait on the grid that wrote X (weights never
+//               change), so with kW8 they are also widened before that wait ends.
 //   thread 32:  MMA issuer; tcgen05.commit frees each stage and finally signals `done`.
-//   all warps:  epilogue: warp w reads TMEM lanes 32 (w % 4) .. + 31 (features n0 + 32 (w % 4)
-//               + lane), 8 rows per tcgen05.ld, into a shared-memory tile; then each warp takes
-//               2 whole rows, lane l the features 4l..4l+3, so stores are 16 bytes and RoPE
-//               pairs in-lane. Sixteen warps instead of four cut each warp's serial share of
-//               the epilogue (GELU, RoPE), which bounds the decode-size launches.
+//   warps 4-11: kW8 only: the converters (widen_w8: the 8 KB int8 tile lands in the upper half of
+//               the stage's 16 KB weight slot and is widened in place).
+//   all warps:  epilogue (drain_tile): warp w reads TMEM lanes 32 (w % 4) .. + 31 (features
+//               n0 + 32 (w % 4) + lane), 8 rows per tcgen05.ld, into a shared-memory tile; then
+//               each warp takes 2 whole rows, lane l the features 4l..4l+3, so stores are 16
+//               bytes and RoPE pairs in-lane. Sixteen warps instead of four cut each warp's
+//               serial share of the epilogue (GELU, RoPE), which bounds the decode-size launches.
 // Every wait is bounded (DEV_ERR_TIMEOUT); after a timeout the CTA still waits, bounded, for the
 // copies it issued and frees its TMEM. No clusters, no multicast.
 #include <cuda.h>
@@ -45,24 +53,83 @@ constexpr int kEpiWarps = 16;
 constexpr int kThreadsTma = 32 * kEpiWarps;
 constexpr int kRowsPerWarp = 32 / kEpiWarps;
 
-// WLO: the weights come as two planes too (hi, lo), and each k step runs a third MMA.
-template <int RT, bool WLO>
+// Weight forms (see the top of this file).
+enum : int { kW16 = 0, kW16Lo = 1, kW8 = 2 };
+constexpr int kConvWarps = 8;   // kW8 converter warps
+constexpr int kConvBar = 2;     // their named barrier (0: __syncthreads, 1: persistent epilogue)
+
+template <int RT, int WM>
 struct TmaTile {
     // 3 stages: a decode tile (RT 32, 74 KB) fits beside the decode attention's compact ring
     // (137 KB) on one SM, and two prompt tiles (RT 64, 97 KB) share an SM, so that one's epilogue
     // overlaps the other's loads and MMAs.
-    static constexpr int kStages = (WLO || RT <= 64) ? 3 : 4;
-    static constexpr int kWBytes = FT * KS * 2;  // 16 KB per weight plane
+    static constexpr int kStages = (WM == kW16Lo || RT <= 64) ? 3 : 4;
+    static constexpr int kWBytes = FT * KS * 2;  // 16 KB per 16-bit weight plane
     static constexpr int kXBytes = RT * KS * 2;  // per activation plane
-    static constexpr int kStageBytes = (WLO ? 2 : 1) * kWBytes + 2 * kXBytes;
-    static constexpr int kXOffset = (WLO ? 2 : 1) * kWBytes;  // X hi, then X lo
+    static constexpr int kStageBytes = (WM == kW16Lo ? 2 : 1) * kWBytes + 2 * kXBytes;
+    static constexpr int kXOffset = (WM == kW16Lo ? 2 : 1) * kWBytes;  // X hi, then X lo
     static constexpr int kBarOffset = kStages * kStageBytes;
     static constexpr int kSmem = 1024 + kBarOffset + 256;  // + alignment slack + barriers
-    static constexpr uint32_t kTmemCols = RT < 32 ? 32 : RT;
-    static_assert(RT % 32 == 0 && RT >= 32 && RT <= 256, "RT: 32..256 in steps of 32");
+    // Weight bytes a stage's copies deliver: the int8 tile (kW8) or the 16-bit plane(s).
+    static constexpr uint32_t kWTx = WM == kW8 ? FT * KS : (WM == kW16Lo ? 2 : 1) * kWBytes;
+    // Accumulator columns: RT rows of the hi plane, then RT rows of the lo plane (one N = 2 RT
+    // MMA covers both, see linear_tma_kernel).
+    static constexpr uint32_t kTmemCols = 2 * RT;
+    static_assert(RT % 32 == 0 && RT >= 32 && RT <= 128, "RT: 32..128 in steps of 32");
     static_assert(kStageBytes % 1024 == 0, "stages stay 1024-byte aligned");
     static_assert(32 * (FT + 4) * 4 <= kBarOffset, "the QKV staging tile fits in the ring");
+    static_assert(4 * kStages * 8 + 8 + 4 <= 256, "barriers fit the tail");
 };
+
+// Named barrier `ID` over N threads that returns whether `v` held in any of them (one answer for
+// all, so a group leaves a loop together).
+template <int ID, int N>
+__device__ __forceinline__ bool bar_any(bool v) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 p, %1, 0;\n\t"
+        "barrier.red.or.pred q, %2, %3, p;\n\t"
+        "selp.u32 %0, 1, 0, q;\n\t}"
+        : "=r"(r)
+        : "r"((uint32_t)v), "n"(ID), "n"(N)
+        : "memory");
+    return r != 0;
+}
+
+// kW8: widen the int8 tile at the upper half of the 16 KB weight slot `w16` (128 rows x 64
+// bytes, dense, as the TMA copied it) in place into the 128-byte-swizzled K-major 16-bit tile
+// (128 rows x 128 bytes: the 16-byte chunk c of row r at chunk c ^ (r % 8)) that the MMA reads.
+// Converter thread t (0..255) takes the 16-byte int8 chunks q = t + 256 i, i < 2 (row q / 4,
+// k 16 (q % 4) .. + 15): the loads are contiguous, and each quarter-warp's stores hit the eight
+// distinct 16-byte bank groups. The int8 tile is the slot's upper half, so every converter loads
+// its share before any stores: one named barrier between them, which is also where the
+// converters agree on the wait for the tile (`landed`: false in any of them, and all return
+// false together, so none is left at a barrier). The proxy fence then makes the stores visible
+// to the tensor core.
+template <bool F16>
+__device__ __forceinline__ bool widen_w8(unsigned char* w16, int t, bool landed) {
+    constexpr int kChunks = FT * KS / 16 / (32 * kConvWarps);  // 16-byte int8 chunks per thread
+    const unsigned char* w8 = w16 + FT * KS;
+    uint4 in[kChunks];
+#pragma unroll
+    for (int i = 0; i < kChunks; ++i) in[i] = *reinterpret_cast<const uint4*>(w8 + 16 * (t + 32 * kConvWarps * i));
+    if (bar_any<kConvBar, 32 * kConvWarps>(!landed)) return false;
+#pragma unroll
+    for (int i = 0; i < kChunks; ++i) {
+        const int q = t + 32 * kConvWarps * i, r = q >> 2, j = q & 3;
+        uint4 a, b;
+        i8x4_convert<F16>(in[i].x, a.x, a.y);
+        i8x4_convert<F16>(in[i].y, a.z, a.w);
+        i8x4_convert<F16>(in[i].z, b.x, b.y);
+        i8x4_convert<F16>(in[i].w, b.z, b.w);
+        unsigned char* row = w16 + r * 128;
+        *reinterpret_cast<uint4*>(row + (((2 * j) ^ (r & 7)) << 4)) = a;
+        *reinterpret_cast<uint4*>(row + (((2 * j + 1) ^ (r & 7)) << 4)) = b;
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    return true;
+}
 
 // Instruction descriptor, kind::f16: D f32 (bits 4-5 = 1), A and B both f16 (formats 0) or both
 // bf16 (format 1 at bits 7-9 and 10-12), both K-major, N >> 3 at bit 17, M >> 4 at bit 24.
@@ -321,23 +388,61 @@ __device__ __forceinline__ void plain_rows(const LinearArgs& p, const float* st,
     }
 }
 
-template <int EPI, int RT, bool WLO>
+// The epilogue of a 128-feature x RT-row tile (all 16 warps; the ring at `smem` is drained):
+// warp w reads TMEM lane quarter w % 4, columns (rows) c + 8 (w / 4) .. + 7 of each 32-row chunk,
+// and transposes them through shared memory, so that lanes then own feature quads and store 16
+// bytes per row (qkv_rows / plain_rows).
+template <int EPI, int RT>
+__device__ __forceinline__ void drain_tile(const LinearArgs& p, unsigned char* smem, uint32_t tmem, int n0,
+                                           int m0, int z, bool got, bool lo_cols) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    __syncwarp();  // tcgen05.ld below is warp-collective
+    tc_fence_after();
+#pragma unroll 1
+    for (int c = 0; c < RT; c += 32) {
+        constexpr int CW = 32 / (kEpiWarps / 4);  // columns (rows) per warp
+        const int quarter = warp & 3, part = warp >> 2;
+        float v[CW];
+        const uint32_t col = tmem + ((uint32_t)(32 * quarter) << 16) + (uint32_t)(c + CW * part);
+        tmem_ld<CW>(col, v);
+        if (lo_cols) {  // the lo plane's products of the same rows, RT columns further
+            float w[CW];
+            tmem_ld<CW>(col + RT, w);
+#pragma unroll
+            for (int j = 0; j < CW; ++j) v[j] += w[j];
+        }
+        float* st = reinterpret_cast<float*>(smem);
+        __syncthreads();  // the previous chunk's readers are done
+#pragma unroll
+        for (int j = 0; j < CW; ++j) st[(CW * part + j) * kStageStride + 32 * quarter + lane] = v[j];
+        __syncthreads();
+        if (got) {
+            if (EPI == EPI_QKV) qkv_rows(p, st, n0, m0 + c);
+            else plain_rows<EPI>(p, st, n0, m0 + c, z);
+        }
+    }
+}
+
+template <int EPI, int RT, int WM>
 __global__ void __launch_bounds__(kThreadsTma) linear_tma_kernel(const __grid_constant__ LinearArgs p,
                                                                  const __grid_constant__ CUtensorMap tm_w,
                                                                  const __grid_constant__ CUtensorMap tm_wlo,
                                                                  const __grid_constant__ CUtensorMap tm_x,
                                                                  const __grid_constant__ CUtensorMap tm_xlo) {
-    using T = TmaTile<RT, WLO>;
+    using T = TmaTile<RT, WM>;
     constexpr int S = T::kStages;
+    constexpr bool W8 = WM == kW8, WLO = WM == kW16Lo;
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t base = (raw + 1023u) & ~1023u;
     unsigned char* smem = smem_raw + (base - raw);
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + T::kBarOffset);
-    uint64_t* empty = full + S;
+    uint64_t* wfull = reinterpret_cast<uint64_t*>(smem + T::kBarOffset);  // a stage's weights landed
+    uint64_t* xfull = wfull + S;                                           // its activations landed
+    uint64_t* conv = xfull + S;                                            // kW8: its weights widened
+    uint64_t* empty = conv + S;                                            // its MMAs are done
     uint64_t* done = empty + S;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
-    __shared__ int s_issued, s_consumed;
+    __shared__ int s_w_issued, s_issued, s_consumed;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int n0 = blockIdx.x * FT, m0 = blockIdx.y * RT, z = blockIdx.z;
@@ -345,13 +450,17 @@ __global__ void __launch_bounds__(kThreadsTma) linear_tma_kernel(const __grid_co
     const int k0 = z * k_len;
     const int KT = k_len / KS;
     const bool has_lo = p.a_lo != nullptr;
-    const uint32_t stage_tx = (WLO ? 2u : 1u) * T::kWBytes + (has_lo ? 2u : 1u) * T::kXBytes;
+    const uint32_t x_tx = (has_lo ? 2u : 1u) * T::kXBytes;
+    const bool converter = W8 && warp >= 4 && warp < 4 + kConvWarps;  // warps 4..11
 
     if (tid == 0) {
+        s_w_issued = 0;
         s_issued = 0;
         s_consumed = 0;
         for (int s = 0; s < S; ++s) {
-            mbar_init(&full[s], 1);
+            mbar_init(&wfull[s], 1);
+            mbar_init(&xfull[s], 1);
+            mbar_init(&conv[s], kConvWarps);
             mbar_init(&empty[s], 1);
         }
         mbar_init(done, 1);
@@ -375,12 +484,15 @@ __global__ void __launch_bounds__(kThreadsTma) linear_tma_kernel(const __grid_co
     if (tid == 0) {
         // ---- TMA producer ----------------------------------------------------------------------
         const uint64_t pol_w = policy_evict_last();  // weights: reread every frame
+        auto load_w = [&](int kt, uint32_t sa, int st) {
+            mbar_arrive_expect_tx(&wfull[st], T::kWTx);
+            // kW8: the int8 tile goes to the upper half of the slot, where the converters find it.
+            tma_load_2d_hint(sa + (W8 ? FT * KS : 0), &tm_w, k0 + kt * KS, n0, &wfull[st], pol_w);
+            if (WLO) tma_load_2d_hint(sa + T::kWBytes, &tm_wlo, k0 + kt * KS, n0, &wfull[st], pol_w);
+            s_w_issued = kt + 1;
+        };
         const int pre = KT < S ? KT : S;
-        for (int kt = 0; kt < pre; ++kt) {
-            mbar_arrive_expect_tx(&full[kt], stage_tx);
-            tma_load_2d_hint(base + kt * T::kStageBytes, &tm_w, k0 + kt * KS, n0, &full[kt], pol_w);
-            if (WLO) tma_load_2d_hint(base + kt * T::kStageBytes + T::kWBytes, &tm_wlo, k0 + kt * KS, n0, &full[kt], pol_w);
-        }
+        for (int kt = 0; kt < pre; ++kt) load_w(kt, base + kt * T::kStageBytes, kt);
         grid_dep_wait();
         stamp_mark(p.stamps, p.stamp, STAMP_START);
         for (int kt = 0; kt < KT; ++kt) {
@@ -391,34 +503,54 @@ __global__ void __launch_bounds__(kThreadsTma) linear_tma_kernel(const __grid_co
                     set_error(p.err, DEV_ERR_TIMEOUT);
                     break;
                 }
-                mbar_arrive_expect_tx(&full[st], stage_tx);
-                tma_load_2d_hint(sa, &tm_w, k0 + kt * KS, n0, &full[st], pol_w);
-                if (WLO) tma_load_2d_hint(sa + T::kWBytes, &tm_wlo, k0 + kt * KS, n0, &full[st], pol_w);
+                load_w(kt, sa, st);
             }
-            tma_load_2d(sa + T::kXOffset, &tm_x, k0 + kt * KS, m0, &full[st]);
-            if (has_lo) tma_load_2d(sa + T::kXOffset + T::kXBytes, &tm_xlo, k0 + kt * KS, m0, &full[st]);
+            mbar_arrive_expect_tx(&xfull[st], x_tx);
+            tma_load_2d(sa + T::kXOffset, &tm_x, k0 + kt * KS, m0, &xfull[st]);
+            if (has_lo) tma_load_2d(sa + T::kXOffset + T::kXBytes, &tm_xlo, k0 + kt * KS, m0, &xfull[st]);
             s_issued = kt + 1;
         }
+    } else if (converter) {
+        // ---- kW8 converters: weights need no predecessor, so they start at once -----------------
+        const int t = tid - 128;
+        for (int kt = 0; kt < KT; ++kt) {
+            const int st = kt % S;
+            const bool landed = mbar_wait(&wfull[st], (kt / S) & 1);
+            const bool ok = p.a_f16 ? widen_w8<true>(smem + st * T::kStageBytes, t, landed)
+                                    : widen_w8<false>(smem + st * T::kStageBytes, t, landed);
+            if (!ok) {
+                set_error(p.err, DEV_ERR_TIMEOUT);
+                break;
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&conv[st]);
+        }
+        grid_dep_wait();  // the epilogue below reads what predecessors wrote
     } else {
         grid_dep_wait();
         if (tid == 32) {
             // ---- MMA issuer --------------------------------------------------------------------
-            const uint32_t idesc = p.a_f16 ? idesc_f16<RT>() : idesc_bf16<RT>();
+            // The X hi and lo tiles lie back to back in the stage (RT rows each, 1024-byte
+            // aligned), so with a lo plane one MMA of N = 2 RT takes both: the weight tile is
+            // read once per k step instead of once per plane. Columns RT.. hold the lo rows.
+            const uint32_t idesc1 = p.a_f16 ? idesc_f16<RT>() : idesc_bf16<RT>();
+            const uint32_t idesc2 = p.a_f16 ? idesc_f16<2 * RT>() : idesc_bf16<2 * RT>();
+            const uint32_t idesc = has_lo ? idesc2 : idesc1;
             for (int kt = 0; kt < KT; ++kt) {
                 const int st = kt % S;
-                if (!mbar_wait(&full[st], (kt / S) & 1)) {
+                const uint32_t ph = (kt / S) & 1;
+                if (!mbar_wait(W8 ? &conv[st] : &wfull[st], ph) || !mbar_wait(&xfull[st], ph)) {
                     set_error(p.err, DEV_ERR_TIMEOUT);
                     break;
                 }
                 tc_fence_after();
                 const uint32_t sa = base + st * T::kStageBytes;
                 const uint64_t dw = sw128_desc(sa), dwl = sw128_desc(sa + T::kWBytes);
-                const uint64_t dx = sw128_desc(sa + T::kXOffset), dxl = sw128_desc(sa + T::kXOffset + T::kXBytes);
+                const uint64_t dx = sw128_desc(sa + T::kXOffset);
 #pragma unroll
                 for (int kk = 0; kk < KS / 16; ++kk) {  // 32 bytes of K per MMA
                     tc_mma(tmem, dw + 2 * kk, dx + 2 * kk, idesc, (kt | kk) ? 1u : 0u);
-                    if (has_lo) tc_mma(tmem, dw + 2 * kk, dxl + 2 * kk, idesc, 1u);
-                    if (WLO) tc_mma(tmem, dwl + 2 * kk, dx + 2 * kk, idesc, 1u);
+                    if (WLO) tc_mma(tmem, dwl + 2 * kk, dx + 2 * kk, idesc1, 1u);  // into the hi columns
                 }
                 tc_commit(&empty[st]);
                 s_consumed = kt + 1;
@@ -434,34 +566,15 @@ __global__ void __launch_bounds__(kThreadsTma) linear_tma_kernel(const __grid_co
     // The next kernel may launch now: its CTAs take SM room only while this epilogue runs, not
     // through the whole pipeline (room a concurrent lane's kernels can use).
     if (tid == 0) grid_dep_launch();
-    __syncwarp();  // tcgen05.ld below is warp-collective
-    tc_fence_after();
-#pragma unroll 1
-    for (int c = 0; c < RT; c += 32) {
-        // Warp w reads lane quarter w % 4, columns (rows) c + 16 (w / 4) .. + 15, and
-        // transposes them through shared memory (the drained ring): lanes then own feature
-        // quads and store 16 bytes per row.
-        constexpr int CW = 32 / (kEpiWarps / 4);  // columns (rows) per warp
-        const int quarter = warp & 3, part = warp >> 2;
-        float v[CW];
-        tmem_ld<CW>(tmem + ((uint32_t)(32 * quarter) << 16) + (uint32_t)(c + CW * part), v);
-        float* st = reinterpret_cast<float*>(smem);
-        __syncthreads();  // the previous chunk's readers are done
-#pragma unroll
-        for (int j = 0; j < CW; ++j) st[(CW * part + j) * kStageStride + 32 * quarter + lane] = v[j];
-        __syncthreads();
-        if (got) {
-            if (EPI == EPI_QKV) qkv_rows(p, st, n0, m0 + c);
-            else plain_rows<EPI>(p, st, n0, m0 + c, z);
-        }
-    }
+    drain_tile<EPI, RT>(p, smem, tmem, n0, m0, z, got, has_lo);
 
     if (tid == 0) stamp_mark(p.stamps, p.stamp, STAMP_END);
     tc_fence_before();
     __syncthreads();
     if (tid == 0) {
         // Copies issued but never consumed (only after a timeout): let them land before exit.
-        for (int kt = s_consumed; kt < s_issued; ++kt) mbar_wait(&full[kt % S], (kt / S) & 1);
+        for (int kt = s_consumed; kt < s_w_issued; ++kt) mbar_wait(&wfull[kt % S], (kt / S) & 1);
+        for (int kt = s_consumed; kt < s_issued; ++kt) mbar_wait(&xfull[kt % S], (kt / S) & 1);
     }
     if (warp == 0) {
         tc_fence_after();
@@ -477,61 +590,59 @@ __global__ void __launch_bounds__(kThreadsTma) linear_tma_kernel(const __grid_co
 // feature tile t % NT, row tile t / NT) with two TMEM accumulators, so the epilogue of one tile
 // runs while the next tile's loads and MMAs do:
 //   warp 0, lane 0: TMA producer over a 4-stage (3 with a weight lo plane) ring of
-//                   {W 128x64 (+ lo), X hi 128x64, X lo}
+//                   {W 128x64 (+ lo), X hi 128x64, X lo}, weights and activations on separate
+//                   barriers
 //   warp 1, lane 0: MMA issuer, tcgen05.commit frees each stage and fills an accumulator
 //   warps 2..17:    epilogue, two accumulators in turn: 4 x 32-row chunks through a staging
 //                   tile (warp w reads TMEM lane quarter w % 4, 8 columns), then the same
 //                   row epilogues as linear_tma_kernel (2 rows per warp and chunk)
+//   warps 18..25:   kW8 only: the converters (widen_w8), one stage after another (the layer
+//                   stack widens a prompt's weights once per call instead, see abi.cu)
 // Every wait is bounded; a timed-out wait sets DEV_ERR_TIMEOUT and a shared abort flag that
 // ends every role's loop.
 constexpr int PT = 128;   // rows per tile (MMA N)
-constexpr int kPersistWarps = 2 + kEpiWarps;
-constexpr int kPersistThreads = 32 * kPersistWarps;
 
-template <bool WLO>
+template <int WM>
 struct PersistTile {
-    static constexpr int PS = WLO ? 3 : 4;  // ring stages: 192 KB either way
+    static constexpr int PS = WM == kW16Lo ? 3 : 4;  // ring stages: 192 KB either way
     static constexpr int kWBytes = FT * KS * 2;
     static constexpr int kXBytes = PT * KS * 2;
-    static constexpr int kStageBytes = (WLO ? 2 : 1) * kWBytes + 2 * kXBytes;
-    static constexpr int kXOffset = (WLO ? 2 : 1) * kWBytes;
+    static constexpr int kStageBytes = (WM == kW16Lo ? 2 : 1) * kWBytes + 2 * kXBytes;
+    static constexpr int kXOffset = (WM == kW16Lo ? 2 : 1) * kWBytes;
     static constexpr int kStageOffset = PS * kStageBytes;              // the epilogue's staging tile
     static constexpr int kBarOffset = kStageOffset + 32 * kStageStride * 4;
     static constexpr int kSmem = 1024 + kBarOffset + 256;
+    static constexpr uint32_t kWTx = WM == kW8 ? FT * KS : (WM == kW16Lo ? 2 : 1) * kWBytes;
+    static constexpr int kConvWarp0 = 2 + kEpiWarps;
+    static constexpr int kWarps = kConvWarp0 + (WM == kW8 ? kConvWarps : 0);
+    static constexpr int kThreads = 32 * kWarps;
     static_assert(kStageBytes % 1024 == 0, "stages stay 1024-byte aligned");
     static_assert(kSmem <= 227 * 1024, "fits one CTA per SM");
+    static_assert(4 * PS * 8 + 4 * 8 + 4 <= 256, "barriers fit the tail");
 };
 
 __device__ __forceinline__ void epi_bar_sync() {  // the 16 epilogue warps only
     asm volatile("bar.sync 1, %0;" ::"r"(32 * kEpiWarps) : "memory");
 }
 // The same barrier, returning whether `v` held in any epilogue thread (one answer for all).
-__device__ __forceinline__ bool epi_bar_any(bool v) {
-    uint32_t r;
-    asm volatile(
-        "{\n\t.reg .pred p, q;\n\t"
-        "setp.ne.u32 p, %1, 0;\n\t"
-        "barrier.red.or.pred q, 1, %2, p;\n\t"
-        "selp.u32 %0, 1, 0, q;\n\t}"
-        : "=r"(r)
-        : "r"((uint32_t)v), "r"(32 * kEpiWarps)
-        : "memory");
-    return r != 0;
-}
+__device__ __forceinline__ bool epi_bar_any(bool v) { return bar_any<1, 32 * kEpiWarps>(v); }
 
-template <int EPI, bool WLO>
-__global__ void __launch_bounds__(kPersistThreads, 1) linear_persist_kernel(
+template <int EPI, int WM>
+__global__ void __launch_bounds__(PersistTile<WM>::kThreads, 1) linear_persist_kernel(
     const __grid_constant__ LinearArgs p, const __grid_constant__ CUtensorMap tm_w,
     const __grid_constant__ CUtensorMap tm_wlo, const __grid_constant__ CUtensorMap tm_x,
     const __grid_constant__ CUtensorMap tm_xlo) {
-    using T = PersistTile<WLO>;
+    using T = PersistTile<WM>;
     constexpr int PS = T::PS;
+    constexpr bool W8 = WM == kW8, WLO = WM == kW16Lo;
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t base = (raw + 1023u) & ~1023u;
     unsigned char* smem = smem_raw + (base - raw);
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + T::kBarOffset);
-    uint64_t* empty = full + PS;
+    uint64_t* wfull = reinterpret_cast<uint64_t*>(smem + T::kBarOffset);
+    uint64_t* xfull = wfull + PS;
+    uint64_t* conv = xfull + PS;
+    uint64_t* empty = conv + PS;
     uint64_t* acc_full = empty + PS;
     uint64_t* acc_empty = acc_full + 2;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
@@ -540,14 +651,16 @@ __global__ void __launch_bounds__(kPersistThreads, 1) linear_persist_kernel(
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int NT = p.N / FT, MT = (p.M + PT - 1) / PT, tiles = NT * MT, KT = p.K / KS;
     const bool has_lo = p.a_lo != nullptr;
-    const uint32_t stage_tx = (WLO ? 2u : 1u) * T::kWBytes + (has_lo ? 2u : 1u) * T::kXBytes;
+    const uint32_t x_tx = (has_lo ? 2u : 1u) * T::kXBytes;
 
     if (tid == 0) {
         s_abort = 0;
         s_issued = 0;
         s_consumed = 0;
         for (int i = 0; i < PS; ++i) {
-            mbar_init(&full[i], 1);
+            mbar_init(&wfull[i], 1);
+            mbar_init(&xfull[i], 1);
+            mbar_init(&conv[i], kConvWarps);
             mbar_init(&empty[i], 1);
         }
         for (int i = 0; i < 2; ++i) {
@@ -591,11 +704,12 @@ __global__ void __launch_bounds__(kPersistThreads, 1) linear_persist_kernel(
                         break;
                     }
                     const uint32_t sa = base + st * T::kStageBytes;
-                    mbar_arrive_expect_tx(&full[st], stage_tx);
-                    tma_load_2d_hint(sa, &tm_w, kt * KS, n0, &full[st], pol_w);
-                    if (WLO) tma_load_2d_hint(sa + T::kWBytes, &tm_wlo, kt * KS, n0, &full[st], pol_w);
-                    tma_load_2d(sa + T::kXOffset, &tm_x, kt * KS, m0, &full[st]);
-                    if (has_lo) tma_load_2d(sa + T::kXOffset + T::kXBytes, &tm_xlo, kt * KS, m0, &full[st]);
+                    mbar_arrive_expect_tx(&wfull[st], T::kWTx);
+                    tma_load_2d_hint(sa + (W8 ? FT * KS : 0), &tm_w, kt * KS, n0, &wfull[st], pol_w);
+                    if (WLO) tma_load_2d_hint(sa + T::kWBytes, &tm_wlo, kt * KS, n0, &wfull[st], pol_w);
+                    mbar_arrive_expect_tx(&xfull[st], x_tx);
+                    tma_load_2d(sa + T::kXOffset, &tm_x, kt * KS, m0, &xfull[st]);
+                    if (has_lo) tma_load_2d(sa + T::kXOffset + T::kXBytes, &tm_xlo, kt * KS, m0, &xfull[st]);
                     s_issued = kk + 1;
                 }
             }
@@ -617,7 +731,8 @@ __global__ void __launch_bounds__(kPersistThreads, 1) linear_persist_kernel(
                 bool ok = true;
                 for (int kt = 0; kt < KT; ++kt, ++kk) {
                     const int st = kk % PS;
-                    if (!mbar_wait(&full[st], (kk / PS) & 1)) {
+                    const uint32_t ph = (kk / PS) & 1;
+                    if (!mbar_wait(W8 ? &conv[st] : &wfull[st], ph) || !mbar_wait(&xfull[st], ph)) {
                         ok = false;
                         break;
                     }
@@ -639,6 +754,26 @@ __global__ void __launch_bounds__(kPersistThreads, 1) linear_persist_kernel(
                     break;
                 }
                 tc_commit(&acc_full[acc]);
+            }
+        }
+    } else if (warp >= T::kConvWarp0) {
+        // ---- kW8 converters -------------------------------------------------------------------
+        const int cv = tid - 32 * T::kConvWarp0;
+        int kk = 0;
+        bool ok = true;
+        for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+            for (int kt = 0; kt < KT; ++kt, ++kk) {
+                const int st = kk % PS;
+                // Leave together on a timeout or an abort elsewhere (one answer for all).
+                const bool landed = !aborted() && mbar_wait(&wfull[st], (kk / PS) & 1);
+                ok = p.a_f16 ? widen_w8<true>(smem + st * T::kStageBytes, cv, landed)
+                             : widen_w8<false>(smem + st * T::kStageBytes, cv, landed);
+                if (!ok) {
+                    fail();
+                    break;
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&conv[st]);
             }
         }
     } else {
@@ -677,7 +812,10 @@ __global__ void __launch_bounds__(kPersistThreads, 1) linear_persist_kernel(
     __syncthreads();
     if (tid == 0) {
         // Copies issued but never consumed (only after a timeout): let them land before exit.
-        for (int kk = s_consumed; kk < s_issued; ++kk) mbar_wait(&full[kk % PS], (kk / PS) & 1);
+        for (int kk = s_consumed; kk < s_issued; ++kk) {
+            mbar_wait(&wfull[kk % PS], (kk / PS) & 1);
+            mbar_wait(&xfull[kk % PS], (kk / PS) & 1);
+        }
     }
     if (warp == 0) {
         tc_fence_after();
@@ -737,73 +875,121 @@ bool f16_map(CUtensorMap* out, const void* ptr, int rows, int cols, int box_rows
     return true;
 }
 
-template <int EPI, int RT, bool WLO>
+// Tensor map of the row-major [rows][cols] int8 weights, box 64 (k, bytes) x box_rows, no
+// swizzle: the box lands as box_rows dense rows of 64 bytes, which widen_w8 reads.
+bool i8_map(CUtensorMap* out, const void* ptr, int rows, int cols, int box_rows) {
+    using Key = std::tuple<const void*, int, int, int>;
+    static std::mutex mu;
+    static std::map<Key, CUtensorMap> cache;
+    const Key key{ptr, rows, cols, box_rows};
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) {
+        *out = it->second;
+        return true;
+    }
+    EncodeTiled enc = encoder();
+    if (!enc) return false;
+    const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)cols};
+    const cuuint32_t box[2] = {(cuuint32_t)KS, (cuuint32_t)box_rows};
+    const cuuint32_t elem[2] = {1, 1};
+    CUtensorMap m;
+    if (enc(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(ptr), dims, strides, box, elem,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return false;
+    if (cache.size() > 4096) cache.clear();
+    cache.emplace(key, m);
+    *out = m;
+    return true;
+}
+
+// The weight map(s) of a launch: the int8 weights (kW8) or the 16-bit plane(s).
+template <int WM>
+bool weight_maps(const LinearArgs& a, CUtensorMap* mw, CUtensorMap* mwl) {
+    if (WM == kW8) {
+        if (!i8_map(mw, a.w, a.N, a.K, FT)) return false;
+        *mwl = *mw;
+        return true;
+    }
+    const bool bf = !a.a_f16;
+    if (!f16_map(mw, a.wh, a.N, a.K, FT, bf)) return false;
+    if (WM == kW16Lo) return f16_map(mwl, a.wh_lo, a.N, a.K, FT, bf);
+    *mwl = *mw;
+    return true;
+}
+
+template <int EPI, int RT, int WM>
 bool launch_tma(const LinearArgs& a, cudaStream_t s) {
-    using T = TmaTile<RT, WLO>;
+    using T = TmaTile<RT, WM>;
     const bool bf = !a.a_f16;
     CUtensorMap mw, mwl, mx, mxl;
-    if (!f16_map(&mw, a.wh, a.N, a.K, FT, bf) || !f16_map(&mx, a.a, a.M, a.K, RT, bf)) return false;
-    if (WLO) {
-        if (!f16_map(&mwl, a.wh_lo, a.N, a.K, FT, bf)) return false;
-    } else {
-        mwl = mw;
-    }
+    if (!weight_maps<WM>(a, &mw, &mwl) || !f16_map(&mx, a.a, a.M, a.K, RT, bf)) return false;
     if (a.a_lo) {
         if (!f16_map(&mxl, a.a_lo, a.M, a.K, RT, bf)) return false;
     } else {
         mxl = mx;
     }
-    set_max_dynamic_smem(reinterpret_cast<const void*>(linear_tma_kernel<EPI, RT, WLO>), T::kSmem);
+    set_max_dynamic_smem(reinterpret_cast<const void*>(linear_tma_kernel<EPI, RT, WM>), T::kSmem);
     dim3 grid(a.N / FT, (a.M + RT - 1) / RT, a.splits);
-    launch_k(linear_tma_kernel<EPI, RT, WLO>, grid, dim3(kThreadsTma), T::kSmem, s, a, mw, mwl, mx, mxl);
+    launch_k(linear_tma_kernel<EPI, RT, WM>, grid, dim3(kThreadsTma), T::kSmem, s, a, mw, mwl, mx, mxl);
     return true;
 }
 
 // Prompt sizes: the persistent kernel, one CTA per SM over all tiles.
-template <int EPI, bool WLO>
+template <int EPI, int WM>
 bool launch_persist(const LinearArgs& a, cudaStream_t s) {
-    using T = PersistTile<WLO>;
+    using T = PersistTile<WM>;
     const bool bf = !a.a_f16;
     CUtensorMap mw, mwl, mx, mxl;
-    if (!f16_map(&mw, a.wh, a.N, a.K, FT, bf) || !f16_map(&mx, a.a, a.M, a.K, PT, bf)) return false;
-    mwl = mw;
-    if (WLO && !f16_map(&mwl, a.wh_lo, a.N, a.K, FT, bf)) return false;
+    if (!weight_maps<WM>(a, &mw, &mwl) || !f16_map(&mx, a.a, a.M, a.K, PT, bf)) return false;
     mxl = mx;
     if (a.a_lo && !f16_map(&mxl, a.a_lo, a.M, a.K, PT, bf)) return false;
-    set_max_dynamic_smem(reinterpret_cast<const void*>(linear_persist_kernel<EPI, WLO>), T::kSmem);
+    set_max_dynamic_smem(reinterpret_cast<const void*>(linear_persist_kernel<EPI, WM>), T::kSmem);
     int dev = 0, sms = 0;
     cudaGetDevice(&dev);
     if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms < 1) sms = 1;
     const int tiles = (a.N / FT) * ((a.M + PT - 1) / PT);
-    launch_k(linear_persist_kernel<EPI, WLO>, dim3(tiles < sms ? tiles : sms), dim3(kPersistThreads), T::kSmem, s, a,
+    launch_k(linear_persist_kernel<EPI, WM>, dim3(tiles < sms ? tiles : sms), dim3(T::kThreads), T::kSmem, s, a,
              mw, mwl, mx, mxl);
     return true;
 }
 
+// The weight form of a launch: 16-bit planes when the layer has them, else its int8 weights.
+int weight_form(const LinearArgs& a) { return a.wh_lo ? kW16Lo : (a.wh ? kW16 : kW8); }
+
 template <int EPI>
 bool launch_tma_rows(const LinearArgs& a, cudaStream_t s) {
-    if (a.M >= 4096 && a.splits == 1 && EPI != EPI_PARTIAL)
-        return a.wh_lo ? launch_persist<EPI, true>(a, s) : launch_persist<EPI, false>(a, s);
-    return a.wh_lo ? launch_tma<EPI, 32, true>(a, s) : launch_tma<EPI, 32, false>(a, s);
+    const int wm = weight_form(a);
+    if (a.M >= kPersistMinRows && a.splits == 1 && EPI != EPI_PARTIAL) {
+        if (wm == kW16Lo) return launch_persist<EPI, kW16Lo>(a, s);
+        return wm == kW16 ? launch_persist<EPI, kW16>(a, s) : launch_persist<EPI, kW8>(a, s);
+    }
+    if (wm == kW16Lo) return launch_tma<EPI, 32, kW16Lo>(a, s);
+    return wm == kW16 ? launch_tma<EPI, 32, kW16>(a, s) : launch_tma<EPI, 32, kW8>(a, s);
 }
 
 // The flow net's linears (bf16 planes, optional weight lo plane), decode-size rows only.
 template <int EPI>
 bool launch_tma_flow(const LinearArgs& a, cudaStream_t s) {
-    return a.wh_lo ? launch_tma<EPI, 32, true>(a, s) : launch_tma<EPI, 32, false>(a, s);
+    return a.wh_lo ? launch_tma<EPI, 32, kW16Lo>(a, s) : launch_tma<EPI, 32, kW16>(a, s);
 }
 
 }  // namespace
 
 bool linear_tc_supported(const LinearArgs& a) {
-    return a.wh != nullptr && a.M > 0 && a.N % FT == 0 && a.K % 8 == 0 && a.splits >= 1 &&
+    return (a.wh != nullptr || a.w != nullptr) && a.M > 0 && a.N % FT == 0 && a.K % 8 == 0 && a.splits >= 1 &&
            a.K % a.splits == 0 && (a.K / a.splits) % KS == 0;
 }
 
 bool launch_linear_tc(const LinearArgs& a, LinearEpi epi, cudaStream_t s) {
     if (!linear_tc_supported(a)) return false;
     const bool flow_epi = epi >= EPI_BIAS;
-    if (!flow_epi && !a.a_f16) return false;  // the layer stack's linears read f16 planes
+    // A 16-bit weight plane has the activations' type: the layer stack's f16 copies pair only
+    // with f16 planes. int8 weights are widened to whichever type the activations have.
+    if (!flow_epi && !a.a_f16 && a.wh) return false;
+    if (flow_epi && !a.wh) return false;  // the flow net's weights come as 16-bit planes
     switch (epi) {
         case EPI_F32: return launch_tma_rows<EPI_F32>(a, s);
         case EPI_QKV: return launch_tma_rows<EPI_QKV>(a, s);

@@ -337,6 +337,30 @@ void launch_i8_to_f16(const int8_t* x, __half* y, long long n, cudaStream_t s) {
     i8_to_f16_kernel<<<(int)(blocks < 4096 ? blocks : 4096), 256, 0, s>>>(x, y, n);
 }
 
+// 16 int8 -> 16 f16 per thread and step (one 16-byte load, two 16-byte stores).
+__global__ void widen_i8_kernel(I8Widen w) {
+    const long long stride = (long long)gridDim.x * blockDim.x;
+    for (int m = 0; m < 4; ++m) {
+        const long long chunks = w.n[m] / 16;
+        const uint4* src = reinterpret_cast<const uint4*>(w.src[m]);
+        uint4* dst = reinterpret_cast<uint4*>(w.dst[m]);
+        for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < chunks; i += stride) {
+            const uint4 q = src[i];
+            uint4 a, b;
+            i8x4_to_f16x4(q.x, a.x, a.y);
+            i8x4_to_f16x4(q.y, a.z, a.w);
+            i8x4_to_f16x4(q.z, b.x, b.y);
+            i8x4_to_f16x4(q.w, b.z, b.w);
+            dst[2 * i] = a;
+            dst[2 * i + 1] = b;
+        }
+    }
+}
+
+void launch_widen_i8(const I8Widen& w, cudaStream_t s) {
+    widen_i8_kernel<<<1184, 256, 0, s>>>(w);
+}
+
 void launch_bf16_to_f32(const __nv_bfloat16* x, float* y, long long n, cudaStream_t s) {
     const long long blocks = (n + 255) / 256;
     launch_k(bf16_to_f32_kernel, dim3((int)(blocks < 4096 ? blocks : 4096)), dim3(256), 0, s, x, y, n);
