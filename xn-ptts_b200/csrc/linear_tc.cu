@@ -584,6 +584,235 @@ __global__ void __launch_bounds__(kThreadsTma) linear_tma_kernel(const __grid_co
     }
 }
 
+// ---- decode-size linears on int8 weights, widened into tensor memory ----------------------------
+//
+// linear_i8_kernel: the kW8 form of linear_tma_kernel (one 128-feature x RT-row tile per CTA,
+// 512 threads, the same MMAs and epilogues) with the widened weights in tensor memory: the MMA
+// takes its A operand (the 128 x 16 weight slice of a k step) from TMEM, so neither the widening
+// nor the MMA's weight reads touch shared memory, and a stage in shared memory is only the int8
+// tile (8 KB) and the activation tiles (hi, lo).
+//   thread 0:     TMA producer; the int8 tiles of the first stages before the wait on the
+//                 predecessor grid (weights never change), the activation tiles after it.
+//   warps 4..11:  converters. Warp w takes TMEM lane quarter w % 4 (its rows: 32 (w % 4) + lane)
+//                 and half (w - 4) / 4 of the stage's 64 k: it reads the row's 32 int8 weights,
+//                 widens them in registers and stores them as 16 packed 16-bit pairs into the
+//                 stage's A slot (tcgen05.st), then waits for the stores (tcgen05.wait::st).
+//   thread 32:    MMA issuer, A from TMEM (lane = feature row, column c = k 2c, 2c + 1), B the
+//                 activation tile in shared memory.
+// The int8 tile is copied with the 64-byte swizzle (16-byte chunk c of row r at c ^ ((r / 2) % 4)),
+// so a quarter-warp's reads of 8 rows hit the eight distinct bank groups.
+//
+// TMEM: the accumulator (2 RT columns) and kStages A slots of 32 columns, 256 columns per CTA.
+// Shared memory (5 stages, 81 KB) keeps at most two CTAs of this kernel on an SM, so CTAs that
+// share an SM never ask for more than the SM's 512 columns (an allocation never waits, which could
+// otherwise deadlock against an early-launched successor holding TMEM while it waits on us).
+template <int RT>
+struct I8Tile {
+    static constexpr int kStages = 5;
+    static constexpr int kW8Bytes = FT * KS;      // int8 tile
+    static constexpr int kXBytes = RT * KS * 2;   // one activation plane
+    static constexpr int kStageBytes = kW8Bytes + 2 * kXBytes;
+    static constexpr int kXOffset = kW8Bytes;
+    static constexpr int kBarOffset = kStages * kStageBytes;
+    static constexpr int kSmem = 1024 + kBarOffset + 256;
+    static constexpr uint32_t kAccCols = 2 * RT;
+    static constexpr uint32_t kACols = KS / 2;    // one stage's A slot: 64 k as 32 packed pairs
+    static constexpr uint32_t kTmemCols = 256;
+    static_assert(kAccCols + kStages * kACols <= kTmemCols, "accumulator and A slots fit");
+    static_assert(kStageBytes % 1024 == 0 && kXBytes % 1024 == 0, "swizzled tiles stay 1024-byte aligned");
+    static_assert(32 * (FT + 4) * 4 <= kBarOffset, "the epilogue's staging tile fits");
+    static_assert(3 * (kSmem + 1024) > 228 * 1024, "at most two CTAs per SM (TMEM: 2 x 256 columns)");
+    static_assert((4 * kStages + 1) * 8 + 4 <= 256, "barriers fit the tail");
+};
+
+// D (TMEM) += A (TMEM) x B (smem), or D = A x B when accumulate is 0.
+__device__ __forceinline__ void tc_mma_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t b_desc, uint32_t idesc,
+                                          uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}"
+        ::"r"(tmem_d), "r"(tmem_a), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// 16 consecutive TMEM columns of this warp's 32 lanes from registers (tcgen05.st.32x32b.x16).
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+        "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};"
+        ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+          "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+        : "memory");
+}
+
+template <int EPI, int RT>
+__global__ void __launch_bounds__(kThreadsTma) linear_i8_kernel(const __grid_constant__ LinearArgs p,
+                                                                const __grid_constant__ CUtensorMap tm_w,
+                                                                const __grid_constant__ CUtensorMap tm_x,
+                                                                const __grid_constant__ CUtensorMap tm_xlo) {
+    using T = I8Tile<RT>;
+    constexpr int S = T::kStages;
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    const uint32_t raw = smem_u32(smem_raw);
+    const uint32_t base = (raw + 1023u) & ~1023u;
+    unsigned char* smem = smem_raw + (base - raw);
+    uint64_t* wfull = reinterpret_cast<uint64_t*>(smem + T::kBarOffset);  // int8 tile landed
+    uint64_t* xfull = wfull + S;                                           // activations landed
+    uint64_t* conv = xfull + S;                                            // A slot written
+    uint64_t* empty = conv + S;                                            // the stage's MMAs done
+    uint64_t* done = empty + S;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+    __shared__ int s_w_issued, s_issued, s_consumed;
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int n0 = blockIdx.x * FT, m0 = blockIdx.y * RT, z = blockIdx.z;
+    const int k_len = p.K / p.splits;
+    const int k0 = z * k_len;
+    const int KT = k_len / KS;
+    const bool has_lo = p.a_lo != nullptr;
+    const uint32_t x_tx = (has_lo ? 2u : 1u) * T::kXBytes;
+
+    if (tid == 0) {
+        s_w_issued = 0;
+        s_issued = 0;
+        s_consumed = 0;
+        for (int i = 0; i < S; ++i) {
+            mbar_init(&wfull[i], 1);
+            mbar_init(&xfull[i], 1);
+            mbar_init(&conv[i], kConvWarps);
+            mbar_init(&empty[i], 1);
+        }
+        mbar_init(done, 1);
+        fence_mbar_init();
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tm_w)) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tm_x)) : "memory");
+    }
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         smem_u32(tmem_slot)),
+                     "r"(T::kTmemCols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const uint32_t tmem_a = tmem + T::kAccCols;  // A slot of stage s: + s * kACols columns
+
+    if (tid == 0) stamp_mark(p.stamps, p.stamp, STAMP_ENTRY);
+    if (tid == 0) {
+        // ---- TMA producer ----------------------------------------------------------------------
+        const uint64_t pol_w = policy_evict_last();  // weights: reread every frame
+        const int pre = KT < S ? KT : S;
+        for (int kt = 0; kt < pre; ++kt) {
+            mbar_arrive_expect_tx(&wfull[kt], T::kW8Bytes);
+            tma_load_2d_hint(base + kt * T::kStageBytes, &tm_w, k0 + kt * KS, n0, &wfull[kt], pol_w);
+            s_w_issued = kt + 1;
+        }
+        grid_dep_wait();
+        stamp_mark(p.stamps, p.stamp, STAMP_START);
+        for (int kt = 0; kt < KT; ++kt) {
+            const int st = kt % S;
+            const uint32_t sa = base + st * T::kStageBytes;
+            if (kt >= pre) {
+                if (!mbar_wait(&empty[st], ((kt / S) & 1) ^ 1)) {
+                    set_error(p.err, DEV_ERR_TIMEOUT);
+                    break;
+                }
+                mbar_arrive_expect_tx(&wfull[st], T::kW8Bytes);
+                tma_load_2d_hint(sa, &tm_w, k0 + kt * KS, n0, &wfull[st], pol_w);
+                s_w_issued = kt + 1;
+            }
+            mbar_arrive_expect_tx(&xfull[st], x_tx);
+            tma_load_2d(sa + T::kXOffset, &tm_x, k0 + kt * KS, m0, &xfull[st]);
+            if (has_lo) tma_load_2d(sa + T::kXOffset + T::kXBytes, &tm_xlo, k0 + kt * KS, m0, &xfull[st]);
+            s_issued = kt + 1;
+        }
+    } else if (warp >= 4 && warp < 4 + kConvWarps) {
+        // ---- converters: int8 row -> 16-bit pairs in the stage's A slot --------------------------
+        const int quarter = warp & 3, half = (warp - 4) >> 2;
+        const int r = 32 * quarter + lane;  // this thread's weight row (TMEM lane)
+        const uint32_t lane_base = (uint32_t)(32 * quarter) << 16;
+        for (int kt = 0; kt < KT; ++kt) {
+            const int st = kt % S;
+            const bool landed = mbar_wait(&wfull[st], (kt / S) & 1);
+            if (__any_sync(0xffffffffu, !landed)) {  // the whole warp leaves together
+                set_error(p.err, DEV_ERR_TIMEOUT);
+                break;
+            }
+            const unsigned char* row = smem + st * T::kStageBytes + r * KS;
+            uint32_t v[16];
+#pragma unroll
+            for (int c2 = 0; c2 < 2; ++c2) {  // 16-byte chunks 2 half + c2 (k 16 (2 half + c2) ..)
+                const int c = 2 * half + c2;
+                const uint4 q = *reinterpret_cast<const uint4*>(row + ((c ^ ((r >> 1) & 3)) << 4));
+                if (p.a_f16) {
+                    i8x4_convert<true>(q.x, v[8 * c2 + 0], v[8 * c2 + 1]);
+                    i8x4_convert<true>(q.y, v[8 * c2 + 2], v[8 * c2 + 3]);
+                    i8x4_convert<true>(q.z, v[8 * c2 + 4], v[8 * c2 + 5]);
+                    i8x4_convert<true>(q.w, v[8 * c2 + 6], v[8 * c2 + 7]);
+                } else {
+                    i8x4_convert<false>(q.x, v[8 * c2 + 0], v[8 * c2 + 1]);
+                    i8x4_convert<false>(q.y, v[8 * c2 + 2], v[8 * c2 + 3]);
+                    i8x4_convert<false>(q.z, v[8 * c2 + 4], v[8 * c2 + 5]);
+                    i8x4_convert<false>(q.w, v[8 * c2 + 6], v[8 * c2 + 7]);
+                }
+            }
+            tmem_st16(tmem_a + lane_base + (uint32_t)(st * T::kACols + 16 * half), v);
+            asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&conv[st]);
+        }
+    } else if (tid == 32) {
+        // ---- MMA issuer --------------------------------------------------------------------
+        const uint32_t idesc1 = p.a_f16 ? idesc_f16<RT>() : idesc_bf16<RT>();
+        const uint32_t idesc2 = p.a_f16 ? idesc_f16<2 * RT>() : idesc_bf16<2 * RT>();
+        const uint32_t idesc = has_lo ? idesc2 : idesc1;
+        for (int kt = 0; kt < KT; ++kt) {
+            const int st = kt % S;
+            const uint32_t ph = (kt / S) & 1;
+            if (!mbar_wait(&conv[st], ph) || !mbar_wait(&xfull[st], ph)) {
+                set_error(p.err, DEV_ERR_TIMEOUT);
+                break;
+            }
+            tc_fence_after();
+            const uint64_t dx = sw128_desc(base + st * T::kStageBytes + T::kXOffset);
+            const uint32_t a = tmem_a + (uint32_t)(st * T::kACols);
+#pragma unroll
+            for (int kk = 0; kk < KS / 16; ++kk)  // 16 k per MMA: 8 A columns, 32 bytes of B
+                tc_mma_ts(tmem, a + 8 * kk, dx + 2 * kk, idesc, (kt | kk) ? 1u : 0u);
+            tc_commit(&empty[st]);
+            s_consumed = kt + 1;
+        }
+        tc_commit(done);  // arrives once every MMA issued above has completed
+    }
+    grid_dep_wait();  // the epilogue reads what predecessors wrote (a no-op once passed)
+    __syncwarp();
+
+    const bool got = mbar_wait(done, 0);
+    if (!got) set_error(p.err, DEV_ERR_TIMEOUT);
+    if (tid == 0) grid_dep_launch();
+    drain_tile<EPI, RT>(p, smem, tmem, n0, m0, z, got, has_lo);
+
+    if (tid == 0) stamp_mark(p.stamps, p.stamp, STAMP_END);
+    tc_fence_before();
+    __syncthreads();
+    if (tid == 0) {
+        // Copies issued but never consumed (only after a timeout): let them land before exit.
+        for (int kt = s_consumed; kt < s_w_issued; ++kt) mbar_wait(&wfull[kt % S], (kt / S) & 1);
+        for (int kt = s_consumed; kt < s_issued; ++kt) mbar_wait(&xfull[kt % S], (kt / S) & 1);
+    }
+    if (warp == 0) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                     "r"(T::kTmemCols)
+                     : "memory");
+    }
+}
+
 // ---- persistent prompt-size linears ----------------------------------------------------------
 //
 // One CTA per SM walks 128-feature x 128-row tiles (tile t = blockIdx.x + i * gridDim.x,
@@ -877,11 +1106,11 @@ bool f16_map(CUtensorMap* out, const void* ptr, int rows, int cols, int box_rows
 
 // Tensor map of the row-major [rows][cols] int8 weights, box 64 (k, bytes) x box_rows, no
 // swizzle: the box lands as box_rows dense rows of 64 bytes, which widen_w8 reads.
-bool i8_map(CUtensorMap* out, const void* ptr, int rows, int cols, int box_rows) {
-    using Key = std::tuple<const void*, int, int, int>;
+bool i8_map(CUtensorMap* out, const void* ptr, int rows, int cols, int box_rows, bool swizzle64 = false) {
+    using Key = std::tuple<const void*, int, int, int, bool>;
     static std::mutex mu;
     static std::map<Key, CUtensorMap> cache;
-    const Key key{ptr, rows, cols, box_rows};
+    const Key key{ptr, rows, cols, box_rows, swizzle64};
     std::lock_guard<std::mutex> lock(mu);
     auto it = cache.find(key);
     if (it != cache.end()) {
@@ -896,8 +1125,8 @@ bool i8_map(CUtensorMap* out, const void* ptr, int rows, int cols, int box_rows)
     const cuuint32_t elem[2] = {1, 1};
     CUtensorMap m;
     if (enc(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(ptr), dims, strides, box, elem,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_NONE,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
         return false;
     if (cache.size() > 4096) cache.clear();
     cache.emplace(key, m);
@@ -937,6 +1166,20 @@ bool launch_tma(const LinearArgs& a, cudaStream_t s) {
     return true;
 }
 
+template <int EPI, int RT>
+bool launch_i8(const LinearArgs& a, cudaStream_t s) {
+    using T = I8Tile<RT>;
+    const bool bf = !a.a_f16;
+    CUtensorMap mw, mx, mxl;
+    if (!i8_map(&mw, a.w, a.N, a.K, FT, true) || !f16_map(&mx, a.a, a.M, a.K, RT, bf)) return false;
+    mxl = mx;
+    if (a.a_lo && !f16_map(&mxl, a.a_lo, a.M, a.K, RT, bf)) return false;
+    set_max_dynamic_smem(reinterpret_cast<const void*>(linear_i8_kernel<EPI, RT>), T::kSmem);
+    dim3 grid(a.N / FT, (a.M + RT - 1) / RT, a.splits);
+    launch_k(linear_i8_kernel<EPI, RT>, grid, dim3(kThreadsTma), T::kSmem, s, a, mw, mx, mxl);
+    return true;
+}
+
 // Prompt sizes: the persistent kernel, one CTA per SM over all tiles.
 template <int EPI, int WM>
 bool launch_persist(const LinearArgs& a, cudaStream_t s) {
@@ -967,7 +1210,14 @@ bool launch_tma_rows(const LinearArgs& a, cudaStream_t s) {
         return wm == kW16 ? launch_persist<EPI, kW16>(a, s) : launch_persist<EPI, kW8>(a, s);
     }
     if (wm == kW16Lo) return launch_tma<EPI, 32, kW16Lo>(a, s);
-    return wm == kW16 ? launch_tma<EPI, 32, kW16>(a, s) : launch_tma<EPI, 32, kW8>(a, s);
+    if (wm == kW16) return launch_tma<EPI, 32, kW16>(a, s);
+    // int8 weights at decode sizes: widened into TMEM (linear_i8_kernel), or with
+    // PTTS_B200_I8=smem in place in shared memory (linear_tma_kernel's kW8 form).
+    static const bool smem_form = [] {
+        const char* e = getenv("PTTS_B200_I8");
+        return e && e[0] == 's';
+    }();
+    return smem_form ? launch_tma<EPI, 32, kW8>(a, s) : launch_i8<EPI, 32>(a, s);
 }
 
 // The flow net's linears (bf16 planes, optional weight lo plane), decode-size rows only.
