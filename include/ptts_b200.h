@@ -272,11 +272,24 @@ int ptts_b200_load_gguf(ptts_b200_model* model, ptts_b200_flow* flow, const char
  * is too small. */
 int ptts_b200_gguf_remap_key(const char* name, char* out, int out_size);
 
+/* The layer scales of StreamingTransformerLayer::forward (transformer.rs:616-618, :632-633;
+ * LayerScale::forward, layer_scale.rs:14-16): x += scale1 * attn(LN1 x) and
+ * x += scale2 * ff(LN2 x), one factor per channel ([d_model] f32, host). Mimi's layers have
+ * them (its transformer is built with a layer_scale); the flow LM's do not. NULL clears one.
+ * They are folded into out_proj's and linear2's per-row scales, so a layer reloaded later keeps
+ * them. */
+int ptts_b200_model_set_layer_scale(ptts_b200_model* model, int layer, const float* scale1_host,
+                                    const float* scale2_host);
+
 /* StreamingTransformer::forward (transformer.rs:742-808) for a ragged batch of independent
  * streams: x [n_rows][d_model] bf16 (device) -> y [n_rows][d_model] f32 (device); per layer
  * x += attn(LN1 x); x += W2 GELU(W1 LN2 x). Sequence i is stream streams_host[i] with
  * rows_host[i] rows (a prompt when > 1, a host-position decode step when 1). Lengths advance
- * by rows_host[i] at the end. */
+ * by rows_host[i] at the end. Windowed streams (ptts_b200_kv_set_window) run Mimi's layers
+ * (MimiStreamingMultiheadAttention::forward, transformer.rs:419-468: positions from the
+ * stream's absolute offset, keys within the last `context` positions, the mask of
+ * transformer.rs:762-785); load such a model with ptts_b200_model_load_layer_f32 and
+ * ptts_b200_model_set_layer_scale. */
 int ptts_b200_forward(ptts_b200_model* model, ptts_b200_kv* kv, const void* x,
                       const int32_t* streams_host, const int32_t* rows_host, int n_seq, float* y,
                       void* cuda_stream);

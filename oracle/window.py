@@ -1,4 +1,5 @@
-"""TEST INFRASTRUCTURE ONLY: numpy restatement of Mimi's windowed streaming attention.
+"""TEST INFRASTRUCTURE ONLY: numpy restatement of Mimi's windowed streaming attention and of
+the Mimi transformer layer around it.
 
 Follows the reference after in_proj: MimiStreamingMultiheadAttention::forward
 (ptts/src/transformer.rs:419-468: RoPE at the cache's absolute offset, append, scores scaled by
@@ -6,8 +7,12 @@ Follows the reference after in_proj: MimiStreamingMultiheadAttention::forward
 trim keeps the last context - 1 rows, absolute_offset counts every row) and the mask of
 StreamingTransformer::forward (transformer.rs:762-785: key visible iff 0 <= query - key <
 context). RoPE as rope.rs:37-95 (interleaved pairs, f32 angle). With `bf16`, rotated k and v
-are rounded to bf16 as they enter the cache (the library's bf16 cache). Parity unpinned, like
-the rest of the oracle; only tests use it.
+are rounded to bf16 as they enter the cache (the library's bf16 cache). The layer
+(mimi_layer) follows MimiStreamingMultiheadAttention::forward (transformer.rs:419-468: in_proj
+without bias, the packed [t, 3, heads, D] split, RoPE, the cache, out_proj) inside
+StreamingTransformerLayer::forward (transformer.rs:591-634: LayerNorm eps 1e-5, the layer
+scales of layer_scale.rs:14-16, GELU erf or the tanh form of transformer.rs:498-503). Parity
+unpinned, like the rest of the oracle; only tests use it.
 """
 from __future__ import annotations
 
@@ -68,3 +73,48 @@ def attend(cache: KvCache, q, k, v, inv_freq, *, bf16: bool):
     cache.k, cache.v = K[max(K.shape[0] - keep, 0):], V[max(V.shape[0] - keep, 0):]
     cache.offset += t
     return out
+
+
+def layer_norm(x, g, b, eps=1e-5):
+    x = np.asarray(x, np.float64)
+    mu = x.mean(-1, keepdims=True)
+    var = ((x - mu) ** 2).mean(-1, keepdims=True)
+    return (x - mu) / np.sqrt(var + eps) * g + b
+
+
+def gelu(x, form="erf"):
+    x = np.asarray(x, np.float64)
+    if form == "tanh":  # x sigmoid(2u), u = sqrt(2/pi) (x + 0.044715 x^3)
+        u2 = (x * x * 0.07135482 + 1.595769) * x
+        return x / (1.0 + np.exp(-u2))
+    from scipy.special import erf
+    return 0.5 * x * (1.0 + erf(x / np.sqrt(2.0)))
+
+
+def mimi_layer(t: dict, prefix: str, x, cache: KvCache, inv_freq, heads: int, *, bf16: bool, gelu_form="erf"):
+    """One StreamingTransformerLayer of Mimi on one stream's rows x [t, d] (float64): returns
+    the new rows; the stream's cache for this layer is appended and trimmed."""
+    g = lambda n: np.asarray(t[prefix + n], np.float64)
+    rows, d = x.shape
+    D = d // heads
+    h = layer_norm(x, g("norm1.weight"), g("norm1.bias"))
+    packed = (h @ g("self_attn.in_proj.weight").T).reshape(rows, 3, heads, D)
+    a = attend(cache, packed[:, 0], packed[:, 1], packed[:, 2], inv_freq, bf16=bf16)
+    a = a @ g("self_attn.out_proj.weight").T
+    if prefix + "layer_scale_1.scale" in t:
+        a = a * g("layer_scale_1.scale")
+    x = x + a
+    h = layer_norm(x, g("norm2.weight"), g("norm2.bias"))
+    f = gelu(h @ g("linear1.weight").T, gelu_form) @ g("linear2.weight").T
+    if prefix + "layer_scale_2.scale" in t:
+        f = f * g("layer_scale_2.scale")
+    return x + f
+
+
+def mimi_forward(t: dict, layers: int, x, caches, inv_freq, heads: int, *, bf16: bool, gelu_form="erf"):
+    """StreamingTransformer::forward (transformer.rs:742-808) of Mimi's layers on one stream:
+    caches[l] is the stream's KvCache of layer l."""
+    x = np.asarray(x, np.float64)
+    for l in range(layers):
+        x = mimi_layer(t, f"layers.{l}.", x, caches[l], inv_freq, heads, bf16=bf16, gelu_form=gelu_form)
+    return x

@@ -255,3 +255,38 @@ def test_with_seq_budget_known_answers():
         out = np.zeros((b, c["budget"], h, d), np.float32)
         out[:, : c["used"]] = k[:, : c["used"]]
         np.testing.assert_array_equal(out.ravel(), np.array(c["want_k"], np.float32))
+
+
+def test_mimi_layer_restatement_agrees_with_the_flow_lm_layer(ptts, oracle):
+    """The numpy Mimi layer (oracle/window.py) with an unbounded window and no layer scales is
+    the flow-LM layer the C oracle restates (transformer.rs:591-634 around either attention):
+    same weights (int8 * row scale as f32), same bf16 cache rounding, prompt then decode rows."""
+    from oracle import window as ow
+    cfg = ptts.FlowLMConfig(num_layers=2)
+    w = ptts.random_weights(cfg, 95)
+    t = {}
+    for l in range(cfg.num_layers):
+        p = f"layers.{l}."
+        t[p + "self_attn.in_proj.weight"] = w.w_qkv[l].astype(np.float32) * w.s_qkv[l][:, None]
+        t[p + "self_attn.out_proj.weight"] = w.w_out[l].astype(np.float32) * w.s_out[l][:, None]
+        t[p + "linear1.weight"] = w.w_ff1[l].astype(np.float32) * w.s_ff1[l][:, None]
+        t[p + "linear2.weight"] = w.w_ff2[l].astype(np.float32) * w.s_ff2[l][:, None]
+        t[p + "norm1.weight"], t[p + "norm1.bias"] = w.ln1_g[l], w.ln1_b[l]
+        t[p + "norm2.weight"], t[p + "norm2.bias"] = w.ln2_g[l], w.ln2_b[l]
+    om = oracle.Model(cfg, w)
+    inv = oracle.rope_inv_freq(64)
+    # Without the bf16 cache the two restatements are the same arithmetic (float64 against f32:
+    # 1e-6); with it, the two sides' keys differ in the last f32 bits before rounding, and a few
+    # bf16 roundings flip (1.5e-4).
+    for store, bf16, tol in ((0, False, 5e-6), (oracle.ROUND_KV, True, 1e-3)):
+        kc = np.zeros((cfg.num_layers, 1, 32, 8, 64), np.float32)
+        vc = np.zeros_like(kc)
+        caches = [ow.KvCache(10 ** 9) for _ in range(cfg.num_layers)]
+        rng = np.random.default_rng(95)
+        length = np.zeros(1, np.int32)
+        for rows in (20, 1, 1, 3):
+            x = oracle.round_bf16(rng.normal(size=(rows, 512)).astype(np.float32))
+            want = om.forward(x, kc, vc, length, [0], [0, rows], store=store)
+            got = ow.mimi_forward(t, cfg.num_layers, x, caches, inv, 8, bf16=bf16)
+            length += rows
+            assert np.abs(got - want).max() / np.abs(want).max() < tol, (store, rows)

@@ -68,8 +68,10 @@ def test_windowed_streams_refuse_what_they_cannot_do(ptts, cuda):
     cfg = ptts.FlowLMConfig(num_layers=1)
     model = ptts.Transformer(cfg)
     model.load(ptts.random_weights(cfg, 1))
-    with pytest.raises(ptts.PttsError, match="ptts_b200_attend"):
-        model.forward(kv, torch.randn(1, 512).bfloat16().to(cuda), [0], [1])
+    # The device step is the flow LM's (transformer.rs:603-605): windowed streams go through
+    # ptts_b200_forward (tests/test_mimi.py) or the attention op.
+    with pytest.raises(ptts.PttsError, match="not the device step"):
+        model.step(kv, [0], torch.randn(1, 512).bfloat16().to(cuda))
     # Positions keep growing past the capacity through decode calls.
     for _ in range(10):
         ptts.attend(kv, 0, row(1), row(1), row(1), [0], [1])

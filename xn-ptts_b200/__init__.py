@@ -49,7 +49,7 @@ EXPORTS = (
     "ptts_b200_kv_start_ring", "ptts_b200_kv_set_ring_slot", "ptts_b200_kv_evict",
     "ptts_b200_model_config", "ptts_b200_model_load_layer_f32", "ptts_b200_model_load_layer_q8_0",
     "ptts_b200_load_gguf", "ptts_b200_gguf_remap_key", "ptts_b200_kv_set_window",
-    "ptts_b200_model_stamps", "ptts_b200_model_stamps_read",
+    "ptts_b200_model_stamps", "ptts_b200_model_stamps_read", "ptts_b200_model_set_layer_scale",
 )
 
 
@@ -162,6 +162,7 @@ def lib() -> ctypes.CDLL:
         L.ptts_b200_model_config.argtypes = [P, ctypes.POINTER(Config)]
         L.ptts_b200_model_load_layer_f32.argtypes = [P, I, ctypes.POINTER(LayerWeightsF32)]
         L.ptts_b200_model_load_layer_q8_0.argtypes = [P, I, ctypes.POINTER(LayerWeightsQ8)]
+        L.ptts_b200_model_set_layer_scale.argtypes = [P, I, P, P]
         L.ptts_b200_load_gguf.argtypes = [P, P, ctypes.c_char_p]
         L.ptts_b200_gguf_remap_key.argtypes = [ctypes.c_char_p, ctypes.c_char_p, I]
         L.ptts_b200_kv_set_window.argtypes = [P, IP, I, I, P]
@@ -452,6 +453,36 @@ class FlowLMConfig:
 # The 31m and 40m flow LMs: 512 wide, 8 heads, ff 2048, theta 10000; 6 vs 9 layers.
 PHONON_31M = FlowLMConfig(num_layers=6)
 PHONON_40M = FlowLMConfig(num_layers=9)
+# Mimi's transformers (encoder and decoder; MimiConfig, mimi.rs:34-40, with the values of
+# ptts-wasm/js/gpu/support.js:13-14 and ptts/tests/fixtures/config.json:33-37): 512 wide, 8 heads,
+# 2 layers, ff 2048, theta 10000, windowed attention over the last 250 positions, layer scale.
+MIMI_TRANSFORMER = FlowLMConfig(num_layers=2)
+MIMI_CONTEXT = 250
+
+
+def random_mimi_tensors(cfg: FlowLMConfig, seed: int, *, layer_scale: float = 0.01) -> dict:
+    """Random-init Mimi transformer tensors under the checkpoint's names: linears U(-1/sqrt(in),
+    1/sqrt(in)) (torch's default), LayerNorm affine near (1, 0), layer scales near `layer_scale`."""
+    rng = np.random.default_rng(seed)
+    d, ff = cfg.d_model, cfg.dim_feedforward
+    out = {}
+
+    def lin(n, k):
+        b = 1.0 / np.sqrt(k)
+        return rng.uniform(-b, b, (n, k)).astype(np.float32)
+
+    for i in range(cfg.num_layers):
+        p = f"layers.{i}."
+        out[p + "self_attn.in_proj.weight"] = lin(3 * d, d)
+        out[p + "self_attn.out_proj.weight"] = lin(d, d)
+        out[p + "linear1.weight"] = lin(ff, d)
+        out[p + "linear2.weight"] = lin(d, ff)
+        for n in ("norm1", "norm2"):
+            out[p + n + ".weight"] = rng.uniform(0.8, 1.2, d).astype(np.float32)
+            out[p + n + ".bias"] = rng.normal(0.0, 0.05, d).astype(np.float32)
+        for n in ("layer_scale_1", "layer_scale_2"):
+            out[p + n + ".scale"] = (layer_scale * rng.uniform(0.5, 1.5, d)).astype(np.float32)
+    return out
 
 
 class Transformer:
@@ -496,6 +527,30 @@ class Transformer:
         keep = {k: np.ascontiguousarray(w[k], dtype=np.float32) for k in self._DENSE}
         lw = LayerWeightsF32(*[keep[n].ctypes.data for n in self._DENSE])
         _check(lib().ptts_b200_model_load_layer_f32(self._h, layer, ctypes.byref(lw)))
+
+    def set_layer_scale(self, layer: int, scale1=None, scale2=None):
+        """LayerScale factors of one layer (ptts_b200_model_set_layer_scale): [d_model] each, or
+        None for none."""
+        keep = [None if v is None else np.ascontiguousarray(v, dtype=np.float32) for v in (scale1, scale2)]
+        for v in keep:
+            if v is not None and v.shape != (self.cfg.d_model,):
+                raise PttsError(ERR_ARG, f"a layer scale has {self.cfg.d_model} entries, not {v.shape}")
+        ptrs = [None if v is None else v.ctypes.data_as(P) for v in keep]
+        _check(lib().ptts_b200_model_set_layer_scale(self._h, layer, *ptrs))
+
+    def load_mimi(self, tensors: dict):
+        """A Mimi transformer's layers under the checkpoint's names (mimi.rs:359-360 and
+        transformer.rs:411-412, 549-563): layers.{i}.self_attn.in_proj.weight [3d, d],
+        self_attn.out_proj.weight, linear1.weight, linear2.weight (f32, no biases), norm1/norm2
+        weight and bias, layer_scale_1.scale and layer_scale_2.scale."""
+        for i in range(self.cfg.num_layers):
+            p = f"layers.{i}."
+            self.load_layer_f32(i, {
+                "in_proj": tensors[p + "self_attn.in_proj.weight"], "out_proj": tensors[p + "self_attn.out_proj.weight"],
+                "linear1": tensors[p + "linear1.weight"], "linear2": tensors[p + "linear2.weight"],
+                "norm1_weight": tensors[p + "norm1.weight"], "norm1_bias": tensors[p + "norm1.bias"],
+                "norm2_weight": tensors[p + "norm2.weight"], "norm2_bias": tensors[p + "norm2.bias"]})
+            self.set_layer_scale(i, tensors.get(p + "layer_scale_1.scale"), tensors.get(p + "layer_scale_2.scale"))
 
     def load_layer_q8_0(self, layer: int, w: dict):
         """GGUF q8_0 block bytes for the four linears (uint8 arrays), f32 norms."""

@@ -259,6 +259,10 @@ struct ptts_b200_model {
         // Layers loaded from f32 or q8_0 weights have no int8 copy: h_* hold f16(W / s_row) and
         // l_* the f16 remainders, s_row a power of two per output row (in s_*).
         DevBuf l_qkv, l_out, l1, l2;
+        // out_proj's and linear2's per-row scales as loaded, and the layer scales (LayerScale,
+        // layer_scale.rs:14-16; empty: none) folded into them: s_out = base_out * ls1 and
+        // s2 = base_2 * ls2, since ls * (x W^T) = x (ls W)^T row by row.
+        std::vector<float> base_out, base_2, ls1, ls2;
         bool loaded = false;
     };
     std::vector<std::unique_ptr<Layer>> layers;
@@ -355,14 +359,16 @@ long long attended_keys(const ptts_b200_kv* kv, int st) {
     return len + 1;
 }
 
-// The layer stack reads RoPE factors from a table of `capacity` positions, while a windowed
-// stream's position grows without bound: windowed streams run through the attention op.
+// Windowed streams (Mimi) run through ptts_b200_forward and the attention op, not the device
+// step: like the reference's, whose device-position step runs flow-LM attention only
+// (transformer.rs:603-605).
 void refuse_window(const ptts_b200_kv* kv, const int32_t* streams, int n) {
     for (int i = 0; i < n; ++i)
         if (kv->is_window(streams[i]))
             fail(PTTS_B200_ERR_UNSUPPORTED,
                  "stream " + std::to_string(streams[i]) +
-                     " is windowed: windowed streams run through ptts_b200_attend, not the layer stack");
+                     " is windowed: windowed streams run through ptts_b200_forward or ptts_b200_attend, "
+                     "not the device step");
 }
 
 void refuse_ring_prompt(const ptts_b200_kv* kv, const int32_t* streams, int n, bool decode) {
@@ -616,6 +622,7 @@ void run_layers(const ptts_b200_model* m, const ptts_b200_kv* kv, bool decode, c
         a.capacity = kv->capacity;
         require(m->rope_rows >= kv->capacity, PTTS_B200_ERR_STATE, "RoPE table shorter than the cache");
         a.rope = m->rope.as<float2>();
+        a.rope_rows = m->rope_rows;
         a.err = err;
         stamp(a, "in_proj");
         require(launch_linear(a, EPI_QKV, s), PTTS_B200_ERR_UNSUPPORTED, "no kernel for in_proj's shape");
@@ -661,6 +668,8 @@ void run_layers(const ptts_b200_model* m, const ptts_b200_kv* kv, bool decode, c
 // so it is dropped when the table moves.
 void ensure_rope(ptts_b200_model* m, int rows, cudaStream_t s) {
     if (m->rope_rows >= rows) return;
+    // Grown geometrically (windowed streams ask for one more position every frame).
+    if (m->rope_rows > 0) rows = std::max(rows, std::min(2 * m->rope_rows, m->rope_rows + (1 << 20)));
     CK(cudaStreamSynchronize(s));
     m->step.reset();
     m->frame.reset();
@@ -698,7 +707,7 @@ uint16_t f16_bits(float f) {
 // s = 2^ceil(log2(max |W_row|)) per row, so W/s is exact to 22 significant bits for weights
 // within 2^-14 of their row's largest (q8_0 weights, 18 bits, are exact); lo is dropped when it
 // is all zero.
-void upload_dense(DevBuf& hi, DevBuf& lo, DevBuf& scale, const float* w, size_t n, size_t k) {
+std::vector<float> upload_dense(DevBuf& hi, DevBuf& lo, DevBuf& scale, const float* w, size_t n, size_t k) {
     std::vector<uint16_t> h(n * k), l(n * k);
     std::vector<float> sc(n);
     bool any_lo = false;
@@ -719,6 +728,20 @@ void upload_dense(DevBuf& hi, DevBuf& lo, DevBuf& scale, const float* w, size_t 
     CK(cudaMemcpy(hi.need(n * k * 2), h.data(), n * k * 2, cudaMemcpyHostToDevice));
     if (any_lo) CK(cudaMemcpy(lo.need(n * k * 2), l.data(), n * k * 2, cudaMemcpyHostToDevice));
     CK(cudaMemcpy(scale.need(n * 4), sc.data(), n * 4, cudaMemcpyHostToDevice));
+    return sc;
+}
+
+// Uploads out_proj's and linear2's effective row scales: the loaded ones times the layer scales.
+void apply_layer_scale(ptts_b200_model::Layer& L) {
+    auto put = [](DevBuf& dst, const std::vector<float>& base, const std::vector<float>& ls) {
+        if (base.empty()) return;
+        std::vector<float> e(base);
+        if (!ls.empty())
+            for (size_t i = 0; i < e.size(); ++i) e[i] *= ls[i];
+        CK(cudaMemcpy(dst.need(e.size() * 4), e.data(), e.size() * 4, cudaMemcpyHostToDevice));
+    };
+    put(L.s_out, L.base_out, L.ls1);
+    put(L.s2, L.base_2, L.ls2);
 }
 
 // GGUF q8_0 blocks (34 bytes: f16 d, then 32 int8 q) of an [n][k] weight -> f32 W = q * d.
@@ -748,14 +771,15 @@ void load_dense_layer(ptts_b200_model* model, int layer, const float* in_proj, c
     auto& L = *model->layers[layer];
     for (DevBuf* b : {&L.w_qkv, &L.w_out, &L.w1, &L.w2, &L.l_qkv, &L.l_out, &L.l1, &L.l2}) b->release();
     upload_dense(L.h_qkv, L.l_qkv, L.s_qkv, in_proj, nqkv, dm);
-    upload_dense(L.h_out, L.l_out, L.s_out, out_proj, dm, hd);
+    L.base_out = upload_dense(L.h_out, L.l_out, L.s_out, out_proj, dm, hd);
     upload_dense(L.h1, L.l1, L.s1, linear1, ff, dm);
-    upload_dense(L.h2, L.l2, L.s2, linear2, dm, ff);
+    L.base_2 = upload_dense(L.h2, L.l2, L.s2, linear2, dm, ff);
     auto put = [](DevBuf& b, const void* src, size_t n) { CK(cudaMemcpy(b.need(n), src, n, cudaMemcpyHostToDevice)); };
     put(L.ln1g, n1w, dm * 4);
     put(L.ln1b, n1b, dm * 4);
     put(L.ln2g, n2w, dm * 4);
     put(L.ln2b, n2b, dm * 4);
+    apply_layer_scale(L);
     CK(cudaDeviceSynchronize());
     L.loaded = true;
 }
@@ -1330,10 +1354,15 @@ int ptts_b200_model_load_layer(ptts_b200_model* model, int layer,
         put(L.s_qkv, w->in_proj_scale_host, nqkv * 4);
         put(L.w_out, w->out_proj_host, dm * hd);
         put(L.s_out, w->out_proj_scale_host, dm * 4);
+        const float* so = static_cast<const float*>(w->out_proj_scale_host);
+        L.base_out.assign(so, so + dm);
         put(L.w1, w->linear1_host, ff * dm);
         put(L.s1, w->linear1_scale_host, ff * 4);
         put(L.w2, w->linear2_host, dm * ff);
         put(L.s2, w->linear2_scale_host, dm * 4);
+        const float* s2 = static_cast<const float*>(w->linear2_scale_host);
+        L.base_2.assign(s2, s2 + dm);
+        apply_layer_scale(L);
         put(L.ln1g, w->norm1_weight_host, dm * 4);
         put(L.ln1b, w->norm1_bias_host, dm * 4);
         put(L.ln2g, w->norm2_weight_host, dm * 4);
@@ -1356,6 +1385,29 @@ int ptts_b200_model_load_layer(ptts_b200_model* model, int layer,
         check_launch();
         CK(cudaDeviceSynchronize());
         L.loaded = true;
+    });
+}
+
+int ptts_b200_model_set_layer_scale(ptts_b200_model* model, int layer, const float* scale1_host,
+                                    const float* scale2_host) {
+    return guarded([&] {
+        require(model != nullptr, PTTS_B200_ERR_ARG, "model is NULL");
+        require(layer >= 0 && layer < model->cfg.num_layers, PTTS_B200_ERR_ARG, "layer out of range");
+        const size_t dm = model->cfg.d_model;
+        auto take = [&](const float* src, std::vector<float>& dst) {
+            if (!src) {
+                dst.clear();
+                return;
+            }
+            for (size_t i = 0; i < dm; ++i) require(std::isfinite(src[i]), PTTS_B200_ERR_ARG, "a layer scale is not finite");
+            dst.assign(src, src + dm);
+        };
+        DeviceScope scope(model->device);
+        auto& L = *model->layers[layer];
+        take(scale1_host, L.ls1);
+        take(scale2_host, L.ls2);
+        apply_layer_scale(L);
+        CK(cudaDeviceSynchronize());
     });
 }
 
@@ -1402,11 +1454,19 @@ int ptts_b200_forward(ptts_b200_model* model, ptts_b200_kv* kv, const void* x,
         bool decode = true;
         for (int i = 0; i < n_seq; ++i) decode = decode && rows_host[i] == 1;
         refuse_ring_prompt(kv, streams_host, n_seq, decode);
-        refuse_window(kv, streams_host, n_seq);
         DeviceScope scope(model->device);
         cudaStream_t s = as_stream(cuda_stream);
         const ptts_b200_config& c = model->cfg;
-        ensure_rope(model, kv->capacity, s);
+        // RoPE factors for every position of the call: a windowed stream's (Mimi's
+        // absolute_offset) grows past the capacity.
+        long long rope_need = kv->capacity;
+        bool windowed = false;
+        for (int i = 0; i < n_seq; ++i)
+            if (kv->is_window(streams_host[i])) {
+                windowed = true;
+                rope_need = std::max<long long>(rope_need, (long long)kv->h_len[streams_host[i]] + rows_host[i]);
+            }
+        ensure_rope(model, (int)rope_need, s);
         std::vector<int32_t> packed(streams_host, streams_host + n_seq);
         packed.insert(packed.end(), offsets.begin(), offsets.end());
         int32_t* d = static_cast<int32_t*>(model->seq_stream.need(sizeof(int32_t) * packed.size()));
@@ -1420,6 +1480,7 @@ int ptts_b200_forward(ptts_b200_model* model, ptts_b200_kv* kv, const void* x,
             const std::vector<int2> t = make_tiles(offsets);
             tiles.dev = static_cast<int2*>(model->tiles.need(sizeof(int2) * t.size()));
             tiles.n = (int)t.size();
+            tiles.windowed = windowed;
             model->staging.upload(const_cast<int2*>(tiles.dev), t.data(), sizeof(int2) * t.size(), s);
         }
         // The residual stream lives in the caller's output y.

@@ -276,6 +276,7 @@ struct LinearArgs {
     // (cos, sin)(f32(pos) * inv_freq[i]) at [pos][i] for pos < capacity (launch_rope_table):
     // the RoPE factors of the QKV epilogue, computed once per model instead of per element.
     const float2* rope;
+    int rope_rows;  // positions in the table (>= capacity; more for windowed streams)
     uint32_t* err;
 };
 // N must be a multiple of 64 and K / splits a multiple of 64. launch_linear runs the TMA-fed

@@ -289,7 +289,7 @@ __global__ void __launch_bounds__(kThreads) linear_kernel(LinearArgs p) {
                 sid[mi][h] = m < p.M ? p.row_stream[m] : 0;
                 const int rpos = m < p.M ? p.row_pos[m] : 0;
                 pos[mi][h] = m < p.M ? p.row_slot[m] : 0;  // cache slot
-                const long long trow = (long long)min(max(rpos, 0), p.capacity - 1) * kMaxPairs;
+                const long long trow = (long long)min(max(rpos, 0), p.rope_rows - 1) * kMaxPairs;
 #pragma unroll
                 for (int ni = 0; ni < NI; ++ni)
                     rt[mi][h][ni] = rotated ? __ldg(p.rope + trow + ((n0 + col0 + ni * 8 + 2 * t) % kHeadDim) / 2)

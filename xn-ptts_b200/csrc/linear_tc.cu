@@ -284,7 +284,7 @@ __device__ __forceinline__ void qkv_rows(const LinearArgs& p, const float* st, i
     for (int i = 0; i < kRowsPerWarp; ++i) {
         const int pos = __shfl_sync(0xffffffffu, pos_l, warp + kEpiWarps * i);
         t[i] = region != 2 ? __ldg(reinterpret_cast<const float4*>(
-                                 p.rope + (long long)min(max(pos, 0), p.capacity - 1) * kMaxPairs + (d >> 1)))
+                                 p.rope + (long long)min(max(pos, 0), p.rope_rows - 1) * kMaxPairs + (d >> 1)))
                            : make_float4(1.f, 0.f, 1.f, 0.f);
     }
 #pragma unroll
