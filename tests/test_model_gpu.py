@@ -224,10 +224,14 @@ def test_two_lane_steps_match_the_oracle(ptts, oracle, cuda):
     assert max(errs) < TOL
 
 
-@pytest.mark.parametrize("env", [{"PTTS_B200_GEMM": "mma"}, {"PTTS_B200_PREFILL": "core"}],
-                         ids=["mma-sync-linears", "cuda-core-prefill"])
+@pytest.mark.parametrize("env", [{"PTTS_B200_GEMM": "mma"}, {"PTTS_B200_PREFILL": "core"},
+                                 {"PTTS_B200_PREFILL": "tc1"}, {"PTTS_B200_WEIGHTS": "f16"},
+                                 {"PTTS_B200_I8": "smem"}],
+                         ids=["mma-sync-linears", "cuda-core-prefill", "one-head-tc-prefill",
+                              "f16-weight-copies", "int8-widened-in-smem"])
 def test_kernel_variants_match_the_oracle(ptts, oracle, cuda, monkeypatch, env):
-    """The opt-in variants (mma.sync linears; the CUDA-core prefill attention) on the same
+    """The opt-in variants (mma.sync linears; the CUDA-core and the one-head-per-CTA tcgen05
+    prefill attention; f16 weight copies; int8 weights widened in shared memory) on the same
     prefill + decode as the default path, against the oracle."""
     import torch
     for k, v in env.items():

@@ -467,10 +467,16 @@ void attention(const ptts_b200_kv* kv, int layer, bool decode, const RowPlan& pl
         a.rows = n_rows;
         a.qscale = qscale;
         a.err = kv->err.as<uint32_t>();
-        if (bf16 && tiles.n > 0 && prefill_on_tensor_cores() && !tiles.windowed)
-            launch_prefill_attn_tc(a, tiles.dev, tiles.n, s);
-        else
+        if (bf16 && tiles.n > 0 && prefill_on_tensor_cores() && !tiles.windowed) {
+            // The head-group pipeline (attn_prefill_fa.cu); PTTS_B200_PREFILL=tc1 keeps the
+            // one-head-per-CTA kernel.
+            const char* e = getenv("PTTS_B200_PREFILL");
+            const bool one_head = e && e[0] == 't' && e[1] == 'c' && e[2] == '1';
+            if (one_head || !launch_prefill_attn_fa(a, tiles.dev, tiles.n, kv->streams, kv->capacity, s))
+                launch_prefill_attn_tc(a, tiles.dev, tiles.n, s);
+        } else {
             launch_prefill_attn(a, bf16, s);
+        }
     }
     check_launch();
 }

@@ -1,6 +1,7 @@
 // Internal launchers of the ptts_b200 kernels (not part of the C ABI).
 #pragma once
 
+#include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -234,6 +235,14 @@ void launch_prefill_attn(const PrefillArgs& a, bool cache_bf16, cudaStream_t s);
 // The same on tcgen05 tiles, bf16 caches: one CTA per (tile of up to 128 consecutive rows of
 // one sequence, head); tiles[i] = (first row, rows).
 void launch_prefill_attn_tc(const PrefillArgs& a, const int2* tiles, int n_tiles, cudaStream_t s);
+// The same with one CTA per (tile, group of heads), the group's (head, key tile) items in one
+// pipeline (attn_prefill_fa.cu). `streams` and `capacity` describe the caches' [streams][capacity]
+// rows of 512 bf16. False when the caches' tensor maps cannot be made (nothing launched).
+bool launch_prefill_attn_fa(const PrefillArgs& a, const int2* tiles, int n_tiles, int streams, int capacity,
+                            cudaStream_t s);
+// Tensor map of a row-major [rows][cols] bf16 matrix, box box_cols (128 bytes) x box_rows,
+// 128-byte swizzle (linear_tc.cu).
+bool bf16_rows_map(CUtensorMap* out, const void* ptr, long long rows, int cols, int box_cols, int box_rows);
 
 // ---- int8 linear (linear.cu) ----------------------------------------------------------
 

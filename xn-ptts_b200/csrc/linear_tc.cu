@@ -1213,11 +1213,8 @@ bool launch_tma_rows(const LinearArgs& a, cudaStream_t s) {
     if (wm == kW16) return launch_tma<EPI, 32, kW16>(a, s);
     // int8 weights at decode sizes: widened into TMEM (linear_i8_kernel), or with
     // PTTS_B200_I8=smem in place in shared memory (linear_tma_kernel's kW8 form).
-    static const bool smem_form = [] {
-        const char* e = getenv("PTTS_B200_I8");
-        return e && e[0] == 's';
-    }();
-    return smem_form ? launch_tma<EPI, 32, kW8>(a, s) : launch_i8<EPI, 32>(a, s);
+    const char* e = getenv("PTTS_B200_I8");
+    return e && e[0] == 's' ? launch_tma<EPI, 32, kW8>(a, s) : launch_i8<EPI, 32>(a, s);
 }
 
 // The flow net's linears (bf16 planes, optional weight lo plane), decode-size rows only.
@@ -1227,6 +1224,18 @@ bool launch_tma_flow(const LinearArgs& a, cudaStream_t s) {
 }
 
 }  // namespace
+
+bool bf16_rows_map(CUtensorMap* out, const void* ptr, long long rows, int cols, int box_cols, int box_rows) {
+    EncodeTiled enc = encoder();
+    if (!enc || rows <= 0 || cols % 8 != 0 || box_cols * 2 != 128) return false;
+    const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
+    const cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
+    const cuuint32_t elem[2] = {1, 1};
+    return enc(out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, elem,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
 
 bool linear_tc_supported(const LinearArgs& a) {
     return (a.wh != nullptr || a.w != nullptr) && a.M > 0 && a.N % FT == 0 && a.K % 8 == 0 && a.splits >= 1 &&
