@@ -100,6 +100,15 @@ bool prefill_on_tensor_cores() {
     return !(e && e[0] == 'c');  // PTTS_B200_PREFILL=core keeps the CUDA-core kernel
 }
 
+// The prompt attention that copies its Q tiles by TMA (attn_prefill_fa.cu), for which the q
+// producers (the in_proj epilogue, rope_append) write q as bf16 hi/lo planes; the other prompt
+// kernels read f32 q. PTTS_B200_PREFILL=tc1 keeps the one-head-per-CTA tcgen05 kernel.
+bool prefill_fa(bool cache_bf16, bool decode, bool windowed) {
+    if (decode || !cache_bf16 || windowed || !prefill_on_tensor_cores()) return false;
+    const char* e = getenv("PTTS_B200_PREFILL");
+    return !(e && e[0] == 't' && e[1] == 'c' && e[2] == '1');
+}
+
 // Process-wide tracing of decode-attention launches (ptts_b200_set_tracing).
 struct Tracer {
     std::mutex mu;
@@ -419,6 +428,8 @@ struct Tiles {
     bool windowed = false;  // a windowed stream is in the call: the CUDA-core kernel maps its slots
 };
 
+// q_rot is the rotated q: f32 [n_rows][512], or for prompts where prefill_fa holds, its bf16 hi
+// plane followed by the lo plane (n_rows x 512 each).
 void attention(const ptts_b200_kv* kv, int layer, bool decode, const RowPlan& plan, int n_rows,
                const float* q_rot, void* out, void* out_lo, int out_mode, DevBuf& part,
                DevBuf& counters, const Tiles& tiles, cudaStream_t s, bool compact = false,
@@ -467,13 +478,15 @@ void attention(const ptts_b200_kv* kv, int layer, bool decode, const RowPlan& pl
         a.rows = n_rows;
         a.qscale = qscale;
         a.err = kv->err.as<uint32_t>();
-        if (bf16 && tiles.n > 0 && prefill_on_tensor_cores() && !tiles.windowed) {
-            // The head-group pipeline (attn_prefill_fa.cu); PTTS_B200_PREFILL=tc1 keeps the
-            // one-head-per-CTA kernel.
-            const char* e = getenv("PTTS_B200_PREFILL");
-            const bool one_head = e && e[0] == 't' && e[1] == 'c' && e[2] == '1';
-            if (one_head || !launch_prefill_attn_fa(a, tiles.dev, tiles.n, kv->streams, kv->capacity, s))
-                launch_prefill_attn_tc(a, tiles.dev, tiles.n, s);
+        if (tiles.n > 0 && prefill_fa(bf16, decode, tiles.windowed)) {
+            // The head-group pipeline (attn_prefill_fa.cu), Q tiles by TMA from the hi/lo planes.
+            a.q = nullptr;
+            a.q_hi = reinterpret_cast<const __nv_bfloat16*>(q_rot);
+            a.q_lo = a.q_hi + (size_t)n_rows * kRowWidth;
+            require(launch_prefill_attn_fa(a, tiles.dev, tiles.n, kv->streams, kv->capacity, s), PTTS_B200_ERR_CUDA,
+                    "could not describe the prompt attention's tensors (cuTensorMapEncodeTiled)");
+        } else if (bf16 && tiles.n > 0 && prefill_on_tensor_cores() && !tiles.windowed) {
+            launch_prefill_attn_tc(a, tiles.dev, tiles.n, s);
         } else {
             launch_prefill_attn(a, bf16, s);
         }
@@ -617,6 +630,11 @@ void run_layers(const ptts_b200_model* m, const ptts_b200_kv* kv, bool decode, c
         a.wh_lo = L.l_qkv.p;
         a.scale = L.s_qkv.as<float>();
         a.yq = w.q_rot.as<float>();
+        if (prefill_fa(kv->dtype == PTTS_B200_BF16, decode, tiles.windowed) && tiles.n > 0) {
+            a.yq_hi = w.q_rot.as<__nv_bfloat16>();  // two bf16 planes in the f32 buffer's bytes
+            a.yq_lo = a.yq_hi + (size_t)rows * hd;
+            a.yq_scale = (1.0f / sqrtf((float)c.head_dim)) * kLog2e;  // transformer.rs:215, exp2 domain
+        }
         a.row_stream = plan.row_stream;
         a.row_pos = plan.row_pos;
         a.row_slot = plan.row_slot;
@@ -1241,6 +1259,13 @@ int ptts_b200_attend(ptts_b200_kv* kv, int layer, const void* q, const void* k, 
         ra.capacity = kv->capacity;
         rope_inv_freq(kv->head_dim, max_period, ra.inv_freq);
         ra.err = kv->err.as<uint32_t>();
+        bool windowed = false;
+        for (int i = 0; i < n_seq; ++i) windowed = windowed || kv->is_window(streams_host[i]);
+        if (prefill_fa(kv->dtype == PTTS_B200_BF16, decode, windowed)) {
+            ra.q_hi = reinterpret_cast<__nv_bfloat16*>(ra.q_out);  // two bf16 planes in the f32 buffer
+            ra.q_lo = ra.q_hi + (size_t)n_rows * kRowWidth;
+            ra.q_scale = (1.0f / sqrtf((float)kv->head_dim)) * kLog2e;  // transformer.rs:215, exp2 domain
+        }
         launch_rope_append(ra, in_dtype == PTTS_B200_BF16, kv->dtype == PTTS_B200_BF16, s);
         check_launch();
         const bool trace = decode && tracing_on();
@@ -1255,7 +1280,7 @@ int ptts_b200_attend(ptts_b200_kv* kv, int layer, const void* q, const void* k, 
             tiles.dev = static_cast<int2*>(kv->tiles.need(sizeof(int2) * t.size()));
             tiles.n = (int)t.size();
             kv->staging.upload(const_cast<int2*>(tiles.dev), t.data(), sizeof(int2) * t.size(), s);
-            for (int i = 0; i < n_seq; ++i) tiles.windowed = tiles.windowed || kv->is_window(streams_host[i]);
+            tiles.windowed = windowed;
         }
         attention(kv, layer, decode, plan, n_rows, ra.q_out, out, nullptr,
                   out_dtype == PTTS_B200_BF16 ? kOutBf16 : kOutF32, kv->part, kv->counters, tiles, s);

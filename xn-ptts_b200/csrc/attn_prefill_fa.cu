@@ -8,22 +8,25 @@
 // A CTA runs its heads' (head, 64-key tile) items as one pipeline, so the tensor cores always
 // have the next item's work while the softmax of this one runs (a prompt of 32-512 rows has only
 // 1-8 key tiles per head: one head per CTA left the chain S -> softmax -> P.V mostly idle).
-//   warps 0-3   one query row per thread (TMEM lane 32 w + lane): write the head's q as bf16
-//               hi/lo tiles (the next head's while this one runs), read S from TMEM, online
-//               softmax in the exp2 domain with the causal mask, write P as bf16 hi/lo into TMEM
+//   warps 0-7   softmax: two threads per query row (row 32 (w % 4) + lane = TMEM lane, half
+//               w / 4 of the keys and of the output dims). Read S from TMEM, online softmax in
+//               the exp2 domain with the causal mask (the two halves of a row exchange their
+//               maximum through shared memory once per item), write P as bf16 hi/lo into TMEM
 //               (tcgen05.st); O accumulates in TMEM, rescaled there only when a row's maximum
 //               grows by more than 2^8; at each head's end O / l goes to the output row.
-//   warp 4      lane 0 issues the MMAs (kind::f16, M = 128, N = 64, bf16):
+//   warp 8      lane 0 issues the MMAs (kind::f16, M = 128, N = 64, bf16):
 //               S = Q_hi K^T + Q_lo K^T     A = Q (smem, K-major), B = K (smem, K-major)
-//               O = P_hi V + P_lo V         A = P (TMEM), B = V (smem, MN-major)
+//               O += P_hi V + P_lo V        A = P (TMEM), B = V (smem, MN-major)
 //               S runs up to two items ahead of P.V (two S buffers in TMEM), across heads.
-//   warp 5      lane 0 copies each item's K and V tiles (64 keys x one head, 128-byte swizzle)
-//               with TMA into a two-slot ring.
-// TMEM (256 columns): S0 0-63, S1 64-127, O 128-191, P hi 192-223, P lo 224-255
-// (bf16 pairs, one row per lane). Keys past the tile's last position are masked in the softmax
-// and their V rows zeroed before P.V (the slots may hold anything, and 0 x NaN is NaN). Every
-// wait is bounded and sets DEV_ERR_TIMEOUT; a CTA that timed out waits, bounded, for its copies.
-// Splitting q and P into hi + lo keeps the products f32-grade, as in the linears.
+//   warp 9      lane 0 copies with TMA each head's Q tiles (the bf16 hi/lo planes the q producer
+//               wrote) and each item's K and V tiles (64 keys x one head, 128-byte swizzle) into
+//               two-slot K and V rings: a K slot frees once its S product is done, so K runs an
+//               item ahead of V.
+// TMEM (256 columns): S0 0-63, S1 64-127, O 128-191, P hi 192-223, P lo 224-255 (bf16 pairs,
+// one row per lane). Keys past the tile's last position are masked in the softmax and their V
+// rows zeroed before P.V (the slots may hold anything, and 0 x NaN is NaN). Every wait is bounded
+// and sets DEV_ERR_TIMEOUT; a CTA that timed out waits, bounded, for its copies. Splitting q and
+// P into hi + lo keeps the products f32-grade, as in the linears.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -33,7 +36,9 @@ namespace {
 constexpr int QT = 128;            // query rows per CTA
 constexpr int KT = 64;             // keys per item
 constexpr int kHeadsPerCta = 4;
-constexpr int kThreadsF = 6 * 32;
+constexpr int kSoftWarps = 8;    // two per TMEM lane quarter (two threads per row)
+constexpr int kMmaWarp = kSoftWarps, kLoadWarp = kSoftWarps + 1;
+constexpr int kThreadsF = (kSoftWarps + 2) * 32;
 constexpr int kQBytes = QT * 128;  // one plane of one head's q: 128 rows x 64 bf16
 constexpr int kKVBytes = KT * 128; // one head's K (or V) tile
 constexpr int kSlots = 2;          // K/V ring
@@ -124,35 +129,44 @@ __device__ __forceinline__ void fa_tma(uint32_t dst, const CUtensorMap* map, int
         : "memory");
 }
 
-// Write 64 f32 values of one row as bf16 hi/lo into two K-major SW128 tiles (row r).
-__device__ __forceinline__ void q_row_hilo(unsigned char* hi, unsigned char* lo, int r, const float* v) {
-#pragma unroll
-    for (int c = 0; c < 8; ++c) {
-        uint4 h, l;
-        uint32_t* hp = &h.x;
-        uint32_t* lp = &l.x;
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            const float a = v[8 * c + 2 * e], b = v[8 * c + 2 * e + 1];
-            hp[e] = pack_bf16x2(a, b);
-            lp[e] = pack_bf16x2(a - bf16lo(hp[e]), b - bf16hi(hp[e]));
-        }
-        const int off = r * 128 + ((c ^ (r & 7)) << 4);
-        *reinterpret_cast<uint4*>(hi + off) = h;
-        *reinterpret_cast<uint4*>(lo + off) = l;
-    }
-}
-
-// Barriers: K/V full and empty per slot, Q ready per buffer, S full and free per buffer, P full,
+// Barriers: K and V full and empty per slot (separate rings: a K slot frees once its S product is
+// done, a V slot once its P.V is), Q ready and free per buffer, S full and free per buffer, P full,
 // O full.
 struct FaBars {
-    uint64_t kvfull[kSlots], kvempty[kSlots], qready[2], sfull[2], sfree[2], pfull, ofull;
+    uint64_t kfull[kSlots], kempty[kSlots], vfull[kSlots], vempty[kSlots], qready[2], qfree[2], sfull[2],
+        sfree[2], pfull, ofull;
 };
 static_assert(sizeof(FaBars) + 4 <= 256, "barriers fit the tail");
+
+// Named barrier 1 + q over the two softmax warps of row quarter q (64 threads), returning
+// whether `v` held in any of them: both leave a loop together.
+template <int ID>
+__device__ __forceinline__ bool pair_any_id(bool v) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 p, %1, 0;\n\t"
+        "barrier.red.or.pred q, %2, 64, p;\n\t"
+        "selp.u32 %0, 1, 0, q;\n\t}"
+        : "=r"(r)
+        : "r"((uint32_t)v), "n"(ID)
+        : "memory");
+    return r != 0;
+}
+__device__ __forceinline__ bool pair_any(int quarter, bool v) {
+    switch (quarter) {
+        case 0: return pair_any_id<1>(v);
+        case 1: return pair_any_id<2>(v);
+        case 2: return pair_any_id<3>(v);
+        default: return pair_any_id<4>(v);
+    }
+}
 
 __global__ void __launch_bounds__(kThreadsF, 2) prefill_fa_kernel(PrefillArgs a, const int2* tiles,
                                                               const __grid_constant__ CUtensorMap tm_k,
                                                               const __grid_constant__ CUtensorMap tm_v,
+                                                              const __grid_constant__ CUtensorMap tm_qh,
+                                                              const __grid_constant__ CUtensorMap tm_ql,
                                                               int capacity) {
     extern __shared__ unsigned char smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
@@ -160,24 +174,30 @@ __global__ void __launch_bounds__(kThreadsF, 2) prefill_fa_kernel(PrefillArgs a,
     unsigned char* sm = smem_raw + (base - raw);
     FaBars* b = reinterpret_cast<FaBars*>(sm + kOffBar);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(b + 1);
-    __shared__ int s_issued, s_consumed;
+    __shared__ int s_k_issued, s_v_issued, s_q_issued;
+    __shared__ float s_xmax[2][2][QT];  // [item parity][half][row]: the halves' row maxima
+    __shared__ float s_xsum[2][QT];     // [half][row]: the halves' row sums at a head's end
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int h0 = blockIdx.y * kHeadsPerCta;
 
     if (tid == 0) {
         for (int i = 0; i < kSlots; ++i) {
-            mbar_init(&b->kvfull[i], 1);
-            mbar_init(&b->kvempty[i], 1);
+            mbar_init(&b->kfull[i], 1);
+            mbar_init(&b->kempty[i], 1);
+            mbar_init(&b->vfull[i], 1);
+            mbar_init(&b->vempty[i], 1);
         }
         for (int i = 0; i < 2; ++i) {
-            mbar_init(&b->qready[i], 4);
+            mbar_init(&b->qready[i], 1);
+            mbar_init(&b->qfree[i], 1);
             mbar_init(&b->sfull[i], 1);
-            mbar_init(&b->sfree[i], 4);
+            mbar_init(&b->sfree[i], kSoftWarps);
         }
-        mbar_init(&b->pfull, 4);
+        mbar_init(&b->pfull, kSoftWarps);
         mbar_init(&b->ofull, 1);
-        s_issued = 0;
-        s_consumed = 0;
+        s_k_issued = 0;
+        s_v_issued = 0;
+        s_q_issued = 0;
         fence_mbar_init();
     }
     if (warp == 0) {
@@ -197,35 +217,21 @@ __global__ void __launch_bounds__(kThreadsF, 2) prefill_fa_kernel(PrefillArgs a,
     const int row0 = tile.x, nrows = tile.y;
     const int sid = a.row_stream[row0];
     const int pos_max = a.row_pos[row0 + nrows - 1];  // the tile's last row sees the most keys
-    const bool bad = sid < 0 || pos_max < 0 || pos_max >= capacity;
+    const bool bad = sid < 0 || pos_max < 0 || pos_max >= capacity || a.q_hi == nullptr;
     const int n_kt = bad ? 0 : (pos_max + KT) / KT;
     const int n_items = kHeadsPerCta * n_kt;  // item i: head h0 + i / n_kt, key tile i % n_kt
 
-    if (warp < 4) {
+    if (warp < kSoftWarps) {
         if (bad && tid == 0) set_error(a.err, DEV_ERR_BOUNDS);
-        const int r = tid;  // this thread's query row in the tile (TMEM lane)
+        const int quarter = warp & 3, half = warp >> 2;
+        const int r = 32 * quarter + lane;  // this thread's query row in the tile (TMEM lane)
         const bool active = r < nrows;
         const int pos = active ? a.row_pos[row0 + r] : -1;
-        const uint32_t lane_base = (uint32_t)(32 * warp) << 16;
-        auto write_q = [&](int hh) {  // q of head h0 + hh into Q buffer hh % 2
-            float q[64];
-            const float* qr = a.q + ((long long)(row0 + (active ? r : 0)) * 8 + h0 + hh) * kHeadDim;
-#pragma unroll
-            for (int i = 0; i < 16; ++i) {
-                const float4 x = active ? *reinterpret_cast<const float4*>(qr + 4 * i) : make_float4(0.f, 0.f, 0.f, 0.f);
-                q[4 * i] = x.x; q[4 * i + 1] = x.y; q[4 * i + 2] = x.z; q[4 * i + 3] = x.w;
-            }
-            unsigned char* qb = sm + kOffQ + (hh & 1) * 2 * kQBytes;
-            q_row_hilo(qb, qb + kQBytes, r, q);
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&b->qready[hh & 1]);
-        };
-        if (n_items > 0) write_q(0);
+        const uint32_t lane_base = (uint32_t)(32 * quarter) << 16;
         // O accumulates in TMEM across a head's key tiles (P.V with accumulate). The exps of a
         // head are taken against m, raised lazily: only when a tile's row maximum exceeds m by
         // more than kRaise (log2 units) is O rescaled in TMEM and m raised, so P stays <= 2^kRaise
-        // and the final O / l is the same softmax.
+        // and the final O / l is the same softmax. Both halves of a row keep the same m.
         constexpr float kRaise = 8.f;
         float m = -1e30f, l = 0.f;
         for (int i = 0; i < n_items; ++i) {
@@ -233,137 +239,137 @@ __global__ void __launch_bounds__(kThreadsF, 2) prefill_fa_kernel(PrefillArgs a,
             if (kt == 0) {
                 m = -1e30f;
                 l = 0.f;
-                // The other Q buffer held head hh - 1, whose S products are all complete.
-                if (hh + 1 < kHeadsPerCta) write_q(hh + 1);
             }
-            // S(i) from TMEM: this thread's row, 64 keys; then the buffer goes back. A timeout
-            // ends the warp's loop as a whole (the TMEM accesses below are warp-collective).
-            if (!__all_sync(0xffffffffu, mbar_wait(&b->sfull[i & 1], (i >> 1) & 1))) {
-                set_error(a.err, DEV_ERR_TIMEOUT);
-                break;
-            }
-            fa_after();
-            float s[64];
-            fa_ld32(tmem + lane_base + (uint32_t)((i & 1) * 64), s);
-            fa_ld32(tmem + lane_base + (uint32_t)((i & 1) * 64 + 32), s + 32);
-            fa_wait_ld();
-            fa_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&b->sfree[i & 1]);
+            // S(i) from TMEM: this thread's row, its 32 keys; then the buffer goes back.
+            bool ok = __all_sync(0xffffffffu, mbar_wait(&b->sfull[i & 1], (i >> 1) & 1));
+            float s[32];
             float mt = -INFINITY;
+            if (ok) {
+                fa_after();
+                fa_ld32(tmem + lane_base + (uint32_t)((i & 1) * 64 + 32 * half), s);
+                fa_wait_ld();
+                fa_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&b->sfree[i & 1]);
+                // q came scaled by log2(e) / sqrt(D): S is in the exp2 domain already.
+                const int key0 = kt * KT + 32 * half;
+                if (__all_sync(0xffffffffu, key0 + 31 <= pos)) {  // no key of this half is masked
 #pragma unroll
-            for (int j = 0; j < 64; ++j) {
-                const int key = kt * KT + j;
-                s[j] = key <= pos ? s[j] * a.qscale : -INFINITY;
-                mt = fmaxf(mt, s[j]);
+                    for (int j = 0; j < 32; ++j) mt = fmaxf(mt, s[j]);
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        s[j] = key0 + j <= pos ? s[j] : -INFINITY;
+                        mt = fmaxf(mt, s[j]);
+                    }
+                }
+                // P.V of the previous item has read P and added into O.
+                if (kt > 0) ok = __all_sync(0xffffffffu, mbar_wait(&b->ofull, (i - 1) & 1));
             }
-            // P.V of the previous item has read P and added into O (cheap by now: issued as soon
-            // as that P was written).
-            if (kt > 0 && !__all_sync(0xffffffffu, mbar_wait(&b->ofull, (i - 1) & 1))) {
+            // The row's maximum over both halves (and a timeout in either warp ends both loops).
+            s_xmax[i & 1][half][r] = mt;
+            if (pair_any(quarter, !ok)) {
                 set_error(a.err, DEV_ERR_TIMEOUT);
                 break;
             }
+            mt = fmaxf(mt, s_xmax[i & 1][half ^ 1][r]);
             fa_after();
             const bool raise = kt == 0 ? true : mt > m + kRaise;
             const float mnew = raise ? fmaxf(mt, m) : m;
-            if (kt > 0 && __any_sync(0xffffffffu, raise)) {  // rescale O rows in TMEM (the whole warp)
+            if (kt > 0 && __any_sync(0xffffffffu, raise)) {  // rescale this half of O in TMEM
                 const float f = raise ? fa_exp2(m - mnew) : 1.f;
                 l *= f;
                 float ot[32];
+                fa_ld32(tmem + lane_base + kColO + 32 * half, ot);
+                fa_wait_ld();
+                uint32_t w[32];
 #pragma unroll
-                for (int half = 0; half < 2; ++half) {
-                    fa_ld32(tmem + lane_base + kColO + 32 * half, ot);
-                    fa_wait_ld();
-                    uint32_t w[32];
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) w[j] = __float_as_uint(ot[j] * f);
-                    fa_st32(tmem + lane_base + kColO + 32 * half, w);
-                }
+                for (int j = 0; j < 32; ++j) w[j] = __float_as_uint(ot[j] * f);
+                fa_st32(tmem + lane_base + kColO + 32 * half, w);
             }
             m = mnew;
-            float rs = 0.f;
-            // P(i) into TMEM, 16 keys (8 columns of bf16 pairs per plane) at a time.
+            // P(i) into TMEM: this half's 32 keys, 16 columns of bf16 pairs per plane.
 #pragma unroll
-            for (int c = 0; c < 4; ++c) {
+            for (int c = 0; c < 2; ++c) {
                 uint32_t ph[8], pl[8];
 #pragma unroll
                 for (int j = 0; j < 8; ++j) {
                     const float e0 = fa_exp2(s[16 * c + 2 * j] - m), e1 = fa_exp2(s[16 * c + 2 * j + 1] - m);
-                    rs += e0 + e1;
+                    l += e0 + e1;
                     ph[j] = pack_bf16x2(e0, e1);
                     pl[j] = pack_bf16x2(e0 - bf16lo(ph[j]), e1 - bf16hi(ph[j]));
                 }
-                fa_st8(tmem + lane_base + kColPh + 8 * c, ph);
-                fa_st8(tmem + lane_base + kColPl + 8 * c, pl);
+                fa_st8(tmem + lane_base + kColPh + 16 * half + 8 * c, ph);
+                fa_st8(tmem + lane_base + kColPl + 16 * half + 8 * c, pl);
             }
             asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-            l += rs;
             if (kt == n_kt - 1 && (kt + 1) * KT - 1 > pos_max) {
-                // Zero the V rows past the tile's last key (read by P.V with P = 0).
+                // Zero the V rows past the tile's last key (read by P.V with P = 0), once V(i)
+                // has landed (its copy runs apart from K's).
+                if (!mbar_wait(&b->vfull[i % kSlots], (i / kSlots) & 1)) set_error(a.err, DEV_ERR_TIMEOUT);
                 unsigned char* vt = sm + kOffKV + (i % kSlots) * 2 * kKVBytes + kKVBytes;
                 const int first = pos_max + 1 - kt * KT;
-                for (int c = first * 8 + tid; c < KT * 8; c += 128)
+                for (int c = first * 8 + tid; c < KT * 8; c += 32 * kSoftWarps)
                     *reinterpret_cast<uint4*>(vt + 16 * c) = make_uint4(0u, 0u, 0u, 0u);
-                // Each warp's zeros precede its own arrival on pfull; P.V waits for all four.
+                // Each warp's zeros precede its own arrival on pfull; P.V waits for all of them.
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             }
             fa_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&b->pfull);
             if (kt < n_kt - 1) continue;
-            // The head's last tile: O / l from TMEM into the output row (16-byte stores).
-            if (!__all_sync(0xffffffffu, mbar_wait(&b->ofull, i & 1))) {
+            // The head's last tile: the row sum over both halves, then O / l into this half of
+            // the output row (16-byte stores).
+            ok = __all_sync(0xffffffffu, mbar_wait(&b->ofull, i & 1));
+            s_xsum[half][r] = l;  // read by the partner before either reaches the next head's end
+            if (pair_any(quarter, !ok)) {
                 set_error(a.err, DEV_ERR_TIMEOUT);
                 break;
             }
+            const float inv = 1.f / (l + s_xsum[half ^ 1][r]);
             fa_after();
-            const float inv = 1.f / l;
-            const long long at = (long long)(row0 + r) * kRowWidth + (h0 + hh) * kHeadDim;
+            float o[32];
+            fa_ld32(tmem + lane_base + kColO + 32 * half, o);
+            fa_wait_ld();
+            if (!active) continue;
+            const long long at = (long long)(row0 + r) * kRowWidth + (h0 + hh) * kHeadDim + 32 * half;
+            if (a.out_mode == kOutF32) {
+                float4* out = reinterpret_cast<float4*>(static_cast<float*>(a.out) + at);
 #pragma unroll
-            for (int half = 0; half < 2; ++half) {
-                float o[32];
-                fa_ld32(tmem + lane_base + kColO + 32 * half, o);
-                fa_wait_ld();
-                if (!active) continue;
-                const long long ah = at + 32 * half;
-                if (a.out_mode == kOutF32) {
-                    float4* out = reinterpret_cast<float4*>(static_cast<float*>(a.out) + ah);
+                for (int j = 0; j < 8; ++j)
+                    out[j] = make_float4(o[4 * j] * inv, o[4 * j + 1] * inv, o[4 * j + 2] * inv, o[4 * j + 3] * inv);
+            } else if (a.out_mode == kOutBf16) {
+                uint4* out = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.out) + at);
 #pragma unroll
-                    for (int j = 0; j < 8; ++j)
-                        out[j] = make_float4(o[4 * j] * inv, o[4 * j + 1] * inv, o[4 * j + 2] * inv, o[4 * j + 3] * inv);
-                } else if (a.out_mode == kOutBf16) {
-                    uint4* out = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.out) + ah);
+                for (int j = 0; j < 4; ++j)
+                    out[j] = make_uint4(pack_bf16x2(o[8 * j] * inv, o[8 * j + 1] * inv),
+                                        pack_bf16x2(o[8 * j + 2] * inv, o[8 * j + 3] * inv),
+                                        pack_bf16x2(o[8 * j + 4] * inv, o[8 * j + 5] * inv),
+                                        pack_bf16x2(o[8 * j + 6] * inv, o[8 * j + 7] * inv));
+            } else {
+                uint4* oh = reinterpret_cast<uint4*>(static_cast<__half*>(a.out) + at);
+                uint4* ol = reinterpret_cast<uint4*>(static_cast<__half*>(a.out_lo) + at);
 #pragma unroll
-                    for (int j = 0; j < 4; ++j)
-                        out[j] = make_uint4(pack_bf16x2(o[8 * j] * inv, o[8 * j + 1] * inv),
-                                            pack_bf16x2(o[8 * j + 2] * inv, o[8 * j + 3] * inv),
-                                            pack_bf16x2(o[8 * j + 4] * inv, o[8 * j + 5] * inv),
-                                            pack_bf16x2(o[8 * j + 6] * inv, o[8 * j + 7] * inv));
-                } else {
-                    uint4* oh = reinterpret_cast<uint4*>(static_cast<__half*>(a.out) + ah);
-                    uint4* ol = reinterpret_cast<uint4*>(static_cast<__half*>(a.out_lo) + ah);
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        uint4 h, lo4;
-                        split_f16x2(o[8 * j] * inv, o[8 * j + 1] * inv, h.x, lo4.x);
-                        split_f16x2(o[8 * j + 2] * inv, o[8 * j + 3] * inv, h.y, lo4.y);
-                        split_f16x2(o[8 * j + 4] * inv, o[8 * j + 5] * inv, h.z, lo4.z);
-                        split_f16x2(o[8 * j + 6] * inv, o[8 * j + 7] * inv, h.w, lo4.w);
-                        oh[j] = h;
-                        ol[j] = lo4;
-                    }
+                for (int j = 0; j < 4; ++j) {
+                    uint4 h, lo4;
+                    split_f16x2(o[8 * j] * inv, o[8 * j + 1] * inv, h.x, lo4.x);
+                    split_f16x2(o[8 * j + 2] * inv, o[8 * j + 3] * inv, h.y, lo4.y);
+                    split_f16x2(o[8 * j + 4] * inv, o[8 * j + 5] * inv, h.z, lo4.z);
+                    split_f16x2(o[8 * j + 6] * inv, o[8 * j + 7] * inv, h.w, lo4.w);
+                    oh[j] = h;
+                    ol[j] = lo4;
                 }
             }
         }
-    } else if (warp == 4 && lane == 0) {
+    } else if (warp == kMmaWarp && lane == 0) {
         // ---- MMA issuer ----------------------------------------------------------------------
-        // Two independent streams of work, polled without blocking: S(i) once item i's K/V have
-        // landed, its Q is written and its S buffer is free; P.V(i) once P(i) is in TMEM. S thus
-        // runs up to two items ahead of P.V, across heads too. Bounded: no progress for
-        // kWaitLimitCycles ends the loop with DEV_ERR_TIMEOUT.
+        // Two independent streams of work, polled without blocking: S(i) once item i's K has
+        // landed, its Q is in and its S buffer is free; P.V(i) once P(i) is in TMEM and V(i) has
+        // landed. S thus runs up to two items ahead of P.V, across heads too. Bounded: no progress
+        // for kWaitLimitCycles ends the loop with DEV_ERR_TIMEOUT.
         auto s_ready = [&](int i) {
             const int hh = i / n_kt;
-            return mbar_test_wait(&b->kvfull[i % kSlots], (i / kSlots) & 1) &&
+            return mbar_test_wait(&b->kfull[i % kSlots], (i / kSlots) & 1) &&
                    mbar_test_wait(&b->qready[hh & 1], (hh >> 1) & 1) &&
                    (i < 2 || mbar_test_wait(&b->sfree[i & 1], ((i >> 1) & 1) ^ 1));
         };
@@ -372,7 +378,7 @@ __global__ void __launch_bounds__(kThreadsF, 2) prefill_fa_kernel(PrefillArgs a,
             fa_after();
             const uint32_t qa = base + kOffQ + (hh & 1) * 2 * kQBytes;
             const uint64_t dqh = desc_k(qa), dql = desc_k(qa + kQBytes);
-            const uint64_t dk = desc_k(base + kOffKV + slot * 2 * kKVBytes);
+            const uint64_t dk = desc_k(base + kOffKV + slot * 2 * kKVBytes);  // K half of the slot
             const uint32_t d = tmem + (uint32_t)((i & 1) * 64);
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk) {  // head dim 64 = 4 x 16: 32 bytes per step
@@ -380,6 +386,8 @@ __global__ void __launch_bounds__(kThreadsF, 2) prefill_fa_kernel(PrefillArgs a,
                 fa_mma_ss(d, dql + 2 * kk, dk + 2 * kk, kIdescSf, 1u);
             }
             fa_commit(&b->sfull[i & 1]);
+            fa_commit(&b->kempty[slot]);  // S(i) has read the K slot
+            if (i % n_kt == n_kt - 1) fa_commit(&b->qfree[hh & 1]);  // the head's Q tiles are read
         };
         auto issue_pv = [&](int i) {
             fa_after();
@@ -392,8 +400,7 @@ __global__ void __launch_bounds__(kThreadsF, 2) prefill_fa_kernel(PrefillArgs a,
                 fa_mma_ts(tmem + kColO, tmem + kColPl + 8 * kk, dv + 128 * kk, kIdescPVf, 1u);
             }
             fa_commit(&b->ofull);
-            fa_commit(&b->kvempty[i % kSlots]);  // S(i) and P.V(i) have read the slot
-            s_consumed = i + 1;
+            fa_commit(&b->vempty[i % kSlots]);  // P.V(i) has read the V slot
         };
         int next_s = 0, next_pv = 0;
         long long t0 = clock64();
@@ -403,7 +410,8 @@ __global__ void __launch_bounds__(kThreadsF, 2) prefill_fa_kernel(PrefillArgs a,
                 issue_s(next_s++);
                 progressed = true;
             }
-            if (next_pv < next_s && mbar_test_wait(&b->pfull, next_pv & 1)) {
+            if (next_pv < next_s && mbar_test_wait(&b->pfull, next_pv & 1) &&
+                mbar_test_wait(&b->vfull[next_pv % kSlots], (next_pv / kSlots) & 1)) {
                 issue_pv(next_pv++);
                 progressed = true;
             }
@@ -416,28 +424,68 @@ __global__ void __launch_bounds__(kThreadsF, 2) prefill_fa_kernel(PrefillArgs a,
                 __nanosleep(20);  // leave the issue slots to the softmax warp sharing this SMSP
             }
         }
-    } else if (warp == 5 && lane == 0) {
-        // ---- K/V producer --------------------------------------------------------------------
+    } else if (warp == kLoadWarp && lane == 0) {
+        // ---- Q, K and V producer ------------------------------------------------------------
         const long long row_base = (long long)sid * capacity;
-        for (int i = 0; i < n_items; ++i) {
+        // Q tiles of head hh (hi, lo: 128 rows x 64 bf16 from row0) into buffer hh % 2, once the
+        // S products of head hh - 2 that read it are done.
+        auto load_q = [&](int hh) -> bool {
+            const int qb = hh & 1;
+            if (hh >= 2 && !mbar_wait(&b->qfree[qb], ((hh >> 1) & 1) ^ 1)) return false;
+            const uint32_t dst = base + kOffQ + qb * 2 * kQBytes;
+            mbar_arrive_expect_tx(&b->qready[qb], 2 * kQBytes);
+            fa_tma(dst, &tm_qh, (h0 + hh) * kHeadDim, row0, &b->qready[qb]);
+            fa_tma(dst + kQBytes, &tm_ql, (h0 + hh) * kHeadDim, row0, &b->qready[qb]);
+            s_q_issued = hh + 1;
+            return true;
+        };
+        // K(j) then V(j - 1): K runs an item ahead of V, its slots freed by S alone.
+        auto load_k = [&](int i) -> bool {
             const int hh = i / n_kt, kt = i - hh * n_kt, slot = i % kSlots;
-            if (i >= kSlots && !mbar_wait(&b->kvempty[slot], ((i / kSlots) & 1) ^ 1)) {
-                set_error(a.err, DEV_ERR_TIMEOUT);
-                break;
+            if (i >= kSlots && !mbar_wait(&b->kempty[slot], ((i / kSlots) & 1) ^ 1)) return false;
+            mbar_arrive_expect_tx(&b->kfull[slot], kKVBytes);
+            fa_tma(base + kOffKV + slot * 2 * kKVBytes, &tm_k, (h0 + hh) * kHeadDim,
+                   (int)(row_base + (long long)kt * KT), &b->kfull[slot]);
+            s_k_issued = i + 1;
+            return true;
+        };
+        auto load_v = [&](int i) -> bool {
+            const int hh = i / n_kt, kt = i - hh * n_kt, slot = i % kSlots;
+            if (i >= kSlots && !mbar_wait(&b->vempty[slot], ((i / kSlots) & 1) ^ 1)) return false;
+            mbar_arrive_expect_tx(&b->vfull[slot], kKVBytes);
+            fa_tma(base + kOffKV + slot * 2 * kKVBytes + kKVBytes, &tm_v, (h0 + hh) * kHeadDim,
+                   (int)(row_base + (long long)kt * KT), &b->vfull[slot]);
+            s_v_issued = i + 1;
+            return true;
+        };
+        int q_loaded = 0;  // heads whose Q tiles are requested
+        bool ok = n_items == 0 || load_q(0);
+        q_loaded = 1;
+        for (int i = 0; i <= n_items && ok; ++i) {
+            if (i < n_items) {
+                const int hh = i / n_kt, kt = i - hh * n_kt;
+                if (kt == 0 && hh + 1 < kHeadsPerCta && q_loaded == hh + 1) {
+                    ok = load_q(hh + 1);
+                    q_loaded = hh + 2;
+                }
+                ok = ok && load_k(i);
             }
-            const uint32_t dst = base + kOffKV + slot * 2 * kKVBytes;
-            mbar_arrive_expect_tx(&b->kvfull[slot], 2 * kKVBytes);
-            const int x = (h0 + hh) * kHeadDim, y = (int)(row_base + (long long)kt * KT);
-            fa_tma(dst, &tm_k, x, y, &b->kvfull[slot]);
-            fa_tma(dst + kKVBytes, &tm_v, x, y, &b->kvfull[slot]);
-            s_issued = i + 1;
+            if (ok && i >= 1) ok = load_v(i - 1);
         }
+        if (!ok) set_error(a.err, DEV_ERR_TIMEOUT);
     }
     fa_before();
     __syncthreads();
     if (tid == 0) {
-        // Copies issued but never consumed (only after a timeout): let them land before exit.
-        for (int i = s_consumed; i < s_issued; ++i) mbar_wait(&b->kvfull[i % kSlots], (i / kSlots) & 1);
+        // The last copies issued into each slot (consumed or not; a completed phase returns at
+        // once): let them land before exit.
+        for (int i = s_k_issued > kSlots ? s_k_issued - kSlots : 0; i < s_k_issued; ++i)
+            mbar_wait(&b->kfull[i % kSlots], (i / kSlots) & 1);
+        for (int i = s_v_issued > kSlots ? s_v_issued - kSlots : 0; i < s_v_issued; ++i)
+            mbar_wait(&b->vfull[i % kSlots], (i / kSlots) & 1);
+        // The Q copies: the last request of each buffer (a completed phase returns at once).
+        for (int hh = s_q_issued > 2 ? s_q_issued - 2 : 0; hh < s_q_issued; ++hh)
+            mbar_wait(&b->qready[hh & 1], (hh >> 1) & 1);
     }
     if (warp == 0) {
         fa_after();
@@ -451,13 +499,21 @@ bool launch_prefill_attn_fa(const PrefillArgs& a, const int2* tiles, int n_tiles
                             cudaStream_t s) {
     const long long rows = (long long)streams * capacity;
     if (rows >= (1LL << 31)) return false;
-    CUtensorMap mk, mv;
+    CUtensorMap mk, mv, mqh, mql;
     if (!bf16_rows_map(&mk, a.k_cache, rows, kRowWidth, kHeadDim, KT) ||
         !bf16_rows_map(&mv, a.v_cache, rows, kRowWidth, kHeadDim, KT))
         return false;
+    if (a.q_hi) {
+        if (!bf16_rows_map(&mqh, a.q_hi, a.rows, kRowWidth, kHeadDim, QT) ||
+            !bf16_rows_map(&mql, a.q_lo, a.rows, kRowWidth, kHeadDim, QT))
+            return false;
+    } else {
+        mqh = mk;  // unused: the softmax warps convert the f32 q
+        mql = mk;
+    }
     set_max_dynamic_smem(reinterpret_cast<const void*>(prefill_fa_kernel), kSmemF);
     launch_k(prefill_fa_kernel, dim3(n_tiles, (kRowWidth / kHeadDim) / kHeadsPerCta), dim3(kThreadsF), kSmemF, s, a,
-             tiles, mk, mv, capacity);
+             tiles, mk, mv, mqh, mql, capacity);
     return true;
 }
 

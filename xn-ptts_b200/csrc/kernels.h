@@ -159,6 +159,12 @@ struct RopeAppendArgs {
     const void* k;         // [rows][KVH][D]
     const void* v;
     float* q_out;          // [rows][H][D] f32, rotated
+    // Instead of q_out, when set: the rotated q times q_scale as bf16 hi and lo planes
+    // [rows][H][D] (hi = bf16(x), lo = bf16(x - hi)), the form the tcgen05 prefill attention
+    // copies by TMA (q_scale = log2(e) / sqrt(D): its scores come out in the exp2 domain).
+    __nv_bfloat16* q_hi = nullptr;
+    __nv_bfloat16* q_lo = nullptr;
+    float q_scale = 1.f;
     void* k_cache;         // layer base [S][cap][H][D]
     void* v_cache;
     const int32_t* row_stream;
@@ -222,6 +228,10 @@ struct PrefillArgs {
     const int32_t* row_pos;
     const int32_t* window = nullptr;  // [streams] context of windowed streams (0: none)
     const float* q;           // [rows][H][D] f32, rotated
+    // The same q times qscale as bf16 hi/lo planes [rows][H*D] (RopeAppendArgs::q_hi), which
+    // the prefill_fa kernel copies by TMA (it needs them).
+    const __nv_bfloat16* q_hi = nullptr;
+    const __nv_bfloat16* q_lo = nullptr;
     void* out;                // [rows][H*D] (see out_mode)
     void* out_lo;
     int out_mode;
@@ -274,6 +284,9 @@ struct LinearArgs {
     void* yb;                 // EPI_GELU: f16 hi plane [M][N]
     void* yb_lo;              // EPI_GELU: f16 lo plane [M][N]
     float* yq;                // EPI_QKV: rotated q [M][H*D] f32
+    __nv_bfloat16* yq_hi = nullptr;  // EPI_QKV: instead of yq, the rotated q times yq_scale as bf16
+    __nv_bfloat16* yq_lo = nullptr;  //          hi/lo planes [M][H*D] (see RopeAppendArgs::q_hi)
+    float yq_scale = 1.f;
     int gelu_tanh;
     // EPI_QKV
     const int32_t* row_stream;

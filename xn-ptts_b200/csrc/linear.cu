@@ -179,7 +179,15 @@ __device__ __forceinline__ void qkv_pair(const LinearArgs& p, int m, int n, floa
     float x0 = c0 * p.scale[n], x1 = c1 * p.scale[n + 1];
     if (n < hd) {
         rot(x0, x1, t);
-        *reinterpret_cast<float2*>(p.yq + (long long)m * hd + n) = make_float2(x0, x1);
+        if (p.yq_hi) {
+            x0 *= p.yq_scale;
+            x1 *= p.yq_scale;
+            const uint32_t hi = pack_bf16x2(x0, x1);
+            *reinterpret_cast<uint32_t*>(p.yq_hi + (long long)m * hd + n) = hi;
+            *reinterpret_cast<uint32_t*>(p.yq_lo + (long long)m * hd + n) = pack_bf16x2(x0 - bf16lo(hi), x1 - bf16hi(hi));
+        } else {
+            *reinterpret_cast<float2*>(p.yq + (long long)m * hd + n) = make_float2(x0, x1);
+        }
         return;
     }
     if (sid < 0 || sid >= p.num_streams || pos < 0 || pos >= p.capacity) {

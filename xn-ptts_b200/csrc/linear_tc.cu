@@ -306,7 +306,19 @@ __device__ __forceinline__ void qkv_rows(const LinearArgs& p, const float* st, i
         }
         if (m >= p.M) continue;
         if (region == 0) {
-            *reinterpret_cast<float4*>(p.yq + (long long)m * hd + f) = make_float4(x0, x1, x2, x3);
+            if (p.yq_hi) {
+                x0 *= p.yq_scale;
+                x1 *= p.yq_scale;
+                x2 *= p.yq_scale;
+                x3 *= p.yq_scale;
+                const uint2 hi = make_uint2(pack_bf16x2(x0, x1), pack_bf16x2(x2, x3));
+                const uint2 lo = make_uint2(pack_bf16x2(x0 - bf16lo(hi.x), x1 - bf16hi(hi.x)),
+                                            pack_bf16x2(x2 - bf16lo(hi.y), x3 - bf16hi(hi.y)));
+                *reinterpret_cast<uint2*>(p.yq_hi + (long long)m * hd + f) = hi;
+                *reinterpret_cast<uint2*>(p.yq_lo + (long long)m * hd + f) = lo;
+            } else {
+                *reinterpret_cast<float4*>(p.yq + (long long)m * hd + f) = make_float4(x0, x1, x2, x3);
+            }
             continue;
         }
         if (sid < 0 || sid >= p.num_streams || pos < 0 || pos >= p.capacity) {

@@ -49,10 +49,19 @@ __global__ void rope_append_kernel(RopeAppendArgs a) {
         y0 = __fsub_rn(__fmul_rn(x0, cs), __fmul_rn(x1, sn));
         y1 = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, cs));
     }
-    if (slot < a.heads) {  // q stays f32: it is only read by this call's attention
-        float* dst = static_cast<float*>(a.q_out) + ((long long)row * a.heads + slot) * kHeadDim;
-        dst[2 * i] = y0;
-        dst[2 * i + 1] = y1;
+    if (slot < a.heads) {  // q stays f32 (or f32-grade hi/lo): only this call's attention reads it
+        const long long at = ((long long)row * a.heads + slot) * kHeadDim + 2 * i;
+        if (a.q_hi) {
+            y0 *= a.q_scale;
+            y1 *= a.q_scale;
+            const uint32_t hi = pack_bf16x2(y0, y1);
+            *reinterpret_cast<uint32_t*>(a.q_hi + at) = hi;
+            *reinterpret_cast<uint32_t*>(a.q_lo + at) = pack_bf16x2(y0 - bf16lo(hi), y1 - bf16hi(hi));
+        } else {
+            float* dst = static_cast<float*>(a.q_out) + at;
+            dst[0] = y0;
+            dst[1] = y1;
+        }
         return;
     }
     const bool is_k = slot < a.heads + a.kv_heads;
