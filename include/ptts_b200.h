@@ -167,9 +167,10 @@ int ptts_b200_kv_check(ptts_b200_kv* kv);
  * p % capacity and a query at p attends positions max(0, p - context + 1) .. p (the mask of
  * transformer.rs:762-785, with the cache trimmed to context - 1 rows between calls). A call
  * adds at most capacity - context + 1 rows to it, so no row a query reads is overwritten.
- * Windowed streams run through ptts_b200_attend (+ kv_advance); the layer stack, rings,
- * load_prefix and set_lengths refuse them; copy_stream copies them whole into a stream of the
- * same capacity; kv_reset makes them appended streams again. */
+ * Windowed streams run through ptts_b200_attend (+ kv_advance) and through the layer stack's
+ * ptts_b200_forward (Mimi's transformer layers); ptts_b200_step, rings, load_prefix and
+ * set_lengths refuse them; copy_stream copies them whole into a stream of the same capacity;
+ * kv_reset makes them appended streams again. */
 int ptts_b200_kv_set_window(ptts_b200_kv* kv, const int32_t* streams_host, int n, int context,
                             void* cuda_stream);
 
@@ -206,9 +207,11 @@ int ptts_b200_attend(ptts_b200_kv* kv, int layer, const void* q, const void* k, 
  * Quantised linear: Q::LinearQ::forward (transformer.rs:195, :224, :627) for int8 weights with
  * one f32 scale per output row. y[m][n] = scale[n] * sum_k x[m][k] * w[n][k].
  * x [m][k] bf16, w [n][k] int8, scale [n] f32, y [m][n] f32; all device pointers.
- * k and n must be multiples of 64. With n a multiple of 128 it runs on the tcgen05 tensor cores
- * (the int8 weights widened to bf16 in shared memory, exactly; the scale applied to the f32
- * accumulator); other n on the mma.sync kernel.
+ * k and n must be multiples of 64. With n a multiple of 128 it runs on the tcgen05 tensor cores,
+ * the int8 weights widened exactly to bf16 on chip and the scale applied to the f32 accumulator:
+ * below 4096 rows widened in registers into tensor memory (the MMA's A operand), from 4096 rows
+ * on in a persistent kernel that widens them in shared memory. Other n run on the mma.sync
+ * kernel.
  * ------------------------------------------------------------------------------------- */
 int ptts_b200_linear_i8(int device, const void* x, const int8_t* w, const float* scale, int m,
                         int n, int k, float* y, void* cuda_stream);
