@@ -85,13 +85,25 @@ void rope_inv_freq(int head_dim, float max_period, float* out) {
 
 constexpr float kLog2e = 1.4426950408889634f;
 
-// Host-side tile list of the tcgen05 prefill kernel: (first row, rows) per 128 rows of each
-// sequence.
-std::vector<int2> make_tiles(const std::vector<int32_t>& offsets) {
-    std::vector<int2> t;
+// Host-side tile list of the tcgen05 prefill kernels: (first row, rows) per 128 rows of each
+// sequence, longest first. A tile's work grows with the keys its last row sees (its stream's
+// length before the call plus its offset in the sequence), and CTAs start in list order, so
+// the short tiles fill the last wave instead of a long one starting late.
+std::vector<int2> make_tiles(const std::vector<int32_t>& offsets, const int32_t* streams,
+                             const std::vector<int32_t>& h_len) {
+    std::vector<std::pair<long long, int2>> keyed;
     for (size_t i = 0; i + 1 < offsets.size(); ++i)
-        for (int r = offsets[i]; r < offsets[i + 1]; r += 128)
-            t.push_back(make_int2(r, std::min(128, offsets[i + 1] - r)));
+        for (int r = offsets[i]; r < offsets[i + 1]; r += 128) {
+            const int n = std::min(128, offsets[i + 1] - r);
+            keyed.push_back({(long long)h_len[streams[i]] + (r - offsets[i]) + n, make_int2(r, n)});
+        }
+    std::stable_sort(keyed.begin(), keyed.end(),
+                     [](const std::pair<long long, int2>& x, const std::pair<long long, int2>& y) {
+                         return x.first > y.first;
+                     });
+    std::vector<int2> t;
+    t.reserve(keyed.size());
+    for (const auto& k : keyed) t.push_back(k.second);
     return t;
 }
 
@@ -1276,7 +1288,7 @@ int ptts_b200_attend(ptts_b200_kv* kv, int layer, const void* q, const void* k, 
         }
         Tiles tiles;
         if (!decode) {
-            const std::vector<int2> t = make_tiles(offsets);
+            const std::vector<int2> t = make_tiles(offsets, streams_host, kv->h_len);
             tiles.dev = static_cast<int2*>(kv->tiles.need(sizeof(int2) * t.size()));
             tiles.n = (int)t.size();
             kv->staging.upload(const_cast<int2*>(tiles.dev), t.data(), sizeof(int2) * t.size(), s);
@@ -1508,7 +1520,7 @@ int ptts_b200_forward(ptts_b200_model* model, ptts_b200_kv* kv, const void* x,
         model->ws.size(c, rows);
         Tiles tiles;
         if (!decode) {
-            const std::vector<int2> t = make_tiles(offsets);
+            const std::vector<int2> t = make_tiles(offsets, streams_host, kv->h_len);
             tiles.dev = static_cast<int2*>(model->tiles.need(sizeof(int2) * t.size()));
             tiles.n = (int)t.size();
             tiles.windowed = windowed;

@@ -12,18 +12,24 @@
 //               w / 4 of the keys and of the output dims). Read S from TMEM, online softmax in
 //               the exp2 domain with the causal mask (the two halves of a row exchange their
 //               maximum through shared memory once per item), write P as bf16 hi/lo into TMEM
-//               (tcgen05.st); O accumulates in TMEM, rescaled there only when a row's maximum
-//               grows by more than 2^8; at each head's end O / l goes to the output row.
+//               (tcgen05.st) over the columns of S it came from; O accumulates in TMEM, rescaled
+//               there only when a row's maximum grows by more than 2^8 (the one case in which
+//               the softmax waits for the previous P.V); at each head's end O / l goes to the
+//               output row.
 //   warp 8      lane 0 issues the MMAs (kind::f16, M = 128, N = 64, bf16):
 //               S = Q_hi K^T + Q_lo K^T     A = Q (smem, K-major), B = K (smem, K-major)
 //               O += P_hi V + P_lo V        A = P (TMEM), B = V (smem, MN-major)
-//               S runs up to two items ahead of P.V (two S buffers in TMEM), across heads.
+//               Two S/P buffers in TMEM: S(i + 2) reuses buffer i % 2 once P.V(i) has read P(i)
+//               from it, so S runs an item ahead of the softmax, across heads, and the softmax
+//               of item i + 1 overlaps P.V(i).
 //   warp 9      lane 0 copies with TMA each head's Q tiles (the bf16 hi/lo planes the q producer
 //               wrote) and each item's K and V tiles (64 keys x one head, 128-byte swizzle) into
 //               two-slot K and V rings: a K slot frees once its S product is done, so K runs an
 //               item ahead of V.
-// TMEM (256 columns): S0 0-63, S1 64-127, O 128-191, P hi 192-223, P lo 224-255 (bf16 pairs,
-// one row per lane). Keys past the tile's last position are masked in the softmax and their V
+// TMEM (256 columns): S/P buffers 0-63 and 64-127, O 128-191. In a buffer, S is f32 (column =
+// key); P replaces it as bf16 pairs, each half of the keys within its own 32 columns: hi of
+// keys 32h + 0..31 in columns 32h + 0..15, lo in 32h + 16..31 (one row per lane), so a thread
+// overwrites only the S values it has read itself. Keys past the tile's last position are masked in the softmax and their V
 // rows zeroed before P.V (the slots may hold anything, and 0 x NaN is NaN). Every wait is bounded
 // and sets DEV_ERR_TIMEOUT; a CTA that timed out waits, bounded, for its copies. Splitting q and
 // P into hi + lo keeps the products f32-grade, as in the linears.
@@ -49,7 +55,7 @@ constexpr int kOffBar = kOffKV + kSlots * 2 * kKVBytes;
 constexpr int kSmemF = 1024 + kOffBar + 256;
 static_assert(2 * (kSmemF + 1024) <= 228 * 1024, "two CTAs per SM");
 constexpr uint32_t kTmemColsF = 256;
-constexpr uint32_t kColO = 128, kColPh = 192, kColPl = 224;
+constexpr uint32_t kColO = 128;
 
 // kind::f16, D f32, A/B bf16, M = 128, N = 64; kIdescPVf additionally marks B MN-major.
 constexpr uint32_t kIdescSf = (1u << 4) | (1u << 7) | (1u << 10) | (8u << 17) | (8u << 24);
@@ -130,11 +136,15 @@ __device__ __forceinline__ void fa_tma(uint32_t dst, const CUtensorMap* map, int
 }
 
 // Barriers: K and V full and empty per slot (separate rings: a K slot frees once its S product is
-// done, a V slot once its P.V is), Q ready and free per buffer, S full and free per buffer, P full,
-// O full.
+// done, a V slot once its P.V is), Q ready and free per buffer, S full and free per S/P buffer (free
+// once the P.V that read its P is done), P full and P.V done per S/P buffer. Item i uses phase
+// i / 2 of buffer i % 2's barriers. A waiter must know that the barrier has not fallen two or more
+// phases behind the one it asks for (a parity wait would take the older phase of the same parity
+// as done) nor run past it: S(i) in TMEM means P.V(i - 2) is done, and P.V(i + 2) needs this
+// warp's P(i + 2), so every wait below asks for a phase within one of the barrier's own.
 struct FaBars {
     uint64_t kfull[kSlots], kempty[kSlots], vfull[kSlots], vempty[kSlots], qready[2], qfree[2], sfull[2],
-        sfree[2], pfull, ofull;
+        sfree[2], pfull[2], ofull[2];
 };
 static_assert(sizeof(FaBars) + 4 <= 256, "barriers fit the tail");
 
@@ -191,10 +201,10 @@ __global__ void __launch_bounds__(kThreadsF, 2) prefill_fa_kernel(PrefillArgs a,
             mbar_init(&b->qready[i], 1);
             mbar_init(&b->qfree[i], 1);
             mbar_init(&b->sfull[i], 1);
-            mbar_init(&b->sfree[i], kSoftWarps);
+            mbar_init(&b->sfree[i], 1);
+            mbar_init(&b->pfull[i], kSoftWarps);
+            mbar_init(&b->ofull[i], 1);
         }
-        mbar_init(&b->pfull, kSoftWarps);
-        mbar_init(&b->ofull, 1);
         s_k_issued = 0;
         s_v_issued = 0;
         s_q_issued = 0;
@@ -248,9 +258,6 @@ __global__ void __launch_bounds__(kThreadsF, 2) prefill_fa_kernel(PrefillArgs a,
                 fa_after();
                 fa_ld32(tmem + lane_base + (uint32_t)((i & 1) * 64 + 32 * half), s);
                 fa_wait_ld();
-                fa_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&b->sfree[i & 1]);
                 // q came scaled by log2(e) / sqrt(D): S is in the exp2 domain already.
                 const int key0 = kt * KT + 32 * half;
                 if (__all_sync(0xffffffffu, key0 + 31 <= pos)) {  // no key of this half is masked
@@ -263,8 +270,6 @@ __global__ void __launch_bounds__(kThreadsF, 2) prefill_fa_kernel(PrefillArgs a,
                         mt = fmaxf(mt, s[j]);
                     }
                 }
-                // P.V of the previous item has read P and added into O.
-                if (kt > 0) ok = __all_sync(0xffffffffu, mbar_wait(&b->ofull, (i - 1) & 1));
             }
             // The row's maximum over both halves (and a timeout in either warp ends both loops).
             s_xmax[i & 1][half][r] = mt;
@@ -277,6 +282,15 @@ __global__ void __launch_bounds__(kThreadsF, 2) prefill_fa_kernel(PrefillArgs a,
             const bool raise = kt == 0 ? true : mt > m + kRaise;
             const float mnew = raise ? fmaxf(mt, m) : m;
             if (kt > 0 && __any_sync(0xffffffffu, raise)) {  // rescale this half of O in TMEM
+                // O must hold P.V(i - 1) first (its commit follows every earlier P.V). The partner
+                // warp (same rows, same maxima) takes this branch too, so both agree on a timeout.
+                const bool done =
+                    __all_sync(0xffffffffu, mbar_wait(&b->ofull[(i - 1) & 1], ((i - 1) >> 1) & 1));
+                if (pair_any(quarter, !done)) {
+                    set_error(a.err, DEV_ERR_TIMEOUT);
+                    break;
+                }
+                fa_after();
                 const float f = raise ? fa_exp2(m - mnew) : 1.f;
                 l *= f;
                 float ot[32];
@@ -288,7 +302,9 @@ __global__ void __launch_bounds__(kThreadsF, 2) prefill_fa_kernel(PrefillArgs a,
                 fa_st32(tmem + lane_base + kColO + 32 * half, w);
             }
             m = mnew;
-            // P(i) into TMEM: this half's 32 keys, 16 columns of bf16 pairs per plane.
+            // P(i) into TMEM over this half's S columns: its 32 keys, 16 columns of bf16 pairs per
+            // plane (hi, then lo). Only this thread's own lane and columns, already read.
+            const uint32_t pcol = (uint32_t)((i & 1) * 64 + 32 * half);
 #pragma unroll
             for (int c = 0; c < 2; ++c) {
                 uint32_t ph[8], pl[8];
@@ -299,8 +315,8 @@ __global__ void __launch_bounds__(kThreadsF, 2) prefill_fa_kernel(PrefillArgs a,
                     ph[j] = pack_bf16x2(e0, e1);
                     pl[j] = pack_bf16x2(e0 - bf16lo(ph[j]), e1 - bf16hi(ph[j]));
                 }
-                fa_st8(tmem + lane_base + kColPh + 16 * half + 8 * c, ph);
-                fa_st8(tmem + lane_base + kColPl + 16 * half + 8 * c, pl);
+                fa_st8(tmem + lane_base + pcol + 8 * c, ph);
+                fa_st8(tmem + lane_base + pcol + 16 + 8 * c, pl);
             }
             asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
             if (kt == n_kt - 1 && (kt + 1) * KT - 1 > pos_max) {
@@ -316,11 +332,11 @@ __global__ void __launch_bounds__(kThreadsF, 2) prefill_fa_kernel(PrefillArgs a,
             }
             fa_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&b->pfull);
+            if (lane == 0) mbar_arrive(&b->pfull[i & 1]);
             if (kt < n_kt - 1) continue;
             // The head's last tile: the row sum over both halves, then O / l into this half of
             // the output row (16-byte stores).
-            ok = __all_sync(0xffffffffu, mbar_wait(&b->ofull, i & 1));
+            ok = __all_sync(0xffffffffu, mbar_wait(&b->ofull[i & 1], (i >> 1) & 1));
             s_xsum[half][r] = l;  // read by the partner before either reaches the next head's end
             if (pair_any(quarter, !ok)) {
                 set_error(a.err, DEV_ERR_TIMEOUT);
@@ -364,8 +380,8 @@ __global__ void __launch_bounds__(kThreadsF, 2) prefill_fa_kernel(PrefillArgs a,
     } else if (warp == kMmaWarp && lane == 0) {
         // ---- MMA issuer ----------------------------------------------------------------------
         // Two independent streams of work, polled without blocking: S(i) once item i's K has
-        // landed, its Q is in and its S buffer is free; P.V(i) once P(i) is in TMEM and V(i) has
-        // landed. S thus runs up to two items ahead of P.V, across heads too. Bounded: no progress
+        // landed, its Q is in and its S/P buffer is free (P.V(i - 2) done); P.V(i) once P(i) is
+        // in TMEM and V(i) has landed. S thus runs an item ahead of the softmax, across heads. Bounded: no progress
         // for kWaitLimitCycles ends the loop with DEV_ERR_TIMEOUT.
         auto s_ready = [&](int i) {
             const int hh = i / n_kt;
@@ -392,15 +408,18 @@ __global__ void __launch_bounds__(kThreadsF, 2) prefill_fa_kernel(PrefillArgs a,
         auto issue_pv = [&](int i) {
             fa_after();
             const uint64_t dv = desc_mn(base + kOffKV + (i % kSlots) * 2 * kKVBytes + kKVBytes);
+            const uint32_t pb = tmem + (uint32_t)((i & 1) * 64);
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk) {  // 64 keys = 4 x 16: P 8 columns, V 2 x 1024 bytes
+                // Keys 16 kk.. of P: half kk / 2 of the buffer, its hi columns 8 (kk % 2) on, lo 16 on.
+                const uint32_t ph = pb + 32 * (kk >> 1) + 8 * (kk & 1);
                 // O accumulates over the head's key tiles; its first tile starts it afresh.
-                fa_mma_ts(tmem + kColO, tmem + kColPh + 8 * kk, dv + 128 * kk, kIdescPVf,
-                          (i % n_kt != 0 || kk) ? 1u : 0u);
-                fa_mma_ts(tmem + kColO, tmem + kColPl + 8 * kk, dv + 128 * kk, kIdescPVf, 1u);
+                fa_mma_ts(tmem + kColO, ph, dv + 128 * kk, kIdescPVf, (i % n_kt != 0 || kk) ? 1u : 0u);
+                fa_mma_ts(tmem + kColO, ph + 16, dv + 128 * kk, kIdescPVf, 1u);
             }
-            fa_commit(&b->ofull);
+            fa_commit(&b->ofull[i & 1]);
             fa_commit(&b->vempty[i % kSlots]);  // P.V(i) has read the V slot
+            fa_commit(&b->sfree[i & 1]);         // ... and P(i): the buffer takes S(i + 2)
         };
         int next_s = 0, next_pv = 0;
         long long t0 = clock64();
@@ -410,7 +429,7 @@ __global__ void __launch_bounds__(kThreadsF, 2) prefill_fa_kernel(PrefillArgs a,
                 issue_s(next_s++);
                 progressed = true;
             }
-            if (next_pv < next_s && mbar_test_wait(&b->pfull, next_pv & 1) &&
+            if (next_pv < next_s && mbar_test_wait(&b->pfull[next_pv & 1], (next_pv >> 1) & 1) &&
                 mbar_test_wait(&b->vfull[next_pv % kSlots], (next_pv / kSlots) & 1)) {
                 issue_pv(next_pv++);
                 progressed = true;
