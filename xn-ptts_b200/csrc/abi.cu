@@ -86,24 +86,26 @@ void rope_inv_freq(int head_dim, float max_period, float* out) {
 constexpr float kLog2e = 1.4426950408889634f;
 
 // Host-side tile list of the tcgen05 prefill kernels: (first row, rows) per 128 rows of each
-// sequence, longest first. A tile's work grows with the keys its last row sees (its stream's
-// length before the call plus its offset in the sequence), and CTAs start in list order, so
-// the short tiles fill the last wave instead of a long one starting late.
+// sequence. A tile's work grows with the keys its last row sees (its stream's length before the
+// call plus its offset in the sequence), and CTAs start in list order, so the sequences come
+// longest first (the short ones fill the last wave instead of a long one starting late), each
+// sequence's tiles together and last tile first (they read the same keys, which stay in L2).
 std::vector<int2> make_tiles(const std::vector<int32_t>& offsets, const int32_t* streams,
                              const std::vector<int32_t>& h_len) {
-    std::vector<std::pair<long long, int2>> keyed;
+    std::vector<std::pair<long long, int>> seqs;  // (keys seen by the last row, sequence)
     for (size_t i = 0; i + 1 < offsets.size(); ++i)
-        for (int r = offsets[i]; r < offsets[i + 1]; r += 128) {
-            const int n = std::min(128, offsets[i + 1] - r);
-            keyed.push_back({(long long)h_len[streams[i]] + (r - offsets[i]) + n, make_int2(r, n)});
-        }
-    std::stable_sort(keyed.begin(), keyed.end(),
-                     [](const std::pair<long long, int2>& x, const std::pair<long long, int2>& y) {
+        if (offsets[i + 1] > offsets[i])
+            seqs.push_back({(long long)h_len[streams[i]] + offsets[i + 1] - offsets[i], (int)i});
+    std::stable_sort(seqs.begin(), seqs.end(),
+                     [](const std::pair<long long, int>& x, const std::pair<long long, int>& y) {
                          return x.first > y.first;
                      });
     std::vector<int2> t;
-    t.reserve(keyed.size());
-    for (const auto& k : keyed) t.push_back(k.second);
+    for (const auto& q : seqs) {
+        const int i = q.second, first = offsets[i], end = offsets[i + 1];
+        for (int r = first + (end - first - 1) / 128 * 128; r >= first; r -= 128)
+            t.push_back(make_int2(r, std::min(128, end - r)));
+    }
     return t;
 }
 

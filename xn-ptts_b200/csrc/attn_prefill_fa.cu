@@ -10,8 +10,9 @@
 // 1-8 key tiles per head: one head per CTA left the chain S -> softmax -> P.V mostly idle).
 //   warps 0-7   softmax: two threads per query row (row 32 (w % 4) + lane = TMEM lane, half
 //               w / 4 of the keys and of the output dims). Read S from TMEM, online softmax in
-//               the exp2 domain with the causal mask (the two halves of a row exchange their
-//               maximum through shared memory once per item), write P as bf16 hi/lo into TMEM
+//               the exp2 domain with the causal mask (the two halves of a row agree through one
+//               barrier.red per item that the maximum stays, or exchange it through shared
+//               memory when a head starts or it must be raised), write P as bf16 hi/lo into TMEM
 //               (tcgen05.st) over the columns of S it came from; O accumulates in TMEM, rescaled
 //               there only when a row's maximum grows by more than 2^8 (the one case in which
 //               the softmax waits for the previous P.V); at each head's end O / l goes to the
@@ -19,18 +20,19 @@
 //   warp 8      lane 0 issues the MMAs (kind::f16, M = 128, N = 64, bf16):
 //               S = Q_hi K^T + Q_lo K^T     A = Q (smem, K-major), B = K (smem, K-major)
 //               O += P_hi V + P_lo V        A = P (TMEM), B = V (smem, MN-major)
-//               Two S/P buffers in TMEM: S(i + 2) reuses buffer i % 2 once P.V(i) has read P(i)
-//               from it, so S runs an item ahead of the softmax, across heads, and the softmax
-//               of item i + 1 overlaps P.V(i).
+//               Three S/P buffers in TMEM: S(i + 3) reuses buffer i % 3 once P.V(i) has read
+//               P(i) from it, so S runs up to two items ahead of the softmax, across heads, and
+//               the softmax of items i + 1 and i + 2 overlaps P.V(i).
 //   warp 9      lane 0 copies with TMA each head's Q tiles (the bf16 hi/lo planes the q producer
 //               wrote) and each item's K and V tiles (64 keys x one head, 128-byte swizzle) into
-//               two-slot K and V rings: a K slot frees once its S product is done, so K runs an
-//               item ahead of V.
-// TMEM (256 columns): S/P buffers 0-63 and 64-127, O 128-191. In a buffer, S is f32 (column =
-// key); P replaces it as bf16 pairs, each half of the keys within its own 32 columns: hi of
-// keys 32h + 0..31 in columns 32h + 0..15, lo in 32h + 16..31 (one row per lane), so a thread
-// overwrites only the S values it has read itself. Keys past the tile's last position are masked in the softmax and their V
-// rows zeroed before P.V (the slots may hold anything, and 0 x NaN is NaN). Every wait is bounded
+//               a two-slot K ring and a three-slot V ring: a K slot frees once its S product is
+//               done, a V slot once its P.V is.
+// TMEM (256 columns): S/P buffers 0-63, 64-127 and 128-191, O 192-255. In a buffer, S is f32
+// (column = key); P replaces it as bf16 pairs, each half of the keys within its own 32 columns:
+// hi of keys 32h + 0..31 in columns 32h + 0..15, lo in 32h + 16..31 (one row per lane), so a
+// thread overwrites only the S values it has read itself. Keys past the tile's last position are
+// masked in the softmax and their V rows zeroed before P.V (the slots may hold anything, and
+// 0 x NaN is NaN). Every wait is bounded
 // and sets DEV_ERR_TIMEOUT; a CTA that timed out waits, bounded, for its copies. Splitting q and
 // P into hi + lo keeps the products f32-grade, as in the linears.
 #include "common.cuh"
@@ -47,15 +49,20 @@ constexpr int kMmaWarp = kSoftWarps, kLoadWarp = kSoftWarps + 1;
 constexpr int kThreadsF = (kSoftWarps + 2) * 32;
 constexpr int kQBytes = QT * 128;  // one plane of one head's q: 128 rows x 64 bf16
 constexpr int kKVBytes = KT * 128; // one head's K (or V) tile
-constexpr int kSlots = 2;          // K/V ring
+constexpr int kKSlots = 2;         // K ring
+constexpr int kVSlots = 3;         // V ring (one per S/P buffer: item i's V is never two phases behind)
 // Shared layout (1024-aligned tiles): two Q buffers (hi, lo), the K/V ring (K, V per slot).
 constexpr int kOffQ = 0;                               // buffer b: hi at b * 2 kQBytes, lo + kQBytes
-constexpr int kOffKV = 2 * 2 * kQBytes;                // slot s: K at s * 2 kKVBytes, V + kKVBytes
-constexpr int kOffBar = kOffKV + kSlots * 2 * kKVBytes;
+constexpr int kOffK = 2 * 2 * kQBytes;                 // K slot s at s * kKVBytes
+constexpr int kOffV = kOffK + kKSlots * kKVBytes;      // V slot s at s * kKVBytes
+constexpr int kOffBar = kOffV + kVSlots * kKVBytes;
 constexpr int kSmemF = 1024 + kOffBar + 256;
-static_assert(2 * (kSmemF + 1024) <= 228 * 1024, "two CTAs per SM");
+constexpr int kStaticSmemF = 4 * 1024;  // s_xmax, s_xsum and the issue counters (3,088 bytes)
+static_assert(2 * (kSmemF + kStaticSmemF + 1024) <= 228 * 1024, "two CTAs per SM");
 constexpr uint32_t kTmemColsF = 256;
-constexpr uint32_t kColO = 128;
+constexpr int kBufs = 3;  // S/P buffers in TMEM, 64 columns each
+constexpr uint32_t kColO = 64 * kBufs;
+static_assert(kColO + 64 <= kTmemColsF, "S/P buffers and O fit the allocation");
 
 // kind::f16, D f32, A/B bf16, M = 128, N = 64; kIdescPVf additionally marks B MN-major.
 constexpr uint32_t kIdescSf = (1u << 4) | (1u << 7) | (1u << 10) | (8u << 17) | (8u << 24);
@@ -138,13 +145,14 @@ __device__ __forceinline__ void fa_tma(uint32_t dst, const CUtensorMap* map, int
 // Barriers: K and V full and empty per slot (separate rings: a K slot frees once its S product is
 // done, a V slot once its P.V is), Q ready and free per buffer, S full and free per S/P buffer (free
 // once the P.V that read its P is done), P full and P.V done per S/P buffer. Item i uses phase
-// i / 2 of buffer i % 2's barriers. A waiter must know that the barrier has not fallen two or more
-// phases behind the one it asks for (a parity wait would take the older phase of the same parity
-// as done) nor run past it: S(i) in TMEM means P.V(i - 2) is done, and P.V(i + 2) needs this
-// warp's P(i + 2), so every wait below asks for a phase within one of the barrier's own.
+// i / n of slot or buffer i % n of a ring of n. A parity wait takes an older phase of the same
+// parity as done, so a waiter must know that the barrier is not two or more phases behind the one
+// it asks for, nor past it. Here S(i) in TMEM means P.V(i - kBufs) is done (so V(i - kVSlots) has
+// landed), and neither S(i + kBufs) nor V(i + kVSlots) can start before P.V(i), which needs the
+// softmax warps' P(i): every wait below asks for a phase within one of the barrier's own.
 struct FaBars {
-    uint64_t kfull[kSlots], kempty[kSlots], vfull[kSlots], vempty[kSlots], qready[2], qfree[2], sfull[2],
-        sfree[2], pfull[2], ofull[2];
+    uint64_t kfull[kKSlots], kempty[kKSlots], vfull[kVSlots], vempty[kVSlots], qready[2], qfree[2], sfull[kBufs],
+        sfree[kBufs], pfull[kBufs], ofull[kBufs];
 };
 static_assert(sizeof(FaBars) + 4 <= 256, "barriers fit the tail");
 
@@ -191,15 +199,19 @@ __global__ void __launch_bounds__(kThreadsF, 2) prefill_fa_kernel(PrefillArgs a,
     const int h0 = blockIdx.y * kHeadsPerCta;
 
     if (tid == 0) {
-        for (int i = 0; i < kSlots; ++i) {
+        for (int i = 0; i < kKSlots; ++i) {
             mbar_init(&b->kfull[i], 1);
             mbar_init(&b->kempty[i], 1);
+        }
+        for (int i = 0; i < kVSlots; ++i) {
             mbar_init(&b->vfull[i], 1);
             mbar_init(&b->vempty[i], 1);
         }
         for (int i = 0; i < 2; ++i) {
             mbar_init(&b->qready[i], 1);
             mbar_init(&b->qfree[i], 1);
+        }
+        for (int i = 0; i < kBufs; ++i) {
             mbar_init(&b->sfull[i], 1);
             mbar_init(&b->sfree[i], 1);
             mbar_init(&b->pfull[i], kSoftWarps);
@@ -250,80 +262,92 @@ __global__ void __launch_bounds__(kThreadsF, 2) prefill_fa_kernel(PrefillArgs a,
                 m = -1e30f;
                 l = 0.f;
             }
-            // S(i) from TMEM: this thread's row, its 32 keys; then the buffer goes back.
-            bool ok = __all_sync(0xffffffffu, mbar_wait(&b->sfull[i & 1], (i >> 1) & 1));
+            // S(i) from TMEM: this thread's row, its 32 keys.
+            const int buf = i % kBufs;
+            const uint32_t ph_i = (uint32_t)(i / kBufs) & 1u;  // phase parity of item i's barriers
+            bool ok = __all_sync(0xffffffffu, mbar_wait(&b->sfull[buf], ph_i));
             float s[32];
             float mt = -INFINITY;
             if (ok) {
                 fa_after();
-                fa_ld32(tmem + lane_base + (uint32_t)((i & 1) * 64 + 32 * half), s);
+                fa_ld32(tmem + lane_base + (uint32_t)(buf * 64 + 32 * half), s);
                 fa_wait_ld();
                 // q came scaled by log2(e) / sqrt(D): S is in the exp2 domain already.
                 const int key0 = kt * KT + 32 * half;
-                if (__all_sync(0xffffffffu, key0 + 31 <= pos)) {  // no key of this half is masked
+                if (!__all_sync(0xffffffffu, key0 + 31 <= pos)) {  // some key of this half is masked
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) mt = fmaxf(mt, s[j]);
-                } else {
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) {
-                        s[j] = key0 + j <= pos ? s[j] : -INFINITY;
-                        mt = fmaxf(mt, s[j]);
-                    }
+                    for (int j = 0; j < 32; ++j) s[j] = key0 + j <= pos ? s[j] : -INFINITY;
                 }
+                float m4[4] = {s[0], s[1], s[2], s[3]};  // four independent chains
+#pragma unroll
+                for (int j = 4; j < 32; ++j) m4[j & 3] = fmaxf(m4[j & 3], s[j]);
+                mt = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
             }
-            // The row's maximum over both halves (and a timeout in either warp ends both loops).
-            s_xmax[i & 1][half][r] = mt;
-            if (pair_any(quarter, !ok)) {
-                set_error(a.err, DEV_ERR_TIMEOUT);
-                break;
-            }
-            mt = fmaxf(mt, s_xmax[i & 1][half ^ 1][r]);
-            fa_after();
-            const bool raise = kt == 0 ? true : mt > m + kRaise;
-            const float mnew = raise ? fmaxf(mt, m) : m;
-            if (kt > 0 && __any_sync(0xffffffffu, raise)) {  // rescale this half of O in TMEM
-                // O must hold P.V(i - 1) first (its commit follows every earlier P.V). The partner
-                // warp (same rows, same maxima) takes this branch too, so both agree on a timeout.
-                const bool done =
-                    __all_sync(0xffffffffu, mbar_wait(&b->ofull[(i - 1) & 1], ((i - 1) >> 1) & 1));
-                if (pair_any(quarter, !done)) {
+            // One barrier.red over the row quarter's two warps: unless a head starts, a wait
+            // timed out, or some row's maximum passed m + kRaise, m stays and nothing is
+            // exchanged. Otherwise the halves exchange their maxima (and timeouts) and raise m.
+            if (pair_any(quarter, !ok || kt == 0 || mt > m + kRaise)) {
+                s_xmax[i & 1][half][r] = mt;
+                if (pair_any(quarter, !ok)) {
                     set_error(a.err, DEV_ERR_TIMEOUT);
                     break;
                 }
+                mt = fmaxf(mt, s_xmax[i & 1][half ^ 1][r]);
                 fa_after();
-                const float f = raise ? fa_exp2(m - mnew) : 1.f;
-                l *= f;
-                float ot[32];
-                fa_ld32(tmem + lane_base + kColO + 32 * half, ot);
-                fa_wait_ld();
-                uint32_t w[32];
+                const bool raise = kt == 0 ? true : mt > m + kRaise;
+                const float mnew = raise ? fmaxf(mt, m) : m;
+                if (kt > 0 && __any_sync(0xffffffffu, raise)) {  // rescale this half of O in TMEM
+                    // O must hold P.V(i - 1) first (its commit follows every earlier P.V). The
+                    // partner warp (same rows, same maxima) takes this branch too, so both agree
+                    // on a timeout.
+                    const bool done =
+                        __all_sync(0xffffffffu, mbar_wait(&b->ofull[(i - 1) % kBufs], ((i - 1) / kBufs) & 1));
+                    if (pair_any(quarter, !done)) {
+                        set_error(a.err, DEV_ERR_TIMEOUT);
+                        break;
+                    }
+                    fa_after();
+                    const float f = raise ? fa_exp2(m - mnew) : 1.f;
+                    l *= f;
+                    float ot[32];
+                    fa_ld32(tmem + lane_base + kColO + 32 * half, ot);
+                    fa_wait_ld();
+                    uint32_t w[32];
 #pragma unroll
-                for (int j = 0; j < 32; ++j) w[j] = __float_as_uint(ot[j] * f);
-                fa_st32(tmem + lane_base + kColO + 32 * half, w);
+                    for (int j = 0; j < 32; ++j) w[j] = __float_as_uint(ot[j] * f);
+                    fa_st32(tmem + lane_base + kColO + 32 * half, w);
+                }
+                m = mnew;
             }
-            m = mnew;
             // P(i) into TMEM over this half's S columns: its 32 keys, 16 columns of bf16 pairs per
-            // plane (hi, then lo). Only this thread's own lane and columns, already read.
-            const uint32_t pcol = (uint32_t)((i & 1) * 64 + 32 * half);
+            // plane (hi, then lo). Only this thread's own lane and columns, already read. Pairs
+            // of keys go through the packed f32x2 add and fma: s - m, the row sum (two chains)
+            // and lo = e - hi (exact: one rounding of an exact difference).
+            const uint32_t pcol = (uint32_t)(buf * 64 + 32 * half);
+            const float2 neg_m = make_float2(-m, -m), minus1 = make_float2(-1.f, -1.f);
+            float2 sum[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
             for (int c = 0; c < 2; ++c) {
                 uint32_t ph[8], pl[8];
 #pragma unroll
                 for (int j = 0; j < 8; ++j) {
-                    const float e0 = fa_exp2(s[16 * c + 2 * j] - m), e1 = fa_exp2(s[16 * c + 2 * j + 1] - m);
-                    l += e0 + e1;
-                    ph[j] = pack_bf16x2(e0, e1);
-                    pl[j] = pack_bf16x2(e0 - bf16lo(ph[j]), e1 - bf16hi(ph[j]));
+                    const float2 x = __fadd2_rn(make_float2(s[16 * c + 2 * j], s[16 * c + 2 * j + 1]), neg_m);
+                    const float2 e = make_float2(fa_exp2(x.x), fa_exp2(x.y));
+                    sum[j & 1] = __fadd2_rn(sum[j & 1], e);
+                    ph[j] = pack_bf16x2(e.x, e.y);
+                    const float2 lo = __ffma2_rn(make_float2(bf16lo(ph[j]), bf16hi(ph[j])), minus1, e);
+                    pl[j] = pack_bf16x2(lo.x, lo.y);
                 }
                 fa_st8(tmem + lane_base + pcol + 8 * c, ph);
                 fa_st8(tmem + lane_base + pcol + 16 + 8 * c, pl);
             }
+            l += (sum[0].x + sum[1].x) + (sum[0].y + sum[1].y);
             asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
             if (kt == n_kt - 1 && (kt + 1) * KT - 1 > pos_max) {
                 // Zero the V rows past the tile's last key (read by P.V with P = 0), once V(i)
                 // has landed (its copy runs apart from K's).
-                if (!mbar_wait(&b->vfull[i % kSlots], (i / kSlots) & 1)) set_error(a.err, DEV_ERR_TIMEOUT);
-                unsigned char* vt = sm + kOffKV + (i % kSlots) * 2 * kKVBytes + kKVBytes;
+                if (!mbar_wait(&b->vfull[i % kVSlots], (i / kVSlots) & 1)) set_error(a.err, DEV_ERR_TIMEOUT);
+                unsigned char* vt = sm + kOffV + (i % kVSlots) * kKVBytes;
                 const int first = pos_max + 1 - kt * KT;
                 for (int c = first * 8 + tid; c < KT * 8; c += 32 * kSoftWarps)
                     *reinterpret_cast<uint4*>(vt + 16 * c) = make_uint4(0u, 0u, 0u, 0u);
@@ -332,11 +356,11 @@ __global__ void __launch_bounds__(kThreadsF, 2) prefill_fa_kernel(PrefillArgs a,
             }
             fa_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&b->pfull[i & 1]);
+            if (lane == 0) mbar_arrive(&b->pfull[buf]);
             if (kt < n_kt - 1) continue;
             // The head's last tile: the row sum over both halves, then O / l into this half of
             // the output row (16-byte stores).
-            ok = __all_sync(0xffffffffu, mbar_wait(&b->ofull[i & 1], (i >> 1) & 1));
+            ok = __all_sync(0xffffffffu, mbar_wait(&b->ofull[buf], ph_i));
             s_xsum[half][r] = l;  // read by the partner before either reaches the next head's end
             if (pair_any(quarter, !ok)) {
                 set_error(a.err, DEV_ERR_TIMEOUT);
@@ -379,36 +403,37 @@ __global__ void __launch_bounds__(kThreadsF, 2) prefill_fa_kernel(PrefillArgs a,
         }
     } else if (warp == kMmaWarp && lane == 0) {
         // ---- MMA issuer ----------------------------------------------------------------------
-        // Two independent streams of work, polled without blocking: S(i) once item i's K has
-        // landed, its Q is in and its S/P buffer is free (P.V(i - 2) done); P.V(i) once P(i) is
-        // in TMEM and V(i) has landed. S thus runs an item ahead of the softmax, across heads. Bounded: no progress
-        // for kWaitLimitCycles ends the loop with DEV_ERR_TIMEOUT.
-        auto s_ready = [&](int i) {
+        // A fixed order, S(0 .. kBufs - 1), then per item i: P.V(i) once P(i) is in TMEM and V(i)
+        // has landed, S(i + kBufs) once its K has landed, its Q is in and P.V(i) has freed the
+        // buffer. Every wait suspends the thread instead of polling: this warp shares its SM
+        // sub-partition with two softmax warps of each CTA, whose issue slots a polling loop
+        // would take. Bounded: a wait that gives up ends the loop with DEV_ERR_TIMEOUT.
+        auto wait_s = [&](int i) {
             const int hh = i / n_kt;
-            return mbar_test_wait(&b->kfull[i % kSlots], (i / kSlots) & 1) &&
-                   mbar_test_wait(&b->qready[hh & 1], (hh >> 1) & 1) &&
-                   (i < 2 || mbar_test_wait(&b->sfree[i & 1], ((i >> 1) & 1) ^ 1));
+            return mbar_wait(&b->kfull[i % kKSlots], (i / kKSlots) & 1) &&
+                   mbar_wait(&b->qready[hh & 1], (hh >> 1) & 1) &&
+                   (i < kBufs || mbar_wait(&b->sfree[i % kBufs], ((i / kBufs) & 1) ^ 1));
         };
         auto issue_s = [&](int i) {
-            const int hh = i / n_kt, slot = i % kSlots;
+            const int hh = i / n_kt, slot = i % kKSlots;
             fa_after();
             const uint32_t qa = base + kOffQ + (hh & 1) * 2 * kQBytes;
             const uint64_t dqh = desc_k(qa), dql = desc_k(qa + kQBytes);
-            const uint64_t dk = desc_k(base + kOffKV + slot * 2 * kKVBytes);  // K half of the slot
-            const uint32_t d = tmem + (uint32_t)((i & 1) * 64);
+            const uint64_t dk = desc_k(base + kOffK + slot * kKVBytes);
+            const uint32_t d = tmem + (uint32_t)((i % kBufs) * 64);
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk) {  // head dim 64 = 4 x 16: 32 bytes per step
                 fa_mma_ss(d, dqh + 2 * kk, dk + 2 * kk, kIdescSf, kk ? 1u : 0u);
                 fa_mma_ss(d, dql + 2 * kk, dk + 2 * kk, kIdescSf, 1u);
             }
-            fa_commit(&b->sfull[i & 1]);
+            fa_commit(&b->sfull[i % kBufs]);
             fa_commit(&b->kempty[slot]);  // S(i) has read the K slot
             if (i % n_kt == n_kt - 1) fa_commit(&b->qfree[hh & 1]);  // the head's Q tiles are read
         };
         auto issue_pv = [&](int i) {
             fa_after();
-            const uint64_t dv = desc_mn(base + kOffKV + (i % kSlots) * 2 * kKVBytes + kKVBytes);
-            const uint32_t pb = tmem + (uint32_t)((i & 1) * 64);
+            const uint64_t dv = desc_mn(base + kOffV + (i % kVSlots) * kKVBytes);
+            const uint32_t pb = tmem + (uint32_t)((i % kBufs) * 64);
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk) {  // 64 keys = 4 x 16: P 8 columns, V 2 x 1024 bytes
                 // Keys 16 kk.. of P: half kk / 2 of the buffer, its hi columns 8 (kk % 2) on, lo 16 on.
@@ -417,32 +442,21 @@ __global__ void __launch_bounds__(kThreadsF, 2) prefill_fa_kernel(PrefillArgs a,
                 fa_mma_ts(tmem + kColO, ph, dv + 128 * kk, kIdescPVf, (i % n_kt != 0 || kk) ? 1u : 0u);
                 fa_mma_ts(tmem + kColO, ph + 16, dv + 128 * kk, kIdescPVf, 1u);
             }
-            fa_commit(&b->ofull[i & 1]);
-            fa_commit(&b->vempty[i % kSlots]);  // P.V(i) has read the V slot
-            fa_commit(&b->sfree[i & 1]);         // ... and P(i): the buffer takes S(i + 2)
+            fa_commit(&b->ofull[i % kBufs]);
+            fa_commit(&b->vempty[i % kVSlots]);  // P.V(i) has read the V slot
+            fa_commit(&b->sfree[i % kBufs]);     // ... and P(i): the buffer takes S(i + kBufs)
         };
-        int next_s = 0, next_pv = 0;
-        long long t0 = clock64();
-        while (next_pv < n_items) {
-            bool progressed = false;
-            if (next_s < n_items && s_ready(next_s)) {
-                issue_s(next_s++);
-                progressed = true;
-            }
-            if (next_pv < next_s && mbar_test_wait(&b->pfull[next_pv & 1], (next_pv >> 1) & 1) &&
-                mbar_test_wait(&b->vfull[next_pv % kSlots], (next_pv / kSlots) & 1)) {
-                issue_pv(next_pv++);
-                progressed = true;
-            }
-            if (progressed) {
-                t0 = clock64();
-            } else if (clock64() - t0 > kWaitLimitCycles) {
-                set_error(a.err, DEV_ERR_TIMEOUT);
-                break;
-            } else {
-                __nanosleep(20);  // leave the issue slots to the softmax warp sharing this SMSP
-            }
+        bool ok = true;
+        for (int i = 0; i < kBufs && i < n_items && ok; ++i)
+            if ((ok = wait_s(i))) issue_s(i);
+        for (int i = 0; i < n_items && ok; ++i) {
+            ok = mbar_wait(&b->pfull[i % kBufs], (i / kBufs) & 1) &&
+                 mbar_wait(&b->vfull[i % kVSlots], (i / kVSlots) & 1);
+            if (!ok) break;
+            issue_pv(i);
+            if (i + kBufs < n_items && (ok = wait_s(i + kBufs))) issue_s(i + kBufs);
         }
+        if (!ok) set_error(a.err, DEV_ERR_TIMEOUT);
     } else if (warp == kLoadWarp && lane == 0) {
         // ---- Q, K and V producer ------------------------------------------------------------
         const long long row_base = (long long)sid * capacity;
@@ -460,19 +474,19 @@ __global__ void __launch_bounds__(kThreadsF, 2) prefill_fa_kernel(PrefillArgs a,
         };
         // K(j) then V(j - 1): K runs an item ahead of V, its slots freed by S alone.
         auto load_k = [&](int i) -> bool {
-            const int hh = i / n_kt, kt = i - hh * n_kt, slot = i % kSlots;
-            if (i >= kSlots && !mbar_wait(&b->kempty[slot], ((i / kSlots) & 1) ^ 1)) return false;
+            const int hh = i / n_kt, kt = i - hh * n_kt, slot = i % kKSlots;
+            if (i >= kKSlots && !mbar_wait(&b->kempty[slot], ((i / kKSlots) & 1) ^ 1)) return false;
             mbar_arrive_expect_tx(&b->kfull[slot], kKVBytes);
-            fa_tma(base + kOffKV + slot * 2 * kKVBytes, &tm_k, (h0 + hh) * kHeadDim,
+            fa_tma(base + kOffK + slot * kKVBytes, &tm_k, (h0 + hh) * kHeadDim,
                    (int)(row_base + (long long)kt * KT), &b->kfull[slot]);
             s_k_issued = i + 1;
             return true;
         };
         auto load_v = [&](int i) -> bool {
-            const int hh = i / n_kt, kt = i - hh * n_kt, slot = i % kSlots;
-            if (i >= kSlots && !mbar_wait(&b->vempty[slot], ((i / kSlots) & 1) ^ 1)) return false;
+            const int hh = i / n_kt, kt = i - hh * n_kt, slot = i % kVSlots;
+            if (i >= kVSlots && !mbar_wait(&b->vempty[slot], ((i / kVSlots) & 1) ^ 1)) return false;
             mbar_arrive_expect_tx(&b->vfull[slot], kKVBytes);
-            fa_tma(base + kOffKV + slot * 2 * kKVBytes + kKVBytes, &tm_v, (h0 + hh) * kHeadDim,
+            fa_tma(base + kOffV + slot * kKVBytes, &tm_v, (h0 + hh) * kHeadDim,
                    (int)(row_base + (long long)kt * KT), &b->vfull[slot]);
             s_v_issued = i + 1;
             return true;
@@ -498,10 +512,10 @@ __global__ void __launch_bounds__(kThreadsF, 2) prefill_fa_kernel(PrefillArgs a,
     if (tid == 0) {
         // The last copies issued into each slot (consumed or not; a completed phase returns at
         // once): let them land before exit.
-        for (int i = s_k_issued > kSlots ? s_k_issued - kSlots : 0; i < s_k_issued; ++i)
-            mbar_wait(&b->kfull[i % kSlots], (i / kSlots) & 1);
-        for (int i = s_v_issued > kSlots ? s_v_issued - kSlots : 0; i < s_v_issued; ++i)
-            mbar_wait(&b->vfull[i % kSlots], (i / kSlots) & 1);
+        for (int i = s_k_issued > kKSlots ? s_k_issued - kKSlots : 0; i < s_k_issued; ++i)
+            mbar_wait(&b->kfull[i % kKSlots], (i / kKSlots) & 1);
+        for (int i = s_v_issued > kVSlots ? s_v_issued - kVSlots : 0; i < s_v_issued; ++i)
+            mbar_wait(&b->vfull[i % kVSlots], (i / kVSlots) & 1);
         // The Q copies: the last request of each buffer (a completed phase returns at once).
         for (int hh = s_q_issued > 2 ? s_q_issued - 2 : 0; hh < s_q_issued; ++hh)
             mbar_wait(&b->qready[hh & 1], (hh >> 1) & 1);
