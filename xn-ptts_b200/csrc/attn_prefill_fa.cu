@@ -15,26 +15,28 @@
 //               memory when a head starts or it must be raised), write P as bf16 hi/lo into TMEM
 //               (tcgen05.st) over the columns of S it came from; O accumulates in TMEM, rescaled
 //               there only when a row's maximum grows by more than 2^8 (the one case in which
-//               the softmax waits for the previous P.V); at each head's end O / l goes to the
-//               output row.
+//               the softmax waits for the previous P.V); O / l of each head goes to the output
+//               rows at the next item.
 //   warp 8      lane 0 issues the MMAs (kind::f16, M = 128, N = 64, bf16):
 //               S = Q_hi K^T + Q_lo K^T     A = Q (smem, K-major), B = K (smem, K-major)
 //               O += P_hi V + P_lo V        A = P (TMEM), B = V (smem, MN-major)
-//               Three S/P buffers in TMEM: S(i + 3) reuses buffer i % 3 once P.V(i) has read
-//               P(i) from it, so S runs up to two items ahead of the softmax, across heads, and
-//               the softmax of items i + 1 and i + 2 overlaps P.V(i).
+//               Two S/P buffers in TMEM: S(i + 2) reuses buffer i % 2 once P.V(i) has read P(i)
+//               from it, so S runs an item ahead of the softmax, across heads, and the softmax
+//               of item i + 1 overlaps P.V(i). Two O buffers (head parity), so the softmax
+//               writes out a head's O during the next head's first item instead of waiting at
+//               the head's end for its last P.V.
 //   warp 9      lane 0 copies with TMA each head's Q tiles (the bf16 hi/lo planes the q producer
 //               wrote) and each item's K and V tiles (64 keys x one head, 128-byte swizzle) into
 //               a two-slot K ring and a three-slot V ring: a K slot frees once its S product is
 //               done, a V slot once its P.V is.
-// TMEM (256 columns): S/P buffers 0-63, 64-127 and 128-191, O 192-255. In a buffer, S is f32
-// (column = key); P replaces it as bf16 pairs, each half of the keys within its own 32 columns:
-// hi of keys 32h + 0..31 in columns 32h + 0..15, lo in 32h + 16..31 (one row per lane), so a
-// thread overwrites only the S values it has read itself. Keys past the tile's last position are
-// masked in the softmax and their V rows zeroed before P.V (the slots may hold anything, and
-// 0 x NaN is NaN). Every wait is bounded
-// and sets DEV_ERR_TIMEOUT; a CTA that timed out waits, bounded, for its copies. Splitting q and
-// P into hi + lo keeps the products f32-grade, as in the linears.
+// TMEM (256 columns): S/P buffers 0-63 and 64-127, O buffers 128-191 and 192-255. In a buffer,
+// S is f32 (column = key); P replaces it as bf16 pairs, each half of the keys within its own 32
+// columns: hi of keys 32h + 0..31 in columns 32h + 0..15, lo in 32h + 16..31 (one row per lane),
+// so a thread overwrites only the S values it has read itself. Keys past the tile's last position
+// are masked in the softmax and their V rows zeroed before P.V (the slots may hold anything, and
+// 0 x NaN is NaN). Every wait is bounded and sets DEV_ERR_TIMEOUT; a CTA that timed out waits,
+// bounded, for its copies. Splitting q and P into hi + lo keeps the products f32-grade, as in the
+// linears.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -57,12 +59,12 @@ constexpr int kOffK = 2 * 2 * kQBytes;                 // K slot s at s * kKVByt
 constexpr int kOffV = kOffK + kKSlots * kKVBytes;      // V slot s at s * kKVBytes
 constexpr int kOffBar = kOffV + kVSlots * kKVBytes;
 constexpr int kSmemF = 1024 + kOffBar + 256;
-constexpr int kStaticSmemF = 4 * 1024;  // s_xmax, s_xsum and the issue counters (3,088 bytes)
+constexpr int kStaticSmemF = 5 * 1024;  // s_xmax, s_xsum and the issue counters (4,112 bytes)
 static_assert(2 * (kSmemF + kStaticSmemF + 1024) <= 228 * 1024, "two CTAs per SM");
 constexpr uint32_t kTmemColsF = 256;
-constexpr int kBufs = 3;  // S/P buffers in TMEM, 64 columns each
-constexpr uint32_t kColO = 64 * kBufs;
-static_assert(kColO + 64 <= kTmemColsF, "S/P buffers and O fit the allocation");
+constexpr int kBufs = 2;  // S/P buffers in TMEM, 64 columns each
+constexpr uint32_t kColO = 64 * kBufs;  // O of head hh at kColO + 64 (hh % 2)
+static_assert(kColO + 2 * 64 <= kTmemColsF, "S/P buffers and two O buffers fit the allocation");
 
 // kind::f16, D f32, A/B bf16, M = 128, N = 64; kIdescPVf additionally marks B MN-major.
 constexpr uint32_t kIdescSf = (1u << 4) | (1u << 7) | (1u << 10) | (8u << 17) | (8u << 24);
@@ -129,6 +131,11 @@ __device__ __forceinline__ void fa_st8(uint32_t taddr, const uint32_t* r) {
                  "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
                  : "memory");
 }
+__device__ __forceinline__ float fa_max3(float x, float y, float z) {  // sm_100 three-input max
+    float r;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(x), "f"(y), "f"(z));
+    return r;
+}
 __device__ __forceinline__ float fa_exp2(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -194,7 +201,7 @@ __global__ void __launch_bounds__(kThreadsF, 2) prefill_fa_kernel(PrefillArgs a,
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(b + 1);
     __shared__ int s_k_issued, s_v_issued, s_q_issued;
     __shared__ float s_xmax[2][2][QT];  // [item parity][half][row]: the halves' row maxima
-    __shared__ float s_xsum[2][QT];     // [half][row]: the halves' row sums at a head's end
+    __shared__ float s_xsum[2][2][QT];  // [head parity][half][row]: the halves' row sums
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int h0 = blockIdx.y * kHeadsPerCta;
 
@@ -256,8 +263,9 @@ __global__ void __launch_bounds__(kThreadsF, 2) prefill_fa_kernel(PrefillArgs a,
         // and the final O / l is the same softmax. Both halves of a row keep the same m.
         constexpr float kRaise = 8.f;
         float m = -1e30f, l = 0.f;
-        for (int i = 0; i < n_items; ++i) {
-            const int hh = i / n_kt, kt = i - hh * n_kt;
+        int pend_h = -1, pend_i = 0;  // a head whose O is still to be written, and its last item
+        float pend_l = 0.f;
+        for (int i = 0, hh = 0, kt = 0; i < n_items; ++i) {  // item i: head h0 + hh, key tile kt
             if (kt == 0) {
                 m = -1e30f;
                 l = 0.f;
@@ -278,10 +286,14 @@ __global__ void __launch_bounds__(kThreadsF, 2) prefill_fa_kernel(PrefillArgs a,
 #pragma unroll
                     for (int j = 0; j < 32; ++j) s[j] = key0 + j <= pos ? s[j] : -INFINITY;
                 }
-                float m4[4] = {s[0], s[1], s[2], s[3]};  // four independent chains
+                float m4[4];  // four independent chains of three-input maxima over 8 keys each
 #pragma unroll
-                for (int j = 4; j < 32; ++j) m4[j & 3] = fmaxf(m4[j & 3], s[j]);
-                mt = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
+                for (int q = 0; q < 4; ++q) {
+                    const float* sq = s + 8 * q;
+                    m4[q] = fa_max3(fa_max3(fa_max3(sq[0], sq[1], sq[2]), sq[3], sq[4]), sq[5], sq[6]);
+                    m4[q] = fmaxf(m4[q], sq[7]);
+                }
+                mt = fmaxf(fa_max3(m4[0], m4[1], m4[2]), m4[3]);
             }
             // One barrier.red over the row quarter's two warps: unless a head starts, a wait
             // timed out, or some row's maximum passed m + kRaise, m stays and nothing is
@@ -310,12 +322,13 @@ __global__ void __launch_bounds__(kThreadsF, 2) prefill_fa_kernel(PrefillArgs a,
                     const float f = raise ? fa_exp2(m - mnew) : 1.f;
                     l *= f;
                     float ot[32];
-                    fa_ld32(tmem + lane_base + kColO + 32 * half, ot);
+                    const uint32_t ocol = kColO + 64 * (hh & 1) + 32 * half;
+                    fa_ld32(tmem + lane_base + ocol, ot);
                     fa_wait_ld();
                     uint32_t w[32];
 #pragma unroll
                     for (int j = 0; j < 32; ++j) w[j] = __float_as_uint(ot[j] * f);
-                    fa_st32(tmem + lane_base + kColO + 32 * half, w);
+                    fa_st32(tmem + lane_base + ocol, w);
                 }
                 m = mnew;
             }
@@ -357,49 +370,75 @@ __global__ void __launch_bounds__(kThreadsF, 2) prefill_fa_kernel(PrefillArgs a,
             fa_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&b->pfull[buf]);
-            if (kt < n_kt - 1) continue;
-            // The head's last tile: the row sum over both halves, then O / l into this half of
-            // the output row (16-byte stores).
-            ok = __all_sync(0xffffffffu, mbar_wait(&b->ofull[buf], ph_i));
-            s_xsum[half][r] = l;  // read by the partner before either reaches the next head's end
-            if (pair_any(quarter, !ok)) {
-                set_error(a.err, DEV_ERR_TIMEOUT);
-                break;
-            }
-            const float inv = 1.f / (l + s_xsum[half ^ 1][r]);
-            fa_after();
-            float o[32];
-            fa_ld32(tmem + lane_base + kColO + 32 * half, o);
-            fa_wait_ld();
-            if (!active) continue;
-            const long long at = (long long)(row0 + r) * kRowWidth + (h0 + hh) * kHeadDim + 32 * half;
-            if (a.out_mode == kOutF32) {
-                float4* out = reinterpret_cast<float4*>(static_cast<float*>(a.out) + at);
+            // Heads to write out now: the one pending from the previous item (its last P.V has
+            // had the time of a softmax pass), then this one if it ends the CTA's work; a head
+            // that ends earlier waits for the next item. O of head hh lives in O buffer hh % 2,
+            // which the first P.V of head hh + 2 overwrites: that needs this warp's P of it, so
+            // comes after the write-out.
+            bool stop = false;
+            for (int pass = 0; pass < 2; ++pass) {
+                int fh, fi;
+                float fl;
+                if (pass == 0) {
+                    if (pend_h < 0) continue;
+                    fh = pend_h, fi = pend_i, fl = pend_l;
+                    pend_h = -1;
+                } else {
+                    if (kt != n_kt - 1) break;
+                    if (i < n_items - 1) {
+                        pend_h = hh, pend_i = i, pend_l = l;
+                        break;
+                    }
+                    fh = hh, fi = i, fl = l;
+                }
+                // The row sum over both halves, then O / l into this half of the output row
+                // (16-byte stores). P.V(fi) done: S(i) in TMEM means P.V(i - kBufs) is done, so
+                // the barrier is within one phase of it.
+                ok = __all_sync(0xffffffffu, mbar_wait(&b->ofull[fi % kBufs], (fi / kBufs) & 1));
+                s_xsum[fh & 1][half][r] = fl;  // slot fh % 2: heads fh and fh + 1 may share an item
+                if (pair_any(quarter, !ok)) {
+                    set_error(a.err, DEV_ERR_TIMEOUT);
+                    stop = true;
+                    break;
+                }
+                const float inv = 1.f / (fl + s_xsum[fh & 1][half ^ 1][r]);
+                fa_after();
+                float o[32];
+                fa_ld32(tmem + lane_base + kColO + 64 * (fh & 1) + 32 * half, o);
+                fa_wait_ld();
+                if (!active) continue;
+                const long long at = (long long)(row0 + r) * kRowWidth + (h0 + fh) * kHeadDim + 32 * half;
+                if (a.out_mode == kOutF32) {
+                    float4* out = reinterpret_cast<float4*>(static_cast<float*>(a.out) + at);
 #pragma unroll
-                for (int j = 0; j < 8; ++j)
-                    out[j] = make_float4(o[4 * j] * inv, o[4 * j + 1] * inv, o[4 * j + 2] * inv, o[4 * j + 3] * inv);
-            } else if (a.out_mode == kOutBf16) {
-                uint4* out = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.out) + at);
+                    for (int j = 0; j < 8; ++j)
+                        out[j] = make_float4(o[4 * j] * inv, o[4 * j + 1] * inv, o[4 * j + 2] * inv,
+                                             o[4 * j + 3] * inv);
+                } else if (a.out_mode == kOutBf16) {
+                    uint4* out = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.out) + at);
 #pragma unroll
-                for (int j = 0; j < 4; ++j)
-                    out[j] = make_uint4(pack_bf16x2(o[8 * j] * inv, o[8 * j + 1] * inv),
-                                        pack_bf16x2(o[8 * j + 2] * inv, o[8 * j + 3] * inv),
-                                        pack_bf16x2(o[8 * j + 4] * inv, o[8 * j + 5] * inv),
-                                        pack_bf16x2(o[8 * j + 6] * inv, o[8 * j + 7] * inv));
-            } else {
-                uint4* oh = reinterpret_cast<uint4*>(static_cast<__half*>(a.out) + at);
-                uint4* ol = reinterpret_cast<uint4*>(static_cast<__half*>(a.out_lo) + at);
+                    for (int j = 0; j < 4; ++j)
+                        out[j] = make_uint4(pack_bf16x2(o[8 * j] * inv, o[8 * j + 1] * inv),
+                                            pack_bf16x2(o[8 * j + 2] * inv, o[8 * j + 3] * inv),
+                                            pack_bf16x2(o[8 * j + 4] * inv, o[8 * j + 5] * inv),
+                                            pack_bf16x2(o[8 * j + 6] * inv, o[8 * j + 7] * inv));
+                } else {
+                    uint4* oh = reinterpret_cast<uint4*>(static_cast<__half*>(a.out) + at);
+                    uint4* ol = reinterpret_cast<uint4*>(static_cast<__half*>(a.out_lo) + at);
 #pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    uint4 h, lo4;
-                    split_f16x2(o[8 * j] * inv, o[8 * j + 1] * inv, h.x, lo4.x);
-                    split_f16x2(o[8 * j + 2] * inv, o[8 * j + 3] * inv, h.y, lo4.y);
-                    split_f16x2(o[8 * j + 4] * inv, o[8 * j + 5] * inv, h.z, lo4.z);
-                    split_f16x2(o[8 * j + 6] * inv, o[8 * j + 7] * inv, h.w, lo4.w);
-                    oh[j] = h;
-                    ol[j] = lo4;
+                    for (int j = 0; j < 4; ++j) {
+                        uint4 h, lo4;
+                        split_f16x2(o[8 * j] * inv, o[8 * j + 1] * inv, h.x, lo4.x);
+                        split_f16x2(o[8 * j + 2] * inv, o[8 * j + 3] * inv, h.y, lo4.y);
+                        split_f16x2(o[8 * j + 4] * inv, o[8 * j + 5] * inv, h.z, lo4.z);
+                        split_f16x2(o[8 * j + 6] * inv, o[8 * j + 7] * inv, h.w, lo4.w);
+                        oh[j] = h;
+                        ol[j] = lo4;
+                    }
                 }
             }
+            if (stop) break;
+            if (++kt == n_kt) kt = 0, ++hh;
         }
     } else if (warp == kMmaWarp && lane == 0) {
         // ---- MMA issuer ----------------------------------------------------------------------
@@ -434,13 +473,14 @@ __global__ void __launch_bounds__(kThreadsF, 2) prefill_fa_kernel(PrefillArgs a,
             fa_after();
             const uint64_t dv = desc_mn(base + kOffV + (i % kVSlots) * kKVBytes);
             const uint32_t pb = tmem + (uint32_t)((i % kBufs) * 64);
+            const uint32_t od = tmem + kColO + 64 * (uint32_t)((i / n_kt) & 1);  // the head's O
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk) {  // 64 keys = 4 x 16: P 8 columns, V 2 x 1024 bytes
                 // Keys 16 kk.. of P: half kk / 2 of the buffer, its hi columns 8 (kk % 2) on, lo 16 on.
                 const uint32_t ph = pb + 32 * (kk >> 1) + 8 * (kk & 1);
                 // O accumulates over the head's key tiles; its first tile starts it afresh.
-                fa_mma_ts(tmem + kColO, ph, dv + 128 * kk, kIdescPVf, (i % n_kt != 0 || kk) ? 1u : 0u);
-                fa_mma_ts(tmem + kColO, ph + 16, dv + 128 * kk, kIdescPVf, 1u);
+                fa_mma_ts(od, ph, dv + 128 * kk, kIdescPVf, (i % n_kt != 0 || kk) ? 1u : 0u);
+                fa_mma_ts(od, ph + 16, dv + 128 * kk, kIdescPVf, 1u);
             }
             fa_commit(&b->ofull[i % kBufs]);
             fa_commit(&b->vempty[i % kVSlots]);  // P.V(i) has read the V slot
