@@ -330,3 +330,57 @@ def test_linear_i8_matches_the_oracle(ptts, oracle, cuda):
         y = ptts.linear_i8(x.to(cuda), torch.from_numpy(w).to(cuda), torch.from_numpy(s).to(cuda))
         want = oracle.linear_i8(_f32(x), w, s)
         assert normwise(_f32(y), want) < 1e-5, (m, n, k)
+
+
+@pytest.mark.parametrize("kernel", ["fa", "tc1", "core"])
+def test_chunked_prompts_equal_the_one_shot_prompt(ptts, cuda, monkeypatch, kernel):
+    """Causal attention makes a prompt split into chunks the same computation as the prompt in
+    one call (the cache holds the earlier chunks' keys, each row sees keys 0..=its position): a
+    row's output depends on its own q and the cached keys only, whatever tile of whichever call
+    it falls in, and on the tensor cores each row's dot products and its softmax are its own.
+    So outputs and caches must agree bit for bit. Chunk edges off the 64-key and 128-row tile
+    grid; three streams of different lengths, one of them with rows already cached."""
+    import torch
+    if kernel != "fa":
+        monkeypatch.setenv("PTTS_B200_PREFILL", kernel)
+    rows = [300, 517, 137]
+    S, cap = 3, 700
+    g = torch.Generator().manual_seed(31)
+    pre = torch.randn(40, 8, 64, generator=g).bfloat16()
+    q, k, v = ([torch.randn(n, 8, 64, generator=g).bfloat16() for n in rows] for _ in range(3))
+
+    def fresh():
+        kv = ptts.KvState(1, S, cap, dtype="bf16")
+        kv.load_prefix(0, 2, pre.to(cuda), pre.to(cuda))  # stream 2 starts at position 40
+        return kv
+
+    one = fresh()
+    want = ptts.attend(one, 0, torch.cat(q).to(cuda), torch.cat(k).to(cuda), torch.cat(v).to(cuda),
+                       [0, 1, 2], rows, out_dtype="f32")
+    one.advance([0, 1, 2], rows)
+    # Chunks: (rows of stream 0, 1, 2) per call; every call has a sequence of more than one row.
+    cuts = [(129, 1, 70), (0, 300, 2), (171, 216, 65)]
+    assert [sum(c[i] for c in cuts) for i in range(3)] == rows
+    many = fresh()
+    got = [[], [], []]
+    done = [0, 0, 0]
+    for c in cuts:
+        streams = [i for i in range(3) if c[i]]
+        n = [c[i] for i in streams]
+        sl = [slice(done[i], done[i] + c[i]) for i in streams]
+        out = ptts.attend(many, 0, torch.cat([q[i][s] for i, s in zip(streams, sl)]).to(cuda),
+                          torch.cat([k[i][s] for i, s in zip(streams, sl)]).to(cuda),
+                          torch.cat([v[i][s] for i, s in zip(streams, sl)]).to(cuda), streams, n,
+                          out_dtype="f32")
+        many.advance(streams, n)
+        o = 0
+        for i, m in zip(streams, n):
+            got[i].append(out[o:o + m])
+            o += m
+            done[i] += m
+    one.check()
+    many.check()
+    got = torch.cat([torch.cat(got[i]) for i in range(3)])
+    assert torch.equal(got, want), (got - want).abs().max().item()
+    for t1, t2 in zip(one.tensors(0), many.tensors(0)):
+        assert torch.equal(t1, t2)

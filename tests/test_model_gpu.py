@@ -487,3 +487,40 @@ def test_kernel_stamps_of_a_two_lane_step(ptts, cuda):
         model.read_stamps()
     model.step(kvs[0], list(range(S)), xs)  # the unstamped graph again
     kvs[0].check()
+
+
+def test_chunked_prompts_through_the_stack_equal_the_one_shot_prompt(ptts, cuda):
+    """The layer stack on a prompt split into chunks equals the prompt in one call, bit for bit:
+    below 1024 rows per call every linear runs the same kernel with the same split of k, each
+    output row of a linear is its own dot products, LayerNorm is per row, and attention is per
+    row over the cache (the attention-op test gives the argument)."""
+    import torch
+    cfg = ptts.FlowLMConfig(num_layers=3)
+    w = ptts.random_weights(cfg, 41)
+    model = ptts.Transformer(cfg)
+    model.load(w)
+    rows = [260, 190, 75]
+    S, cap = 3, 300
+    g = torch.Generator().manual_seed(42)
+    xs = [torch.randn(n, 512, generator=g).bfloat16() for n in rows]
+    one = ptts.KvState(cfg.num_layers, S, cap, dtype="bf16")
+    want = model.forward(one, torch.cat(xs).to(cuda), [0, 1, 2], rows)
+    cuts = [(100, 64, 2), (160, 126, 73)]
+    many = ptts.KvState(cfg.num_layers, S, cap, dtype="bf16")
+    got = [[], [], []]
+    done = [0, 0, 0]
+    for c in cuts:
+        x = torch.cat([xs[i][done[i]:done[i] + c[i]] for i in range(3)]).to(cuda)
+        y = model.forward(many, x, [0, 1, 2], list(c))
+        o = 0
+        for i in range(3):
+            got[i].append(y[o:o + c[i]])
+            o += c[i]
+            done[i] += c[i]
+    one.check()
+    many.check()
+    got = torch.cat([torch.cat(got[i]) for i in range(3)])
+    assert torch.equal(got, want), (got - want).abs().max().item()
+    for l in range(cfg.num_layers):
+        for t1, t2 in zip(one.tensors(l)[:2], many.tensors(l)[:2]):
+            assert torch.equal(t1, t2), l
