@@ -284,7 +284,7 @@ __global__ void __launch_bounds__(kThreads) linear_kernel(LinearArgs p) {
     }
     cp_async_wait<0>();
 
-    if (EPI == EPI_QKV) {
+    if constexpr (EPI == EPI_QKV) {
         // Row metadata and RoPE entries of all this thread's outputs first, then the stores.
         int sid[MI][2], pos[MI][2];
         float2 rt[MI][2][NI];
@@ -313,16 +313,16 @@ __global__ void __launch_bounds__(kThreads) linear_kernel(LinearArgs p) {
                 if (m + 8 < p.M)
                     qkv_pair(p, m + 8, n, acc[mi][ni][2], acc[mi][ni][3], sid[mi][1], pos[mi][1], rt[mi][1][ni]);
             }
-        return;
-    }
+    } else {
 #pragma unroll
-    for (int mi = 0; mi < MI; ++mi) {
+        for (int mi = 0; mi < MI; ++mi) {
 #pragma unroll
-        for (int ni = 0; ni < NI; ++ni) {
-            const int m = m0 + row0 + mi * 16 + g;
-            const int n = n0 + col0 + ni * 8 + 2 * t;
-            if (m < p.M) epilogue_pair<EPI>(p, m, n, z, acc[mi][ni][0], acc[mi][ni][1]);
-            if (m + 8 < p.M) epilogue_pair<EPI>(p, m + 8, n, z, acc[mi][ni][2], acc[mi][ni][3]);
+            for (int ni = 0; ni < NI; ++ni) {
+                const int m = m0 + row0 + mi * 16 + g;
+                const int n = n0 + col0 + ni * 8 + 2 * t;
+                if (m < p.M) epilogue_pair<EPI>(p, m, n, z, acc[mi][ni][0], acc[mi][ni][1]);
+                if (m + 8 < p.M) epilogue_pair<EPI>(p, m + 8, n, z, acc[mi][ni][2], acc[mi][ni][3]);
+            }
         }
     }
 }
