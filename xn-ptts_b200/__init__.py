@@ -201,9 +201,16 @@ def _ip(a: np.ndarray):
 
 
 def _stream(stream=None) -> ctypes.c_void_p:
+    """The CUDA stream handle for a call: `stream`'s, else torch's current stream on the current
+    device (read through torch's raw-stream query, a few microseconds cheaper per call than
+    building a torch.cuda.Stream object)."""
     import torch
-    s = stream if stream is not None else torch.cuda.current_stream()
-    return ctypes.c_void_p(s.cuda_stream)
+    if stream is not None:
+        return ctypes.c_void_p(stream.cuda_stream)
+    raw = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+    if raw is not None:
+        return ctypes.c_void_p(raw(torch._C._cuda_getDevice()))
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
 
 
 def _dptr(t) -> ctypes.c_void_p:

@@ -109,6 +109,19 @@ std::vector<int2> make_tiles(const std::vector<int32_t>& offsets, const int32_t*
     return t;
 }
 
+// Appends the tile list to a per-call int32 list that goes to the device in one copy, at an
+// even index (8-byte aligned on the device, the list's buffer being 256-byte aligned); returns
+// that index.
+size_t append_tiles(std::vector<int32_t>& packed, const std::vector<int2>& tiles) {
+    if (packed.size() % 2) packed.push_back(0);
+    const size_t at = packed.size();
+    for (const int2& t : tiles) {
+        packed.push_back(t.x);
+        packed.push_back(t.y);
+    }
+    return at;
+}
+
 bool prefill_on_tensor_cores() {
     const char* e = getenv("PTTS_B200_PREFILL");
     return !(e && e[0] == 'c');  // PTTS_B200_PREFILL=core keeps the CUDA-core kernel
@@ -165,7 +178,7 @@ struct ptts_b200_kv {
     DevBuf window;
     std::vector<int32_t> h_window;
     // scratch of the attention op
-    DevBuf seq_stream, row_offsets, row_stream, row_pos, prefix, part, q_rot, counters, tiles;
+    DevBuf seq_stream, row_offsets, row_stream, row_pos, prefix, part, q_rot, counters;
     Staging staging;
     // What seq_stream holds after the last upload_seq, and on which CUDA stream it was copied: a
     // decode loop that attends and advances the same streams step after step copies the list
@@ -292,7 +305,7 @@ struct ptts_b200_model {
     DevBuf rope;        // RoPE (cos, sin) table [rope_rows][kMaxPairs]
     int rope_rows = 0;
     // forward() workspace
-    DevBuf seq_stream, row_stream, row_pos, prefix, tiles;
+    DevBuf seq_stream, row_stream, row_pos, prefix;
     Workspace ws;
     Staging staging;
     std::unique_ptr<StepGraph> step;
@@ -1252,6 +1265,9 @@ int ptts_b200_attend(ptts_b200_kv* kv, int layer, const void* q, const void* k, 
         cudaStream_t s = as_stream(cuda_stream);
         std::vector<int32_t> packed(streams_host, streams_host + n_seq);
         packed.insert(packed.end(), offsets.begin(), offsets.end());
+        // A prompt's tile list travels in the same copy (8-byte aligned after the lists).
+        const std::vector<int2> tl = decode ? std::vector<int2>{} : make_tiles(offsets, streams_host, kv->h_len);
+        const size_t tile_at = append_tiles(packed, tl);
         const int32_t* d = kv->upload_seq(packed, s);
         const RowPlan plan = make_plan(kv, decode, d, d + n_seq, n_seq, n_rows, kv->row_stream,
                                        kv->row_pos, kv->prefix, s);
@@ -1290,10 +1306,8 @@ int ptts_b200_attend(ptts_b200_kv* kv, int layer, const void* q, const void* k, 
         }
         Tiles tiles;
         if (!decode) {
-            const std::vector<int2> t = make_tiles(offsets, streams_host, kv->h_len);
-            tiles.dev = static_cast<int2*>(kv->tiles.need(sizeof(int2) * t.size()));
-            tiles.n = (int)t.size();
-            kv->staging.upload(const_cast<int2*>(tiles.dev), t.data(), sizeof(int2) * t.size(), s);
+            tiles.dev = reinterpret_cast<const int2*>(d + tile_at);
+            tiles.n = (int)tl.size();
             tiles.windowed = windowed;
         }
         attention(kv, layer, decode, plan, n_rows, ra.q_out, out, nullptr,
@@ -1514,6 +1528,9 @@ int ptts_b200_forward(ptts_b200_model* model, ptts_b200_kv* kv, const void* x,
         ensure_rope(model, (int)rope_need, s);
         std::vector<int32_t> packed(streams_host, streams_host + n_seq);
         packed.insert(packed.end(), offsets.begin(), offsets.end());
+        // A prompt's tile list travels in the same copy.
+        const std::vector<int2> tl = decode ? std::vector<int2>{} : make_tiles(offsets, streams_host, kv->h_len);
+        const size_t tile_at = append_tiles(packed, tl);
         int32_t* d = static_cast<int32_t*>(model->seq_stream.need(sizeof(int32_t) * packed.size()));
         model->staging.upload(d, packed.data(), sizeof(int32_t) * packed.size(), s);
         const RowPlan plan = make_plan(kv, decode, d, d + n_seq, n_seq, rows, model->row_stream,
@@ -1522,11 +1539,9 @@ int ptts_b200_forward(ptts_b200_model* model, ptts_b200_kv* kv, const void* x,
         model->ws.size(c, rows);
         Tiles tiles;
         if (!decode) {
-            const std::vector<int2> t = make_tiles(offsets, streams_host, kv->h_len);
-            tiles.dev = static_cast<int2*>(model->tiles.need(sizeof(int2) * t.size()));
-            tiles.n = (int)t.size();
+            tiles.dev = reinterpret_cast<const int2*>(d + tile_at);
+            tiles.n = (int)tl.size();
             tiles.windowed = windowed;
-            model->staging.upload(const_cast<int2*>(tiles.dev), t.data(), sizeof(int2) * t.size(), s);
         }
         // The residual stream lives in the caller's output y.
         run_layers(model, kv, decode, plan, rows, static_cast<const __nv_bfloat16*>(x), y, model->ws, s,
@@ -1795,10 +1810,18 @@ int ptts_b200_kv_set_lengths(ptts_b200_kv* kv, const int32_t* streams_host,
         }
         DeviceScope scope(kv->device);
         cudaStream_t s = as_stream(cuda_stream);
-        std::vector<int32_t> packed(streams_host, streams_host + n);
-        packed.insert(packed.end(), lengths_host, lengths_host + n);
-        const int32_t* d = kv->upload_scratch(packed.data(), sizeof(int32_t) * packed.size(), s);
-        launch_set_lengths(kv->len.as<int32_t>(), d, d + n, n, s);
+        if (n <= kSetLengthsInline) {  // a short list rides in the launch, no copy
+            SetLengthsInline l;
+            l.n = n;
+            std::memcpy(l.stream, streams_host, sizeof(int32_t) * n);
+            std::memcpy(l.value, lengths_host, sizeof(int32_t) * n);
+            launch_set_lengths_inline(kv->len.as<int32_t>(), l, s);
+        } else {
+            std::vector<int32_t> packed(streams_host, streams_host + n);
+            packed.insert(packed.end(), lengths_host, lengths_host + n);
+            const int32_t* d = kv->upload_scratch(packed.data(), sizeof(int32_t) * packed.size(), s);
+            launch_set_lengths(kv->len.as<int32_t>(), d, d + n, n, s);
+        }
         check_launch();
         for (int i = 0; i < n; ++i) kv->h_len[streams_host[i]] = lengths_host[i];
     });

@@ -141,6 +141,14 @@ struct RingEvictArgs {
 void launch_ring_evict(const RingEvictArgs& a, cudaStream_t s);
 
 // lengths[streams[i]] = values[i].
+// Up to kSetLengthsInline (stream, value) pairs carried in the launch's parameters.
+constexpr int kSetLengthsInline = 128;
+struct SetLengthsInline {
+    int n;
+    int32_t stream[kSetLengthsInline];
+    int32_t value[kSetLengthsInline];
+};
+void launch_set_lengths_inline(int32_t* lengths, const SetLengthsInline& l, cudaStream_t s);
 void launch_set_lengths(int32_t* lengths, const int32_t* streams, const int32_t* values, int n,
                         cudaStream_t s);
 

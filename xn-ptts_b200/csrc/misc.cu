@@ -236,6 +236,14 @@ __global__ void set_lengths_kernel(int32_t* lengths, const int32_t* __restrict__
     if (i < n) lengths[streams[i]] = values[i];
 }
 
+// The same for a short list passed in the kernel's parameters (no host-to-device copy).
+__global__ void set_lengths_inline_kernel(int32_t* lengths, SetLengthsInline l) {
+    grid_dep_wait();
+    grid_dep_launch();
+    const int i = threadIdx.x;
+    if (i < l.n) lengths[l.stream[i]] = l.value[i];
+}
+
 __global__ void reset_streams_kernel(uint4* k, uint4* v, int32_t* lengths,
                                      const int32_t* __restrict__ streams, int n, int layers,
                                      long long layer_vec, long long stream_vec) {
@@ -302,6 +310,10 @@ void launch_ring_evict(const RingEvictArgs& a, cudaStream_t s) {
 void launch_set_lengths(int32_t* lengths, const int32_t* streams, const int32_t* values, int n,
                         cudaStream_t s) {
     launch_k(set_lengths_kernel, dim3((n + 255) / 256), dim3(256), 0, s, lengths, streams, values, n);
+}
+
+void launch_set_lengths_inline(int32_t* lengths, const SetLengthsInline& l, cudaStream_t s) {
+    launch_k(set_lengths_inline_kernel, dim3(1), dim3(kSetLengthsInline), 0, s, lengths, l);
 }
 
 void launch_reset_streams(void* k, void* v, int32_t* lengths, const int32_t* streams, int n,
