@@ -1,5 +1,5 @@
 // Causal prefill attention on tcgen05, one CTA per (tile of up to 128 query rows of one sequence,
-// group of kHeadsPerCta heads), sm_100a.
+// group of 1, 2 or 4 heads: 8 / gridDim.y), sm_100a.
 //
 // Reference: the t > 1 branch of StreamingMultiheadAttention::forward (transformer.rs:231-248),
 // softmax(q k^T * 1/sqrt(d) + mask) v with materialize_causal_mask (transformer.rs:94-108): the
@@ -45,7 +45,7 @@ namespace {
 
 constexpr int QT = 128;            // query rows per CTA
 constexpr int KT = 64;             // keys per item
-constexpr int kHeadsPerCta = 4;
+constexpr int kHeadsPerCtaMax = 4;  // heads per CTA for large grids; fewer when tiles are few
 constexpr int kSoftWarps = 8;    // two per TMEM lane quarter (two threads per row)
 constexpr int kMmaWarp = kSoftWarps, kLoadWarp = kSoftWarps + 1;
 constexpr int kThreadsF = (kSoftWarps + 2) * 32;
@@ -203,7 +203,8 @@ __global__ void __launch_bounds__(kThreadsF, 2) prefill_fa_kernel(PrefillArgs a,
     __shared__ float s_xmax[2][2][QT];  // [item parity][half][row]: the halves' row maxima
     __shared__ float s_xsum[2][2][QT];  // [head parity][half][row]: the halves' row sums
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int h0 = blockIdx.y * kHeadsPerCta;
+    const int heads_per_cta = (kRowWidth / kHeadDim) / (int)gridDim.y;
+    const int h0 = blockIdx.y * heads_per_cta;
 
     if (tid == 0) {
         for (int i = 0; i < kKSlots; ++i) {
@@ -248,7 +249,7 @@ __global__ void __launch_bounds__(kThreadsF, 2) prefill_fa_kernel(PrefillArgs a,
     const int pos_max = a.row_pos[row0 + nrows - 1];  // the tile's last row sees the most keys
     const bool bad = sid < 0 || pos_max < 0 || pos_max >= capacity || a.q_hi == nullptr;
     const int n_kt = bad ? 0 : (pos_max + KT) / KT;
-    const int n_items = kHeadsPerCta * n_kt;  // item i: head h0 + i / n_kt, key tile i % n_kt
+    const int n_items = heads_per_cta * n_kt;  // item i: head h0 + i / n_kt, key tile i % n_kt
 
     if (warp < kSoftWarps) {
         if (bad && tid == 0) set_error(a.err, DEV_ERR_BOUNDS);
@@ -537,7 +538,7 @@ __global__ void __launch_bounds__(kThreadsF, 2) prefill_fa_kernel(PrefillArgs a,
         for (int i = 0; i <= n_items && ok; ++i) {
             if (i < n_items) {
                 const int hh = i / n_kt, kt = i - hh * n_kt;
-                if (kt == 0 && hh + 1 < kHeadsPerCta && q_loaded == hh + 1) {
+                if (kt == 0 && hh + 1 < heads_per_cta && q_loaded == hh + 1) {
                     ok = load_q(hh + 1);
                     q_loaded = hh + 2;
                 }
@@ -585,7 +586,14 @@ bool launch_prefill_attn_fa(const PrefillArgs& a, const int2* tiles, int n_tiles
         mql = mk;
     }
     set_max_dynamic_smem(reinterpret_cast<const void*>(prefill_fa_kernel), kSmemF);
-    launch_k(prefill_fa_kernel, dim3(n_tiles, (kRowWidth / kHeadDim) / kHeadsPerCta), dim3(kThreadsF), kSmemF, s, a,
+    // Four heads per CTA give each CTA a long pipeline; with few tiles (short prompts), fewer
+    // heads per CTA keep the SMs busy: two CTAs per SM want at least 2 x SMs CTAs.
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    int hpc = kHeadsPerCtaMax;
+    while (hpc > 1 && (long long)n_tiles * ((kRowWidth / kHeadDim) / hpc) < 2LL * sms) hpc /= 2;
+    launch_k(prefill_fa_kernel, dim3(n_tiles, (kRowWidth / kHeadDim) / hpc), dim3(kThreadsF), kSmemF, s, a,
              tiles, mk, mv, mqh, mql, capacity);
     return true;
 }
