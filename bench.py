@@ -751,7 +751,7 @@ def run_config2(args):
         "value": ms, "unit": "ms", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": ms, "higher_is_better": False, "dtype": "bf16", "data": "synthetic",
         "config": {"workload": "config2", "rows": 256,
-                   "note": "per call: plan, RoPE + append, tcgen05 prefill attention (2 query tiles x 2 groups of 4 heads); host-bound: about 60 us with any of the three prefill kernels"},
+                   "note": "per call: plan, RoPE + append, tcgen05 prefill attention (2 query tiles x 8 heads, one head per CTA for so few tiles); the host side (Python wrapper, the list copy, three launches) takes about as long as the kernels"},
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                      "frac": achieved / peak, "peak_kind": kind,
                      "algorithmic_flops_per_call": flops}}), flush=True)
