@@ -758,6 +758,145 @@ def run_config2(args):
     kv.check()
 
 
+def run_ring(args):
+    """Ring caches in the config-5 frame (StreamingTransformer::start_ring / set_ring_slot /
+    evict, transformer.rs:840-929): the shard's 512 streams on the 40m stack, prompts
+    U{32..512} prefilled, then every stream a ring of 200 frame slots past its prompt. 200
+    frames fill the slots, the oldest 50 of every ring are evicted (the kept keys past the
+    prompt rotated back), and the timed frames write into the freed slots: per frame one
+    ptts_b200_kv_set_ring_slots call for all 512 rings and one graph-replayed step. Every
+    frame's attention reads each ring's slots up to its highest filled one (prompt + 200), the
+    50 evicted ones masked; roofline bytes count all slots read."""
+    import numpy as np
+    import torch
+
+    ring, evict = 200, 50
+    if args.warmup + args.steps + 5 > evict:
+        raise SystemExit(f"--warmup + --steps + 5 traced frames must fit the {evict} freed slots")
+    ptts, wl = load()
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda:0")
+    cfg, B, prefixes, seed, desc = workload_spec(args, ptts, wl, 0)
+    model = ptts.Transformer(cfg, 0)
+    model.load(ptts.random_weights(cfg, seed))
+    cap = int(prefixes.max()) + ring
+    streams = np.arange(B, dtype=np.int32)
+    kv = ptts.KvState(cfg.num_layers, B, cap, dtype="bf16")
+    g = torch.Generator(device=dev).manual_seed(seed * 1000)
+    model.forward(kv, torch.randn(int(prefixes.sum()), cfg.d_model, generator=g, device=dev).bfloat16(),
+                  streams, prefixes)
+    kv.start_ring(streams)
+    xs = [torch.randn(B, cfg.d_model, generator=g, device=dev).bfloat16() for _ in range(8)]
+    y = torch.empty(B, cfg.d_model, dtype=torch.float32, device=dev)
+    for f in range(ring):
+        kv.set_ring_slots(streams, prefixes + f)
+        model.step(kv, streams, xs[f % 8], out=y)
+    t0 = time.perf_counter()
+    for st in streams:
+        p = int(prefixes[st])
+        kv.evict(int(st), p, list(range(p, p + evict)))
+    torch.cuda.synchronize()
+    evict_ms = (time.perf_counter() - t0) * 1e3
+    state = {"f": 0}
+
+    def frame():
+        kv.set_ring_slots(streams, prefixes + state["f"])  # the freed slots, oldest first
+        model.step(kv, streams, xs[state["f"] % 8], out=y)
+        state["f"] += 1
+
+    for _ in range(args.warmup):
+        frame()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        frame()
+    e1.record()
+    e1.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    ptts.set_tracing(True)
+    ptts.trace(reset=True)
+    for _ in range(5):
+        frame()
+    torch.cuda.synchronize()
+    tr = ptts.trace(reset=True)
+    ptts.set_tracing(False)
+    kv.check()
+    peak, peak_kind = peaks()
+    per_launch_bytes = tr["attn_bytes"] / max(tr["attn_launches"], 1)
+    per_launch_ms = tr["attn_ms"] / max(tr["attn_launches"], 1)
+    achieved = per_launch_bytes / (per_launch_ms / 1e3) / 1e9
+    print(json.dumps({
+        "metric": "flow-LM frames/s with ring caches (a hole of 50 evicted frames in each ring)",
+        "value": B / (ms / 1e3), "unit": "frames/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "dtype": "bf16",
+        "data": "synthetic (seeded random-init int8 weights and N(0,1) hidden rows)",
+        "config": {"workload": "ring: config5 shard (40m, 512 streams, prefixes U{32..512}), rings of "
+                               f"{ring} frame slots, {evict} evicted, timed frames in the freed slots",
+                   "lanes": ptts.step_lanes(B)},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "peak_kind": peak_kind,
+                     "kernel": "decode_attn_kernel<bf16> (split-KV, ring masks)",
+                     "algorithmic_bytes_per_launch": per_launch_bytes, "launch_ms": per_launch_ms,
+                     "launches_timed": tr["attn_launches"]},
+        "evict_ms_all_streams": evict_ms}), flush=True)
+
+
+def run_mimi(args):
+    """Mimi's transformer, the phonon codec's (2 layers, d 512, 8 heads, ff 2048, context 250:
+    MimiStreamingMultiheadAttention inside StreamingTransformerLayer, transformer.rs:395-468 and
+    :591-634), decoding one frame per stream for 512 windowed streams per GPU whose positions
+    lie past the window, through ptts_b200_forward (windowed streams run the host-position path,
+    not the graph-replayed step). Random f32 layers with layer scales 0.01, synthetic rows. A
+    step is one frame for all streams; value = stream-frames/s. The attention reads the last
+    250 K and V rows of every stream in both layers (bf16, 1 KB per row each)."""
+    import numpy as np
+    import torch
+
+    ptts, wl = load()
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda:0")
+    cfg, ctx = ptts.MIMI_TRANSFORMER, ptts.MIMI_CONTEXT
+    B, cap, prompt = 512, 512, 260  # a call adds at most cap - ctx + 1 = 263 rows to a stream
+    model = ptts.Transformer(cfg)
+    model.load_mimi(ptts.random_mimi_tensors(cfg, 7))
+    kv = ptts.KvState(cfg.num_layers, B, cap, dtype="bf16")
+    streams = list(range(B))
+    kv.set_window(streams, ctx)
+    g = torch.Generator(device=dev).manual_seed(7)
+    for s0 in range(0, B, 64):  # the prompts, 64 streams per call
+        x = torch.randn(64 * prompt, cfg.d_model, generator=g, device=dev).bfloat16()
+        model.forward(kv, x, streams[s0:s0 + 64], [prompt] * 64)
+    frames = [torch.randn(B, cfg.d_model, generator=g, device=dev).bfloat16() for _ in range(4)]
+    ones = [1] * B
+
+    def step(i):
+        model.forward(kv, frames[i % 4], streams, ones)
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(args.steps):
+        step(args.warmup + i)
+    e1.record()
+    e1.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    kv.check()
+    kv_bytes = B * cfg.num_layers * ctx * 2 * 1024
+    print(json.dumps({
+        "metric": "Mimi transformer decode (windowed streams past the 250-position window)",
+        "value": B / (ms / 1e3), "unit": "frames/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "dtype": "bf16",
+        "data": "synthetic (random f32 layers, layer scale 0.01, N(0,1) rows)",
+        "config": {"workload": "mimi: 2 layers, d 512, 8 heads, ff 2048, context 250, 512 streams, "
+                               f"positions {prompt + args.warmup}..{prompt + args.warmup + args.steps}",
+                   "path": "ptts_b200_forward, one row per stream (host positions, no graph)"},
+        "kv_bytes_per_step": kv_bytes,
+        "kv_gbs_over_the_whole_step": kv_bytes / (ms / 1e3) / 1e9}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -774,9 +913,12 @@ def main():
                     help="write the kernel timeline (device stamps) of one decode step to this file")
     ap.add_argument("--no-flow", action="store_true",
                     help="skip the extra line item: whole frames with the flow head (ptts_b200_frame)")
-    ap.add_argument("--workload", choices=["config5", "config4", "config3", "config2"], default="config5",
+    ap.add_argument("--workload", choices=["config5", "config4", "config3", "config2", "mimi", "ring"],
+                    default="config5",
                     help="config5: the flow-LM frame, 512 streams/GPU (default); config4: 31m, "
-                         "64 streams, prefix 128; config3: the attention op alone")
+                         "64 streams, prefix 128; config3: the attention op alone; config2: one "
+                         "256-row prompt; mimi: Mimi's transformer decoding 512 windowed streams; "
+                         "ring: the config-5 frame with ring caches after an eviction")
     ap.add_argument("--layers", type=int, default=0,
                     help="profiling aid: override the layer count (recorded in config.workload)")
     args = ap.parse_args()
@@ -788,6 +930,10 @@ def main():
         run_config3(args)
     elif args.workload == "config2":
         run_config2(args)
+    elif args.workload == "mimi":
+        run_mimi(args)
+    elif args.workload == "ring":
+        run_ring(args)
     else:
         run_ours(args)
 

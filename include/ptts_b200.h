@@ -178,6 +178,13 @@ int ptts_b200_kv_set_window(ptts_b200_kv* kv, const int32_t* streams_host, int n
 int ptts_b200_kv_start_ring(ptts_b200_kv* kv, const int32_t* streams_host, int n, void* cuda_stream);
 /* The slot of a ring stream's next row, 0 <= slot < capacity. */
 int ptts_b200_kv_set_ring_slot(ptts_b200_kv* kv, int stream, int slot, void* cuda_stream);
+/* set_ring_slot for n ring streams at once: slot slots_host[i] for stream streams_host[i] (no
+ * stream twice), in one copy and one launch where n calls of ptts_b200_kv_set_ring_slot take n
+ * copies (a batch of sessions sets every ring's slot each frame). The reference sets one
+ * state's slot per call (StreamingTransformer::set_ring_slot, transformer.rs:855-872); every
+ * entry is checked as there before anything changes. */
+int ptts_b200_kv_set_ring_slots(ptts_b200_kv* kv, const int32_t* streams_host, const int32_t* slots_host,
+                                int n, void* cuda_stream);
 /* Drop the rows in slots[0..n) of a ring stream (each at or past `prefix` and holding a row,
  * no repeats, n at most the length); keys past `prefix` are rotated back by n positions with
  * the RoPE of max_period (RotaryEmbedding::shift_back, rope.rs:26-35), in every layer. */

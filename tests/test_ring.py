@@ -201,3 +201,53 @@ def test_misuse_of_a_ring_is_refused(ptts, cuda):
         kv.set_ring_slot(0, 0)
     model.forward(kv, row(3), [0], [3])  # an appended stream again
     assert kv.lengths()[0] == 3
+
+
+@pytest.mark.parametrize("S", [12, 150], ids=["in-launch", "copied"])
+def test_set_ring_slots_is_set_ring_slot_for_each_stream(ptts, cuda, S):
+    """ptts_b200_kv_set_ring_slots sets every listed ring's write slot in one call: frames
+    stepped after it equal, bit for bit, the same frames stepped after one set_ring_slot per
+    stream, on a second cache (both list forms: carried in the launch, and copied). A list
+    naming a stream twice, or a stream that is not a ring, is refused and changes nothing: the
+    frame after the refusals still matches."""
+    import torch
+    cfg = ptts.FlowLMConfig(num_layers=2)
+    w = ptts.random_weights(cfg, 25)
+    model = ptts.Transformer(cfg)
+    model.load(w)
+    P, cap = 6, 20
+    streams = list(range(S))
+    g = torch.Generator().manual_seed(26)
+    prompt = torch.randn(S * P, 512, generator=g).bfloat16().to(cuda)
+    kvs = [ptts.KvState(cfg.num_layers, S, cap, dtype="bf16") for _ in range(2)]
+    rings = streams[: S - 2]  # two appended streams stay in the batch
+    for kv in kvs:
+        model.forward(kv, prompt, streams, [P] * S)
+        kv.start_ring(rings)
+        for r in rings[::3]:
+            kv.evict(r, 2, [3, 4])
+
+    def frame(f):
+        # Free slots past the prompt, a different one per frame for each ring.
+        slots = [(f + 3 * r) % (cap - P) + P for r in rings]
+        for r, sl in zip(rings, slots):
+            kvs[0].set_ring_slot(r, sl)
+        kvs[1].set_ring_slots(rings, slots)
+        x = torch.randn(S, 512, generator=g).bfloat16().to(cuda)
+        a, b = model.step(kvs[0], streams, x), model.step(kvs[1], streams, x)
+        torch.cuda.synchronize()
+        assert torch.equal(a, b), f
+
+    for f in range(4):
+        frame(f)
+    with pytest.raises(ptts.PttsError, match="twice"):
+        kvs[1].set_ring_slots([rings[0], rings[0]], [P, P + 1])
+    with pytest.raises(ptts.PttsError, match="not a ring"):
+        kvs[1].set_ring_slots([rings[0], S - 1], [P, P])
+    frame(4)
+    for kv in kvs:
+        kv.check()
+    np.testing.assert_array_equal(kvs[0].lengths(), kvs[1].lengths())
+    for l in range(cfg.num_layers):
+        for t1, t2 in zip(kvs[0].tensors(l)[:2], kvs[1].tensors(l)[:2]):
+            assert torch.equal(t1, t2)

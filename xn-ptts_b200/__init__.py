@@ -46,7 +46,7 @@ EXPORTS = (
     "ptts_b200_forward", "ptts_b200_step", "ptts_b200_attend_decode_noalloc",
     "ptts_b200_flow_create", "ptts_b200_flow_destroy", "ptts_b200_flow_set_tensor",
     "ptts_b200_flow_finish", "ptts_b200_flow_sample", "ptts_b200_frame",
-    "ptts_b200_kv_start_ring", "ptts_b200_kv_set_ring_slot", "ptts_b200_kv_evict",
+    "ptts_b200_kv_start_ring", "ptts_b200_kv_set_ring_slot", "ptts_b200_kv_set_ring_slots", "ptts_b200_kv_evict",
     "ptts_b200_model_config", "ptts_b200_model_load_layer_f32", "ptts_b200_model_load_layer_q8_0",
     "ptts_b200_load_gguf", "ptts_b200_gguf_remap_key", "ptts_b200_kv_set_window",
     "ptts_b200_model_stamps", "ptts_b200_model_stamps_read", "ptts_b200_model_set_layer_scale",
@@ -168,6 +168,7 @@ def lib() -> ctypes.CDLL:
         L.ptts_b200_kv_set_window.argtypes = [P, IP, I, I, P]
         L.ptts_b200_kv_start_ring.argtypes = [P, IP, I, P]
         L.ptts_b200_kv_set_ring_slot.argtypes = [P, I, I, P]
+        L.ptts_b200_kv_set_ring_slots.argtypes = [P, IP, IP, I, P]
         L.ptts_b200_kv_evict.argtypes = [P, I, I, IP, I, F, P]
         L.ptts_b200_flow_create.argtypes = [I, ctypes.POINTER(FlowConfigC), ctypes.POINTER(P)]
         L.ptts_b200_flow_destroy.argtypes = [P]
@@ -297,6 +298,13 @@ class KvState:
 
     def set_ring_slot(self, stream_index: int, slot: int, stream=None):
         _check(lib().ptts_b200_kv_set_ring_slot(self._h, stream_index, slot, _stream(stream)))
+
+    def set_ring_slots(self, streams: Sequence[int], slots: Sequence[int], stream=None):
+        """set_ring_slot for many ring streams in one call (ptts_b200_kv_set_ring_slots)."""
+        st, sl = _i32(streams), _i32(slots)
+        if len(st) != len(sl):
+            raise PttsError(ERR_ARG, "one slot per stream")
+        _check(lib().ptts_b200_kv_set_ring_slots(self._h, _ip(st), _ip(sl), len(st), _stream(stream)))
 
     def evict(self, stream_index: int, prefix: int, slots: Sequence[int], max_period: float = 10000.0,
               stream=None):

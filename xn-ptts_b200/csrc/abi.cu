@@ -1742,6 +1742,41 @@ int ptts_b200_kv_set_ring_slot(ptts_b200_kv* kv, int stream, int slot, void* cud
     });
 }
 
+int ptts_b200_kv_set_ring_slots(ptts_b200_kv* kv, const int32_t* streams_host, const int32_t* slots_host,
+                                int n, void* cuda_stream) {
+    return guarded([&] {
+        check_kv(kv);
+        require(n > 0 && streams_host && slots_host, PTTS_B200_ERR_ARG, "no streams");
+        std::vector<char> seen(kv->streams, 0);
+        for (int i = 0; i < n; ++i) {
+            const int st = streams_host[i], slot = slots_host[i];
+            require(st >= 0 && st < kv->streams, PTTS_B200_ERR_ARG, "stream out of range");
+            require(!seen[st], PTTS_B200_ERR_ARG, "stream " + std::to_string(st) + " appears twice");
+            seen[st] = 1;
+            require(kv->is_ring(st), PTTS_B200_ERR_STATE, "not a ring cache, see ptts_b200_kv_start_ring");
+            require(slot >= 0 && slot < kv->capacity, PTTS_B200_ERR_ARG,
+                    "slot " + std::to_string(slot) + " of a " + std::to_string(kv->capacity) + "-slot ring");
+        }
+        DeviceScope scope(kv->device);
+        cudaStream_t s = as_stream(cuda_stream);
+        // The same int32 scatter as set_lengths, into the write slots.
+        if (n <= kSetLengthsInline) {
+            SetLengthsInline l;
+            l.n = n;
+            std::memcpy(l.stream, streams_host, sizeof(int32_t) * n);
+            std::memcpy(l.value, slots_host, sizeof(int32_t) * n);
+            launch_set_lengths_inline(kv->ring_write.as<int32_t>(), l, s);
+        } else {
+            std::vector<int32_t> packed(streams_host, streams_host + n);
+            packed.insert(packed.end(), slots_host, slots_host + n);
+            const int32_t* d = kv->upload_scratch(packed.data(), sizeof(int32_t) * packed.size(), s);
+            launch_set_lengths(kv->ring_write.as<int32_t>(), d, d + n, n, s);
+        }
+        check_launch();
+        for (int i = 0; i < n; ++i) kv->h_ring_write[streams_host[i]] = slots_host[i];
+    });
+}
+
 int ptts_b200_kv_evict(ptts_b200_kv* kv, int stream, int prefix, const int32_t* slots_host, int n,
                        float max_period, void* cuda_stream) {
     return guarded([&] {
