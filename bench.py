@@ -303,6 +303,29 @@ def workload_spec(args, ptts, wl, rank):
     return cfg, B, prefixes, seed, desc
 
 
+def q8_0_layers(weights, cfg) -> list:
+    """The same int8 weights as GGUF q8_0 linears (blocks of 34 bytes per 32 weights: an f16
+    scale d, then the 32 int8 q; W = q * d, the published ggml layout): every block of a row takes
+    that row's scale, rounded to f16. Norms as they are."""
+    import numpy as np
+    out = []
+    for l in range(cfg.num_layers):
+        w = weights.layer(l)
+        layer = {}
+        for name in ("in_proj", "out_proj", "linear1", "linear2"):
+            q = np.ascontiguousarray(w[name])
+            n, k = q.shape
+            d = np.repeat(w[name + "_scale"].astype(np.float16)[:, None], k // 32, axis=1)
+            blocks = np.zeros((n, k // 32, 34), np.uint8)
+            blocks[:, :, :2] = np.ascontiguousarray(d).view(np.uint8).reshape(n, k // 32, 2)
+            blocks[:, :, 2:] = q.view(np.uint8).reshape(n, k // 32, 32)
+            layer[name] = blocks.reshape(n, -1)
+        for name in ("norm1_weight", "norm1_bias", "norm2_weight", "norm2_bias"):
+            layer[name] = w[name]
+        out.append(layer)
+    return out
+
+
 def run_ours(args):
     import numpy as np
     import torch
@@ -325,7 +348,11 @@ def run_ours(args):
     L = cfg.num_layers
     weights = ptts.random_weights(cfg, seed)
     model = ptts.Transformer(cfg, local)
-    model.load(weights)
+    if args.weights == "q8_0":
+        for l, layer in enumerate(q8_0_layers(weights, cfg)):
+            model.load_layer_q8_0(l, layer)
+    else:
+        model.load(weights)
     cap = int(prefixes.max()) + FRAMES
     streams = np.arange(B, dtype=np.int32)
     stream = torch.cuda.current_stream()
@@ -590,6 +617,8 @@ def run_ours(args):
                        "streams_per_gpu": B, "total_streams": world * B, "layers": L,
                        "kv_capacity": cap, "parallelism": f"stream-sharded x{world}, no collectives",
                        "lanes": lanes,
+                       "weights": "int8, one f32 scale per output row" if args.weights == "int8" else
+                                  "GGUF q8_0 blocks (an f16 scale per 32 weights), the same int8 values",
                        "timed_frames": "whole window, cycled from frame 0" if cycling else [t0, t0 + args.steps],
                        "repeats": len(jobs),
                        "l2": f"inputs larger than L2: {kv_bytes_per_step / 1e9:.2f} GB of KV read per step per GPU"
@@ -919,6 +948,9 @@ def main():
                          "64 streams, prefix 128; config3: the attention op alone; config2: one "
                          "256-row prompt; mimi: Mimi's transformer decoding 512 windowed streams; "
                          "ring: the config-5 frame with ring caches after an eviction")
+    ap.add_argument("--weights", choices=["int8", "q8_0"], default="int8",
+                    help="int8 with per-row scales (default), or the same values as GGUF q8_0 blocks "
+                         "(the published checkpoints' format: f16-plane linears)")
     ap.add_argument("--layers", type=int, default=0,
                     help="profiling aid: override the layer count (recorded in config.workload)")
     args = ap.parse_args()

@@ -62,8 +62,10 @@ template <int RT, int WM>
 struct TmaTile {
     // 3 stages: a decode tile (RT 32, 74 KB) fits beside the decode attention's compact ring
     // (137 KB) on one SM, and two prompt tiles (RT 64, 97 KB) share an SM, so that one's epilogue
-    // overlaps the other's loads and MMAs.
-    static constexpr int kStages = (WM == kW16Lo || RT <= 64) ? 3 : 4;
+    // overlaps the other's loads and MMAs. A decode tile with a weight lo plane (40 KB a stage)
+    // takes 2 stages (81 KB) for the same reason: with 3 (121 KB) a two-lane step's linears
+    // waited for the other lane's attention to leave the SMs.
+    static constexpr int kStages = (WM == kW16Lo && RT <= 32) ? 2 : ((WM == kW16Lo || RT <= 64) ? 3 : 4);
     static constexpr int kWBytes = FT * KS * 2;  // 16 KB per 16-bit weight plane
     static constexpr int kXBytes = RT * KS * 2;  // per activation plane
     static constexpr int kStageBytes = (WM == kW16Lo ? 2 : 1) * kWBytes + 2 * kXBytes;
