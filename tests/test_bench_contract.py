@@ -45,3 +45,28 @@ def test_fewer_than_three_warmup_steps_are_refused():
     r = _bench("--impl", "reference", "--steps", "1", "--warmup", "2")
     assert r.returncode != 0
     assert "warmup" in r.stderr
+
+
+def test_q8_0_layers_are_the_published_block_layout(ptts):
+    """bench.py --weights q8_0 packs the int8 weights as GGUF q8_0 blocks: per 32 weights an
+    f16 scale, then the 32 int8 (W = q * d), each row's scale in every block of the row. Checked
+    against the test fixture's own writer of that layout, and by decoding the blocks back."""
+    import numpy as np
+    sys.path.insert(0, ROOT)
+    import bench
+    from gguf_fixture import q8_0_blocks
+    cfg = ptts.FlowLMConfig(num_layers=2)
+    w = ptts.random_weights(cfg, 5)
+    layers = bench.q8_0_layers(w, cfg)
+    assert len(layers) == 2
+    for l, layer in enumerate(layers):
+        for name in ("in_proj", "out_proj", "linear1", "linear2"):
+            q, s = w.layer(l)[name], w.layer(l)[name + "_scale"]
+            n, k = q.shape
+            d = np.repeat(s.astype(np.float16)[:, None], k // 32, axis=1)
+            np.testing.assert_array_equal(layer[name], q8_0_blocks(q, d))
+            blocks = layer[name].reshape(n, k // 32, 34)
+            back = blocks[:, :, 2:].view(np.int8).astype(np.float32) * blocks[:, :, :2].copy().view(np.float16).astype(np.float32)
+            np.testing.assert_array_equal(back.reshape(n, k), q.astype(np.float32) * s.astype(np.float16).astype(np.float32)[:, None])
+        for name in ("norm1_weight", "norm1_bias", "norm2_weight", "norm2_bias"):
+            np.testing.assert_array_equal(layer[name], w.layer(l)[name])
