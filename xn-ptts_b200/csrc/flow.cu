@@ -150,6 +150,74 @@ __global__ void __launch_bounds__(128) flow_ln_mod_kernel(FlowModArgs p) {
     }
 }
 
+// The flow net's last two steps in one pass, one warp per row (FinalLayer, mlp.rs:125-157, and
+// the solver update): LayerNorm (no affine) + modulate as flow_ln_mod_kernel does, then the L
+// (<= 32) outputs h . w[j] + bias[j] and out = cur + step_scale * dir. Each lane sums its 16
+// columns for every output; a reduce-scatter over the warp (31 shuffles) leaves output j's sum
+// in lane j. The modulated row never goes to memory.
+template <int PER>
+__global__ void __launch_bounds__(128) flow_final_kernel(FlowModArgs m, FlowOutArgs o) {
+    grid_dep_wait();
+    grid_dep_launch();
+    const int row = blockIdx.x * 4 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (row >= m.M) return;
+    constexpr int C = PER * 32, Q = PER / 4;
+    float v[PER];
+#pragma unroll
+    for (int i = 0; i < Q; ++i) {
+        const float4 x = *reinterpret_cast<const float4*>(m.x + (long long)row * C + 4 * (lane + 32 * i));
+        v[4 * i] = x.x; v[4 * i + 1] = x.y; v[4 * i + 2] = x.z; v[4 * i + 3] = x.w;
+    }
+    float mean, inv;
+    row_stats<PER>(v, C, m.eps, mean, inv);
+    const float* sh = m.shift + (long long)row * m.stride;
+    const float* sc = m.scale + (long long)row * m.stride;
+#pragma unroll
+    for (int i = 0; i < Q; ++i) {
+        const int k = 4 * (lane + 32 * i);
+        const float4 sv = *reinterpret_cast<const float4*>(sc + k);
+        const float4 t = *reinterpret_cast<const float4*>(sh + k);
+        v[4 * i] = (v[4 * i] - mean) * inv * (1.f + sv.x) + t.x;
+        v[4 * i + 1] = (v[4 * i + 1] - mean) * inv * (1.f + sv.y) + t.y;
+        v[4 * i + 2] = (v[4 * i + 2] - mean) * inv * (1.f + sv.z) + t.z;
+        v[4 * i + 3] = (v[4 * i + 3] - mean) * inv * (1.f + sv.w) + t.w;
+    }
+    float part[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+        float a = 0.f;
+        if (j < o.L) {
+            const float* wr = o.w + (long long)j * C;
+#pragma unroll
+            for (int i = 0; i < Q; ++i) {
+                const float4 w = __ldg(reinterpret_cast<const float4*>(wr + 4 * (lane + 32 * i)));
+                a = fmaf(v[4 * i], w.x, a);
+                a = fmaf(v[4 * i + 1], w.y, a);
+                a = fmaf(v[4 * i + 2], w.z, a);
+                a = fmaf(v[4 * i + 3], w.w, a);
+            }
+        }
+        part[j] = a;
+    }
+    // Reduce-scatter: after the stage of offset `off` a lane holds `off` sums, those of the
+    // outputs whose bits above `off` match its own lane bits; at the end part[0] is output lane.
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) {
+        const bool upper = (lane & off) != 0;
+#pragma unroll
+        for (int j = 0; j < off; ++j) {
+            const float send = upper ? part[j] : part[j + off];
+            const float keep = upper ? part[j + off] : part[j];
+            part[j] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+        }
+    }
+    if (lane < o.L) {
+        const float dir = part[0] + o.bias[lane];
+        const long long at = (long long)row * o.L + lane;
+        o.out[at] = o.cur ? o.cur[at] + o.step_scale * dir : dir;
+    }
+}
+
 // Eight rows per block (one per warp); the weights sit transposed in shared memory, [C][L + 1]
 // (the extra column keeps both the transposing stores and the reads free of bank conflicts),
 // so lane j reads output j's column. L <= 64 (lanes j and j + 32).
@@ -216,6 +284,12 @@ void launch_flow_ln_mod(const FlowModArgs& a, cudaStream_t s) {
         case 1024: launch_k(flow_ln_mod_kernel<32>, grid, dim3(128), 0, s, a); break;
         default: break;  // refused at flow creation
     }
+}
+
+bool launch_flow_final(const FlowModArgs& m, const FlowOutArgs& o, cudaStream_t s) {
+    if (m.C != 512 || o.C != 512 || o.L > 32 || m.gamma || m.y || m.hi) return false;
+    launch_k(flow_final_kernel<16>, dim3((m.M + 3) / 4), dim3(128), 0, s, m, o);
+    return true;
 }
 
 void launch_flow_out(const FlowOutArgs& a, cudaStream_t s) {

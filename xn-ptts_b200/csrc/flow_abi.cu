@@ -279,9 +279,6 @@ void sample(ptts_b200_flow* f, const float* src, bool normalise, int n, const fl
         m.shift = ada + (size_t)c.flow_depth * 3 * C;
         m.scale = ada + (size_t)c.flow_depth * 3 * C + C;
         m.stride = W;
-        m.y = hf;
-        launch_flow_ln_mod(m, s);
-        CK(cudaGetLastError());
         FlowOutArgs o{};
         o.M = n;
         o.C = C;
@@ -293,7 +290,12 @@ void sample(ptts_b200_flow* f, const float* src, bool normalise, int n, const fl
         o.step_scale = c.flow_type == PTTS_B200_FLOW_LSD ? 1.0f / (float)steps : 1.0f;
         float* next = i + 1 == steps ? latent : (i % 2 == 0 ? cur_a : cur_b);
         o.out = next;
-        launch_flow_out(o, s);
+        if (!launch_flow_final(m, o, s)) {  // other shapes: the modulated rows through memory
+            m.y = hf;
+            launch_flow_ln_mod(m, s);
+            CK(cudaGetLastError());
+            launch_flow_out(o, s);
+        }
         CK(cudaGetLastError());
         cur = next;
     }

@@ -383,6 +383,10 @@ struct FlowOutArgs {
     float* out;
 };
 void launch_flow_out(const FlowOutArgs& a, cudaStream_t s);
+// The final layer's LayerNorm + modulate (`m`, no affine, no output: y, hi and lo unset) and the
+// flow_out step (`o`, its h unused) in one kernel, for C = 512 and L <= 32; false (nothing
+// launched) for other shapes.
+bool launch_flow_final(const FlowModArgs& m, const FlowOutArgs& o, cudaStream_t s);
 
 // RoPE table: out[pos][i] = (cos, sin)(f32(pos) * inv_freq[i]) for pos < rows, i < kMaxPairs.
 struct RopeFreqs {
