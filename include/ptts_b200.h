@@ -256,7 +256,9 @@ int ptts_b200_model_load_layer_f32(ptts_b200_model* model, int layer,
 
 /* A layer from GGUF q8_0 linears (the reference's model.q8.gguf, examples/quantize.rs:46-47):
  * each weight [out][in] as rows of in/32 blocks of 34 bytes, an f16 scale d then 32 int8 q,
- * W = q * d (kernels.js:252, :302). Dequantized exactly into the planes above. */
+ * W = q * d (kernels.js:252, :302). Dequantized exactly into the planes above; the layer also
+ * keeps q and d / s (s the row's power of two) as f16, from which decode-size calls widen the
+ * same weights on chip (the planes when a d / s is not an exact f16). */
 typedef struct {
     const void* in_proj_q8_0;
     const void* out_proj_q8_0;

@@ -160,3 +160,41 @@ def test_gguf_refusals(ptts, cuda, tmp_path):
     flow = ptts.Flow(ptts.PHONON_FLOW)
     with pytest.raises(ptts.PttsError, match="flow tensor missing"):
         model.load_gguf(str(full), flow)
+
+
+@pytest.mark.gpu
+def test_q8_0_widened_on_chip_equals_the_planes(ptts, cuda, tmp_path, monkeypatch):
+    """Below 4096 rows a q8_0 layer's linears read the int8 values and block scales and widen
+    them on chip into the f16 hi/lo weights its planes hold (lo mostly f16 subnormals); with
+    the same MMA order that is bit for bit the planes path (PTTS_B200_Q8=planes), prompts and
+    decode steps alike. Layer 1 has blocks whose scale over the row's power of two is not an
+    exact f16 (2^10 below the rest): that layer keeps to its planes."""
+    import torch
+    cfg = ptts.FlowLMConfig(num_layers=2, scale_group=32)
+    layers = _q8_layers(cfg, 51)
+    # Blocks of mixed magnitude in a row: the row's power of two then sits well above some.
+    for lay, f in zip(layers, (1.0 / 8, 1.0 / 1024)):
+        q, s = lay["linear1"]
+        s[:, ::7] *= f
+        lay["linear1"] = (q, s.astype(np.float16).astype(np.float32))
+    path = tmp_path / "model.q8.gguf"
+    _write_checkpoint(ptts, path, cfg, layers, {})
+    rows, S = [30, 7, 1, 12], 4
+    x = torch.randn(sum(rows), 512, generator=torch.Generator().manual_seed(52)).bfloat16()
+    xs = [torch.randn(S, 512, generator=torch.Generator().manual_seed(53 + i)).bfloat16() for i in range(3)]
+
+    def run():
+        model = ptts.Transformer(cfg)
+        model.load_gguf(str(path))
+        kv = ptts.KvState(cfg.num_layers, S, max(rows) + 8, dtype="bf16")
+        out = [model.forward(kv, x.to(cuda), list(range(S)), rows).cpu()]
+        out += [model.step(kv, list(range(S)), v.to(cuda)).cpu() for v in xs]
+        kv.check()
+        return out
+
+    monkeypatch.delenv("PTTS_B200_Q8", raising=False)
+    on_chip = run()
+    monkeypatch.setenv("PTTS_B200_Q8", "planes")
+    planes = run()
+    for a, b in zip(on_chip, planes):
+        assert torch.equal(a, b)

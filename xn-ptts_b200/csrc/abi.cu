@@ -295,6 +295,10 @@ struct ptts_b200_model {
         // Layers loaded from f32 or q8_0 weights have no int8 copy: h_* hold f16(W / s_row) and
         // l_* the f16 remainders, s_row a power of two per output row (in s_*).
         DevBuf l_qkv, l_out, l1, l2;
+        // q8_0 layers also keep their int8 values (q8_*) and block scales divided by the row's
+        // power of two (bq_*: [n][k / 32] f16), from which the decode-size linears widen the
+        // same hi/lo weights on chip instead of reading the planes (PTTS_B200_Q8=planes: not).
+        DevBuf q8_qkv, q8_out, q8_1, q8_2, bq_qkv, bq_out, bq1, bq2;
         // out_proj's and linear2's per-row scales as loaded, and the layer scales (LayerScale,
         // layer_scale.rs:14-16; empty: none) folded into them: s_out = base_out * ls1 and
         // s2 = base_2 * ls2, since ls * (x W^T) = x (ls W)^T row by row.
@@ -546,6 +550,13 @@ int split_for(int rows, int k, int want) {
     return sp;
 }
 
+// Whether decode-size linears of q8_0 layers widen the block-scaled int8 values on chip
+// (default) or read the f16 planes (PTTS_B200_Q8=planes).
+bool q8_on_chip() {
+    const char* e = getenv("PTTS_B200_Q8");
+    return !(e && e[0] == 'p');
+}
+
 // StreamingTransformer::forward / forward_step body (transformer.rs:591-634 for every layer):
 //   LN1 (+ previous layer's split-K slices) -> in_proj (RoPE + append) -> attention ->
 //   out_proj (split-K) -> LN2 (+ slices) -> linear1 + GELU -> linear2 (split-K),
@@ -594,8 +605,23 @@ void run_layers(const ptts_b200_model* m, const ptts_b200_kv* kv, bool decode, c
         check_launch();
         pending = 0;
     };
+    // The weight fields of a linear: the q8_0 on-chip form at decode sizes (q8 set per layer),
+    // else the int8 values or the 16-bit planes.
+    bool q8 = false;
+    auto set_weights = [&](LinearArgs& x, const DevBuf& wq, const void* wh, const DevBuf& wl, const DevBuf& q8v,
+                           const DevBuf& bq) {
+        if (q8) {
+            x.w = q8v.as<int8_t>();
+            x.wblk = bq.as<__half>();
+        } else {
+            x.w = wq.as<int8_t>();
+            x.wh = wh;
+            x.wh_lo = wl.p;
+        }
+    };
     auto residual_gemm = [&](const void* a_hi, const void* a_lo, const DevBuf& wq, const void* wh,
-                             const DevBuf& wl, const DevBuf& sc, int k, int splits) {
+                             const DevBuf& wl, const DevBuf& q8v, const DevBuf& bq, const DevBuf& sc, int k,
+                             int splits) {
         LinearArgs o{};
         o.M = rows;
         o.N = c.d_model;
@@ -603,9 +629,7 @@ void run_layers(const ptts_b200_model* m, const ptts_b200_kv* kv, bool decode, c
         o.splits = splits;
         o.a = a_hi;
         o.a_lo = a_lo;
-        o.w = wq.as<int8_t>();
-        o.wh = wh;
-        o.wh_lo = wl.p;
+        set_weights(o, wq, wh, wl, q8v, bq);
         o.scale = sc.as<float>();
         o.y = splits > 1 ? split : resid;
         o.err = err;
@@ -625,6 +649,7 @@ void run_layers(const ptts_b200_model* m, const ptts_b200_kv* kv, bool decode, c
     for (int l = 0; l < c.num_layers; ++l) {
         layer = l;
         const auto& L = *m->layers[l];
+        q8 = rows < kPersistMinRows && L.bq_qkv.p && q8_on_chip();
         // Per-linear 16-bit weights: the layer's own planes, the widened prompt copy, or none.
         const void *wh_qkv = L.h_qkv.p, *wh_out = L.h_out.p, *wh_1 = L.h1.p, *wh_2 = L.h2.p;
         if (widen && L.w_qkv.p && !L.h_qkv.p) {
@@ -652,9 +677,7 @@ void run_layers(const ptts_b200_model* m, const ptts_b200_kv* kv, bool decode, c
         a.K = c.d_model;
         a.a = h_hi;
         a.a_lo = h_lo;
-        a.w = L.w_qkv.as<int8_t>();
-        a.wh = wh_qkv;
-        a.wh_lo = L.l_qkv.p;
+        set_weights(a, L.w_qkv, wh_qkv, L.l_qkv, L.q8_qkv, L.bq_qkv);
         a.scale = L.s_qkv.as<float>();
         a.yq = w.q_rot.as<float>();
         if (prefill_fa(kv->dtype == PTTS_B200_BF16, decode, tiles.windowed) && tiles.n > 0) {
@@ -687,8 +710,8 @@ void run_layers(const ptts_b200_model* m, const ptts_b200_kv* kv, bool decode, c
                   kOutHiLo, w.part, w.counters, tiles, s, lo.lane, stamped.stamps, stamped.stamp);
         if (attn_ev) CK(cudaEventRecord(attn_ev[2 * l + 1], s));
         // out_proj + residual
-        residual_gemm(w.attn_hi.as<__half>(), w.attn_lo.as<__half>(), L.w_out, wh_out, L.l_out, L.s_out,
-                      hd, s_out);
+        residual_gemm(w.attn_hi.as<__half>(), w.attn_lo.as<__half>(), L.w_out, wh_out, L.l_out, L.q8_out,
+                      L.bq_out, L.s_out, hd, s_out);
         // LN2, linear1 + GELU
         ln(L.ln2g.as<float>(), L.ln2b.as<float>(), nullptr, true, "ln2");
         LinearArgs f1{};
@@ -697,9 +720,7 @@ void run_layers(const ptts_b200_model* m, const ptts_b200_kv* kv, bool decode, c
         f1.K = c.d_model;
         f1.a = h_hi;
         f1.a_lo = h_lo;
-        f1.w = L.w1.as<int8_t>();
-        f1.wh = wh_1;
-        f1.wh_lo = L.l1.p;
+        set_weights(f1, L.w1, wh_1, L.l1, L.q8_1, L.bq1);
         f1.scale = L.s1.as<float>();
         f1.yb = w.ff_hi.as<__half>();
         f1.yb_lo = w.ff_lo.as<__half>();
@@ -709,7 +730,7 @@ void run_layers(const ptts_b200_model* m, const ptts_b200_kv* kv, bool decode, c
         require(launch_linear(f1, EPI_GELU, s), PTTS_B200_ERR_UNSUPPORTED, "no kernel for linear1's shape");
         check_launch();
         // linear2 + residual
-        residual_gemm(w.ff_hi.as<__half>(), w.ff_lo.as<__half>(), L.w2, wh_2, L.l2, L.s2,
+        residual_gemm(w.ff_hi.as<__half>(), w.ff_lo.as<__half>(), L.w2, wh_2, L.l2, L.q8_2, L.bq2, L.s2,
                       c.dim_feedforward, s_ff2);
     }
     if (pending) ln(nullptr, nullptr, nullptr, false, "ln_out");
@@ -808,6 +829,35 @@ std::vector<float> dequant_q8_0(const void* blocks, size_t n, size_t k) {
     return w;
 }
 
+// A q8_0 linear's values (int8 [n][k]) and its block scales d over the row's power of two 2^e
+// (upload_dense's row scale for the same weights: e from the row's largest |q d|), [n][k / 32]
+// f16: q * (d 2^-e) is exactly the value the row's f16 hi/lo planes split. False (nothing
+// uploaded) when a scale d 2^-e is not exact in f16 (a block 2^14 and more below its row's
+// largest): the kernel's f16 arithmetic then could not reproduce the planes.
+bool upload_q8_blocks(DevBuf& q8, DevBuf& bq, const void* blocks, const float* w, size_t n, size_t k) {
+    std::vector<int8_t> q(n * k);
+    std::vector<uint16_t> d(n * k / 32);
+    const unsigned char* b = static_cast<const unsigned char*>(blocks);
+    for (size_t r = 0; r < n; ++r) {
+        float amax = 0.f;
+        for (size_t c = 0; c < k; ++c) amax = std::max(amax, std::fabs(w[r * k + c]));
+        int e = 0;
+        if (amax > 0.f) std::frexp(amax, &e);
+        for (size_t blk = 0; blk < k / 32; ++blk) {
+            const unsigned char* p = b + (r * (k / 32) + blk) * 34;
+            uint16_t d16;
+            std::memcpy(&d16, p, 2);
+            const float ds = std::ldexp(f16_value(d16), -e);
+            d[r * (k / 32) + blk] = f16_bits(ds);
+            if (f16_value(d[r * (k / 32) + blk]) != ds) return false;
+            std::memcpy(&q[r * k + blk * 32], p + 2, 32);
+        }
+    }
+    CK(cudaMemcpy(q8.need(q.size()), q.data(), q.size(), cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(bq.need(d.size() * 2), d.data(), d.size() * 2, cudaMemcpyHostToDevice));
+    return true;
+}
+
 // A layer from f32 linears: the f16 planes above, no int8 copy.
 void load_dense_layer(ptts_b200_model* model, int layer, const float* in_proj, const float* out_proj,
                       const float* linear1, const float* linear2, const float* n1w, const float* n1b,
@@ -820,7 +870,9 @@ void load_dense_layer(ptts_b200_model* model, int layer, const float* in_proj, c
     const size_t nqkv = hd + 2 * (size_t)c.num_kv_heads * c.head_dim, ff = c.dim_feedforward;
     DeviceScope scope(model->device);
     auto& L = *model->layers[layer];
-    for (DevBuf* b : {&L.w_qkv, &L.w_out, &L.w1, &L.w2, &L.l_qkv, &L.l_out, &L.l1, &L.l2}) b->release();
+    for (DevBuf* b : {&L.w_qkv, &L.w_out, &L.w1, &L.w2, &L.l_qkv, &L.l_out, &L.l1, &L.l2, &L.q8_qkv, &L.q8_out,
+                      &L.q8_1, &L.q8_2, &L.bq_qkv, &L.bq_out, &L.bq1, &L.bq2})
+        b->release();
     upload_dense(L.h_qkv, L.l_qkv, L.s_qkv, in_proj, nqkv, dm);
     L.base_out = upload_dense(L.h_out, L.l_out, L.s_out, out_proj, dm, hd);
     upload_dense(L.h1, L.l1, L.s1, linear1, ff, dm);
@@ -1499,6 +1551,16 @@ int ptts_b200_model_load_layer_q8_0(ptts_b200_model* model, int layer, const ptt
         const auto l1 = dequant_q8_0(w->linear1_q8_0, ff, dm), l2 = dequant_q8_0(w->linear2_q8_0, dm, ff);
         load_dense_layer(model, layer, qkv.data(), out.data(), l1.data(), l2.data(), w->norm1_weight_host,
                          w->norm1_bias_host, w->norm2_weight_host, w->norm2_bias_host);
+        DeviceScope scope(model->device);
+        auto& L = *model->layers[layer];
+        // All four linears in the on-chip form, or none (the layer then reads its planes).
+        const bool all = upload_q8_blocks(L.q8_qkv, L.bq_qkv, w->in_proj_q8_0, qkv.data(), nqkv, dm) &&
+                         upload_q8_blocks(L.q8_out, L.bq_out, w->out_proj_q8_0, out.data(), dm, hd) &&
+                         upload_q8_blocks(L.q8_1, L.bq1, w->linear1_q8_0, l1.data(), ff, dm) &&
+                         upload_q8_blocks(L.q8_2, L.bq2, w->linear2_q8_0, l2.data(), dm, ff);
+        if (!all)
+            for (DevBuf* b : {&L.q8_qkv, &L.q8_out, &L.q8_1, &L.q8_2, &L.bq_qkv, &L.bq_out, &L.bq1, &L.bq2})
+                b->release();
     });
 }
 

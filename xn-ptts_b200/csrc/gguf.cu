@@ -156,8 +156,8 @@ struct Gguf {
         return it->second;
     }
 
-    // The tensor as f32, checked against the expected dims (innermost first).
-    std::vector<float> f32(const std::string& name, std::vector<uint64_t> want) const {
+    // The tensor's bytes, checked against the expected dims (innermost first) and the file's end.
+    const unsigned char* bytes_of(const std::string& name, const std::vector<uint64_t>& want) const {
         const Tensor& t = find(name);
         std::vector<uint64_t> have = t.dims;
         while (have.size() > want.size() && have.back() == 1) have.pop_back();
@@ -179,7 +179,19 @@ struct Gguf {
         }
         require(t.offset <= bytes.size() - data && bytes_needed <= bytes.size() - data - t.offset,
                 PTTS_B200_ERR_ARG, name + ": data past the end of the file");
-        const unsigned char* p = bytes.data() + data + t.offset;
+        return bytes.data() + data + t.offset;
+    }
+
+    // The q8_0 blocks of a tensor stored as q8_0 (checked as above), else nullptr.
+    const unsigned char* q8_0(const std::string& name, const std::vector<uint64_t>& want) const {
+        return find(name).type == kQ8_0 ? bytes_of(name, want) : nullptr;
+    }
+
+    // The tensor as f32, checked against the expected dims (innermost first).
+    std::vector<float> f32(const std::string& name, const std::vector<uint64_t>& want) const {
+        const Tensor& t = find(name);
+        const unsigned char* p = bytes_of(name, want);
+        const uint64_t n = t.numel();
         std::vector<float> out(n);
         if (t.type == kF32) {
             std::memcpy(out.data(), p, 4 * n);
@@ -234,12 +246,23 @@ extern "C" int ptts_b200_load_gguf(ptts_b200_model* model, ptts_b200_flow* flow,
         const uint64_t nqkv = hd + 2ull * c.num_kv_heads * c.head_dim, ff = c.dim_feedforward;
         for (int l = 0; l < c.num_layers; ++l) {
             const std::string p = "flow_lm.transformer.layers." + std::to_string(l) + ".";
+            // q8_0 linears (the reference's model.q8.gguf) keep their blocks: the layer then
+            // holds the int8 values and block scales beside the exact f16 planes.
+            const unsigned char* b_qkv = g.q8_0(p + "self_attn.in_proj.weight", {dm, nqkv});
+            const unsigned char* b_out = g.q8_0(p + "self_attn.out_proj.weight", {hd, dm});
+            const unsigned char* b_1 = g.q8_0(p + "linear1.weight", {dm, ff});
+            const unsigned char* b_2 = g.q8_0(p + "linear2.weight", {ff, dm});
+            const auto n1w = g.f32(p + "norm1.weight", {dm}), n1b = g.f32(p + "norm1.bias", {dm});
+            const auto n2w = g.f32(p + "norm2.weight", {dm}), n2b = g.f32(p + "norm2.bias", {dm});
+            if (b_qkv && b_out && b_1 && b_2) {
+                ptts_b200_layer_weights_q8_0 q{b_qkv, b_out, b_1, b_2, n1w.data(), n1b.data(), n2w.data(), n2b.data()};
+                check_rc(ptts_b200_model_load_layer_q8_0(model, l, &q));
+                continue;
+            }
             const auto qkv = g.f32(p + "self_attn.in_proj.weight", {dm, nqkv});
             const auto out = g.f32(p + "self_attn.out_proj.weight", {hd, dm});
             const auto l1 = g.f32(p + "linear1.weight", {dm, ff});
             const auto l2 = g.f32(p + "linear2.weight", {ff, dm});
-            const auto n1w = g.f32(p + "norm1.weight", {dm}), n1b = g.f32(p + "norm1.bias", {dm});
-            const auto n2w = g.f32(p + "norm2.weight", {dm}), n2b = g.f32(p + "norm2.bias", {dm});
             ptts_b200_layer_weights_f32 w{qkv.data(), out.data(), l1.data(), l2.data(),
                                           n1w.data(), n1b.data(), n2w.data(), n2b.data()};
             check_rc(ptts_b200_model_load_layer_f32(model, l, &w));

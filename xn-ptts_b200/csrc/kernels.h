@@ -284,6 +284,10 @@ struct LinearArgs {
                                  // hi plane, the flow net's bf16 hi plane, or an f16 copy of w);
                                  // nullptr: the tcgen05 kernel widens the int8 `w` on chip
     const void* wh_lo = nullptr; // flow net: bf16 lo plane of the weights, or nullptr
+    // q8_0 layers at decode sizes: `w` holds the q8_0 values and wblk [N][K / 32] each block's
+    // scale divided by its row's power of two (`scale`), exact in f16; the tcgen05 kernel widens
+    // q * d into the same f16 hi/lo weights as the layer's planes, on chip (a_f16 only).
+    const __half* wblk = nullptr;
     const float* scale;       // [N], or nullptr (1) for the flow net
     const float* bias = nullptr;  // flow epilogues: [N] or nullptr
     const float* aux = nullptr;   // EPI_COND: time embedding [N]; EPI_GATE_RESID: gates

@@ -430,7 +430,7 @@ bool launch_linear(const LinearArgs& a, LinearEpi epi, cudaStream_t s) {
     // The tcgen05 kernel wherever it applies (decode batches and prompts alike: 56 ms against
     // 90 ms for config 5's 139k-row prefill); weights without an int8 copy (f32 or q8_0
     // layers) only have it. PTTS_B200_GEMM=mma selects the mma.sync kernel where both exist.
-    if (a.w == nullptr) return launch_linear_tc(a, epi, s);
+    if (a.w == nullptr || a.wblk) return launch_linear_tc(a, epi, s);  // wblk: tcgen05 only
     const char* sel = getenv("PTTS_B200_GEMM");
     const bool use_tc = !(sel && sel[0] == 'm');
     if (use_tc && launch_linear_tc(a, epi, s)) return true;

@@ -587,6 +587,7 @@ __global__ void __launch_bounds__(kThreadsTma) linear_tma_kernel(const __grid_co
 template <int RT>
 struct I8Tile {
     static constexpr int kStages = 5;
+    static constexpr int kQ8Stages = 3;           // q8_0 form: a hi and a lo A slot per stage
     static constexpr int kW8Bytes = FT * KS;      // int8 tile
     static constexpr int kXBytes = RT * KS * 2;   // one activation plane
     static constexpr int kStageBytes = kW8Bytes + 2 * kXBytes;
@@ -597,6 +598,7 @@ struct I8Tile {
     static constexpr uint32_t kACols = KS / 2;    // one stage's A slot: 64 k as 32 packed pairs
     static constexpr uint32_t kTmemCols = 256;
     static_assert(kAccCols + kStages * kACols <= kTmemCols, "accumulator and A slots fit");
+    static_assert(kAccCols + kQ8Stages * 2 * kACols <= kTmemCols, "q8_0: accumulator and hi/lo A slots fit");
     static_assert(kStageBytes % 1024 == 0 && kXBytes % 1024 == 0, "swizzled tiles stay 1024-byte aligned");
     static_assert(32 * (FT + 4) * 4 <= kBarOffset, "the epilogue's staging tile fits");
     static_assert(3 * (kSmem + 1024) > 228 * 1024, "at most two CTAs per SM (TMEM: 2 x 256 columns)");
@@ -624,13 +626,22 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16
         : "memory");
 }
 
-template <int EPI, int RT>
+// 8 consecutive TMEM columns of this warp's 32 lanes from registers (tcgen05.st.32x32b.x8).
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&r)[8]) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr), "r"(r[0]),
+                 "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+                 : "memory");
+}
+
+template <int EPI, int RT, bool Q8>
 __global__ void __launch_bounds__(kThreadsTma) linear_i8_kernel(const __grid_constant__ LinearArgs p,
                                                                 const __grid_constant__ CUtensorMap tm_w,
                                                                 const __grid_constant__ CUtensorMap tm_x,
                                                                 const __grid_constant__ CUtensorMap tm_xlo) {
     using T = I8Tile<RT>;
-    constexpr int S = T::kStages;
+    // q8_0 form (Q8, p.wblk): 3 stages, each with a hi and a lo A slot; else 5 with one.
+    constexpr int S = Q8 ? T::kQ8Stages : T::kStages;
+    constexpr uint32_t slot_cols = Q8 ? 2 * T::kACols : T::kACols;
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t base = (raw + 1023u) & ~1023u;
@@ -677,7 +688,7 @@ __global__ void __launch_bounds__(kThreadsTma) linear_i8_kernel(const __grid_con
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    const uint32_t tmem_a = tmem + T::kAccCols;  // A slot of stage s: + s * kACols columns
+    const uint32_t tmem_a = tmem + T::kAccCols;  // A slot(s) of stage s: + s * slot_cols columns
 
     if (tid == 0) stamp_mark(p.stamps, p.stamp, STAMP_ENTRY);
     if (tid == 0) {
@@ -721,6 +732,44 @@ __global__ void __launch_bounds__(kThreadsTma) linear_i8_kernel(const __grid_con
                 break;
             }
             const unsigned char* row = smem + st * T::kStageBytes + r * KS;
+            if constexpr (Q8) {
+                // hi = RN16(q d) and lo = RN16(q d - hi) in f16 arithmetic: q and d (the block
+                // scale over the row's power of two, an exact f16) are exact, the product is
+                // rounded once (mul) and the residual once (fma), subnormals kept: the layer's
+                // own f16 planes, bit for bit. This thread's 32 weights are one q8_0 block
+                // (k 32 half .. of the stage), stored 16 k at a time (the kernel stays within
+                // 56 registers a thread, so that a CTA still fits beside the decode attention's
+                // on an SM: each quarter of the register file holds four of these warps and up
+                // to three of the attention's).
+                const __half d = p.wblk[(size_t)(n0 + r) * (p.K / 32) + (k0 + kt * KS) / 32 + half];
+                const __half2 d2 = __halves2half2(d, d);
+                const uint32_t at = tmem_a + lane_base + (uint32_t)st * slot_cols + 16 * half;
+#pragma unroll
+                for (int c2 = 0; c2 < 2; ++c2) {
+                    const int c = 2 * half + c2;
+                    const uint4 q = *reinterpret_cast<const uint4*>(row + ((c ^ ((r >> 1) & 3)) << 4));
+                    uint32_t hv[8], lv[8];
+                    i8x4_to_f16x4(q.x, hv[0], hv[1]);
+                    i8x4_to_f16x4(q.y, hv[2], hv[3]);
+                    i8x4_to_f16x4(q.z, hv[4], hv[5]);
+                    i8x4_to_f16x4(q.w, hv[6], hv[7]);
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        const __half2 qj = *reinterpret_cast<const __half2*>(&hv[j]);
+                        const __half2 h = __hmul2(qj, d2);
+                        const __half2 l = __hfma2(qj, d2, __hneg2(h));
+                        hv[j] = *reinterpret_cast<const uint32_t*>(&h);
+                        lv[j] = *reinterpret_cast<const uint32_t*>(&l);
+                    }
+                    tmem_st8(at + 8 * c2, hv);
+                    tmem_st8(at + T::kACols + 8 * c2, lv);
+                }
+                asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&conv[st]);
+                continue;
+            }
             uint32_t v[16];
 #pragma unroll
             for (int c2 = 0; c2 < 2; ++c2) {  // 16-byte chunks 2 half + c2 (k 16 (2 half + c2) ..)
@@ -738,7 +787,7 @@ __global__ void __launch_bounds__(kThreadsTma) linear_i8_kernel(const __grid_con
                     i8x4_convert<false>(q.w, v[8 * c2 + 6], v[8 * c2 + 7]);
                 }
             }
-            tmem_st16(tmem_a + lane_base + (uint32_t)(st * T::kACols + 16 * half), v);
+            tmem_st16(tmem_a + lane_base + (uint32_t)st * slot_cols + 16 * half, v);
             asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
             tc_fence_before();
             __syncwarp();
@@ -758,10 +807,14 @@ __global__ void __launch_bounds__(kThreadsTma) linear_i8_kernel(const __grid_con
             }
             tc_fence_after();
             const uint64_t dx = sw128_desc(base + st * T::kStageBytes + T::kXOffset);
-            const uint32_t a = tmem_a + (uint32_t)(st * T::kACols);
+            const uint32_t a = tmem_a + (uint32_t)st * slot_cols;
 #pragma unroll
-            for (int kk = 0; kk < KS / 16; ++kk)  // 16 k per MMA: 8 A columns, 32 bytes of B
+            for (int kk = 0; kk < KS / 16; ++kk) {  // 16 k per MMA: 8 A columns, 32 bytes of B
                 tc_mma_ts(tmem, a + 8 * kk, dx + 2 * kk, idesc, (kt | kk) ? 1u : 0u);
+                // q8_0: the weights' lo plane times the activations' hi rows (the first RT rows
+                // of the stage's B tile; lo x lo is below the products' f32 rounding).
+                if (Q8) tc_mma_ts(tmem, a + T::kACols + 8 * kk, dx + 2 * kk, idesc1, 1u);
+            }
             tc_commit(&empty[st]);
             s_consumed = kt + 1;
         }
@@ -1144,7 +1197,7 @@ bool launch_tma(const LinearArgs& a, cudaStream_t s) {
     return true;
 }
 
-template <int EPI, int RT>
+template <int EPI, int RT, bool Q8 = false>
 bool launch_i8(const LinearArgs& a, cudaStream_t s) {
     using T = I8Tile<RT>;
     const bool bf = !a.a_f16;
@@ -1152,9 +1205,9 @@ bool launch_i8(const LinearArgs& a, cudaStream_t s) {
     if (!i8_map(&mw, a.w, a.N, a.K, FT, true) || !f16_map(&mx, a.a, a.M, a.K, RT, bf)) return false;
     mxl = mx;
     if (a.a_lo && !f16_map(&mxl, a.a_lo, a.M, a.K, RT, bf)) return false;
-    set_max_dynamic_smem(reinterpret_cast<const void*>(linear_i8_kernel<EPI, RT>), T::kSmem);
+    set_max_dynamic_smem(reinterpret_cast<const void*>(linear_i8_kernel<EPI, RT, Q8>), T::kSmem);
     dim3 grid(a.N / FT, (a.M + RT - 1) / RT, a.splits);
-    launch_k(linear_i8_kernel<EPI, RT>, grid, dim3(kThreadsTma), T::kSmem, s, a, mw, mx, mxl);
+    launch_k(linear_i8_kernel<EPI, RT, Q8>, grid, dim3(kThreadsTma), T::kSmem, s, a, mw, mx, mxl);
     return true;
 }
 
@@ -1182,6 +1235,8 @@ int weight_form(const LinearArgs& a) { return a.wh_lo ? kW16Lo : (a.wh ? kW16 : 
 
 template <int EPI>
 bool launch_tma_rows(const LinearArgs& a, cudaStream_t s) {
+    // q8_0 values with block scales: only linear_i8_kernel's q8 form reads them (decode sizes).
+    if (a.wblk) return a.a_f16 && a.M < kPersistMinRows && launch_i8<EPI, 32, true>(a, s);
     const int wm = weight_form(a);
     if (a.M >= kPersistMinRows && a.splits == 1 && EPI != EPI_PARTIAL) {
         if (wm == kW16Lo) return launch_persist<EPI, kW16Lo>(a, s);
