@@ -22,13 +22,16 @@
  *   - calls on one object are serialised by the caller (one generation per session, as the
  *     reference's in-flight guard enforces at ptts/src/synth.rs:958-975).
  *
- * Layouts. K/V caches: [num_layers][num_streams][capacity][num_heads][head_dim], the layout of
- * StreamingMHAState::k_cache per layer (transformer.rs:15-18). Rows of q/k/v or hidden states are
- * row-major with heads-major, then head_dim, within a row (transformer.rs:197-211).
+ * Layouts. K/V caches: [num_layers][num_heads / 8][num_streams][capacity][8][head_dim]: per
+ * layer the layout of StreamingMHAState::k_cache ([num_streams][capacity][num_heads][head_dim],
+ * transformer.rs:15-18) when num_heads is 8, and for more heads one such block per group of 8
+ * heads (heads 8g .. 8g + 7 in block g), so that every position's row of a group is 1 KB (bf16)
+ * of contiguous memory. Rows of q/k/v or hidden states are row-major with heads-major, then
+ * head_dim, within a row (transformer.rs:197-211).
  *
- * Supported shapes: head_dim 64 and num_heads * head_dim = 512 (the 31m/40m flow LMs);
- * d_model and dim_feedforward multiples of 64; num_kv_heads dividing num_heads.
- * Others are refused with PTTS_B200_ERR_UNSUPPORTED.
+ * Supported shapes: head_dim 64 and num_heads a multiple of 8 (8 in the 31m/40m flow LMs, 16 in
+ * the reference's 1024-wide test config); d_model and dim_feedforward multiples of 64;
+ * num_kv_heads dividing num_heads. Others are refused with PTTS_B200_ERR_UNSUPPORTED.
  */
 #ifndef PTTS_B200_H
 #define PTTS_B200_H
@@ -115,8 +118,9 @@ void ptts_b200_kv_destroy(ptts_b200_kv* kv);
 /* The filled length (current_end) of every stream, from the host-side mirror, no sync. */
 int ptts_b200_kv_lengths(const ptts_b200_kv* kv, int32_t* lengths_host);
 
-/* Device pointers of one layer's K and V caches ([num_streams][capacity][H][D]) and of the
- * device lengths ([num_streams] int32). Borrowed; valid until ptts_b200_kv_destroy. */
+/* Device pointers of one layer's K and V caches ([H / 8][num_streams][capacity][8][D], see
+ * Layouts) and of the device lengths ([num_streams] int32). Borrowed; valid until
+ * ptts_b200_kv_destroy. */
 int ptts_b200_kv_pointers(const ptts_b200_kv* kv, int layer, void** k, void** v,
                           int32_t** lengths);
 

@@ -325,17 +325,20 @@ class KvState:
         return k.value, v.value, ln.value
 
     def tensors(self, layer: int):
-        """Views (torch, no copy) of one layer's K and V caches [S, cap, H, D] and the device
-        lengths [S]."""
+        """Views (torch, no copy) of one layer's K and V caches and the device lengths [S]: the
+        caches as [S, cap, H, D] with 8 heads, and as [S, cap, H / 8, 8, D] with more (each
+        group of 8 heads is its own [S, cap, 8, D] block; `.reshape(S, cap, H, D)` copies)."""
         import torch
         k, v, ln = self.pointers(layer)
-        shape = (self.num_streams, self.capacity, self.num_heads, self.head_dim)
+        G = self.num_heads // 8
+        shape = (G, self.num_streams, self.capacity, 8, self.head_dim)
         if self.dtype == "bf16":
             kt = torch.as_tensor(_Cai(k, shape, "<i2"), device=f"cuda:{self.device}").view(torch.bfloat16)
             vt = torch.as_tensor(_Cai(v, shape, "<i2"), device=f"cuda:{self.device}").view(torch.bfloat16)
         else:
             kt = torch.as_tensor(_Cai(k, shape, "<f4"), device=f"cuda:{self.device}")
             vt = torch.as_tensor(_Cai(v, shape, "<f4"), device=f"cuda:{self.device}")
+        kt, vt = (t[0] if G == 1 else t.permute(1, 2, 0, 3, 4) for t in (kt, vt))
         lt = torch.as_tensor(_Cai(ln, (self.num_streams,), "<i4"), device=f"cuda:{self.device}")
         return kt, vt, lt
 

@@ -44,7 +44,7 @@ struct Workspace {
         ff_hi.need(r * c.dim_feedforward * 2);
         ff_lo.need(r * c.dim_feedforward * 2);
         split.need(4 * r * c.d_model * 4);
-        counters.need_zeroed(decode_counter_ints(r) * sizeof(int));
+        counters.need_zeroed(decode_counter_ints(r) * sizeof(int) * (c.num_heads / kGroupHeads));
     }
 };
 
@@ -226,10 +226,17 @@ struct ptts_b200_kv {
         h_ring_valid[(size_t)s * capacity + w] = 1;
         h_ring_filled[s] = std::max(h_ring_filled[s], w + 1);
     }
-    size_t layer_bytes() const { return (size_t)streams * capacity * row_bytes; }
-    size_t stream_bytes() const { return (size_t)capacity * row_bytes; }
+    // A layer holds its heads in groups of 8 (kv_offset): per group a [streams][capacity] block
+    // of rows of 8 heads (group_row_bytes each), groups one after another.
+    int groups() const { return heads / kGroupHeads; }
+    size_t group_row_bytes() const { return row_bytes / groups(); }
+    size_t stream_bytes() const { return (size_t)capacity * group_row_bytes(); }  // in one group
+    size_t group_bytes() const { return (size_t)streams * stream_bytes(); }
+    size_t layer_bytes() const { return (size_t)groups() * group_bytes(); }
     char* k_layer(int l) const { return k.as<char>() + l * layer_bytes(); }
     char* v_layer(int l) const { return v.as<char>() + l * layer_bytes(); }
+    char* k_group(int l, int g) const { return k_layer(l) + g * group_bytes(); }
+    char* v_group(int l, int g) const { return v_layer(l) + g * group_bytes(); }
 };
 
 // What besides the stream set a recorded step graph depends on: a frame graph also records the
@@ -459,28 +466,34 @@ struct Tiles {
     bool windowed = false;  // a windowed stream is in the call: the CUDA-core kernel maps its slots
 };
 
-// q_rot is the rotated q: f32 [n_rows][512], or for prompts where prefill_fa holds, its bf16 hi
-// plane followed by the lo plane (n_rows x 512 each).
-void attention(const ptts_b200_kv* kv, int layer, bool decode, const RowPlan& plan, int n_rows,
-               const float* q_rot, void* out, void* out_lo, int out_mode, DevBuf& part,
-               DevBuf& counters, const Tiles& tiles, cudaStream_t s, bool compact = false,
-               unsigned long long* stamps = nullptr, int stamp = -1) {
+// The attention of head group g (heads 8g .. 8g + 7) on its cache block and its columns of q_rot
+// and out (rows of ld = H * 64 elements): one launch.
+void attention_group(const ptts_b200_kv* kv, int layer, int g, bool decode, const RowPlan& plan, int n_rows,
+                     const float* q_rot, void* out, void* out_lo, int out_mode, DevBuf& part, DevBuf& counters,
+                     const Tiles& tiles, cudaStream_t s, bool compact, unsigned long long* stamps, int stamp) {
     const bool bf16 = kv->dtype == PTTS_B200_BF16;
     const float qscale = (1.0f / sqrtf((float)kv->head_dim)) * kLog2e;  // transformer.rs:215
+    const int ld = kv->heads * kHeadDim, G = kv->groups();
+    const size_t col = (size_t)g * kRowWidth, out_elem = out_mode == kOutF32 ? 4 : 2;
+    void* o = static_cast<char*>(out) + col * out_elem;
+    void* o_lo = out_lo ? static_cast<char*>(out_lo) + col * out_elem : nullptr;
     if (decode) {
         const int grid = decode_grid(kv->device, compact);
+        // Partial records and merge counters: a slice per group.
+        const size_t n_part = decode_part_floats(n_rows, grid), n_cnt = decode_counter_ints(n_rows);
         DecodeArgs a{};
-        a.k_cache = kv->k_layer(layer);
-        a.v_cache = kv->v_layer(layer);
+        a.k_cache = kv->k_group(layer, g);
+        a.v_cache = kv->v_group(layer, g);
         a.stream_bytes = (long long)kv->stream_bytes();
         a.row_stream = plan.row_stream;
         a.prefix = plan.prefix;
-        a.q = q_rot;
-        a.out = out;
-        a.out_lo = out_lo;
+        a.q = q_rot + col;
+        a.out = o;
+        a.out_lo = o_lo;
         a.out_mode = out_mode;
-        a.part = static_cast<float*>(part.need(sizeof(float) * decode_part_floats(n_rows, grid)));
-        a.counters = static_cast<int*>(counters.need_zeroed(sizeof(int) * decode_counter_ints(n_rows)));
+        a.ld = ld;
+        a.part = static_cast<float*>(part.need(sizeof(float) * n_part * G)) + n_part * g;
+        a.counters = static_cast<int*>(counters.need_zeroed(sizeof(int) * n_cnt * G)) + n_cnt * g;
         a.cta_first = plan.cta_first;
         a.B = n_rows;
         a.qscale = qscale;
@@ -490,30 +503,33 @@ void attention(const ptts_b200_kv* kv, int layer, bool decode, const RowPlan& pl
         a.capacity = kv->capacity;
         a.window = kv->window.as<int32_t>();
         a.row_pos = plan.row_pos;
-        a.prestart = true;  // the in_proj or rope_append launch sits between the plan and this one
+        // The in_proj or rope_append launch (or, past group 0, the previous group's attention,
+        // which runs only after it) sits between the plan and this one.
+        a.prestart = true;
         a.stamps = stamps;
         a.stamp = stamp;
         launch_decode_attn(a, bf16, grid, s, decode_ring_compact(compact));
     } else {
         PrefillArgs a{};
-        a.k_cache = kv->k_layer(layer);
-        a.v_cache = kv->v_layer(layer);
+        a.k_cache = kv->k_group(layer, g);
+        a.v_cache = kv->v_group(layer, g);
         a.stream_elems = (long long)kv->capacity * kRowWidth;
         a.row_stream = plan.row_stream;
         a.row_pos = plan.row_pos;
         a.window = kv->window.as<int32_t>();
-        a.q = q_rot;
-        a.out = out;
-        a.out_lo = out_lo;
+        a.q = q_rot + col;
+        a.out = o;
+        a.out_lo = o_lo;
         a.out_mode = out_mode;
+        a.ld = ld;
         a.rows = n_rows;
         a.qscale = qscale;
         a.err = kv->err.as<uint32_t>();
         if (tiles.n > 0 && prefill_fa(bf16, decode, tiles.windowed)) {
             // The head-group pipeline (attn_prefill_fa.cu), Q tiles by TMA from the hi/lo planes.
             a.q = nullptr;
-            a.q_hi = reinterpret_cast<const __nv_bfloat16*>(q_rot);
-            a.q_lo = a.q_hi + (size_t)n_rows * kRowWidth;
+            a.q_hi = reinterpret_cast<const __nv_bfloat16*>(q_rot) + col;
+            a.q_lo = reinterpret_cast<const __nv_bfloat16*>(q_rot) + (size_t)n_rows * ld + col;
             require(launch_prefill_attn_fa(a, tiles.dev, tiles.n, kv->streams, kv->capacity, s), PTTS_B200_ERR_CUDA,
                     "could not describe the prompt attention's tensors (cuTensorMapEncodeTiled)");
         } else if (bf16 && tiles.n > 0 && prefill_on_tensor_cores() && !tiles.windowed) {
@@ -523,6 +539,17 @@ void attention(const ptts_b200_kv* kv, int layer, bool decode, const RowPlan& pl
         }
     }
     check_launch();
+}
+
+// q_rot is the rotated q: f32 [n_rows][H * 64], or for prompts where prefill_fa holds, its bf16
+// hi plane followed by the lo plane (n_rows x H * 64 each). One launch per group of 8 heads.
+void attention(const ptts_b200_kv* kv, int layer, bool decode, const RowPlan& plan, int n_rows,
+               const float* q_rot, void* out, void* out_lo, int out_mode, DevBuf& part,
+               DevBuf& counters, const Tiles& tiles, cudaStream_t s, bool compact = false,
+               unsigned long long* stamps = nullptr, int stamp = -1) {
+    for (int g = 0; g < kv->groups(); ++g)
+        attention_group(kv, layer, g, decode, plan, n_rows, q_rot, out, out_lo, out_mode, part, counters, tiles, s,
+                        compact, stamps, g == 0 ? stamp : -1);
 }
 
 void check_model_kv(const ptts_b200_model* m, const ptts_b200_kv* kv) {
@@ -958,7 +985,7 @@ void run_step(ptts_b200_model* model, ptts_b200_kv* kv, const int32_t* streams_h
             ln.n = i == 0 ? n0 : n - n0;
             const int r = std::max(ln.n, 1);
             ln.ws.size(c, r);
-            ln.ws.part.need(sizeof(float) * decode_part_floats(r, grid));
+            ln.ws.part.need(sizeof(float) * decode_part_floats(r, grid) * (c.num_heads / kGroupHeads));
             ln.row_stream.need(sizeof(int32_t) * r);
             ln.row_pos.need(2 * sizeof(int32_t) * r);  // positions, then slots
             ln.prefix.need(sizeof(int32_t) * (r + 1 + kMaxDecodeGrid));
@@ -1028,7 +1055,7 @@ void run_step(ptts_b200_model* model, ptts_b200_kv* kv, const int32_t* streams_h
         CK(cudaEventSynchronize(ev[E + 1]));
         double bytes = 0.0;  // K and V rows read, f32 q read, bf16 output written
         for (int i = 0; i < n; ++i) bytes += (double)attended_keys(kv, streams_host[i]) * kv->row_bytes * 2;
-        bytes += (double)n * kRowWidth * (4 + 2);
+        bytes += (double)n * kv->heads * kHeadDim * (4 + 2);
         double attn_ms = 0.0;
         for (int l = 0; l < L * n_lanes; ++l) {
             float ms = 0.f;
@@ -1078,8 +1105,8 @@ int ptts_b200_kv_create(int device, int num_layers, int num_streams, int capacit
         *out = nullptr;
         require(num_layers > 0 && num_streams > 0 && capacity > 0, PTTS_B200_ERR_ARG,
                 "layers, streams and capacity must be positive");
-        require(head_dim == kHeadDim && num_heads * head_dim == kRowWidth, PTTS_B200_ERR_UNSUPPORTED,
-                "only head_dim 64 with num_heads * head_dim = 512 is implemented");
+        require(head_dim == kHeadDim && num_heads > 0 && num_heads % kGroupHeads == 0, PTTS_B200_ERR_UNSUPPORTED,
+                "only head_dim 64 with a multiple of 8 heads is implemented");
         require(dtype == PTTS_B200_F32 || dtype == PTTS_B200_BF16, PTTS_B200_ERR_ARG, "unknown dtype");
         DeviceScope scope(device);
         static uint64_t next_uid = 1;
@@ -1171,8 +1198,9 @@ int ptts_b200_kv_reset(ptts_b200_kv* kv, const int32_t* streams_host, int n, voi
         DeviceScope scope(kv->device);
         cudaStream_t s = as_stream(cuda_stream);
         const int32_t* d = kv->upload_scratch(streams_host, sizeof(int32_t) * n, s);
-        launch_reset_streams(kv->k.p, kv->v.p, kv->len.as<int32_t>(), d, n, kv->layers,
-                             (long long)kv->layer_bytes(), (long long)kv->stream_bytes(), s);
+        // Every (layer, head group) block in turn: groups() blocks of group_bytes() per layer.
+        launch_reset_streams(kv->k.p, kv->v.p, kv->len.as<int32_t>(), d, n, kv->layers * kv->groups(),
+                             (long long)kv->group_bytes(), (long long)kv->stream_bytes(), s);
         check_launch();
         for (int i = 0; i < n; ++i) {
             const int st = streams_host[i];
@@ -1204,8 +1232,19 @@ int ptts_b200_kv_load_prefix(ptts_b200_kv* kv, int layer, int stream, const void
         const size_t off = (size_t)stream * kv->stream_bytes();
         if (len > 0) {
             require(k && v, PTTS_B200_ERR_ARG, "k/v are NULL");
-            CK(cudaMemcpyAsync(kv->k_layer(layer) + off, k, len * kv->row_bytes, cudaMemcpyDefault, s));
-            CK(cudaMemcpyAsync(kv->v_layer(layer) + off, v, len * kv->row_bytes, cudaMemcpyDefault, s));
+            if (kv->groups() == 1) {
+                CK(cudaMemcpyAsync(kv->k_layer(layer) + off, k, len * kv->row_bytes, cudaMemcpyDefault, s));
+                CK(cudaMemcpyAsync(kv->v_layer(layer) + off, v, len * kv->row_bytes, cudaMemcpyDefault, s));
+            } else {
+                // [len][H][D] rows into each head group's block: 8 heads of every row per group.
+                const size_t gw = kv->group_row_bytes();
+                for (int g = 0; g < kv->groups(); ++g) {
+                    CK(cudaMemcpy2DAsync(kv->k_group(layer, g) + off, gw, static_cast<const char*>(k) + g * gw,
+                                         kv->row_bytes, gw, len, cudaMemcpyDefault, s));
+                    CK(cudaMemcpy2DAsync(kv->v_group(layer, g) + off, gw, static_cast<const char*>(v) + g * gw,
+                                         kv->row_bytes, gw, len, cudaMemcpyDefault, s));
+                }
+            }
         }
         if (set_length) {
             kv->h_len[stream] = len;
@@ -1236,14 +1275,15 @@ int ptts_b200_kv_copy_stream(ptts_b200_kv* dst, int dst_stream, const ptts_b200_
                     "a windowed cache is copied whole, into a stream of the same capacity");
             DeviceScope scope(dst->device);
             cudaStream_t s = as_stream(cuda_stream);
-            for (int l = 0; l < dst->layers; ++l) {
-                CK(cudaMemcpyAsync(dst->k_layer(l) + (size_t)dst_stream * dst->stream_bytes(),
-                                   src->k_layer(l) + (size_t)src_stream * src->stream_bytes(), dst->stream_bytes(),
-                                   cudaMemcpyDeviceToDevice, s));
-                CK(cudaMemcpyAsync(dst->v_layer(l) + (size_t)dst_stream * dst->stream_bytes(),
-                                   src->v_layer(l) + (size_t)src_stream * src->stream_bytes(), dst->stream_bytes(),
-                                   cudaMemcpyDeviceToDevice, s));
-            }
+            for (int l = 0; l < dst->layers; ++l)
+                for (int g = 0; g < dst->groups(); ++g) {
+                    CK(cudaMemcpyAsync(dst->k_group(l, g) + (size_t)dst_stream * dst->stream_bytes(),
+                                       src->k_group(l, g) + (size_t)src_stream * src->stream_bytes(),
+                                       dst->stream_bytes(), cudaMemcpyDeviceToDevice, s));
+                    CK(cudaMemcpyAsync(dst->v_group(l, g) + (size_t)dst_stream * dst->stream_bytes(),
+                                       src->v_group(l, g) + (size_t)src_stream * src->stream_bytes(),
+                                       dst->stream_bytes(), cudaMemcpyDeviceToDevice, s));
+                }
             dst->h_len[dst_stream] = src->h_len[src_stream];
             dst->h_window[dst_stream] = src->h_window[src_stream];
             dst->staging.upload(dst->len.as<int32_t>() + dst_stream, &dst->h_len[dst_stream], sizeof(int32_t), s);
@@ -1257,12 +1297,13 @@ int ptts_b200_kv_copy_stream(ptts_b200_kv* dst, int dst_stream, const ptts_b200_
                                              std::to_string(dst->capacity));
         DeviceScope scope(dst->device);
         cudaStream_t s = as_stream(cuda_stream);
-        for (int l = 0; l < dst->layers; ++l) {
-            char* dk = dst->k_layer(l) + (size_t)dst_stream * dst->stream_bytes();
-            char* dv = dst->v_layer(l) + (size_t)dst_stream * dst->stream_bytes();
-            const char* sk = src->k_layer(l) + (size_t)src_stream * src->stream_bytes();
-            const char* sv = src->v_layer(l) + (size_t)src_stream * src->stream_bytes();
-            const size_t n = (size_t)used * dst->row_bytes;
+        for (int lg = 0; lg < dst->layers * dst->groups(); ++lg) {
+            const int l = lg / dst->groups(), g = lg % dst->groups();
+            char* dk = dst->k_group(l, g) + (size_t)dst_stream * dst->stream_bytes();
+            char* dv = dst->v_group(l, g) + (size_t)dst_stream * dst->stream_bytes();
+            const char* sk = src->k_group(l, g) + (size_t)src_stream * src->stream_bytes();
+            const char* sv = src->v_group(l, g) + (size_t)src_stream * src->stream_bytes();
+            const size_t n = (size_t)used * dst->group_row_bytes();
             if (n) {
                 CK(cudaMemcpyAsync(dk, sk, n, cudaMemcpyDeviceToDevice, s));
                 CK(cudaMemcpyAsync(dv, sv, n, cudaMemcpyDeviceToDevice, s));
@@ -1328,7 +1369,8 @@ int ptts_b200_attend(ptts_b200_kv* kv, int layer, const void* q, const void* k, 
         ra.q = q;
         ra.k = k;
         ra.v = v;
-        ra.q_out = static_cast<float*>(kv->q_rot.need((size_t)n_rows * kRowWidth * sizeof(float)));
+        const size_t hd = (size_t)kv->heads * kHeadDim;
+        ra.q_out = static_cast<float*>(kv->q_rot.need((size_t)n_rows * hd * sizeof(float)));
         ra.k_cache = kv->k_layer(layer);
         ra.v_cache = kv->v_layer(layer);
         ra.row_stream = plan.row_stream;
@@ -1345,7 +1387,7 @@ int ptts_b200_attend(ptts_b200_kv* kv, int layer, const void* q, const void* k, 
         for (int i = 0; i < n_seq; ++i) windowed = windowed || kv->is_window(streams_host[i]);
         if (prefill_fa(kv->dtype == PTTS_B200_BF16, decode, windowed)) {
             ra.q_hi = reinterpret_cast<__nv_bfloat16*>(ra.q_out);  // two bf16 planes in the f32 buffer
-            ra.q_lo = ra.q_hi + (size_t)n_rows * kRowWidth;
+            ra.q_lo = ra.q_hi + (size_t)n_rows * hd;
             ra.q_scale = (1.0f / sqrtf((float)kv->head_dim)) * kLog2e;  // transformer.rs:215, exp2 domain
         }
         launch_rope_append(ra, in_dtype == PTTS_B200_BF16, kv->dtype == PTTS_B200_BF16, s);
@@ -1372,7 +1414,7 @@ int ptts_b200_attend(ptts_b200_kv* kv, int layer, const void* q, const void* k, 
             double bytes = 0.0;
             for (int i = 0; i < n_seq; ++i)
                 bytes += (double)attended_keys(kv, streams_host[i]) * kv->row_bytes * 2;
-            bytes += (double)n_seq * kRowWidth * (4 + (out_dtype == PTTS_B200_BF16 ? 2 : 4));
+            bytes += (double)n_seq * hd * (4 + (out_dtype == PTTS_B200_BF16 ? 2 : 4));
             trace_add(1, ms, bytes, 0, 0.0);
         }
     });
@@ -1413,8 +1455,8 @@ int ptts_b200_model_create(int device, const ptts_b200_config* config, ptts_b200
             fail(PTTS_B200_ERR_ARG, "the config's " + std::to_string(c.num_kv_heads) +
                                         " key/value heads do not divide its " +
                                         std::to_string(c.num_heads) + " attention heads");
-        require(c.head_dim == kHeadDim && c.num_heads * c.head_dim == kRowWidth,
-                PTTS_B200_ERR_UNSUPPORTED, "only head_dim 64 with num_heads * head_dim = 512 is implemented");
+        require(c.head_dim == kHeadDim && c.num_heads % kGroupHeads == 0, PTTS_B200_ERR_UNSUPPORTED,
+                "only head_dim 64 with a multiple of 8 heads is implemented");
         require(c.d_model > 0 && c.d_model % 128 == 0 && c.d_model <= 1024, PTTS_B200_ERR_UNSUPPORTED,
                 "d_model must be a multiple of 128 up to 1024");
         require(c.dim_feedforward > 0 && c.dim_feedforward % 64 == 0, PTTS_B200_ERR_UNSUPPORTED,
@@ -1868,7 +1910,7 @@ int ptts_b200_kv_evict(ptts_b200_kv* kv, int stream, int prefix, const int32_t* 
         a.layers = kv->layers;
         const long long elem = kv->dtype == PTTS_B200_BF16 ? 2 : 4;
         a.layer_elems = (long long)kv->layer_bytes() / elem;
-        a.stream_elems = (long long)kv->stream_bytes() / elem;
+        a.streams = kv->streams;
         a.row_elems = kv->heads * kv->head_dim;
         a.capacity = kv->capacity;
         a.sid = stream;

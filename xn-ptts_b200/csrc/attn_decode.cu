@@ -171,7 +171,7 @@ __device__ __forceinline__ void merge_head(const DecodeArgs& a, int b, int h, in
         n1 += f * __ldcg(rec + 2 * lane + 1);
     }
     const float inv = 1.f / den;
-    const long long at = (long long)b * kRowWidth + h * kHeadDim + 2 * lane;
+    const long long at = (long long)b * a.ld + h * kHeadDim + 2 * lane;
     const float o0 = n0 * inv, o1 = n1 * inv;
     if (a.out_mode == kOutF32) {
         *reinterpret_cast<float2*>(static_cast<float*>(a.out) + at) = make_float2(o0, o1);
@@ -250,7 +250,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(DecodeArgs a) 
             stamp_mark(a.stamps, a.stamp, STAMP_START);
             waited = true;
             for (int i = 0; i < n_deferred; ++i)
-                bulk_g2s(smem + q_stage[i] * kStageBytes + kDataBytes, a.q + (long long)q_row[i] * kRowWidth,
+                bulk_g2s(smem + q_stage[i] * kStageBytes + kDataBytes, a.q + (long long)q_row[i] * a.ld,
                          kQStageBytes, &full[q_stage[i]], pol);
         };
         for (int b = b0; b < a.B && ok; ++b) {
@@ -290,7 +290,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(DecodeArgs a) 
                 mbar_arrive_expect_tx(&full[st], 2u * n * RB + (p == s0 && !q_loaded ? (uint32_t)kQStageBytes : 0u));
                 if (p == s0 && !q_loaded) {
                     if (waited) {
-                        bulk_g2s(sb + kDataBytes, a.q + (long long)b * kRowWidth, kQStageBytes, &full[st], pol);
+                        bulk_g2s(sb + kDataBytes, a.q + (long long)b * a.ld, kQStageBytes, &full[st], pol);
                     } else {
                         q_stage[n_deferred] = st;
                         q_row[n_deferred++] = b;
@@ -333,7 +333,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(DecodeArgs a) 
     float q_first[8];
     if (a.prestart && a.cta_first) {
         const int b0 = min(max(a.cta_first[c], 0), max(a.B - 1, 0));
-        load_q<T>(a.q + (long long)b0 * kRowWidth + h * kHeadDim, j, q_first);
+        load_q<T>(a.q + (long long)b0 * a.ld + h * kHeadDim, j, q_first);
     }
     for (int it = 0;; ++it) {
         const int st = it % kStages;
@@ -455,7 +455,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(DecodeArgs a) 
                 const float inv = 1.f / ll;
 #pragma unroll
                 for (int i = 0; i < 8; ++i) aa[i] *= inv;
-                store_out<T>(a, (long long)b * kRowWidth + h * kHeadDim, j, aa);
+                store_out<T>(a, (long long)b * a.ld + h * kHeadDim, j, aa);
             }
             continue;
         }

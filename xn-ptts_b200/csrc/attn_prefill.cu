@@ -63,7 +63,7 @@ __global__ void __launch_bounds__(256) prefill_attn_kernel(PrefillArgs a) {
     const T* vb = static_cast<const T*>(a.v_cache) + (long long)sid * a.stream_elems + h * kHeadDim;
     float q[8];
     {
-        const float* qh = a.q + ((long long)row * kHeads + h) * kHeadDim;
+        const float* qh = a.q + (long long)row * a.ld + h * kHeadDim;
         const float4 x = *reinterpret_cast<const float4*>(qh + (sizeof(T) == 2 ? 8 * j : 4 * j));
         const float4 y = *reinterpret_cast<const float4*>(qh + (sizeof(T) == 2 ? 8 * j + 4 : 32 + 4 * j));
         q[0] = x.x; q[1] = x.y; q[2] = x.z; q[3] = x.w;
@@ -117,7 +117,7 @@ __global__ void __launch_bounds__(256) prefill_attn_kernel(PrefillArgs a) {
     }
     if (g != 0) return;
     const float inv = 1.f / l;
-    const long long at = (long long)row * kRowWidth + h * kHeadDim;
+    const long long at = (long long)row * a.ld + h * kHeadDim;
     if (a.out_mode == kOutF32) {
         float* o = static_cast<float*>(a.out) + at;
 #pragma unroll

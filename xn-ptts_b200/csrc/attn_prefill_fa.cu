@@ -408,7 +408,7 @@ __global__ void __launch_bounds__(kThreadsF, 2) prefill_fa_kernel(PrefillArgs a,
                 fa_ld32(tmem + lane_base + kColO + 64 * (fh & 1) + 32 * half, o);
                 fa_wait_ld();
                 if (!active) continue;
-                const long long at = (long long)(row0 + r) * kRowWidth + (h0 + fh) * kHeadDim + 32 * half;
+                const long long at = (long long)(row0 + r) * a.ld + (h0 + fh) * kHeadDim + 32 * half;
                 if (a.out_mode == kOutF32) {
                     float4* out = reinterpret_cast<float4*>(static_cast<float*>(a.out) + at);
 #pragma unroll
@@ -578,8 +578,8 @@ bool launch_prefill_attn_fa(const PrefillArgs& a, const int2* tiles, int n_tiles
         !bf16_rows_map(&mv, a.v_cache, rows, kRowWidth, kHeadDim, KT))
         return false;
     if (a.q_hi) {
-        if (!bf16_rows_map(&mqh, a.q_hi, a.rows, kRowWidth, kHeadDim, QT) ||
-            !bf16_rows_map(&mql, a.q_lo, a.rows, kRowWidth, kHeadDim, QT))
+        if (!bf16_rows_map(&mqh, a.q_hi, a.rows, kRowWidth, kHeadDim, QT, a.ld) ||
+            !bf16_rows_map(&mql, a.q_lo, a.rows, kRowWidth, kHeadDim, QT, a.ld))
             return false;
     } else {
         mqh = mk;  // unused: the softmax warps convert the f32 q

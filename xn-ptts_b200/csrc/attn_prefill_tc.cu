@@ -185,7 +185,7 @@ __global__ void __maxnreg__(168) prefill_tc_kernel(PrefillArgs a, const int2* ti
         // Q (rotated, f32) -> bf16 hi/lo tiles.
         {
             float q[64];
-            const float* qr = a.q + ((long long)(row0 + (active ? r : 0)) * 8 + h) * kHeadDim;
+            const float* qr = a.q + (long long)(row0 + (active ? r : 0)) * a.ld + h * kHeadDim;
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
                 const float4 x = active ? *reinterpret_cast<const float4*>(qr + 4 * i) : make_float4(0.f, 0.f, 0.f, 0.f);
@@ -260,7 +260,7 @@ __global__ void __maxnreg__(168) prefill_tc_kernel(PrefillArgs a, const int2* ti
         }
         if (active && ok && n_kt > 0) {
             const float inv = 1.f / l;
-            const long long at = (long long)(row0 + r) * kRowWidth + h * kHeadDim;
+            const long long at = (long long)(row0 + r) * a.ld + h * kHeadDim;
             if (a.out_mode == kOutF32) {
                 float* out = static_cast<float*>(a.out) + at;
 #pragma unroll

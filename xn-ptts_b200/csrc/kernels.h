@@ -57,7 +57,15 @@ inline cudaError_t launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, siz
 enum { STAMP_ENTRY = 0, STAMP_START = 1, STAMP_END = 2, STAMP_LAST_ENTRY = 3 };
 
 constexpr int kHeadDim = 64;   // D: the only head size the kernels implement
-constexpr int kRowWidth = 512; // H * D: one cache row of all heads
+constexpr int kRowWidth = 512; // one cache row of a group of 8 heads (kGroupHeads * D)
+constexpr int kGroupHeads = kRowWidth / kHeadDim;  // heads per group: 8
+// Heads come in groups of 8. A layer's cache holds each group as one [streams][capacity][8][64]
+// block, groups one after another, so every kernel reads a group's key or value rows as the
+// contiguous 1 KB (bf16) rows of an 8-head layer. Element offset of (stream, slot, head) there:
+__host__ __device__ inline long long kv_offset(int sid, int slot, int head, int num_streams, int capacity) {
+    return (((long long)(head / kGroupHeads) * num_streams + sid) * capacity + slot) * kRowWidth +
+           (head % kGroupHeads) * kHeadDim;
+}
 constexpr int kMaxPairs = kHeadDim / 2;
 
 // Per-call row plan on the device: which arena stream, position and cache slot each row has.
@@ -128,7 +136,7 @@ struct RingEvictArgs {
     void* k_cache;            // all layers
     int layers;
     long long layer_elems;    // elements per layer
-    long long stream_elems;   // elements per stream (capacity * H * D)
+    int streams;              // streams of the arena (head groups: see kv_offset)
     int row_elems;            // H * D
     int capacity, sid, prefix, filled, shift;
     bool bf16;
@@ -189,15 +197,16 @@ void launch_rope_append(const RopeAppendArgs& a, bool in_bf16, bool cache_bf16, 
 struct DecodeArgs {
     unsigned long long* stamps = nullptr;  // kernel timeline slot (see stamp_mark), or none
     int stamp = -1;
-    const void* k_cache;      // layer base [S][cap][H][D]
+    const void* k_cache;      // this launch's head group of the layer: [S][cap][8][D]
     const void* v_cache;
     long long stream_bytes;   // capacity * row bytes
     const int32_t* row_stream;  // [B] arena stream of each sequence
     const int32_t* prefix;      // [B + 1] prefix sums of attended keys
-    const float* q;           // [B][H][D] f32, rotated
-    void* out;                // [B][H*D]: f32, bf16, or the hi plane (see out_mode)
-    void* out_lo;             // [B][H*D] bf16 lo plane when out_mode == kOutHiLo
+    const float* q;           // [B][ld] f32, rotated: this launch's 8 heads from q
+    void* out;                // [B][ld]: f32, bf16, or the hi plane (see out_mode)
+    void* out_lo;             // [B][ld] bf16 lo plane when out_mode == kOutHiLo
     int out_mode;
+    int ld = kRowWidth;       // elements from one row of q and out to the next (H * D)
     float* part;              // [(B + grid) * H * kPartStride]
     int* counters;            // [B * H], zero between launches (the merging warp resets its entry)
     const int32_t* cta_first = nullptr;  // [grid] the stream each CTA starts in, or nullptr (search)
@@ -229,9 +238,9 @@ size_t decode_part_floats(int B, int grid);
 size_t decode_counter_ints(int B);
 
 struct PrefillArgs {
-    const void* k_cache;
+    const void* k_cache;      // this launch's head group of the layer: [S][cap][8][D]
     const void* v_cache;
-    long long stream_elems;   // capacity * H * D
+    long long stream_elems;   // capacity * 8 * D
     const int32_t* row_stream;
     const int32_t* row_pos;
     const int32_t* window = nullptr;  // [streams] context of windowed streams (0: none)
@@ -240,9 +249,10 @@ struct PrefillArgs {
     // the prefill_fa kernel copies by TMA (it needs them).
     const __nv_bfloat16* q_hi = nullptr;
     const __nv_bfloat16* q_lo = nullptr;
-    void* out;                // [rows][H*D] (see out_mode)
-    void* out_lo;
+    void* out;                // [rows][ld] (see out_mode); q, q_hi, q_lo, out, out_lo start at
+    void* out_lo;             // this launch's 8 heads
     int out_mode;
+    int ld = kRowWidth;       // elements from one row of q (q_hi, q_lo) and out to the next
     int rows;
     float qscale;
     uint32_t* err;
@@ -260,7 +270,8 @@ bool launch_prefill_attn_fa(const PrefillArgs& a, const int2* tiles, int n_tiles
                             cudaStream_t s);
 // Tensor map of a row-major [rows][cols] bf16 matrix, box box_cols (128 bytes) x box_rows,
 // 128-byte swizzle (linear_tc.cu).
-bool bf16_rows_map(CUtensorMap* out, const void* ptr, long long rows, int cols, int box_cols, int box_rows);
+bool bf16_rows_map(CUtensorMap* out, const void* ptr, long long rows, int cols, int box_cols, int box_rows,
+                   int ld = 0);
 
 // ---- int8 linear (linear.cu) ----------------------------------------------------------
 

@@ -199,9 +199,10 @@ __device__ __forceinline__ void qkv_pair(const LinearArgs& p, int m, int n, floa
     if (is_k) rot(x0, x1, t);
     const uint32_t packed = pack_bf16x2(x0, x1);
     const int group = p.heads / p.kv_heads;
-    __nv_bfloat16* base = (is_k ? p.k_cache : p.v_cache) + ((long long)sid * p.capacity + pos) * hd + d;
+    __nv_bfloat16* cache = is_k ? p.k_cache : p.v_cache;
     for (int rep = 0; rep < group; ++rep)
-        *reinterpret_cast<uint32_t*>(base + (kvh * group + rep) * kHeadDim) = packed;
+        *reinterpret_cast<uint32_t*>(cache + kv_offset(sid, pos, kvh * group + rep, p.num_streams, p.capacity) + d) =
+            packed;
 }
 
 template <int EPI, int TM, bool F16>

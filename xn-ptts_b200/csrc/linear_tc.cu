@@ -294,9 +294,10 @@ __device__ __forceinline__ void qkv_rows(const LinearArgs& p, const float* st, i
         const bool is_k = region == 1;
         const int kvh = (f - hd - (is_k ? 0 : kvd)) / kHeadDim;
         const uint2 packed = make_uint2(pack_bf16x2(x0, x1), pack_bf16x2(x2, x3));
-        __nv_bfloat16* base = (is_k ? p.k_cache : p.v_cache) + ((long long)sid * p.capacity + pos) * hd + d;
+        __nv_bfloat16* cache = is_k ? p.k_cache : p.v_cache;
         for (int rep = 0; rep < group; ++rep)
-            *reinterpret_cast<uint2*>(base + (kvh * group + rep) * kHeadDim) = packed;
+            *reinterpret_cast<uint2*>(cache + kv_offset(sid, pos, kvh * group + rep, p.num_streams, p.capacity) + d) =
+                packed;
     }
 }
 
@@ -1258,11 +1259,13 @@ bool launch_tma_flow(const LinearArgs& a, cudaStream_t s) {
 
 }  // namespace
 
-bool bf16_rows_map(CUtensorMap* out, const void* ptr, long long rows, int cols, int box_cols, int box_rows) {
+bool bf16_rows_map(CUtensorMap* out, const void* ptr, long long rows, int cols, int box_cols, int box_rows,
+                   int ld) {
     EncodeTiled enc = encoder();
-    if (!enc || rows <= 0 || cols % 8 != 0 || box_cols * 2 != 128) return false;
+    if (ld == 0) ld = cols;
+    if (!enc || rows <= 0 || cols % 8 != 0 || ld % 8 != 0 || ld < cols || box_cols * 2 != 128) return false;
     const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
-    const cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
+    const cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
     const cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
     const cuuint32_t elem[2] = {1, 1};
     return enc(out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, elem,

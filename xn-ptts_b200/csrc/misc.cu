@@ -219,7 +219,8 @@ __global__ void ring_rotate_kernel(RingEvictArgs a) {
         const int d2 = pr % (kHeadDim / 2);  // pair index within the head
         float sn, cs;
         sincosf((float)(-a.shift) * a.inv_freq[d2], &sn, &cs);
-        T* e = k + layer * a.layer_elems + a.sid * a.stream_elems + (long long)slot * a.row_elems + 2 * pr;
+        T* e = k + layer * a.layer_elems + kv_offset(a.sid, slot, pr / (kHeadDim / 2), a.streams, a.capacity) +
+               2 * d2;
         const float x0 = (float)e[0], x1 = (float)e[1];
         const float y0 = __fsub_rn(__fmul_rn(x0, cs), __fmul_rn(x1, sn));
         const float y1 = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, cs));

@@ -67,10 +67,9 @@ __global__ void rope_append_kernel(RopeAppendArgs a) {
     const bool is_k = slot < a.heads + a.kv_heads;
     const int g = is_k ? slot - a.heads : slot - a.heads - a.kv_heads;
     const int group = a.heads / a.kv_heads;
-    T* base = static_cast<T*>(is_k ? a.k_cache : a.v_cache) +
-              ((long long)sid * a.capacity + cslot) * a.heads * kHeadDim;
+    T* cache = static_cast<T*>(is_k ? a.k_cache : a.v_cache);
     for (int rep = 0; rep < group; ++rep) {
-        T* dst = base + (long long)(g * group + rep) * kHeadDim;
+        T* dst = cache + kv_offset(sid, cslot, g * group + rep, a.num_streams, a.capacity);
         dst[2 * i] = from_f32<T>(y0);
         dst[2 * i + 1] = from_f32<T>(y1);
     }
