@@ -201,6 +201,23 @@ __device__ __forceinline__ void i8x4_convert(uint32_t w, uint32_t& b01, uint32_t
     else i8x4_to_bf16x4(w, b01, b23);
 }
 
+// GELU, erf form (transformer.rs's gelu: 0.5 x (1 + erf(x / sqrt 2))), with erf from
+// Abramowitz & Stegun, Handbook of Mathematical Functions (1964), formula 7.1.26: for z >= 0,
+// erfc(z) = t (a1 + t (a2 + t (a3 + t (a4 + t a5)))) exp(-z^2), t = 1 / (1 + p z), with an
+// absolute error of at most 1.5e-7. 1 + erf(z) is 2 - erfc(z) for z >= 0 and erfc(-z) for
+// z < 0, so negative inputs lose no digits to cancellation. Branch-free: one reciprocal and one
+// exp2 on the MUFU pipe (approximate forms, errors near 2^-22), the rest FMAs.
+__device__ __forceinline__ float gelu_erf(float x) {
+    const float z = fabsf(x) * 0.70710678118654752f;
+    float t, e;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(t) : "f"(fmaf(0.3275911f, z, 1.0f)));
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(-1.4426950408889634f * z * z));
+    const float poly =
+        fmaf(t, fmaf(t, fmaf(t, fmaf(t, 1.061405429f, -1.453152027f), 1.421413741f), -0.284496736f), 0.254829592f);
+    const float c = t * poly * e;  // erfc(z)
+    return 0.5f * x * (x >= 0.f ? 2.0f - c : c);
+}
+
 __device__ __forceinline__ float to_f32(float x) { return x; }
 __device__ __forceinline__ float to_f32(__nv_bfloat16 x) { return __bfloat162float(x); }
 

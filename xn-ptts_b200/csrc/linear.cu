@@ -89,7 +89,7 @@ __device__ __forceinline__ float gelu(float x, int tanh_form) {
         const float u2 = (x * x * 0.07135482f + 1.595769f) * x;
         return x / (1.0f + expf(-u2));
     }
-    return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f));
+    return gelu_erf(x);
 }
 
 template <int MI>

@@ -223,7 +223,7 @@ __device__ __forceinline__ float gelu_tc(float x, int tanh_form) {
         const float u2 = (x * x * 0.07135482f + 1.595769f) * x;
         return x / (1.0f + expf(-u2));
     }
-    return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f));
+    return gelu_erf(x);
 }
 
 // Staged tile row stride in floats: 128 features + 4 (keeps float4 alignment, spreads banks).
@@ -1084,6 +1084,224 @@ __global__ void __launch_bounds__(PersistTile<WM>::kThreads, 1) linear_persist_k
     }
 }
 
+// linear_rows_kernel: the prompt-size linears with the operands' roles swapped. A is a tile of 128
+// activation rows (hi and lo planes, two MMAs), B 256 weight features (MMA N = 256), so an
+// accumulator is 128 rows (TMEM lanes) x 256 features (columns) and each activation byte that
+// crosses from L2 feeds twice the features of linear_persist_kernel's 128-feature tiles:
+// 64 KB per stage for 8.4 MFLOP against 48 KB for 4.2. Same roles and barriers otherwise:
+//   warp 0, lane 0: TMA producer (3 stages of X hi, X lo and W; 2 with a weight lo plane)
+//   warp 1, lane 0: MMA issuer into two 256-column accumulators (all 512 TMEM columns)
+//   warps 2..17:    epilogue, per 32-row x 128-feature chunk: the four warps of the chunk's TMEM
+//                   lane quarter read 32 columns each into the staging tile, then all 16 run the
+//                   row epilogues of linear_tma_kernel on it (2 rows per warp)
+// N must be a multiple of 256 and the weights 16-bit (planes or the widened prompt copy).
+constexpr int NT2 = 256;  // features per tile (MMA N)
+
+template <int WM>
+struct RowsTile {
+    static constexpr bool WLO = WM == kW16Lo;
+    static constexpr int PS = WLO ? 2 : 3;             // ring stages: 192 KB either way
+    static constexpr int kXBytes = PT * KS * 2;         // one activation plane: 16 KB
+    static constexpr int kWBytes = NT2 * KS * 2;        // one weight plane: 32 KB
+    static constexpr int kWOffset = 2 * kXBytes;
+    static constexpr int kStageBytes = 2 * kXBytes + (WLO ? 2 : 1) * kWBytes;
+    static constexpr int kStageOffset = PS * kStageBytes;  // the epilogue's staging tile
+    static constexpr int kBarOffset = kStageOffset + 32 * kStageStride * 4;
+    static constexpr int kSmem = 1024 + kBarOffset + 256;
+    static constexpr int kThreads = 32 * (2 + kEpiWarps);
+    static_assert(kStageBytes % 1024 == 0, "stages stay 1024-byte aligned");
+    static_assert(kSmem <= 227 * 1024, "fits one CTA per SM");
+    static_assert(3 * PS * 8 + 4 * 8 + 4 <= 256, "barriers fit the tail");
+};
+
+// 32 consecutive TMEM columns of this warp's 32 lanes (tcgen05.ld.32x32b.x32), one wait.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+template <int EPI, int WM>
+__global__ void __launch_bounds__(RowsTile<WM>::kThreads, 1) linear_rows_kernel(
+    const __grid_constant__ LinearArgs p, const __grid_constant__ CUtensorMap tm_w,
+    const __grid_constant__ CUtensorMap tm_wlo, const __grid_constant__ CUtensorMap tm_x,
+    const __grid_constant__ CUtensorMap tm_xlo) {
+    using T = RowsTile<WM>;
+    constexpr int PS = T::PS;
+    constexpr bool WLO = T::WLO;
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    const uint32_t raw = smem_u32(smem_raw);
+    const uint32_t base = (raw + 1023u) & ~1023u;
+    unsigned char* smem = smem_raw + (base - raw);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + T::kBarOffset);  // a stage landed
+    uint64_t* empty = full + PS;                                         // its MMAs are done
+    uint64_t* acc_full = empty + PS;
+    uint64_t* acc_empty = acc_full + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+    __shared__ int s_abort, s_issued, s_consumed;
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int NT = p.N / NT2, MT = (p.M + PT - 1) / PT, tiles = NT * MT, KT = p.K / KS;
+    const bool has_lo = p.a_lo != nullptr;
+    const uint32_t tx = (has_lo ? 2u : 1u) * T::kXBytes + (WLO ? 2u : 1u) * T::kWBytes;
+
+    if (tid == 0) {
+        s_abort = 0;
+        s_issued = 0;
+        s_consumed = 0;
+        for (int i = 0; i < PS; ++i) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&acc_full[i], 1);
+            mbar_init(&acc_empty[i], kEpiWarps);
+        }
+        fence_mbar_init();
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tm_w)) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tm_x)) : "memory");
+    }
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(2 * NT2)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    if (tid == 0) stamp_mark(p.stamps, p.stamp, STAMP_ENTRY);
+    auto fail = [&]() {
+        set_error(p.err, DEV_ERR_TIMEOUT);
+        atomicExch(&s_abort, 1);
+    };
+    auto aborted = [&]() { return *reinterpret_cast<volatile int*>(&s_abort) != 0; };
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ---- TMA producer ------------------------------------------------------------------
+            const uint64_t pol_w = policy_evict_last();
+            grid_dep_wait();
+            stamp_mark(p.stamps, p.stamp, STAMP_START);
+            int kk = 0;
+            for (int t = blockIdx.x; t < tiles && !aborted(); t += gridDim.x) {
+                const int n0 = (t % NT) * NT2, m0 = (t / NT) * PT;
+                for (int kt = 0; kt < KT; ++kt, ++kk) {
+                    const int st = kk % PS;
+                    if (kk >= PS && !mbar_wait(&empty[st], ((kk / PS) & 1) ^ 1)) {
+                        fail();
+                        break;
+                    }
+                    const uint32_t sa = base + st * T::kStageBytes;
+                    mbar_arrive_expect_tx(&full[st], tx);
+                    tma_load_2d(sa, &tm_x, kt * KS, m0, &full[st]);
+                    if (has_lo) tma_load_2d(sa + T::kXBytes, &tm_xlo, kt * KS, m0, &full[st]);
+                    tma_load_2d_hint(sa + T::kWOffset, &tm_w, kt * KS, n0, &full[st], pol_w);
+                    if (WLO) tma_load_2d_hint(sa + T::kWOffset + T::kWBytes, &tm_wlo, kt * KS, n0, &full[st], pol_w);
+                    s_issued = kk + 1;
+                }
+            }
+            grid_dep_launch();
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // ---- MMA issuer --------------------------------------------------------------------
+            // M = 128 rows (A: activations), N = 256 features (B: weights), both K-major.
+            const uint32_t idesc = p.a_f16 ? idesc_f16<NT2>() : idesc_bf16<NT2>();
+            int kk = 0, i = 0;
+            for (int t = blockIdx.x; t < tiles && !aborted(); t += gridDim.x, ++i) {
+                const int acc = i & 1, use = i >> 1;
+                if (use > 0 && !mbar_wait(&acc_empty[acc], (use - 1) & 1)) {
+                    fail();
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d = tmem + (uint32_t)(acc * NT2);
+                bool ok = true;
+                for (int kt = 0; kt < KT; ++kt, ++kk) {
+                    const int st = kk % PS;
+                    if (!mbar_wait(&full[st], (kk / PS) & 1)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t sa = base + st * T::kStageBytes;
+                    const uint64_t dx = sw128_desc(sa), dxl = sw128_desc(sa + T::kXBytes);
+                    const uint64_t dw = sw128_desc(sa + T::kWOffset), dwl = sw128_desc(sa + T::kWOffset + T::kWBytes);
+#pragma unroll
+                    for (int k2 = 0; k2 < KS / 16; ++k2) {
+                        tc_mma(d, dx + 2 * k2, dw + 2 * k2, idesc, (kt | k2) ? 1u : 0u);
+                        if (has_lo) tc_mma(d, dxl + 2 * k2, dw + 2 * k2, idesc, 1u);
+                        if (WLO) tc_mma(d, dx + 2 * k2, dwl + 2 * k2, idesc, 1u);
+                    }
+                    tc_commit(&empty[st]);
+                    s_consumed = kk + 1;
+                }
+                if (!ok) {
+                    fail();
+                    break;
+                }
+                tc_commit(&acc_full[acc]);
+            }
+        }
+    } else {
+        // ---- epilogue ------------------------------------------------------------------------
+        grid_dep_wait();  // the residual epilogues read what predecessors wrote
+        const int ew = warp - 2, quarter = warp & 3, part = ew >> 2;
+        float* stg = reinterpret_cast<float*>(smem + T::kStageOffset);
+        int i = 0;
+        for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++i) {
+            const int acc = i & 1, use = i >> 1;
+            const int n0 = (t % NT) * NT2, m0 = (t / NT) * PT;
+            const bool got = !aborted() && mbar_wait(&acc_full[acc], use & 1);
+            if (!got) fail();
+            if (epi_bar_any(!got)) break;  // every epilogue warp leaves together
+            __syncwarp();
+            tc_fence_after();
+#pragma unroll 1
+            for (int c = 0; c < 8; ++c) {  // chunk c: rows 32 (c % 4) .., features 128 (c / 4) ..
+                const int q = c & 3, h = c >> 2;
+                if (quarter == q) {
+                    float v[32];
+                    tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(acc * NT2 + 128 * h + 32 * part), v);
+                    float4* row = reinterpret_cast<float4*>(stg + lane * kStageStride + 32 * part);
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) row[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+                }
+                epi_bar_sync();
+                if (EPI == EPI_QKV) qkv_rows(p, stg, n0 + 128 * h, m0 + 32 * q, ew);
+                else plain_rows<EPI>(p, stg, n0 + 128 * h, m0 + 32 * q, 0, ew);
+                epi_bar_sync();  // the chunk's readers are done with the staging tile
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty[acc]);
+        }
+        if (tid == 64) stamp_mark(p.stamps, p.stamp, STAMP_END);
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (tid == 0) {
+        // Copies issued but never consumed (only after a timeout): let them land before exit.
+        for (int kk = s_consumed; kk < s_issued; ++kk) mbar_wait(&full[kk % PS], (kk / PS) & 1);
+    }
+    if (warp == 0) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * NT2) : "memory");
+    }
+}
+
 // ---- tensor maps ---------------------------------------------------------------------------
 
 using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -1231,6 +1449,37 @@ bool launch_persist(const LinearArgs& a, cudaStream_t s) {
     return true;
 }
 
+// Prompt sizes with 16-bit weights and N a multiple of 256: linear_rows_kernel.
+template <int EPI, int WM>
+bool launch_rows(const LinearArgs& a, cudaStream_t s) {
+    using T = RowsTile<WM>;
+    const bool bf = !a.a_f16;
+    CUtensorMap mw, mwl, mx, mxl;
+    if (!f16_map(&mw, a.wh, a.N, a.K, NT2, bf) || !f16_map(&mx, a.a, a.M, a.K, PT, bf)) return false;
+    mwl = mw;
+    if (WM == kW16Lo && !f16_map(&mwl, a.wh_lo, a.N, a.K, NT2, bf)) return false;
+    mxl = mx;
+    if (a.a_lo && !f16_map(&mxl, a.a_lo, a.M, a.K, PT, bf)) return false;
+    set_max_dynamic_smem(reinterpret_cast<const void*>(linear_rows_kernel<EPI, WM>), T::kSmem);
+    int dev = 0, sms = 0;
+    cudaGetDevice(&dev);
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms < 1) sms = 1;
+    const int tiles = (a.N / NT2) * ((a.M + PT - 1) / PT);
+    launch_k(linear_rows_kernel<EPI, WM>, dim3(tiles < sms ? tiles : sms), dim3(T::kThreads), T::kSmem, s, a, mw,
+             mwl, mx, mxl);
+    return true;
+}
+
+// Whether prompt-size linears with 16-bit weights and N a multiple of 256 take linear_rows_kernel
+// (default) or linear_persist_kernel (PTTS_B200_PERSIST=features).
+bool rows_tiles() {
+    static const bool on = [] {
+        const char* e = getenv("PTTS_B200_PERSIST");
+        return !(e && e[0] == 'f');
+    }();
+    return on;
+}
+
 // The weight form of a launch: 16-bit planes when the layer has them, else its int8 weights.
 int weight_form(const LinearArgs& a) { return a.wh_lo ? kW16Lo : (a.wh ? kW16 : kW8); }
 
@@ -1240,6 +1489,8 @@ bool launch_tma_rows(const LinearArgs& a, cudaStream_t s) {
     if (a.wblk) return a.a_f16 && a.M < kPersistMinRows && launch_i8<EPI, 32, true>(a, s);
     const int wm = weight_form(a);
     if (a.M >= kPersistMinRows && a.splits == 1 && EPI != EPI_PARTIAL) {
+        if (wm != kW8 && a.N % NT2 == 0 && rows_tiles())
+            return wm == kW16Lo ? launch_rows<EPI, kW16Lo>(a, s) : launch_rows<EPI, kW16>(a, s);
         if (wm == kW16Lo) return launch_persist<EPI, kW16Lo>(a, s);
         return wm == kW16 ? launch_persist<EPI, kW16>(a, s) : launch_persist<EPI, kW8>(a, s);
     }
