@@ -2,7 +2,7 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--repeats R] [--impl ours|reference]
 
-Workload (the largest single-GPU configuration): the 40m flow LM shape
+Workload (config 5, the largest single-GPU configuration): the 40m flow LM shape
 (9 layers, d_model 512, 8 heads of 64, ff 2048), random-init int8 per-output-channel weights
 (scales U(0.005, 0.02), seed 4), 512 independent streams per GPU (GPU g holds streams
 512g..512g+511 of 4096), prefixes U{32..512} prefilled before timing, then decode frames: one
