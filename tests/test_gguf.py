@@ -28,6 +28,26 @@ def test_remap_key_renames_and_drops(ptts):
         assert ptts.gguf_remap_key(src) == dst, src
 
 
+def test_q8_0_quantizer_is_the_published_format(ptts):
+    """quantize_q8_0 (the q8_0 of Q8Linear::from_linear, q8.rs:29-35): per 32 weights an f16
+    d = max |w| / 127 and int8 q = round(w / d), laid out as the GGUF blocks; dequantized with
+    the stored f16 d, every weight is within half a step of the original plus the f16 rounding
+    of d over at most 127 steps (d (1/2 + 127 * 2^-11)), and all-zero blocks stay zero."""
+    from gguf_fixture import q8_0_blocks
+    rng = np.random.default_rng(97)
+    w = rng.normal(0.0, 0.05, (48, 96)).astype(np.float32)
+    w[3, 32:64] = 0.0
+    blocks = ptts.quantize_q8_0(w)
+    assert blocks.shape == (48, 3 * 34) and blocks.dtype == np.uint8
+    b = blocks.reshape(48, 3, 34)
+    d = b[..., :2].copy().view(np.float16).reshape(48, 3).astype(np.float32)
+    q = b[..., 2:].copy().view(np.int8).astype(np.float32)
+    np.testing.assert_array_equal(blocks, q8_0_blocks(q.reshape(48, 96).astype(np.int8), d))
+    deq = (q * d[..., None]).reshape(48, 96)
+    assert np.all(np.abs(deq - w) <= (0.5 + 127 * 2.0 ** -11) * np.repeat(d, 32, axis=1) * (1 + 1e-3) + 1e-12)
+    assert np.all(deq[3, 32:64] == 0.0) and d[3, 1] == 0.0
+
+
 def _q8_layers(cfg, seed):
     """Per layer: int8 q ~ U{-127..127} and f16 block scales ~ U(0.005, 0.02) for the four
     linears (the regime of the int8 tests), LayerNorm gain 1/16."""

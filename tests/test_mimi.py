@@ -89,3 +89,34 @@ def test_layer_scale_folds_into_the_residual_linears(ptts, cuda):
     assert normwise(got, want) < 1e-5
     model.set_layer_scale(0, None, None)
     assert torch.equal(run(), plain)
+
+
+def test_a_q8_mimi_transformer_matches_the_f32_one(ptts, cuda):
+    """transformer.rs:1321-1338: a Mimi transformer whose linears are quantized to q8_0
+    (prepare_q8 / apply_q8) gives the f32 one's outputs within a relative RMS error of 1e-2,
+    and not exactly. Here over windowed prompts and decode rows past the window, through the
+    q8_0 layer loader (f16 hi/lo planes for prompts, block-scaled int8 widened on chip for
+    decode rows), with the layer scales."""
+    import torch
+    cfg = ptts.FlowLMConfig(num_layers=2)
+    tensors = ptts.random_mimi_tensors(cfg, 95, layer_scale=0.5)
+    S, cap, ctx = 3, 20, 12
+    outs = []
+    for q8 in (False, True):
+        model = ptts.Transformer(cfg)
+        model.load_mimi(tensors, q8_0=q8)
+        kv = ptts.KvState(cfg.num_layers, S, cap, dtype="bf16")
+        kv.set_window(list(range(S)), ctx)
+        g = torch.Generator().manual_seed(95)
+        ys = []
+        for call in _calls():
+            streams = [s for s, _ in call]
+            rows = [r for _, r in call]
+            x = torch.randn(sum(rows), 512, generator=g).bfloat16()
+            ys.append(model.forward(kv, x.to(cuda), streams, rows).cpu().numpy())
+        kv.check()
+        outs.append(np.concatenate(ys))
+    want, got = outs
+    err = float(np.sqrt(np.sum((got - want) ** 2) / np.sum(want ** 2)))
+    print("q8_0 against f32 Mimi layers: relative RMS error", err)
+    assert 0.0 < err < 0.01

@@ -503,6 +503,24 @@ def random_mimi_tensors(cfg: FlowLMConfig, seed: int, *, layer_scale: float = 0.
     return out
 
 
+def quantize_q8_0(w) -> np.ndarray:
+    """f32 weights [n][k] (k a multiple of 32) as GGUF q8_0 blocks, uint8 [n][k / 32 * 34]: per
+    32 weights along k, d = max |w| / 127 stored as f16, then q = round(w / d) as int8 (the q8_0
+    format of ggml, which Q8Linear::from_linear quantizes to, q8.rs:29-35). W = q * f16(d)."""
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    n, k = w.shape
+    if k % 32:
+        raise PttsError(ERR_ARG, f"q8_0 needs rows of a multiple of 32 weights, not {k}")
+    b = w.reshape(n, k // 32, 32)
+    d = np.abs(b).max(axis=2) / 127.0
+    inv = np.divide(1.0, d, out=np.zeros_like(d), where=d > 0)
+    q = np.clip(np.rint(b * inv[..., None]), -127, 127).astype(np.int8)
+    out = np.empty((n, k // 32, 34), np.uint8)
+    out[..., :2] = d.astype(np.float16).view(np.uint8).reshape(n, k // 32, 2)
+    out[..., 2:] = q.view(np.uint8)
+    return out.reshape(n, k // 32 * 34)
+
+
 class Transformer:
     """StreamingTransformer (transformer.rs:674-930) for the flow LM, int8 per-channel."""
 
@@ -556,18 +574,24 @@ class Transformer:
         ptrs = [None if v is None else v.ctypes.data_as(P) for v in keep]
         _check(lib().ptts_b200_model_set_layer_scale(self._h, layer, *ptrs))
 
-    def load_mimi(self, tensors: dict):
+    def load_mimi(self, tensors: dict, q8_0: bool = False):
         """A Mimi transformer's layers under the checkpoint's names (mimi.rs:359-360 and
         transformer.rs:411-412, 549-563): layers.{i}.self_attn.in_proj.weight [3d, d],
         self_attn.out_proj.weight, linear1.weight, linear2.weight (f32, no biases), norm1/norm2
-        weight and bias, layer_scale_1.scale and layer_scale_2.scale."""
+        weight and bias, layer_scale_1.scale and layer_scale_2.scale. With q8_0, the four
+        linears are quantized to q8_0 first (prepare_q8 / apply_q8, transformer.rs:642-673)."""
         for i in range(self.cfg.num_layers):
             p = f"layers.{i}."
-            self.load_layer_f32(i, {
-                "in_proj": tensors[p + "self_attn.in_proj.weight"], "out_proj": tensors[p + "self_attn.out_proj.weight"],
-                "linear1": tensors[p + "linear1.weight"], "linear2": tensors[p + "linear2.weight"],
-                "norm1_weight": tensors[p + "norm1.weight"], "norm1_bias": tensors[p + "norm1.bias"],
-                "norm2_weight": tensors[p + "norm2.weight"], "norm2_bias": tensors[p + "norm2.bias"]})
+            w = {"in_proj": tensors[p + "self_attn.in_proj.weight"], "out_proj": tensors[p + "self_attn.out_proj.weight"],
+                 "linear1": tensors[p + "linear1.weight"], "linear2": tensors[p + "linear2.weight"],
+                 "norm1_weight": tensors[p + "norm1.weight"], "norm1_bias": tensors[p + "norm1.bias"],
+                 "norm2_weight": tensors[p + "norm2.weight"], "norm2_bias": tensors[p + "norm2.bias"]}
+            if q8_0:
+                for k in ("in_proj", "out_proj", "linear1", "linear2"):
+                    w[k] = quantize_q8_0(w[k])
+                self.load_layer_q8_0(i, w)
+            else:
+                self.load_layer_f32(i, w)
             self.set_layer_scale(i, tensors.get(p + "layer_scale_1.scale"), tensors.get(p + "layer_scale_2.scale"))
 
     def load_layer_q8_0(self, layer: int, w: dict):
