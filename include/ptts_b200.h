@@ -70,7 +70,7 @@ typedef struct ptts_b200_flow ptts_b200_flow; /* the flow head, see "Flow head" 
  * transformer arguments of StreamingTransformer::load (transformer.rs:680-717). */
 typedef struct {
     int32_t d_model;          /* 512 */
-    int32_t num_heads;        /* 8 */
+    int32_t num_heads;        /* 8 (any multiple of 8: 16 in the reference's 1024-wide test config) */
     int32_t num_kv_heads;     /* 8 (grouped-query attention when smaller) */
     int32_t head_dim;         /* 64 */
     int32_t num_layers;       /* 6 (31m) or 9 (40m) */

@@ -264,8 +264,9 @@ void launch_prefill_attn(const PrefillArgs& a, bool cache_bf16, cudaStream_t s);
 // one sequence, head); tiles[i] = (first row, rows).
 void launch_prefill_attn_tc(const PrefillArgs& a, const int2* tiles, int n_tiles, cudaStream_t s);
 // The same with one CTA per (tile, group of heads), the group's (head, key tile) items in one
-// pipeline (attn_prefill_fa.cu). `streams` and `capacity` describe the caches' [streams][capacity]
-// rows of 512 bf16. False when the caches' tensor maps cannot be made (nothing launched).
+// pipeline (attn_prefill_fa.cu). `streams` and `capacity` describe the head group's cache block:
+// [streams][capacity] rows of 512 bf16. False when the tensor maps cannot be made (nothing
+// launched).
 bool launch_prefill_attn_fa(const PrefillArgs& a, const int2* tiles, int n_tiles, int streams, int capacity,
                             cudaStream_t s);
 // Tensor map of a row-major [rows][cols] bf16 matrix, box box_cols (128 bytes) x box_rows,
