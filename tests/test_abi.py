@@ -63,6 +63,19 @@ def test_heads_that_do_not_divide_the_width_are_an_error(ptts, heads):
     assert "heads" in ptts.lib().ptts_b200_last_error().decode()
 
 
+@pytest.mark.parametrize("heads", [4, 12])
+def test_head_counts_other_than_multiples_of_8_are_unsupported(ptts, heads):
+    """Heads come in groups of 8 (the cache's blocks): 4 or 12 heads of 64 are refused before any
+    device work, for the cache and for the model, naming the rule."""
+    lib = ptts.lib()
+    out = ctypes.c_void_p()
+    assert lib.ptts_b200_kv_create(0, 1, 1, 16, heads, 64, ptts.BF16, ctypes.byref(out)) == ptts.ERR_UNSUPPORTED
+    assert "multiple of 8 heads" in lib.ptts_b200_last_error().decode()
+    cfg = ptts.FlowLMConfig(d_model=64 * heads, num_heads=heads, num_kv_heads=heads).c_struct()
+    assert lib.ptts_b200_model_create(0, ctypes.byref(cfg), ctypes.byref(out)) == ptts.ERR_UNSUPPORTED
+    assert "multiple of 8 heads" in lib.ptts_b200_last_error().decode()
+
+
 def test_null_handles_are_refused(ptts):
     lib = ptts.lib()
     n = (ctypes.c_int32 * 4)()
